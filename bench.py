@@ -1,0 +1,440 @@
+#!/usr/bin/env python
+"""Benchmark of the quantized-matmul hot path on B200 (one JSON line).
+
+Headline workload (the shape the reference's own CPU
+kernel runs): the Llama-7B decode projection x f32 [1,4096] -> per-tensor
+INT8 quantization -> W int8 [N=11008, K=4096] per-channel GEMV -> f32
+[1,11008].  metric = weight GB/s (45,088,768 int8 weight bytes per call).
+
+  step     = 256 independent decode-projection calls (256 distinct activation
+             vectors), replayed from one CUDA graph; weights rotate over 6
+             device copies (270 MB > 2x the 126 MB L2) so every call streams
+             its weights from HBM.
+  value    = weight bytes of all calls on all ranks / max-over-ranks time.
+  e2e      = the same calls through the host-buffer C-ABI drop-in
+             (mri_host_matmul_int8_from_f32): pinned x H2D, kernel, out D2H,
+             stream sync, per call.
+  roofline = algorithmic bytes per launch (weights + scales + x_q + out) /
+             mean launch duration, against the measured HBM copy bandwidth.
+
+Multi-GPU (torchrun): each rank runs its own projections (independent units,
+no data-path collective; weak scaling).  `--impl reference` times the
+reference's CPU path (C++ restatement of proj_int8_par: quantize_symmetric +
+matmul_int8_parallel, forward_int8.rs:87-96) on the host cores, rank 0 only.
+"""
+import argparse
+import ctypes
+import datetime
+import importlib
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+for p in (REPO, os.path.join(REPO, "oracle")):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+K_DIM, N_DIM = 4096, 11008
+WEIGHT_BYTES = N_DIM * K_DIM                          # int8 weights per call
+ALG_BYTES = WEIGHT_BYTES + 4 * N_DIM + K_DIM * 4 + 4 * N_DIM  # + scales + x f32 + out f32
+CALLS_PER_STEP = 256
+WEIGHT_COPIES = 6
+REF_CALLS_PER_STEP = 4
+
+THROTTLE_BITS = {0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+                 0x80: "hw_power_brake_slowdown", 0x4: "sw_power_cap", 0x2: "applications_clocks",
+                 0x1: "gpu_idle", 0x10: "sync_boost"}
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-secondary", action="store_true",
+                    help="skip the Q8_0 / Q4_0 / prefill side measurements")
+    ap.add_argument("--no-cpu-baseline", action="store_true",
+                    help="skip the timed CPU sample (profiling runs)")
+    return ap.parse_args()
+
+
+def dist_env():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)),
+            int(os.environ.get("LOCAL_RANK", 0)))
+
+
+def measured_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def committed_traffic(kernel_key):
+    """DRAM bytes per launch from the committed ncu summary, if any."""
+    path = os.path.join(REPO, "profiles", "ncu_traffic.json")
+    if not os.path.exists(path):
+        return None
+    with open(path) as f:
+        return json.load(f).get(kernel_key)
+
+
+class ClockSampler:
+    """Polls NVML (SM clock + clock-event reasons) while the timed region runs."""
+
+    def __init__(self, device, period_s=0.002):
+        self.samples, self.reasons, self.max_mhz = [], 0, None
+        self._stop = threading.Event()
+        self._period = period_s
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(device)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:  # noqa: BLE001 - NVML missing: report no clocks
+            self._nv = None
+        self._t = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self._nv.nvmlDeviceGetClockInfo(self._h, self._nv.NVML_CLOCK_SM))
+                self.reasons |= int(self._nv.nvmlDeviceGetCurrentClocksEventReasons(self._h))
+            except Exception:  # noqa: BLE001
+                pass
+            time.sleep(self._period)
+
+    def __enter__(self):
+        if self._nv is not None:
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._nv is not None:
+            self._t.join()
+
+    def summary(self):
+        if not self.samples:
+            return None
+        names = [n for b, n in THROTTLE_BITS.items() if self.reasons & b and n != "gpu_idle"]
+        return {"sm_mhz": float(statistics.median(self.samples)), "sm_max_mhz": self.max_mhz,
+                "samples": len(self.samples), "reasons": names}
+
+
+def cpu_baseline_sample(seconds=10.0):
+    """The reference's decode projection on the host (C++ restatement of
+    proj_int8_par = quantize_symmetric + matmul_int8_parallel), bounded."""
+    import oracle
+    rng = np.random.default_rng(0)
+    w = rng.integers(-127, 128, size=N_DIM * K_DIM, dtype=np.int8)
+    ws = rng.uniform(0.001, 0.02, size=N_DIM).astype(np.float32)
+    x = rng.normal(0, 1, size=K_DIM).astype(np.float32)
+    out = np.empty((1, N_DIM), np.float32)
+    threads = oracle.hardware_threads()
+    calls, t0 = 0, time.perf_counter()
+    while True:
+        aq, s = oracle.quantize_symmetric(x)
+        oracle.matmul_int8_parallel(aq, s, w, ws, N_DIM, K_DIM, 1, n_threads=threads, out=out)
+        calls += 1
+        el = time.perf_counter() - t0
+        if (el >= seconds and calls >= 2) or el >= 3 * seconds:
+            break
+    return calls, el
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    import oracle
+    rng = np.random.default_rng(0)
+    w = rng.integers(-127, 128, size=N_DIM * K_DIM, dtype=np.int8)
+    ws = rng.uniform(0.001, 0.02, size=N_DIM).astype(np.float32)
+    xs = rng.normal(0, 1, size=(REF_CALLS_PER_STEP, K_DIM)).astype(np.float32)
+    out = np.empty((1, N_DIM), np.float32)
+    threads = oracle.hardware_threads()
+
+    def step():
+        for i in range(REF_CALLS_PER_STEP):
+            aq, s = oracle.quantize_symmetric(xs[i])
+            oracle.matmul_int8_parallel(aq, s, w, ws, N_DIM, K_DIM, 1, n_threads=threads, out=out)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    el = time.perf_counter() - t0
+    gbs = args.steps * REF_CALLS_PER_STEP * WEIGHT_BYTES / el / 1e9
+    sample = (f"{REF_CALLS_PER_STEP} decode projections [1,4096]x[4096,11008] per step; "
+              f"matmul_int8_parallel at M=1 runs one row task (parallel.rs:334), so 1 of {threads} "
+              f"host threads works")
+    line = {
+        "impl": "reference", "metric": "decode GEMV weight GB/s", "value": round(gbs, 4), "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(el / args.steps * 1e3, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8->int32->f32", "data": "synthetic (seed 0)",
+        "config": {"workload": "decode projection [1,4096]x[4096,11008] int8 per-channel, per-tensor act quant",
+                   "calls_per_step": REF_CALLS_PER_STEP},
+        "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": 1, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def graph_of(torch, stream, fn):
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        fn()
+    return g
+
+
+def time_graph(torch, stream, g, steps, warmup):
+    for _ in range(warmup):
+        g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        g.replay()
+    e1.record(stream)
+    e1.synchronize()
+    return e0.elapsed_time(e1)
+
+
+def secondary_measurements(torch, mri, lib, device, peak_hbm, peak_tc):
+    """Q8_0 / Q4_0 decode (M=1, M=8) and the prefill GEMM, 1 GPU, each from a
+    CUDA graph over rotating weight copies."""
+    res = {}
+    rng = np.random.default_rng(0)
+    wf = rng.normal(0, 0.02, size=(N_DIM, K_DIM)).astype(np.float32)
+    s = torch.cuda.Stream(device)
+    ctx = mri.Context(device, stream=s)
+    for fmt in ("q8_0", "q4_0"):
+        wb = mri.formats.quantize_q8_0(wf, N_DIM, K_DIM) if fmt == "q8_0" else \
+            mri.formats.quantize_q4_0(wf, N_DIM, K_DIM)
+        copies = max(3, int(np.ceil(300e6 / wb.size)))
+        ws = [mri.Q8_0WeightMatrix.from_raw_bytes(wb, N_DIM, K_DIM, ctx=ctx) if fmt == "q8_0"
+              else mri.Q4_0Matrix(wb, N_DIM, K_DIM, ctx=ctx) for _ in range(copies)]
+        fn = lib.mri_matmul_q8_0_direct if fmt == "q8_0" else lib.mri_matmul_q4_0_dequant
+        for m in (1, 8):
+            calls = 32
+            x = torch.randn(calls, m, K_DIM, device=f"cuda:{device}", generator=None)
+            out = torch.empty(calls, m, N_DIM, device=f"cuda:{device}")
+
+            def body():
+                for i in range(calls):
+                    rc = fn(ctx.handle, ctypes.c_void_p(x[i].data_ptr()), m, K_DIM,
+                            ws[i % copies].handle, ctypes.c_void_p(out[i].data_ptr()))
+                    assert rc == 0, mri._lib.last_error()
+            body()
+            ctx.synchronize()
+            g = graph_of(torch, s, body)
+            ms = time_graph(torch, s, g, 20, 3)
+            per_call_s = ms / 1e3 / (20 * calls)
+            alg = wb.size + m * K_DIM * 4 + m * N_DIM * 4
+            res[f"{fmt}_m{m}"] = {"weight_gbs": round(wb.size / per_call_s / 1e9, 1),
+                                  "us_per_call": round(per_call_s * 1e6, 3),
+                                  "roofline_frac_hbm": round(alg / per_call_s / 1e9 / peak_hbm, 4)}
+            del g
+        del ws
+    # Prefill GEMM [512,4096] x [4096,11008]^T
+    try:
+        M = 512
+        wq = rng.integers(-127, 128, size=N_DIM * K_DIM, dtype=np.int8)
+        wsc = rng.uniform(0.001, 0.02, size=N_DIM).astype(np.float32)
+        copies = 3
+        qms = [mri.QuantizedMatrix(wq, wsc, N_DIM, K_DIM, ctx=ctx, keep_host=False) for _ in range(copies)]
+        x = torch.randn(M, K_DIM, device=f"cuda:{device}")
+        out = torch.empty(M, N_DIM, device=f"cuda:{device}")
+        path = ctx.int8_path(M, N_DIM, K_DIM)
+
+        def body():
+            for i in range(copies):
+                rc = lib.mri_matmul_int8_from_f32(ctx.handle, ctypes.c_void_p(x.data_ptr()), M, K_DIM,
+                                                  qms[i].handle, ctypes.c_void_p(out.data_ptr()))
+                assert rc == 0, mri._lib.last_error()
+        body()
+        ctx.synchronize()
+        g = graph_of(torch, s, body)
+        ms = time_graph(torch, s, g, 10, 2)
+        per_call_s = ms / 1e3 / (10 * copies)
+        tops = 2.0 * M * K_DIM * N_DIM / per_call_s / 1e12
+        res["prefill_m512"] = {"tops": round(tops, 2), "us_per_call": round(per_call_s * 1e6, 2),
+                               "path": {0: "stream-gemv", 1: "generic-gemv", 2: "tcgen05-gemm"}[path],
+                               "roofline_frac_int8": round(tops / (2 * peak_tc), 4),
+                               "int8_peak_note": "int8 dense peak taken as 2x measured bf16"}
+        del g
+    except Exception as e:  # noqa: BLE001 - side measurement only
+        res["prefill_m512"] = {"error": str(e)[:200]}
+    ctx.synchronize()
+    return res
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    mri = importlib.import_module("mini-rust-inference_b200")
+    lib = mri._lib.load()
+    device = local_rank
+    torch.cuda.set_device(device)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device(f"cuda:{device}"))
+    peak_hbm, peak_tc, peak_kind = measured_peaks()
+
+    rng = np.random.default_rng(0)
+    wq = rng.integers(-127, 128, size=N_DIM * K_DIM, dtype=np.int8)
+    ws = rng.uniform(0.001, 0.02, size=N_DIM).astype(np.float32)
+    xs_host = rng.normal(0, 1, size=(CALLS_PER_STEP, K_DIM)).astype(np.float32)
+
+    s = torch.cuda.Stream(device)
+    ctx = mri.Context(device, stream=s)
+    weights = [mri.QuantizedMatrix(wq, ws, N_DIM, K_DIM, ctx=ctx, keep_host=False)
+               for _ in range(WEIGHT_COPIES)]
+    x = torch.from_numpy(xs_host).to(f"cuda:{device}")
+    out = torch.empty(CALLS_PER_STEP, N_DIM, device=f"cuda:{device}")
+    xp, op = x.data_ptr(), out.data_ptr()
+
+    def body():
+        for i in range(CALLS_PER_STEP):
+            rc = lib.mri_matmul_int8_from_f32(ctx.handle, ctypes.c_void_p(xp + i * K_DIM * 4), 1, K_DIM,
+                                              weights[i % WEIGHT_COPIES].handle,
+                                              ctypes.c_void_p(op + i * N_DIM * 4))
+            if rc != 0:
+                raise RuntimeError(mri._lib.last_error())
+
+    body()
+    ctx.synchronize()
+    ctx.check_device_status()
+    n0 = ctx.launch_count
+    g = graph_of(torch, s, body)
+    launches_per_step = ctx.launch_count - n0
+
+    for _ in range(args.warmup):
+        g.replay()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(device) as clk:
+        e0.record(s)
+        for _ in range(args.steps):
+            g.replay()
+        e1.record(s)
+        e1.synchronize()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    if dist:
+        t = torch.tensor([ms], device=f"cuda:{device}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    ctx.check_device_status()
+    del g
+
+    calls = args.steps * CALLS_PER_STEP
+    value = world * calls * WEIGHT_BYTES / (ms / 1e3) / 1e9
+    launch_s = ms / 1e3 / calls
+    achieved = ALG_BYTES / launch_s / 1e9
+
+    # e2e: host buffers through the synchronous C-ABI drop-in, per call.
+    ctx_e2e = mri.Context(device)
+    xh = torch.from_numpy(xs_host).pin_memory()
+    oh = torch.empty(CALLS_PER_STEP, N_DIM).pin_memory()
+    xhp, ohp = xh.data_ptr(), oh.data_ptr()
+    e2e_steps = max(1, min(args.steps, 20))
+
+    def e2e_step():
+        for i in range(CALLS_PER_STEP):
+            rc = lib.mri_host_matmul_int8_from_f32(ctx_e2e.handle, ctypes.c_void_p(xhp + i * K_DIM * 4), 1,
+                                                   K_DIM, weights[i % WEIGHT_COPIES].handle,
+                                                   ctypes.c_void_p(ohp + i * N_DIM * 4))
+            if rc != 0:
+                raise RuntimeError(mri._lib.last_error())
+    e2e_step()
+    es = torch.cuda.ExternalStream(ctx_e2e.stream_handle, device=f"cuda:{device}")
+    if dist:
+        dist.barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(es)
+    for _ in range(e2e_steps):
+        e2e_step()
+    f1.record(es)
+    f1.synchronize()
+    e2e_ms = f0.elapsed_time(f1)
+    if dist:
+        t = torch.tensor([e2e_ms], device=f"cuda:{device}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = world * e2e_steps * CALLS_PER_STEP * WEIGHT_BYTES / (e2e_ms / 1e3) / 1e9
+
+    secondary = None
+    if world == 1 and not args.no_secondary:
+        secondary = secondary_measurements(torch, mri, lib, device, peak_hbm, peak_tc)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        import oracle
+        calls_c, el = cpu_baseline_sample()
+        cpu = {"value": round(calls_c * WEIGHT_BYTES / el / 1e9, 4), "unit": "GB/s", "cores": 1,
+               "kind": "port",
+               "sample": f"{calls_c} decode projections in {el:.1f}s: quantize_symmetric + "
+                         f"matmul_int8_parallel restated in C++ (AVX2 maddubs dot); M=1 gives one "
+                         f"row task, so 1 of {oracle.hardware_threads()} host threads works"}
+
+    if rank == 0:
+        line = {
+            "metric": "decode GEMV weight GB/s", "value": round(value, 2), "unit": "GB/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8->int32->f32", "data": "synthetic (seed 0)",
+            "config": {"workload": "decode projection [1,4096]x[4096,11008] int8 per-channel, "
+                                   "per-tensor act quant fused (BASELINE config 0)",
+                       "calls_per_step": CALLS_PER_STEP, "parallelism": f"replicas x{world}",
+                       "l2": f"weights rotate over {WEIGHT_COPIES} copies "
+                             f"({WEIGHT_COPIES * WEIGHT_BYTES / 1e6:.0f} MB > 2x L2)",
+                       "graph": "one CUDA graph per step"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak_hbm, "unit": "GB/s",
+                         "frac": round(achieved / peak_hbm, 4), "peak_kind": peak_kind,
+                         "bytes_per_launch": ALG_BYTES,
+                         "traffic": committed_traffic("gemv_i8_tma_decode")},
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
+                    "h2d_bytes_per_step": CALLS_PER_STEP * K_DIM * 4,
+                    "d2h_bytes_per_step": CALLS_PER_STEP * N_DIM * 4},
+            "gpu_launches": int(launches_per_step * args.steps),
+            "clocks": clk.summary(),
+            "cpu_baseline": cpu,
+        }
+        if secondary is not None:
+            line["secondary"] = secondary
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse_args()
+    rank, world, local_rank = dist_env()
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    run_ours(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,169 @@
+/*
+ * mri_gpu.h — C ABI of the B200 (sm_100a) quantized-matmul hot path of
+ * mini-rust-inference.
+ *
+ * Every entry point is `extern "C"`, takes plain pointers and sizes, and
+ * returns an int32 status.  The reference's operators are Rust free functions
+ * returning Result<Tensor<f32>, TensorError>; the status codes map 1:1 onto
+ * that error enum (src/tensor/error.rs:7-29):
+ *   MRI_ERR_INVALID_SHAPE  <-> TensorError::InvalidShape
+ *   MRI_ERR_SHAPE_MISMATCH <-> TensorError::ShapeMismatch
+ * and mri_last_error() returns the reason text of the calling thread's last
+ * failure (the `reason` / expected-vs-got of the Rust error).
+ *
+ * Conventions
+ *   - Weights live on the device: QuantizedMatrix, Q8_0WeightMatrix and the
+ *     Q4_0 byte slice are uploaded once into opaque handles (the reference
+ *     loads them once in LlamaModelInt8::from_loader, forward_int8.rs:461-507).
+ *   - `*_dev` pointers are device memory; calls on them are asynchronous on
+ *     the context's stream.  `mri_host_*` calls take host memory and are
+ *     synchronous (H2D, kernels, D2H, stream sync) — they are the drop-ins for
+ *     the reference functions, which take and return host tensors.
+ *   - A context owns one CUDA stream and its scratch buffers; use one context
+ *     per host thread (the reference functions are reentrant; contexts give the
+ *     same property).
+ *   - There is no CPU fallback: without a usable sm_100 device every compute
+ *     call returns MRI_ERR_CUDA.
+ */
+#ifndef MRI_GPU_H
+#define MRI_GPU_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MRI_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define MRI_API __attribute__((visibility("default")))
+#else
+#define MRI_API
+#endif
+
+enum mri_status {
+  MRI_OK = 0,
+  MRI_ERR_INVALID_SHAPE = 1,   /* TensorError::InvalidShape */
+  MRI_ERR_SHAPE_MISMATCH = 2,  /* TensorError::ShapeMismatch */
+  MRI_ERR_CUDA = 3,            /* CUDA runtime / driver failure, no device */
+  MRI_ERR_COMM = 4,            /* NCCL failure (sharded calls) */
+  MRI_ERR_TIMEOUT = 5,         /* a bounded device-side wait gave up */
+  MRI_ERR_INVALID_ARGUMENT = 6 /* null handle or pointer, bad enum value */
+};
+
+/* Activation-quantization granularity. */
+enum mri_granularity {
+  MRI_PER_TENSOR = 0, /* one scale for all M*K values: quantize_symmetric over
+                         the whole [M,K] buffer (int8.rs:141, forward_int8.rs:94) */
+  MRI_PER_ROW = 1     /* one scale per row (q8_direct.rs:260-264) */
+};
+
+typedef struct mri_ctx mri_ctx;
+typedef struct mri_qmatrix mri_qmatrix;         /* QuantizedMatrix, per_channel.rs:29-40 */
+typedef struct mri_q8_0_matrix mri_q8_0_matrix; /* Q8_0WeightMatrix, q8_direct.rs:60-69 */
+typedef struct mri_q4_0_matrix mri_q4_0_matrix; /* Q4_0 bytes + (n_out, k), q4_0.rs:94-99 */
+
+MRI_API int mri_abi_version(void);
+/* Reason text of the calling thread's last failed call ("" if none). */
+MRI_API const char* mri_last_error(void);
+
+/* ── context ──────────────────────────────────────────────────────────────── */
+/* Creates a context on `device` with its own non-blocking stream. */
+MRI_API int mri_ctx_create(int device, mri_ctx** out);
+/* Same, but enqueues on the caller's `cudaStream_t` (not owned). */
+MRI_API int mri_ctx_create_on_stream(int device, void* cuda_stream, mri_ctx** out);
+MRI_API int mri_ctx_destroy(mri_ctx* ctx);
+MRI_API int mri_ctx_synchronize(mri_ctx* ctx);
+MRI_API void* mri_ctx_stream(mri_ctx* ctx);
+/* Reads and clears the device-side status word that bounded waits write
+ * (MRI_OK or MRI_ERR_TIMEOUT).  Synchronizes the stream. */
+MRI_API int mri_ctx_check_device_status(mri_ctx* ctx);
+/* Number of kernels this context has launched (for launch accounting). */
+MRI_API uint64_t mri_ctx_launch_count(const mri_ctx* ctx);
+
+/* ── device-resident weights ──────────────────────────────────────────────── */
+/* QuantizedMatrix { data: [n_out,k_in] i8 row-major, scales: [n_out] f32 }
+ * (per_channel.rs:29-40).  Host pointers; synchronous upload. */
+MRI_API int mri_qmatrix_upload(mri_ctx* ctx, const int8_t* data, const float* scales,
+                       size_t n_out, size_t k_in, mri_qmatrix** out);
+/* Uploads rows [row_begin, row_end) only: the column shard a rank holds when
+ * the output dimension N is split across GPUs. */
+MRI_API int mri_qmatrix_upload_rows(mri_ctx* ctx, const int8_t* data, const float* scales,
+                            size_t n_out, size_t k_in, size_t row_begin, size_t row_end,
+                            mri_qmatrix** out);
+MRI_API int mri_qmatrix_free(mri_qmatrix* w);
+MRI_API int mri_qmatrix_dims(const mri_qmatrix* w, size_t* n_out, size_t* k_in);
+
+/* Q8_0WeightMatrix::from_raw_bytes (q8_direct.rs:80-107): k_in % 32 == 0 and
+ * len == n_out*(k_in/32)*34, else MRI_ERR_INVALID_SHAPE. */
+MRI_API int mri_q8_0_upload(mri_ctx* ctx, const uint8_t* bytes, size_t len, size_t n_out,
+                    size_t k_in, mri_q8_0_matrix** out);
+MRI_API int mri_q8_0_free(mri_q8_0_matrix* w);
+/* Q4_0 byte slice of a [n_out, k] matrix (q4_0.rs:8-21); the same k % 32 and
+ * byte-length checks as matmul_q4_0_dequant (q4_0.rs:121-140). */
+MRI_API int mri_q4_0_upload(mri_ctx* ctx, const uint8_t* bytes, size_t len, size_t n_out,
+                    size_t k, mri_q4_0_matrix** out);
+MRI_API int mri_q4_0_free(mri_q4_0_matrix* w);
+
+/* ── activation quantizer (quantize_symmetric, symmetric.rs:42-57) ────────── */
+/* x_dev [m,k] f32 -> q_dev [m,k] i8 and scale_dev (1 value for PER_TENSOR,
+ * m values for PER_ROW). */
+MRI_API int mri_quantize_symmetric(mri_ctx* ctx, const float* x_dev, size_t m, size_t k,
+                           int granularity, int8_t* q_dev, float* scale_dev);
+
+/* ── INT8 x INT8 -> INT32 -> f32 (int8.rs / int8_avx2.rs / parallel.rs) ──── */
+/* matmul_int8(act_q, act_scale, weights, m) (int8.rs:61-98; same contract as
+ * matmul_int8_avx2 int8_avx2.rs:174, matmul_int8_neon int8_neon.rs:158 and
+ * matmul_int8_parallel parallel.rs:308).  act_len != m*k_in -> INVALID_SHAPE.
+ * out_dev [m,n] f32; acc_dev (nullable) receives the i32 accumulators. */
+MRI_API int mri_matmul_int8(mri_ctx* ctx, const int8_t* act_q_dev, size_t act_len, float act_scale,
+                    const mri_qmatrix* w, size_t m, float* out_dev, int32_t* acc_dev);
+/* Same, with the activation scale(s) already on the device: one value, or m
+ * values when scale_per_row != 0. */
+MRI_API int mri_matmul_int8_dscale(mri_ctx* ctx, const int8_t* act_q_dev, size_t act_len,
+                           const float* act_scale_dev, int scale_per_row,
+                           const mri_qmatrix* w, size_t m, float* out_dev, int32_t* acc_dev);
+/* matmul_int8_from_f32(input, weights) (int8.rs:113-143): k != k_in ->
+ * SHAPE_MISMATCH; per-tensor quantization of the whole [m,k] input, fused. */
+MRI_API int mri_matmul_int8_from_f32(mri_ctx* ctx, const float* x_dev, size_t m, size_t k,
+                             const mri_qmatrix* w, float* out_dev);
+/* Explicit-granularity variant (MRI_PER_ROW quantizes each input row on its
+ * own, the form BASELINE's prefill config describes). */
+MRI_API int mri_matmul_int8_from_f32_g(mri_ctx* ctx, const float* x_dev, size_t m, size_t k,
+                               int granularity, const mri_qmatrix* w, float* out_dev);
+
+/* ── block-quantized products ─────────────────────────────────────────────── */
+/* matmul_q8_0_direct(input, weights) (q8_direct.rs:229-289): per-row
+ * activation quantization, per-block i32 dot, f32 accumulation over blocks
+ * in block order (bit-exact with the reference). */
+MRI_API int mri_matmul_q8_0_direct(mri_ctx* ctx, const float* x_dev, size_t m, size_t k,
+                           const mri_q8_0_matrix* w, float* out_dev);
+/* matmul_q4_0_dequant(input, weight_q4, n_out, k) (q4_0.rs:94-181): f32 x
+ * dequantized nibbles, f32 accumulation (tolerance, not bit-exact: the sum
+ * is reassociated across the warp). */
+MRI_API int mri_matmul_q4_0_dequant(mri_ctx* ctx, const float* x_dev, size_t m, size_t k,
+                            const mri_q4_0_matrix* w, float* out_dev);
+
+/* ── host-buffer drop-ins (synchronous) ───────────────────────────────────── */
+MRI_API int mri_host_quantize_symmetric(mri_ctx* ctx, const float* x, size_t m, size_t k,
+                                int granularity, int8_t* q, float* scale);
+MRI_API int mri_host_matmul_int8(mri_ctx* ctx, const int8_t* act_q, size_t act_len, float act_scale,
+                         const mri_qmatrix* w, size_t m, float* out, int32_t* acc);
+MRI_API int mri_host_matmul_int8_from_f32(mri_ctx* ctx, const float* x, size_t m, size_t k,
+                                  const mri_qmatrix* w, float* out);
+MRI_API int mri_host_matmul_q8_0_direct(mri_ctx* ctx, const float* x, size_t m, size_t k,
+                                const mri_q8_0_matrix* w, float* out);
+MRI_API int mri_host_matmul_q4_0_dequant(mri_ctx* ctx, const float* x, size_t m, size_t k,
+                                 const mri_q4_0_matrix* w, float* out);
+
+/* ── diagnostics ──────────────────────────────────────────────────────────── */
+/* Kernel path chosen for an INT8 product of this shape:
+ * 0 = streaming GEMV (TMA bulk), 1 = generic GEMV, 2 = tensor-core GEMM. */
+MRI_API int mri_int8_path(mri_ctx* ctx, size_t m, size_t n, size_t k);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MRI_GPU_H */

@@ -1,0 +1,398 @@
+"""mini-rust-inference B200: the quantized-matmul hot path on sm_100a.
+
+Host-side mirror of the reference's operator API (Rust crate
+`llm-inference-engine`, module `ops::matmul` and `quant::int8`), backed by the
+C ABI of libmri_gpu.so (include/mri_gpu.h).  Names, argument meaning and error
+classes follow the reference:
+
+  quantize_symmetric(values)                 quant/int8/symmetric.rs:42
+  quantize_per_channel(weights, n_out, k_in) quant/int8/per_channel.rs:98
+  matmul_int8(act_q, act_scale, weights, m)  ops/matmul/int8.rs:61
+  matmul_int8_from_f32(input, weights)       ops/matmul/int8.rs:113
+  matmul_int8_avx2 / _neon / _parallel       int8_avx2.rs:174, int8_neon.rs:158, parallel.rs:308
+  matmul_q8_0_direct(input, weights)         ops/matmul/q8_direct.rs:229
+  matmul_q4_0_dequant(input, w_q4, n_out, k) ops/matmul/q4_0.rs:94
+
+Errors raise InvalidShape / ShapeMismatch (TensorError variants,
+src/tensor/error.rs:7-29).  Inputs may be numpy arrays (host; synchronous
+calls with H2D/D2H inside) or CUDA torch tensors (device; asynchronous on the
+context's stream).  There is no CPU compute path.
+
+Import with importlib (the directory name is not an identifier):
+    mri = importlib.import_module("mini-rust-inference_b200")
+"""
+import ctypes
+import threading
+
+import numpy as np
+
+from . import _lib
+from . import formats
+
+__all__ = [
+    "TensorError", "InvalidShape", "ShapeMismatch", "CudaError", "DeviceTimeout",
+    "Context", "default_context", "QuantizedMatrix", "Q8_0WeightMatrix", "Q4_0Matrix",
+    "quantize_symmetric", "quantize_symmetric_rows", "quantize_per_channel",
+    "matmul_int8", "matmul_int8_avx2", "matmul_int8_neon", "matmul_int8_parallel",
+    "matmul_int8_from_f32", "matmul_q8_0_direct", "matmul_q4_0_dequant", "formats",
+]
+
+
+class TensorError(Exception):
+    kind = "TensorError"
+
+
+class InvalidShape(TensorError):
+    kind = "InvalidShape"
+
+
+class ShapeMismatch(TensorError):
+    kind = "ShapeMismatch"
+
+
+class CudaError(RuntimeError):
+    kind = "CudaError"
+
+
+class DeviceTimeout(RuntimeError):
+    kind = "Timeout"
+
+
+class CommError(RuntimeError):
+    kind = "CommError"
+
+
+_ERRORS = {
+    _lib.INVALID_SHAPE: InvalidShape,
+    _lib.SHAPE_MISMATCH: ShapeMismatch,
+    _lib.CUDA_ERROR: CudaError,
+    _lib.COMM_ERROR: CommError,
+    _lib.TIMEOUT: DeviceTimeout,
+    _lib.INVALID_ARGUMENT: ValueError,
+}
+
+
+def _check(rc):
+    if rc != _lib.OK:
+        raise _ERRORS.get(rc, RuntimeError)(_lib.last_error())
+
+
+def _vp(arr):
+    if arr is None:
+        return None
+    if isinstance(arr, np.ndarray):
+        return arr.ctypes.data_as(ctypes.c_void_p)
+    return ctypes.c_void_p(arr.data_ptr())
+
+
+def _is_cuda_tensor(x):
+    return hasattr(x, "is_cuda") and bool(getattr(x, "is_cuda"))
+
+
+# ── contexts ──────────────────────────────────────────────────────────────────
+
+class Context:
+    """One CUDA stream + scratch on one device (mri_ctx)."""
+
+    def __init__(self, device=0, stream=None):
+        lib = _lib.load()
+        h = ctypes.c_void_p()
+        if stream is None:
+            _check(lib.mri_ctx_create(int(device), ctypes.byref(h)))
+        else:
+            handle = stream.cuda_stream if hasattr(stream, "cuda_stream") else int(stream)
+            _check(lib.mri_ctx_create_on_stream(int(device), ctypes.c_void_p(handle), ctypes.byref(h)))
+        self.handle = h
+        self.device = int(device)
+        self._lib = lib
+
+    def close(self):
+        if self.handle:
+            self._lib.mri_ctx_destroy(self.handle)
+            self.handle = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001 - interpreter shutdown
+            pass
+
+    def synchronize(self):
+        _check(self._lib.mri_ctx_synchronize(self.handle))
+
+    def check_device_status(self):
+        _check(self._lib.mri_ctx_check_device_status(self.handle))
+
+    @property
+    def launch_count(self):
+        return int(self._lib.mri_ctx_launch_count(self.handle))
+
+    @property
+    def stream_handle(self):
+        return int(self._lib.mri_ctx_stream(self.handle) or 0)
+
+    def int8_path(self, m, n, k):
+        return int(self._lib.mri_int8_path(self.handle, m, n, k))
+
+
+_tls = threading.local()
+
+
+def default_context(device=0):
+    """Per-thread, per-device context with its own stream."""
+    ctxs = getattr(_tls, "ctxs", None)
+    if ctxs is None:
+        ctxs = _tls.ctxs = {}
+    if device not in ctxs:
+        ctxs[device] = Context(device)
+    return ctxs[device]
+
+
+def _ctx_for(ctx, x=None):
+    if ctx is not None:
+        return ctx
+    dev = x.device.index if _is_cuda_tensor(x) else 0
+    return default_context(dev or 0)
+
+
+# ── weights ───────────────────────────────────────────────────────────────────
+
+class QuantizedMatrix:
+    """Device-resident QuantizedMatrix {data [n_out,k_in] i8, scales [n_out] f32}
+    (quant/int8/per_channel.rs:29-40).  `rows=(begin, end)` uploads only that
+    row range (an N-shard)."""
+
+    def __init__(self, data, scales, n_out, k_in, ctx=None, rows=None, keep_host=True):
+        self.ctx = ctx or default_context()
+        data = np.ascontiguousarray(data, dtype=np.int8).reshape(-1)
+        scales = np.ascontiguousarray(scales, dtype=np.float32).reshape(-1)
+        if data.size != n_out * k_in or scales.size != n_out:
+            raise InvalidShape(f"QuantizedMatrix: data.len()={data.size}, scales.len()={scales.size} "
+                               f"for n_out={n_out}, k_in={k_in}")
+        begin, end = rows if rows is not None else (0, n_out)
+        h = ctypes.c_void_p()
+        _check(self.ctx._lib.mri_qmatrix_upload_rows(self.ctx.handle, _vp(data), _vp(scales), n_out,
+                                                     k_in, begin, end, ctypes.byref(h)))
+        self.handle = h
+        self.n_out = end - begin
+        self.k_in = k_in
+        self.row_range = (begin, end)
+        if keep_host:
+            self.data = data.reshape(n_out, k_in)[begin:end].reshape(-1)
+            self.scales = scales[begin:end]
+
+    def __del__(self):
+        try:
+            if self.handle:
+                self.ctx._lib.mri_qmatrix_free(self.handle)
+        except Exception:  # noqa: BLE001
+            pass
+
+    def row(self, n):
+        """per_channel.rs:45-48"""
+        return self.data[n * self.k_in:(n + 1) * self.k_in]
+
+    def dequantize_row(self, n):
+        return self.row(n).astype(np.float32) * self.scales[n]
+
+    def dequantize_all(self):
+        return (self.data.reshape(self.n_out, self.k_in).astype(np.float32) * self.scales[:, None]).reshape(-1)
+
+
+class Q8_0WeightMatrix:
+    """Device-resident raw Q8_0 bytes (ops/matmul/q8_direct.rs:60-197)."""
+
+    def __init__(self, handle, data, n_out, k_in, ctx):
+        self.handle, self.data, self.n_out, self.k_in, self.ctx = handle, data, n_out, k_in, ctx
+        self.n_blocks = k_in // 32
+
+    @classmethod
+    def from_raw_bytes(cls, data, n_out, k_in, ctx=None):
+        """q8_direct.rs:80-107 (InvalidShape on k % 32 or byte length)."""
+        ctx = ctx or default_context()
+        d = np.frombuffer(bytes(data), dtype=np.uint8) if isinstance(data, (bytes, bytearray)) \
+            else np.ascontiguousarray(data, dtype=np.uint8).reshape(-1)
+        h = ctypes.c_void_p()
+        _check(ctx._lib.mri_q8_0_upload(ctx.handle, _vp(d), d.size, n_out, k_in, ctypes.byref(h)))
+        return cls(h, d, n_out, k_in, ctx)
+
+    @classmethod
+    def from_f32_tensor(cls, t, ctx=None):
+        """q8_direct.rs:118-158"""
+        t = np.asarray(t, dtype=np.float32)
+        if t.ndim != 2:
+            raise InvalidShape(f"Q8_0WeightMatrix::from_f32_tensor: expected 2-D, got {t.ndim}D")
+        n_out, k_in = t.shape
+        if k_in % 32:
+            raise InvalidShape(f"Q8_0WeightMatrix::from_f32_tensor: k_in={k_in} not a multiple of 32")
+        return cls.from_raw_bytes(formats.quantize_q8_0(t, n_out, k_in), n_out, k_in, ctx)
+
+    def block_scale(self, n, b):
+        off = (n * self.n_blocks + b) * 34
+        return formats.f16_to_f32(self.data[off:off + 2].copy().view(np.uint16))[0]
+
+    def dequantize_all(self):
+        return formats.dequantize_q8_0(self.data)
+
+    def __del__(self):
+        try:
+            if self.handle:
+                self.ctx._lib.mri_q8_0_free(self.handle)
+        except Exception:  # noqa: BLE001
+            pass
+
+
+class Q4_0Matrix:
+    """Device-resident Q4_0 bytes of a [n_out, k] weight (q4_0.rs:8-21)."""
+
+    def __init__(self, data, n_out, k, ctx=None):
+        self.ctx = ctx or default_context()
+        d = np.frombuffer(bytes(data), dtype=np.uint8) if isinstance(data, (bytes, bytearray)) \
+            else np.ascontiguousarray(data, dtype=np.uint8).reshape(-1)
+        h = ctypes.c_void_p()
+        _check(self.ctx._lib.mri_q4_0_upload(self.ctx.handle, _vp(d), d.size, n_out, k, ctypes.byref(h)))
+        self.handle, self.data, self.n_out, self.k = h, d, n_out, k
+
+    def __del__(self):
+        try:
+            if self.handle:
+                self.ctx._lib.mri_q4_0_free(self.handle)
+        except Exception:  # noqa: BLE001
+            pass
+
+
+# ── quantizers ────────────────────────────────────────────────────────────────
+
+def _host_quantize(values, m, k, granularity, ctx):
+    ctx = ctx or default_context()
+    x = np.ascontiguousarray(values, dtype=np.float32).reshape(-1)
+    q = np.empty(m * k, dtype=np.int8)
+    s = np.empty(max(m, 1) if granularity == _lib.PER_ROW else 1, dtype=np.float32)
+    _check(ctx._lib.mri_host_quantize_symmetric(ctx.handle, _vp(x), m, k, granularity, _vp(q), _vp(s)))
+    return q, s
+
+
+def quantize_symmetric(values, ctx=None):
+    """symmetric.rs:42-57 -> (q: int8[len], scale: float32)."""
+    v = np.asarray(values, dtype=np.float32).reshape(-1)
+    q, s = _host_quantize(v, 1, v.size, _lib.PER_TENSOR, ctx)
+    return q, np.float32(s[0])
+
+
+def quantize_symmetric_rows(values, m, k, ctx=None):
+    """quantize_symmetric applied to each row (q8_direct.rs:260-264)."""
+    q, s = _host_quantize(values, m, k, _lib.PER_ROW, ctx)
+    return q, s[:m]
+
+
+def quantize_per_channel(weights, n_out, k_in, ctx=None, rows=None):
+    """per_channel.rs:98-128, run on the GPU (per-row absmax quantization has
+    the same formula), returning the device-resident matrix."""
+    w = np.asarray(weights, dtype=np.float32).reshape(-1)
+    assert w.size == n_out * k_in, f"weights.len()={w.size} != n_out*k_in={n_out * k_in}"
+    q, s = _host_quantize(w, n_out, k_in, _lib.PER_ROW, ctx)
+    return QuantizedMatrix(q, s[:n_out], n_out, k_in, ctx=ctx, rows=rows)
+
+
+# ── products ──────────────────────────────────────────────────────────────────
+
+def _as_2d(input_, fn):
+    if _is_cuda_tensor(input_):
+        if input_.dim() != 2:
+            raise InvalidShape(f"{fn}: input must be 2-D, got {input_.dim()}D (shape {list(input_.shape)})")
+        return input_.contiguous()
+    a = np.asarray(input_, dtype=np.float32)
+    if a.ndim != 2:
+        raise InvalidShape(f"{fn}: input must be 2-D, got {a.ndim}D (shape {list(a.shape)})")
+    return np.ascontiguousarray(a)
+
+
+def _new_out(like, m, n):
+    if _is_cuda_tensor(like):
+        import torch
+        return torch.empty((m, n), dtype=torch.float32, device=like.device)
+    return np.empty((m, n), dtype=np.float32)
+
+
+def matmul_int8(act_q, act_scale, weights, m, acc_out=None):
+    """ops/matmul/int8.rs:61-98.  Returns f32 [m, n]; `acc_out` (optional,
+    int32 [m, n], same residency as act_q) receives the INT32 accumulators."""
+    ctx = weights.ctx
+    n = weights.n_out
+    if _is_cuda_tensor(act_q):
+        out = _new_out(act_q, m, n)
+        _check(ctx._lib.mri_matmul_int8(ctx.handle, _vp(act_q), act_q.numel(), float(act_scale),
+                                        weights.handle, m, _vp(out), _vp(acc_out)))
+        return out
+    a = np.ascontiguousarray(act_q, dtype=np.int8).reshape(-1)
+    out = np.empty((m, n), dtype=np.float32)
+    _check(ctx._lib.mri_host_matmul_int8(ctx.handle, _vp(a), a.size, float(act_scale), weights.handle,
+                                         m, _vp(out), _vp(acc_out)))
+    return out
+
+
+# One GPU kernel serves every reference variant (scalar, AVX2, NEON, rayon).
+matmul_int8_avx2 = matmul_int8
+matmul_int8_neon = matmul_int8
+matmul_int8_parallel = matmul_int8
+
+
+def matmul_int8_from_f32(input, weights, granularity=_lib.PER_TENSOR):  # noqa: A002 - reference name
+    """ops/matmul/int8.rs:113-143 (per-tensor activation scale by default)."""
+    x = _as_2d(input, "matmul_int8_from_f32")
+    m, k = x.shape
+    if k != weights.k_in:
+        raise ShapeMismatch(f"expected [{m}, {weights.k_in}], got [{m}, {k}]")
+    ctx = weights.ctx
+    out = _new_out(x, m, weights.n_out)
+    if _is_cuda_tensor(x):
+        _check(ctx._lib.mri_matmul_int8_from_f32_g(ctx.handle, _vp(x), m, k, granularity,
+                                                   weights.handle, _vp(out)))
+    elif granularity == _lib.PER_TENSOR:
+        _check(ctx._lib.mri_host_matmul_int8_from_f32(ctx.handle, _vp(x), m, k, weights.handle, _vp(out)))
+    else:
+        q, s = quantize_symmetric_rows(x, m, k, ctx)
+        import torch  # per-row host path goes through device buffers
+        dq = torch.from_numpy(q).cuda(ctx.device)
+        ds = torch.from_numpy(s).cuda(ctx.device)
+        dout = torch.empty((m, weights.n_out), dtype=torch.float32, device=f"cuda:{ctx.device}")
+        _check(ctx._lib.mri_matmul_int8_dscale(ctx.handle, _vp(dq), m * k, _vp(ds), 1, weights.handle,
+                                               m, _vp(dout), None))
+        ctx.synchronize()
+        out = dout.cpu().numpy()
+    return out
+
+
+def matmul_q8_0_direct(input, weights):  # noqa: A002
+    """ops/matmul/q8_direct.rs:229-289 (bit-exact)."""
+    x = _as_2d(input, "matmul_q8_0_direct")
+    m, k = x.shape
+    if k != weights.k_in:
+        raise ShapeMismatch(f"expected [{m}, {weights.k_in}], got [{m}, {k}]")
+    ctx = weights.ctx
+    out = _new_out(x, m, weights.n_out)
+    fn = ctx._lib.mri_matmul_q8_0_direct if _is_cuda_tensor(x) else ctx._lib.mri_host_matmul_q8_0_direct
+    _check(fn(ctx.handle, _vp(x), m, k, weights.handle, _vp(out)))
+    return out
+
+
+def matmul_q4_0_dequant(input, weight_q4, n_out, k, ctx=None):  # noqa: A002
+    """ops/matmul/q4_0.rs:94-181.  `weight_q4` is the raw byte slice (uploaded
+    for this call) or a Q4_0Matrix already on the device.  Checks run in the
+    reference's order: 2-D, K mismatch, k % 32, byte length."""
+    x = _as_2d(input, "matmul_q4_0_dequant")
+    m, k_in = x.shape
+    if k_in != k:
+        raise ShapeMismatch(f"expected [{m}, {k}], got [{m}, {k_in}]")
+    w = weight_q4 if isinstance(weight_q4, Q4_0Matrix) else Q4_0Matrix(weight_q4, n_out, k, ctx=ctx)
+    if (w.n_out, w.k) != (n_out, k):
+        raise InvalidShape(f"Q4_0Matrix is [{w.n_out}, {w.k}], call says [{n_out}, {k}]")
+    c = w.ctx
+    out = _new_out(x, m, n_out)
+    fn = c._lib.mri_matmul_q4_0_dequant if _is_cuda_tensor(x) else c._lib.mri_host_matmul_q4_0_dequant
+    _check(fn(c.handle, _vp(x), m, k, w.handle, _vp(out)))
+    return out
+
+
+def library_path():
+    return _lib.library_path()

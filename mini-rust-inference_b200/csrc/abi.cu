@@ -1,0 +1,641 @@
+// abi.cu — the C ABI (include/mri_gpu.h): contexts, device-resident weight
+// handles, argument validation with the reference's error classes, and
+// dispatch to the kernels.  No CPU compute path exists here: every product
+// runs on the GPU or the call fails.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "internal.h"
+#include "mri_gpu.h"
+
+using mri::ActArgs;
+
+struct mri_ctx {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  bool own_stream = false;
+  mri::DeviceInfo dev;
+  int* d_status = nullptr;
+  uint8_t* scratch = nullptr;
+  size_t scratch_bytes = 0;
+  mri::LaunchStats ls;
+};
+
+struct mri_qmatrix {
+  int device;
+  int8_t* data;
+  float* scales;
+  size_t n_out, k_in;
+};
+
+struct mri_q8_0_matrix {
+  int device;
+  uint8_t* data;
+  size_t n_out, k_in;
+};
+
+struct mri_q4_0_matrix {
+  int device;
+  uint8_t* data;
+  size_t n_out, k;
+};
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* where) {
+  return fail(MRI_ERR_CUDA, "%s: %s", where, cudaGetErrorString(e));
+}
+
+#define MRI_CUDA_TRY(expr)                                   \
+  do {                                                       \
+    cudaError_t _e = (expr);                                 \
+    if (_e != cudaSuccess) return cuda_fail(_e, #expr);      \
+  } while (0)
+
+// Device allocations of weights carry this many bytes of zeroed slack: bulk
+// copies round their size up to 16 bytes and may read past the last row.
+constexpr size_t kWeightPad = 256;
+
+int use_device(int device) {
+  int cur = -1;
+  cudaError_t e = cudaGetDevice(&cur);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (cur != device) MRI_CUDA_TRY(cudaSetDevice(device));
+  return MRI_OK;
+}
+
+int enter(mri_ctx* ctx) {
+  if (!ctx) return fail(MRI_ERR_INVALID_ARGUMENT, "null context");
+  g_last_error.clear();
+  return use_device(ctx->device);
+}
+
+// Scratch is one growing device buffer per context, carved by the callers.
+int ensure_scratch(mri_ctx* ctx, size_t bytes) {
+  if (bytes <= ctx->scratch_bytes) return MRI_OK;
+  if (ctx->scratch) {
+    MRI_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    MRI_CUDA_TRY(cudaFree(ctx->scratch));
+    ctx->scratch = nullptr;
+    ctx->scratch_bytes = 0;
+  }
+  const size_t sz = std::max<size_t>(bytes, 1 << 20);
+  MRI_CUDA_TRY(cudaMalloc(&ctx->scratch, sz));
+  ctx->scratch_bytes = sz;
+  return MRI_OK;
+}
+
+size_t al(size_t v) { return (v + 255) / 256 * 256; }
+
+template <typename T>
+int upload_bytes(const T* host, size_t count, T** dev) {
+  const size_t bytes = count * sizeof(T);
+  void* p = nullptr;
+  MRI_CUDA_TRY(cudaMalloc(&p, bytes + kWeightPad));
+  cudaError_t e = cudaMemset(p, 0, bytes + kWeightPad);
+  if (e == cudaSuccess && bytes) e = cudaMemcpy(p, host, bytes, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return cuda_fail(e, "weight upload");
+  }
+  *dev = static_cast<T*>(p);
+  return MRI_OK;
+}
+
+// ── INT8 dispatch ────────────────────────────────────────────────────────────
+// `act` describes the full [m, K] activation set.  Small m uses the fused
+// streaming GEMV; larger m quantizes once (per-tensor scale over all rows,
+// as the reference does) and runs the tensor-core GEMM or, where that does
+// not apply, the GEMV over 8-row chunks.
+int run_int8(mri_ctx* ctx, ActArgs act, const mri_qmatrix* w, size_t m, float* out,
+             int32_t* acc) {
+  const size_t N = w->n_out, K = w->k_in;
+  if (m == 0 || N == 0) return MRI_OK;
+  cudaStream_t st = ctx->stream;
+  const bool f32_in = act.mode == mri::ACT_F32_PER_TENSOR || act.mode == mri::ACT_F32_PER_ROW;
+
+  if (m <= 8 && mri::gemv_i8_tma_supported(ctx->dev, static_cast<int>(m), K)) {
+    MRI_CUDA_TRY(mri::launch_gemv_i8_tma(ctx->dev, st, static_cast<int>(m), w->data, w->scales, N,
+                                         K, act, out, acc, ctx->d_status, &ctx->ls));
+    return MRI_OK;
+  }
+
+  // Materialize quantized activations (and device scales) if needed.
+  const int8_t* xq = act.xq;
+  const float* sdev = act.scale_dev;
+  int per_row = act.mode == mri::ACT_I8_DEV_ROW_SCALE || act.mode == mri::ACT_F32_PER_ROW;
+  if (f32_in || act.mode == mri::ACT_I8_HOST_SCALE) {
+    const size_t need = al(m * sizeof(float)) * 2 + al(m * K);
+    if (int rc = ensure_scratch(ctx, need)) return rc;
+    float* amax = reinterpret_cast<float*>(ctx->scratch);
+    float* scales = reinterpret_cast<float*>(ctx->scratch + al(m * sizeof(float)));
+    int8_t* q = reinterpret_cast<int8_t*>(ctx->scratch + 2 * al(m * sizeof(float)));
+    if (f32_in) {
+      MRI_CUDA_TRY(mri::launch_quantize(ctx->dev, st, act.x, m, K, per_row, q, scales, amax,
+                                        &ctx->ls));
+      xq = q;
+    } else {
+      MRI_CUDA_TRY(cudaMemcpyAsync(scales, &act.scale_host, sizeof(float),
+                                   cudaMemcpyHostToDevice, st));
+      per_row = 0;
+    }
+    sdev = scales;
+  }
+
+  if (mri::gemm_i8_tc_supported(ctx->dev, m, N, K)) {
+    MRI_CUDA_TRY(mri::launch_gemm_i8_tc(ctx->dev, st, xq, sdev, per_row, w->data, w->scales, m, N,
+                                        K, out, acc, ctx->d_status, &ctx->ls));
+    return MRI_OK;
+  }
+  for (size_t m0 = 0; m0 < m; m0 += 8) {
+    const int mc = static_cast<int>(std::min<size_t>(8, m - m0));
+    ActArgs a;
+    a.xq = xq + m0 * K;
+    a.mode = per_row ? mri::ACT_I8_DEV_ROW_SCALE : mri::ACT_I8_DEV_SCALE;
+    a.scale_dev = per_row ? sdev + m0 : sdev;
+    float* o = out + m0 * N;
+    int32_t* ac = acc ? acc + m0 * N : nullptr;
+    if (mri::gemv_i8_tma_supported(ctx->dev, mc, K)) {
+      MRI_CUDA_TRY(mri::launch_gemv_i8_tma(ctx->dev, st, mc, w->data, w->scales, N, K, a, o, ac,
+                                           ctx->d_status, &ctx->ls));
+    } else {
+      MRI_CUDA_TRY(mri::launch_gemv_i8_generic(ctx->dev, st, mc, w->data, w->scales, N, K, a, o,
+                                               ac, &ctx->ls));
+    }
+  }
+  return MRI_OK;
+}
+
+int run_q8_0(mri_ctx* ctx, const float* x, size_t m, const mri_q8_0_matrix* w, float* out) {
+  const size_t N = w->n_out, K = w->k_in;
+  if (m == 0 || N == 0) return MRI_OK;
+  cudaStream_t st = ctx->stream;
+  if (K > 0 && mri::gemv_q8_0_tma_supported(ctx->dev, static_cast<int>(std::min<size_t>(m, 8)), K)) {
+    for (size_t m0 = 0; m0 < m; m0 += 8) {
+      const int mc = static_cast<int>(std::min<size_t>(8, m - m0));
+      MRI_CUDA_TRY(mri::launch_gemv_q8_0_tma(ctx->dev, st, mc, w->data, N, K, x + m0 * K,
+                                             out + m0 * N, ctx->d_status, &ctx->ls));
+    }
+    return MRI_OK;
+  }
+  const size_t need = al(m * sizeof(float)) * 2 + al(m * K);
+  if (int rc = ensure_scratch(ctx, need)) return rc;
+  float* amax = reinterpret_cast<float*>(ctx->scratch);
+  float* scales = reinterpret_cast<float*>(ctx->scratch + al(m * sizeof(float)));
+  int8_t* q = reinterpret_cast<int8_t*>(ctx->scratch + 2 * al(m * sizeof(float)));
+  MRI_CUDA_TRY(mri::launch_quantize(ctx->dev, st, x, m, K, 1, q, scales, amax, &ctx->ls));
+  for (size_t m0 = 0; m0 < m; m0 += 8) {
+    const int mc = static_cast<int>(std::min<size_t>(8, m - m0));
+    MRI_CUDA_TRY(mri::launch_gemv_q8_0_generic(ctx->dev, st, mc, w->data, N, K, q + m0 * K,
+                                               scales + m0, out + m0 * N, &ctx->ls));
+  }
+  return MRI_OK;
+}
+
+int run_q4_0(mri_ctx* ctx, const float* x, size_t m, const mri_q4_0_matrix* w, float* out) {
+  const size_t N = w->n_out, K = w->k;
+  if (m == 0 || N == 0) return MRI_OK;
+  cudaStream_t st = ctx->stream;
+  const bool tma = K > 0 && mri::gemv_q4_0_tma_supported(ctx->dev, static_cast<int>(std::min<size_t>(m, 8)), K);
+  for (size_t m0 = 0; m0 < m; m0 += 8) {
+    const int mc = static_cast<int>(std::min<size_t>(8, m - m0));
+    if (tma) {
+      MRI_CUDA_TRY(mri::launch_gemv_q4_0_tma(ctx->dev, st, mc, w->data, N, K, x + m0 * K,
+                                             out + m0 * N, ctx->d_status, &ctx->ls));
+    } else {
+      MRI_CUDA_TRY(mri::launch_gemv_q4_0_generic(ctx->dev, st, mc, w->data, N, K, x + m0 * K,
+                                                 out + m0 * N, &ctx->ls));
+    }
+  }
+  return MRI_OK;
+}
+
+int check_act_len(const char* fn, size_t act_len, size_t m, size_t k) {
+  // int8.rs:68-78 / parallel.rs:315-325
+  if (act_len != m * k)
+    return fail(MRI_ERR_INVALID_SHAPE, "%s: act_q.len()=%zu != m*k=%zu*%zu=%zu", fn, act_len, m, k,
+                m * k);
+  return MRI_OK;
+}
+
+int check_k(const char* fn, size_t m, size_t k, size_t k_w) {
+  // int8.rs:127-132, q8_direct.rs:241-246, q4_0.rs:114-119
+  if (k != k_w)
+    return fail(MRI_ERR_SHAPE_MISMATCH, "%s: ShapeMismatch expected [%zu, %zu], got [%zu, %zu]", fn,
+                m, k_w, m, k);
+  return MRI_OK;
+}
+
+// Host-call staging: [x | act_q] [out] [acc] in scratch after the quantizer area.
+struct HostStage {
+  uint8_t* in;
+  float* out;
+  int32_t* acc;
+};
+
+int host_stage(mri_ctx* ctx, size_t in_bytes, size_t out_bytes, size_t acc_bytes, size_t quant_m,
+               size_t quant_k, HostStage* hs) {
+  const size_t quant = al(quant_m * sizeof(float)) * 2 + al(quant_m * quant_k);
+  const size_t need = quant + al(in_bytes) + al(out_bytes) + al(acc_bytes);
+  if (int rc = ensure_scratch(ctx, need)) return rc;
+  hs->in = ctx->scratch + quant;
+  hs->out = reinterpret_cast<float*>(hs->in + al(in_bytes));
+  hs->acc = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(hs->out) + al(out_bytes));
+  return MRI_OK;
+}
+
+// The quantizer area at the front of scratch must not overlap the host
+// staging area, so host calls reserve it explicitly (host_stage quant_*),
+// and run_int8/run_q8_0 carve from offset 0 within that reservation.
+
+}  // namespace
+
+extern "C" {
+
+int mri_abi_version(void) { return MRI_ABI_VERSION; }
+
+const char* mri_last_error(void) { return g_last_error.c_str(); }
+
+static int ctx_create(int device, void* stream, bool own, mri_ctx** out) {
+  if (!out) return fail(MRI_ERR_INVALID_ARGUMENT, "null output pointer");
+  *out = nullptr;
+  g_last_error.clear();
+  int count = 0;
+  cudaError_t e = cudaGetDeviceCount(&count);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceCount");
+  if (device < 0 || device >= count)
+    return fail(MRI_ERR_CUDA, "device %d not present (%d devices)", device, count);
+  MRI_CUDA_TRY(cudaSetDevice(device));
+  cudaDeviceProp prop;
+  MRI_CUDA_TRY(cudaGetDeviceProperties(&prop, device));
+  if (prop.major != 10)
+    return fail(MRI_ERR_CUDA, "device %d is sm_%d%d; this library is built for sm_100a", device,
+                prop.major, prop.minor);
+  mri_ctx* c = new mri_ctx();
+  c->device = device;
+  c->dev.device = device;
+  c->dev.sm_count = prop.multiProcessorCount;
+  c->dev.max_smem_optin = static_cast<int>(prop.sharedMemPerBlockOptin);
+  c->dev.cc_major = prop.major;
+  c->dev.cc_minor = prop.minor;
+  c->dev.l2_bytes = prop.l2CacheSize;
+  if (own) {
+    e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) {
+      delete c;
+      return cuda_fail(e, "cudaStreamCreate");
+    }
+  } else {
+    c->stream = static_cast<cudaStream_t>(stream);
+  }
+  c->own_stream = own;
+  e = cudaMalloc(&c->d_status, sizeof(int));
+  if (e == cudaSuccess) e = cudaMemset(c->d_status, 0, sizeof(int));
+  if (e != cudaSuccess) {
+    if (own) cudaStreamDestroy(c->stream);
+    delete c;
+    return cuda_fail(e, "status word");
+  }
+  *out = c;
+  return MRI_OK;
+}
+
+int mri_ctx_create(int device, mri_ctx** out) { return ctx_create(device, nullptr, true, out); }
+
+int mri_ctx_create_on_stream(int device, void* cuda_stream, mri_ctx** out) {
+  return ctx_create(device, cuda_stream, false, out);
+}
+
+int mri_ctx_destroy(mri_ctx* ctx) {
+  if (!ctx) return MRI_OK;
+  use_device(ctx->device);
+  cudaStreamSynchronize(ctx->stream);
+  if (ctx->scratch) cudaFree(ctx->scratch);
+  if (ctx->d_status) cudaFree(ctx->d_status);
+  if (ctx->own_stream) cudaStreamDestroy(ctx->stream);
+  delete ctx;
+  return MRI_OK;
+}
+
+int mri_ctx_synchronize(mri_ctx* ctx) {
+  if (int rc = enter(ctx)) return rc;
+  MRI_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+  return MRI_OK;
+}
+
+void* mri_ctx_stream(mri_ctx* ctx) { return ctx ? static_cast<void*>(ctx->stream) : nullptr; }
+
+int mri_ctx_check_device_status(mri_ctx* ctx) {
+  if (int rc = enter(ctx)) return rc;
+  int st = 0;
+  MRI_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+  MRI_CUDA_TRY(cudaMemcpy(&st, ctx->d_status, sizeof(int), cudaMemcpyDeviceToHost));
+  MRI_CUDA_TRY(cudaMemset(ctx->d_status, 0, sizeof(int)));
+  if (st != MRI_OK) return fail(st, "a device-side bounded wait timed out");
+  return MRI_OK;
+}
+
+uint64_t mri_ctx_launch_count(const mri_ctx* ctx) { return ctx ? ctx->ls.launches : 0; }
+
+// ── weights ──────────────────────────────────────────────────────────────────
+
+int mri_qmatrix_upload_rows(mri_ctx* ctx, const int8_t* data, const float* scales, size_t n_out,
+                            size_t k_in, size_t row_begin, size_t row_end, mri_qmatrix** out) {
+  if (int rc = enter(ctx)) return rc;
+  if (!out) return fail(MRI_ERR_INVALID_ARGUMENT, "null output pointer");
+  if (row_begin > row_end || row_end > n_out)
+    return fail(MRI_ERR_INVALID_SHAPE, "row range [%zu, %zu) outside n_out=%zu", row_begin,
+                row_end, n_out);
+  const size_t rows = row_end - row_begin;
+  if ((rows * k_in > 0 && !data) || (rows > 0 && !scales))
+    return fail(MRI_ERR_INVALID_ARGUMENT, "null weight pointer");
+  mri_qmatrix* w = new mri_qmatrix{ctx->device, nullptr, nullptr, rows, k_in};
+  int rc = upload_bytes(data ? data + row_begin * k_in : data, rows * k_in, &w->data);
+  if (rc == MRI_OK) rc = upload_bytes(scales ? scales + row_begin : scales, rows, &w->scales);
+  if (rc != MRI_OK) {
+    if (w->data) cudaFree(w->data);
+    delete w;
+    return rc;
+  }
+  *out = w;
+  return MRI_OK;
+}
+
+int mri_qmatrix_upload(mri_ctx* ctx, const int8_t* data, const float* scales, size_t n_out,
+                       size_t k_in, mri_qmatrix** out) {
+  return mri_qmatrix_upload_rows(ctx, data, scales, n_out, k_in, 0, n_out, out);
+}
+
+int mri_qmatrix_free(mri_qmatrix* w) {
+  if (!w) return MRI_OK;
+  use_device(w->device);
+  cudaFree(w->data);
+  cudaFree(w->scales);
+  delete w;
+  return MRI_OK;
+}
+
+int mri_qmatrix_dims(const mri_qmatrix* w, size_t* n_out, size_t* k_in) {
+  if (!w) return fail(MRI_ERR_INVALID_ARGUMENT, "null matrix");
+  if (n_out) *n_out = w->n_out;
+  if (k_in) *k_in = w->k_in;
+  return MRI_OK;
+}
+
+int mri_q8_0_upload(mri_ctx* ctx, const uint8_t* bytes, size_t len, size_t n_out, size_t k_in,
+                    mri_q8_0_matrix** out) {
+  if (int rc = enter(ctx)) return rc;
+  if (!out) return fail(MRI_ERR_INVALID_ARGUMENT, "null output pointer");
+  // q8_direct.rs:81-104
+  if (k_in % 32 != 0)
+    return fail(MRI_ERR_INVALID_SHAPE, "Q8_0WeightMatrix: k_in=%zu is not a multiple of 32", k_in);
+  const size_t expected = n_out * (k_in / 32) * 34;
+  if (len != expected)
+    return fail(MRI_ERR_INVALID_SHAPE,
+                "Q8_0WeightMatrix: data.len()=%zu != expected %zu (n_out=%zu, n_blocks=%zu, "
+                "block_size=34)",
+                len, expected, n_out, k_in / 32);
+  if (len && !bytes) return fail(MRI_ERR_INVALID_ARGUMENT, "null weight pointer");
+  mri_q8_0_matrix* w = new mri_q8_0_matrix{ctx->device, nullptr, n_out, k_in};
+  if (int rc = upload_bytes(bytes, len, &w->data)) {
+    delete w;
+    return rc;
+  }
+  *out = w;
+  return MRI_OK;
+}
+
+int mri_q8_0_free(mri_q8_0_matrix* w) {
+  if (!w) return MRI_OK;
+  use_device(w->device);
+  cudaFree(w->data);
+  delete w;
+  return MRI_OK;
+}
+
+int mri_q4_0_upload(mri_ctx* ctx, const uint8_t* bytes, size_t len, size_t n_out, size_t k,
+                    mri_q4_0_matrix** out) {
+  if (int rc = enter(ctx)) return rc;
+  if (!out) return fail(MRI_ERR_INVALID_ARGUMENT, "null output pointer");
+  // q4_0.rs:121-140
+  if (k % 32 != 0)
+    return fail(MRI_ERR_INVALID_SHAPE,
+                "matmul_q4_0_dequant: k=%zu must be a multiple of 32 (Q4_0 block size)", k);
+  const size_t expected = n_out * (k / 32) * 18;
+  if (len != expected)
+    return fail(MRI_ERR_INVALID_SHAPE,
+                "matmul_q4_0_dequant: weight_q4 has %zu bytes, expected %zu for shape [%zu, %zu]",
+                len, expected, n_out, k);
+  if (len && !bytes) return fail(MRI_ERR_INVALID_ARGUMENT, "null weight pointer");
+  mri_q4_0_matrix* w = new mri_q4_0_matrix{ctx->device, nullptr, n_out, k};
+  if (int rc = upload_bytes(bytes, len, &w->data)) {
+    delete w;
+    return rc;
+  }
+  *out = w;
+  return MRI_OK;
+}
+
+int mri_q4_0_free(mri_q4_0_matrix* w) {
+  if (!w) return MRI_OK;
+  use_device(w->device);
+  cudaFree(w->data);
+  delete w;
+  return MRI_OK;
+}
+
+// ── quantizer ────────────────────────────────────────────────────────────────
+
+int mri_quantize_symmetric(mri_ctx* ctx, const float* x_dev, size_t m, size_t k, int granularity,
+                           int8_t* q_dev, float* scale_dev) {
+  if (int rc = enter(ctx)) return rc;
+  if (granularity != MRI_PER_TENSOR && granularity != MRI_PER_ROW)
+    return fail(MRI_ERR_INVALID_ARGUMENT, "granularity must be MRI_PER_TENSOR or MRI_PER_ROW");
+  if ((m * k && (!x_dev || !q_dev)) || !scale_dev)
+    return fail(MRI_ERR_INVALID_ARGUMENT, "null device pointer");
+  if (int rc = ensure_scratch(ctx, al(std::max<size_t>(m, 1) * sizeof(float)))) return rc;
+  MRI_CUDA_TRY(mri::launch_quantize(ctx->dev, ctx->stream, x_dev, m, k, granularity, q_dev,
+                                    scale_dev, reinterpret_cast<float*>(ctx->scratch), &ctx->ls));
+  return MRI_OK;
+}
+
+// ── INT8 products ────────────────────────────────────────────────────────────
+
+int mri_matmul_int8(mri_ctx* ctx, const int8_t* act_q_dev, size_t act_len, float act_scale,
+                    const mri_qmatrix* w, size_t m, float* out_dev, int32_t* acc_dev) {
+  if (int rc = enter(ctx)) return rc;
+  if (!w) return fail(MRI_ERR_INVALID_ARGUMENT, "null weight handle");
+  if (int rc = check_act_len("matmul_int8", act_len, m, w->k_in)) return rc;
+  if (m * w->n_out && !out_dev) return fail(MRI_ERR_INVALID_ARGUMENT, "null output pointer");
+  ActArgs a;
+  a.xq = act_q_dev;
+  a.mode = mri::ACT_I8_HOST_SCALE;
+  a.scale_host = act_scale;
+  return run_int8(ctx, a, w, m, out_dev, acc_dev);
+}
+
+int mri_matmul_int8_dscale(mri_ctx* ctx, const int8_t* act_q_dev, size_t act_len,
+                           const float* act_scale_dev, int scale_per_row, const mri_qmatrix* w,
+                           size_t m, float* out_dev, int32_t* acc_dev) {
+  if (int rc = enter(ctx)) return rc;
+  if (!w || !act_scale_dev) return fail(MRI_ERR_INVALID_ARGUMENT, "null argument");
+  if (int rc = check_act_len("matmul_int8", act_len, m, w->k_in)) return rc;
+  ActArgs a;
+  a.xq = act_q_dev;
+  a.mode = scale_per_row ? mri::ACT_I8_DEV_ROW_SCALE : mri::ACT_I8_DEV_SCALE;
+  a.scale_dev = act_scale_dev;
+  return run_int8(ctx, a, w, m, out_dev, acc_dev);
+}
+
+int mri_matmul_int8_from_f32_g(mri_ctx* ctx, const float* x_dev, size_t m, size_t k,
+                               int granularity, const mri_qmatrix* w, float* out_dev) {
+  if (int rc = enter(ctx)) return rc;
+  if (!w) return fail(MRI_ERR_INVALID_ARGUMENT, "null weight handle");
+  if (granularity != MRI_PER_TENSOR && granularity != MRI_PER_ROW)
+    return fail(MRI_ERR_INVALID_ARGUMENT, "granularity must be MRI_PER_TENSOR or MRI_PER_ROW");
+  if (int rc = check_k("matmul_int8_from_f32", m, k, w->k_in)) return rc;
+  ActArgs a;
+  a.x = x_dev;
+  a.mode = granularity == MRI_PER_ROW ? mri::ACT_F32_PER_ROW : mri::ACT_F32_PER_TENSOR;
+  return run_int8(ctx, a, w, m, out_dev, nullptr);
+}
+
+int mri_matmul_int8_from_f32(mri_ctx* ctx, const float* x_dev, size_t m, size_t k,
+                             const mri_qmatrix* w, float* out_dev) {
+  return mri_matmul_int8_from_f32_g(ctx, x_dev, m, k, MRI_PER_TENSOR, w, out_dev);
+}
+
+int mri_matmul_q8_0_direct(mri_ctx* ctx, const float* x_dev, size_t m, size_t k,
+                           const mri_q8_0_matrix* w, float* out_dev) {
+  if (int rc = enter(ctx)) return rc;
+  if (!w) return fail(MRI_ERR_INVALID_ARGUMENT, "null weight handle");
+  if (int rc = check_k("matmul_q8_0_direct", m, k, w->k_in)) return rc;
+  return run_q8_0(ctx, x_dev, m, w, out_dev);
+}
+
+int mri_matmul_q4_0_dequant(mri_ctx* ctx, const float* x_dev, size_t m, size_t k,
+                            const mri_q4_0_matrix* w, float* out_dev) {
+  if (int rc = enter(ctx)) return rc;
+  if (!w) return fail(MRI_ERR_INVALID_ARGUMENT, "null weight handle");
+  if (int rc = check_k("matmul_q4_0_dequant", m, k, w->k)) return rc;
+  return run_q4_0(ctx, x_dev, m, w, out_dev);
+}
+
+// ── host-buffer drop-ins ─────────────────────────────────────────────────────
+
+int mri_host_quantize_symmetric(mri_ctx* ctx, const float* x, size_t m, size_t k, int granularity,
+                                int8_t* q, float* scale) {
+  if (int rc = enter(ctx)) return rc;
+  if (granularity != MRI_PER_TENSOR && granularity != MRI_PER_ROW)
+    return fail(MRI_ERR_INVALID_ARGUMENT, "granularity must be MRI_PER_TENSOR or MRI_PER_ROW");
+  const size_t ns = granularity == MRI_PER_ROW ? m : 1;
+  HostStage hs;
+  if (int rc = host_stage(ctx, m * k * 4 + al(m * k), ns * 4, 0, std::max<size_t>(m, 1), 0, &hs))
+    return rc;
+  float* xd = reinterpret_cast<float*>(hs.in);
+  int8_t* qd = reinterpret_cast<int8_t*>(hs.in + al(m * k * 4));
+  if (m * k) MRI_CUDA_TRY(cudaMemcpyAsync(xd, x, m * k * 4, cudaMemcpyHostToDevice, ctx->stream));
+  MRI_CUDA_TRY(mri::launch_quantize(ctx->dev, ctx->stream, xd, m, k, granularity, qd, hs.out,
+                                    reinterpret_cast<float*>(ctx->scratch), &ctx->ls));
+  if (m * k) MRI_CUDA_TRY(cudaMemcpyAsync(q, qd, m * k, cudaMemcpyDeviceToHost, ctx->stream));
+  if (ns) MRI_CUDA_TRY(cudaMemcpyAsync(scale, hs.out, ns * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  MRI_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+  return mri_ctx_check_device_status(ctx);
+}
+
+int mri_host_matmul_int8(mri_ctx* ctx, const int8_t* act_q, size_t act_len, float act_scale,
+                         const mri_qmatrix* w, size_t m, float* out, int32_t* acc) {
+  if (int rc = enter(ctx)) return rc;
+  if (!w) return fail(MRI_ERR_INVALID_ARGUMENT, "null weight handle");
+  if (int rc = check_act_len("matmul_int8", act_len, m, w->k_in)) return rc;
+  const size_t N = w->n_out;
+  HostStage hs;
+  if (int rc = host_stage(ctx, act_len, m * N * 4, acc ? m * N * 4 : 0, m, w->k_in, &hs)) return rc;
+  if (act_len)
+    MRI_CUDA_TRY(cudaMemcpyAsync(hs.in, act_q, act_len, cudaMemcpyHostToDevice, ctx->stream));
+  ActArgs a;
+  a.xq = reinterpret_cast<int8_t*>(hs.in);
+  a.mode = mri::ACT_I8_HOST_SCALE;
+  a.scale_host = act_scale;
+  if (int rc = run_int8(ctx, a, w, m, hs.out, acc ? hs.acc : nullptr)) return rc;
+  if (m * N) {
+    MRI_CUDA_TRY(cudaMemcpyAsync(out, hs.out, m * N * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    if (acc) MRI_CUDA_TRY(cudaMemcpyAsync(acc, hs.acc, m * N * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  }
+  MRI_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+  return mri_ctx_check_device_status(ctx);
+}
+
+int mri_host_matmul_int8_from_f32(mri_ctx* ctx, const float* x, size_t m, size_t k,
+                                  const mri_qmatrix* w, float* out) {
+  if (int rc = enter(ctx)) return rc;
+  if (!w) return fail(MRI_ERR_INVALID_ARGUMENT, "null weight handle");
+  if (int rc = check_k("matmul_int8_from_f32", m, k, w->k_in)) return rc;
+  const size_t N = w->n_out;
+  HostStage hs;
+  if (int rc = host_stage(ctx, m * k * 4, m * N * 4, 0, m, k, &hs)) return rc;
+  if (m * k) MRI_CUDA_TRY(cudaMemcpyAsync(hs.in, x, m * k * 4, cudaMemcpyHostToDevice, ctx->stream));
+  ActArgs a;
+  a.x = reinterpret_cast<float*>(hs.in);
+  a.mode = mri::ACT_F32_PER_TENSOR;
+  if (int rc = run_int8(ctx, a, w, m, hs.out, nullptr)) return rc;
+  if (m * N) MRI_CUDA_TRY(cudaMemcpyAsync(out, hs.out, m * N * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  MRI_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+  return mri_ctx_check_device_status(ctx);
+}
+
+int mri_host_matmul_q8_0_direct(mri_ctx* ctx, const float* x, size_t m, size_t k,
+                                const mri_q8_0_matrix* w, float* out) {
+  if (int rc = enter(ctx)) return rc;
+  if (!w) return fail(MRI_ERR_INVALID_ARGUMENT, "null weight handle");
+  if (int rc = check_k("matmul_q8_0_direct", m, k, w->k_in)) return rc;
+  const size_t N = w->n_out;
+  HostStage hs;
+  if (int rc = host_stage(ctx, m * k * 4, m * N * 4, 0, m, k, &hs)) return rc;
+  if (m * k) MRI_CUDA_TRY(cudaMemcpyAsync(hs.in, x, m * k * 4, cudaMemcpyHostToDevice, ctx->stream));
+  if (int rc = run_q8_0(ctx, reinterpret_cast<float*>(hs.in), m, w, hs.out)) return rc;
+  if (m * N) MRI_CUDA_TRY(cudaMemcpyAsync(out, hs.out, m * N * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  MRI_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+  return mri_ctx_check_device_status(ctx);
+}
+
+int mri_host_matmul_q4_0_dequant(mri_ctx* ctx, const float* x, size_t m, size_t k,
+                                 const mri_q4_0_matrix* w, float* out) {
+  if (int rc = enter(ctx)) return rc;
+  if (!w) return fail(MRI_ERR_INVALID_ARGUMENT, "null weight handle");
+  if (int rc = check_k("matmul_q4_0_dequant", m, k, w->k)) return rc;
+  const size_t N = w->n_out;
+  HostStage hs;
+  if (int rc = host_stage(ctx, m * k * 4, m * N * 4, 0, 0, 0, &hs)) return rc;
+  if (m * k) MRI_CUDA_TRY(cudaMemcpyAsync(hs.in, x, m * k * 4, cudaMemcpyHostToDevice, ctx->stream));
+  if (int rc = run_q4_0(ctx, reinterpret_cast<float*>(hs.in), m, w, hs.out)) return rc;
+  if (m * N) MRI_CUDA_TRY(cudaMemcpyAsync(out, hs.out, m * N * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  MRI_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+  return mri_ctx_check_device_status(ctx);
+}
+
+int mri_int8_path(mri_ctx* ctx, size_t m, size_t n, size_t k) {
+  if (!ctx) return -1;
+  if (m <= 8 && m > 0 && mri::gemv_i8_tma_supported(ctx->dev, static_cast<int>(m), k)) return 0;
+  if (mri::gemm_i8_tc_supported(ctx->dev, m, n, k)) return 2;
+  return 1;
+}
+
+}  // extern "C"

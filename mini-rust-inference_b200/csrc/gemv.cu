@@ -1,0 +1,741 @@
+// gemv.cu — K2/K4/K5: memory-bound products for M <= 8 activation rows.
+//
+// Shape of every "stream" kernel (one CTA per SM, persistent over a balanced,
+// contiguous range of weight rows):
+//   warp 0, lane 0 : producer.  Streams 8-row groups of the weight matrix
+//                    into a ring of shared-memory stages with 1-D bulk TMA
+//                    copies (cp.async.bulk, L2 evict-first), one mbarrier
+//                    "full" per stage, waiting on "empty" before reuse.
+//   warps 1..8     : consumers.  Warp w owns row w of each stage; its lanes
+//                    split the row's K bytes, the activations sit in shared
+//                    memory (quantized once per CTA in the prologue, which
+//                    overlaps the first weight copies), and the epilogue
+//                    rescales to f32.
+// Every wait is bounded (mbar_wait); on timeout the kernel records
+// MRI_ERR_TIMEOUT in the context status word and returns.
+//
+// Bit-exactness: INT8 products sum integers (order-free) and apply the
+// reference epilogue `(f32)acc * s_a * s_w`; Q8_0 computes each block term
+// `(f32)dot * s_a * d` and adds the terms in block order on one lane, as
+// q8_direct.rs:266-285 does.  Q4_0 reassociates its f32 sum (tolerance).
+#include <algorithm>
+#include <map>
+#include <mutex>
+#include <utility>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace mri {
+namespace {
+
+constexpr int kConsumerWarps = 8;
+constexpr int kRowsPerStage = kConsumerWarps;
+constexpr int kThreads = 32 * (kConsumerWarps + 1);
+constexpr int kConsumerThreads = 32 * kConsumerWarps;
+constexpr int kMaxStages = 6;
+constexpr size_t kSmemBudget = 220 * 1024;  // of the 227 KB opt-in per CTA
+
+__host__ __device__ constexpr size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Shared-memory layout of a stream kernel.
+struct StreamLayout {
+  size_t bars;       // 2 * stages mbarriers
+  size_t scales;     // 8 activation scales + 8 reduction slots
+  size_t act;        // activation buffer
+  size_t extra;      // per-warp scratch (Q8_0 term buffer)
+  size_t stage;      // first stage buffer
+  size_t stage_bytes;
+  size_t total;
+  int stages;
+};
+
+__host__ __device__ inline StreamLayout make_layout(size_t act_bytes, size_t extra_bytes,
+                                                    size_t stage_bytes, int stages) {
+  StreamLayout L{};
+  L.stages = stages;
+  L.bars = 0;
+  L.scales = align_up(2 * stages * sizeof(uint64_t), 16);
+  L.act = align_up(L.scales + 16 * sizeof(float), 128);
+  L.extra = align_up(L.act + act_bytes, 128);
+  L.stage = align_up(L.extra + extra_bytes, 128);
+  L.stage_bytes = align_up(stage_bytes, 128);
+  // 16 bytes of slack: block loaders read whole words and may pass the end
+  // of the last row by up to 2 bytes.
+  L.total = L.stage + L.stage_bytes * stages + 16;
+  return L;
+}
+
+// Rows [begin, end) of this CTA: a balanced split of N in units of `gran` rows.
+__device__ __forceinline__ void cta_rows(size_t N, size_t gran, size_t& begin, size_t& end) {
+  const size_t units = (N + gran - 1) / gran;
+  const size_t u0 = units * blockIdx.x / gridDim.x;
+  const size_t u1 = units * (blockIdx.x + 1) / gridDim.x;
+  begin = u0 * gran;
+  end = std::min(N, u1 * gran);
+}
+
+// Producer loop shared by all stream kernels: stage `it` holds rows
+// [begin + 8*it, ...) whose bytes start at W + row*row_bytes.
+__device__ void stream_producer(const uint8_t* W, size_t row_bytes, size_t begin, size_t end,
+                                uint64_t* full, uint64_t* empty, uint8_t* stages_base,
+                                size_t stage_stride, int n_stages, int* status) {
+  const uint64_t policy = l2_policy_evict_first();
+  const int iters = static_cast<int>((end - begin + kRowsPerStage - 1) / kRowsPerStage);
+  int issued = 0;
+  for (int it = 0; it < iters; ++it) {
+    const int s = it % n_stages;
+    if (it >= n_stages) {
+      if (!mbar_wait(&empty[s], ((it / n_stages) - 1) & 1, status)) break;
+    }
+    const size_t r0 = begin + static_cast<size_t>(it) * kRowsPerStage;
+    const size_t nrows = std::min<size_t>(kRowsPerStage, end - r0);
+    const uint32_t bytes = static_cast<uint32_t>(align_up(nrows * row_bytes, 16));
+    mbar_arrive_expect_tx(&full[s], bytes);
+    bulk_copy_g2s_stream(stages_base + s * stage_stride, W + r0 * row_bytes, bytes, &full[s],
+                         policy);
+    issued = it + 1;
+  }
+  // Drain: return only once every copy this thread issued has landed.
+  for (int it = std::max(0, issued - n_stages); it < issued; ++it)
+    mbar_wait(&full[it % n_stages], (it / n_stages) & 1, status);
+}
+
+__device__ __forceinline__ void init_barriers(uint64_t* full, uint64_t* empty, int n_stages) {
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < n_stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+}
+
+// ── activation prologue (consumer threads only) ──────────────────────────────
+
+// Block-wide (consumer) max; `red` holds kConsumerWarps floats.
+__device__ __forceinline__ float consumer_max(float v, float* red) {
+  const int cw = (threadIdx.x >> 5) - 1;
+  v = warp_max(v);
+  if ((threadIdx.x & 31) == 0) red[cw] = v;
+  named_bar_sync(1, kConsumerThreads);
+  float r = 0.0f;
+#pragma unroll
+  for (int i = 0; i < kConsumerWarps; ++i) r = fmaxf(r, red[i]);
+  named_bar_sync(1, kConsumerThreads);
+  return r;
+}
+
+// Quantize (or copy) the M activation rows into shared memory as int8 [M][K]
+// row-major and fill s_scale[0..M).
+template <int M>
+__device__ void load_act_i8_rowmajor(const ActArgs& act, size_t K, int8_t* s_act, float* s_scale,
+                                     float* red) {
+  const int ct = threadIdx.x - 32;
+  const size_t total = static_cast<size_t>(M) * K;
+  if (act.mode == ACT_F32_PER_TENSOR || act.mode == ACT_F32_PER_ROW) {
+    const float* x = act.x;
+    const bool vec = (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (K % 4) == 0;
+    for (int r = 0; r < (act.mode == ACT_F32_PER_ROW ? M : 1); ++r) {
+      const size_t lo = act.mode == ACT_F32_PER_ROW ? r * K : 0;
+      const size_t hi = act.mode == ACT_F32_PER_ROW ? lo + K : total;
+      float m = 0.0f;
+      if (vec) {
+        for (size_t i = lo / 4 + ct; i < hi / 4; i += kConsumerThreads) {
+          const float4 v = __ldg(reinterpret_cast<const float4*>(x) + i);
+          m = absmax_acc(absmax_acc(absmax_acc(absmax_acc(m, v.x), v.y), v.z), v.w);
+        }
+      } else {
+        for (size_t i = lo + ct; i < hi; i += kConsumerThreads) m = absmax_acc(m, __ldg(x + i));
+      }
+      const float scale = sym_scale(consumer_max(m, red));
+      const float inv = __fdiv_rn(1.0f, scale);
+      if (act.mode == ACT_F32_PER_ROW) {
+        if (ct == 0) s_scale[r] = scale;
+      } else if (ct < M) {
+        s_scale[ct] = scale;
+      }
+      if (vec) {
+        for (size_t i = lo / 4 + ct; i < hi / 4; i += kConsumerThreads) {
+          const float4 v = __ldg(reinterpret_cast<const float4*>(x) + i);
+          char4 o;
+          o.x = sym_quant(v.x, inv);
+          o.y = sym_quant(v.y, inv);
+          o.z = sym_quant(v.z, inv);
+          o.w = sym_quant(v.w, inv);
+          reinterpret_cast<char4*>(s_act)[i] = o;
+        }
+      } else {
+        for (size_t i = lo + ct; i < hi; i += kConsumerThreads) s_act[i] = sym_quant(__ldg(x + i), inv);
+      }
+    }
+  } else {
+    const int8_t* xq = act.xq;
+    if ((reinterpret_cast<uintptr_t>(xq) & 15) == 0 && (total % 16) == 0) {
+      for (size_t i = ct; i < total / 16; i += kConsumerThreads)
+        reinterpret_cast<uint4*>(s_act)[i] = __ldg(reinterpret_cast<const uint4*>(xq) + i);
+    } else {
+      for (size_t i = ct; i < total; i += kConsumerThreads) s_act[i] = xq[i];
+    }
+    if (ct < M) {
+      if (act.mode == ACT_I8_HOST_SCALE) s_scale[ct] = act.scale_host;
+      else if (act.mode == ACT_I8_DEV_SCALE) s_scale[ct] = act.scale_dev[0];
+      else s_scale[ct] = act.scale_dev[ct];
+    }
+  }
+  named_bar_sync(1, kConsumerThreads);
+}
+
+// ── K2: INT8 per-channel streaming GEMV (K % 16 == 0) ───────────────────────
+
+template <int M>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemv_i8_tma_kernel(const int8_t* __restrict__ W, const float* __restrict__ w_scales, size_t N,
+                       size_t K, ActArgs act, float* __restrict__ out, int32_t* __restrict__ acc_out,
+                       int n_stages, int* status) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const StreamLayout L = make_layout(M * K, 0, kRowsPerStage * K, n_stages);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
+  uint64_t* empty = full + n_stages;
+  float* s_scale = reinterpret_cast<float*>(smem + L.scales);
+  float* red = s_scale + 8;
+  int8_t* s_act = reinterpret_cast<int8_t*>(smem + L.act);
+  uint8_t* stage0 = smem + L.stage;
+
+  size_t begin, end;
+  cta_rows(N, 1, begin, end);
+  init_barriers(full, empty, n_stages);
+  if (begin >= end) return;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp == 0) {
+    if (lane == 0)
+      stream_producer(reinterpret_cast<const uint8_t*>(W), K, begin, end, full, empty, stage0,
+                      L.stage_bytes, n_stages, status);
+    return;
+  }
+  load_act_i8_rowmajor<M>(act, K, s_act, s_scale, red);
+  float s_a[M];
+#pragma unroll
+  for (int m = 0; m < M; ++m) s_a[m] = s_scale[m];
+
+  const int cw = warp - 1;
+  const int chunks = static_cast<int>(K / 16);
+  const int iters = static_cast<int>((end - begin + kRowsPerStage - 1) / kRowsPerStage);
+  for (int it = 0; it < iters; ++it) {
+    const int s = it % n_stages;
+    if (!mbar_wait(&full[s], (it / n_stages) & 1, status)) return;
+    const size_t row = begin + static_cast<size_t>(it) * kRowsPerStage + cw;
+    if (row < end) {
+      const uint4* wrow = reinterpret_cast<const uint4*>(stage0 + s * L.stage_bytes + cw * K);
+      int acc[M];
+#pragma unroll
+      for (int m = 0; m < M; ++m) acc[m] = 0;
+#pragma unroll 4
+      for (int c = lane; c < chunks; c += 32) {
+        const uint4 w = wrow[c];
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+          const uint4 a = reinterpret_cast<const uint4*>(s_act + m * K)[c];
+          acc[m] = dp4a(w.x, a.x, acc[m]);
+          acc[m] = dp4a(w.y, a.y, acc[m]);
+          acc[m] = dp4a(w.z, a.z, acc[m]);
+          acc[m] = dp4a(w.w, a.w, acc[m]);
+        }
+      }
+#pragma unroll
+      for (int m = 0; m < M; ++m) acc[m] = warp_sum_i(acc[m]);
+      const float sw = __ldg(w_scales + row);
+#pragma unroll
+      for (int m = 0; m < M; ++m) {
+        if (lane == m) {
+          out[m * N + row] = rescale(acc[m], s_a[m], sw);
+          if (acc_out) acc_out[m * N + row] = acc[m];
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+  }
+}
+
+// ── generic INT8 GEMV: any K / alignment, pre-quantized activations ─────────
+
+template <int M>
+__global__ void __launch_bounds__(256) gemv_i8_generic_kernel(const int8_t* __restrict__ W,
+                                                              const float* __restrict__ w_scales,
+                                                              size_t N, size_t K, ActArgs act,
+                                                              float* __restrict__ out,
+                                                              int32_t* __restrict__ acc_out) {
+  const int lane = threadIdx.x & 31;
+  const size_t warps = static_cast<size_t>(gridDim.x) * (blockDim.x >> 5);
+  float s_a[M];
+#pragma unroll
+  for (int m = 0; m < M; ++m)
+    s_a[m] = act.mode == ACT_I8_HOST_SCALE ? act.scale_host
+             : act.mode == ACT_I8_DEV_SCALE ? act.scale_dev[0]
+                                            : act.scale_dev[m];
+  for (size_t row = static_cast<size_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+       row < N; row += warps) {
+    const int8_t* wr = W + row * K;
+    int acc[M];
+#pragma unroll
+    for (int m = 0; m < M; ++m) acc[m] = 0;
+    for (size_t k = lane; k < K; k += 32) {
+      const int w = wr[k];
+#pragma unroll
+      for (int m = 0; m < M; ++m) acc[m] += w * static_cast<int>(act.xq[m * K + k]);
+    }
+#pragma unroll
+    for (int m = 0; m < M; ++m) acc[m] = warp_sum_i(acc[m]);
+    const float sw = w_scales[row];
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      if (lane == m) {
+        out[m * N + row] = rescale(acc[m], s_a[m], sw);
+        if (acc_out) acc_out[m * N + row] = acc[m];
+      }
+    }
+  }
+}
+
+// ── Q8_0 helpers ─────────────────────────────────────────────────────────────
+
+// Loads block `blk` (34 bytes at an even address) from any address space:
+// d (f16 bits) and the 32 quants as 8 little-endian words.
+__device__ __forceinline__ void load_q8_block(const uint8_t* blk, uint32_t& dbits, uint32_t q[8]) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(blk);
+  const uint32_t* w = reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3));
+  const bool odd = (a & 2) != 0;  // block starts 2 bytes into a word
+  uint32_t r[9];  // 36 bytes from the aligned-down start cover the block
+#pragma unroll
+  for (int i = 0; i < 9; ++i) r[i] = w[i];
+  dbits = odd ? (r[0] >> 16) : (r[0] & 0xFFFFu);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) q[i] = odd ? r[i + 1] : __funnelshift_r(r[i], r[i + 1], 16);
+}
+
+// ── K4: Q8_0 streaming GEMV, bit-exact ───────────────────────────────────────
+// Activations live in shared memory as words transposed to [m][word 0..7][block]
+// so that lane b of a warp reads word w of block b without bank conflicts.
+// Each consumer warp keeps a term buffer T[m][nb+1]: lanes write the block
+// terms of their blocks, then lane m adds row m's terms in block order.
+
+template <int M>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemv_q8_0_tma_kernel(const uint8_t* __restrict__ W, size_t N, size_t K,
+                         const float* __restrict__ x, float* __restrict__ out, int n_stages,
+                         int* status) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const size_t nb = K / 32;
+  const size_t row_bytes = nb * 34;
+  const StreamLayout L = make_layout(M * K, kConsumerWarps * M * (nb + 1) * sizeof(float),
+                                     kRowsPerStage * row_bytes, n_stages);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
+  uint64_t* empty = full + n_stages;
+  float* s_scale = reinterpret_cast<float*>(smem + L.scales);
+  float* red = s_scale + 8;
+  uint32_t* s_actw = reinterpret_cast<uint32_t*>(smem + L.act);
+  float* s_terms = reinterpret_cast<float*>(smem + L.extra);
+  uint8_t* stage0 = smem + L.stage;
+
+  // Row ranges must start 16-byte aligned: begin * 34 * nb % 16 == 0.
+  const size_t g = 8 / (nb % 8 == 0 ? 8 : (nb % 4 == 0 ? 4 : (nb % 2 == 0 ? 2 : 1)));
+  size_t begin, end;
+  cta_rows(N, g, begin, end);
+  init_barriers(full, empty, n_stages);
+  if (begin >= end) return;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp == 0) {
+    if (lane == 0)
+      stream_producer(W, row_bytes, begin, end, full, empty, stage0, L.stage_bytes, n_stages,
+                      status);
+    return;
+  }
+
+  // Prologue: per-row quantization (q8_direct.rs:264) into the transposed layout.
+  const int ct = threadIdx.x - 32;
+  for (int r = 0; r < M; ++r) {
+    const float* xr = x + r * K;
+    float m = 0.0f;
+    for (size_t i = ct; i < K; i += kConsumerThreads) m = absmax_acc(m, __ldg(xr + i));
+    const float scale = sym_scale(consumer_max(m, red));
+    const float inv = __fdiv_rn(1.0f, scale);
+    if (ct == 0) s_scale[r] = scale;
+    for (size_t wi = ct; wi < K / 4; wi += kConsumerThreads) {
+      const size_t k = wi * 4;
+      const uint32_t b0 = static_cast<uint8_t>(sym_quant(__ldg(xr + k), inv));
+      const uint32_t b1 = static_cast<uint8_t>(sym_quant(__ldg(xr + k + 1), inv));
+      const uint32_t b2 = static_cast<uint8_t>(sym_quant(__ldg(xr + k + 2), inv));
+      const uint32_t b3 = static_cast<uint8_t>(sym_quant(__ldg(xr + k + 3), inv));
+      const size_t blk = k / 32, word = (k % 32) / 4;
+      s_actw[(r * 8 + word) * nb + blk] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+    }
+  }
+  named_bar_sync(1, kConsumerThreads);
+  float s_a[M];
+#pragma unroll
+  for (int m = 0; m < M; ++m) s_a[m] = s_scale[m];
+
+  const int cw = warp - 1;
+  float* T = s_terms + static_cast<size_t>(cw) * M * (nb + 1);
+  const int iters = static_cast<int>((end - begin + kRowsPerStage - 1) / kRowsPerStage);
+  for (int it = 0; it < iters; ++it) {
+    const int s = it % n_stages;
+    if (!mbar_wait(&full[s], (it / n_stages) & 1, status)) return;
+    const size_t row = begin + static_cast<size_t>(it) * kRowsPerStage + cw;
+    if (row < end) {
+      const uint8_t* rowp = stage0 + s * L.stage_bytes + cw * row_bytes;
+      for (size_t b = lane; b < nb; b += 32) {
+        uint32_t dbits, q[8];
+        load_q8_block(rowp + b * 34, dbits, q);
+        const float d = f16_bits_to_f32(dbits);
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+          int dot = 0;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) dot = dp4a(q[i], s_actw[(m * 8 + i) * nb + b], dot);
+          T[m * (nb + 1) + b] = __fmul_rn(__fmul_rn(__int2float_rn(dot), s_a[m]), d);
+        }
+      }
+      __syncwarp();
+      if (lane < M) {
+        const float* t = T + lane * (nb + 1);
+        float acc = 0.0f;
+        for (size_t b = 0; b < nb; ++b) acc = __fadd_rn(acc, t[b]);
+        out[lane * N + row] = acc;
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+  }
+}
+
+// Generic Q8_0: pre-quantized activations in global memory (row-major),
+// warp per row, block terms added in order with a lane-serial shuffle chain.
+template <int M>
+__global__ void __launch_bounds__(256) gemv_q8_0_generic_kernel(const uint8_t* __restrict__ W,
+                                                                size_t N, size_t K,
+                                                                const int8_t* __restrict__ xq,
+                                                                const float* __restrict__ scales,
+                                                                float* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const size_t nb = K / 32;
+  const size_t warps = static_cast<size_t>(gridDim.x) * (blockDim.x >> 5);
+  float s_a[M];
+#pragma unroll
+  for (int m = 0; m < M; ++m) s_a[m] = scales[m];
+  for (size_t row = static_cast<size_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+       row < N; row += warps) {
+    const uint8_t* rowp = W + row * nb * 34;
+    float acc[M];
+#pragma unroll
+    for (int m = 0; m < M; ++m) acc[m] = 0.0f;
+    for (size_t b0 = 0; b0 < nb; b0 += 32) {
+      const size_t b = b0 + lane;
+      float t[M];
+#pragma unroll
+      for (int m = 0; m < M; ++m) t[m] = 0.0f;
+      if (b < nb) {
+        const uint8_t* blk = rowp + b * 34;
+        const float d = f16_bits_to_f32(blk[0] | (blk[1] << 8));
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+          int dot = 0;
+          for (int i = 0; i < 32; ++i)
+            dot += static_cast<int>(static_cast<int8_t>(blk[2 + i])) *
+                   static_cast<int>(xq[m * K + b * 32 + i]);
+          t[m] = __fmul_rn(__fmul_rn(__int2float_rn(dot), s_a[m]), d);
+        }
+      }
+      const int valid = static_cast<int>(std::min<size_t>(32, nb - b0));
+      for (int i = 0; i < valid; ++i) {
+#pragma unroll
+        for (int m = 0; m < M; ++m) acc[m] = __fadd_rn(acc[m], __shfl_sync(0xffffffffu, t[m], i));
+      }
+    }
+#pragma unroll
+    for (int m = 0; m < M; ++m)
+      if (lane == m) out[m * N + row] = acc[m];
+  }
+}
+
+// ── K5: Q4_0 streaming GEMV (f32 activations) ───────────────────────────────
+// Activations are stored transposed to [m][element 0..31][block] floats.
+
+__device__ __forceinline__ void load_q4_block(const uint8_t* blk, uint32_t& dbits, uint32_t q[4]) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(blk);
+  const uint32_t* w = reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3));
+  const bool odd = (a & 2) != 0;
+  uint32_t r[5];
+#pragma unroll
+  for (int i = 0; i < 5; ++i) r[i] = w[i];
+  dbits = odd ? (r[0] >> 16) : (r[0] & 0xFFFFu);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) q[i] = odd ? r[i + 1] : __funnelshift_r(r[i], r[i + 1], 16);
+}
+
+template <int M>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemv_q4_0_tma_kernel(const uint8_t* __restrict__ W, size_t N, size_t K,
+                         const float* __restrict__ x, float* __restrict__ out, int n_stages,
+                         int* status) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const size_t nb = K / 32;
+  const size_t row_bytes = nb * 18;
+  const StreamLayout L = make_layout(M * K * sizeof(float), 0, kRowsPerStage * row_bytes, n_stages);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
+  uint64_t* empty = full + n_stages;
+  float* s_x = reinterpret_cast<float*>(smem + L.act);
+  uint8_t* stage0 = smem + L.stage;
+
+  const size_t g = 8 / (nb % 8 == 0 ? 8 : (nb % 4 == 0 ? 4 : (nb % 2 == 0 ? 2 : 1)));
+  size_t begin, end;
+  cta_rows(N, g, begin, end);
+  init_barriers(full, empty, n_stages);
+  if (begin >= end) return;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp == 0) {
+    if (lane == 0)
+      stream_producer(W, row_bytes, begin, end, full, empty, stage0, L.stage_bytes, n_stages,
+                      status);
+    return;
+  }
+  const int ct = threadIdx.x - 32;
+  for (size_t i = ct; i < static_cast<size_t>(M) * K; i += kConsumerThreads) {
+    const size_t r = i / K, k = i % K;
+    s_x[(r * 32 + (k % 32)) * nb + k / 32] = __ldg(x + i);
+  }
+  named_bar_sync(1, kConsumerThreads);
+
+  const int cw = warp - 1;
+  const int iters = static_cast<int>((end - begin + kRowsPerStage - 1) / kRowsPerStage);
+  for (int it = 0; it < iters; ++it) {
+    const int s = it % n_stages;
+    if (!mbar_wait(&full[s], (it / n_stages) & 1, status)) return;
+    const size_t row = begin + static_cast<size_t>(it) * kRowsPerStage + cw;
+    if (row < end) {
+      const uint8_t* rowp = stage0 + s * L.stage_bytes + cw * row_bytes;
+      float acc[M];
+#pragma unroll
+      for (int m = 0; m < M; ++m) acc[m] = 0.0f;
+      for (size_t b = lane; b < nb; b += 32) {
+        uint32_t dbits, q[4];
+        load_q4_block(rowp + b * 18, dbits, q);
+        const float d = f16_bits_to_f32(dbits);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const uint32_t byte = (q[j >> 2] >> (8 * (j & 3))) & 0xFFu;
+          // dequant_block_into (q4_0.rs:59-68): scale * (nibble - 8)
+          const float lo = __fmul_rn(d, static_cast<float>(static_cast<int>(byte & 15u) - 8));
+          const float hi = __fmul_rn(d, static_cast<float>(static_cast<int>(byte >> 4) - 8));
+#pragma unroll
+          for (int m = 0; m < M; ++m) {
+            acc[m] = __fmaf_rn(s_x[(m * 32 + 2 * j) * nb + b], lo, acc[m]);
+            acc[m] = __fmaf_rn(s_x[(m * 32 + 2 * j + 1) * nb + b], hi, acc[m]);
+          }
+        }
+      }
+#pragma unroll
+      for (int m = 0; m < M; ++m) acc[m] = warp_sum_f(acc[m]);
+#pragma unroll
+      for (int m = 0; m < M; ++m)
+        if (lane == m) out[m * N + row] = acc[m];
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+  }
+}
+
+template <int M>
+__global__ void __launch_bounds__(256) gemv_q4_0_generic_kernel(const uint8_t* __restrict__ W,
+                                                                size_t N, size_t K,
+                                                                const float* __restrict__ x,
+                                                                float* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const size_t nb = K / 32;
+  const size_t warps = static_cast<size_t>(gridDim.x) * (blockDim.x >> 5);
+  for (size_t row = static_cast<size_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+       row < N; row += warps) {
+    const uint8_t* rowp = W + row * nb * 18;
+    float acc[M];
+#pragma unroll
+    for (int m = 0; m < M; ++m) acc[m] = 0.0f;
+    for (size_t b = lane; b < nb; b += 32) {
+      const uint8_t* blk = rowp + b * 18;
+      const float d = f16_bits_to_f32(blk[0] | (blk[1] << 8));
+      for (int j = 0; j < 16; ++j) {
+        const uint32_t byte = blk[2 + j];
+        const float lo = __fmul_rn(d, static_cast<float>(static_cast<int>(byte & 15u) - 8));
+        const float hi = __fmul_rn(d, static_cast<float>(static_cast<int>(byte >> 4) - 8));
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+          acc[m] = __fmaf_rn(__ldg(x + m * K + b * 32 + 2 * j), lo, acc[m]);
+          acc[m] = __fmaf_rn(__ldg(x + m * K + b * 32 + 2 * j + 1), hi, acc[m]);
+        }
+      }
+    }
+#pragma unroll
+    for (int m = 0; m < M; ++m) acc[m] = warp_sum_f(acc[m]);
+#pragma unroll
+    for (int m = 0; m < M; ++m)
+      if (lane == m) out[m * N + row] = acc[m];
+  }
+}
+
+// ── host side: layouts, attributes, dispatch on M ────────────────────────────
+
+int pick_stages(size_t fixed_bytes, size_t stage_bytes) {
+  for (int s = kMaxStages; s >= 2; --s) {
+    const StreamLayout L = make_layout(0, 0, stage_bytes, s);
+    if (fixed_bytes + L.total + 256 <= kSmemBudget) return s;
+  }
+  return 0;
+}
+
+size_t fixed_bytes_of(size_t act_bytes, size_t extra_bytes) {
+  return align_up(act_bytes, 128) + align_up(extra_bytes, 128) + 256;
+}
+
+// Raises a kernel's dynamic shared-memory limit once per (kernel, device,
+// size): later launches make no runtime call, so they stay legal inside
+// CUDA-graph capture.
+template <typename KernelT>
+cudaError_t set_smem(KernelT k, size_t bytes, int device) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, size_t> done;
+  std::lock_guard<std::mutex> lock(mu);
+  const auto key = std::make_pair(reinterpret_cast<const void*>(k), device);
+  auto it = done.find(key);
+  if (it != done.end() && bytes <= it->second) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(bytes));
+  if (e == cudaSuccess) done[key] = bytes;
+  return e;
+}
+
+int stream_grid(const DeviceInfo& dev, size_t units) {
+  return static_cast<int>(std::max<size_t>(1, std::min<size_t>(dev.sm_count, units)));
+}
+
+#define MRI_DISPATCH_M(M, ...)                           \
+  switch (M) {                                           \
+    case 1: { constexpr int kM = 1; __VA_ARGS__; } break; \
+    case 2: { constexpr int kM = 2; __VA_ARGS__; } break; \
+    case 3: { constexpr int kM = 3; __VA_ARGS__; } break; \
+    case 4: { constexpr int kM = 4; __VA_ARGS__; } break; \
+    case 5: { constexpr int kM = 5; __VA_ARGS__; } break; \
+    case 6: { constexpr int kM = 6; __VA_ARGS__; } break; \
+    case 7: { constexpr int kM = 7; __VA_ARGS__; } break; \
+    case 8: { constexpr int kM = 8; __VA_ARGS__; } break; \
+    default: return cudaErrorInvalidValue;               \
+  }
+
+}  // namespace
+
+bool gemv_i8_tma_supported(const DeviceInfo&, int M, size_t K) {
+  if (M < 1 || M > 8 || K == 0 || K % 16 != 0) return false;
+  return pick_stages(fixed_bytes_of(M * K, 0), kRowsPerStage * K) >= 3;
+}
+
+cudaError_t launch_gemv_i8_tma(const DeviceInfo& dev, cudaStream_t st, int M, const int8_t* W,
+                               const float* w_scales, size_t N, size_t K, const ActArgs& act,
+                               float* out, int32_t* acc_out, int* status, LaunchStats* ls) {
+  const int stages = pick_stages(fixed_bytes_of(M * K, 0), kRowsPerStage * K);
+  if (stages < 2) return cudaErrorInvalidValue;
+  const size_t smem = make_layout(M * K, 0, kRowsPerStage * K, stages).total;
+  const int grid = stream_grid(dev, N);
+  MRI_DISPATCH_M(M, {
+    cudaError_t e = set_smem(gemv_i8_tma_kernel<kM>, smem, dev.device);
+    if (e != cudaSuccess) return e;
+    gemv_i8_tma_kernel<kM><<<grid, kThreads, smem, st>>>(W, w_scales, N, K, act, out, acc_out,
+                                                          stages, status);
+  });
+  if (ls) ls->launches++;
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gemv_i8_generic(const DeviceInfo& dev, cudaStream_t st, int M, const int8_t* W,
+                                   const float* w_scales, size_t N, size_t K, const ActArgs& act,
+                                   float* out, int32_t* acc_out, LaunchStats* ls) {
+  const int grid = static_cast<int>(std::max<size_t>(1, std::min<size_t>((N + 7) / 8, dev.sm_count * 8)));
+  MRI_DISPATCH_M(M, {
+    gemv_i8_generic_kernel<kM><<<grid, 256, 0, st>>>(W, w_scales, N, K, act, out, acc_out);
+  });
+  if (ls) ls->launches++;
+  return cudaGetLastError();
+}
+
+bool gemv_q8_0_tma_supported(const DeviceInfo&, int M, size_t K) {
+  if (M < 1 || M > 8 || K == 0 || K % 32 != 0) return false;
+  const size_t nb = K / 32;
+  return pick_stages(fixed_bytes_of(M * K, kConsumerWarps * M * (nb + 1) * 4),
+                     kRowsPerStage * nb * 34) >= 3;
+}
+
+cudaError_t launch_gemv_q8_0_tma(const DeviceInfo& dev, cudaStream_t st, int M, const uint8_t* W,
+                                 size_t N, size_t K, const float* x, float* out, int* status,
+                                 LaunchStats* ls) {
+  const size_t nb = K / 32;
+  const size_t extra = kConsumerWarps * M * (nb + 1) * 4;
+  const int stages = pick_stages(fixed_bytes_of(M * K, extra), kRowsPerStage * nb * 34);
+  if (stages < 2) return cudaErrorInvalidValue;
+  const size_t smem = make_layout(M * K, extra, kRowsPerStage * nb * 34, stages).total;
+  const int grid = stream_grid(dev, N);
+  MRI_DISPATCH_M(M, {
+    cudaError_t e = set_smem(gemv_q8_0_tma_kernel<kM>, smem, dev.device);
+    if (e != cudaSuccess) return e;
+    gemv_q8_0_tma_kernel<kM><<<grid, kThreads, smem, st>>>(W, N, K, x, out, stages, status);
+  });
+  if (ls) ls->launches++;
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gemv_q8_0_generic(const DeviceInfo& dev, cudaStream_t st, int M,
+                                     const uint8_t* W, size_t N, size_t K, const int8_t* xq,
+                                     const float* scales, float* out, LaunchStats* ls) {
+  const int grid = static_cast<int>(std::max<size_t>(1, std::min<size_t>((N + 7) / 8, dev.sm_count * 8)));
+  MRI_DISPATCH_M(M, {
+    gemv_q8_0_generic_kernel<kM><<<grid, 256, 0, st>>>(W, N, K, xq, scales, out);
+  });
+  if (ls) ls->launches++;
+  return cudaGetLastError();
+}
+
+bool gemv_q4_0_tma_supported(const DeviceInfo&, int M, size_t K) {
+  if (M < 1 || M > 8 || K == 0 || K % 32 != 0) return false;
+  return pick_stages(fixed_bytes_of(M * K * 4, 0), kRowsPerStage * (K / 32) * 18) >= 3;
+}
+
+cudaError_t launch_gemv_q4_0_tma(const DeviceInfo& dev, cudaStream_t st, int M, const uint8_t* W,
+                                 size_t N, size_t K, const float* x, float* out, int* status,
+                                 LaunchStats* ls) {
+  const size_t stage_bytes = kRowsPerStage * (K / 32) * 18;
+  const int stages = pick_stages(fixed_bytes_of(M * K * 4, 0), stage_bytes);
+  if (stages < 2) return cudaErrorInvalidValue;
+  const size_t smem = make_layout(M * K * 4, 0, stage_bytes, stages).total;
+  const int grid = stream_grid(dev, N);
+  MRI_DISPATCH_M(M, {
+    cudaError_t e = set_smem(gemv_q4_0_tma_kernel<kM>, smem, dev.device);
+    if (e != cudaSuccess) return e;
+    gemv_q4_0_tma_kernel<kM><<<grid, kThreads, smem, st>>>(W, N, K, x, out, stages, status);
+  });
+  if (ls) ls->launches++;
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gemv_q4_0_generic(const DeviceInfo& dev, cudaStream_t st, int M,
+                                     const uint8_t* W, size_t N, size_t K, const float* x,
+                                     float* out, LaunchStats* ls) {
+  const int grid = static_cast<int>(std::max<size_t>(1, std::min<size_t>((N + 7) / 8, dev.sm_count * 8)));
+  MRI_DISPATCH_M(M, {
+    gemv_q4_0_generic_kernel<kM><<<grid, 256, 0, st>>>(W, N, K, x, out);
+  });
+  if (ls) ls->launches++;
+  return cudaGetLastError();
+}
+
+}  // namespace mri

@@ -1,0 +1,86 @@
+// internal.h — launch interfaces between the ABI layer (abi.cu) and the
+// kernel translation units.  Not part of the public C ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace mri {
+
+// Where the activations of a product come from.
+enum ActMode : int {
+  ACT_F32_PER_TENSOR = 0,  // x f32 [M,K]: quantize with one scale over all M*K values
+  ACT_F32_PER_ROW = 1,     // x f32 [M,K]: quantize each row with its own scale
+  ACT_I8_HOST_SCALE = 2,   // xq i8 [M,K] + one scale passed by value
+  ACT_I8_DEV_SCALE = 3,    // xq i8 [M,K] + one scale in device memory
+  ACT_I8_DEV_ROW_SCALE = 4 // xq i8 [M,K] + M scales in device memory
+};
+
+struct ActArgs {
+  const float* x = nullptr;
+  const int8_t* xq = nullptr;
+  const float* scale_dev = nullptr;
+  float scale_host = 1.0f;
+  int mode = ACT_F32_PER_TENSOR;
+};
+
+// Kernel counts for launch accounting.
+struct LaunchStats {
+  unsigned long long launches = 0;
+};
+
+// Per-device properties the launchers need.
+struct DeviceInfo {
+  int device = 0;
+  int sm_count = 0;
+  int max_smem_optin = 0;
+  int cc_major = 0, cc_minor = 0;
+  size_t l2_bytes = 0;
+};
+
+// ── quantizer (quant.cu) ─────────────────────────────────────────────────────
+// amax_scratch: M floats (PER_ROW) or 1 float (PER_TENSOR); it is cleared here.
+cudaError_t launch_quantize(const DeviceInfo& dev, cudaStream_t st, const float* x, size_t m,
+                            size_t k, int per_row, int8_t* q, float* scale, float* amax_scratch,
+                            LaunchStats* ls);
+
+// ── streaming GEMV family (gemv.cu), M <= 8 rows of activations ─────────────
+// INT8 per-channel.  Requires K % 16 == 0 and 16-byte aligned W.
+bool gemv_i8_tma_supported(const DeviceInfo& dev, int M, size_t K);
+cudaError_t launch_gemv_i8_tma(const DeviceInfo& dev, cudaStream_t st, int M, const int8_t* W,
+                               const float* w_scales, size_t N, size_t K, const ActArgs& act,
+                               float* out, int32_t* acc_out, int* status, LaunchStats* ls);
+// Any K, any alignment; activations must be pre-quantized (modes 2-4).
+cudaError_t launch_gemv_i8_generic(const DeviceInfo& dev, cudaStream_t st, int M, const int8_t* W,
+                                   const float* w_scales, size_t N, size_t K, const ActArgs& act,
+                                   float* out, int32_t* acc_out, LaunchStats* ls);
+
+// Q8_0 (34-byte blocks).  Per-row activation quantization is fused.
+bool gemv_q8_0_tma_supported(const DeviceInfo& dev, int M, size_t K);
+cudaError_t launch_gemv_q8_0_tma(const DeviceInfo& dev, cudaStream_t st, int M, const uint8_t* W,
+                                 size_t N, size_t K, const float* x, float* out, int* status,
+                                 LaunchStats* ls);
+// Generic: activations pre-quantized per row into xq/scales (device).
+cudaError_t launch_gemv_q8_0_generic(const DeviceInfo& dev, cudaStream_t st, int M,
+                                     const uint8_t* W, size_t N, size_t K, const int8_t* xq,
+                                     const float* scales, float* out, LaunchStats* ls);
+
+// Q4_0 (18-byte blocks), f32 activations.
+bool gemv_q4_0_tma_supported(const DeviceInfo& dev, int M, size_t K);
+cudaError_t launch_gemv_q4_0_tma(const DeviceInfo& dev, cudaStream_t st, int M, const uint8_t* W,
+                                 size_t N, size_t K, const float* x, float* out, int* status,
+                                 LaunchStats* ls);
+cudaError_t launch_gemv_q4_0_generic(const DeviceInfo& dev, cudaStream_t st, int M,
+                                     const uint8_t* W, size_t N, size_t K, const float* x,
+                                     float* out, LaunchStats* ls);
+
+// ── tensor-core INT8 GEMM (gemm_tc.cu) ──────────────────────────────────────
+bool gemm_i8_tc_supported(const DeviceInfo& dev, size_t M, size_t N, size_t K);
+// xq [M,K] i8, W [N,K] i8 (both K-major), scale(s) in device memory.
+cudaError_t launch_gemm_i8_tc(const DeviceInfo& dev, cudaStream_t st, const int8_t* xq,
+                              const float* act_scale_dev, int scale_per_row, const int8_t* W,
+                              const float* w_scales, size_t M, size_t N, size_t K, float* out,
+                              int32_t* acc_out, int* status, LaunchStats* ls);
+
+}  // namespace mri

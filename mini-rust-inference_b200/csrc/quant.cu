@@ -1,0 +1,134 @@
+// quant.cu — K1: symmetric INT8 activation quantizer (quantize_symmetric,
+// src/quant/int8/symmetric.rs:42-57), per tensor or per row.
+//
+// Two passes over HBM/L2: an absmax reduction (order-independent, so the
+// scale is bit-identical to the reference's sequential fold) and the
+// element-wise quantization.  HBM-bound: 4 B read + 1 B written per element in
+// the second pass, 4 B read in the first.
+#include "common.cuh"
+#include "internal.h"
+
+namespace mri {
+namespace {
+
+constexpr int kQThreads = 256;
+
+// Per-tensor: every block folds its grid-stride share, then one atomicMax on
+// the float bit pattern (valid ordering for non-negative floats).
+__global__ void __launch_bounds__(kQThreads) absmax_tensor_kernel(const float* __restrict__ x,
+                                                                  size_t n, float* amax) {
+  float m = 0.0f;
+  const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+  size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if ((reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+    const size_t n4 = n / 4;
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    for (size_t j = i; j < n4; j += stride) {
+      const float4 v = __ldg(x4 + j);
+      m = absmax_acc(absmax_acc(absmax_acc(absmax_acc(m, v.x), v.y), v.z), v.w);
+    }
+    for (size_t j = n4 * 4 + i; j < n; j += stride) m = absmax_acc(m, __ldg(x + j));
+  } else {
+    for (size_t j = i; j < n; j += stride) m = absmax_acc(m, __ldg(x + j));
+  }
+  m = warp_max(m);
+  __shared__ float red[kQThreads / 32];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < kQThreads / 32 ? red[threadIdx.x] : 0.0f;
+    v = warp_max(v);
+    if (threadIdx.x == 0) atomicMax(reinterpret_cast<unsigned int*>(amax), __float_as_uint(v));
+  }
+}
+
+// Per-row: one block per row.
+__global__ void __launch_bounds__(kQThreads) absmax_row_kernel(const float* __restrict__ x,
+                                                               size_t k, float* amax) {
+  const float* row = x + static_cast<size_t>(blockIdx.x) * k;
+  float m = 0.0f;
+  for (size_t j = threadIdx.x; j < k; j += kQThreads) m = absmax_acc(m, __ldg(row + j));
+  m = warp_max(m);
+  __shared__ float red[kQThreads / 32];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < kQThreads / 32 ? red[threadIdx.x] : 0.0f;
+    v = warp_max(v);
+    if (threadIdx.x == 0) amax[blockIdx.x] = v;
+  }
+}
+
+__global__ void __launch_bounds__(kQThreads) quant_apply_kernel(const float* __restrict__ x,
+                                                                size_t m, size_t k, int per_row,
+                                                                const float* __restrict__ amax,
+                                                                int8_t* __restrict__ q,
+                                                                float* __restrict__ scale_out) {
+  const size_t n = m * k;
+  const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+  const size_t tid = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (!per_row) {
+    const float scale = sym_scale(amax[0]);
+    const float inv = __fdiv_rn(1.0f, scale);
+    if (tid == 0) scale_out[0] = scale;
+    if ((reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(q) & 3) == 0) {
+      const size_t n4 = n / 4;
+      for (size_t j = tid; j < n4; j += stride) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(x) + j);
+        char4 o;
+        o.x = sym_quant(v.x, inv);
+        o.y = sym_quant(v.y, inv);
+        o.z = sym_quant(v.z, inv);
+        o.w = sym_quant(v.w, inv);
+        reinterpret_cast<char4*>(q)[j] = o;
+      }
+      for (size_t j = n4 * 4 + tid; j < n; j += stride) q[j] = sym_quant(__ldg(x + j), inv);
+    } else {
+      for (size_t j = tid; j < n; j += stride) q[j] = sym_quant(__ldg(x + j), inv);
+    }
+  } else {
+    for (size_t r = tid; r < m; r += stride) scale_out[r] = sym_scale(amax[r]);
+    for (size_t j = tid; j < n; j += stride) {
+      const size_t r = j / k;
+      const float scale = sym_scale(amax[r]);
+      q[j] = sym_quant(__ldg(x + j), __fdiv_rn(1.0f, scale));
+    }
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_quantize(const DeviceInfo& dev, cudaStream_t st, const float* x, size_t m,
+                            size_t k, int per_row, int8_t* q, float* scale, float* amax_scratch,
+                            LaunchStats* ls) {
+  const size_t n = m * k;
+  if (n == 0) {
+    // Empty input: the reference's fold yields 0 -> scale 1.0.
+    if (!per_row) {
+      const float one = 1.0f;
+      return cudaMemcpyAsync(scale, &one, sizeof(float), cudaMemcpyHostToDevice, st);
+    }
+    if (m == 0) return cudaSuccess;
+  }
+  const int blocks = static_cast<int>(
+      std::min<size_t>(static_cast<size_t>(dev.sm_count) * 8, (n + kQThreads * 4 - 1) / (kQThreads * 4) + 1));
+  if (!per_row) {
+    cudaError_t e = cudaMemsetAsync(amax_scratch, 0, sizeof(float), st);
+    if (e != cudaSuccess) return e;
+    absmax_tensor_kernel<<<blocks, kQThreads, 0, st>>>(x, n, amax_scratch);
+  } else {
+    absmax_row_kernel<<<static_cast<unsigned>(m), kQThreads, 0, st>>>(x, k, amax_scratch);
+  }
+  if (ls) ls->launches++;
+  if (n > 0) {
+    quant_apply_kernel<<<blocks, kQThreads, 0, st>>>(x, m, k, per_row, amax_scratch, q, scale);
+    if (ls) ls->launches++;
+  } else {
+    // m > 0 rows of k == 0: every row scale is 1.0.
+    quant_apply_kernel<<<1, kQThreads, 0, st>>>(x, m, k, per_row, amax_scratch, q, scale);
+    if (ls) ls->launches++;
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace mri

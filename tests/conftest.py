@@ -18,3 +18,22 @@ def oracle():
     import oracle as _oracle
     _oracle.build()
     return _oracle
+
+
+def load_mri():
+    """The product package (directory name is not an identifier)."""
+    import importlib
+    return importlib.import_module("mini-rust-inference_b200")
+
+
+@pytest.fixture(scope="session")
+def mri():
+    return load_mri()
+
+
+@pytest.fixture(scope="session")
+def gpu_ctx(mri):
+    import torch
+    if not torch.cuda.is_available():
+        pytest.fail("GPU test collected on a machine without CUDA")
+    return mri.default_context(0)

@@ -1,0 +1,91 @@
+"""CPU-only checks of the boundary: the C-ABI library loads, exports every
+symbol include/*.h declares, fails loudly without a GPU, and the host-side
+weight codecs match the oracle bit for bit."""
+import glob
+import os
+import re
+
+import numpy as np
+import pytest
+
+from conftest import REPO
+
+
+def declared_symbols():
+    names = set()
+    for h in glob.glob(os.path.join(REPO, "include", "*.h")):
+        src = open(h).read()
+        names |= set(re.findall(r"MRI_API\s+[\w\s\*]+?\b(mri_\w+)\s*\(", src))
+    return names
+
+
+def test_header_declares_entry_points():
+    names = declared_symbols()
+    assert "mri_matmul_int8" in names and "mri_matmul_q8_0_direct" in names
+    assert len(names) >= 25
+
+
+def test_library_exports_every_declared_symbol(mri):
+    import ctypes
+    lib = ctypes.CDLL(mri.library_path())
+    missing = [n for n in sorted(declared_symbols()) if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_ctypes_table_matches_header(mri):
+    from importlib import import_module
+    table = import_module("mini-rust-inference_b200._lib").SIGNATURES
+    assert set(table) == declared_symbols()
+
+
+def test_library_links_cudart_statically(mri):
+    import subprocess
+    out = subprocess.run(["ldd", mri.library_path()], capture_output=True, text=True).stdout
+    assert "libcudart" not in out
+
+
+def test_no_gpu_fails_loudly(mri):
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    with pytest.raises(mri.CudaError):
+        mri.Context(0)
+
+
+@pytest.mark.parametrize("seed", [0, 1, 2])
+def test_q8_0_codec_matches_oracle(mri, oracle, seed):
+    rng = np.random.default_rng(seed)
+    n, k = 7, 256
+    w = rng.normal(0, 0.02 * (seed + 1), size=(n, k)).astype(np.float32)
+    w[0, :32] = 0.0                       # all-zero block -> scale 0, quants 0
+    w[1, 5] = np.float32(1e-6)            # tiny block scale (f16 subnormal branch)
+    w[1, 32:64] = np.float32(3e-6)
+    assert np.array_equal(mri.formats.quantize_q8_0(w, n, k), oracle.quantize_q8_0_matrix(w, n, k))
+
+
+@pytest.mark.parametrize("seed", [0, 1, 2])
+def test_q4_0_codec_matches_oracle(mri, oracle, seed):
+    rng = np.random.default_rng(seed)
+    n, k = 5, 128
+    w = rng.normal(0, 0.5, size=(n, k)).astype(np.float32)
+    w[2, :32] = 0.0                       # all-zero block -> 0x88 bytes
+    assert np.array_equal(mri.formats.quantize_q4_0(w, n, k), oracle.quantize_q4_0_matrix(w, n, k))
+
+
+def test_f16_truncation_matches_oracle(mri, oracle):
+    rng = np.random.default_rng(3)
+    vals = np.concatenate([rng.normal(0, 1e-4, 2000), rng.normal(0, 100, 2000),
+                           [0.0, -0.0, 65504.0, 70000.0, 1e-9, 6e-8, 6.1e-5, np.inf, -np.inf]]
+                          ).astype(np.float32)
+    got = mri.formats.f32_to_f16_trunc(vals)
+    want = np.array([oracle.f32_to_f16(v) for v in vals], dtype=np.uint16)
+    assert np.array_equal(got, want)
+
+
+def test_dequantize_codecs_match_oracle(mri, oracle):
+    rng = np.random.default_rng(4)
+    w = rng.normal(0, 1, size=(3, 64)).astype(np.float32)
+    b8 = oracle.quantize_q8_0_matrix(w, 3, 64)
+    b4 = oracle.quantize_q4_0_matrix(w, 3, 64)
+    assert np.array_equal(mri.formats.dequantize_q8_0(b8), oracle.dequantize_q8_0(b8))
+    assert np.array_equal(mri.formats.dequantize_q4_0(b4), oracle.dequantize_q4_0(b4))

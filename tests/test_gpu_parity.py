@@ -1,0 +1,283 @@
+"""GPU parity: the CUDA path (through the C ABI) against the CPU oracle.
+
+Bars (north_star): INT32 accumulators bit-exact; INT8 f32 outputs bit-exact
+(the reference epilogue is reproduced exactly, which is tighter than the
+1e-5 relative budget); Q8_0 bit-exact (block terms added in block order);
+Q4_0 within 1e-3 relative of the reference's sequential f32 sum, with an
+absolute floor of 1e-5 * sum_k |x_k * w_k| for outputs that cancel to ~0.
+"""
+import numpy as np
+import pytest
+
+from golden_checks import check_case, load_cases
+
+pytestmark = pytest.mark.gpu
+
+Q4_REL = 1e-3
+Q4_FLOOR = 1e-5
+
+
+class GpuImpl:
+    """golden_checks interface over the product package (GPU)."""
+
+    def __init__(self, mri, oracle):
+        self.mri, self.o = mri, oracle
+
+    def quantize_symmetric(self, x):
+        return self.mri.quantize_symmetric(x)
+
+    def quantize_per_channel(self, w, n, k):
+        qm = self.mri.quantize_per_channel(w, n, k)
+        return qm.data, qm.scales
+
+    def dot_i8(self, a, b):
+        k = a.size
+        qm = self.mri.QuantizedMatrix(b, np.ones(1, np.float32), 1, k)
+        acc = np.zeros((1, 1), dtype=np.int32)
+        self.mri.matmul_int8(a, 1.0, qm, 1, acc_out=acc)
+        return int(acc[0, 0])
+
+    def matmul_int8_from_f32(self, x, m, k, wq, ws, n, k_in):
+        qm = self.mri.QuantizedMatrix(wq, ws, n, k_in)
+        return self.mri.matmul_int8_from_f32(np.asarray(x, np.float32).reshape(m, k), qm)
+
+    def matmul_int8(self, aq, s, wq, ws, n, k_in, m):
+        qm = self.mri.QuantizedMatrix(wq, ws, n, k_in)
+        return self.mri.matmul_int8(aq, s, qm, m)
+
+    def int8_variants(self):
+        def wrap(fn):
+            return lambda aq, s, wq, ws, n, k_in, m: fn(aq, s, self.mri.QuantizedMatrix(wq, ws, n, k_in), m)
+        return [wrap(self.mri.matmul_int8_avx2), wrap(self.mri.matmul_int8_parallel)]
+
+    def q8_0_from_raw_ok(self, n_len, n, k):
+        try:
+            self.mri.Q8_0WeightMatrix.from_raw_bytes(np.zeros(n_len, np.uint8), n, k)
+            return True
+        except self.mri.InvalidShape:
+            return False
+
+    def matmul_q8_0_direct(self, x, m, k, wb, n, k_in):
+        w = self.mri.Q8_0WeightMatrix.from_raw_bytes(wb, n, k_in)
+        return self.mri.matmul_q8_0_direct(np.asarray(x, np.float32).reshape(m, k), w)
+
+    def matmul_q4_0(self, x, m, k, wb, n, k_in):
+        return self.mri.matmul_q4_0_dequant(np.asarray(x, np.float32).reshape(m, k), wb, n, k_in)
+
+    def dequantize_q8_0(self, d):
+        if np.asarray(d).size % 34:
+            raise type("AlignmentError", (Exception,), {"kind": "AlignmentError"})()
+        return self.mri.formats.dequantize_q8_0(d)
+
+    def dequantize_q4_0(self, d):
+        if np.asarray(d).size % 18:
+            raise type("AlignmentError", (Exception,), {"kind": "AlignmentError"})()
+        return self.mri.formats.dequantize_q4_0(d)
+
+    def create_q8_0_block(self, v):
+        return self.mri.formats.quantize_q8_0(v, 1, 32)
+
+    def create_q4_0_block(self, v):
+        return self.mri.formats.quantize_q4_0(v, 1, 32)
+
+    def f16_to_f32(self, h):
+        return self.mri.formats.f16_to_f32(np.array([h], np.uint16))[0]
+
+    def f32_to_f16(self, f):
+        return int(self.mri.formats.f32_to_f16_trunc(np.array([f], np.float32))[0])
+
+
+CASES = load_cases()
+
+
+@pytest.mark.parametrize("case", CASES, ids=[c["id"] for c in CASES])
+def test_gpu_known_answer(case, mri, oracle, gpu_ctx):
+    check_case(GpuImpl(mri, oracle), case, oracle)
+
+
+def bits(a):
+    return np.ascontiguousarray(a, dtype=np.float32).view(np.uint32)
+
+
+def rand_case(rng, m, n, k, x_sigma=1.0):
+    x = rng.normal(0, x_sigma, size=(m, k)).astype(np.float32)
+    wq = rng.integers(-127, 128, size=n * k, dtype=np.int8)
+    ws = rng.uniform(0.001, 0.02, size=n).astype(np.float32)
+    return x, wq, ws
+
+
+INT8_SHAPES = [(1, 11008, 4096), (1, 1, 16), (1, 7, 33), (2, 33, 32), (3, 100, 100), (4, 257, 4096),
+               (5, 1000, 512), (6, 64, 48), (7, 129, 1024), (8, 511, 4096), (8, 3, 4099), (9, 40, 64),
+               (17, 300, 256), (31, 130, 4096), (32, 16, 32), (64, 96, 128), (1, 5, 0)]
+
+
+@pytest.mark.parametrize("m,n,k", INT8_SHAPES)
+def test_int8_from_f32_bit_exact(m, n, k, mri, oracle, gpu_ctx):
+    rng = np.random.default_rng(1000 + m * 7 + n + k)
+    x, wq, ws = rand_case(rng, m, n, k)
+    qm = mri.QuantizedMatrix(wq, ws, n, k)
+    got = mri.matmul_int8_from_f32(x, qm)
+    want = oracle.matmul_int8_from_f32(x, m, k, wq, ws, n, k)
+    assert got.shape == (m, n)
+    assert np.array_equal(bits(got), bits(want))
+
+
+@pytest.mark.parametrize("m,n,k", INT8_SHAPES)
+def test_int8_prequantized_acc_bit_exact(m, n, k, mri, oracle, gpu_ctx):
+    rng = np.random.default_rng(2000 + m + n * 3 + k)
+    x, wq, ws = rand_case(rng, m, n, k)
+    aq, s = oracle.quantize_symmetric(x)
+    qm = mri.QuantizedMatrix(wq, ws, n, k)
+    acc = np.zeros((m, n), dtype=np.int32)
+    got = mri.matmul_int8(aq, s, qm, m, acc_out=acc)
+    want, want_acc = oracle.matmul_int8(aq, s, wq, ws, n, k, m)
+    assert np.array_equal(acc, want_acc)
+    assert np.array_equal(bits(got), bits(want))
+
+
+def test_int8_extreme_values(mri, oracle, gpu_ctx):
+    """All +-127 (max |acc|) and -128 weights (reachable through the raw
+    QuantizedMatrix fields) stay exact."""
+    m, n, k = 4, 64, 4096
+    aq = np.full(m * k, 127, np.int8)
+    aq[k:2 * k] = -127
+    wq = np.full(n * k, 127, np.int8)
+    wq[: k] = -128
+    ws = np.ones(n, np.float32)
+    qm = mri.QuantizedMatrix(wq, ws, n, k)
+    acc = np.zeros((m, n), np.int32)
+    got = mri.matmul_int8(aq, np.float32(1.0), qm, m, acc_out=acc)
+    want, want_acc = oracle.matmul_int8(aq, np.float32(1.0), wq, ws, n, k, m)
+    assert np.array_equal(acc, want_acc) and np.array_equal(bits(got), bits(want))
+
+
+def test_int8_device_tensors_match_host(mri, oracle, gpu_ctx):
+    import torch
+    rng = np.random.default_rng(5)
+    m, n, k = 8, 2048, 4096
+    x, wq, ws = rand_case(rng, m, n, k)
+    qm = mri.QuantizedMatrix(wq, ws, n, k)
+    xd = torch.from_numpy(x).cuda()
+    got = mri.matmul_int8_from_f32(xd, qm)
+    qm.ctx.synchronize()
+    want = oracle.matmul_int8_from_f32(x, m, k, wq, ws, n, k)
+    assert np.array_equal(bits(got.cpu().numpy()), bits(want))
+
+
+@pytest.mark.parametrize("m,k", [(1, 4096), (8, 4096), (3, 100), (16, 4096), (512, 4096)])
+def test_int8_per_row_granularity(m, k, mri, oracle, gpu_ctx):
+    rng = np.random.default_rng(77 + m)
+    n = 300
+    x, wq, ws = rand_case(rng, m, n, k)
+    x[1 % m] *= 50.0
+    qm = mri.QuantizedMatrix(wq, ws, n, k)
+    got = mri.matmul_int8_from_f32(x, qm, granularity=1)
+    for r in range(m):
+        aq, s = oracle.quantize_symmetric(x[r])
+        want, _ = oracle.matmul_int8(aq, s, wq, ws, n, k, 1)
+        assert np.array_equal(bits(got[r:r + 1]), bits(want)), r
+
+
+@pytest.mark.parametrize("m,k", [(1, 4096), (8, 4096), (512, 4096), (3, 7), (1, 1), (64, 8192)])
+def test_quantizer_bit_exact(m, k, mri, oracle, gpu_ctx):
+    rng = np.random.default_rng(m * 31 + k)
+    x = rng.normal(0, 1, size=(m, k)).astype(np.float32)
+    x.reshape(-1)[0] = 0.5 * np.abs(x).max()  # exercise exact half-way candidates
+    q, s = mri.quantize_symmetric(x)
+    q2, s2 = oracle.quantize_symmetric(x)
+    assert np.float32(s) == s2 and np.array_equal(q, q2)
+    qr, sr = mri.quantize_symmetric_rows(x, m, k)
+    qr2, sr2 = oracle.quantize_symmetric_rows(x, m, k)
+    assert np.array_equal(bits(sr), bits(sr2)) and np.array_equal(qr, qr2)
+
+
+def test_quantizer_specials(mri, oracle, gpu_ctx):
+    x = np.array([0.0, -0.0, np.nan, 1.0, -2.0, np.inf, 3.0, -np.inf], np.float32)
+    for vals in (x[:2], x[:5], x, np.zeros(16, np.float32), np.array([np.nan, 1.0], np.float32)):
+        q, s = mri.quantize_symmetric(vals)
+        q2, s2 = oracle.quantize_symmetric(vals)
+        assert np.array_equal(q, q2)
+        assert (np.isnan(s) and np.isnan(s2)) or np.float32(s) == s2
+
+
+def test_quantize_per_channel_matches_oracle(mri, oracle, gpu_ctx):
+    rng = np.random.default_rng(9)
+    n, k = 300, 1000
+    w = rng.normal(0, 0.02, size=(n, k)).astype(np.float32)
+    w[3] = 0
+    qm = mri.quantize_per_channel(w, n, k)
+    d2, s2 = oracle.quantize_per_channel(w, n, k)
+    assert np.array_equal(qm.data, d2) and np.array_equal(bits(qm.scales), bits(s2))
+
+
+Q8_SHAPES = [(1, 11008, 4096), (8, 11008, 4096), (1, 1, 32), (2, 33, 64), (3, 100, 96), (5, 77, 1024),
+             (8, 9, 4096), (9, 50, 256), (1, 64, 28672), (4, 20, 40960), (16, 128, 512)]
+
+
+@pytest.mark.parametrize("m,n,k", Q8_SHAPES)
+def test_q8_0_bit_exact(m, n, k, mri, oracle, gpu_ctx):
+    rng = np.random.default_rng(3000 + m + n + k)
+    w = rng.normal(0, 0.02, size=(n, k)).astype(np.float32)
+    x = rng.normal(0, 1, size=(m, k)).astype(np.float32)
+    wb = oracle.quantize_q8_0_matrix(w, n, k)
+    W = mri.Q8_0WeightMatrix.from_raw_bytes(wb, n, k)
+    got = mri.matmul_q8_0_direct(x, W)
+    want = oracle.matmul_q8_0_direct(x, m, k, wb, n, k)
+    assert np.array_equal(bits(got), bits(want))
+
+
+def q4_close(got, want, x, wdeq):
+    floor = Q4_FLOOR * (np.abs(x) @ np.abs(wdeq).T)
+    err = np.abs(got - want)
+    return np.all(err <= np.maximum(Q4_REL * np.abs(want), floor)), float(np.max(err / np.maximum(np.abs(want), 1e-30)))
+
+
+@pytest.mark.parametrize("m,n,k", Q8_SHAPES)
+def test_q4_0_within_tolerance(m, n, k, mri, oracle, gpu_ctx):
+    rng = np.random.default_rng(4000 + m + n + k)
+    w = rng.normal(0, 0.02, size=(n, k)).astype(np.float32)
+    x = rng.normal(0, 1, size=(m, k)).astype(np.float32)
+    wb = oracle.quantize_q4_0_matrix(w, n, k)
+    got = mri.matmul_q4_0_dequant(x, wb, n, k)
+    want = oracle.matmul_q4_0_dequant(x, m, k, wb, n, k)
+    ok, worst = q4_close(got, want, x, oracle.dequantize_q4_0(wb).reshape(n, k))
+    assert ok, worst
+
+
+def test_sharded_equals_unsharded(mri, oracle, gpu_ctx):
+    """An N-column shard computes bit-identical columns (the per-(m, n)
+    arithmetic does not depend on the other rows of W)."""
+    rng = np.random.default_rng(11)
+    m, n, k = 3, 1376 * 4 + 5, 4096
+    x, wq, ws = rand_case(rng, m, n, k)
+    full = mri.matmul_int8_from_f32(x, mri.QuantizedMatrix(wq, ws, n, k))
+    parts = []
+    P = 4
+    for r in range(P):
+        b, e = n * r // P, n * (r + 1) // P
+        parts.append(mri.matmul_int8_from_f32(x, mri.QuantizedMatrix(wq, ws, n, k, rows=(b, e))))
+    assert np.array_equal(bits(np.concatenate(parts, axis=1)), bits(full))
+
+
+def test_prefill_shape_sampled_rows_exact(mri, oracle, gpu_ctx):
+    """BASELINE prefill config [512,4096]x[4096,11008]: all INT32 accumulators
+    of 12 sampled rows equal the oracle's; the per-tensor scale is global."""
+    rng = np.random.default_rng(1)
+    m, n, k = 512, 11008, 4096
+    x = rng.normal(0, 1, size=(m, k)).astype(np.float32)
+    wf = rng.normal(0, 0.02, size=(n, k)).astype(np.float32)
+    wq, ws = oracle.quantize_per_channel(wf, n, k)
+    qm = mri.QuantizedMatrix(wq, ws, n, k)
+    aq, s = oracle.quantize_symmetric(x)
+    acc = np.zeros((m, n), np.int32)
+    got = mri.matmul_int8(aq, s, qm, m, acc_out=acc)
+    rows = rng.choice(m, size=12, replace=False)
+    sub = aq.reshape(m, k)[rows].reshape(-1)
+    want, want_acc = oracle.matmul_int8(sub, s, wq, ws, n, k, len(rows))
+    assert np.array_equal(acc[rows], want_acc)
+    assert np.array_equal(bits(got[rows]), bits(want))
+
+
+def test_device_status_clean(mri, gpu_ctx):
+    """No bounded device-side wait gave up during the tests above."""
+    gpu_ctx.check_device_status()

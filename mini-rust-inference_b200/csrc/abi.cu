@@ -159,7 +159,7 @@ int run_int8(mri_ctx* ctx, ActArgs act, const mri_qmatrix* w, size_t m, float* o
     sdev = scales;
   }
 
-  if (mri::gemm_i8_tc_supported(ctx->dev, m, N, K)) {
+  if (mri::gemm_i8_tc_supported(ctx->dev, m, N, K) && (reinterpret_cast<uintptr_t>(xq) & 15) == 0) {
     MRI_CUDA_TRY(mri::launch_gemm_i8_tc(ctx->dev, st, xq, sdev, per_row, w->data, w->scales, m, N,
                                         K, out, acc, ctx->d_status, &ctx->ls));
     return MRI_OK;
@@ -634,7 +634,7 @@ int mri_host_matmul_q4_0_dequant(mri_ctx* ctx, const float* x, size_t m, size_t 
 int mri_int8_path(mri_ctx* ctx, size_t m, size_t n, size_t k) {
   if (!ctx) return -1;
   if (m <= 8 && m > 0 && mri::gemv_i8_tma_supported(ctx->dev, static_cast<int>(m), k)) return 0;
-  if (mri::gemm_i8_tc_supported(ctx->dev, m, n, k)) return 2;
+  if (mri::gemm_i8_tc_supported(ctx->dev, m, n, k)) return 2;  // (16-byte aligned activations)
   return 1;
 }
 

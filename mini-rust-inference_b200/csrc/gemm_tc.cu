@@ -1,15 +1,398 @@
-// gemm_tc.cu — K3: tcgen05 INT8 GEMM (placeholder until the tensor-core
-// kernel lands; the dispatcher then uses the streaming GEMV per 8-row chunk).
+// gemm_tc.cu — K3: INT8 x INT8 -> INT32 GEMM on the 5th-generation tensor
+// cores (tcgen05.mma kind::i8, accumulators in TMEM) with the reference's
+// rescale fused into the epilogue:  out[m,n] = ((f32)acc * s_a) * s_w[n]
+// (ops/matmul/int8.rs:93, parallel.rs:340).
+//
+// C[M,N] = A[M,K] * B[N,K]^T with A = quantized activations and B = the
+// QuantizedMatrix rows; both are K-major, which is the "TN" form tcgen05
+// reads directly.  The INT32 sums are exact (no saturation), so the result
+// is bit-identical to the reference's scalar loop.
+//
+// Persistent kernel, one CTA per SM, warp-specialised:
+//   warp 0      : TMA producer.  2-D tiled loads (128-byte swizzle, no
+//                 multicast) of a 128 x 128 A tile and a BN x 128 B tile per
+//                 stage into a kStages-deep shared-memory ring.
+//   warp 1      : allocates 2*BN TMEM columns (two accumulator buffers);
+//                 one lane issues tcgen05.mma (M=128, N=BN, K=32 per
+//                 instruction) and tcgen05.commit's stage releases and
+//                 "accumulator ready" signals to mbarriers.
+//   warps 2..5  : epilogue.  tcgen05.ld of their 32-lane TMEM quarter,
+//                 rescale, vectorised f32 stores; the other accumulator
+//                 buffer is being filled meanwhile.
+// Every mbarrier wait is bounded; a timeout records MRI_ERR_TIMEOUT, raises
+// a CTA-wide abort flag, drains in-flight copies / MMAs, frees TMEM, returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstdlib>
+#include <map>
+#include <mutex>
+#include <utility>
+
+#include "common.cuh"
 #include "internal.h"
 
 namespace mri {
+namespace {
 
-bool gemm_i8_tc_supported(const DeviceInfo&, size_t, size_t, size_t) { return false; }
+constexpr int BM = 128;
+constexpr int BK = 128;  // K bytes per stage = one 128-byte swizzle row
+constexpr int UMMA_K = 32;
+constexpr int kStages = 4;
+constexpr int kEpiWarps = 4;
+constexpr int kTcThreads = 32 * (2 + kEpiWarps);
 
-cudaError_t launch_gemm_i8_tc(const DeviceInfo&, cudaStream_t, const int8_t*, const float*, int,
-                              const int8_t*, const float*, size_t, size_t, size_t, float*,
-                              int32_t*, int*, LaunchStats*) {
-  return cudaErrorNotSupported;
+template <int BN>
+struct TcLayout {
+  static constexpr size_t a_bytes = BM * BK;
+  static constexpr size_t b_bytes = BN * BK;
+  static constexpr size_t stage_bytes = a_bytes + b_bytes;
+  static constexpr size_t bars = kStages * stage_bytes;
+  // full[S], empty[S], tfull[2], tempty[2], mma_done, abort flag + tmem slot
+  static constexpr size_t bars_bytes = (2 * kStages + 5) * 8 + 16;
+  static constexpr size_t total = bars + bars_bytes + 1024;  // + alignment slack
+};
+
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, int* status,
+                                              volatile int* abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  for (int i = 0;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 63) == 0 && *abort_flag) return false;
+    if (clock64() - t0 > kWaitBudgetClocks) {
+      if (status) atomicExch(status, MRI_ERR_TIMEOUT);
+      *abort_flag = 1;
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, int x, int y,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(smem_addr(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+
+// K-major operand, 128-byte swizzle: rows of 128 bytes, 8-row atoms of 1024
+// bytes (SBO), LBO unused (1), descriptor version 1, layout type 2.
+__device__ __forceinline__ uint64_t smem_desc_sw128(const void* p) {
+  const uint32_t a = smem_addr(p);
+  return (uint64_t((a >> 4) & 0x3FFF)) | (uint64_t(1) << 16) | (uint64_t(1024 >> 4) << 32) |
+         (uint64_t(1) << 46) | (uint64_t(2) << 61);
+}
+
+// kind::i8 instruction descriptor: D s32, A/B signed 8-bit, both K-major.
+template <int BN>
+__device__ __forceinline__ uint32_t idesc_i8() {
+  return (2u << 4) | (1u << 7) | (1u << 10) | (uint32_t(BN >> 3) << 17) | (uint32_t(BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                        uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_addr(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld_32cols(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+        "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]),
+        "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]),
+        "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+template <int BN>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                      const float* __restrict__ act_scale, int scale_per_row,
+                      const float* __restrict__ w_scales, float* __restrict__ out,
+                      int32_t* __restrict__ acc_out, int M, int N, int K, int* status) {
+  using L = TcLayout<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_addr(smem_raw);
+  uint8_t* smem = smem_raw + ((1024 - (raw & 1023)) & 1023);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::bars);
+  uint64_t* empty = full + kStages;
+  uint64_t* tfull = empty + kStages;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* mma_done = tempty + 2;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(mma_done + 1);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1) + 1;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m_tiles = (M + BM - 1) / BM, n_tiles = (N + BN - 1) / BN;
+  const int num_tiles = m_tiles * n_tiles;
+  const int kblocks = (K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], kEpiWarps);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_addr(tmem_slot)),
+                 "r"(2 * BN)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
+      int it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int m_blk = tile % m_tiles, n_blk = tile / m_tiles;
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = it % kStages;
+          if (it >= kStages && !wait_or_abort(&empty[s], ((it / kStages) - 1) & 1, status, abort_flag)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + s * L::stage_bytes;
+          mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(L::stage_bytes));
+          tma_load_2d(sa, &tmA, kb * BK, m_blk * BM, &full[s]);
+          tma_load_2d(sa + L::a_bytes, &tmB, kb * BK, n_blk * BN, &full[s]);
+        }
+      }
+      // Drain: every copy issued by this thread has landed before it exits.
+      for (int j = std::max(0, it - kStages); j < it; ++j)
+        mbar_wait(&full[j % kStages], (j / kStages) & 1, status);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_i8<BN>();
+      int it = 0, t = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++t) {
+        const int b = t & 1;
+        if (t >= 2 && !wait_or_abort(&tempty[b], ((t >> 1) - 1) & 1, status, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + b * BN;
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = it % kStages;
+          if (!wait_or_abort(&full[s], (it / kStages) & 1, status, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint8_t* sa = smem + s * L::stage_bytes;
+          const uint64_t adesc = smem_desc_sw128(sa);
+          const uint64_t bdesc = smem_desc_sw128(sa + L::a_bytes);
+#pragma unroll
+          for (int j = 0; j < BK / UMMA_K; ++j)
+            umma_i8(d_tmem, adesc + 2 * j, bdesc + 2 * j, idesc, (kb | j) != 0);
+          umma_commit(&empty[s]);
+        }
+        if (ok) umma_commit(&tfull[b]);
+      }
+      // All MMAs issued by this thread are complete before TMEM is freed.
+      umma_commit(mma_done);
+      mbar_wait(mma_done, 0, status);
+    }
+    __syncwarp();
+  } else {
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    int t = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++t) {
+      const int b = t & 1;
+      // Warp-uniform outcome: tcgen05.ld below is a .sync.aligned warp op.
+      const bool ok = wait_or_abort(&tfull[b], (t >> 1) & 1, status, abort_flag);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      tc_fence_after();
+      const int m_blk = tile % m_tiles, n_blk = tile / m_tiles;
+      const int row = m_blk * BM + q * 32 + lane;
+      const float s_a = scale_per_row ? (row < M ? act_scale[row] : 0.0f) : act_scale[0];
+      float* orow = out + static_cast<size_t>(row) * N;
+      int32_t* arow = acc_out ? acc_out + static_cast<size_t>(row) * N : nullptr;
+      const bool vec = (N % 4) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0 &&
+                       (reinterpret_cast<uintptr_t>(acc_out) & 15) == 0;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld_32cols(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + b * BN + c * 32, v);
+        const int col0 = n_blk * BN + c * 32;
+        if (row < M) {
+          if (vec && col0 + 32 <= N) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+              const float4 sw = __ldg(reinterpret_cast<const float4*>(w_scales + col0 + j));
+              float4 o;
+              o.x = rescale(static_cast<int>(v[j]), s_a, sw.x);
+              o.y = rescale(static_cast<int>(v[j + 1]), s_a, sw.y);
+              o.z = rescale(static_cast<int>(v[j + 2]), s_a, sw.z);
+              o.w = rescale(static_cast<int>(v[j + 3]), s_a, sw.w);
+              *reinterpret_cast<float4*>(orow + col0 + j) = o;
+              if (arow)
+                *reinterpret_cast<int4*>(arow + col0 + j) =
+                    make_int4(static_cast<int>(v[j]), static_cast<int>(v[j + 1]),
+                              static_cast<int>(v[j + 2]), static_cast<int>(v[j + 3]));
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int col = col0 + j;
+              if (col < N) {
+                orow[col] = rescale(static_cast<int>(v[j]), s_a, __ldg(w_scales + col));
+                if (arow) arow[col] = static_cast<int>(v[j]);
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[b]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(2 * BN)
+                 : "memory");
+  }
+}
+
+// ── host side ────────────────────────────────────────────────────────────────
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+bool make_map(CUtensorMap* tm, const void* base, size_t rows, size_t k, int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(k)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(BK), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <typename KernelT>
+cudaError_t set_smem_tc(KernelT k, size_t bytes, int device) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, size_t> done;
+  std::lock_guard<std::mutex> lock(mu);
+  const auto key = std::make_pair(reinterpret_cast<const void*>(k), device);
+  auto it = done.find(key);
+  if (it != done.end() && bytes <= it->second) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(bytes));
+  if (e == cudaSuccess) done[key] = bytes;
+  return e;
+}
+
+// Tile width: the one whose wave count times tile width is smallest (ties
+// go to the wider tile, which reads less shared memory per MAC).
+int pick_bn(const DeviceInfo& dev, size_t M, size_t N) {
+  if (const char* e = std::getenv("MRI_GEMM_BN")) {
+    const int v = std::atoi(e);
+    if (v == 128 || v == 256) return v;
+  }
+  const size_t mt = (M + BM - 1) / BM;
+  auto cost = [&](size_t bn) {
+    const size_t tiles = mt * ((N + bn - 1) / bn);
+    return ((tiles + dev.sm_count - 1) / dev.sm_count) * bn;
+  };
+  return cost(128) < cost(256) ? 128 : 256;
+}
+
+template <int BN>
+cudaError_t launch_bn(const DeviceInfo& dev, cudaStream_t st, const CUtensorMap& ta,
+                      const CUtensorMap& tb, const float* act_scale, int per_row,
+                      const float* w_scales, size_t M, size_t N, size_t K, float* out,
+                      int32_t* acc_out, int* status) {
+  const size_t smem = TcLayout<BN>::total;
+  cudaError_t e = set_smem_tc(gemm_i8_tc_kernel<BN>, smem, dev.device);
+  if (e != cudaSuccess) return e;
+  const size_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  const int grid = static_cast<int>(std::min<size_t>(tiles, dev.sm_count));
+  gemm_i8_tc_kernel<BN><<<grid, kTcThreads, smem, st>>>(
+      ta, tb, act_scale, per_row, w_scales, out, acc_out, static_cast<int>(M), static_cast<int>(N),
+      static_cast<int>(K), status);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+bool gemm_i8_tc_supported(const DeviceInfo& dev, size_t M, size_t N, size_t K) {
+  if (dev.cc_major != 10) return false;
+  if (M < 1 || N < 1 || K < 16 || K % 16 != 0) return false;
+  if (M > (1u << 30) || N > (1u << 30) || K > (1u << 30)) return false;
+  return encode_fn() != nullptr;
+}
+
+cudaError_t launch_gemm_i8_tc(const DeviceInfo& dev, cudaStream_t st, const int8_t* xq,
+                              const float* act_scale_dev, int scale_per_row, const int8_t* W,
+                              const float* w_scales, size_t M, size_t N, size_t K, float* out,
+                              int32_t* acc_out, int* status, LaunchStats* ls) {
+  if ((reinterpret_cast<uintptr_t>(xq) & 15) || (reinterpret_cast<uintptr_t>(W) & 15))
+    return cudaErrorMisalignedAddress;
+  const int bn = pick_bn(dev, M, N);
+  CUtensorMap ta, tb;
+  if (!make_map(&ta, xq, M, K, BM) || !make_map(&tb, W, N, K, bn)) return cudaErrorInvalidValue;
+  cudaError_t e = bn == 128 ? launch_bn<128>(dev, st, ta, tb, act_scale_dev, scale_per_row, w_scales,
+                                             M, N, K, out, acc_out, status)
+                            : launch_bn<256>(dev, st, ta, tb, act_scale_dev, scale_per_row, w_scales,
+                                             M, N, K, out, acc_out, status);
+  if (ls) ls->launches++;
+  return e;
 }
 
 }  // namespace mri

@@ -64,6 +64,9 @@ class GpuImpl:
     def matmul_q4_0(self, x, m, k, wb, n, k_in):
         return self.mri.matmul_q4_0_dequant(np.asarray(x, np.float32).reshape(m, k), wb, n, k_in)
 
+    def q4_close(self, got, want, x, wdeq):
+        return q4_close(got, want, x, wdeq)[0]
+
     def dequantize_q8_0(self, d):
         if np.asarray(d).size % 34:
             raise type("AlignmentError", (Exception,), {"kind": "AlignmentError"})()

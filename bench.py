@@ -201,15 +201,18 @@ def graph_of(torch, stream, fn):
 
 
 def time_graph(torch, stream, g, steps, warmup):
-    for _ in range(warmup):
-        g.replay()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(steps):
-        g.replay()
-    e1.record(stream)
-    e1.synchronize()
+    # CUDAGraph.replay() launches on the current stream: make it `stream`,
+    # the one the events are recorded on.
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            g.replay()
+        e1.record(stream)
+        e1.synchronize()
     return e0.elapsed_time(e1)
 
 
@@ -323,14 +326,15 @@ def run_ours(args, rank, world, local_rank):
     g = graph_of(torch, s, body)
     launches_per_step = ctx.launch_count - n0
 
-    for _ in range(args.warmup):
-        g.replay()
+    with torch.cuda.stream(s):  # replay() launches on the current stream
+        for _ in range(args.warmup):
+            g.replay()
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(device) as clk:
+    with ClockSampler(device) as clk, torch.cuda.stream(s):
         e0.record(s)
         for _ in range(args.steps):
             g.replay()

@@ -20,7 +20,8 @@ struct mri_ctx {
   cudaStream_t stream = nullptr;
   bool own_stream = false;
   mri::DeviceInfo dev;
-  int* d_status = nullptr;
+  int* d_status = nullptr;   // device view of the status word
+  int* h_status = nullptr;   // host view (mapped pinned memory)
   uint8_t* scratch = nullptr;
   size_t scratch_bytes = 0;
   mri::LaunchStats ls;
@@ -243,6 +244,17 @@ int check_k(const char* fn, size_t m, size_t k, size_t k_w) {
   return MRI_OK;
 }
 
+// Reads and clears the mapped status word (the stream must be idle).
+int read_status(mri_ctx* ctx) {
+  volatile int* hs = ctx->h_status;
+  const int st = *hs;
+  if (st != MRI_OK) {
+    *hs = MRI_OK;
+    return fail(st, "a device-side bounded wait timed out");
+  }
+  return MRI_OK;
+}
+
 // Host-call staging: [x | act_q] [out] [acc] in scratch after the quantizer area.
 struct HostStage {
   uint8_t* in;
@@ -306,8 +318,14 @@ static int ctx_create(int device, void* stream, bool own, mri_ctx** out) {
     c->stream = static_cast<cudaStream_t>(stream);
   }
   c->own_stream = own;
-  e = cudaMalloc(&c->d_status, sizeof(int));
-  if (e == cudaSuccess) e = cudaMemset(c->d_status, 0, sizeof(int));
+  // The status word lives in mapped pinned host memory: kernels store to it
+  // through the device alias and the host reads it after a stream sync, with
+  // no extra copy.
+  e = cudaHostAlloc(&c->h_status, sizeof(int), cudaHostAllocMapped);
+  if (e == cudaSuccess) {
+    *c->h_status = 0;
+    e = cudaHostGetDevicePointer(&c->d_status, c->h_status, 0);
+  }
   if (e != cudaSuccess) {
     if (own) cudaStreamDestroy(c->stream);
     delete c;
@@ -328,7 +346,7 @@ int mri_ctx_destroy(mri_ctx* ctx) {
   use_device(ctx->device);
   cudaStreamSynchronize(ctx->stream);
   if (ctx->scratch) cudaFree(ctx->scratch);
-  if (ctx->d_status) cudaFree(ctx->d_status);
+  if (ctx->h_status) cudaFreeHost(ctx->h_status);
   if (ctx->own_stream) cudaStreamDestroy(ctx->stream);
   delete ctx;
   return MRI_OK;
@@ -344,12 +362,8 @@ void* mri_ctx_stream(mri_ctx* ctx) { return ctx ? static_cast<void*>(ctx->stream
 
 int mri_ctx_check_device_status(mri_ctx* ctx) {
   if (int rc = enter(ctx)) return rc;
-  int st = 0;
   MRI_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
-  MRI_CUDA_TRY(cudaMemcpy(&st, ctx->d_status, sizeof(int), cudaMemcpyDeviceToHost));
-  MRI_CUDA_TRY(cudaMemset(ctx->d_status, 0, sizeof(int)));
-  if (st != MRI_OK) return fail(st, "a device-side bounded wait timed out");
-  return MRI_OK;
+  return read_status(ctx);
 }
 
 uint64_t mri_ctx_launch_count(const mri_ctx* ctx) { return ctx ? ctx->ls.launches : 0; }
@@ -557,7 +571,7 @@ int mri_host_quantize_symmetric(mri_ctx* ctx, const float* x, size_t m, size_t k
   if (m * k) MRI_CUDA_TRY(cudaMemcpyAsync(q, qd, m * k, cudaMemcpyDeviceToHost, ctx->stream));
   if (ns) MRI_CUDA_TRY(cudaMemcpyAsync(scale, hs.out, ns * 4, cudaMemcpyDeviceToHost, ctx->stream));
   MRI_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
-  return mri_ctx_check_device_status(ctx);
+  return read_status(ctx);
 }
 
 int mri_host_matmul_int8(mri_ctx* ctx, const int8_t* act_q, size_t act_len, float act_scale,
@@ -580,7 +594,7 @@ int mri_host_matmul_int8(mri_ctx* ctx, const int8_t* act_q, size_t act_len, floa
     if (acc) MRI_CUDA_TRY(cudaMemcpyAsync(acc, hs.acc, m * N * 4, cudaMemcpyDeviceToHost, ctx->stream));
   }
   MRI_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
-  return mri_ctx_check_device_status(ctx);
+  return read_status(ctx);
 }
 
 int mri_host_matmul_int8_from_f32(mri_ctx* ctx, const float* x, size_t m, size_t k,
@@ -598,7 +612,7 @@ int mri_host_matmul_int8_from_f32(mri_ctx* ctx, const float* x, size_t m, size_t
   if (int rc = run_int8(ctx, a, w, m, hs.out, nullptr)) return rc;
   if (m * N) MRI_CUDA_TRY(cudaMemcpyAsync(out, hs.out, m * N * 4, cudaMemcpyDeviceToHost, ctx->stream));
   MRI_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
-  return mri_ctx_check_device_status(ctx);
+  return read_status(ctx);
 }
 
 int mri_host_matmul_q8_0_direct(mri_ctx* ctx, const float* x, size_t m, size_t k,
@@ -613,7 +627,7 @@ int mri_host_matmul_q8_0_direct(mri_ctx* ctx, const float* x, size_t m, size_t k
   if (int rc = run_q8_0(ctx, reinterpret_cast<float*>(hs.in), m, w, hs.out)) return rc;
   if (m * N) MRI_CUDA_TRY(cudaMemcpyAsync(out, hs.out, m * N * 4, cudaMemcpyDeviceToHost, ctx->stream));
   MRI_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
-  return mri_ctx_check_device_status(ctx);
+  return read_status(ctx);
 }
 
 int mri_host_matmul_q4_0_dequant(mri_ctx* ctx, const float* x, size_t m, size_t k,
@@ -628,7 +642,7 @@ int mri_host_matmul_q4_0_dequant(mri_ctx* ctx, const float* x, size_t m, size_t 
   if (int rc = run_q4_0(ctx, reinterpret_cast<float*>(hs.in), m, w, hs.out)) return rc;
   if (m * N) MRI_CUDA_TRY(cudaMemcpyAsync(out, hs.out, m * N * 4, cudaMemcpyDeviceToHost, ctx->stream));
   MRI_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
-  return mri_ctx_check_device_status(ctx);
+  return read_status(ctx);
 }
 
 int mri_int8_path(mri_ctx* ctx, size_t m, size_t n, size_t k) {

@@ -60,7 +60,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
   for (;;) {
     if (mbar_try_wait(bar, parity)) return true;
     if (clock64() - t0 > kWaitBudgetClocks) {
-      if (status) atomicExch(status, MRI_ERR_TIMEOUT);
+      if (status) *reinterpret_cast<volatile int*>(status) = MRI_ERR_TIMEOUT;
       return false;
     }
   }

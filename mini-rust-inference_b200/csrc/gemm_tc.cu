@@ -62,7 +62,7 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, in
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 63) == 0 && *abort_flag) return false;
     if (clock64() - t0 > kWaitBudgetClocks) {
-      if (status) atomicExch(status, MRI_ERR_TIMEOUT);
+      if (status) *reinterpret_cast<volatile int*>(status) = MRI_ERR_TIMEOUT;
       *abort_flag = 1;
       return false;
     }

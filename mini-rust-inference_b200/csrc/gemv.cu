@@ -134,7 +134,36 @@ __device__ void load_act_i8_rowmajor(const ActArgs& act, size_t K, int8_t* s_act
                                      float* red) {
   const int ct = threadIdx.x - 32;
   const size_t total = static_cast<size_t>(M) * K;
-  if (act.mode == ACT_F32_PER_TENSOR || act.mode == ACT_F32_PER_ROW) {
+  constexpr int kRegVec = 4;  // float4 per consumer thread held in registers
+  if (act.mode == ACT_F32_PER_TENSOR && (reinterpret_cast<uintptr_t>(act.x) & 15) == 0 &&
+      total % 4 == 0 && total <= static_cast<size_t>(kRegVec) * 4 * kConsumerThreads) {
+    // Small per-tensor input (decode): one global read, values kept in
+    // registers between the absmax and the quantization pass.
+    const float4* x4 = reinterpret_cast<const float4*>(act.x);
+    float4 v[kRegVec];
+    float m = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kRegVec; ++j) {
+      const size_t i = ct + static_cast<size_t>(j) * kConsumerThreads;
+      v[j] = i < total / 4 ? __ldg(x4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      m = absmax_acc(absmax_acc(absmax_acc(absmax_acc(m, v[j].x), v[j].y), v[j].z), v[j].w);
+    }
+    const float scale = sym_scale(consumer_max(m, red));
+    const float inv = __fdiv_rn(1.0f, scale);
+    if (ct < M) s_scale[ct] = scale;
+#pragma unroll
+    for (int j = 0; j < kRegVec; ++j) {
+      const size_t i = ct + static_cast<size_t>(j) * kConsumerThreads;
+      if (i < total / 4) {
+        char4 o;
+        o.x = sym_quant(v[j].x, inv);
+        o.y = sym_quant(v[j].y, inv);
+        o.z = sym_quant(v[j].z, inv);
+        o.w = sym_quant(v[j].w, inv);
+        reinterpret_cast<char4*>(s_act)[i] = o;
+      }
+    }
+  } else if (act.mode == ACT_F32_PER_TENSOR || act.mode == ACT_F32_PER_ROW) {
     const float* x = act.x;
     const bool vec = (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (K % 4) == 0;
     for (int r = 0; r < (act.mode == ACT_F32_PER_ROW ? M : 1); ++r) {
@@ -223,10 +252,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int cw = warp - 1;
   const int chunks = static_cast<int>(K / 16);
   const int iters = static_cast<int>((end - begin + kRowsPerStage - 1) / kRowsPerStage);
+  // The per-row weight scale is loaded one stage ahead so its global-load
+  // latency overlaps the stage wait and the dot product.
+  float sw_next = begin + cw < end ? __ldg(w_scales + begin + cw) : 0.0f;
   for (int it = 0; it < iters; ++it) {
     const int s = it % n_stages;
-    if (!mbar_wait(&full[s], (it / n_stages) & 1, status)) return;
     const size_t row = begin + static_cast<size_t>(it) * kRowsPerStage + cw;
+    const float sw = sw_next;
+    if (row + kRowsPerStage < end) sw_next = __ldg(w_scales + row + kRowsPerStage);
+    if (!mbar_wait(&full[s], (it / n_stages) & 1, status)) return;
     if (row < end) {
       const uint4* wrow = reinterpret_cast<const uint4*>(stage0 + s * L.stage_bytes + cw * K);
       int acc[M];
@@ -246,7 +280,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
 #pragma unroll
       for (int m = 0; m < M; ++m) acc[m] = warp_sum_i(acc[m]);
-      const float sw = __ldg(w_scales + row);
 #pragma unroll
       for (int m = 0; m < M; ++m) {
         if (lane == m) {

@@ -158,6 +158,32 @@ MRI_API int mri_host_matmul_q8_0_direct(mri_ctx* ctx, const float* x, size_t m, 
 MRI_API int mri_host_matmul_q4_0_dequant(mri_ctx* ctx, const float* x, size_t m, size_t k,
                                  const mri_q4_0_matrix* w, float* out);
 
+/* ── allocation-free entry point ───────────────────────────────────────────── */
+/* No counterpart in the reference.  For callers that cannot allocate device
+ * memory at call time (a host runtime that owns the device memory pool and
+ * forbids cudaMalloc/cudaFree, or code that must not touch an allocator while
+ * a framework manages the stream): matmul_int8_from_f32 with per-tensor
+ * quantization, whose scratch (quantized activations, absmax, scale) lives in
+ * a fixed file-scope device array instead of a context buffer.
+ *   - Takes raw device pointers and a cudaStream_t (NULL = legacy stream);
+ *     needs no context.  w_dev: [n,k] int8 row-major (16-byte aligned),
+ *     w_scales_dev: [n] f32, x_dev: [m,k] f32, out_dev: [m,n] f32.
+ *   - m*k must not exceed MRI_NOALLOC_MAX_ACT_BYTES, else
+ *     MRI_ERR_INVALID_ARGUMENT; k must be a positive multiple of 16.
+ *   - The first call on a device resolves the array's device address
+ *     (cudaGetSymbolAddress) and device properties; make that first call
+ *     before any stream capture.
+ *   - All calls share the one array: calls that overlap on the GPU (other
+ *     streams, other threads) race.  Serialize them on one stream.
+ *   - Every GPU that loads this library keeps the array allocated until the
+ *     process exits.
+ *   - Errors: mri_noalloc_last_error(). */
+#define MRI_NOALLOC_MAX_ACT_BYTES (4u << 20)
+MRI_API int mri_matmul_int8_from_f32_noalloc(const float* x_dev, size_t m, size_t k,
+                                             const int8_t* w_dev, const float* w_scales_dev,
+                                             size_t n, float* out_dev, void* cuda_stream);
+MRI_API const char* mri_noalloc_last_error(void);
+
 /* ── diagnostics ──────────────────────────────────────────────────────────── */
 /* Kernel path chosen for an INT8 product of this shape:
  * 0 = streaming GEMV (TMA bulk), 1 = generic GEMV, 2 = tensor-core GEMM. */

@@ -58,6 +58,8 @@ SIGNATURES = {
     "mri_host_matmul_q8_0_direct": (_I, [_P, _P, _SZ, _SZ, _P, _P]),
     "mri_host_matmul_q4_0_dequant": (_I, [_P, _P, _SZ, _SZ, _P, _P]),
     "mri_int8_path": (_I, [_P, _SZ, _SZ, _SZ]),
+    "mri_matmul_int8_from_f32_noalloc": (_I, [_P, _SZ, _SZ, _P, _P, _SZ, _P, _P]),
+    "mri_noalloc_last_error": (ctypes.c_char_p, []),
 }
 
 _lock = threading.Lock()

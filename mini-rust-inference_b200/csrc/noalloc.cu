@@ -1,0 +1,126 @@
+// noalloc.cu — an allocation-free variant of the prefill product
+// (per-tensor activation quantization into scratch, then the tcgen05 GEMM).
+//
+// Who needs it: callers that must not allocate device memory at call time —
+// code running inside a memory pool they do not own, an embedding runtime
+// that forbids cudaMalloc/cudaFree on its threads, or a stream that is being
+// fed by a framework whose allocator would otherwise be bypassed.  The
+// regular entry points keep their scratch in a per-context buffer that grows
+// with cudaMalloc; this one keeps it in a fixed, file-scope device array.
+//
+// The array holds the quantized activations (up to kNoAllocMaxActBytes) plus
+// a small header (absmax accumulator, activation scale, wait-status word).
+// Every GPU that loads this library holds the array until the process exits.
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <mutex>
+#include <string>
+
+#include "internal.h"
+#include "mri_gpu.h"
+
+namespace {
+
+constexpr size_t kHeaderBytes = 256;
+constexpr size_t kNoAllocMaxActBytes = MRI_NOALLOC_MAX_ACT_BYTES;
+
+// Layout: [0] absmax (f32), [4] activation scale (f32), [8] status (i32),
+// then the quantized activations at kHeaderBytes.
+__device__ __align__(256) uint8_t g_noalloc_scratch[kHeaderBytes + kNoAllocMaxActBytes];
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceSetup {
+  bool ready = false;
+  uint8_t* scratch = nullptr;  // device address of g_noalloc_scratch on this device
+  mri::DeviceInfo dev;
+};
+
+std::mutex g_setup_mu;
+DeviceSetup g_setup[kMaxDevices];
+thread_local std::string g_noalloc_error;
+
+int fail(int code, const char* msg) {
+  g_noalloc_error = msg;
+  return code;
+}
+
+// Once per device, with that device current: resolve the device address of
+// the file-scope array (in host code its name is only a stand-in) and read
+// the device properties the launchers need.  Allocation-free.
+int setup_device(int device, DeviceSetup** out) {
+  if (device < 0 || device >= kMaxDevices) return fail(MRI_ERR_CUDA, "device index out of range");
+  std::lock_guard<std::mutex> lock(g_setup_mu);
+  DeviceSetup& s = g_setup[device];
+  if (!s.ready) {
+    void* ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess) return fail(MRI_ERR_CUDA, cudaGetErrorString(e));
+    int sms = 0, major = 0, minor = 0;
+    if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device)) != cudaSuccess ||
+        (e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device)) != cudaSuccess ||
+        (e = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device)) != cudaSuccess)
+      return fail(MRI_ERR_CUDA, cudaGetErrorString(e));
+    if (major != 10) return fail(MRI_ERR_CUDA, "device is not sm_100 (this library is built for sm_100a)");
+    s.scratch = static_cast<uint8_t*>(ptr);
+    s.dev.device = device;
+    s.dev.sm_count = sms;
+    s.dev.cc_major = major;
+    s.dev.cc_minor = minor;
+    s.ready = true;
+  }
+  *out = &s;
+  return MRI_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* mri_noalloc_last_error(void) { return g_noalloc_error.c_str(); }
+
+int mri_matmul_int8_from_f32_noalloc(const float* x_dev, size_t m, size_t k, const int8_t* w_dev,
+                                     const float* w_scales_dev, size_t n, float* out_dev,
+                                     void* cuda_stream) {
+  g_noalloc_error.clear();
+  if (m * k > kNoAllocMaxActBytes) {
+    char buf[160];
+    snprintf(buf, sizeof(buf),
+             "matmul_int8_from_f32_noalloc: m*k=%zu exceeds the fixed scratch of %zu bytes", m * k,
+             kNoAllocMaxActBytes);
+    return fail(MRI_ERR_INVALID_ARGUMENT, buf);
+  }
+  if (m == 0 || n == 0) return MRI_OK;
+  if (!x_dev || !w_dev || !w_scales_dev || !out_dev)
+    return fail(MRI_ERR_INVALID_ARGUMENT, "null device pointer");
+  if (k < 16 || k % 16 != 0)
+    return fail(MRI_ERR_INVALID_SHAPE, "matmul_int8_from_f32_noalloc: k must be a positive multiple of 16");
+  if (reinterpret_cast<uintptr_t>(w_dev) & 15)
+    return fail(MRI_ERR_INVALID_ARGUMENT, "weights must be 16-byte aligned");
+  int device = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess) return fail(MRI_ERR_CUDA, cudaGetErrorString(e));
+  DeviceSetup* s = nullptr;
+  if (int rc = setup_device(device, &s)) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
+  float* amax = reinterpret_cast<float*>(s->scratch);
+  float* scale = amax + 1;
+  int* status = reinterpret_cast<int*>(s->scratch + 8);
+  int8_t* xq = reinterpret_cast<int8_t*>(s->scratch + kHeaderBytes);
+  // The array keeps the previous call's contents: the absmax accumulator and
+  // the status word must start at zero (launch_quantize clears the absmax).
+  if ((e = cudaMemsetAsync(status, 0, sizeof(int), st)) != cudaSuccess)
+    return fail(MRI_ERR_CUDA, cudaGetErrorString(e));
+  if ((e = mri::launch_quantize(s->dev, st, x_dev, m, k, /*per_row=*/0, xq, scale, amax, nullptr)) !=
+      cudaSuccess)
+    return fail(MRI_ERR_CUDA, cudaGetErrorString(e));
+  if (!mri::gemm_i8_tc_supported(s->dev, m, n, k))
+    return fail(MRI_ERR_CUDA, "tensor-core GEMM unavailable on this device/driver");
+  if ((e = mri::launch_gemm_i8_tc(s->dev, st, xq, scale, /*scale_per_row=*/0, w_dev, w_scales_dev, m,
+                                  n, k, out_dev, nullptr, status, nullptr)) != cudaSuccess)
+    return fail(MRI_ERR_CUDA, cudaGetErrorString(e));
+  return MRI_OK;
+}
+
+}  // extern "C"

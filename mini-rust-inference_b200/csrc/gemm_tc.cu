@@ -39,11 +39,10 @@ namespace {
 constexpr int BM = 128;
 constexpr int BK = 128;  // K bytes per stage = one 128-byte swizzle row
 constexpr int UMMA_K = 32;
-constexpr int kStages = 4;
 constexpr int kEpiWarps = 4;
 constexpr int kTcThreads = 32 * (2 + kEpiWarps);
 
-template <int BN>
+template <int BN, int kStages>
 struct TcLayout {
   static constexpr size_t a_bytes = BM * BK;
   static constexpr size_t b_bytes = BN * BK;
@@ -128,13 +127,13 @@ __device__ __forceinline__ void tmem_ld_32cols(uint32_t taddr, uint32_t (&v)[32]
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-template <int BN>
+template <int BN, int kStages>
 __global__ void __launch_bounds__(kTcThreads, 1)
     gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const float* __restrict__ act_scale, int scale_per_row,
                       const float* __restrict__ w_scales, float* __restrict__ out,
                       int32_t* __restrict__ acc_out, int M, int N, int K, int* status) {
-  using L = TcLayout<BN>;
+  using L = TcLayout<BN, kStages>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_addr(smem_raw);
   uint8_t* smem = smem_raw + ((1024 - (raw & 1023)) & 1023);
@@ -175,6 +174,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Programmatic dependent launch: let the next kernel start early, and read
+  // nothing a previous kernel may still be writing (activations, scales)
+  // before griddepcontrol.wait.  No-ops without the launch attribute.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 
   if (warp == 0) {
     if (lane == 0) {
@@ -338,6 +342,14 @@ cudaError_t set_smem_tc(KernelT k, size_t bytes, int device) {
   return e;
 }
 
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("MRI_PDL");
+    return e == nullptr || std::atoi(e) != 0;
+  }();
+  return on;
+}
+
 // Tile width: the one whose wave count times tile width is smallest (ties
 // go to the wider tile, which reads less shared memory per MAC).
 int pick_bn(const DeviceInfo& dev, size_t M, size_t N) {
@@ -353,20 +365,28 @@ int pick_bn(const DeviceInfo& dev, size_t M, size_t N) {
   return cost(128) < cost(256) ? 128 : 256;
 }
 
-template <int BN>
+template <int BN, int kStages>
 cudaError_t launch_bn(const DeviceInfo& dev, cudaStream_t st, const CUtensorMap& ta,
                       const CUtensorMap& tb, const float* act_scale, int per_row,
                       const float* w_scales, size_t M, size_t N, size_t K, float* out,
                       int32_t* acc_out, int* status) {
-  const size_t smem = TcLayout<BN>::total;
-  cudaError_t e = set_smem_tc(gemm_i8_tc_kernel<BN>, smem, dev.device);
+  const size_t smem = TcLayout<BN, kStages>::total;
+  cudaError_t e = set_smem_tc(gemm_i8_tc_kernel<BN, kStages>, smem, dev.device);
   if (e != cudaSuccess) return e;
   const size_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
-  const int grid = static_cast<int>(std::min<size_t>(tiles, dev.sm_count));
-  gemm_i8_tc_kernel<BN><<<grid, kTcThreads, smem, st>>>(
-      ta, tb, act_scale, per_row, w_scales, out, acc_out, static_cast<int>(M), static_cast<int>(N),
-      static_cast<int>(K), status);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(std::min<size_t>(tiles, dev.sm_count)));
+  cfg.blockDim = dim3(kTcThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, gemm_i8_tc_kernel<BN, kStages>, ta, tb, act_scale, per_row, w_scales,
+                            out, acc_out, static_cast<int>(M), static_cast<int>(N),
+                            static_cast<int>(K), status);
 }
 
 }  // namespace
@@ -387,10 +407,11 @@ cudaError_t launch_gemm_i8_tc(const DeviceInfo& dev, cudaStream_t st, const int8
   const int bn = pick_bn(dev, M, N);
   CUtensorMap ta, tb;
   if (!make_map(&ta, xq, M, K, BM) || !make_map(&tb, W, N, K, bn)) return cudaErrorInvalidValue;
-  cudaError_t e = bn == 128 ? launch_bn<128>(dev, st, ta, tb, act_scale_dev, scale_per_row, w_scales,
-                                             M, N, K, out, acc_out, status)
-                            : launch_bn<256>(dev, st, ta, tb, act_scale_dev, scale_per_row, w_scales,
-                                             M, N, K, out, acc_out, status);
+  // Four 48 KB stages (BN=256) or six 32 KB stages (BN=128): 192 KB either way.
+  cudaError_t e = bn == 128 ? launch_bn<128, 6>(dev, st, ta, tb, act_scale_dev, scale_per_row,
+                                                w_scales, M, N, K, out, acc_out, status)
+                            : launch_bn<256, 4>(dev, st, ta, tb, act_scale_dev, scale_per_row,
+                                                w_scales, M, N, K, out, acc_out, status);
   if (ls) ls->launches++;
   return e;
 }

@@ -19,6 +19,7 @@
 // `(f32)dot * s_a * d` and adds the terms in block order on one lane, as
 // q8_direct.rs:266-285 does.  Q4_0 reassociates its f32 sum (tolerance).
 #include <algorithm>
+#include <cstdlib>
 #include <map>
 #include <mutex>
 #include <utility>
@@ -37,6 +38,16 @@ constexpr int kMaxStages = 6;
 constexpr size_t kSmemBudget = 220 * 1024;  // of the 227 KB opt-in per CTA
 
 __host__ __device__ constexpr size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Programmatic dependent launch: the next kernel in the stream may start as
+// soon as every CTA of this one has passed pdl_launch_dependents(); it must
+// call pdl_wait() before touching anything this kernel writes.  Weights are
+// constant, so producers stream them before pdl_wait(); activations are read
+// and outputs written only after it.  Both are no-ops without the attribute.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 // Shared-memory layout of a stream kernel.
 struct StreamLayout {
@@ -110,6 +121,7 @@ __device__ __forceinline__ void init_barriers(uint64_t* full, uint64_t* empty, i
     fence_barrier_init();
   }
   __syncthreads();
+  pdl_launch_dependents();
 }
 
 // ── activation prologue (consumer threads only) ──────────────────────────────
@@ -244,6 +256,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                       L.stage_bytes, n_stages, status);
     return;
   }
+  pdl_wait();
   load_act_i8_rowmajor<M>(act, K, s_act, s_scale, red);
   float s_a[M];
 #pragma unroll
@@ -350,10 +363,12 @@ __device__ __forceinline__ void load_q8_block(const uint8_t* blk, uint32_t& dbit
 }
 
 // ── K4: Q8_0 streaming GEMV, bit-exact ───────────────────────────────────────
-// Activations live in shared memory as words transposed to [m][word 0..7][block]
-// so that lane b of a warp reads word w of block b without bank conflicts.
-// Each consumer warp keeps a term buffer T[m][nb+1]: lanes write the block
-// terms of their blocks, then lane m adds row m's terms in block order.
+// Activations are quantized per row into shared memory (row-major int8, so
+// block b of row m is the 32 bytes at m*K + 32*b).  Each consumer warp keeps
+// a term buffer T[m][ts]: lanes write the terms of their blocks, then lane m
+// adds row m's terms in block order (vectorised loads, a plain FADD chain).
+
+__host__ __device__ constexpr size_t q8_term_stride(size_t nb) { return align_up(nb, 4) + 4; }
 
 template <int M>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -363,13 +378,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ __align__(128) uint8_t smem[];
   const size_t nb = K / 32;
   const size_t row_bytes = nb * 34;
-  const StreamLayout L = make_layout(M * K, kConsumerWarps * M * (nb + 1) * sizeof(float),
+  const size_t ts = q8_term_stride(nb);
+  const StreamLayout L = make_layout(M * K, kConsumerWarps * M * ts * sizeof(float),
                                      kRowsPerStage * row_bytes, n_stages);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
   uint64_t* empty = full + n_stages;
   float* s_scale = reinterpret_cast<float*>(smem + L.scales);
   float* red = s_scale + 8;
-  uint32_t* s_actw = reinterpret_cast<uint32_t*>(smem + L.act);
+  int8_t* s_act = reinterpret_cast<int8_t*>(smem + L.act);
   float* s_terms = reinterpret_cast<float*>(smem + L.extra);
   uint8_t* stage0 = smem + L.stage;
 
@@ -387,33 +403,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                       status);
     return;
   }
-
-  // Prologue: per-row quantization (q8_direct.rs:264) into the transposed layout.
-  const int ct = threadIdx.x - 32;
-  for (int r = 0; r < M; ++r) {
-    const float* xr = x + r * K;
-    float m = 0.0f;
-    for (size_t i = ct; i < K; i += kConsumerThreads) m = absmax_acc(m, __ldg(xr + i));
-    const float scale = sym_scale(consumer_max(m, red));
-    const float inv = __fdiv_rn(1.0f, scale);
-    if (ct == 0) s_scale[r] = scale;
-    for (size_t wi = ct; wi < K / 4; wi += kConsumerThreads) {
-      const size_t k = wi * 4;
-      const uint32_t b0 = static_cast<uint8_t>(sym_quant(__ldg(xr + k), inv));
-      const uint32_t b1 = static_cast<uint8_t>(sym_quant(__ldg(xr + k + 1), inv));
-      const uint32_t b2 = static_cast<uint8_t>(sym_quant(__ldg(xr + k + 2), inv));
-      const uint32_t b3 = static_cast<uint8_t>(sym_quant(__ldg(xr + k + 3), inv));
-      const size_t blk = k / 32, word = (k % 32) / 4;
-      s_actw[(r * 8 + word) * nb + blk] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
-    }
-  }
-  named_bar_sync(1, kConsumerThreads);
+  pdl_wait();
+  // Prologue: per-row quantization (q8_direct.rs:264).
+  ActArgs act;
+  act.x = x;
+  act.mode = ACT_F32_PER_ROW;
+  load_act_i8_rowmajor<M>(act, K, s_act, s_scale, red);
   float s_a[M];
 #pragma unroll
   for (int m = 0; m < M; ++m) s_a[m] = s_scale[m];
 
   const int cw = warp - 1;
-  float* T = s_terms + static_cast<size_t>(cw) * M * (nb + 1);
+  float* T = s_terms + static_cast<size_t>(cw) * M * ts;
   const int iters = static_cast<int>((end - begin + kRowsPerStage - 1) / kRowsPerStage);
   for (int it = 0; it < iters; ++it) {
     const int s = it % n_stages;
@@ -427,17 +428,35 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float d = f16_bits_to_f32(dbits);
 #pragma unroll
         for (int m = 0; m < M; ++m) {
-          int dot = 0;
-#pragma unroll
-          for (int i = 0; i < 8; ++i) dot = dp4a(q[i], s_actw[(m * 8 + i) * nb + b], dot);
-          T[m * (nb + 1) + b] = __fmul_rn(__fmul_rn(__int2float_rn(dot), s_a[m]), d);
+          const uint4* a4 = reinterpret_cast<const uint4*>(s_act + m * K + b * 32);
+          const uint4 a0 = a4[0], a1 = a4[1];
+          int dot = dp4a(q[0], a0.x, 0);
+          dot = dp4a(q[1], a0.y, dot);
+          dot = dp4a(q[2], a0.z, dot);
+          dot = dp4a(q[3], a0.w, dot);
+          dot = dp4a(q[4], a1.x, dot);
+          dot = dp4a(q[5], a1.y, dot);
+          dot = dp4a(q[6], a1.z, dot);
+          dot = dp4a(q[7], a1.w, dot);
+          T[m * ts + b] = __fmul_rn(__fmul_rn(__int2float_rn(dot), s_a[m]), d);
         }
       }
       __syncwarp();
       if (lane < M) {
-        const float* t = T + lane * (nb + 1);
+        // acc += term in block order (q8_direct.rs:281), starting from 0.0.
+        const float* t = T + lane * ts;
+        const float4* t4 = reinterpret_cast<const float4*>(t);
         float acc = 0.0f;
-        for (size_t b = 0; b < nb; ++b) acc = __fadd_rn(acc, t[b]);
+        const size_t nb4 = nb / 4;
+#pragma unroll 8
+        for (size_t j = 0; j < nb4; ++j) {
+          const float4 v = t4[j];
+          acc = __fadd_rn(acc, v.x);
+          acc = __fadd_rn(acc, v.y);
+          acc = __fadd_rn(acc, v.z);
+          acc = __fadd_rn(acc, v.w);
+        }
+        for (size_t b = nb4 * 4; b < nb; ++b) acc = __fadd_rn(acc, t[b]);
         out[lane * N + row] = acc;
       }
     }
@@ -510,6 +529,13 @@ __device__ __forceinline__ void load_q4_block(const uint8_t* blk, uint32_t& dbit
   for (int i = 0; i < 4; ++i) q[i] = odd ? r[i + 1] : __funnelshift_r(r[i], r[i + 1], 16);
 }
 
+// Nibble j (0..3) of the 4 packed in `lo_w`/`hi_w` as an exact float q - 8:
+// the byte is placed in the mantissa of 2^23 and 2^23 + 8 subtracted.
+__device__ __forceinline__ float nib_minus8(uint32_t v, uint32_t byte_idx) {
+  return __int_as_float(static_cast<int>(__byte_perm(v, 0x4B000000u, 0x7540u | byte_idx))) -
+         8388616.0f;
+}
+
 template <int M>
 __global__ void __launch_bounds__(kThreads, 1)
     gemv_q4_0_tma_kernel(const uint8_t* __restrict__ W, size_t N, size_t K,
@@ -521,7 +547,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const StreamLayout L = make_layout(M * K * sizeof(float), 0, kRowsPerStage * row_bytes, n_stages);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
   uint64_t* empty = full + n_stages;
-  float* s_x = reinterpret_cast<float*>(smem + L.act);
+  float4* s_x4 = reinterpret_cast<float4*>(smem + L.act);
   uint8_t* stage0 = smem + L.stage;
 
   const size_t g = 8 / (nb % 8 == 0 ? 8 : (nb % 4 == 0 ? 4 : (nb % 2 == 0 ? 2 : 1)));
@@ -537,10 +563,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                       status);
     return;
   }
+  pdl_wait();
+  // Activations as float4 chunks transposed to [m][chunk 0..7][block], so
+  // lane b reads chunk c of block b conflict-free.
   const int ct = threadIdx.x - 32;
-  for (size_t i = ct; i < static_cast<size_t>(M) * K; i += kConsumerThreads) {
-    const size_t r = i / K, k = i % K;
-    s_x[(r * 32 + (k % 32)) * nb + k / 32] = __ldg(x + i);
+  for (size_t i = ct; i < static_cast<size_t>(M) * K / 4; i += kConsumerThreads) {
+    const size_t r = (i * 4) / K, k = (i * 4) % K;
+    float4 v;
+    v.x = __ldg(x + r * K + k);
+    v.y = __ldg(x + r * K + k + 1);
+    v.z = __ldg(x + r * K + k + 2);
+    v.w = __ldg(x + r * K + k + 3);
+    s_x4[(r * 8 + (k % 32) / 4) * nb + k / 32] = v;
   }
   named_bar_sync(1, kConsumerThreads);
 
@@ -559,18 +593,30 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t dbits, q[4];
         load_q4_block(rowp + b * 18, dbits, q);
         const float d = f16_bits_to_f32(dbits);
+        // Per block: sum_k x_k * (q_k - 8), then one multiply by d
+        // (dequant_block_into, q4_0.rs:59-68, reassociated).
+        float p0[M], p1[M];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const uint32_t byte = (q[j >> 2] >> (8 * (j & 3))) & 0xFFu;
-          // dequant_block_into (q4_0.rs:59-68): scale * (nibble - 8)
-          const float lo = __fmul_rn(d, static_cast<float>(static_cast<int>(byte & 15u) - 8));
-          const float hi = __fmul_rn(d, static_cast<float>(static_cast<int>(byte >> 4) - 8));
+        for (int m = 0; m < M; ++m) p0[m] = p1[m] = 0.0f;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const uint32_t w = q[c >> 1];
+          const uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
+          const uint32_t j = (c & 1) * 2;
+          const float e0 = nib_minus8(lo, j), e1 = nib_minus8(hi, j);
+          const float e2 = nib_minus8(lo, j + 1), e3 = nib_minus8(hi, j + 1);
 #pragma unroll
           for (int m = 0; m < M; ++m) {
-            acc[m] = __fmaf_rn(s_x[(m * 32 + 2 * j) * nb + b], lo, acc[m]);
-            acc[m] = __fmaf_rn(s_x[(m * 32 + 2 * j + 1) * nb + b], hi, acc[m]);
+            const float4 xv = s_x4[(m * 8 + c) * nb + b];
+            float& p = (c & 1) ? p1[m] : p0[m];
+            p = __fmaf_rn(xv.x, e0, p);
+            p = __fmaf_rn(xv.y, e1, p);
+            p = __fmaf_rn(xv.z, e2, p);
+            p = __fmaf_rn(xv.w, e3, p);
           }
         }
+#pragma unroll
+        for (int m = 0; m < M; ++m) acc[m] = __fmaf_rn(d, p0[m] + p1[m], acc[m]);
       }
 #pragma unroll
       for (int m = 0; m < M; ++m) acc[m] = warp_sum_f(acc[m]);
@@ -621,10 +667,33 @@ __global__ void __launch_bounds__(256) gemv_q4_0_generic_kernel(const uint8_t* _
 
 // ── host side: layouts, attributes, dispatch on M ────────────────────────────
 
+// Launch tuning, read once from the environment (defaults are the measured
+// best on B200; the variables exist for sweeps):
+//   MRI_GEMV_SMEM_KB   shared-memory budget per CTA for the stage ring
+//   MRI_GEMV_CTAS_PER_SM  persistent CTAs per SM
+//   MRI_PDL            1 = programmatic dependent launch between kernels
+struct GemvTuning {
+  size_t smem_budget = 220 * 1024;
+  int ctas_per_sm = 1;
+  bool pdl = true;
+};
+
+const GemvTuning& tuning() {
+  static GemvTuning t = [] {
+    GemvTuning v;
+    if (const char* e = std::getenv("MRI_GEMV_SMEM_KB")) v.smem_budget = std::strtoul(e, nullptr, 10) * 1024;
+    if (const char* e = std::getenv("MRI_GEMV_CTAS_PER_SM")) v.ctas_per_sm = std::max(1, std::atoi(e));
+    if (const char* e = std::getenv("MRI_PDL")) v.pdl = std::atoi(e) != 0;
+    v.smem_budget = std::min<size_t>(v.smem_budget, kSmemBudget);
+    return v;
+  }();
+  return t;
+}
+
 int pick_stages(size_t fixed_bytes, size_t stage_bytes) {
   for (int s = kMaxStages; s >= 2; --s) {
     const StreamLayout L = make_layout(0, 0, stage_bytes, s);
-    if (fixed_bytes + L.total + 256 <= kSmemBudget) return s;
+    if (fixed_bytes + L.total + 256 <= tuning().smem_budget) return s;
   }
   return 0;
 }
@@ -651,7 +720,25 @@ cudaError_t set_smem(KernelT k, size_t bytes, int device) {
 }
 
 int stream_grid(const DeviceInfo& dev, size_t units) {
-  return static_cast<int>(std::max<size_t>(1, std::min<size_t>(dev.sm_count, units)));
+  return static_cast<int>(
+      std::max<size_t>(1, std::min<size_t>(static_cast<size_t>(dev.sm_count) * tuning().ctas_per_sm, units)));
+}
+
+// Launch with the programmatic-stream-serialization attribute when enabled.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_stream_kernel(void (*k)(KArgs...), int grid, size_t smem, cudaStream_t st,
+                                 Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = tuning().pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, k, std::forward<Args>(args)...);
 }
 
 #define MRI_DISPATCH_M(M, ...)                           \
@@ -684,8 +771,9 @@ cudaError_t launch_gemv_i8_tma(const DeviceInfo& dev, cudaStream_t st, int M, co
   MRI_DISPATCH_M(M, {
     cudaError_t e = set_smem(gemv_i8_tma_kernel<kM>, smem, dev.device);
     if (e != cudaSuccess) return e;
-    gemv_i8_tma_kernel<kM><<<grid, kThreads, smem, st>>>(W, w_scales, N, K, act, out, acc_out,
-                                                          stages, status);
+    e = launch_stream_kernel(gemv_i8_tma_kernel<kM>, grid, smem, st, W, w_scales, N, K, act, out,
+                             acc_out, stages, status);
+    if (e != cudaSuccess) return e;
   });
   if (ls) ls->launches++;
   return cudaGetLastError();
@@ -705,7 +793,7 @@ cudaError_t launch_gemv_i8_generic(const DeviceInfo& dev, cudaStream_t st, int M
 bool gemv_q8_0_tma_supported(const DeviceInfo&, int M, size_t K) {
   if (M < 1 || M > 8 || K == 0 || K % 32 != 0) return false;
   const size_t nb = K / 32;
-  return pick_stages(fixed_bytes_of(M * K, kConsumerWarps * M * (nb + 1) * 4),
+  return pick_stages(fixed_bytes_of(M * K, kConsumerWarps * M * q8_term_stride(nb) * 4),
                      kRowsPerStage * nb * 34) >= 3;
 }
 
@@ -713,7 +801,7 @@ cudaError_t launch_gemv_q8_0_tma(const DeviceInfo& dev, cudaStream_t st, int M, 
                                  size_t N, size_t K, const float* x, float* out, int* status,
                                  LaunchStats* ls) {
   const size_t nb = K / 32;
-  const size_t extra = kConsumerWarps * M * (nb + 1) * 4;
+  const size_t extra = kConsumerWarps * M * q8_term_stride(nb) * 4;
   const int stages = pick_stages(fixed_bytes_of(M * K, extra), kRowsPerStage * nb * 34);
   if (stages < 2) return cudaErrorInvalidValue;
   const size_t smem = make_layout(M * K, extra, kRowsPerStage * nb * 34, stages).total;
@@ -721,7 +809,9 @@ cudaError_t launch_gemv_q8_0_tma(const DeviceInfo& dev, cudaStream_t st, int M, 
   MRI_DISPATCH_M(M, {
     cudaError_t e = set_smem(gemv_q8_0_tma_kernel<kM>, smem, dev.device);
     if (e != cudaSuccess) return e;
-    gemv_q8_0_tma_kernel<kM><<<grid, kThreads, smem, st>>>(W, N, K, x, out, stages, status);
+    e = launch_stream_kernel(gemv_q8_0_tma_kernel<kM>, grid, smem, st, W, N, K, x, out, stages,
+                             status);
+    if (e != cudaSuccess) return e;
   });
   if (ls) ls->launches++;
   return cudaGetLastError();
@@ -754,7 +844,9 @@ cudaError_t launch_gemv_q4_0_tma(const DeviceInfo& dev, cudaStream_t st, int M, 
   MRI_DISPATCH_M(M, {
     cudaError_t e = set_smem(gemv_q4_0_tma_kernel<kM>, smem, dev.device);
     if (e != cudaSuccess) return e;
-    gemv_q4_0_tma_kernel<kM><<<grid, kThreads, smem, st>>>(W, N, K, x, out, stages, status);
+    e = launch_stream_kernel(gemv_q4_0_tma_kernel<kM>, grid, smem, st, W, N, K, x, out, stages,
+                             status);
+    if (e != cudaSuccess) return e;
   });
   if (ls) ls->launches++;
   return cudaGetLastError();

@@ -105,6 +105,9 @@ int ensure_scratch(mri_ctx* ctx, size_t bytes) {
 
 size_t al(size_t v) { return (v + 255) / 256 * 256; }
 
+// Bytes of the quantizer's maxima area at the front of scratch.
+size_t amax_bytes(size_t m) { return al(std::max(m, mri::kQuantPartials) * sizeof(float)); }
+
 template <typename T>
 int upload_bytes(const T* host, size_t count, T** dev) {
   const size_t bytes = count * sizeof(T);
@@ -143,11 +146,11 @@ int run_int8(mri_ctx* ctx, ActArgs act, const mri_qmatrix* w, size_t m, float* o
   const float* sdev = act.scale_dev;
   int per_row = act.mode == mri::ACT_I8_DEV_ROW_SCALE || act.mode == mri::ACT_F32_PER_ROW;
   if (f32_in || act.mode == mri::ACT_I8_HOST_SCALE) {
-    const size_t need = al(m * sizeof(float)) * 2 + al(m * K);
+    const size_t need = amax_bytes(m) + al(m * sizeof(float)) + al(m * K);
     if (int rc = ensure_scratch(ctx, need)) return rc;
     float* amax = reinterpret_cast<float*>(ctx->scratch);
-    float* scales = reinterpret_cast<float*>(ctx->scratch + al(m * sizeof(float)));
-    int8_t* q = reinterpret_cast<int8_t*>(ctx->scratch + 2 * al(m * sizeof(float)));
+    float* scales = reinterpret_cast<float*>(ctx->scratch + amax_bytes(m));
+    int8_t* q = reinterpret_cast<int8_t*>(ctx->scratch + amax_bytes(m) + al(m * sizeof(float)));
     if (f32_in) {
       MRI_CUDA_TRY(mri::launch_quantize(ctx->dev, st, act.x, m, K, per_row, q, scales, amax,
                                         &ctx->ls));
@@ -196,11 +199,11 @@ int run_q8_0(mri_ctx* ctx, const float* x, size_t m, const mri_q8_0_matrix* w, f
     }
     return MRI_OK;
   }
-  const size_t need = al(m * sizeof(float)) * 2 + al(m * K);
+  const size_t need = amax_bytes(m) + al(m * sizeof(float)) + al(m * K);
   if (int rc = ensure_scratch(ctx, need)) return rc;
   float* amax = reinterpret_cast<float*>(ctx->scratch);
-  float* scales = reinterpret_cast<float*>(ctx->scratch + al(m * sizeof(float)));
-  int8_t* q = reinterpret_cast<int8_t*>(ctx->scratch + 2 * al(m * sizeof(float)));
+  float* scales = reinterpret_cast<float*>(ctx->scratch + amax_bytes(m));
+  int8_t* q = reinterpret_cast<int8_t*>(ctx->scratch + amax_bytes(m) + al(m * sizeof(float)));
   MRI_CUDA_TRY(mri::launch_quantize(ctx->dev, st, x, m, K, 1, q, scales, amax, &ctx->ls));
   for (size_t m0 = 0; m0 < m; m0 += 8) {
     const int mc = static_cast<int>(std::min<size_t>(8, m - m0));
@@ -264,7 +267,7 @@ struct HostStage {
 
 int host_stage(mri_ctx* ctx, size_t in_bytes, size_t out_bytes, size_t acc_bytes, size_t quant_m,
                size_t quant_k, HostStage* hs) {
-  const size_t quant = al(quant_m * sizeof(float)) * 2 + al(quant_m * quant_k);
+  const size_t quant = amax_bytes(quant_m) + al(quant_m * sizeof(float)) + al(quant_m * quant_k);
   const size_t need = quant + al(in_bytes) + al(out_bytes) + al(acc_bytes);
   if (int rc = ensure_scratch(ctx, need)) return rc;
   hs->in = ctx->scratch + quant;
@@ -484,7 +487,7 @@ int mri_quantize_symmetric(mri_ctx* ctx, const float* x_dev, size_t m, size_t k,
     return fail(MRI_ERR_INVALID_ARGUMENT, "granularity must be MRI_PER_TENSOR or MRI_PER_ROW");
   if ((m * k && (!x_dev || !q_dev)) || !scale_dev)
     return fail(MRI_ERR_INVALID_ARGUMENT, "null device pointer");
-  if (int rc = ensure_scratch(ctx, al(std::max<size_t>(m, 1) * sizeof(float)))) return rc;
+  if (int rc = ensure_scratch(ctx, amax_bytes(m))) return rc;
   MRI_CUDA_TRY(mri::launch_quantize(ctx->dev, ctx->stream, x_dev, m, k, granularity, q_dev,
                                     scale_dev, reinterpret_cast<float*>(ctx->scratch), &ctx->ls));
   return MRI_OK;

@@ -422,13 +422,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     const size_t row = begin + static_cast<size_t>(it) * kRowsPerStage + cw;
     if (row < end) {
       const uint8_t* rowp = stage0 + s * L.stage_bytes + cw * row_bytes;
-      for (size_t b = lane; b < nb; b += 32) {
+      const uint32_t nb32 = static_cast<uint32_t>(nb), K32 = static_cast<uint32_t>(K);
+      const uint32_t ts32 = static_cast<uint32_t>(ts);
+      for (uint32_t b = lane; b < nb32; b += 32) {
         uint32_t dbits, q[8];
-        load_q8_block(rowp + b * 34, dbits, q);
+        load_q8_block(rowp + b * 34u, dbits, q);
         const float d = f16_bits_to_f32(dbits);
 #pragma unroll
         for (int m = 0; m < M; ++m) {
-          const uint4* a4 = reinterpret_cast<const uint4*>(s_act + m * K + b * 32);
+          const uint4* a4 = reinterpret_cast<const uint4*>(s_act + m * K32 + b * 32u);
           const uint4 a0 = a4[0], a1 = a4[1];
           int dot = dp4a(q[0], a0.x, 0);
           dot = dp4a(q[1], a0.y, dot);
@@ -438,7 +440,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           dot = dp4a(q[5], a1.y, dot);
           dot = dp4a(q[6], a1.z, dot);
           dot = dp4a(q[7], a1.w, dot);
-          T[m * ts + b] = __fmul_rn(__fmul_rn(__int2float_rn(dot), s_a[m]), d);
+          T[m * ts32 + b] = __fmul_rn(__fmul_rn(__int2float_rn(dot), s_a[m]), d);
         }
       }
       __syncwarp();
@@ -589,9 +591,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       float acc[M];
 #pragma unroll
       for (int m = 0; m < M; ++m) acc[m] = 0.0f;
-      for (size_t b = lane; b < nb; b += 32) {
+      const uint32_t nb32 = static_cast<uint32_t>(nb);
+      for (uint32_t b = lane; b < nb32; b += 32) {
         uint32_t dbits, q[4];
-        load_q4_block(rowp + b * 18, dbits, q);
+        load_q4_block(rowp + b * 18u, dbits, q);
         const float d = f16_bits_to_f32(dbits);
         // Per block: sum_k x_k * (q_k - 8), then one multiply by d
         // (dequant_block_into, q4_0.rs:59-68, reassociated).
@@ -607,7 +610,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float e2 = nib_minus8(lo, j + 1), e3 = nib_minus8(hi, j + 1);
 #pragma unroll
           for (int m = 0; m < M; ++m) {
-            const float4 xv = s_x4[(m * 8 + c) * nb + b];
+            const float4 xv = s_x4[(m * 8 + c) * nb32 + b];
             float& p = (c & 1) ? p1[m] : p0[m];
             p = __fmaf_rn(xv.x, e0, p);
             p = __fmaf_rn(xv.y, e1, p);
@@ -673,8 +676,8 @@ __global__ void __launch_bounds__(256) gemv_q4_0_generic_kernel(const uint8_t* _
 //   MRI_GEMV_CTAS_PER_SM  persistent CTAs per SM
 //   MRI_PDL            1 = programmatic dependent launch between kernels
 struct GemvTuning {
-  size_t smem_budget = 220 * 1024;
-  int ctas_per_sm = 1;
+  size_t smem_budget = 0;  // 0 = automatic (see pick_config)
+  int ctas_per_sm = 0;     // 0 = automatic
   bool pdl = true;
 };
 
@@ -690,12 +693,42 @@ const GemvTuning& tuning() {
   return t;
 }
 
-int pick_stages(size_t fixed_bytes, size_t stage_bytes) {
+int stages_within(size_t fixed_bytes, size_t stage_bytes, size_t budget) {
   for (int s = kMaxStages; s >= 2; --s) {
     const StreamLayout L = make_layout(0, 0, stage_bytes, s);
-    if (fixed_bytes + L.total + 256 <= tuning().smem_budget) return s;
+    if (fixed_bytes + L.total + 256 <= budget) return s;
   }
   return 0;
+}
+
+// Stage count and CTAs per SM: two co-resident CTAs of <= 112 KB when at least
+// three stages fit (with programmatic dependent launch the next kernel's CTA
+// then starts streaming while this one drains), else one CTA of <= 220 KB.
+struct StreamConfig {
+  int stages = 0;
+  int ctas_per_sm = 1;
+};
+
+StreamConfig pick_config(size_t fixed_bytes, size_t stage_bytes) {
+  const GemvTuning& t = tuning();
+  StreamConfig c;
+  if (t.smem_budget) {
+    c.stages = stages_within(fixed_bytes, stage_bytes, t.smem_budget);
+    c.ctas_per_sm = t.ctas_per_sm ? t.ctas_per_sm : 1;
+    return c;
+  }
+  c.stages = std::min(4, stages_within(fixed_bytes, stage_bytes, 112 * 1024));
+  if (c.stages >= 3) {
+    c.ctas_per_sm = t.ctas_per_sm ? t.ctas_per_sm : 2;
+    return c;
+  }
+  c.stages = stages_within(fixed_bytes, stage_bytes, kSmemBudget);
+  c.ctas_per_sm = t.ctas_per_sm ? t.ctas_per_sm : 1;
+  return c;
+}
+
+int pick_stages(size_t fixed_bytes, size_t stage_bytes) {
+  return pick_config(fixed_bytes, stage_bytes).stages;
 }
 
 size_t fixed_bytes_of(size_t act_bytes, size_t extra_bytes) {
@@ -719,9 +752,9 @@ cudaError_t set_smem(KernelT k, size_t bytes, int device) {
   return e;
 }
 
-int stream_grid(const DeviceInfo& dev, size_t units) {
+int stream_grid(const DeviceInfo& dev, size_t units, int ctas_per_sm) {
   return static_cast<int>(
-      std::max<size_t>(1, std::min<size_t>(static_cast<size_t>(dev.sm_count) * tuning().ctas_per_sm, units)));
+      std::max<size_t>(1, std::min<size_t>(static_cast<size_t>(dev.sm_count) * ctas_per_sm, units)));
 }
 
 // Launch with the programmatic-stream-serialization attribute when enabled.
@@ -764,10 +797,11 @@ bool gemv_i8_tma_supported(const DeviceInfo&, int M, size_t K) {
 cudaError_t launch_gemv_i8_tma(const DeviceInfo& dev, cudaStream_t st, int M, const int8_t* W,
                                const float* w_scales, size_t N, size_t K, const ActArgs& act,
                                float* out, int32_t* acc_out, int* status, LaunchStats* ls) {
-  const int stages = pick_stages(fixed_bytes_of(M * K, 0), kRowsPerStage * K);
+  const StreamConfig cfg = pick_config(fixed_bytes_of(M * K, 0), kRowsPerStage * K);
+  const int stages = cfg.stages;
   if (stages < 2) return cudaErrorInvalidValue;
   const size_t smem = make_layout(M * K, 0, kRowsPerStage * K, stages).total;
-  const int grid = stream_grid(dev, N);
+  const int grid = stream_grid(dev, N, cfg.ctas_per_sm);
   MRI_DISPATCH_M(M, {
     cudaError_t e = set_smem(gemv_i8_tma_kernel<kM>, smem, dev.device);
     if (e != cudaSuccess) return e;
@@ -802,10 +836,11 @@ cudaError_t launch_gemv_q8_0_tma(const DeviceInfo& dev, cudaStream_t st, int M, 
                                  LaunchStats* ls) {
   const size_t nb = K / 32;
   const size_t extra = kConsumerWarps * M * q8_term_stride(nb) * 4;
-  const int stages = pick_stages(fixed_bytes_of(M * K, extra), kRowsPerStage * nb * 34);
+  const StreamConfig cfg = pick_config(fixed_bytes_of(M * K, extra), kRowsPerStage * nb * 34);
+  const int stages = cfg.stages;
   if (stages < 2) return cudaErrorInvalidValue;
   const size_t smem = make_layout(M * K, extra, kRowsPerStage * nb * 34, stages).total;
-  const int grid = stream_grid(dev, N);
+  const int grid = stream_grid(dev, N, cfg.ctas_per_sm);
   MRI_DISPATCH_M(M, {
     cudaError_t e = set_smem(gemv_q8_0_tma_kernel<kM>, smem, dev.device);
     if (e != cudaSuccess) return e;
@@ -837,10 +872,11 @@ cudaError_t launch_gemv_q4_0_tma(const DeviceInfo& dev, cudaStream_t st, int M, 
                                  size_t N, size_t K, const float* x, float* out, int* status,
                                  LaunchStats* ls) {
   const size_t stage_bytes = kRowsPerStage * (K / 32) * 18;
-  const int stages = pick_stages(fixed_bytes_of(M * K * 4, 0), stage_bytes);
+  const StreamConfig cfg = pick_config(fixed_bytes_of(M * K * 4, 0), stage_bytes);
+  const int stages = cfg.stages;
   if (stages < 2) return cudaErrorInvalidValue;
   const size_t smem = make_layout(M * K * 4, 0, stage_bytes, stages).total;
-  const int grid = stream_grid(dev, N);
+  const int grid = stream_grid(dev, N, cfg.ctas_per_sm);
   MRI_DISPATCH_M(M, {
     cudaError_t e = set_smem(gemv_q4_0_tma_kernel<kM>, smem, dev.device);
     if (e != cudaSuccess) return e;

@@ -40,7 +40,9 @@ struct DeviceInfo {
 };
 
 // ── quantizer (quant.cu) ─────────────────────────────────────────────────────
-// amax_scratch: M floats (PER_ROW) or 1 float (PER_TENSOR); it is cleared here.
+// amax_scratch: max(M, kQuantPartials) floats of device scratch (per-block
+// partial maxima for PER_TENSOR, per-row maxima for PER_ROW).
+constexpr size_t kQuantPartials = 1024;
 cudaError_t launch_quantize(const DeviceInfo& dev, cudaStream_t st, const float* x, size_t m,
                             size_t k, int per_row, int8_t* q, float* scale, float* amax_scratch,
                             LaunchStats* ls);

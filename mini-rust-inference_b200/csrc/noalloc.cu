@@ -22,11 +22,13 @@
 
 namespace {
 
-constexpr size_t kHeaderBytes = 256;
+// Header: maxima area (kQuantPartials floats), activation scale, status word.
+constexpr size_t kHeaderBytes = mri::kQuantPartials * sizeof(float) + 256;
 constexpr size_t kNoAllocMaxActBytes = MRI_NOALLOC_MAX_ACT_BYTES;
 
-// Layout: [0] absmax (f32), [4] activation scale (f32), [8] status (i32),
-// then the quantized activations at kHeaderBytes.
+// Layout: [0, 4096) per-block absmax partials (f32), then the activation
+// scale (f32) and the status word (i32), then the quantized activations at
+// kHeaderBytes.
 __device__ __align__(256) uint8_t g_noalloc_scratch[kHeaderBytes + kNoAllocMaxActBytes];
 
 constexpr int kMaxDevices = 64;
@@ -105,11 +107,11 @@ int mri_matmul_int8_from_f32_noalloc(const float* x_dev, size_t m, size_t k, con
   if (int rc = setup_device(device, &s)) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
   float* amax = reinterpret_cast<float*>(s->scratch);
-  float* scale = amax + 1;
-  int* status = reinterpret_cast<int*>(s->scratch + 8);
+  float* scale = reinterpret_cast<float*>(s->scratch + mri::kQuantPartials * sizeof(float));
+  int* status = reinterpret_cast<int*>(s->scratch + mri::kQuantPartials * sizeof(float) + 8);
   int8_t* xq = reinterpret_cast<int8_t*>(s->scratch + kHeaderBytes);
-  // The array keeps the previous call's contents: the absmax accumulator and
-  // the status word must start at zero (launch_quantize clears the absmax).
+  // The array keeps the previous call's contents: the status word must start
+  // at zero (the absmax partials are written before they are read).
   if ((e = cudaMemsetAsync(status, 0, sizeof(int), st)) != cudaSuccess)
     return fail(MRI_ERR_CUDA, cudaGetErrorString(e));
   if ((e = mri::launch_quantize(s->dev, st, x_dev, m, k, /*per_row=*/0, xq, scale, amax, nullptr)) !=

@@ -5,6 +5,8 @@
 // scale is bit-identical to the reference's sequential fold) and the
 // element-wise quantization.  HBM-bound: 4 B read + 1 B written per element in
 // the second pass, 4 B read in the first.
+#include <algorithm>
+
 #include "common.cuh"
 #include "internal.h"
 
@@ -13,10 +15,10 @@ namespace {
 
 constexpr int kQThreads = 256;
 
-// Per-tensor: every block folds its grid-stride share, then one atomicMax on
-// the float bit pattern (valid ordering for non-negative floats).
+// Per-tensor, pass 1: every block folds its grid-stride share and writes its
+// partial maximum to partial[blockIdx.x] (no atomics, no clearing needed).
 __global__ void __launch_bounds__(kQThreads) absmax_tensor_kernel(const float* __restrict__ x,
-                                                                  size_t n, float* amax) {
+                                                                  size_t n, float* partial) {
   float m = 0.0f;
   const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
   size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -38,8 +40,26 @@ __global__ void __launch_bounds__(kQThreads) absmax_tensor_kernel(const float* _
   if (threadIdx.x < 32) {
     float v = threadIdx.x < kQThreads / 32 ? red[threadIdx.x] : 0.0f;
     v = warp_max(v);
-    if (threadIdx.x == 0) atomicMax(reinterpret_cast<unsigned int*>(amax), __float_as_uint(v));
+    if (threadIdx.x == 0) partial[blockIdx.x] = v;
   }
+}
+
+// Max over the `count` partial maxima, computed by every block of pass 2.
+__device__ float reduce_partials(const float* __restrict__ partial, int count) {
+  __shared__ float red[kQThreads / 32];
+  __shared__ float result;
+  float m = 0.0f;
+  for (int i = threadIdx.x; i < count; i += kQThreads) m = fmaxf(m, partial[i]);
+  m = warp_max(m);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < kQThreads / 32 ? red[threadIdx.x] : 0.0f;
+    v = warp_max(v);
+    if (threadIdx.x == 0) result = v;
+  }
+  __syncthreads();
+  return result;
 }
 
 // Per-row: one block per row.
@@ -62,13 +82,14 @@ __global__ void __launch_bounds__(kQThreads) absmax_row_kernel(const float* __re
 __global__ void __launch_bounds__(kQThreads) quant_apply_kernel(const float* __restrict__ x,
                                                                 size_t m, size_t k, int per_row,
                                                                 const float* __restrict__ amax,
+                                                                int n_partials,
                                                                 int8_t* __restrict__ q,
                                                                 float* __restrict__ scale_out) {
   const size_t n = m * k;
   const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
   const size_t tid = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (!per_row) {
-    const float scale = sym_scale(amax[0]);
+    const float scale = sym_scale(reduce_partials(amax, n_partials));
     const float inv = __fdiv_rn(1.0f, scale);
     if (tid == 0) scale_out[0] = scale;
     if ((reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(q) & 3) == 0) {
@@ -110,24 +131,22 @@ cudaError_t launch_quantize(const DeviceInfo& dev, cudaStream_t st, const float*
     }
     if (m == 0) return cudaSuccess;
   }
-  const int blocks = static_cast<int>(
-      std::min<size_t>(static_cast<size_t>(dev.sm_count) * 8, (n + kQThreads * 4 - 1) / (kQThreads * 4) + 1));
+  // Pass 1 writes one partial maximum per block into amax_scratch, which must
+  // hold kQuantPartials floats (per tensor) or m floats (per row).
+  const int blocks = static_cast<int>(std::max<size_t>(
+      1, std::min<size_t>(std::min<size_t>(static_cast<size_t>(dev.sm_count) * 2, kQuantPartials),
+                          (n + kQThreads * 16 - 1) / (kQThreads * 16))));
   if (!per_row) {
-    cudaError_t e = cudaMemsetAsync(amax_scratch, 0, sizeof(float), st);
-    if (e != cudaSuccess) return e;
     absmax_tensor_kernel<<<blocks, kQThreads, 0, st>>>(x, n, amax_scratch);
   } else {
     absmax_row_kernel<<<static_cast<unsigned>(m), kQThreads, 0, st>>>(x, k, amax_scratch);
   }
   if (ls) ls->launches++;
-  if (n > 0) {
-    quant_apply_kernel<<<blocks, kQThreads, 0, st>>>(x, m, k, per_row, amax_scratch, q, scale);
-    if (ls) ls->launches++;
-  } else {
-    // m > 0 rows of k == 0: every row scale is 1.0.
-    quant_apply_kernel<<<1, kQThreads, 0, st>>>(x, m, k, per_row, amax_scratch, q, scale);
-    if (ls) ls->launches++;
-  }
+  const int apply_blocks = static_cast<int>(std::max<size_t>(
+      1, std::min<size_t>(static_cast<size_t>(dev.sm_count) * 8, (n + kQThreads * 4 - 1) / (kQThreads * 4))));
+  quant_apply_kernel<<<apply_blocks, kQThreads, 0, st>>>(x, m, k, per_row, amax_scratch, blocks, q,
+                                                         scale);
+  if (ls) ls->launches++;
   return cudaGetLastError();
 }
 

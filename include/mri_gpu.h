@@ -158,6 +158,46 @@ MRI_API int mri_host_matmul_q8_0_direct(mri_ctx* ctx, const float* x, size_t m, 
 MRI_API int mri_host_matmul_q4_0_dequant(mri_ctx* ctx, const float* x, size_t m, size_t k,
                                  const mri_q4_0_matrix* w, float* out);
 
+/* ── LlamaModelInt8 (model/llama/forward_int8.rs:416-547) ────────────────── */
+/* The device-resident model around the projections: flat f32 KV cache
+ * [layer][max_seq][kv_dim], per-tensor INT8 projections (Q/K/V and gate/up
+ * stored concatenated; bit-identical per element to separate calls), f32
+ * RMSNorm / RoPE / causal GQA attention / SwiGLU / residual glue. */
+typedef struct mri_llama mri_llama;
+typedef struct mri_llama_config {
+  uint32_t n_layers, dim, n_heads, n_kv_heads /* 0 = n_heads */, ffn_dim, vocab, max_seq;
+  float rope_base, rms_eps;
+} mri_llama_config;
+MRI_API int mri_llama_create(mri_ctx* ctx, const mri_llama_config* cfg, mri_llama** out);
+MRI_API int mri_llama_free(mri_llama* m);
+MRI_API const char* mri_llama_last_error(void);
+/* Weights from host memory (LlamaModelInt8::new, forward_int8.rs:427-440). */
+MRI_API int mri_llama_set_rope(mri_llama* m, const float* cos_t, const float* sin_t); /* [max_seq, hd/2] */
+MRI_API int mri_llama_set_embedding(mri_llama* m, const float* token_embd);        /* [vocab, dim] */
+MRI_API int mri_llama_set_norms(mri_llama* m, const float* attn_norm /*[L,dim]*/,
+                                const float* ffn_norm /*[L,dim]*/, const float* output_norm);
+MRI_API int mri_llama_set_layer(mri_llama* m, uint32_t layer, const int8_t* wq, const float* sq,
+                                const int8_t* wk, const float* sk, const int8_t* wv, const float* sv,
+                                const int8_t* wo, const float* so, const int8_t* wgate,
+                                const float* sgate, const int8_t* wup, const float* sup,
+                                const int8_t* wdown, const float* sdown);
+MRI_API int mri_llama_set_output(mri_llama* m, const int8_t* w, const float* s); /* [vocab, dim] */
+/* Synthetic weights generated on the device (benchmarking only). */
+MRI_API int mri_llama_init_random(mri_llama* m, uint64_t seed);
+/* LlamaModelInt8::forward (forward_int8.rs:516-529): logits [n, vocab]; also
+ * fills the KV cache for positions [0, n). */
+MRI_API int mri_llama_forward(mri_llama* m, const uint32_t* tokens, size_t n, float* logits);
+/* LlamaModelInt8::forward_decode (forward_int8.rs:538-546): logits [vocab]. */
+MRI_API int mri_llama_forward_decode(mri_llama* m, uint32_t token, size_t pos, float* logits);
+/* Prefill the prompt into the cache (an addition: the reference has no
+ * cached prefill at model level), then n_decode greedy steps replayed from a
+ * captured CUDA graph.  out_tokens receives n_decode + 1 tokens (the first
+ * from the prompt's last logits).  Device-timed prefill / decode in ms. */
+MRI_API int mri_llama_generate_greedy(mri_llama* m, const uint32_t* prompt, size_t n_prompt,
+                                      size_t n_decode, uint32_t* out_tokens, float* prefill_ms,
+                                      float* decode_ms);
+MRI_API int mri_llama_launches_per_decode_step(const mri_llama* m, size_t* count);
+
 /* ── allocation-free entry point ───────────────────────────────────────────── */
 /* No counterpart in the reference.  For callers that cannot allocate device
  * memory at call time (a host runtime that owns the device memory pool and

@@ -35,6 +35,7 @@ __all__ = [
     "quantize_symmetric", "quantize_symmetric_rows", "quantize_per_channel",
     "matmul_int8", "matmul_int8_avx2", "matmul_int8_neon", "matmul_int8_parallel",
     "matmul_int8_from_f32", "matmul_q8_0_direct", "matmul_q4_0_dequant", "formats",
+    "LlamaConfig", "LlamaModelInt8",
 ]
 
 
@@ -396,3 +397,118 @@ def matmul_q4_0_dequant(input, weight_q4, n_out, k, ctx=None):  # noqa: A002
 
 def library_path():
     return _lib.library_path()
+
+
+# ── LlamaModelInt8 (model/llama/forward_int8.rs:416-547) ─────────────────────
+
+class LlamaConfig(ctypes.Structure):
+    """Mirror of LlamaConfig (model/llama/config.rs:31-52), the fields the INT8
+    forward pass uses; n_kv_heads = 0 means n_heads."""
+    _fields_ = [("n_layers", ctypes.c_uint32), ("dim", ctypes.c_uint32), ("n_heads", ctypes.c_uint32),
+                ("n_kv_heads", ctypes.c_uint32), ("ffn_dim", ctypes.c_uint32), ("vocab", ctypes.c_uint32),
+                ("max_seq", ctypes.c_uint32), ("rope_base", ctypes.c_float), ("rms_eps", ctypes.c_float)]
+
+    def __init__(self, n_layers, dim, n_heads, ffn_dim, vocab, max_seq, n_kv_heads=0,
+                 rope_base=10000.0, rms_eps=1e-5):
+        super().__init__(n_layers, dim, n_heads, n_kv_heads, ffn_dim, vocab, max_seq, rope_base, rms_eps)
+
+    @property
+    def head_dim(self):
+        return self.dim // self.n_heads
+
+    @property
+    def kv_heads(self):
+        return self.n_kv_heads or self.n_heads
+
+
+def _check_model(rc, lib):
+    if rc != _lib.OK:
+        raise _ERRORS.get(rc, RuntimeError)(lib.mri_llama_last_error().decode(errors="replace"))
+
+
+class LlamaModelInt8:
+    """Device-resident LlamaModelInt8.  Build with `from_weights` (host arrays,
+    as LlamaModelInt8::new takes pre-quantized blocks) or `random` (synthetic
+    weights generated on the GPU, for benchmarks)."""
+
+    def __init__(self, cfg, ctx=None):
+        self.ctx = ctx or default_context()
+        self.cfg = cfg
+        self._lib = self.ctx._lib
+        h = ctypes.c_void_p()
+        _check_model(self._lib.mri_llama_create(self.ctx.handle, ctypes.byref(cfg), ctypes.byref(h)), self._lib)
+        self.handle = h
+
+    def __del__(self):
+        try:
+            if self.handle:
+                self._lib.mri_llama_free(self.handle)
+        except Exception:  # noqa: BLE001
+            pass
+
+    def set_rope(self, cos_t=None, sin_t=None):
+        if cos_t is None:
+            cos_t, sin_t = formats.rope_table(self.cfg.max_seq, self.cfg.head_dim, self.cfg.rope_base)
+        c, s = np.ascontiguousarray(cos_t, np.float32), np.ascontiguousarray(sin_t, np.float32)
+        _check_model(self._lib.mri_llama_set_rope(self.handle, _vp(c), _vp(s)), self._lib)
+
+    @classmethod
+    def from_weights(cls, cfg, w, ctx=None, rope=None):
+        """w: dict with token_embd [vocab*dim] f32, attn_norm/ffn_norm [L*dim],
+        output_norm [dim], output (data, scales), and layers: list of dicts with
+        wq, wk, wv, wo, wgate, wup, wdown each (int8 data, f32 scales)."""
+        m = cls(cfg, ctx)
+        lib = m._lib
+        f32 = lambda a: np.ascontiguousarray(a, np.float32)  # noqa: E731
+        i8 = lambda a: np.ascontiguousarray(a, np.int8)  # noqa: E731
+        keep = []
+        _check_model(lib.mri_llama_set_embedding(m.handle, _vp(f32(w["token_embd"]))), lib)
+        an, fn, on = f32(w["attn_norm"]), f32(w["ffn_norm"]), f32(w["output_norm"])
+        _check_model(lib.mri_llama_set_norms(m.handle, _vp(an), _vp(fn), _vp(on)), lib)
+        for li, layer in enumerate(w["layers"]):
+            args = []
+            for name in ("wq", "wk", "wv", "wo", "wgate", "wup", "wdown"):
+                d, s = i8(layer[name][0]), f32(layer[name][1])
+                keep += [d, s]
+                args += [_vp(d), _vp(s)]
+            _check_model(lib.mri_llama_set_layer(m.handle, li, *args), lib)
+        od, os_ = i8(w["output"][0]), f32(w["output"][1])
+        _check_model(lib.mri_llama_set_output(m.handle, _vp(od), _vp(os_)), lib)
+        m.set_rope(*(rope or (None, None)))
+        return m
+
+    @classmethod
+    def random(cls, cfg, seed=0, ctx=None):
+        m = cls(cfg, ctx)
+        _check_model(m._lib.mri_llama_init_random(m.handle, int(seed)), m._lib)
+        m.set_rope()
+        return m
+
+    def forward(self, tokens):
+        """forward_int8.rs:516-529: logits [len(tokens), vocab]."""
+        t = np.ascontiguousarray(tokens, np.uint32)
+        out = np.empty((t.size, self.cfg.vocab), np.float32)
+        _check_model(self._lib.mri_llama_forward(self.handle, _vp(t), t.size, _vp(out)), self._lib)
+        return out
+
+    def forward_decode(self, token, pos):
+        """forward_int8.rs:538-546: logits [vocab] for `token` at `pos` (the
+        cache must hold positions [0, pos))."""
+        out = np.empty(self.cfg.vocab, np.float32)
+        _check_model(self._lib.mri_llama_forward_decode(self.handle, int(token), int(pos), _vp(out)), self._lib)
+        return out
+
+    def generate_greedy(self, prompt, n_decode):
+        """Prefill + n_decode greedy steps; returns (tokens [n_decode+1],
+        prefill_ms, decode_ms), device-timed."""
+        p = np.ascontiguousarray(prompt, np.uint32)
+        toks = np.empty(n_decode + 1, np.uint32)
+        pm, dm = ctypes.c_float(), ctypes.c_float()
+        _check_model(self._lib.mri_llama_generate_greedy(self.handle, _vp(p), p.size, n_decode, _vp(toks),
+                                                         ctypes.byref(pm), ctypes.byref(dm)), self._lib)
+        return toks, pm.value, dm.value
+
+    def kernels_per_decode_step(self):
+        n = ctypes.c_size_t()
+        _check_model(self._lib.mri_llama_launches_per_decode_step(self.handle, ctypes.byref(n)), self._lib)
+        return n.value

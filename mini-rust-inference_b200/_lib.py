@@ -58,6 +58,19 @@ SIGNATURES = {
     "mri_host_matmul_q8_0_direct": (_I, [_P, _P, _SZ, _SZ, _P, _P]),
     "mri_host_matmul_q4_0_dequant": (_I, [_P, _P, _SZ, _SZ, _P, _P]),
     "mri_int8_path": (_I, [_P, _SZ, _SZ, _SZ]),
+    "mri_llama_create": (_I, [_P, _P, _PP]),
+    "mri_llama_free": (_I, [_P]),
+    "mri_llama_last_error": (ctypes.c_char_p, []),
+    "mri_llama_set_rope": (_I, [_P, _P, _P]),
+    "mri_llama_set_embedding": (_I, [_P, _P]),
+    "mri_llama_set_norms": (_I, [_P, _P, _P, _P]),
+    "mri_llama_set_layer": (_I, [_P, ctypes.c_uint32] + [_P] * 14),
+    "mri_llama_set_output": (_I, [_P, _P, _P]),
+    "mri_llama_init_random": (_I, [_P, ctypes.c_uint64]),
+    "mri_llama_forward": (_I, [_P, _P, _SZ, _P]),
+    "mri_llama_forward_decode": (_I, [_P, ctypes.c_uint32, _SZ, _P]),
+    "mri_llama_generate_greedy": (_I, [_P, _P, _SZ, _SZ, _P, _P, _P]),
+    "mri_llama_launches_per_decode_step": (_I, [_P, ctypes.POINTER(_SZ)]),
     "mri_matmul_int8_from_f32_noalloc": (_I, [_P, _SZ, _SZ, _P, _P, _SZ, _P, _P]),
     "mri_noalloc_last_error": (ctypes.c_char_p, []),
 }

@@ -15,37 +15,6 @@
 
 using mri::ActArgs;
 
-struct mri_ctx {
-  int device = 0;
-  cudaStream_t stream = nullptr;
-  bool own_stream = false;
-  mri::DeviceInfo dev;
-  int* d_status = nullptr;   // device view of the status word
-  int* h_status = nullptr;   // host view (mapped pinned memory)
-  uint8_t* scratch = nullptr;
-  size_t scratch_bytes = 0;
-  mri::LaunchStats ls;
-};
-
-struct mri_qmatrix {
-  int device;
-  int8_t* data;
-  float* scales;
-  size_t n_out, k_in;
-};
-
-struct mri_q8_0_matrix {
-  int device;
-  uint8_t* data;
-  size_t n_out, k_in;
-};
-
-struct mri_q4_0_matrix {
-  int device;
-  uint8_t* data;
-  size_t n_out, k;
-};
-
 namespace {
 
 thread_local std::string g_last_error;
@@ -135,7 +104,8 @@ int run_int8(mri_ctx* ctx, ActArgs act, const mri_qmatrix* w, size_t m, float* o
   cudaStream_t st = ctx->stream;
   const bool f32_in = act.mode == mri::ACT_F32_PER_TENSOR || act.mode == mri::ACT_F32_PER_ROW;
 
-  if (m <= 8 && mri::gemv_i8_tma_supported(ctx->dev, static_cast<int>(m), K)) {
+  const bool w_aligned = (reinterpret_cast<uintptr_t>(w->data) & 15) == 0;
+  if (m <= 8 && w_aligned && mri::gemv_i8_tma_supported(ctx->dev, static_cast<int>(m), K)) {
     MRI_CUDA_TRY(mri::launch_gemv_i8_tma(ctx->dev, st, static_cast<int>(m), w->data, w->scales, N,
                                          K, act, out, acc, ctx->d_status, &ctx->ls));
     return MRI_OK;
@@ -163,7 +133,8 @@ int run_int8(mri_ctx* ctx, ActArgs act, const mri_qmatrix* w, size_t m, float* o
     sdev = scales;
   }
 
-  if (mri::gemm_i8_tc_supported(ctx->dev, m, N, K) && (reinterpret_cast<uintptr_t>(xq) & 15) == 0) {
+  if (w_aligned && mri::gemm_i8_tc_supported(ctx->dev, m, N, K) &&
+      (reinterpret_cast<uintptr_t>(xq) & 15) == 0) {
     MRI_CUDA_TRY(mri::launch_gemm_i8_tc(ctx->dev, st, xq, sdev, per_row, w->data, w->scales, m, N,
                                         K, out, acc, ctx->d_status, &ctx->ls));
     return MRI_OK;
@@ -176,7 +147,7 @@ int run_int8(mri_ctx* ctx, ActArgs act, const mri_qmatrix* w, size_t m, float* o
     a.scale_dev = per_row ? sdev + m0 : sdev;
     float* o = out + m0 * N;
     int32_t* ac = acc ? acc + m0 * N : nullptr;
-    if (mri::gemv_i8_tma_supported(ctx->dev, mc, K)) {
+    if (w_aligned && mri::gemv_i8_tma_supported(ctx->dev, mc, K)) {
       MRI_CUDA_TRY(mri::launch_gemv_i8_tma(ctx->dev, st, mc, w->data, w->scales, N, K, a, o, ac,
                                            ctx->d_status, &ctx->ls));
     } else {
@@ -383,7 +354,7 @@ int mri_qmatrix_upload_rows(mri_ctx* ctx, const int8_t* data, const float* scale
   const size_t rows = row_end - row_begin;
   if ((rows * k_in > 0 && !data) || (rows > 0 && !scales))
     return fail(MRI_ERR_INVALID_ARGUMENT, "null weight pointer");
-  mri_qmatrix* w = new mri_qmatrix{ctx->device, nullptr, nullptr, rows, k_in};
+  mri_qmatrix* w = new mri_qmatrix{ctx->device, nullptr, nullptr, rows, k_in, true};
   int rc = upload_bytes(data ? data + row_begin * k_in : data, rows * k_in, &w->data);
   if (rc == MRI_OK) rc = upload_bytes(scales ? scales + row_begin : scales, rows, &w->scales);
   if (rc != MRI_OK) {
@@ -403,8 +374,10 @@ int mri_qmatrix_upload(mri_ctx* ctx, const int8_t* data, const float* scales, si
 int mri_qmatrix_free(mri_qmatrix* w) {
   if (!w) return MRI_OK;
   use_device(w->device);
-  cudaFree(w->data);
-  cudaFree(w->scales);
+  if (w->owns) {
+    cudaFree(w->data);
+    cudaFree(w->scales);
+  }
   delete w;
   return MRI_OK;
 }

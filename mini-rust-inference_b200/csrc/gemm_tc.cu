@@ -252,7 +252,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       float* orow = out + static_cast<size_t>(row) * N;
       int32_t* arow = acc_out ? acc_out + static_cast<size_t>(row) * N : nullptr;
       const bool vec = (N % 4) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0 &&
-                       (reinterpret_cast<uintptr_t>(acc_out) & 15) == 0;
+                       (reinterpret_cast<uintptr_t>(acc_out) & 15) == 0 &&
+                       (reinterpret_cast<uintptr_t>(w_scales) & 15) == 0;
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t v[32];

@@ -86,3 +86,36 @@ cudaError_t launch_gemm_i8_tc(const DeviceInfo& dev, cudaStream_t st, const int8
                               int32_t* acc_out, int* status, LaunchStats* ls);
 
 }  // namespace mri
+
+// ── handle definitions shared by abi.cu and llama.cu ────────────────────────
+struct mri_ctx {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  bool own_stream = false;
+  mri::DeviceInfo dev;
+  int* d_status = nullptr;   // device view of the status word
+  int* h_status = nullptr;   // host view (mapped pinned memory)
+  uint8_t* scratch = nullptr;
+  size_t scratch_bytes = 0;
+  mri::LaunchStats ls;
+};
+
+struct mri_qmatrix {
+  int device;
+  int8_t* data;
+  float* scales;
+  size_t n_out, k_in;
+  bool owns = true;  // false when the storage belongs to a larger allocation
+};
+
+struct mri_q8_0_matrix {
+  int device;
+  uint8_t* data;
+  size_t n_out, k_in;
+};
+
+struct mri_q4_0_matrix {
+  int device;
+  uint8_t* data;
+  size_t n_out, k;
+};

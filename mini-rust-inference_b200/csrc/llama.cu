@@ -1,0 +1,836 @@
+// llama.cu — device-resident LlamaModelInt8 (model/llama/forward_int8.rs:
+// 148-547) around the quantized projections: the caller of the hot path for
+// the full-model config (32 layers, 512-token prefill, greedy decode).
+//
+// Everything stays on the GPU: embeddings, norms, RoPE tables, the flat f32
+// KV cache ([layer][max_seq][kv_dim], cache/kv_cache.rs:44-175), activations.
+// Each projection is the library's INT8 product with the reference's
+// per-tensor activation quantization (proj_int8, forward_int8.rs:72-96):
+// small token counts take the fused streaming GEMV, prefill the tcgen05 GEMM.
+// Q, K and V (and gate and up) weights are stored as one concatenated
+// QuantizedMatrix; since each projection quantizes the same input with the
+// same per-tensor scale, every output element is bit-identical to separate
+// calls.  The glue (RMSNorm, RoPE, attention, SwiGLU, residual adds, greedy
+// argmax) is plain CUDA; it is f32 and tolerance-checked, not bit-exact (its
+// exp/sum order differs from the reference's).
+//
+// A decode step reads the token and position from device memory, so one
+// captured CUDA graph replays every step of greedy generation.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "internal.h"
+#include "mri_gpu.h"
+
+namespace {
+
+constexpr int kAttnChunk = 64;   // keys per split in decode attention
+constexpr int kPrefillQ = 16;    // queries per block in prefill attention
+constexpr int kPrefillKT = 64;   // keys per shared-memory tile in prefill attention
+constexpr int kMaxHeadDim = 128;
+
+// ── glue kernels ─────────────────────────────────────────────────────────────
+
+// forward_int8.rs:125-140 (row copy); token ids are validated on the host for
+// host-supplied tokens and are < vocab by construction for argmax outputs.
+__global__ void embed_kernel(const uint32_t* __restrict__ tokens, const float* __restrict__ embd,
+                             int d, float* __restrict__ x) {
+  const uint32_t tok = tokens[blockIdx.x];
+  const float* src = embd + static_cast<size_t>(tok) * d;
+  float* dst = x + static_cast<size_t>(blockIdx.x) * d;
+  for (int i = threadIdx.x; i < d; i += blockDim.x) dst[i] = src[i];
+}
+
+// ops/norm/rmsnorm.rs:51-117: out = w * (x * (1 / sqrt(mean(x^2) + eps))).
+__global__ void __launch_bounds__(256) rmsnorm_kernel(const float* __restrict__ x,
+                                                      const float* __restrict__ w, int d, float eps,
+                                                      float* __restrict__ out) {
+  const float* xr = x + static_cast<size_t>(blockIdx.x) * d;
+  float* orow = out + static_cast<size_t>(blockIdx.x) * d;
+  float ss = 0.0f;
+  for (int i = threadIdx.x; i < d; i += blockDim.x) ss = __fmaf_rn(xr[i], xr[i], ss);
+  ss = mri::warp_sum_f(ss);
+  __shared__ float red[8];
+  __shared__ float inv;
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.0f;
+    for (int i = 0; i < static_cast<int>(blockDim.x >> 5); ++i) t += red[i];
+    const float mean_sq = __fdiv_rn(t, static_cast<float>(d));
+    inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean_sq, eps)));
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < d; i += blockDim.x) orow[i] = __fmul_rn(w[i], __fmul_rn(xr[i], inv));
+}
+
+// ops/rope.rs:121-190 on q and k of the fused qkv rows, then the cache write
+// of attention/cached.rs:90-93 / :161-163 (k rotated, v as is).  Row i sits at
+// absolute position base + i, where base is *pos_dev if given, else pos0.
+__global__ void rope_kv_kernel(float* __restrict__ qkv, int ld, int n_heads, int n_kv, int hd,
+                               const float* __restrict__ cos_t, const float* __restrict__ sin_t,
+                               int pos0, const int* __restrict__ pos_dev, float* __restrict__ kc,
+                               float* __restrict__ vc) {
+  const int i = blockIdx.x;
+  const int pos = (pos_dev ? *pos_dev : pos0) + i;
+  const int half = hd / 2;
+  float* row = qkv + static_cast<size_t>(i) * ld;
+  const int kvd = n_kv * hd;
+  const int qd = n_heads * hd;
+  for (int p = threadIdx.x; p < (n_heads + n_kv) * half; p += blockDim.x) {
+    const int h = p / half, j = p % half;
+    float* base = h < n_heads ? row + h * hd : row + qd + (h - n_heads) * hd;
+    const float c = cos_t[pos * half + j], sn = sin_t[pos * half + j];
+    const float x0 = base[2 * j], x1 = base[2 * j + 1];
+    base[2 * j] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
+    base[2 * j + 1] = __fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, sn));
+  }
+  __syncthreads();
+  float* krow = kc + static_cast<size_t>(pos) * kvd;
+  float* vrow = vc + static_cast<size_t>(pos) * kvd;
+  for (int t = threadIdx.x; t < kvd; t += blockDim.x) {
+    krow[t] = row[qd + t];
+    vrow[t] = row[qd + kvd + t];
+  }
+}
+
+// Decode attention, split over keys (attention/cached.rs:141-190 with
+// gqa.rs:217-237): block (h, s) handles keys [s*64, min(s*64+64, pos+1)) and
+// writes its running max, exp-sum and weighted V sum.
+__global__ void __launch_bounds__(128) attn_decode_partial(const float* __restrict__ q, int n_heads,
+                                                           int n_kv, int hd,
+                                                           const float* __restrict__ kc,
+                                                           const float* __restrict__ vc,
+                                                           const int* __restrict__ pos_dev, float scale,
+                                                           float* __restrict__ part, int max_splits) {
+  const int h = blockIdx.x, s = blockIdx.y;
+  const int pos = *pos_dev;
+  const int j0 = s * kAttnChunk;
+  float* pout = part + (static_cast<size_t>(h) * max_splits + s) * (kMaxHeadDim + 2);
+  if (j0 > pos) {
+    if (threadIdx.x == 0) {
+      pout[0] = -INFINITY;
+      pout[1] = 0.0f;
+    }
+    return;
+  }
+  const int j1 = min(j0 + kAttnChunk, pos + 1);
+  const int kv_h = h / (n_heads / n_kv);
+  const int kvd = n_kv * hd;
+  __shared__ float sq[kMaxHeadDim];
+  __shared__ float sp[kAttnChunk];
+  __shared__ float red[4];
+  for (int t = threadIdx.x; t < hd; t += blockDim.x) sq[t] = q[h * hd + t];
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int j = j0 + warp; j < j1; j += 4) {
+    const float* krow = kc + static_cast<size_t>(j) * kvd + kv_h * hd;
+    float dot = 0.0f;
+    for (int t = lane; t < hd; t += 32) dot = __fmaf_rn(sq[t], krow[t], dot);
+    dot = mri::warp_sum_f(dot);
+    if (lane == 0) sp[j - j0] = __fmul_rn(dot, scale);
+  }
+  __syncthreads();
+  float mx = -INFINITY;
+  for (int j = threadIdx.x; j < j1 - j0; j += blockDim.x) mx = fmaxf(mx, sp[j]);
+  mx = mri::warp_max(mx);
+  if (lane == 0) red[warp] = mx;
+  __syncthreads();
+  mx = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+  __syncthreads();
+  float l = 0.0f;
+  for (int j = threadIdx.x; j < j1 - j0; j += blockDim.x) {
+    const float p = expf(sp[j] - mx);
+    sp[j] = p;
+    l += p;
+  }
+  l = mri::warp_sum_f(l);
+  if (lane == 0) red[warp] = l;
+  __syncthreads();
+  l = red[0] + red[1] + red[2] + red[3];
+  for (int t = threadIdx.x; t < hd; t += blockDim.x) {
+    float o = 0.0f;
+    for (int j = j0; j < j1; ++j) o = __fmaf_rn(sp[j - j0], vc[static_cast<size_t>(j) * kvd + kv_h * hd + t], o);
+    pout[2 + t] = o;
+  }
+  if (threadIdx.x == 0) {
+    pout[0] = mx;
+    pout[1] = l;
+  }
+}
+
+__global__ void __launch_bounds__(128) attn_decode_combine(const float* __restrict__ part, int hd,
+                                                           int max_splits, float* __restrict__ out) {
+  const int h = blockIdx.x;
+  const float* p = part + static_cast<size_t>(h) * max_splits * (kMaxHeadDim + 2);
+  float mx = -INFINITY;
+  for (int s = 0; s < max_splits; ++s) mx = fmaxf(mx, p[s * (kMaxHeadDim + 2)]);
+  float l = 0.0f;
+  for (int s = 0; s < max_splits; ++s) {
+    const float ms = p[s * (kMaxHeadDim + 2)];
+    if (ms != -INFINITY) l += p[s * (kMaxHeadDim + 2) + 1] * expf(ms - mx);
+  }
+  const float inv = __fdiv_rn(1.0f, l);
+  for (int t = threadIdx.x; t < hd; t += blockDim.x) {
+    float o = 0.0f;
+    for (int s = 0; s < max_splits; ++s) {
+      const float ms = p[s * (kMaxHeadDim + 2)];
+      if (ms != -INFINITY) o += p[s * (kMaxHeadDim + 2) + 2 + t] * expf(ms - mx);
+    }
+    out[h * hd + t] = o * inv;
+  }
+}
+
+// Prefill attention (gqa.rs:217-237 with mask.rs:77-115): block (h, qb)
+// handles queries [qb*16, qb*16+16) at absolute positions start + i against
+// cached keys [0, start + i], online softmax over 64-key tiles in shared memory.
+__global__ void __launch_bounds__(256) attn_prefill_kernel(const float* __restrict__ qkv, int ld,
+                                                           int n_heads, int n_kv, int hd, int M,
+                                                           int start, const float* __restrict__ kc,
+                                                           const float* __restrict__ vc, float scale,
+                                                           float* __restrict__ out, int out_ld) {
+  extern __shared__ float sm[];
+  float* sk = sm;                                   // [64][hd+1]
+  float* sv = sk + kPrefillKT * (kMaxHeadDim + 1);  // [64][hd]
+  float* sq = sv + kPrefillKT * kMaxHeadDim;        // [16][hd]
+  const int h = blockIdx.x, q0 = blockIdx.y * kPrefillQ;
+  const int kv_h = h / (n_heads / n_kv);
+  const int kvd = n_kv * hd;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int t = threadIdx.x; t < kPrefillQ * hd; t += blockDim.x) {
+    const int qi = t / hd, d = t % hd;
+    sq[t] = q0 + qi < M ? qkv[static_cast<size_t>(q0 + qi) * ld + h * hd + d] : 0.0f;
+  }
+  // Each warp owns two queries; each lane keeps hd/32 output dims per query.
+  const int qa = q0 + warp * 2, qb = qa + 1;
+  float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.0f, l_b = 0.0f;
+  float o_a[kMaxHeadDim / 32], o_b[kMaxHeadDim / 32];
+#pragma unroll
+  for (int i = 0; i < kMaxHeadDim / 32; ++i) o_a[i] = o_b[i] = 0.0f;
+  const int last_key = start + min(q0 + kPrefillQ, M) - 1;
+  for (int kt = 0; kt <= last_key; kt += kPrefillKT) {
+    __syncthreads();
+    const int nk = min(kPrefillKT, last_key + 1 - kt);
+    for (int t = threadIdx.x; t < nk * hd; t += blockDim.x) {
+      const int j = t / hd, d = t % hd;
+      sk[j * (kMaxHeadDim + 1) + d] = kc[static_cast<size_t>(kt + j) * kvd + kv_h * hd + d];
+      sv[j * kMaxHeadDim + d] = vc[static_cast<size_t>(kt + j) * kvd + kv_h * hd + d];
+    }
+    __syncthreads();
+    // Lane handles keys kt+lane and kt+lane+32 for both queries.
+    float s[2][2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const int j = lane + 32 * r;
+      float da = 0.0f, db = 0.0f;
+      if (j < nk) {
+        for (int d = 0; d < hd; ++d) {
+          const float kv = sk[j * (kMaxHeadDim + 1) + d];
+          da = __fmaf_rn(sq[(warp * 2) * hd + d], kv, da);
+          db = __fmaf_rn(sq[(warp * 2 + 1) * hd + d], kv, db);
+        }
+      }
+      const int key = kt + j;
+      s[0][r] = (j < nk && qa < M && key <= start + qa) ? __fmul_rn(da, scale) : -INFINITY;
+      s[1][r] = (j < nk && qb < M && key <= start + qb) ? __fmul_rn(db, scale) : -INFINITY;
+    }
+#pragma unroll
+    for (int qq = 0; qq < 2; ++qq) {
+      float& m = qq ? m_b : m_a;
+      float& l = qq ? l_b : l_a;
+      float* o = qq ? o_b : o_a;
+      float tmax = mri::warp_max(fmaxf(s[qq][0], s[qq][1]));
+      const float mnew = fmaxf(m, tmax);
+      if (mnew == -INFINITY) continue;  // nothing visible yet
+      const float corr = expf(m - mnew);
+      const float p0 = expf(s[qq][0] - mnew), p1 = expf(s[qq][1] - mnew);
+      l = l * corr + mri::warp_sum_f(p0 + p1);
+#pragma unroll
+      for (int i = 0; i < kMaxHeadDim / 32; ++i) o[i] *= corr;
+      for (int j = 0; j < nk; ++j) {
+        const float pj = __shfl_sync(0xffffffffu, j < 32 ? p0 : p1, j & 31);
+#pragma unroll
+        for (int i = 0; i < kMaxHeadDim / 32; ++i) {
+          const int d = lane + 32 * i;
+          if (d < hd) o[i] = __fmaf_rn(pj, sv[j * kMaxHeadDim + d], o[i]);
+        }
+      }
+      m = mnew;
+    }
+  }
+#pragma unroll
+  for (int qq = 0; qq < 2; ++qq) {
+    const int qi = qq ? qb : qa;
+    if (qi >= M) continue;
+    const float inv = __fdiv_rn(1.0f, qq ? l_b : l_a);
+    const float* o = qq ? o_b : o_a;
+#pragma unroll
+    for (int i = 0; i < kMaxHeadDim / 32; ++i) {
+      const int d = lane + 32 * i;
+      if (d < hd) out[static_cast<size_t>(qi) * out_ld + h * hd + d] = o[i] * inv;
+    }
+  }
+}
+
+// ops/activation/swiglu.rs:39-61: h = silu(gate) * up, silu(g) = g / (1 + exp(-g)).
+__global__ void swiglu_kernel(const float* __restrict__ gu, int ffn, int M, float* __restrict__ hout) {
+  const size_t n = static_cast<size_t>(M) * ffn;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const size_t r = i / ffn, c = i % ffn;
+    const float g = gu[r * 2 * ffn + c], u = gu[r * 2 * ffn + ffn + c];
+    hout[i] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+  }
+}
+
+// forward_int8.rs:100-121: x = x + y.
+__global__ void add_kernel(float* __restrict__ x, const float* __restrict__ y, size_t n) {
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x)
+    x[i] = __fadd_rn(x[i], y[i]);
+}
+
+// Greedy sampling: argmax (first index on ties) -> next token; position += 1.
+__global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ logits, int V,
+                                                      uint32_t* __restrict__ token,
+                                                      int* __restrict__ pos,
+                                                      uint32_t* __restrict__ gen) {
+  float best = -INFINITY;
+  int idx = 0x7fffffff;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    const float v = logits[i];
+    if (v > best || (v == best && i < idx)) {
+      best = v;
+      idx = i;
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+    if (ob > best || (ob == best && oi < idx)) {
+      best = ob;
+      idx = oi;
+    }
+  }
+  __shared__ float sb[32];
+  __shared__ int si[32];
+  if ((threadIdx.x & 31) == 0) {
+    sb[threadIdx.x >> 5] = best;
+    si[threadIdx.x >> 5] = idx;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w)
+      if (sb[w] > best || (sb[w] == best && si[w] < idx)) {
+        best = sb[w];
+        idx = si[w];
+      }
+    const uint32_t t = static_cast<uint32_t>(idx == 0x7fffffff ? 0 : idx);
+    *token = t;
+    gen[*pos + 1] = t;  // the token generated for position pos + 1
+    *pos += 1;
+  }
+}
+
+// Synthetic weights for benchmarking: int8 uniform in [-127, 127] and scales
+// uniform in [lo, hi] from a counter-based hash (splitmix64).
+__device__ __forceinline__ uint64_t mix64(uint64_t z) {
+  z += 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+__global__ void fill_i8_kernel(int8_t* __restrict__ w, size_t n, uint64_t seed) {
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x)
+    w[i] = static_cast<int8_t>(static_cast<int>(mix64(seed ^ (i * 0xD1B54A32D192ED03ull)) % 255u) - 127);
+}
+
+__global__ void fill_f32_kernel(float* __restrict__ w, size_t n, uint64_t seed, float lo, float hi) {
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const float u = static_cast<float>(mix64(seed ^ (i * 0xA24BAED4963EE407ull)) >> 40) * (1.0f / 16777216.0f);
+    w[i] = lo + (hi - lo) * u;
+  }
+}
+
+thread_local std::string g_model_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[400];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_model_error = buf;
+  return code;
+}
+
+#define LL_TRY(expr)                                                              \
+  do {                                                                            \
+    cudaError_t _e = (expr);                                                      \
+    if (_e != cudaSuccess) return fail(MRI_ERR_CUDA, "%s: %s", #expr, cudaGetErrorString(_e)); \
+  } while (0)
+
+#define LL_RC(expr)                                         \
+  do {                                                      \
+    int _rc = (expr);                                       \
+    if (_rc != MRI_OK) return fail(_rc, "%s", mri_last_error()); \
+  } while (0)
+
+int grid_for(size_t n, int threads, int sms) {
+  return static_cast<int>(std::max<size_t>(1, std::min<size_t>((n + threads - 1) / threads, sms * 16)));
+}
+
+}  // namespace
+
+struct mri_llama {
+  mri_ctx* ctx = nullptr;
+  mri_llama_config cfg{};
+  int hd = 0, qd = 0, kvd = 0, qkv_w = 0;
+  size_t max_tokens = 0;
+  // weights
+  float* embd = nullptr;
+  float* attn_norm = nullptr;
+  float* ffn_norm = nullptr;
+  float* out_norm = nullptr;
+  int8_t* w_blob = nullptr;  // all int8 projection weights
+  float* s_blob = nullptr;   // all per-channel scales
+  std::vector<mri_qmatrix> wqkv, wo, wgu, wdown;
+  mri_qmatrix wout{};
+  float* rope_cos = nullptr;
+  float* rope_sin = nullptr;
+  // cache and activations
+  float *kc = nullptr, *vc = nullptr;
+  float *x = nullptr, *xn = nullptr, *qkv = nullptr, *attn = nullptr, *tmp = nullptr;
+  float *gu = nullptr, *h = nullptr, *logits = nullptr, *part = nullptr;
+  uint32_t* d_tokens = nullptr;
+  uint32_t* d_gen = nullptr;  // [max_seq + 1] tokens produced by greedy argmax
+  int* d_pos = nullptr;
+  int max_splits = 0;
+  cudaGraphExec_t decode_exec = nullptr;
+  size_t graph_kernels = 0;
+  std::vector<void*> allocs;
+};
+
+namespace {
+
+template <typename T>
+int dalloc(mri_llama* m, T** p, size_t count) {
+  void* v = nullptr;
+  LL_TRY(cudaMalloc(&v, std::max<size_t>(count * sizeof(T), 256)));
+  m->allocs.push_back(v);
+  *p = static_cast<T*>(v);
+  return MRI_OK;
+}
+
+// Layout of the weight blobs: per layer [wqkv | wo | wgu | wdown], then the
+// LM head.  Offsets in elements.
+struct BlobLayout {
+  size_t per_layer_w, per_layer_s, total_w, total_s;
+  size_t qkv_w, o_w, gu_w, down_w;
+};
+
+BlobLayout blob_layout(const mri_llama* m) {
+  const auto& c = m->cfg;
+  BlobLayout b{};
+  b.qkv_w = static_cast<size_t>(m->qkv_w) * c.dim;
+  b.o_w = static_cast<size_t>(c.dim) * m->qd;
+  b.gu_w = static_cast<size_t>(2) * c.ffn_dim * c.dim;
+  b.down_w = static_cast<size_t>(c.dim) * c.ffn_dim;
+  b.per_layer_w = b.qkv_w + b.o_w + b.gu_w + b.down_w;
+  b.per_layer_s = static_cast<size_t>(m->qkv_w) + c.dim + 2 * c.ffn_dim + c.dim;
+  // Every matrix is padded to 256 bytes (weights) / 64 floats (scales).
+  auto pw = [](size_t v) { return (v + 255) / 256 * 256; };
+  auto ps = [](size_t v) { return (v + 63) / 64 * 64; };
+  b.per_layer_w = pw(b.qkv_w) + pw(b.o_w) + pw(b.gu_w) + pw(b.down_w);
+  b.per_layer_s = ps(m->qkv_w) + ps(c.dim) + ps(2 * static_cast<size_t>(c.ffn_dim)) + ps(c.dim);
+  b.total_w = b.per_layer_w * c.n_layers + pw(static_cast<size_t>(c.vocab) * c.dim);
+  b.total_s = b.per_layer_s * c.n_layers + ps(c.vocab);
+  return b;
+}
+
+// One INT8 projection with per-tensor quantization of x [m, k].
+int proj(mri_llama* m, const float* x, size_t rows, const mri_qmatrix& w, float* out) {
+  LL_RC(mri_matmul_int8_from_f32(m->ctx, x, rows, w.k_in, &w, out));
+  return MRI_OK;
+}
+
+// Runs the blocks and the final norm for `rows` tokens already embedded in
+// m->x, at absolute positions [pos0, pos0+rows) (or *d_pos when decode_dev).
+int run_blocks(mri_llama* m, size_t rows, int pos0, bool decode_dev) {
+  const auto& c = m->cfg;
+  cudaStream_t st = m->ctx->stream;
+  const int sms = m->ctx->dev.sm_count;
+  const float scale = 1.0f / std::sqrt(static_cast<float>(m->hd));
+  const size_t layer_kv = static_cast<size_t>(c.max_seq) * m->kvd;
+  for (uint32_t l = 0; l < c.n_layers; ++l) {
+    float* kc = m->kc + l * layer_kv;
+    float* vc = m->vc + l * layer_kv;
+    rmsnorm_kernel<<<static_cast<unsigned>(rows), 256, 0, st>>>(m->x, m->attn_norm + l * c.dim, c.dim,
+                                                                c.rms_eps, m->xn);
+    if (int rc = proj(m, m->xn, rows, m->wqkv[l], m->qkv)) return rc;
+    rope_kv_kernel<<<static_cast<unsigned>(rows), 128, 0, st>>>(m->qkv, m->qkv_w, c.n_heads,
+                                                                c.n_kv_heads, m->hd, m->rope_cos,
+                                                                m->rope_sin, pos0,
+                                                                decode_dev ? m->d_pos : nullptr, kc, vc);
+    if (decode_dev) {
+      attn_decode_partial<<<dim3(c.n_heads, m->max_splits), 128, 0, st>>>(
+          m->qkv, c.n_heads, c.n_kv_heads, m->hd, kc, vc, m->d_pos, scale, m->part, m->max_splits);
+      attn_decode_combine<<<c.n_heads, 128, 0, st>>>(m->part, m->hd, m->max_splits, m->attn);
+    } else {
+      const size_t smem = (kPrefillKT * (kMaxHeadDim + 1) + kPrefillKT * kMaxHeadDim +
+                           kPrefillQ * kMaxHeadDim) * sizeof(float);
+      static bool attr_set[64] = {false};
+      const int dv = m->ctx->device;
+      if (dv >= 0 && dv < 64 && !attr_set[dv]) {
+        LL_TRY(cudaFuncSetAttribute(attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(smem)));
+        attr_set[dv] = true;
+      }
+      attn_prefill_kernel<<<dim3(c.n_heads, static_cast<unsigned>((rows + kPrefillQ - 1) / kPrefillQ)),
+                            256, smem, st>>>(m->qkv, m->qkv_w, c.n_heads, c.n_kv_heads, m->hd,
+                                             static_cast<int>(rows), pos0, kc, vc, scale, m->attn,
+                                             m->qd);
+    }
+    if (int rc = proj(m, m->attn, rows, m->wo[l], m->tmp)) return rc;
+    add_kernel<<<grid_for(rows * c.dim, 256, sms), 256, 0, st>>>(m->x, m->tmp, rows * c.dim);
+    rmsnorm_kernel<<<static_cast<unsigned>(rows), 256, 0, st>>>(m->x, m->ffn_norm + l * c.dim, c.dim,
+                                                                c.rms_eps, m->xn);
+    if (int rc = proj(m, m->xn, rows, m->wgu[l], m->gu)) return rc;
+    swiglu_kernel<<<grid_for(rows * c.ffn_dim, 256, sms), 256, 0, st>>>(m->gu, c.ffn_dim,
+                                                                        static_cast<int>(rows), m->h);
+    if (int rc = proj(m, m->h, rows, m->wdown[l], m->tmp)) return rc;
+    add_kernel<<<grid_for(rows * c.dim, 256, sms), 256, 0, st>>>(m->x, m->tmp, rows * c.dim);
+  }
+  rmsnorm_kernel<<<static_cast<unsigned>(rows), 256, 0, st>>>(m->x, m->out_norm, c.dim, c.rms_eps,
+                                                              m->xn);
+  LL_TRY(cudaGetLastError());
+  return MRI_OK;
+}
+
+// Logits for rows [first, first+count) of m->xn into m->logits.
+int lm_head(mri_llama* m, size_t first, size_t count) {
+  return proj(m, m->xn + first * m->cfg.dim, count, m->wout, m->logits);
+}
+
+int check_tokens(const mri_llama* m, const uint32_t* tokens, size_t n) {
+  if (n == 0) return fail(MRI_ERR_INVALID_SHAPE, "forward: token list must not be empty");
+  if (n > m->max_tokens)
+    return fail(MRI_ERR_INVALID_SHAPE, "forward: %zu tokens exceed max_seq=%u", n, m->cfg.max_seq);
+  for (size_t i = 0; i < n; ++i)
+    if (tokens[i] >= m->cfg.vocab)
+      return fail(MRI_ERR_INVALID_SHAPE, "token id %u >= vocab_size %u", tokens[i], m->cfg.vocab);
+  return MRI_OK;
+}
+
+// Prefill `n` host tokens at positions [0, n) (writes the cache).
+int prefill(mri_llama* m, const uint32_t* tokens, size_t n) {
+  cudaStream_t st = m->ctx->stream;
+  LL_TRY(cudaMemcpyAsync(m->d_tokens, tokens, n * sizeof(uint32_t), cudaMemcpyHostToDevice, st));
+  embed_kernel<<<static_cast<unsigned>(n), 256, 0, st>>>(m->d_tokens, m->embd, m->cfg.dim, m->x);
+  return run_blocks(m, n, 0, false);
+}
+
+// One decode step entirely on the device: token from d_tokens[0], position
+// from *d_pos; ends with argmax -> d_tokens[0] and *d_pos += 1.
+int decode_step(mri_llama* m) {
+  cudaStream_t st = m->ctx->stream;
+  embed_kernel<<<1, 256, 0, st>>>(m->d_tokens, m->embd, m->cfg.dim, m->x);
+  if (int rc = run_blocks(m, 1, 0, true)) return rc;
+  if (int rc = lm_head(m, 0, 1)) return rc;
+  argmax_kernel<<<1, 1024, 0, st>>>(m->logits, m->cfg.vocab, m->d_tokens, m->d_pos, m->d_gen);
+  LL_TRY(cudaGetLastError());
+  return MRI_OK;
+}
+
+int ensure_decode_graph(mri_llama* m) {
+  if (m->decode_exec) return MRI_OK;
+  cudaStream_t st = m->ctx->stream;
+  // One eager step first: sizes every lazily-grown buffer and sets kernel
+  // attributes, so the captured launches make no allocation.  It runs on a
+  // scratch position, which the caller's next state overwrites.
+  const int scratch_pos = static_cast<int>(m->cfg.max_seq) - 1;
+  LL_TRY(cudaMemcpyAsync(m->d_pos, &scratch_pos, sizeof(int), cudaMemcpyHostToDevice, st));
+  LL_TRY(cudaMemsetAsync(m->d_tokens, 0, sizeof(uint32_t), st));
+  if (int rc = decode_step(m)) return rc;
+  LL_TRY(cudaStreamSynchronize(st));
+  cudaGraph_t g = nullptr;
+  LL_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+  const int rc = decode_step(m);
+  cudaError_t e = cudaStreamEndCapture(st, &g);
+  if (rc != MRI_OK) {
+    if (g) cudaGraphDestroy(g);
+    return rc;
+  }
+  LL_TRY(e);
+  cudaGraphGetNodes(g, nullptr, &m->graph_kernels);
+  e = cudaGraphInstantiate(&m->decode_exec, g, 0);
+  cudaGraphDestroy(g);
+  LL_TRY(e);
+  return MRI_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* mri_llama_last_error(void) { return g_model_error.c_str(); }
+
+int mri_llama_create(mri_ctx* ctx, const mri_llama_config* cfg, mri_llama** out) {
+  g_model_error.clear();
+  if (!ctx || !cfg || !out) return fail(MRI_ERR_INVALID_ARGUMENT, "null argument");
+  const auto& c = *cfg;
+  if (c.n_layers == 0 || c.dim == 0 || c.n_heads == 0 || c.ffn_dim == 0 || c.vocab == 0 ||
+      c.max_seq == 0)
+    return fail(MRI_ERR_INVALID_SHAPE, "config fields must be non-zero");
+  const uint32_t n_kv = c.n_kv_heads ? c.n_kv_heads : c.n_heads;
+  if (c.dim % c.n_heads || c.n_heads % n_kv)
+    return fail(MRI_ERR_INVALID_SHAPE, "dim %% n_heads and n_heads %% n_kv_heads must be 0");
+  const int hd = static_cast<int>(c.dim / c.n_heads);
+  if (hd % 2 || hd > kMaxHeadDim)
+    return fail(MRI_ERR_INVALID_SHAPE, "head_dim=%d must be even and <= %d", hd, kMaxHeadDim);
+  cudaSetDevice(ctx->device);
+  mri_llama* m = new mri_llama();
+  m->ctx = ctx;
+  m->cfg = c;
+  m->cfg.n_kv_heads = n_kv;
+  m->hd = hd;
+  m->qd = static_cast<int>(c.n_heads) * hd;
+  m->kvd = static_cast<int>(n_kv) * hd;
+  m->qkv_w = m->qd + 2 * m->kvd;
+  m->max_tokens = c.max_seq;
+  m->max_splits = static_cast<int>((c.max_seq + kAttnChunk - 1) / kAttnChunk);
+  const size_t T = m->max_tokens;
+  const BlobLayout b = blob_layout(m);
+  int rc = MRI_OK;
+  rc = rc ? rc : dalloc(m, &m->embd, static_cast<size_t>(c.vocab) * c.dim);
+  rc = rc ? rc : dalloc(m, &m->attn_norm, static_cast<size_t>(c.n_layers) * c.dim);
+  rc = rc ? rc : dalloc(m, &m->ffn_norm, static_cast<size_t>(c.n_layers) * c.dim);
+  rc = rc ? rc : dalloc(m, &m->out_norm, c.dim);
+  rc = rc ? rc : dalloc(m, &m->w_blob, b.total_w + 256);
+  rc = rc ? rc : dalloc(m, &m->s_blob, b.total_s + 64);
+  rc = rc ? rc : dalloc(m, &m->rope_cos, static_cast<size_t>(c.max_seq) * (hd / 2));
+  rc = rc ? rc : dalloc(m, &m->rope_sin, static_cast<size_t>(c.max_seq) * (hd / 2));
+  rc = rc ? rc : dalloc(m, &m->kc, static_cast<size_t>(c.n_layers) * c.max_seq * m->kvd);
+  rc = rc ? rc : dalloc(m, &m->vc, static_cast<size_t>(c.n_layers) * c.max_seq * m->kvd);
+  rc = rc ? rc : dalloc(m, &m->x, T * c.dim);
+  rc = rc ? rc : dalloc(m, &m->xn, T * c.dim);
+  rc = rc ? rc : dalloc(m, &m->qkv, T * m->qkv_w);
+  rc = rc ? rc : dalloc(m, &m->attn, T * m->qd);
+  rc = rc ? rc : dalloc(m, &m->tmp, T * c.dim);
+  rc = rc ? rc : dalloc(m, &m->gu, T * 2 * c.ffn_dim);
+  rc = rc ? rc : dalloc(m, &m->h, T * c.ffn_dim);
+  rc = rc ? rc : dalloc(m, &m->logits, T * c.vocab);
+  rc = rc ? rc : dalloc(m, &m->part, static_cast<size_t>(c.n_heads) * m->max_splits * (kMaxHeadDim + 2));
+  rc = rc ? rc : dalloc(m, &m->d_tokens, T);
+  rc = rc ? rc : dalloc(m, &m->d_gen, T + 1);
+  rc = rc ? rc : dalloc(m, &m->d_pos, 1);
+  if (rc != MRI_OK) {
+    mri_llama_free(m);
+    return rc;
+  }
+  cudaMemset(m->kc, 0, static_cast<size_t>(c.n_layers) * c.max_seq * m->kvd * sizeof(float));
+  cudaMemset(m->vc, 0, static_cast<size_t>(c.n_layers) * c.max_seq * m->kvd * sizeof(float));
+  // Carve the blobs into QuantizedMatrix views, each starting 256-byte
+  // aligned (TMA and vector loads need 16-byte aligned rows and scales).
+  size_t wo = 0, so = 0;
+  auto view = [&](size_t n_out, size_t k_in) {
+    mri_qmatrix q{ctx->device, m->w_blob + wo, m->s_blob + so, n_out, k_in, false};
+    wo += (n_out * k_in + 255) / 256 * 256;
+    so += (n_out + 63) / 64 * 64;
+    return q;
+  };
+  for (uint32_t l = 0; l < c.n_layers; ++l) {
+    m->wqkv.push_back(view(m->qkv_w, c.dim));
+    m->wo.push_back(view(c.dim, m->qd));
+    m->wgu.push_back(view(2 * static_cast<size_t>(c.ffn_dim), c.dim));
+    m->wdown.push_back(view(c.dim, c.ffn_dim));
+  }
+  m->wout = view(c.vocab, c.dim);
+  *out = m;
+  return MRI_OK;
+}
+
+int mri_llama_free(mri_llama* m) {
+  if (!m) return MRI_OK;
+  cudaSetDevice(m->ctx->device);
+  cudaStreamSynchronize(m->ctx->stream);
+  if (m->decode_exec) cudaGraphExecDestroy(m->decode_exec);
+  for (void* p : m->allocs) cudaFree(p);
+  delete m;
+  return MRI_OK;
+}
+
+int mri_llama_set_rope(mri_llama* m, const float* cos_t, const float* sin_t) {
+  if (!m || !cos_t || !sin_t) return fail(MRI_ERR_INVALID_ARGUMENT, "null argument");
+  const size_t n = static_cast<size_t>(m->cfg.max_seq) * (m->hd / 2) * sizeof(float);
+  LL_TRY(cudaMemcpy(m->rope_cos, cos_t, n, cudaMemcpyHostToDevice));
+  LL_TRY(cudaMemcpy(m->rope_sin, sin_t, n, cudaMemcpyHostToDevice));
+  return MRI_OK;
+}
+
+int mri_llama_set_embedding(mri_llama* m, const float* token_embd) {
+  if (!m || !token_embd) return fail(MRI_ERR_INVALID_ARGUMENT, "null argument");
+  LL_TRY(cudaMemcpy(m->embd, token_embd, static_cast<size_t>(m->cfg.vocab) * m->cfg.dim * 4,
+                    cudaMemcpyHostToDevice));
+  return MRI_OK;
+}
+
+int mri_llama_set_norms(mri_llama* m, const float* attn_norm, const float* ffn_norm,
+                        const float* output_norm) {
+  if (!m || !attn_norm || !ffn_norm || !output_norm) return fail(MRI_ERR_INVALID_ARGUMENT, "null argument");
+  const size_t ld = static_cast<size_t>(m->cfg.n_layers) * m->cfg.dim * 4;
+  LL_TRY(cudaMemcpy(m->attn_norm, attn_norm, ld, cudaMemcpyHostToDevice));
+  LL_TRY(cudaMemcpy(m->ffn_norm, ffn_norm, ld, cudaMemcpyHostToDevice));
+  LL_TRY(cudaMemcpy(m->out_norm, output_norm, m->cfg.dim * 4, cudaMemcpyHostToDevice));
+  return MRI_OK;
+}
+
+static int put_rows(const mri_qmatrix& q, size_t row0, const int8_t* w, const float* s, size_t rows) {
+  LL_TRY(cudaMemcpy(q.data + row0 * q.k_in, w, rows * q.k_in, cudaMemcpyHostToDevice));
+  LL_TRY(cudaMemcpy(q.scales + row0, s, rows * 4, cudaMemcpyHostToDevice));
+  return MRI_OK;
+}
+
+int mri_llama_set_layer(mri_llama* m, uint32_t layer, const int8_t* wq, const float* sq,
+                        const int8_t* wk, const float* sk, const int8_t* wv, const float* sv,
+                        const int8_t* wo, const float* so, const int8_t* wgate, const float* sgate,
+                        const int8_t* wup, const float* sup, const int8_t* wdown, const float* sdown) {
+  if (!m) return fail(MRI_ERR_INVALID_ARGUMENT, "null model");
+  if (layer >= m->cfg.n_layers) return fail(MRI_ERR_INVALID_SHAPE, "layer %u out of range", layer);
+  const auto& c = m->cfg;
+  if (int rc = put_rows(m->wqkv[layer], 0, wq, sq, m->qd)) return rc;
+  if (int rc = put_rows(m->wqkv[layer], m->qd, wk, sk, m->kvd)) return rc;
+  if (int rc = put_rows(m->wqkv[layer], m->qd + m->kvd, wv, sv, m->kvd)) return rc;
+  if (int rc = put_rows(m->wo[layer], 0, wo, so, c.dim)) return rc;
+  if (int rc = put_rows(m->wgu[layer], 0, wgate, sgate, c.ffn_dim)) return rc;
+  if (int rc = put_rows(m->wgu[layer], c.ffn_dim, wup, sup, c.ffn_dim)) return rc;
+  if (int rc = put_rows(m->wdown[layer], 0, wdown, sdown, c.dim)) return rc;
+  return MRI_OK;
+}
+
+int mri_llama_set_output(mri_llama* m, const int8_t* w, const float* s) {
+  if (!m) return fail(MRI_ERR_INVALID_ARGUMENT, "null model");
+  return put_rows(m->wout, 0, w, s, m->cfg.vocab);
+}
+
+int mri_llama_init_random(mri_llama* m, uint64_t seed) {
+  if (!m) return fail(MRI_ERR_INVALID_ARGUMENT, "null model");
+  const auto& c = m->cfg;
+  const BlobLayout b = blob_layout(m);
+  const int sms = m->ctx->dev.sm_count;
+  cudaStream_t st = m->ctx->stream;
+  fill_i8_kernel<<<sms * 8, 256, 0, st>>>(m->w_blob, b.total_w, seed);
+  // Per-channel scales of N(0, 0.02)-like weights quantized to int8.
+  fill_f32_kernel<<<sms * 8, 256, 0, st>>>(m->s_blob, b.total_s, seed + 1, 4e-4f, 8e-4f);
+  fill_f32_kernel<<<sms * 8, 256, 0, st>>>(m->embd, static_cast<size_t>(c.vocab) * c.dim, seed + 2,
+                                           -1.0f, 1.0f);
+  fill_f32_kernel<<<sms, 256, 0, st>>>(m->attn_norm, static_cast<size_t>(c.n_layers) * c.dim, seed + 3,
+                                       1.0f, 1.0f);
+  fill_f32_kernel<<<sms, 256, 0, st>>>(m->ffn_norm, static_cast<size_t>(c.n_layers) * c.dim, seed + 4,
+                                       1.0f, 1.0f);
+  fill_f32_kernel<<<1, 256, 0, st>>>(m->out_norm, c.dim, seed + 5, 1.0f, 1.0f);
+  LL_TRY(cudaGetLastError());
+  LL_TRY(cudaStreamSynchronize(st));
+  return MRI_OK;
+}
+
+int mri_llama_forward(mri_llama* m, const uint32_t* tokens, size_t n, float* logits) {
+  if (!m || !tokens) return fail(MRI_ERR_INVALID_ARGUMENT, "null argument");
+  g_model_error.clear();
+  if (int rc = check_tokens(m, tokens, n)) return rc;
+  cudaSetDevice(m->ctx->device);
+  if (int rc = prefill(m, tokens, n)) return rc;
+  if (int rc = lm_head(m, 0, n)) return rc;
+  if (logits)
+    LL_TRY(cudaMemcpyAsync(logits, m->logits, n * m->cfg.vocab * 4, cudaMemcpyDeviceToHost,
+                           m->ctx->stream));
+  LL_TRY(cudaStreamSynchronize(m->ctx->stream));
+  return mri_ctx_check_device_status(m->ctx) ? fail(MRI_ERR_TIMEOUT, "%s", mri_last_error()) : MRI_OK;
+}
+
+int mri_llama_forward_decode(mri_llama* m, uint32_t token, size_t pos, float* logits) {
+  if (!m) return fail(MRI_ERR_INVALID_ARGUMENT, "null model");
+  g_model_error.clear();
+  if (token >= m->cfg.vocab)
+    return fail(MRI_ERR_INVALID_SHAPE, "token id %u >= vocab_size %u", token, m->cfg.vocab);
+  if (pos >= m->cfg.max_seq)
+    return fail(MRI_ERR_INVALID_SHAPE, "position %zu beyond max_seq %u", pos, m->cfg.max_seq);
+  cudaSetDevice(m->ctx->device);
+  if (int rc = ensure_decode_graph(m)) return rc;
+  cudaStream_t st = m->ctx->stream;
+  const int p = static_cast<int>(pos);
+  LL_TRY(cudaMemcpyAsync(m->d_tokens, &token, sizeof(uint32_t), cudaMemcpyHostToDevice, st));
+  LL_TRY(cudaMemcpyAsync(m->d_pos, &p, sizeof(int), cudaMemcpyHostToDevice, st));
+  LL_TRY(cudaGraphLaunch(m->decode_exec, st));
+  if (logits)
+    LL_TRY(cudaMemcpyAsync(logits, m->logits, m->cfg.vocab * 4, cudaMemcpyDeviceToHost, st));
+  LL_TRY(cudaStreamSynchronize(st));
+  return mri_ctx_check_device_status(m->ctx) ? fail(MRI_ERR_TIMEOUT, "%s", mri_last_error()) : MRI_OK;
+}
+
+int mri_llama_generate_greedy(mri_llama* m, const uint32_t* prompt, size_t n_prompt,
+                              size_t n_decode, uint32_t* out_tokens, float* prefill_ms,
+                              float* decode_ms) {
+  if (!m || !prompt) return fail(MRI_ERR_INVALID_ARGUMENT, "null argument");
+  g_model_error.clear();
+  if (int rc = check_tokens(m, prompt, n_prompt)) return rc;
+  if (n_prompt + n_decode > m->cfg.max_seq)
+    return fail(MRI_ERR_INVALID_SHAPE, "prompt %zu + %zu decode steps exceed max_seq %u", n_prompt,
+                n_decode, m->cfg.max_seq);
+  cudaSetDevice(m->ctx->device);
+  if (int rc = ensure_decode_graph(m)) return rc;
+  cudaStream_t st = m->ctx->stream;
+  cudaEvent_t e0, e1, e2;
+  cudaEventCreate(&e0);
+  cudaEventCreate(&e1);
+  cudaEventCreate(&e2);
+  int rc = MRI_OK;
+  cudaEventRecord(e0, st);
+  rc = prefill(m, prompt, n_prompt);
+  if (rc == MRI_OK) rc = lm_head(m, n_prompt - 1, 1);
+  if (rc == MRI_OK) {
+    const int p = static_cast<int>(n_prompt) - 1;  // argmax advances it to n_prompt
+    cudaMemcpyAsync(m->d_pos, &p, sizeof(int), cudaMemcpyHostToDevice, st);
+    argmax_kernel<<<1, 1024, 0, st>>>(m->logits, m->cfg.vocab, m->d_tokens, m->d_pos, m->d_gen);
+    cudaEventRecord(e1, st);
+    for (size_t i = 0; i < n_decode && rc == MRI_OK; ++i)
+      if (cudaGraphLaunch(m->decode_exec, st) != cudaSuccess) rc = fail(MRI_ERR_CUDA, "graph launch");
+    cudaEventRecord(e2, st);
+    if (out_tokens)
+      cudaMemcpyAsync(out_tokens, m->d_gen + n_prompt, (n_decode + 1) * sizeof(uint32_t),
+                      cudaMemcpyDeviceToHost, st);
+  }
+  cudaError_t e = cudaStreamSynchronize(st);
+  if (rc == MRI_OK && e != cudaSuccess) rc = fail(MRI_ERR_CUDA, "%s", cudaGetErrorString(e));
+  if (rc == MRI_OK) {
+    float a = 0, b = 0;
+    cudaEventElapsedTime(&a, e0, e1);
+    cudaEventElapsedTime(&b, e1, e2);
+    if (prefill_ms) *prefill_ms = a;
+    if (decode_ms) *decode_ms = b;
+  }
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  cudaEventDestroy(e2);
+  if (rc == MRI_OK && mri_ctx_check_device_status(m->ctx))
+    rc = fail(MRI_ERR_TIMEOUT, "%s", mri_last_error());
+  return rc;
+}
+
+int mri_llama_launches_per_decode_step(const mri_llama* m, size_t* count) {
+  if (!m || !count) return fail(MRI_ERR_INVALID_ARGUMENT, "null argument");
+  *count = m->graph_kernels;  // kernel nodes of the captured decode step (0 before capture)
+  return MRI_OK;
+}
+
+}  // extern "C"

@@ -116,3 +116,13 @@ def dequantize_q4_0(data):
     hi = (b[:, 2:] >> 4).astype(np.int32) - 8
     q = np.stack([lo, hi], axis=-1).reshape(-1, 32).astype(np.float32)
     return (scale[:, None] * q).reshape(-1)
+
+
+def rope_table(max_seq, head_dim, base=10000.0):
+    """RopeTable::new (ops/rope.rs:43-76): cos/sin [max_seq, head_dim/2] of
+    pos * base^(-2i/head_dim), evaluated in f64 and rounded to f32."""
+    half = head_dim // 2
+    i = np.arange(half, dtype=np.float64)
+    theta = 1.0 / np.power(np.float64(base), 2.0 * i / head_dim)
+    ang = np.arange(max_seq, dtype=np.float64)[:, None] * theta[None, :]
+    return np.cos(ang).astype(np.float32).reshape(-1), np.sin(ang).astype(np.float32).reshape(-1)

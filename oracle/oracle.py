@@ -59,6 +59,12 @@ def lib():
             "oref_matmul_q8_0_direct": (ctypes.c_int, [_P, _SZ, _SZ, _P, _SZ, _SZ, _P]),
             "oref_matmul_q4_0_dequant": (ctypes.c_int, [_P, _SZ, _SZ, _P, _SZ, _SZ, _SZ, _P]),
             "oref_hardware_threads": (ctypes.c_int, []),
+            "oref_rmsnorm": (None, [_P, _SZ, _SZ, _P, ctypes.c_float, _P]),
+            "oref_rope_table": (None, [_SZ, _SZ, ctypes.c_float, _P, _P]),
+            "oref_rope_apply": (None, [_P, _SZ, _SZ, _SZ, _P, _P, _SZ]),
+            "oref_gqa_causal_offset": (None, [_P, _P, _P, _SZ, _SZ, _SZ, _SZ, _SZ, _SZ, _P]),
+            "oref_swiglu": (None, [_P, _P, _SZ, _P]),
+            "oref_smooth_weight": (None, [_SZ, _SZ, ctypes.c_float, _P]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -254,3 +260,45 @@ def matmul_q4_0_dequant(x, m, k_x, w_bytes, n_out, k):
 
 def hardware_threads():
     return int(lib().oref_hardware_threads())
+
+
+# ── model glue (LlamaModelInt8 checker) ──────────────────────────────────────
+
+def rmsnorm(x, d, w, eps):
+    x = _f32(x).reshape(-1)
+    out = np.empty_like(x)
+    lib().oref_rmsnorm(_ptr(x), x.size // d, d, _ptr(_f32(w)), ctypes.c_float(eps), _ptr(out))
+    return out
+
+
+def rope_table(max_seq, head_dim, base):
+    c = np.empty(max_seq * (head_dim // 2), np.float32)
+    s = np.empty_like(c)
+    lib().oref_rope_table(max_seq, head_dim, ctypes.c_float(base), _ptr(c), _ptr(s))
+    return c, s
+
+
+def rope_apply(x, seq, n_heads, head_dim, cos_t, sin_t, start_pos):
+    x = np.array(x, dtype=np.float32, copy=True).reshape(-1)
+    lib().oref_rope_apply(_ptr(x), seq, n_heads, head_dim, _ptr(_f32(cos_t)), _ptr(_f32(sin_t)), start_pos)
+    return x
+
+
+def gqa_causal_offset(q, k, v, seq_q, seq_k, n_heads, n_kv, head_dim, start_pos):
+    out = np.empty(seq_q * n_heads * head_dim, np.float32)
+    lib().oref_gqa_causal_offset(_ptr(_f32(q)), _ptr(_f32(k)), _ptr(_f32(v)), seq_q, seq_k, n_heads, n_kv,
+                                 head_dim, start_pos, _ptr(out))
+    return out
+
+
+def swiglu(gate, up):
+    g, u = _f32(gate).reshape(-1), _f32(up).reshape(-1)
+    out = np.empty_like(g)
+    lib().oref_swiglu(_ptr(g), _ptr(u), g.size, _ptr(out))
+    return out
+
+
+def smooth_weight(rows, cols, seed):
+    out = np.empty(rows * cols, np.float32)
+    lib().oref_smooth_weight(rows, cols, ctypes.c_float(seed), _ptr(out))
+    return out

@@ -434,4 +434,115 @@ int oref_matmul_q4_0_dequant(const float* x, size_t m, size_t k_x,
   return OREF_OK;
 }
 
+// ── model glue ──────────────────────────────────────────────────────────────
+
+// ops/norm/rmsnorm.rs:51-117
+void oref_rmsnorm(const float* x, size_t rows, size_t d, const float* w, float eps, float* out) {
+  for (size_t r = 0; r < rows; ++r) {
+    const float* xr = x + r * d;
+    float sum = 0.0f;
+    for (size_t i = 0; i < d; ++i) sum += xr[i] * xr[i];
+    const float mean_sq = sum / static_cast<float>(d);
+    const float rms_inv = 1.0f / std::sqrt(mean_sq + eps);
+    for (size_t i = 0; i < d; ++i) out[r * d + i] = w[i] * (xr[i] * rms_inv);
+  }
+}
+
+// ops/rope.rs:43-76
+void oref_rope_table(size_t max_seq, size_t head_dim, float base, float* cos_out, float* sin_out) {
+  const size_t half = head_dim / 2;
+  std::vector<float> thetas(half);
+  for (size_t i = 0; i < half; ++i)
+    thetas[i] = 1.0f / std::pow(base, 2.0f * static_cast<float>(i) / static_cast<float>(head_dim));
+  for (size_t pos = 0; pos < max_seq; ++pos)
+    for (size_t i = 0; i < half; ++i) {
+      const float angle = static_cast<float>(pos) * thetas[i];
+      cos_out[pos * half + i] = std::cos(angle);
+      sin_out[pos * half + i] = std::sin(angle);
+    }
+}
+
+// ops/rope.rs:121-190
+void oref_rope_apply(float* x, size_t seq, size_t n_heads, size_t head_dim, const float* cos_t,
+                     const float* sin_t, size_t start_pos) {
+  const size_t half = head_dim / 2;
+  for (size_t s = 0; s < seq; ++s) {
+    const size_t pos = start_pos + s;
+    for (size_t h = 0; h < n_heads; ++h) {
+      float* base = x + s * n_heads * head_dim + h * head_dim;
+      for (size_t i = 0; i < half; ++i) {
+        const float c = cos_t[pos * half + i], sn = sin_t[pos * half + i];
+        const float x0 = base[2 * i], x1 = base[2 * i + 1];
+        base[2 * i] = x0 * c - x1 * sn;
+        base[2 * i + 1] = x1 * c + x0 * sn;
+      }
+    }
+  }
+}
+
+// ops/softmax.rs:36-57
+static void softmax_row(float* row, size_t n) {
+  if (n == 0) return;
+  float mx = -INFINITY;
+  for (size_t i = 0; i < n; ++i) mx = std::fmax(mx, row[i]);
+  float sum = 0.0f;
+  for (size_t i = 0; i < n; ++i) {
+    row[i] = std::exp(row[i] - mx);
+    sum += row[i];
+  }
+  const float inv_sum = 1.0f / sum;
+  for (size_t i = 0; i < n; ++i) row[i] *= inv_sum;
+}
+
+// attention/gqa.rs:217-237, attention/sdpa.rs:168-235, attention/mask.rs:77-115
+void oref_gqa_causal_offset(const float* q, const float* k, const float* v, size_t seq_q,
+                            size_t seq_k, size_t n_heads, size_t n_kv_heads, size_t head_dim,
+                            size_t start_pos, float* out) {
+  const size_t groups = n_heads / n_kv_heads;
+  const size_t qd = n_heads * head_dim, kvd = n_kv_heads * head_dim;
+  const float scale = 1.0f / std::sqrt(static_cast<float>(head_dim));
+  std::vector<float> scores(seq_q * seq_k), acc(seq_q * head_dim);
+  for (size_t h = 0; h < n_heads; ++h) {
+    const size_t kv_h = h / groups;
+    // scores = q_h @ k_h^T in the ikj order of matmul_naive (sequential over p)
+    std::fill(scores.begin(), scores.end(), 0.0f);
+    for (size_t i = 0; i < seq_q; ++i)
+      for (size_t p = 0; p < head_dim; ++p) {
+        const float a = q[i * qd + h * head_dim + p];
+        for (size_t j = 0; j < seq_k; ++j) scores[i * seq_k + j] += a * k[j * kvd + kv_h * head_dim + p];
+      }
+    for (size_t i = 0; i < seq_q; ++i) {
+      const size_t abs_pos = start_pos + i;
+      for (size_t j = 0; j < seq_k; ++j) {
+        const float bias = j > abs_pos ? -INFINITY : 0.0f;
+        scores[i * seq_k + j] = scores[i * seq_k + j] * scale + bias;
+      }
+      softmax_row(&scores[i * seq_k], seq_k);
+    }
+    std::fill(acc.begin(), acc.end(), 0.0f);
+    for (size_t i = 0; i < seq_q; ++i)
+      for (size_t p = 0; p < seq_k; ++p) {
+        const float wgt = scores[i * seq_k + p];
+        for (size_t j = 0; j < head_dim; ++j) acc[i * head_dim + j] += wgt * v[p * kvd + kv_h * head_dim + j];
+      }
+    for (size_t i = 0; i < seq_q; ++i)
+      for (size_t j = 0; j < head_dim; ++j) out[i * qd + h * head_dim + j] = acc[i * head_dim + j];
+  }
+}
+
+// ops/activation/swiglu.rs:39-61, silu.rs:23-26
+void oref_swiglu(const float* gate, const float* up, size_t n, float* out) {
+  for (size_t i = 0; i < n; ++i) {
+    const float g = gate[i];
+    out[i] = (g / (1.0f + std::exp(-g))) * up[i];
+  }
+}
+
+// model/llama/forward_int8.rs:575-580
+void oref_smooth_weight(size_t rows, size_t cols, float seed, float* out) {
+  const float total = static_cast<float>(rows * cols);
+  for (size_t i = 0; i < rows * cols; ++i)
+    out[i] = std::sin(static_cast<float>(i) * seed * 0.01f - total * seed * 0.005f) * 0.5f;
+}
+
 }  // extern "C"

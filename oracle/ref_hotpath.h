@@ -100,6 +100,25 @@ int oref_matmul_q4_0_dequant(const float* x, size_t m, size_t k_x,
                              const uint8_t* w_bytes, size_t w_len,
                              size_t n_out, size_t k, float* out);
 
+/* ── model glue around the projections (LlamaModelInt8 checker) ───────────── */
+/* ops/norm/rmsnorm.rs:51-117: per row, sequential sum of squares / d,
+ * rms_inv = 1 / sqrt(mean_sq + eps), out = w * (x * rms_inv). */
+void oref_rmsnorm(const float* x, size_t rows, size_t d, const float* w, float eps, float* out);
+/* ops/rope.rs:43-76: cos/sin tables [max_seq, head_dim/2]. */
+void oref_rope_table(size_t max_seq, size_t head_dim, float base, float* cos_out, float* sin_out);
+/* ops/rope.rs:121-190: x [seq, n_heads, head_dim] in place, interleaved pairs. */
+void oref_rope_apply(float* x, size_t seq, size_t n_heads, size_t head_dim, const float* cos_t,
+                     const float* sin_t, size_t start_pos);
+/* attention/gqa.rs:217-237 + attention/sdpa.rs:168-235 + attention/mask.rs:77-115:
+ * q [seq_q, n_heads*hd], k/v [seq_k, n_kv*hd] -> out [seq_q, n_heads*hd]. */
+void oref_gqa_causal_offset(const float* q, const float* k, const float* v, size_t seq_q,
+                            size_t seq_k, size_t n_heads, size_t n_kv_heads, size_t head_dim,
+                            size_t start_pos, float* out);
+/* ops/activation/swiglu.rs:39-61: silu(g) * u, silu(x) = x / (1 + exp(-x)). */
+void oref_swiglu(const float* gate, const float* up, size_t n, float* out);
+/* forward_int8.rs:575-580 (test helper smooth_weight), for fixtures. */
+void oref_smooth_weight(size_t rows, size_t cols, float seed, float* out);
+
 /* Hardware threads the parallel restatement would use. */
 int oref_hardware_threads(void);
 

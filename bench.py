@@ -282,7 +282,35 @@ def secondary_measurements(torch, mri, lib, device, peak_hbm, peak_tc):
     except Exception as e:  # noqa: BLE001 - side measurement only
         res["prefill_m512"] = {"error": str(e)[:200]}
     ctx.synchronize()
+    res["llama7b_int8"] = model_measurement(mri, device, peak_hbm)
     return res
+
+
+def model_measurement(mri, device, peak_hbm):
+    """Llama-7B-shaped LlamaModelInt8 (32 layers, d=4096,
+    32 heads, FFN 11008, vocab 32000), synthetic weights generated on the
+    device, 512-token prefill then 128 greedy decode steps (CUDA graph per
+    step).  The second of two runs is reported."""
+    try:
+        L, d, ffn, V = 32, 4096, 11008, 32000
+        cfg = mri.LlamaConfig(L, d, 32, ffn, V, 640)
+        m = mri.LlamaModelInt8.random(cfg, seed=1, ctx=mri.Context(device))
+        prompt = np.random.default_rng(0).integers(0, V, size=512).astype(np.uint32)
+        for _ in range(2):
+            toks, pre_ms, dec_ms = m.generate_greedy(prompt, 128)
+        w_bytes = L * (3 * d * d + d * d + 2 * ffn * d + d * ffn) + V * d
+        kv_bytes = L * 2 * (512 + 64) * d * 4  # mean cached positions per step
+        step_s = dec_ms / 1e3 / 128
+        res = {"prefill_tok_s": round(512 / (pre_ms / 1e3), 1), "decode_tok_s": round(128 / (dec_ms / 1e3), 1),
+               "prefill_ms": round(pre_ms, 3), "decode_ms_per_token": round(step_s * 1e3, 4),
+               "decode_roofline_frac_hbm": round((w_bytes + kv_bytes) / step_s / 1e9 / peak_hbm, 4),
+               "decode_bytes_per_token": w_bytes + kv_bytes,
+               "kernels_per_decode_step": m.kernels_per_decode_step(),
+               "data": "synthetic weights (device hash RNG), random prompt (seed 0)"}
+        del m
+        return res
+    except Exception as e:  # noqa: BLE001 - side measurement only
+        return {"error": str(e)[:300]}
 
 
 def run_ours(args, rank, world, local_rank):

@@ -92,6 +92,17 @@ int upload_bytes(const T* host, size_t count, T** dev) {
   return MRI_OK;
 }
 
+}  // namespace
+
+namespace mri {
+int ctx_reserve_scratch(::mri_ctx* ctx, size_t bytes) { return ensure_scratch(ctx, bytes); }
+size_t int8_scratch_bytes(size_t m, size_t k) {
+  return amax_bytes(m) + al(m * sizeof(float)) + al(m * k);
+}
+}  // namespace mri
+
+namespace {
+
 // ── INT8 dispatch ────────────────────────────────────────────────────────────
 // `act` describes the full [m, K] activation set.  Small m uses the fused
 // streaming GEMV; larger m quantizes once (per-tensor scale over all rows,

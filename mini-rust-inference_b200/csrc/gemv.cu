@@ -229,14 +229,53 @@ __device__ void load_act_i8_rowmajor(const ActArgs& act, size_t K, int8_t* s_act
 }
 
 // ── K2: INT8 per-channel streaming GEMV (K % 16 == 0) ───────────────────────
+// Rows are streamed in groups of 8 (one per consumer warp).  When 8 full rows
+// would not leave room for three stages, each group is split into nk K-chunks
+// of kc bytes: stage (g, c) holds bytes [c*kc, c*kc + kc) of the group's rows,
+// copied row by row, and a warp keeps its row's INT32 partial sums in
+// registers across the chunks (integer sums: the split is exact).
+
+__device__ void stream_producer_i8(const int8_t* W, size_t K, size_t kc, int nk, size_t begin,
+                                   size_t end, uint64_t* full, uint64_t* empty, uint8_t* stages_base,
+                                   size_t stage_stride, int n_stages, int* status) {
+  const uint64_t policy = l2_policy_evict_first();
+  const int groups = static_cast<int>((end - begin + kRowsPerStage - 1) / kRowsPerStage);
+  const int iters = groups * nk;
+  int issued = 0;
+  for (int it = 0; it < iters; ++it) {
+    const int s = it % n_stages;
+    if (it >= n_stages) {
+      if (!mbar_wait(&empty[s], ((it / n_stages) - 1) & 1, status)) break;
+    }
+    const int g = it / nk, c = it % nk;
+    const size_t r0 = begin + static_cast<size_t>(g) * kRowsPerStage;
+    const size_t nrows = std::min<size_t>(kRowsPerStage, end - r0);
+    uint8_t* dst = stages_base + s * stage_stride;
+    if (nk == 1) {
+      const uint32_t bytes = static_cast<uint32_t>(nrows * K);
+      mbar_arrive_expect_tx(&full[s], bytes);
+      bulk_copy_g2s_stream(dst, W + r0 * K, bytes, &full[s], policy);
+    } else {
+      const size_t k0 = static_cast<size_t>(c) * kc;
+      const uint32_t bytes = static_cast<uint32_t>(std::min(kc, K - k0));
+      mbar_arrive_expect_tx(&full[s], bytes * static_cast<uint32_t>(nrows));
+      for (size_t r = 0; r < nrows; ++r)
+        bulk_copy_g2s_stream(dst + r * kc, W + (r0 + r) * K + k0, bytes, &full[s], policy);
+    }
+    issued = it + 1;
+  }
+  for (int it = std::max(0, issued - n_stages); it < issued; ++it)
+    mbar_wait(&full[it % n_stages], (it / n_stages) & 1, status);
+}
 
 template <int M>
 __global__ void __launch_bounds__(kThreads, 1)
     gemv_i8_tma_kernel(const int8_t* __restrict__ W, const float* __restrict__ w_scales, size_t N,
                        size_t K, ActArgs act, float* __restrict__ out, int32_t* __restrict__ acc_out,
-                       int n_stages, int* status) {
+                       int n_stages, int nk, int* status) {
   extern __shared__ __align__(128) uint8_t smem[];
-  const StreamLayout L = make_layout(M * K, 0, kRowsPerStage * K, n_stages);
+  const size_t kc = nk == 1 ? K : align_up((K + nk - 1) / nk, 16);
+  const StreamLayout L = make_layout(M * K, 0, kRowsPerStage * kc, n_stages);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
   uint64_t* empty = full + n_stages;
   float* s_scale = reinterpret_cast<float*>(smem + L.scales);
@@ -252,8 +291,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (warp == 0) {
     if (lane == 0)
-      stream_producer(reinterpret_cast<const uint8_t*>(W), K, begin, end, full, empty, stage0,
-                      L.stage_bytes, n_stages, status);
+      stream_producer_i8(W, K, kc, nk, begin, end, full, empty, stage0, L.stage_bytes, n_stages,
+                         status);
     return;
   }
   pdl_wait();
@@ -263,34 +302,43 @@ __global__ void __launch_bounds__(kThreads, 1)
   for (int m = 0; m < M; ++m) s_a[m] = s_scale[m];
 
   const int cw = warp - 1;
-  const int chunks = static_cast<int>(K / 16);
-  const int iters = static_cast<int>((end - begin + kRowsPerStage - 1) / kRowsPerStage);
-  // The per-row weight scale is loaded one stage ahead so its global-load
-  // latency overlaps the stage wait and the dot product.
+  const int groups = static_cast<int>((end - begin + kRowsPerStage - 1) / kRowsPerStage);
+  // The per-row weight scale is loaded one group ahead so its global-load
+  // latency overlaps the stage waits and the dot products.
   float sw_next = begin + cw < end ? __ldg(w_scales + begin + cw) : 0.0f;
-  for (int it = 0; it < iters; ++it) {
-    const int s = it % n_stages;
-    const size_t row = begin + static_cast<size_t>(it) * kRowsPerStage + cw;
+  int it = 0;
+  for (int g = 0; g < groups; ++g) {
+    const size_t row = begin + static_cast<size_t>(g) * kRowsPerStage + cw;
     const float sw = sw_next;
     if (row + kRowsPerStage < end) sw_next = __ldg(w_scales + row + kRowsPerStage);
-    if (!mbar_wait(&full[s], (it / n_stages) & 1, status)) return;
-    if (row < end) {
-      const uint4* wrow = reinterpret_cast<const uint4*>(stage0 + s * L.stage_bytes + cw * K);
-      int acc[M];
+    int acc[M];
 #pragma unroll
-      for (int m = 0; m < M; ++m) acc[m] = 0;
+    for (int m = 0; m < M; ++m) acc[m] = 0;
+    for (int c = 0; c < nk; ++c, ++it) {
+      const int s = it % n_stages;
+      if (!mbar_wait(&full[s], (it / n_stages) & 1, status)) return;
+      if (row < end) {
+        const size_t k0 = static_cast<size_t>(c) * kc;
+        const int chunks = static_cast<int>(std::min(kc, K - k0) / 16);
+        const uint4* wrow = reinterpret_cast<const uint4*>(stage0 + s * L.stage_bytes + cw * kc);
+        const int8_t* arow = s_act + k0;
 #pragma unroll 4
-      for (int c = lane; c < chunks; c += 32) {
-        const uint4 w = wrow[c];
+        for (int q = lane; q < chunks; q += 32) {
+          const uint4 w = wrow[q];
 #pragma unroll
-        for (int m = 0; m < M; ++m) {
-          const uint4 a = reinterpret_cast<const uint4*>(s_act + m * K)[c];
-          acc[m] = dp4a(w.x, a.x, acc[m]);
-          acc[m] = dp4a(w.y, a.y, acc[m]);
-          acc[m] = dp4a(w.z, a.z, acc[m]);
-          acc[m] = dp4a(w.w, a.w, acc[m]);
+          for (int m = 0; m < M; ++m) {
+            const uint4 a = reinterpret_cast<const uint4*>(arow + m * K)[q];
+            acc[m] = dp4a(w.x, a.x, acc[m]);
+            acc[m] = dp4a(w.y, a.y, acc[m]);
+            acc[m] = dp4a(w.z, a.z, acc[m]);
+            acc[m] = dp4a(w.w, a.w, acc[m]);
+          }
         }
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    if (row < end) {
 #pragma unroll
       for (int m = 0; m < M; ++m) acc[m] = warp_sum_i(acc[m]);
 #pragma unroll
@@ -301,8 +349,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
   }
 }
 
@@ -789,24 +835,41 @@ cudaError_t launch_stream_kernel(void (*k)(KArgs...), int grid, size_t smem, cud
 
 }  // namespace
 
+// K-chunk count for the INT8 stream: the smallest nk whose 8 x kc stage
+// leaves room for three stages next to the activations.
+int i8_chunks(int M, size_t K, StreamConfig* cfg_out) {
+  for (int nk = 1; nk <= 64; ++nk) {
+    const size_t kc = nk == 1 ? K : align_up((K + nk - 1) / nk, 16);
+    if (nk > 1 && kc * (nk - 1) >= K) break;  // chunks would be empty
+    const StreamConfig c = pick_config(fixed_bytes_of(M * K, 0), kRowsPerStage * kc);
+    if (c.stages >= 3) {
+      if (cfg_out) *cfg_out = c;
+      return nk;
+    }
+  }
+  return 0;
+}
+
 bool gemv_i8_tma_supported(const DeviceInfo&, int M, size_t K) {
   if (M < 1 || M > 8 || K == 0 || K % 16 != 0) return false;
-  return pick_stages(fixed_bytes_of(M * K, 0), kRowsPerStage * K) >= 3;
+  return i8_chunks(M, K, nullptr) > 0;
 }
 
 cudaError_t launch_gemv_i8_tma(const DeviceInfo& dev, cudaStream_t st, int M, const int8_t* W,
                                const float* w_scales, size_t N, size_t K, const ActArgs& act,
                                float* out, int32_t* acc_out, int* status, LaunchStats* ls) {
-  const StreamConfig cfg = pick_config(fixed_bytes_of(M * K, 0), kRowsPerStage * K);
+  StreamConfig cfg;
+  const int nk = i8_chunks(M, K, &cfg);
+  if (nk == 0) return cudaErrorInvalidValue;
+  const size_t kc = nk == 1 ? K : align_up((K + nk - 1) / nk, 16);
   const int stages = cfg.stages;
-  if (stages < 2) return cudaErrorInvalidValue;
-  const size_t smem = make_layout(M * K, 0, kRowsPerStage * K, stages).total;
+  const size_t smem = make_layout(M * K, 0, kRowsPerStage * kc, stages).total;
   const int grid = stream_grid(dev, N, cfg.ctas_per_sm);
   MRI_DISPATCH_M(M, {
     cudaError_t e = set_smem(gemv_i8_tma_kernel<kM>, smem, dev.device);
     if (e != cudaSuccess) return e;
     e = launch_stream_kernel(gemv_i8_tma_kernel<kM>, grid, smem, st, W, w_scales, N, K, act, out,
-                             acc_out, stages, status);
+                             acc_out, stages, nk, status);
     if (e != cudaSuccess) return e;
   });
   if (ls) ls->launches++;

@@ -6,6 +6,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+struct mri_ctx;
+
 namespace mri {
 
 // Where the activations of a product come from.
@@ -76,6 +78,14 @@ cudaError_t launch_gemv_q4_0_tma(const DeviceInfo& dev, cudaStream_t st, int M, 
 cudaError_t launch_gemv_q4_0_generic(const DeviceInfo& dev, cudaStream_t st, int M,
                                      const uint8_t* W, size_t N, size_t K, const float* x,
                                      float* out, LaunchStats* ls);
+
+// Grows the context scratch to at least `bytes` (synchronizes the stream
+// when it reallocates).  Callers that capture CUDA graphs reserve their
+// maximum first: a captured launch keeps the scratch address it saw.
+int ctx_reserve_scratch(struct ::mri_ctx* ctx, size_t bytes);
+// Scratch bytes an INT8 product with per-tensor quantization of an [m, k]
+// input needs.
+size_t int8_scratch_bytes(size_t m, size_t k);
 
 // ── tensor-core INT8 GEMM (gemm_tc.cu) ──────────────────────────────────────
 bool gemm_i8_tc_supported(const DeviceInfo& dev, size_t M, size_t N, size_t K);

@@ -600,7 +600,13 @@ int mri_llama_create(mri_ctx* ctx, const mri_llama_config* cfg, mri_llama** out)
     return fail(MRI_ERR_INVALID_SHAPE, "head_dim=%d must be even and <= %d", hd, kMaxHeadDim);
   cudaSetDevice(ctx->device);
   mri_llama* m = new mri_llama();
-  m->ctx = ctx;
+  // A private context on the caller's stream: its scratch is the model's own,
+  // so products run by the caller on `ctx` cannot move it under the captured
+  // decode graph.
+  if (mri_ctx_create_on_stream(ctx->device, ctx->stream, &m->ctx) != MRI_OK) {
+    delete m;
+    return fail(MRI_ERR_CUDA, "model context: %s", mri_last_error());
+  }
   m->cfg = c;
   m->cfg.n_kv_heads = n_kv;
   m->hd = hd;
@@ -638,13 +644,20 @@ int mri_llama_create(mri_ctx* ctx, const mri_llama_config* cfg, mri_llama** out)
     mri_llama_free(m);
     return rc;
   }
+  // Reserve the context scratch for the largest projection input now: the
+  // captured decode graph keeps the scratch address it was captured with.
+  const size_t kmax = std::max<size_t>(std::max<size_t>(c.dim, c.ffn_dim), m->qd);
+  if (int r = mri::ctx_reserve_scratch(m->ctx, mri::int8_scratch_bytes(T, kmax))) {
+    mri_llama_free(m);
+    return fail(r, "scratch reservation: %s", mri_last_error());
+  }
   cudaMemset(m->kc, 0, static_cast<size_t>(c.n_layers) * c.max_seq * m->kvd * sizeof(float));
   cudaMemset(m->vc, 0, static_cast<size_t>(c.n_layers) * c.max_seq * m->kvd * sizeof(float));
   // Carve the blobs into QuantizedMatrix views, each starting 256-byte
   // aligned (TMA and vector loads need 16-byte aligned rows and scales).
   size_t wo = 0, so = 0;
   auto view = [&](size_t n_out, size_t k_in) {
-    mri_qmatrix q{ctx->device, m->w_blob + wo, m->s_blob + so, n_out, k_in, false};
+    mri_qmatrix q{m->ctx->device, m->w_blob + wo, m->s_blob + so, n_out, k_in, false};
     wo += (n_out * k_in + 255) / 256 * 256;
     so += (n_out + 63) / 64 * 64;
     return q;
@@ -666,6 +679,7 @@ int mri_llama_free(mri_llama* m) {
   cudaStreamSynchronize(m->ctx->stream);
   if (m->decode_exec) cudaGraphExecDestroy(m->decode_exec);
   for (void* p : m->allocs) cudaFree(p);
+  mri_ctx_destroy(m->ctx);
   delete m;
   return MRI_OK;
 }

@@ -103,7 +103,9 @@ __global__ void rope_kv_kernel(float* __restrict__ qkv, int ld, int n_heads, int
 
 // Decode attention, split over keys (attention/cached.rs:141-190 with
 // gqa.rs:217-237): block (h, s) handles keys [s*64, min(s*64+64, pos+1)) and
-// writes its running max, exp-sum and weighted V sum.
+// writes its running max, exp-sum and weighted V sum.  Two threads per key
+// each load half of the key row (16 float4 loads in flight per thread), so
+// the score pass is bandwidth- rather than latency-bound.
 __global__ void __launch_bounds__(128) attn_decode_partial(const float* __restrict__ q, int n_heads,
                                                            int n_kv, int hd,
                                                            const float* __restrict__ kc,
@@ -121,32 +123,55 @@ __global__ void __launch_bounds__(128) attn_decode_partial(const float* __restri
     }
     return;
   }
-  const int j1 = min(j0 + kAttnChunk, pos + 1);
+  const int nkeys = min(kAttnChunk, pos + 1 - j0);
   const int kv_h = h / (n_heads / n_kv);
   const int kvd = n_kv * hd;
-  __shared__ float sq[kMaxHeadDim];
+  __shared__ __align__(16) float sq[kMaxHeadDim];
   __shared__ float sp[kAttnChunk];
   __shared__ float red[4];
   for (int t = threadIdx.x; t < hd; t += blockDim.x) sq[t] = q[h * hd + t];
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int j = j0 + warp; j < j1; j += 4) {
-    const float* krow = kc + static_cast<size_t>(j) * kvd + kv_h * hd;
+  {
+    // thread pair (2j, 2j+1) -> key j; each thread covers hd/2 dims.
+    const int j = threadIdx.x >> 1, half = threadIdx.x & 1;
+    const int hh = hd / 2;
     float dot = 0.0f;
-    for (int t = lane; t < hd; t += 32) dot = __fmaf_rn(sq[t], krow[t], dot);
-    dot = mri::warp_sum_f(dot);
-    if (lane == 0) sp[j - j0] = __fmul_rn(dot, scale);
+    if (j < nkeys) {
+      const float* krow = kc + static_cast<size_t>(j0 + j) * kvd + kv_h * hd + half * hh;
+      if ((hh & 3) == 0) {
+        const float4* k4 = reinterpret_cast<const float4*>(krow);
+        const float4* q4 = reinterpret_cast<const float4*>(sq + half * hh);
+        float4 kv[kMaxHeadDim / 8];
+#pragma unroll
+        for (int i = 0; i < kMaxHeadDim / 8; ++i)
+          if (i < hh / 4) kv[i] = __ldg(k4 + i);
+#pragma unroll
+        for (int i = 0; i < kMaxHeadDim / 8; ++i)
+          if (i < hh / 4) {
+            const float4 qq = q4[i];
+            dot = __fmaf_rn(qq.x, kv[i].x, dot);
+            dot = __fmaf_rn(qq.y, kv[i].y, dot);
+            dot = __fmaf_rn(qq.z, kv[i].z, dot);
+            dot = __fmaf_rn(qq.w, kv[i].w, dot);
+          }
+      } else {
+        for (int i = 0; i < hh; ++i) dot = __fmaf_rn(sq[half * hh + i], krow[i], dot);
+      }
+    }
+    dot += __shfl_xor_sync(0xffffffffu, dot, 1);
+    if (half == 0 && j < nkeys) sp[j] = __fmul_rn(dot, scale);
   }
   __syncthreads();
   float mx = -INFINITY;
-  for (int j = threadIdx.x; j < j1 - j0; j += blockDim.x) mx = fmaxf(mx, sp[j]);
+  for (int j = threadIdx.x; j < nkeys; j += blockDim.x) mx = fmaxf(mx, sp[j]);
   mx = mri::warp_max(mx);
   if (lane == 0) red[warp] = mx;
   __syncthreads();
   mx = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
   __syncthreads();
   float l = 0.0f;
-  for (int j = threadIdx.x; j < j1 - j0; j += blockDim.x) {
+  for (int j = threadIdx.x; j < nkeys; j += blockDim.x) {
     const float p = expf(sp[j] - mx);
     sp[j] = p;
     l += p;
@@ -156,9 +181,21 @@ __global__ void __launch_bounds__(128) attn_decode_partial(const float* __restri
   __syncthreads();
   l = red[0] + red[1] + red[2] + red[3];
   for (int t = threadIdx.x; t < hd; t += blockDim.x) {
-    float o = 0.0f;
-    for (int j = j0; j < j1; ++j) o = __fmaf_rn(sp[j - j0], vc[static_cast<size_t>(j) * kvd + kv_h * hd + t], o);
-    pout[2 + t] = o;
+    const float* vcol = vc + static_cast<size_t>(j0) * kvd + kv_h * hd + t;
+    float o0 = 0.0f, o1 = 0.0f, o2 = 0.0f, o3 = 0.0f;
+    int j = 0;
+    for (; j + 4 <= nkeys; j += 4) {
+      const float v0 = __ldg(vcol + static_cast<size_t>(j) * kvd);
+      const float v1 = __ldg(vcol + static_cast<size_t>(j + 1) * kvd);
+      const float v2 = __ldg(vcol + static_cast<size_t>(j + 2) * kvd);
+      const float v3 = __ldg(vcol + static_cast<size_t>(j + 3) * kvd);
+      o0 = __fmaf_rn(sp[j], v0, o0);
+      o1 = __fmaf_rn(sp[j + 1], v1, o1);
+      o2 = __fmaf_rn(sp[j + 2], v2, o2);
+      o3 = __fmaf_rn(sp[j + 3], v3, o3);
+    }
+    for (; j < nkeys; ++j) o0 = __fmaf_rn(sp[j], __ldg(vcol + static_cast<size_t>(j) * kvd), o0);
+    pout[2 + t] = (o0 + o1) + (o2 + o3);
   }
   if (threadIdx.x == 0) {
     pout[0] = mx;

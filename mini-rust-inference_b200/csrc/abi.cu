@@ -57,6 +57,8 @@ int enter(mri_ctx* ctx) {
   return use_device(ctx->device);
 }
 
+int check_k(const char* fn, size_t m, size_t k, size_t k_w);
+
 // Scratch is one growing device buffer per context, carved by the callers.
 int ensure_scratch(mri_ctx* ctx, size_t bytes) {
   if (bytes <= ctx->scratch_bytes) return MRI_OK;
@@ -75,7 +77,7 @@ int ensure_scratch(mri_ctx* ctx, size_t bytes) {
 size_t al(size_t v) { return (v + 255) / 256 * 256; }
 
 // Bytes of the quantizer's maxima area at the front of scratch.
-size_t amax_bytes(size_t m) { return al(std::max(m, mri::kQuantPartials) * sizeof(float)); }
+size_t amax_bytes(size_t m) { return al(2 * std::max(m, mri::kQuantPartials) * sizeof(float)); }
 
 template <typename T>
 int upload_bytes(const T* host, size_t count, T** dev) {
@@ -109,7 +111,7 @@ namespace {
 // as the reference does) and runs the tensor-core GEMM or, where that does
 // not apply, the GEMV over 8-row chunks.
 int run_int8(mri_ctx* ctx, ActArgs act, const mri_qmatrix* w, size_t m, float* out,
-             int32_t* acc) {
+             int32_t* acc, const float* residual = nullptr) {
   const size_t N = w->n_out, K = w->k_in;
   if (m == 0 || N == 0) return MRI_OK;
   cudaStream_t st = ctx->stream;
@@ -118,7 +120,7 @@ int run_int8(mri_ctx* ctx, ActArgs act, const mri_qmatrix* w, size_t m, float* o
   const bool w_aligned = (reinterpret_cast<uintptr_t>(w->data) & 15) == 0;
   if (m <= 8 && w_aligned && mri::gemv_i8_tma_supported(ctx->dev, static_cast<int>(m), K)) {
     MRI_CUDA_TRY(mri::launch_gemv_i8_tma(ctx->dev, st, static_cast<int>(m), w->data, w->scales, N,
-                                         K, act, out, acc, ctx->d_status, &ctx->ls));
+                                         K, act, out, acc, ctx->d_status, &ctx->ls, residual));
     return MRI_OK;
   }
 
@@ -134,7 +136,7 @@ int run_int8(mri_ctx* ctx, ActArgs act, const mri_qmatrix* w, size_t m, float* o
     int8_t* q = reinterpret_cast<int8_t*>(ctx->scratch + amax_bytes(m) + al(m * sizeof(float)));
     if (f32_in) {
       MRI_CUDA_TRY(mri::launch_quantize(ctx->dev, st, act.x, m, K, per_row, q, scales, amax,
-                                        &ctx->ls));
+                                        &ctx->ls, act.norm_w, act.eps, act.swiglu));
       xq = q;
     } else {
       MRI_CUDA_TRY(cudaMemcpyAsync(scales, &act.scale_host, sizeof(float),
@@ -147,7 +149,7 @@ int run_int8(mri_ctx* ctx, ActArgs act, const mri_qmatrix* w, size_t m, float* o
   if (w_aligned && mri::gemm_i8_tc_supported(ctx->dev, m, N, K) &&
       (reinterpret_cast<uintptr_t>(xq) & 15) == 0) {
     MRI_CUDA_TRY(mri::launch_gemm_i8_tc(ctx->dev, st, xq, sdev, per_row, w->data, w->scales, m, N,
-                                        K, out, acc, ctx->d_status, &ctx->ls));
+                                        K, out, acc, ctx->d_status, &ctx->ls, residual));
     return MRI_OK;
   }
   for (size_t m0 = 0; m0 < m; m0 += 8) {
@@ -166,8 +168,28 @@ int run_int8(mri_ctx* ctx, ActArgs act, const mri_qmatrix* w, size_t m, float* o
                                                ac, &ctx->ls));
     }
   }
+  if (residual) MRI_CUDA_TRY(mri::launch_add_residual(ctx->dev, st, out, residual, m * N, &ctx->ls));
   return MRI_OK;
 }
+
+}  // namespace
+
+int mri::matmul_int8_fused(::mri_ctx* ctx, const float* x, size_t m, size_t k, const float* norm_w,
+                           float eps, int swiglu, const ::mri_qmatrix* w, const float* residual,
+                           float* out) {
+  if (int rc = enter(ctx)) return rc;
+  if (!w) return fail(MRI_ERR_INVALID_ARGUMENT, "null weight handle");
+  if (int rc = check_k("matmul_int8_fused", m, k, w->k_in)) return rc;
+  ActArgs a;
+  a.x = x;
+  a.mode = mri::ACT_F32_PER_TENSOR;
+  a.norm_w = norm_w;
+  a.eps = eps;
+  a.swiglu = swiglu;
+  return run_int8(ctx, a, w, m, out, nullptr, residual);
+}
+
+namespace {
 
 int run_q8_0(mri_ctx* ctx, const float* x, size_t m, const mri_q8_0_matrix* w, float* out) {
   const size_t N = w->n_out, K = w->k_in;

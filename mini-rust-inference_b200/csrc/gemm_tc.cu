@@ -131,8 +131,9 @@ template <int BN, int kStages>
 __global__ void __launch_bounds__(kTcThreads, 1)
     gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const float* __restrict__ act_scale, int scale_per_row,
-                      const float* __restrict__ w_scales, float* __restrict__ out,
-                      int32_t* __restrict__ acc_out, int M, int N, int K, int* status) {
+                      const float* __restrict__ w_scales, float* out,
+                      int32_t* __restrict__ acc_out, int M, int N, int K, int* status,
+                      const float* residual) {
   using L = TcLayout<BN, kStages>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_addr(smem_raw);
@@ -250,10 +251,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const int row = m_blk * BM + q * 32 + lane;
       const float s_a = scale_per_row ? (row < M ? act_scale[row] : 0.0f) : act_scale[0];
       float* orow = out + static_cast<size_t>(row) * N;
+      // forward_int8.rs:100-121: x + projected; residual may alias out.
+      const float* rrow = residual ? residual + static_cast<size_t>(row) * N : nullptr;
       int32_t* arow = acc_out ? acc_out + static_cast<size_t>(row) * N : nullptr;
       const bool vec = (N % 4) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0 &&
                        (reinterpret_cast<uintptr_t>(acc_out) & 15) == 0 &&
-                       (reinterpret_cast<uintptr_t>(w_scales) & 15) == 0;
+                       (reinterpret_cast<uintptr_t>(w_scales) & 15) == 0 &&
+                       (reinterpret_cast<uintptr_t>(residual) & 15) == 0;
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t v[32];
@@ -269,6 +273,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
               o.y = rescale(static_cast<int>(v[j + 1]), s_a, sw.y);
               o.z = rescale(static_cast<int>(v[j + 2]), s_a, sw.z);
               o.w = rescale(static_cast<int>(v[j + 3]), s_a, sw.w);
+              if (rrow) {
+                const float4 r = *reinterpret_cast<const float4*>(rrow + col0 + j);
+                o.x = __fadd_rn(r.x, o.x);
+                o.y = __fadd_rn(r.y, o.y);
+                o.z = __fadd_rn(r.z, o.z);
+                o.w = __fadd_rn(r.w, o.w);
+              }
               *reinterpret_cast<float4*>(orow + col0 + j) = o;
               if (arow)
                 *reinterpret_cast<int4*>(arow + col0 + j) =
@@ -280,7 +291,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             for (int j = 0; j < 32; ++j) {
               const int col = col0 + j;
               if (col < N) {
-                orow[col] = rescale(static_cast<int>(v[j]), s_a, __ldg(w_scales + col));
+                const float val = rescale(static_cast<int>(v[j]), s_a, __ldg(w_scales + col));
+                orow[col] = rrow ? __fadd_rn(rrow[col], val) : val;
                 if (arow) arow[col] = static_cast<int>(v[j]);
               }
             }
@@ -370,7 +382,7 @@ template <int BN, int kStages>
 cudaError_t launch_bn(const DeviceInfo& dev, cudaStream_t st, const CUtensorMap& ta,
                       const CUtensorMap& tb, const float* act_scale, int per_row,
                       const float* w_scales, size_t M, size_t N, size_t K, float* out,
-                      int32_t* acc_out, int* status) {
+                      int32_t* acc_out, int* status, const float* residual) {
   const size_t smem = TcLayout<BN, kStages>::total;
   cudaError_t e = set_smem_tc(gemm_i8_tc_kernel<BN, kStages>, smem, dev.device);
   if (e != cudaSuccess) return e;
@@ -387,7 +399,7 @@ cudaError_t launch_bn(const DeviceInfo& dev, cudaStream_t st, const CUtensorMap&
   cfg.numAttrs = pdl_enabled() ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, gemm_i8_tc_kernel<BN, kStages>, ta, tb, act_scale, per_row, w_scales,
                             out, acc_out, static_cast<int>(M), static_cast<int>(N),
-                            static_cast<int>(K), status);
+                            static_cast<int>(K), status, residual);
 }
 
 }  // namespace
@@ -402,7 +414,8 @@ bool gemm_i8_tc_supported(const DeviceInfo& dev, size_t M, size_t N, size_t K) {
 cudaError_t launch_gemm_i8_tc(const DeviceInfo& dev, cudaStream_t st, const int8_t* xq,
                               const float* act_scale_dev, int scale_per_row, const int8_t* W,
                               const float* w_scales, size_t M, size_t N, size_t K, float* out,
-                              int32_t* acc_out, int* status, LaunchStats* ls) {
+                              int32_t* acc_out, int* status, LaunchStats* ls,
+                              const float* residual) {
   if ((reinterpret_cast<uintptr_t>(xq) & 15) || (reinterpret_cast<uintptr_t>(W) & 15))
     return cudaErrorMisalignedAddress;
   const int bn = pick_bn(dev, M, N);
@@ -410,9 +423,9 @@ cudaError_t launch_gemm_i8_tc(const DeviceInfo& dev, cudaStream_t st, const int8
   if (!make_map(&ta, xq, M, K, BM) || !make_map(&tb, W, N, K, bn)) return cudaErrorInvalidValue;
   // Four 48 KB stages (BN=256) or six 32 KB stages (BN=128): 192 KB either way.
   cudaError_t e = bn == 128 ? launch_bn<128, 6>(dev, st, ta, tb, act_scale_dev, scale_per_row,
-                                                w_scales, M, N, K, out, acc_out, status)
+                                                w_scales, M, N, K, out, acc_out, status, residual)
                             : launch_bn<256, 4>(dev, st, ta, tb, act_scale_dev, scale_per_row,
-                                                w_scales, M, N, K, out, acc_out, status);
+                                                w_scales, M, N, K, out, acc_out, status, residual);
   if (ls) ls->launches++;
   return e;
 }

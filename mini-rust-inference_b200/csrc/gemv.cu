@@ -139,75 +139,172 @@ __device__ __forceinline__ float consumer_max(float v, float* red) {
   return r;
 }
 
+__device__ __forceinline__ float consumer_sum(float v, float* red) {
+  const int cw = (threadIdx.x >> 5) - 1;
+  v = warp_sum_f(v);
+  if ((threadIdx.x & 31) == 0) red[cw] = v;
+  named_bar_sync(1, kConsumerThreads);
+  float r = 0.0f;
+#pragma unroll
+  for (int i = 0; i < kConsumerWarps; ++i) r += red[i];
+  named_bar_sync(1, kConsumerThreads);
+  return r;
+}
+
+// silu(g) * u (ops/activation/swiglu.rs:39-61, silu.rs:23-26).
+__device__ __forceinline__ float swiglu1(float g, float u) {
+  return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+}
+
+// The f32 activation element the quantizer sees: x itself, its RMSNorm
+// (w[k] * (x * inv_rms[r])), or silu(gate) * up.  Four elements at a time;
+// K % 4 == 0 and 16-byte aligned rows (checked by the launcher).
+struct ActView {
+  const float* x;
+  const float* w;       // RMSNorm weight or nullptr
+  const float* inv;     // per-row 1/rms (shared memory) when w != nullptr
+  size_t K, ld;         // ld = K, or 2K for [gate | up] rows
+  int swiglu;
+
+  __device__ __forceinline__ float4 get(int r, size_t k) const {
+    const float* row = x + r * ld;
+    if (swiglu) {
+      const float4 g = __ldg(reinterpret_cast<const float4*>(row + k));
+      const float4 u = __ldg(reinterpret_cast<const float4*>(row + K + k));
+      return make_float4(swiglu1(g.x, u.x), swiglu1(g.y, u.y), swiglu1(g.z, u.z), swiglu1(g.w, u.w));
+    }
+    float4 v = __ldg(reinterpret_cast<const float4*>(row + k));
+    if (w) v = norm(v, r, k);
+    return v;
+  }
+  __device__ __forceinline__ float4 norm(float4 v, int r, size_t k) const {
+    const float4 ww = __ldg(reinterpret_cast<const float4*>(w + k));
+    const float iv = inv[r];
+    return make_float4(__fmul_rn(ww.x, __fmul_rn(v.x, iv)), __fmul_rn(ww.y, __fmul_rn(v.y, iv)),
+                       __fmul_rn(ww.z, __fmul_rn(v.z, iv)), __fmul_rn(ww.w, __fmul_rn(v.w, iv)));
+  }
+};
+
+__device__ __forceinline__ float absmax4(float m, float4 v) {
+  return absmax_acc(absmax_acc(absmax_acc(absmax_acc(m, v.x), v.y), v.z), v.w);
+}
+
+__device__ __forceinline__ char4 quant4(float4 v, float inv) {
+  char4 o;
+  o.x = sym_quant(v.x, inv);
+  o.y = sym_quant(v.y, inv);
+  o.z = sym_quant(v.z, inv);
+  o.w = sym_quant(v.w, inv);
+  return o;
+}
+
 // Quantize (or copy) the M activation rows into shared memory as int8 [M][K]
-// row-major and fill s_scale[0..M).
+// row-major and fill s_scale[0..M).  Optional fused producer ops (RMSNorm,
+// SwiGLU) are applied to the f32 values first.
 template <int M>
 __device__ void load_act_i8_rowmajor(const ActArgs& act, size_t K, int8_t* s_act, float* s_scale,
                                      float* red) {
   const int ct = threadIdx.x - 32;
   const size_t total = static_cast<size_t>(M) * K;
-  constexpr int kRegVec = 4;  // float4 per consumer thread held in registers
-  if (act.mode == ACT_F32_PER_TENSOR && (reinterpret_cast<uintptr_t>(act.x) & 15) == 0 &&
-      total % 4 == 0 && total <= static_cast<size_t>(kRegVec) * 4 * kConsumerThreads) {
-    // Small per-tensor input (decode): one global read, values kept in
-    // registers between the absmax and the quantization pass.
-    const float4* x4 = reinterpret_cast<const float4*>(act.x);
-    float4 v[kRegVec];
-    float m = 0.0f;
+  __shared__ float s_inv[8];
+  if (act.mode == ACT_F32_PER_TENSOR || act.mode == ACT_F32_PER_ROW) {
+    ActView v{act.x, act.norm_w, s_inv, K, act.swiglu ? 2 * K : K, act.swiglu};
+    constexpr int kRegVec = 4;  // float4 per consumer thread held in registers
+    const bool vec = (reinterpret_cast<uintptr_t>(act.x) & 15) == 0 && K % 4 == 0 &&
+                     (!act.norm_w || (reinterpret_cast<uintptr_t>(act.norm_w) & 15) == 0);
+    if (vec && act.mode == ACT_F32_PER_TENSOR && !act.swiglu &&
+        total <= static_cast<size_t>(kRegVec) * 4 * kConsumerThreads) {
+      // Decode-size input: one global read, values kept in registers through
+      // the RMSNorm statistics, the absmax and the quantization.
+      float4 x4[kRegVec];
 #pragma unroll
-    for (int j = 0; j < kRegVec; ++j) {
-      const size_t i = ct + static_cast<size_t>(j) * kConsumerThreads;
-      v[j] = i < total / 4 ? __ldg(x4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-      m = absmax_acc(absmax_acc(absmax_acc(absmax_acc(m, v[j].x), v[j].y), v[j].z), v[j].w);
-    }
-    const float scale = sym_scale(consumer_max(m, red));
-    const float inv = __fdiv_rn(1.0f, scale);
-    if (ct < M) s_scale[ct] = scale;
-#pragma unroll
-    for (int j = 0; j < kRegVec; ++j) {
-      const size_t i = ct + static_cast<size_t>(j) * kConsumerThreads;
-      if (i < total / 4) {
-        char4 o;
-        o.x = sym_quant(v[j].x, inv);
-        o.y = sym_quant(v[j].y, inv);
-        o.z = sym_quant(v[j].z, inv);
-        o.w = sym_quant(v[j].w, inv);
-        reinterpret_cast<char4*>(s_act)[i] = o;
+      for (int j = 0; j < kRegVec; ++j) {
+        const size_t i = ct + static_cast<size_t>(j) * kConsumerThreads;
+        x4[j] = i < total / 4 ? __ldg(reinterpret_cast<const float4*>(act.x) + i)
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
       }
-    }
-  } else if (act.mode == ACT_F32_PER_TENSOR || act.mode == ACT_F32_PER_ROW) {
-    const float* x = act.x;
-    const bool vec = (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (K % 4) == 0;
-    for (int r = 0; r < (act.mode == ACT_F32_PER_ROW ? M : 1); ++r) {
-      const size_t lo = act.mode == ACT_F32_PER_ROW ? r * K : 0;
-      const size_t hi = act.mode == ACT_F32_PER_ROW ? lo + K : total;
-      float m = 0.0f;
-      if (vec) {
-        for (size_t i = lo / 4 + ct; i < hi / 4; i += kConsumerThreads) {
-          const float4 v = __ldg(reinterpret_cast<const float4*>(x) + i);
-          m = absmax_acc(absmax_acc(absmax_acc(absmax_acc(m, v.x), v.y), v.z), v.w);
+      if (act.norm_w) {
+        for (int r = 0; r < M; ++r) {
+          float ss = 0.0f;
+#pragma unroll
+          for (int j = 0; j < kRegVec; ++j) {
+            const size_t i = ct + static_cast<size_t>(j) * kConsumerThreads;
+            if (i < total / 4 && (i * 4) / K == static_cast<size_t>(r)) {
+              ss = __fmaf_rn(x4[j].x, x4[j].x, ss);
+              ss = __fmaf_rn(x4[j].y, x4[j].y, ss);
+              ss = __fmaf_rn(x4[j].z, x4[j].z, ss);
+              ss = __fmaf_rn(x4[j].w, x4[j].w, ss);
+            }
+          }
+          ss = consumer_sum(ss, red);
+          if (ct == 0) s_inv[r] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(K)), act.eps)));
         }
-      } else {
-        for (size_t i = lo + ct; i < hi; i += kConsumerThreads) m = absmax_acc(m, __ldg(x + i));
+        named_bar_sync(1, kConsumerThreads);
+#pragma unroll
+        for (int j = 0; j < kRegVec; ++j) {
+          const size_t i = ct + static_cast<size_t>(j) * kConsumerThreads;
+          if (i < total / 4) x4[j] = v.norm(x4[j], static_cast<int>((i * 4) / K), (i * 4) % K);
+        }
       }
+      float m = 0.0f;
+#pragma unroll
+      for (int j = 0; j < kRegVec; ++j) m = absmax4(m, x4[j]);
       const float scale = sym_scale(consumer_max(m, red));
       const float inv = __fdiv_rn(1.0f, scale);
-      if (act.mode == ACT_F32_PER_ROW) {
-        if (ct == 0) s_scale[r] = scale;
-      } else if (ct < M) {
-        s_scale[ct] = scale;
+      if (ct < M) s_scale[ct] = scale;
+#pragma unroll
+      for (int j = 0; j < kRegVec; ++j) {
+        const size_t i = ct + static_cast<size_t>(j) * kConsumerThreads;
+        if (i < total / 4) reinterpret_cast<char4*>(s_act)[i] = quant4(x4[j], inv);
       }
-      if (vec) {
-        for (size_t i = lo / 4 + ct; i < hi / 4; i += kConsumerThreads) {
-          const float4 v = __ldg(reinterpret_cast<const float4*>(x) + i);
-          char4 o;
-          o.x = sym_quant(v.x, inv);
-          o.y = sym_quant(v.y, inv);
-          o.z = sym_quant(v.z, inv);
-          o.w = sym_quant(v.w, inv);
-          reinterpret_cast<char4*>(s_act)[i] = o;
+    } else if (vec) {
+      if (act.norm_w) {
+        for (int r = 0; r < M; ++r) {
+          const float* row = act.x + r * K;
+          float ss = 0.0f;
+          for (size_t i = ct; i < K / 4; i += kConsumerThreads) {
+            const float4 t = __ldg(reinterpret_cast<const float4*>(row) + i);
+            ss = __fmaf_rn(t.x, t.x, ss);
+            ss = __fmaf_rn(t.y, t.y, ss);
+            ss = __fmaf_rn(t.z, t.z, ss);
+            ss = __fmaf_rn(t.w, t.w, ss);
+          }
+          ss = consumer_sum(ss, red);
+          if (ct == 0) s_inv[r] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(K)), act.eps)));
         }
-      } else {
+        named_bar_sync(1, kConsumerThreads);
+      }
+      const bool per_row = act.mode == ACT_F32_PER_ROW;
+      for (int r = 0; r < (per_row ? M : 1); ++r) {
+        const size_t lo = per_row ? r * K / 4 : 0, hi = per_row ? (r + 1) * K / 4 : total / 4;
+        float m = 0.0f;
+        for (size_t i = lo + ct; i < hi; i += kConsumerThreads)
+          m = absmax4(m, v.get(static_cast<int>((i * 4) / K), (i * 4) % K));
+        const float scale = sym_scale(consumer_max(m, red));
+        const float inv = __fdiv_rn(1.0f, scale);
+        if (per_row) {
+          if (ct == 0) s_scale[r] = scale;
+        } else if (ct < M) {
+          s_scale[ct] = scale;
+        }
+        for (size_t i = lo + ct; i < hi; i += kConsumerThreads)
+          reinterpret_cast<char4*>(s_act)[i] = quant4(v.get(static_cast<int>((i * 4) / K), (i * 4) % K), inv);
+      }
+    } else {
+      // Scalar path (unaligned input; no fused producer ops reach here).
+      const float* x = act.x;
+      for (int r = 0; r < (act.mode == ACT_F32_PER_ROW ? M : 1); ++r) {
+        const size_t lo = act.mode == ACT_F32_PER_ROW ? r * K : 0;
+        const size_t hi = act.mode == ACT_F32_PER_ROW ? lo + K : total;
+        float m = 0.0f;
+        for (size_t i = lo + ct; i < hi; i += kConsumerThreads) m = absmax_acc(m, __ldg(x + i));
+        const float scale = sym_scale(consumer_max(m, red));
+        const float inv = __fdiv_rn(1.0f, scale);
+        if (act.mode == ACT_F32_PER_ROW) {
+          if (ct == 0) s_scale[r] = scale;
+        } else if (ct < M) {
+          s_scale[ct] = scale;
+        }
         for (size_t i = lo + ct; i < hi; i += kConsumerThreads) s_act[i] = sym_quant(__ldg(x + i), inv);
       }
     }
@@ -271,8 +368,8 @@ __device__ void stream_producer_i8(const int8_t* W, size_t K, size_t kc, int nk,
 template <int M>
 __global__ void __launch_bounds__(kThreads, 1)
     gemv_i8_tma_kernel(const int8_t* __restrict__ W, const float* __restrict__ w_scales, size_t N,
-                       size_t K, ActArgs act, float* __restrict__ out, int32_t* __restrict__ acc_out,
-                       int n_stages, int nk, int* status) {
+                       size_t K, ActArgs act, float* out, int32_t* __restrict__ acc_out,
+                       int n_stages, int nk, int* status, const float* residual) {
   extern __shared__ __align__(128) uint8_t smem[];
   const size_t kc = nk == 1 ? K : align_up((K + nk - 1) / nk, 16);
   const StreamLayout L = make_layout(M * K, 0, kRowsPerStage * kc, n_stages);
@@ -344,7 +441,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int m = 0; m < M; ++m) {
         if (lane == m) {
-          out[m * N + row] = rescale(acc[m], s_a[m], sw);
+          const float val = rescale(acc[m], s_a[m], sw);
+          // forward_int8.rs:100-121: x + projected (residual may alias out).
+          out[m * N + row] = residual ? __fadd_rn(residual[m * N + row], val) : val;
           if (acc_out) acc_out[m * N + row] = acc[m];
         }
       }
@@ -857,7 +956,8 @@ bool gemv_i8_tma_supported(const DeviceInfo&, int M, size_t K) {
 
 cudaError_t launch_gemv_i8_tma(const DeviceInfo& dev, cudaStream_t st, int M, const int8_t* W,
                                const float* w_scales, size_t N, size_t K, const ActArgs& act,
-                               float* out, int32_t* acc_out, int* status, LaunchStats* ls) {
+                               float* out, int32_t* acc_out, int* status, LaunchStats* ls,
+                               const float* residual) {
   StreamConfig cfg;
   const int nk = i8_chunks(M, K, &cfg);
   if (nk == 0) return cudaErrorInvalidValue;
@@ -869,7 +969,7 @@ cudaError_t launch_gemv_i8_tma(const DeviceInfo& dev, cudaStream_t st, int M, co
     cudaError_t e = set_smem(gemv_i8_tma_kernel<kM>, smem, dev.device);
     if (e != cudaSuccess) return e;
     e = launch_stream_kernel(gemv_i8_tma_kernel<kM>, grid, smem, st, W, w_scales, N, K, act, out,
-                             acc_out, stages, nk, status);
+                             acc_out, stages, nk, status, residual);
     if (e != cudaSuccess) return e;
   });
   if (ls) ls->launches++;

@@ -7,6 +7,7 @@
 #include <stdint.h>
 
 struct mri_ctx;
+struct mri_qmatrix;
 
 namespace mri {
 
@@ -25,6 +26,14 @@ struct ActArgs {
   const float* scale_dev = nullptr;
   float scale_host = 1.0f;
   int mode = ACT_F32_PER_TENSOR;
+  // Optional producer ops fused in front of the f32 quantization (modes 0/1):
+  //   norm_w: RMSNorm of each row (ops/norm/rmsnorm.rs:51-117) with weight
+  //           norm_w [K] and epsilon eps, before quantization;
+  //   swiglu: the input rows are [gate | up] of width 2K and the quantized
+  //           value is silu(gate) * up (ops/activation/swiglu.rs:39-61).
+  const float* norm_w = nullptr;
+  float eps = 0.0f;
+  int swiglu = 0;
 };
 
 // Kernel counts for launch accounting.
@@ -42,19 +51,27 @@ struct DeviceInfo {
 };
 
 // ── quantizer (quant.cu) ─────────────────────────────────────────────────────
-// amax_scratch: max(M, kQuantPartials) floats of device scratch (per-block
-// partial maxima for PER_TENSOR, per-row maxima for PER_ROW).
+// amax_scratch: 2 * max(M, kQuantPartials) floats of device scratch (per-block
+// partial maxima for PER_TENSOR, per-row maxima for PER_ROW, per-row 1/rms
+// when norm_w is given).
 constexpr size_t kQuantPartials = 1024;
 cudaError_t launch_quantize(const DeviceInfo& dev, cudaStream_t st, const float* x, size_t m,
                             size_t k, int per_row, int8_t* q, float* scale, float* amax_scratch,
-                            LaunchStats* ls);
+                            LaunchStats* ls, const float* norm_w = nullptr, float eps = 0.0f,
+                            int swiglu = 0);
+
+// out[i] = residual[i] + out[i] (the reference's x + projected).
+cudaError_t launch_add_residual(const DeviceInfo& dev, cudaStream_t st, float* out,
+                                const float* residual, size_t n, LaunchStats* ls);
 
 // ── streaming GEMV family (gemv.cu), M <= 8 rows of activations ─────────────
 // INT8 per-channel.  Requires K % 16 == 0 and 16-byte aligned W.
 bool gemv_i8_tma_supported(const DeviceInfo& dev, int M, size_t K);
+// residual (nullable): out = residual + product, element-wise (may alias out).
 cudaError_t launch_gemv_i8_tma(const DeviceInfo& dev, cudaStream_t st, int M, const int8_t* W,
                                const float* w_scales, size_t N, size_t K, const ActArgs& act,
-                               float* out, int32_t* acc_out, int* status, LaunchStats* ls);
+                               float* out, int32_t* acc_out, int* status, LaunchStats* ls,
+                               const float* residual = nullptr);
 // Any K, any alignment; activations must be pre-quantized (modes 2-4).
 cudaError_t launch_gemv_i8_generic(const DeviceInfo& dev, cudaStream_t st, int M, const int8_t* W,
                                    const float* w_scales, size_t N, size_t K, const ActArgs& act,
@@ -79,6 +96,13 @@ cudaError_t launch_gemv_q4_0_generic(const DeviceInfo& dev, cudaStream_t st, int
                                      const uint8_t* W, size_t N, size_t K, const float* x,
                                      float* out, LaunchStats* ls);
 
+// INT8 product of an f32 [m, k] input with per-tensor quantization and the
+// optional fused producer ops of ActArgs (RMSNorm or SwiGLU; for SwiGLU the
+// input rows are 2k wide) and residual epilogue.  Status code as the C ABI.
+int matmul_int8_fused(struct ::mri_ctx* ctx, const float* x, size_t m, size_t k,
+                      const float* norm_w, float eps, int swiglu,
+                      const struct ::mri_qmatrix* w, const float* residual, float* out);
+
 // Grows the context scratch to at least `bytes` (synchronizes the stream
 // when it reallocates).  Callers that capture CUDA graphs reserve their
 // maximum first: a captured launch keeps the scratch address it saw.
@@ -93,7 +117,8 @@ bool gemm_i8_tc_supported(const DeviceInfo& dev, size_t M, size_t N, size_t K);
 cudaError_t launch_gemm_i8_tc(const DeviceInfo& dev, cudaStream_t st, const int8_t* xq,
                               const float* act_scale_dev, int scale_per_row, const int8_t* W,
                               const float* w_scales, size_t M, size_t N, size_t K, float* out,
-                              int32_t* acc_out, int* status, LaunchStats* ls);
+                              int32_t* acc_out, int* status, LaunchStats* ls,
+                              const float* residual = nullptr);
 
 }  // namespace mri
 

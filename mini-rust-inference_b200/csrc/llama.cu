@@ -10,9 +10,11 @@
 // Q, K and V (and gate and up) weights are stored as one concatenated
 // QuantizedMatrix; since each projection quantizes the same input with the
 // same per-tensor scale, every output element is bit-identical to separate
-// calls.  The glue (RMSNorm, RoPE, attention, SwiGLU, residual adds, greedy
-// argmax) is plain CUDA; it is f32 and tolerance-checked, not bit-exact (its
-// exp/sum order differs from the reference's).
+// calls.  RMSNorm and SwiGLU run fused in front of the projection that
+// consumes them (inside the activation-quantization prologue) and the
+// residual add behind it (in the product's epilogue); RoPE, attention and the
+// greedy argmax are plain CUDA.  The glue is f32 and tolerance-checked, not
+// bit-exact (its exp/sum order differs from the reference's).
 //
 // A decode step reads the token and position from device memory, so one
 // captured CUDA graph replays every step of greedy generation.
@@ -48,56 +50,38 @@ __global__ void embed_kernel(const uint32_t* __restrict__ tokens, const float* _
   for (int i = threadIdx.x; i < d; i += blockDim.x) dst[i] = src[i];
 }
 
-// ops/norm/rmsnorm.rs:51-117: out = w * (x * (1 / sqrt(mean(x^2) + eps))).
-__global__ void __launch_bounds__(256) rmsnorm_kernel(const float* __restrict__ x,
-                                                      const float* __restrict__ w, int d, float eps,
-                                                      float* __restrict__ out) {
-  const float* xr = x + static_cast<size_t>(blockIdx.x) * d;
-  float* orow = out + static_cast<size_t>(blockIdx.x) * d;
-  float ss = 0.0f;
-  for (int i = threadIdx.x; i < d; i += blockDim.x) ss = __fmaf_rn(xr[i], xr[i], ss);
-  ss = mri::warp_sum_f(ss);
-  __shared__ float red[8];
-  __shared__ float inv;
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    float t = 0.0f;
-    for (int i = 0; i < static_cast<int>(blockDim.x >> 5); ++i) t += red[i];
-    const float mean_sq = __fdiv_rn(t, static_cast<float>(d));
-    inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean_sq, eps)));
-  }
-  __syncthreads();
-  for (int i = threadIdx.x; i < d; i += blockDim.x) orow[i] = __fmul_rn(w[i], __fmul_rn(xr[i], inv));
-}
-
 // ops/rope.rs:121-190 on q and k of the fused qkv rows, then the cache write
-// of attention/cached.rs:90-93 / :161-163 (k rotated, v as is).  Row i sits at
-// absolute position base + i, where base is *pos_dev if given, else pos0.
+// of attention/cached.rs:90-93 / :161-163 (k rotated, v as is).  Block
+// (i, h): head h of token row i at absolute position base + i, where base is
+// *pos_dev if given, else pos0; heads [0, H) are queries, [H, H+Hkv) keys
+// (whose blocks also copy the matching value head into the cache).
 __global__ void rope_kv_kernel(float* __restrict__ qkv, int ld, int n_heads, int n_kv, int hd,
                                const float* __restrict__ cos_t, const float* __restrict__ sin_t,
                                int pos0, const int* __restrict__ pos_dev, float* __restrict__ kc,
                                float* __restrict__ vc) {
-  const int i = blockIdx.x;
+  const int i = blockIdx.x, h = blockIdx.y;
   const int pos = (pos_dev ? *pos_dev : pos0) + i;
   const int half = hd / 2;
   float* row = qkv + static_cast<size_t>(i) * ld;
-  const int kvd = n_kv * hd;
-  const int qd = n_heads * hd;
-  for (int p = threadIdx.x; p < (n_heads + n_kv) * half; p += blockDim.x) {
-    const int h = p / half, j = p % half;
-    float* base = h < n_heads ? row + h * hd : row + qd + (h - n_heads) * hd;
+  const int kvd = n_kv * hd, qd = n_heads * hd;
+  float* base = h < n_heads ? row + h * hd : row + qd + (h - n_heads) * hd;
+  for (int j = threadIdx.x; j < half; j += blockDim.x) {
     const float c = cos_t[pos * half + j], sn = sin_t[pos * half + j];
     const float x0 = base[2 * j], x1 = base[2 * j + 1];
-    base[2 * j] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
-    base[2 * j + 1] = __fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, sn));
-  }
-  __syncthreads();
-  float* krow = kc + static_cast<size_t>(pos) * kvd;
-  float* vrow = vc + static_cast<size_t>(pos) * kvd;
-  for (int t = threadIdx.x; t < kvd; t += blockDim.x) {
-    krow[t] = row[qd + t];
-    vrow[t] = row[qd + kvd + t];
+    const float y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
+    const float y1 = __fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, sn));
+    base[2 * j] = y0;
+    base[2 * j + 1] = y1;
+    if (h >= n_heads) {
+      const int kh = h - n_heads;
+      float* krow = kc + static_cast<size_t>(pos) * kvd + kh * hd;
+      float* vrow = vc + static_cast<size_t>(pos) * kvd + kh * hd;
+      const float* vsrc = row + qd + kvd + kh * hd;
+      krow[2 * j] = y0;
+      krow[2 * j + 1] = y1;
+      vrow[2 * j] = vsrc[2 * j];
+      vrow[2 * j + 1] = vsrc[2 * j + 1];
+    }
   }
 }
 
@@ -316,24 +300,6 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(const float* __restri
   }
 }
 
-// ops/activation/swiglu.rs:39-61: h = silu(gate) * up, silu(g) = g / (1 + exp(-g)).
-__global__ void swiglu_kernel(const float* __restrict__ gu, int ffn, int M, float* __restrict__ hout) {
-  const size_t n = static_cast<size_t>(M) * ffn;
-  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
-       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
-    const size_t r = i / ffn, c = i % ffn;
-    const float g = gu[r * 2 * ffn + c], u = gu[r * 2 * ffn + ffn + c];
-    hout[i] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
-  }
-}
-
-// forward_int8.rs:100-121: x = x + y.
-__global__ void add_kernel(float* __restrict__ x, const float* __restrict__ y, size_t n) {
-  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
-       i += static_cast<size_t>(gridDim.x) * blockDim.x)
-    x[i] = __fadd_rn(x[i], y[i]);
-}
-
 // Greedy sampling: argmax (first index on ties) -> next token; position += 1.
 __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ logits, int V,
                                                       uint32_t* __restrict__ token,
@@ -423,10 +389,6 @@ int fail(int code, const char* fmt, ...) {
     if (_rc != MRI_OK) return fail(_rc, "%s", mri_last_error()); \
   } while (0)
 
-int grid_for(size_t n, int threads, int sms) {
-  return static_cast<int>(std::max<size_t>(1, std::min<size_t>((n + threads - 1) / threads, sms * 16)));
-}
-
 }  // namespace
 
 struct mri_llama {
@@ -447,8 +409,8 @@ struct mri_llama {
   float* rope_sin = nullptr;
   // cache and activations
   float *kc = nullptr, *vc = nullptr;
-  float *x = nullptr, *xn = nullptr, *qkv = nullptr, *attn = nullptr, *tmp = nullptr;
-  float *gu = nullptr, *h = nullptr, *logits = nullptr, *part = nullptr;
+  float *x = nullptr, *qkv = nullptr, *attn = nullptr, *gu = nullptr;
+  float *logits = nullptr, *part = nullptr;
   uint32_t* d_tokens = nullptr;
   uint32_t* d_gen = nullptr;  // [max_seq + 1] tokens produced by greedy argmax
   int* d_pos = nullptr;
@@ -495,30 +457,34 @@ BlobLayout blob_layout(const mri_llama* m) {
   return b;
 }
 
-// One INT8 projection with per-tensor quantization of x [m, k].
-int proj(mri_llama* m, const float* x, size_t rows, const mri_qmatrix& w, float* out) {
-  LL_RC(mri_matmul_int8_from_f32(m->ctx, x, rows, w.k_in, &w, out));
+// One INT8 projection with per-tensor quantization of x [rows, k], with the
+// producer op fused in front (RMSNorm weight `norm`, or SwiGLU over [gate|up]
+// rows) and the residual add fused behind (out = residual + product).
+int proj(mri_llama* m, const float* x, size_t rows, const mri_qmatrix& w, float* out,
+         const float* norm = nullptr, int swiglu = 0, const float* residual = nullptr) {
+  LL_RC(mri::matmul_int8_fused(m->ctx, x, rows, w.k_in, norm, m->cfg.rms_eps, swiglu, &w, residual,
+                               out));
   return MRI_OK;
 }
 
-// Runs the blocks and the final norm for `rows` tokens already embedded in
-// m->x, at absolute positions [pos0, pos0+rows) (or *d_pos when decode_dev).
+// Runs the blocks for `rows` tokens already embedded in m->x, at absolute
+// positions [pos0, pos0+rows) (or *d_pos when decode_dev).  Per block:
+//   qkv = proj(rmsnorm(x, attn_norm))        (forward_int8.rs:361-372)
+//   rope + cache write; attention
+//   x   = x + proj(attn, wo)                 (:374-393)
+//   x   = x + proj(swiglu(proj(rmsnorm(x, ffn_norm), wgu)), wdown)  (:395-402)
 int run_blocks(mri_llama* m, size_t rows, int pos0, bool decode_dev) {
   const auto& c = m->cfg;
   cudaStream_t st = m->ctx->stream;
-  const int sms = m->ctx->dev.sm_count;
   const float scale = 1.0f / std::sqrt(static_cast<float>(m->hd));
   const size_t layer_kv = static_cast<size_t>(c.max_seq) * m->kvd;
   for (uint32_t l = 0; l < c.n_layers; ++l) {
     float* kc = m->kc + l * layer_kv;
     float* vc = m->vc + l * layer_kv;
-    rmsnorm_kernel<<<static_cast<unsigned>(rows), 256, 0, st>>>(m->x, m->attn_norm + l * c.dim, c.dim,
-                                                                c.rms_eps, m->xn);
-    if (int rc = proj(m, m->xn, rows, m->wqkv[l], m->qkv)) return rc;
-    rope_kv_kernel<<<static_cast<unsigned>(rows), 128, 0, st>>>(m->qkv, m->qkv_w, c.n_heads,
-                                                                c.n_kv_heads, m->hd, m->rope_cos,
-                                                                m->rope_sin, pos0,
-                                                                decode_dev ? m->d_pos : nullptr, kc, vc);
+    if (int rc = proj(m, m->x, rows, m->wqkv[l], m->qkv, m->attn_norm + l * c.dim)) return rc;
+    rope_kv_kernel<<<dim3(static_cast<unsigned>(rows), c.n_heads + c.n_kv_heads), 64, 0, st>>>(
+        m->qkv, m->qkv_w, c.n_heads, c.n_kv_heads, m->hd, m->rope_cos, m->rope_sin, pos0,
+        decode_dev ? m->d_pos : nullptr, kc, vc);
     if (decode_dev) {
       attn_decode_partial<<<dim3(c.n_heads, m->max_splits), 128, 0, st>>>(
           m->qkv, c.n_heads, c.n_kv_heads, m->hd, kc, vc, m->d_pos, scale, m->part, m->max_splits);
@@ -538,25 +504,18 @@ int run_blocks(mri_llama* m, size_t rows, int pos0, bool decode_dev) {
                                              static_cast<int>(rows), pos0, kc, vc, scale, m->attn,
                                              m->qd);
     }
-    if (int rc = proj(m, m->attn, rows, m->wo[l], m->tmp)) return rc;
-    add_kernel<<<grid_for(rows * c.dim, 256, sms), 256, 0, st>>>(m->x, m->tmp, rows * c.dim);
-    rmsnorm_kernel<<<static_cast<unsigned>(rows), 256, 0, st>>>(m->x, m->ffn_norm + l * c.dim, c.dim,
-                                                                c.rms_eps, m->xn);
-    if (int rc = proj(m, m->xn, rows, m->wgu[l], m->gu)) return rc;
-    swiglu_kernel<<<grid_for(rows * c.ffn_dim, 256, sms), 256, 0, st>>>(m->gu, c.ffn_dim,
-                                                                        static_cast<int>(rows), m->h);
-    if (int rc = proj(m, m->h, rows, m->wdown[l], m->tmp)) return rc;
-    add_kernel<<<grid_for(rows * c.dim, 256, sms), 256, 0, st>>>(m->x, m->tmp, rows * c.dim);
+    if (int rc = proj(m, m->attn, rows, m->wo[l], m->x, nullptr, 0, m->x)) return rc;
+    if (int rc = proj(m, m->x, rows, m->wgu[l], m->gu, m->ffn_norm + l * c.dim)) return rc;
+    if (int rc = proj(m, m->gu, rows, m->wdown[l], m->x, nullptr, 1, m->x)) return rc;
   }
-  rmsnorm_kernel<<<static_cast<unsigned>(rows), 256, 0, st>>>(m->x, m->out_norm, c.dim, c.rms_eps,
-                                                              m->xn);
   LL_TRY(cudaGetLastError());
   return MRI_OK;
 }
 
-// Logits for rows [first, first+count) of m->xn into m->logits.
+// Logits for rows [first, first+count) of m->x: output RMSNorm fused into the
+// LM-head projection (forward_int8.rs:526-528).
 int lm_head(mri_llama* m, size_t first, size_t count) {
-  return proj(m, m->xn + first * m->cfg.dim, count, m->wout, m->logits);
+  return proj(m, m->x + first * m->cfg.dim, count, m->wout, m->logits, m->out_norm);
 }
 
 int check_tokens(const mri_llama* m, const uint32_t* tokens, size_t n) {
@@ -666,12 +625,9 @@ int mri_llama_create(mri_ctx* ctx, const mri_llama_config* cfg, mri_llama** out)
   rc = rc ? rc : dalloc(m, &m->kc, static_cast<size_t>(c.n_layers) * c.max_seq * m->kvd);
   rc = rc ? rc : dalloc(m, &m->vc, static_cast<size_t>(c.n_layers) * c.max_seq * m->kvd);
   rc = rc ? rc : dalloc(m, &m->x, T * c.dim);
-  rc = rc ? rc : dalloc(m, &m->xn, T * c.dim);
   rc = rc ? rc : dalloc(m, &m->qkv, T * m->qkv_w);
   rc = rc ? rc : dalloc(m, &m->attn, T * m->qd);
-  rc = rc ? rc : dalloc(m, &m->tmp, T * c.dim);
   rc = rc ? rc : dalloc(m, &m->gu, T * 2 * c.ffn_dim);
-  rc = rc ? rc : dalloc(m, &m->h, T * c.ffn_dim);
   rc = rc ? rc : dalloc(m, &m->logits, T * c.vocab);
   rc = rc ? rc : dalloc(m, &m->part, static_cast<size_t>(c.n_heads) * m->max_splits * (kMaxHeadDim + 2));
   rc = rc ? rc : dalloc(m, &m->d_tokens, T);

@@ -117,12 +117,118 @@ __global__ void __launch_bounds__(kQThreads) quant_apply_kernel(const float* __r
   }
 }
 
+// Fused producer ops (RMSNorm or SwiGLU) in front of the quantizer.  Pass 1,
+// one block per row: 1/rms of the row (RMSNorm) into row_inv[r] and the
+// absmax of the row's transformed values into partial[r].
+__device__ __forceinline__ float xform(const float* __restrict__ x, size_t k, size_t K, int r,
+                                       const float* __restrict__ norm_w, float inv_r, int swiglu) {
+  if (swiglu) {
+    const float g = __ldg(x + static_cast<size_t>(r) * 2 * K + k);
+    const float u = __ldg(x + static_cast<size_t>(r) * 2 * K + K + k);
+    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+  }
+  const float v = __ldg(x + static_cast<size_t>(r) * K + k);
+  return norm_w ? __fmul_rn(__ldg(norm_w + k), __fmul_rn(v, inv_r)) : v;
+}
+
+__global__ void __launch_bounds__(kQThreads) row_stats_kernel(const float* __restrict__ x, size_t K,
+                                                              const float* __restrict__ norm_w,
+                                                              float eps, int swiglu,
+                                                              float* __restrict__ row_inv,
+                                                              float* __restrict__ partial) {
+  const int r = blockIdx.x;
+  __shared__ float red[kQThreads / 32];
+  __shared__ float inv_s;
+  float inv_r = 1.0f;
+  if (norm_w) {
+    float ss = 0.0f;
+    for (size_t k = threadIdx.x; k < K; k += kQThreads) {
+      const float v = __ldg(x + static_cast<size_t>(r) * K + k);
+      ss = __fmaf_rn(v, v, ss);
+    }
+    ss = warp_sum_f(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float t = 0.0f;
+      for (int i = 0; i < kQThreads / 32; ++i) t += red[i];
+      inv_s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, static_cast<float>(K)), eps)));
+      row_inv[r] = inv_s;
+    }
+    __syncthreads();
+    inv_r = inv_s;
+  }
+  float m = 0.0f;
+  for (size_t k = threadIdx.x; k < K; k += kQThreads) m = absmax_acc(m, xform(x, k, K, r, norm_w, inv_r, swiglu));
+  m = warp_max(m);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.0f;
+    for (int i = 0; i < kQThreads / 32; ++i) t = fmaxf(t, red[i]);
+    partial[r] = t;
+  }
+}
+
+// Pass 2: per-tensor (or per-row) scale from the row maxima, quantize the
+// transformed values.
+__global__ void __launch_bounds__(kQThreads) quant_apply_xform_kernel(
+    const float* __restrict__ x, size_t m, size_t K, int per_row, const float* __restrict__ partial,
+    const float* __restrict__ norm_w, const float* __restrict__ row_inv, int swiglu,
+    int8_t* __restrict__ q, float* __restrict__ scale_out) {
+  const size_t n = m * K;
+  const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+  const size_t tid = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  float inv_t = 0.0f;
+  if (!per_row) {
+    const float scale = sym_scale(reduce_partials(partial, static_cast<int>(m)));
+    inv_t = __fdiv_rn(1.0f, scale);
+    if (tid == 0) scale_out[0] = scale;
+  } else {
+    for (size_t r = tid; r < m; r += stride) scale_out[r] = sym_scale(partial[r]);
+  }
+  for (size_t j = tid; j < n; j += stride) {
+    const int r = static_cast<int>(j / K);
+    const size_t k = j % K;
+    const float inv = per_row ? __fdiv_rn(1.0f, sym_scale(partial[r])) : inv_t;
+    q[j] = sym_quant(xform(x, k, K, r, norm_w, norm_w ? row_inv[r] : 1.0f, swiglu), inv);
+  }
+}
+
+__global__ void add_inplace_kernel(float* __restrict__ out, const float* __restrict__ res, size_t n) {
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x)
+    out[i] = __fadd_rn(res[i], out[i]);
+}
+
 }  // namespace
+
+cudaError_t launch_add_residual(const DeviceInfo& dev, cudaStream_t st, float* out,
+                                const float* residual, size_t n, LaunchStats* ls) {
+  const int blocks = static_cast<int>(std::max<size_t>(1, std::min<size_t>(dev.sm_count * 8, (n + 255) / 256)));
+  add_inplace_kernel<<<blocks, 256, 0, st>>>(out, residual, n);
+  if (ls) ls->launches++;
+  return cudaGetLastError();
+}
 
 cudaError_t launch_quantize(const DeviceInfo& dev, cudaStream_t st, const float* x, size_t m,
                             size_t k, int per_row, int8_t* q, float* scale, float* amax_scratch,
-                            LaunchStats* ls) {
+                            LaunchStats* ls, const float* norm_w, float eps, int swiglu) {
   const size_t n = m * k;
+  if ((norm_w || swiglu) && n > 0) {
+    // amax_scratch holds 2 * max(m, kQuantPartials) floats: row maxima, then 1/rms.
+    float* partial = amax_scratch;
+    float* row_inv = amax_scratch + std::max(m, kQuantPartials);
+    row_stats_kernel<<<static_cast<unsigned>(m), kQThreads, 0, st>>>(x, k, norm_w, eps, swiglu, row_inv,
+                                                                    partial);
+    const int apply_blocks = static_cast<int>(std::max<size_t>(
+        1, std::min<size_t>(static_cast<size_t>(dev.sm_count) * 8, (n + kQThreads * 4 - 1) / (kQThreads * 4))));
+    quant_apply_xform_kernel<<<apply_blocks, kQThreads, 0, st>>>(x, m, k, per_row, partial, norm_w,
+                                                                 row_inv, swiglu, q, scale);
+    if (ls) ls->launches += 2;
+    return cudaGetLastError();
+  }
   if (n == 0) {
     // Empty input: the reference's fold yields 0 -> scale 1.0.
     if (!per_row) {

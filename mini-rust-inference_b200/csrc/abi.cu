@@ -110,19 +110,25 @@ namespace {
 // streaming GEMV; larger m quantizes once (per-tensor scale over all rows,
 // as the reference does) and runs the tensor-core GEMM or, where that does
 // not apply, the GEMV over 8-row chunks.
+bool stream_gemv_applies(const mri_ctx* ctx, size_t m, const mri_qmatrix* w) {
+  return m >= 1 && m <= 8 && (reinterpret_cast<uintptr_t>(w->data) & 15) == 0 &&
+         mri::gemv_i8_tma_supported(ctx->dev, static_cast<int>(m), w->k_in);
+}
+
 int run_int8(mri_ctx* ctx, ActArgs act, const mri_qmatrix* w, size_t m, float* out,
-             int32_t* acc, const float* residual = nullptr) {
+             int32_t* acc, const float* residual = nullptr, const mri::EpiArgs* epi = nullptr) {
   const size_t N = w->n_out, K = w->k_in;
   if (m == 0 || N == 0) return MRI_OK;
   cudaStream_t st = ctx->stream;
   const bool f32_in = act.mode == mri::ACT_F32_PER_TENSOR || act.mode == mri::ACT_F32_PER_ROW;
 
   const bool w_aligned = (reinterpret_cast<uintptr_t>(w->data) & 15) == 0;
-  if (m <= 8 && w_aligned && mri::gemv_i8_tma_supported(ctx->dev, static_cast<int>(m), K)) {
+  if (stream_gemv_applies(ctx, m, w)) {
     MRI_CUDA_TRY(mri::launch_gemv_i8_tma(ctx->dev, st, static_cast<int>(m), w->data, w->scales, N,
-                                         K, act, out, acc, ctx->d_status, &ctx->ls, residual));
+                                         K, act, out, acc, ctx->d_status, &ctx->ls, residual, epi));
     return MRI_OK;
   }
+  if (epi) return fail(MRI_ERR_INVALID_ARGUMENT, "pair epilogue needs the streaming GEMV path (m <= 8, K %% 16 == 0)");
 
   // Materialize quantized activations (and device scales) if needed.
   const int8_t* xq = act.xq;
@@ -174,9 +180,13 @@ int run_int8(mri_ctx* ctx, ActArgs act, const mri_qmatrix* w, size_t m, float* o
 
 }  // namespace
 
+bool mri::matmul_int8_epilogue_supported(const ::mri_ctx* ctx, size_t m, const ::mri_qmatrix* w) {
+  return ctx && w && w->n_out % 2 == 0 && stream_gemv_applies(ctx, m, w);
+}
+
 int mri::matmul_int8_fused(::mri_ctx* ctx, const float* x, size_t m, size_t k, const float* norm_w,
                            float eps, int swiglu, const ::mri_qmatrix* w, const float* residual,
-                           float* out) {
+                           float* out, const EpiArgs* epi) {
   if (int rc = enter(ctx)) return rc;
   if (!w) return fail(MRI_ERR_INVALID_ARGUMENT, "null weight handle");
   if (int rc = check_k("matmul_int8_fused", m, k, w->k_in)) return rc;
@@ -186,7 +196,8 @@ int mri::matmul_int8_fused(::mri_ctx* ctx, const float* x, size_t m, size_t k, c
   a.norm_w = norm_w;
   a.eps = eps;
   a.swiglu = swiglu;
-  return run_int8(ctx, a, w, m, out, nullptr, residual);
+  if (epi && (residual || w->n_out % 2)) return fail(MRI_ERR_INVALID_ARGUMENT, "pair epilogue needs even N and no residual");
+  return run_int8(ctx, a, w, m, out, nullptr, residual, epi);
 }
 
 namespace {

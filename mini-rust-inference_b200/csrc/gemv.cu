@@ -22,6 +22,7 @@
 #include <cstdlib>
 #include <map>
 #include <mutex>
+#include <tuple>
 #include <utility>
 
 #include "common.cuh"
@@ -163,15 +164,15 @@ struct ActView {
   const float* x;
   const float* w;       // RMSNorm weight or nullptr
   const float* inv;     // per-row 1/rms (shared memory) when w != nullptr
-  size_t K, ld;         // ld = K, or 2K for [gate | up] rows
+  size_t K, ld;         // ld = K, or 2K for interleaved gate/up rows
   int swiglu;
 
   __device__ __forceinline__ float4 get(int r, size_t k) const {
     const float* row = x + r * ld;
     if (swiglu) {
-      const float4 g = __ldg(reinterpret_cast<const float4*>(row + k));
-      const float4 u = __ldg(reinterpret_cast<const float4*>(row + K + k));
-      return make_float4(swiglu1(g.x, u.x), swiglu1(g.y, u.y), swiglu1(g.z, u.z), swiglu1(g.w, u.w));
+      const float4 a = __ldg(reinterpret_cast<const float4*>(row + 2 * k));
+      const float4 b = __ldg(reinterpret_cast<const float4*>(row + 2 * k + 4));
+      return make_float4(swiglu1(a.x, a.y), swiglu1(a.z, a.w), swiglu1(b.x, b.y), swiglu1(b.z, b.w));
     }
     float4 v = __ldg(reinterpret_cast<const float4*>(row + k));
     if (w) v = norm(v, r, k);
@@ -209,7 +210,7 @@ __device__ void load_act_i8_rowmajor(const ActArgs& act, size_t K, int8_t* s_act
   __shared__ float s_inv[8];
   if (act.mode == ACT_F32_PER_TENSOR || act.mode == ACT_F32_PER_ROW) {
     ActView v{act.x, act.norm_w, s_inv, K, act.swiglu ? 2 * K : K, act.swiglu};
-    constexpr int kRegVec = 4;  // float4 per consumer thread held in registers
+    constexpr int kRegVec = 12;  // float4 per consumer thread held in registers (K <= 12288 at M=1)
     const bool vec = (reinterpret_cast<uintptr_t>(act.x) & 15) == 0 && K % 4 == 0 &&
                      (!act.norm_w || (reinterpret_cast<uintptr_t>(act.norm_w) & 15) == 0);
     if (vec && act.mode == ACT_F32_PER_TENSOR && !act.swiglu &&
@@ -217,19 +218,19 @@ __device__ void load_act_i8_rowmajor(const ActArgs& act, size_t K, int8_t* s_act
       // Decode-size input: one global read, values kept in registers through
       // the RMSNorm statistics, the absmax and the quantization.
       float4 x4[kRegVec];
+      const int n4 = static_cast<int>(total / 4), K32 = static_cast<int>(K);
 #pragma unroll
       for (int j = 0; j < kRegVec; ++j) {
-        const size_t i = ct + static_cast<size_t>(j) * kConsumerThreads;
-        x4[j] = i < total / 4 ? __ldg(reinterpret_cast<const float4*>(act.x) + i)
-                              : make_float4(0.f, 0.f, 0.f, 0.f);
+        const int i = ct + j * kConsumerThreads;
+        x4[j] = i < n4 ? __ldg(reinterpret_cast<const float4*>(act.x) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
       }
       if (act.norm_w) {
         for (int r = 0; r < M; ++r) {
           float ss = 0.0f;
 #pragma unroll
           for (int j = 0; j < kRegVec; ++j) {
-            const size_t i = ct + static_cast<size_t>(j) * kConsumerThreads;
-            if (i < total / 4 && (i * 4) / K == static_cast<size_t>(r)) {
+            const int i = ct + j * kConsumerThreads;
+            if (i < n4 && (M == 1 || (i * 4) / K32 == r)) {
               ss = __fmaf_rn(x4[j].x, x4[j].x, ss);
               ss = __fmaf_rn(x4[j].y, x4[j].y, ss);
               ss = __fmaf_rn(x4[j].z, x4[j].z, ss);
@@ -242,8 +243,8 @@ __device__ void load_act_i8_rowmajor(const ActArgs& act, size_t K, int8_t* s_act
         named_bar_sync(1, kConsumerThreads);
 #pragma unroll
         for (int j = 0; j < kRegVec; ++j) {
-          const size_t i = ct + static_cast<size_t>(j) * kConsumerThreads;
-          if (i < total / 4) x4[j] = v.norm(x4[j], static_cast<int>((i * 4) / K), (i * 4) % K);
+          const int i = ct + j * kConsumerThreads;
+          if (i < n4) x4[j] = v.norm(x4[j], M == 1 ? 0 : (i * 4) / K32, M == 1 ? i * 4 : (i * 4) % K32);
         }
       }
       float m = 0.0f;
@@ -254,8 +255,8 @@ __device__ void load_act_i8_rowmajor(const ActArgs& act, size_t K, int8_t* s_act
       if (ct < M) s_scale[ct] = scale;
 #pragma unroll
       for (int j = 0; j < kRegVec; ++j) {
-        const size_t i = ct + static_cast<size_t>(j) * kConsumerThreads;
-        if (i < total / 4) reinterpret_cast<char4*>(s_act)[i] = quant4(x4[j], inv);
+        const int i = ct + j * kConsumerThreads;
+        if (i < n4) reinterpret_cast<char4*>(s_act)[i] = quant4(x4[j], inv);
       }
     } else if (vec) {
       if (act.norm_w) {
@@ -365,12 +366,46 @@ __device__ void stream_producer_i8(const int8_t* W, size_t K, size_t kc, int nk,
     mbar_wait(&full[it % n_stages], (it / n_stages) & 1, status);
 }
 
+// Pair epilogue (EpiArgs): the warps of rows 2i and 2i+1 swap their values
+// through shared memory (double-buffered by group parity, one 64-thread named
+// barrier per warp pair and group) and combine them.
+__device__ __forceinline__ void pair_epilogue(const EpiArgs& epi, int M, size_t N, size_t row,
+                                              bool valid, float val, int lane, int cw, int g,
+                                              float (*s_pair)[kConsumerWarps][8], float* out) {
+  if (lane < M) s_pair[g & 1][cw][lane] = val;
+  named_bar_sync(2 + (cw >> 1), 64);
+  if (!valid || lane >= M) return;
+  const float other = s_pair[g & 1][cw ^ 1][lane];
+  const int m = lane;
+  if (epi.mode == EPI_SWIGLU) {
+    // silu(gate) * up (ops/activation/swiglu.rs:39-61, silu.rs:23-26)
+    if ((row & 1) == 0) out[m * (N / 2) + row / 2] = swiglu1(val, other);
+    return;
+  }
+  const int r = static_cast<int>(row);
+  const int pos = (epi.pos_dev ? *epi.pos_dev : epi.pos0) + m;
+  const int qk = epi.qd + epi.kvd;
+  float y = val;
+  if (r < qk) {
+    // ops/rope.rs:121-190: (x0, x1) -> (x0 c - x1 s, x1 c + x0 s), pair j of the head.
+    const int half = epi.hd / 2;
+    const int j = (r % epi.hd) >> 1;
+    const float c = __ldg(epi.cos_t + pos * half + j), sn = __ldg(epi.sin_t + pos * half + j);
+    y = (r & 1) == 0 ? __fsub_rn(__fmul_rn(val, c), __fmul_rn(other, sn))
+                     : __fadd_rn(__fmul_rn(val, c), __fmul_rn(other, sn));
+  }
+  out[m * N + row] = y;
+  if (r >= epi.qd && r < qk) epi.kc[static_cast<size_t>(pos) * epi.kvd + (r - epi.qd)] = y;
+  else if (r >= qk) epi.vc[static_cast<size_t>(pos) * epi.kvd + (r - qk)] = y;
+}
+
 template <int M>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, M <= 2 ? 2 : 1)
     gemv_i8_tma_kernel(const int8_t* __restrict__ W, const float* __restrict__ w_scales, size_t N,
                        size_t K, ActArgs act, float* out, int32_t* __restrict__ acc_out,
-                       int n_stages, int nk, int* status, const float* residual) {
+                       int n_stages, int nk, int* status, const float* residual, EpiArgs epi) {
   extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ float s_pair[2][kConsumerWarps][8];
   const size_t kc = nk == 1 ? K : align_up((K + nk - 1) / nk, 16);
   const StreamLayout L = make_layout(M * K, 0, kRowsPerStage * kc, n_stages);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
@@ -381,7 +416,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* stage0 = smem + L.stage;
 
   size_t begin, end;
-  cta_rows(N, 1, begin, end);
+  // Pair epilogues need both rows of a pair in the same CTA and stage.
+  cta_rows(N, epi.mode != EPI_NONE ? 2 : 1, begin, end);
   init_barriers(full, empty, n_stages);
   if (begin >= end) return;
 
@@ -403,6 +439,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   // The per-row weight scale is loaded one group ahead so its global-load
   // latency overlaps the stage waits and the dot products.
   float sw_next = begin + cw < end ? __ldg(w_scales + begin + cw) : 0.0f;
+  // After a stage wait gives up (status set), the warp still walks the loop
+  // without waiting or computing, so every warp reaches the same barriers.
+  bool ok = true;
   int it = 0;
   for (int g = 0; g < groups; ++g) {
     const size_t row = begin + static_cast<size_t>(g) * kRowsPerStage + cw;
@@ -413,8 +452,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int m = 0; m < M; ++m) acc[m] = 0;
     for (int c = 0; c < nk; ++c, ++it) {
       const int s = it % n_stages;
-      if (!mbar_wait(&full[s], (it / n_stages) & 1, status)) return;
-      if (row < end) {
+      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&full[s], (it / n_stages) & 1, status));
+      if (ok && row < end) {
         const size_t k0 = static_cast<size_t>(c) * kc;
         const int chunks = static_cast<int>(std::min(kc, K - k0) / 16);
         const uint4* wrow = reinterpret_cast<const uint4*>(stage0 + s * L.stage_bytes + cw * kc);
@@ -433,19 +472,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
+      if (ok && lane == 0) mbar_arrive(&empty[s]);
     }
-    if (row < end) {
+    const bool valid = ok && row < end;
+    float val = 0.0f;
+    if (valid) {
 #pragma unroll
       for (int m = 0; m < M; ++m) acc[m] = warp_sum_i(acc[m]);
 #pragma unroll
-      for (int m = 0; m < M; ++m) {
-        if (lane == m) {
-          const float val = rescale(acc[m], s_a[m], sw);
-          // forward_int8.rs:100-121: x + projected (residual may alias out).
-          out[m * N + row] = residual ? __fadd_rn(residual[m * N + row], val) : val;
-          if (acc_out) acc_out[m * N + row] = acc[m];
-        }
+      for (int m = 0; m < M; ++m)
+        if (lane == m) val = rescale(acc[m], s_a[m], sw);
+    }
+    if (epi.mode != EPI_NONE) {
+      pair_epilogue(epi, M, N, row, valid, val, lane, cw, g, s_pair, out);
+    } else if (valid && lane < M) {
+      // forward_int8.rs:100-121: x + projected (residual may alias out).
+      out[lane * N + row] = residual ? __fadd_rn(residual[lane * N + row], val) : val;
+      if (acc_out) {
+#pragma unroll
+        for (int m = 0; m < M; ++m)
+          if (lane == m) acc_out[m * N + row] = acc[m];
       }
     }
   }
@@ -516,7 +562,7 @@ __device__ __forceinline__ void load_q8_block(const uint8_t* blk, uint32_t& dbit
 __host__ __device__ constexpr size_t q8_term_stride(size_t nb) { return align_up(nb, 4) + 4; }
 
 template <int M>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, M <= 2 ? 2 : 1)
     gemv_q8_0_tma_kernel(const uint8_t* __restrict__ W, size_t N, size_t K,
                          const float* __restrict__ x, float* __restrict__ out, int n_stages,
                          int* status) {
@@ -684,7 +730,7 @@ __device__ __forceinline__ float nib_minus8(uint32_t v, uint32_t byte_idx) {
 }
 
 template <int M>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, M <= 2 ? 2 : 1)
     gemv_q4_0_tma_kernel(const uint8_t* __restrict__ W, size_t N, size_t K,
                          const float* __restrict__ x, float* __restrict__ out, int n_stages,
                          int* status) {
@@ -902,6 +948,27 @@ int stream_grid(const DeviceInfo& dev, size_t units, int ctas_per_sm) {
       std::max<size_t>(1, std::min<size_t>(static_cast<size_t>(dev.sm_count) * ctas_per_sm, units)));
 }
 
+// CTAs of `k` that fit on one SM with `smem` dynamic bytes (registers and
+// shared memory), cached per (kernel, device, smem).  The persistent grid is
+// never sized above it: a second wave would double the kernel's time.
+template <typename KernelT>
+int resident_ctas(KernelT k, size_t smem, int device) {
+  static std::mutex mu;
+  static std::map<std::tuple<const void*, int, size_t>, int> done;
+  std::lock_guard<std::mutex> lock(mu);
+  const auto key = std::make_tuple(reinterpret_cast<const void*>(k), device, smem);
+  auto it = done.find(key);
+  if (it != done.end()) return it->second;
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, kThreads, smem) != cudaSuccess) {
+    cudaGetLastError();
+    n = 1;
+  }
+  n = std::max(1, n);
+  done[key] = n;
+  return n;
+}
+
 // Launch with the programmatic-stream-serialization attribute when enabled.
 template <typename... KArgs, typename... Args>
 cudaError_t launch_stream_kernel(void (*k)(KArgs...), int grid, size_t smem, cudaStream_t st,
@@ -957,19 +1024,25 @@ bool gemv_i8_tma_supported(const DeviceInfo&, int M, size_t K) {
 cudaError_t launch_gemv_i8_tma(const DeviceInfo& dev, cudaStream_t st, int M, const int8_t* W,
                                const float* w_scales, size_t N, size_t K, const ActArgs& act,
                                float* out, int32_t* acc_out, int* status, LaunchStats* ls,
-                               const float* residual) {
+                               const float* residual, const EpiArgs* epi) {
   StreamConfig cfg;
   const int nk = i8_chunks(M, K, &cfg);
+  EpiArgs e_args;
+  if (epi) {
+    if (N % 2 || residual || acc_out) return cudaErrorInvalidValue;
+    e_args = *epi;
+  }
   if (nk == 0) return cudaErrorInvalidValue;
   const size_t kc = nk == 1 ? K : align_up((K + nk - 1) / nk, 16);
   const int stages = cfg.stages;
   const size_t smem = make_layout(M * K, 0, kRowsPerStage * kc, stages).total;
-  const int grid = stream_grid(dev, N, cfg.ctas_per_sm);
   MRI_DISPATCH_M(M, {
     cudaError_t e = set_smem(gemv_i8_tma_kernel<kM>, smem, dev.device);
     if (e != cudaSuccess) return e;
+    const int grid = stream_grid(
+        dev, N, std::min(cfg.ctas_per_sm, resident_ctas(gemv_i8_tma_kernel<kM>, smem, dev.device)));
     e = launch_stream_kernel(gemv_i8_tma_kernel<kM>, grid, smem, st, W, w_scales, N, K, act, out,
-                             acc_out, stages, nk, status, residual);
+                             acc_out, stages, nk, status, residual, e_args);
     if (e != cudaSuccess) return e;
   });
   if (ls) ls->launches++;
@@ -1003,10 +1076,11 @@ cudaError_t launch_gemv_q8_0_tma(const DeviceInfo& dev, cudaStream_t st, int M, 
   const int stages = cfg.stages;
   if (stages < 2) return cudaErrorInvalidValue;
   const size_t smem = make_layout(M * K, extra, kRowsPerStage * nb * 34, stages).total;
-  const int grid = stream_grid(dev, N, cfg.ctas_per_sm);
   MRI_DISPATCH_M(M, {
     cudaError_t e = set_smem(gemv_q8_0_tma_kernel<kM>, smem, dev.device);
     if (e != cudaSuccess) return e;
+    const int grid = stream_grid(
+        dev, N, std::min(cfg.ctas_per_sm, resident_ctas(gemv_q8_0_tma_kernel<kM>, smem, dev.device)));
     e = launch_stream_kernel(gemv_q8_0_tma_kernel<kM>, grid, smem, st, W, N, K, x, out, stages,
                              status);
     if (e != cudaSuccess) return e;
@@ -1039,10 +1113,11 @@ cudaError_t launch_gemv_q4_0_tma(const DeviceInfo& dev, cudaStream_t st, int M, 
   const int stages = cfg.stages;
   if (stages < 2) return cudaErrorInvalidValue;
   const size_t smem = make_layout(M * K * 4, 0, stage_bytes, stages).total;
-  const int grid = stream_grid(dev, N, cfg.ctas_per_sm);
   MRI_DISPATCH_M(M, {
     cudaError_t e = set_smem(gemv_q4_0_tma_kernel<kM>, smem, dev.device);
     if (e != cudaSuccess) return e;
+    const int grid = stream_grid(
+        dev, N, std::min(cfg.ctas_per_sm, resident_ctas(gemv_q4_0_tma_kernel<kM>, smem, dev.device)));
     e = launch_stream_kernel(gemv_q4_0_tma_kernel<kM>, grid, smem, st, W, N, K, x, out, stages,
                              status);
     if (e != cudaSuccess) return e;

@@ -29,11 +29,37 @@ struct ActArgs {
   // Optional producer ops fused in front of the f32 quantization (modes 0/1):
   //   norm_w: RMSNorm of each row (ops/norm/rmsnorm.rs:51-117) with weight
   //           norm_w [K] and epsilon eps, before quantization;
-  //   swiglu: the input rows are [gate | up] of width 2K and the quantized
-  //           value is silu(gate) * up (ops/activation/swiglu.rs:39-61).
+  //   swiglu: the input rows are 2K wide with gate and up interleaved
+  //           (element k: gate at 2k, up at 2k+1) and the quantized value is
+  //           silu(gate) * up (ops/activation/swiglu.rs:39-61).
   const float* norm_w = nullptr;
   float eps = 0.0f;
   int swiglu = 0;
+};
+
+// Optional epilogues of the streaming INT8 GEMV that combine adjacent output
+// rows (2i, 2i+1) of the same activation row.  Both need N even.
+enum EpiMode : int {
+  EPI_NONE = 0,
+  // out[m, i] = silu(y[m, 2i]) * y[m, 2i+1]  (gate/up rows interleaved; out
+  // is [M, N/2]; ops/activation/swiglu.rs:39-61).
+  EPI_SWIGLU = 1,
+  // Fused QKV rows [q (qd) | k (kvd) | v (kvd)]: q and k rotated in adjacent
+  // pairs at position pos + m (ops/rope.rs:121-190; pos = *pos_dev when given,
+  // else pos0), written to out; rotated k and plain v also written to the
+  // cache rows kc/vc [pos + m] (attention/cached.rs:90-93).
+  EPI_ROPE_KV = 2,
+};
+
+struct EpiArgs {
+  int mode = EPI_NONE;
+  const int* pos_dev = nullptr;
+  int pos0 = 0;
+  const float* cos_t = nullptr;  // [max_seq, hd/2]
+  const float* sin_t = nullptr;
+  int hd = 0, qd = 0, kvd = 0;
+  float* kc = nullptr;  // [max_seq, kvd]
+  float* vc = nullptr;
 };
 
 // Kernel counts for launch accounting.
@@ -68,10 +94,11 @@ cudaError_t launch_add_residual(const DeviceInfo& dev, cudaStream_t st, float* o
 // INT8 per-channel.  Requires K % 16 == 0 and 16-byte aligned W.
 bool gemv_i8_tma_supported(const DeviceInfo& dev, int M, size_t K);
 // residual (nullable): out = residual + product, element-wise (may alias out).
+// epi (nullable): a pair epilogue (EpiArgs); not combined with residual or acc_out.
 cudaError_t launch_gemv_i8_tma(const DeviceInfo& dev, cudaStream_t st, int M, const int8_t* W,
                                const float* w_scales, size_t N, size_t K, const ActArgs& act,
                                float* out, int32_t* acc_out, int* status, LaunchStats* ls,
-                               const float* residual = nullptr);
+                               const float* residual = nullptr, const EpiArgs* epi = nullptr);
 // Any K, any alignment; activations must be pre-quantized (modes 2-4).
 cudaError_t launch_gemv_i8_generic(const DeviceInfo& dev, cudaStream_t st, int M, const int8_t* W,
                                    const float* w_scales, size_t N, size_t K, const ActArgs& act,
@@ -98,10 +125,15 @@ cudaError_t launch_gemv_q4_0_generic(const DeviceInfo& dev, cudaStream_t st, int
 
 // INT8 product of an f32 [m, k] input with per-tensor quantization and the
 // optional fused producer ops of ActArgs (RMSNorm or SwiGLU; for SwiGLU the
-// input rows are 2k wide) and residual epilogue.  Status code as the C ABI.
+// input rows are 2k wide) and residual epilogue.  `epi` (nullable) selects a
+// pair epilogue; it is only available on the streaming GEMV path
+// (matmul_int8_epilogue_supported).  Status code as the C ABI.
 int matmul_int8_fused(struct ::mri_ctx* ctx, const float* x, size_t m, size_t k,
                       const float* norm_w, float eps, int swiglu,
-                      const struct ::mri_qmatrix* w, const float* residual, float* out);
+                      const struct ::mri_qmatrix* w, const float* residual, float* out,
+                      const EpiArgs* epi = nullptr);
+bool matmul_int8_epilogue_supported(const struct ::mri_ctx* ctx, size_t m,
+                                    const struct ::mri_qmatrix* w);
 
 // Grows the context scratch to at least `bytes` (synchronizes the stream
 // when it reallocates).  Callers that capture CUDA graphs reserve their

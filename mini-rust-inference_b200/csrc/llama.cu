@@ -23,7 +23,9 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdarg>
+#include <utility>
 #include <cstdio>
+#include <cstring>
 #include <string>
 #include <vector>
 
@@ -39,11 +41,20 @@ constexpr int kPrefillKT = 64;   // keys per shared-memory tile in prefill atten
 constexpr int kMaxHeadDim = 128;
 
 // ── glue kernels ─────────────────────────────────────────────────────────────
+// The decode-step kernels are launched with programmatic dependent launch:
+// each lets its successor be scheduled early (pdl_trigger) and touches memory
+// only after griddepcontrol.wait, which returns once the predecessor grid has
+// completed and its writes are visible.
+
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 // forward_int8.rs:125-140 (row copy); token ids are validated on the host for
 // host-supplied tokens and are < vocab by construction for argmax outputs.
 __global__ void embed_kernel(const uint32_t* __restrict__ tokens, const float* __restrict__ embd,
                              int d, float* __restrict__ x) {
+  pdl_trigger();
+  pdl_wait();
   const uint32_t tok = tokens[blockIdx.x];
   const float* src = embd + static_cast<size_t>(tok) * d;
   float* dst = x + static_cast<size_t>(blockIdx.x) * d;
@@ -59,6 +70,8 @@ __global__ void rope_kv_kernel(float* __restrict__ qkv, int ld, int n_heads, int
                                const float* __restrict__ cos_t, const float* __restrict__ sin_t,
                                int pos0, const int* __restrict__ pos_dev, float* __restrict__ kc,
                                float* __restrict__ vc) {
+  pdl_trigger();
+  pdl_wait();
   const int i = blockIdx.x, h = blockIdx.y;
   const int pos = (pos_dev ? *pos_dev : pos0) + i;
   const int half = hd / 2;
@@ -86,127 +99,129 @@ __global__ void rope_kv_kernel(float* __restrict__ qkv, int ld, int n_heads, int
 }
 
 // Decode attention, split over keys (attention/cached.rs:141-190 with
-// gqa.rs:217-237): block (h, s) handles keys [s*64, min(s*64+64, pos+1)) and
-// writes its running max, exp-sum and weighted V sum.  Two threads per key
-// each load half of the key row (16 float4 loads in flight per thread), so
-// the score pass is bandwidth- rather than latency-bound.
-__global__ void __launch_bounds__(128) attn_decode_partial(const float* __restrict__ q, int n_heads,
-                                                           int n_kv, int hd,
-                                                           const float* __restrict__ kc,
-                                                           const float* __restrict__ vc,
-                                                           const int* __restrict__ pos_dev, float scale,
-                                                           float* __restrict__ part, int max_splits) {
+// gqa.rs:217-237): block (h, s) handles keys [s*64, min(s*64+64, pos+1)).
+// Every thread issues its V-tile loads and its K loads (two threads per key,
+// half a row each) before using any of them, so the block waits for memory
+// about once.  Each block writes its max, exp-sum and weighted V sum; the
+// last block of a head to finish (ticket counter) merges the head's splits
+// and resets the counter for the next launch.  hd % 8 == 0, hd <= 128.
+__global__ void __launch_bounds__(128) attn_decode_kernel(const float* __restrict__ q, int n_heads,
+                                                          int n_kv, int hd,
+                                                          const float* __restrict__ kc,
+                                                          const float* __restrict__ vc,
+                                                          const int* __restrict__ pos_dev, float scale,
+                                                          float* __restrict__ part, int max_splits,
+                                                          int* __restrict__ tickets,
+                                                          float* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   const int h = blockIdx.x, s = blockIdx.y;
   const int pos = *pos_dev;
   const int j0 = s * kAttnChunk;
-  float* pout = part + (static_cast<size_t>(h) * max_splits + s) * (kMaxHeadDim + 2);
-  if (j0 > pos) {
-    if (threadIdx.x == 0) {
-      pout[0] = -INFINITY;
-      pout[1] = 0.0f;
-    }
-    return;
-  }
+  if (j0 > pos) return;
+  const int active = pos / kAttnChunk + 1;
   const int nkeys = min(kAttnChunk, pos + 1 - j0);
   const int kv_h = h / (n_heads / n_kv);
   const int kvd = n_kv * hd;
+  constexpr int kStride = kMaxHeadDim + 2;
   __shared__ __align__(16) float sq[kMaxHeadDim];
+  __shared__ __align__(16) float sv[kAttnChunk * kMaxHeadDim];
   __shared__ float sp[kAttnChunk];
   __shared__ float red[4];
+  __shared__ int last;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int hd4 = hd / 4;
+  const float* kbase = kc + static_cast<size_t>(j0) * kvd + kv_h * hd;
+  const float* vbase = vc + static_cast<size_t>(j0) * kvd + kv_h * hd;
+  constexpr int kV4 = kAttnChunk * kMaxHeadDim / 4 / 128;  // float4 of the V tile per thread
+  float4 v4[kV4];
+#pragma unroll
+  for (int i = 0; i < kV4; ++i) {
+    const int idx = threadIdx.x + 128 * i;
+    const int j = idx / hd4, d4 = idx - j * hd4;
+    v4[i] = j < nkeys ? __ldg(reinterpret_cast<const float4*>(vbase + static_cast<size_t>(j) * kvd) + d4)
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  const int jk = threadIdx.x >> 1, half = threadIdx.x & 1;
+  const int hh4 = hd4 / 2;
+  float4 k4[kMaxHeadDim / 8];
+#pragma unroll
+  for (int i = 0; i < kMaxHeadDim / 8; ++i)
+    k4[i] = (jk < nkeys && i < hh4)
+                ? __ldg(reinterpret_cast<const float4*>(kbase + static_cast<size_t>(jk) * kvd) + half * hh4 + i)
+                : make_float4(0.f, 0.f, 0.f, 0.f);
   for (int t = threadIdx.x; t < hd; t += blockDim.x) sq[t] = q[h * hd + t];
   __syncthreads();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  {
-    // thread pair (2j, 2j+1) -> key j; each thread covers hd/2 dims.
-    const int j = threadIdx.x >> 1, half = threadIdx.x & 1;
-    const int hh = hd / 2;
-    float dot = 0.0f;
-    if (j < nkeys) {
-      const float* krow = kc + static_cast<size_t>(j0 + j) * kvd + kv_h * hd + half * hh;
-      if ((hh & 3) == 0) {
-        const float4* k4 = reinterpret_cast<const float4*>(krow);
-        const float4* q4 = reinterpret_cast<const float4*>(sq + half * hh);
-        float4 kv[kMaxHeadDim / 8];
+  float dot = 0.0f;
 #pragma unroll
-        for (int i = 0; i < kMaxHeadDim / 8; ++i)
-          if (i < hh / 4) kv[i] = __ldg(k4 + i);
-#pragma unroll
-        for (int i = 0; i < kMaxHeadDim / 8; ++i)
-          if (i < hh / 4) {
-            const float4 qq = q4[i];
-            dot = __fmaf_rn(qq.x, kv[i].x, dot);
-            dot = __fmaf_rn(qq.y, kv[i].y, dot);
-            dot = __fmaf_rn(qq.z, kv[i].z, dot);
-            dot = __fmaf_rn(qq.w, kv[i].w, dot);
-          }
-      } else {
-        for (int i = 0; i < hh; ++i) dot = __fmaf_rn(sq[half * hh + i], krow[i], dot);
-      }
+  for (int i = 0; i < kMaxHeadDim / 8; ++i) {
+    if (i < hh4) {
+      const float4 qq = reinterpret_cast<const float4*>(sq)[half * hh4 + i];
+      dot = __fmaf_rn(qq.x, k4[i].x, dot);
+      dot = __fmaf_rn(qq.y, k4[i].y, dot);
+      dot = __fmaf_rn(qq.z, k4[i].z, dot);
+      dot = __fmaf_rn(qq.w, k4[i].w, dot);
     }
-    dot += __shfl_xor_sync(0xffffffffu, dot, 1);
-    if (half == 0 && j < nkeys) sp[j] = __fmul_rn(dot, scale);
   }
+  dot += __shfl_xor_sync(0xffffffffu, dot, 1);
+  if (half == 0 && jk < nkeys) sp[jk] = __fmul_rn(dot, scale);
+#pragma unroll
+  for (int i = 0; i < kV4; ++i) reinterpret_cast<float4*>(sv)[threadIdx.x + 128 * i] = v4[i];
   __syncthreads();
   float mx = -INFINITY;
-  for (int j = threadIdx.x; j < nkeys; j += blockDim.x) mx = fmaxf(mx, sp[j]);
+  for (int t = threadIdx.x; t < nkeys; t += blockDim.x) mx = fmaxf(mx, sp[t]);
   mx = mri::warp_max(mx);
   if (lane == 0) red[warp] = mx;
   __syncthreads();
   mx = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
   __syncthreads();
   float l = 0.0f;
-  for (int j = threadIdx.x; j < nkeys; j += blockDim.x) {
-    const float p = expf(sp[j] - mx);
-    sp[j] = p;
+  for (int t = threadIdx.x; t < nkeys; t += blockDim.x) {
+    const float p = expf(sp[t] - mx);
+    sp[t] = p;
     l += p;
   }
   l = mri::warp_sum_f(l);
   if (lane == 0) red[warp] = l;
   __syncthreads();
   l = red[0] + red[1] + red[2] + red[3];
+  float* pout = part + (static_cast<size_t>(h) * max_splits + s) * kStride;
   for (int t = threadIdx.x; t < hd; t += blockDim.x) {
-    const float* vcol = vc + static_cast<size_t>(j0) * kvd + kv_h * hd + t;
     float o0 = 0.0f, o1 = 0.0f, o2 = 0.0f, o3 = 0.0f;
     int j = 0;
     for (; j + 4 <= nkeys; j += 4) {
-      const float v0 = __ldg(vcol + static_cast<size_t>(j) * kvd);
-      const float v1 = __ldg(vcol + static_cast<size_t>(j + 1) * kvd);
-      const float v2 = __ldg(vcol + static_cast<size_t>(j + 2) * kvd);
-      const float v3 = __ldg(vcol + static_cast<size_t>(j + 3) * kvd);
-      o0 = __fmaf_rn(sp[j], v0, o0);
-      o1 = __fmaf_rn(sp[j + 1], v1, o1);
-      o2 = __fmaf_rn(sp[j + 2], v2, o2);
-      o3 = __fmaf_rn(sp[j + 3], v3, o3);
+      o0 = __fmaf_rn(sp[j], sv[j * hd + t], o0);
+      o1 = __fmaf_rn(sp[j + 1], sv[(j + 1) * hd + t], o1);
+      o2 = __fmaf_rn(sp[j + 2], sv[(j + 2) * hd + t], o2);
+      o3 = __fmaf_rn(sp[j + 3], sv[(j + 3) * hd + t], o3);
     }
-    for (; j < nkeys; ++j) o0 = __fmaf_rn(sp[j], __ldg(vcol + static_cast<size_t>(j) * kvd), o0);
+    for (; j < nkeys; ++j) o0 = __fmaf_rn(sp[j], sv[j * hd + t], o0);
     pout[2 + t] = (o0 + o1) + (o2 + o3);
   }
   if (threadIdx.x == 0) {
     pout[0] = mx;
     pout[1] = l;
   }
-}
-
-__global__ void __launch_bounds__(128) attn_decode_combine(const float* __restrict__ part, int hd,
-                                                           int max_splits, float* __restrict__ out) {
-  const int h = blockIdx.x;
-  const float* p = part + static_cast<size_t>(h) * max_splits * (kMaxHeadDim + 2);
-  float mx = -INFINITY;
-  for (int s = 0; s < max_splits; ++s) mx = fmaxf(mx, p[s * (kMaxHeadDim + 2)]);
-  float l = 0.0f;
-  for (int s = 0; s < max_splits; ++s) {
-    const float ms = p[s * (kMaxHeadDim + 2)];
-    if (ms != -INFINITY) l += p[s * (kMaxHeadDim + 2) + 1] * expf(ms - mx);
-  }
-  const float inv = __fdiv_rn(1.0f, l);
-  for (int t = threadIdx.x; t < hd; t += blockDim.x) {
+  // Publish this split, then take a ticket; the last split of the head merges.
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) last = atomicAdd(&tickets[h], 1) == active - 1;
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  const float* ph = part + static_cast<size_t>(h) * max_splits * kStride;
+  float gm = -INFINITY;
+  for (int t = 0; t < active; ++t) gm = fmaxf(gm, __ldcg(ph + t * kStride));
+  float gl = 0.0f;
+  for (int t = 0; t < active; ++t) gl += __ldcg(ph + t * kStride + 1) * expf(__ldcg(ph + t * kStride) - gm);
+  const float inv = __fdiv_rn(1.0f, gl);
+  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
     float o = 0.0f;
-    for (int s = 0; s < max_splits; ++s) {
-      const float ms = p[s * (kMaxHeadDim + 2)];
-      if (ms != -INFINITY) o += p[s * (kMaxHeadDim + 2) + 2 + t] * expf(ms - mx);
-    }
-    out[h * hd + t] = o * inv;
+    for (int t = 0; t < active; ++t)
+      o += __ldcg(ph + t * kStride + 2 + d) * expf(__ldcg(ph + t * kStride) - gm);
+    out[h * hd + d] = o * inv;
   }
+  if (threadIdx.x == 0) tickets[h] = 0;
 }
 
 // Prefill attention (gqa.rs:217-237 with mask.rs:77-115): block (h, qb)
@@ -300,45 +315,72 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(const float* __restri
   }
 }
 
-// Greedy sampling: argmax (first index on ties) -> next token; position += 1.
-__global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ logits, int V,
-                                                      uint32_t* __restrict__ token,
-                                                      int* __restrict__ pos,
-                                                      uint32_t* __restrict__ gen) {
-  float best = -INFINITY;
-  int idx = 0x7fffffff;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
-    const float v = logits[i];
-    if (v > best || (v == best && i < idx)) {
-      best = v;
-      idx = i;
-    }
+// Greedy sampling: argmax (first index on ties; NaN never wins) -> next
+// token; position += 1.  Block b reduces a slice of the logits into
+// part[b]; the last block to finish (ticket) reduces the partials, writes the
+// token to *token and gen[*pos + 1], advances *pos and resets the ticket.
+constexpr int kArgmaxBlocks = 32;
+
+__device__ __forceinline__ void better(float& best, int& idx, float v, int i) {
+  if (v > best || (v == best && i < idx)) {
+    best = v;
+    idx = i;
   }
+}
+
+__device__ __forceinline__ void block_argmax(float& best, int& idx, float* sb, int* si) {
   for (int o = 16; o > 0; o >>= 1) {
     const float ob = __shfl_xor_sync(0xffffffffu, best, o);
     const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
-    if (ob > best || (ob == best && oi < idx)) {
-      best = ob;
-      idx = oi;
-    }
+    better(best, idx, ob, oi);
   }
-  __shared__ float sb[32];
-  __shared__ int si[32];
   if ((threadIdx.x & 31) == 0) {
     sb[threadIdx.x >> 5] = best;
     si[threadIdx.x >> 5] = idx;
   }
   __syncthreads();
+  if (threadIdx.x == 0)
+    for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) better(best, idx, sb[w], si[w]);
+}
+
+__global__ void __launch_bounds__(256) argmax_kernel(const float* __restrict__ logits, int V,
+                                                     float* __restrict__ part_v,
+                                                     int* __restrict__ part_i, int* __restrict__ ticket,
+                                                     uint32_t* __restrict__ token,
+                                                     int* __restrict__ pos,
+                                                     uint32_t* __restrict__ gen) {
+  pdl_trigger();
+  pdl_wait();
+  __shared__ float sb[8];
+  __shared__ int si[8];
+  __shared__ int last;
+  const int per = (V + gridDim.x - 1) / gridDim.x;
+  const int lo = blockIdx.x * per, hi = min(V, lo + per);
+  float best = -INFINITY;
+  int idx = 0x7fffffff;
+  for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) better(best, idx, logits[i], i);
+  block_argmax(best, idx, sb, si);
   if (threadIdx.x == 0) {
-    for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w)
-      if (sb[w] > best || (sb[w] == best && si[w] < idx)) {
-        best = sb[w];
-        idx = si[w];
-      }
+    part_v[blockIdx.x] = best;
+    part_i[blockIdx.x] = idx;
+    __threadfence();
+    last = atomicAdd(ticket, 1) == static_cast<int>(gridDim.x) - 1;
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  best = -INFINITY;
+  idx = 0x7fffffff;
+  for (int b = threadIdx.x; b < static_cast<int>(gridDim.x); b += blockDim.x)
+    better(best, idx, __ldcg(part_v + b), __ldcg(part_i + b));
+  __syncthreads();
+  block_argmax(best, idx, sb, si);
+  if (threadIdx.x == 0) {
     const uint32_t t = static_cast<uint32_t>(idx == 0x7fffffff ? 0 : idx);
     *token = t;
     gen[*pos + 1] = t;  // the token generated for position pos + 1
     *pos += 1;
+    *ticket = 0;
   }
 }
 
@@ -411,6 +453,10 @@ struct mri_llama {
   float *kc = nullptr, *vc = nullptr;
   float *x = nullptr, *qkv = nullptr, *attn = nullptr, *gu = nullptr;
   float *logits = nullptr, *part = nullptr;
+  int* tickets = nullptr;      // [n_heads] decode-attention split counters, then 1 argmax counter
+  float* amax_v = nullptr;     // argmax partials
+  int* amax_i = nullptr;
+  bool fused_decode = false;   // decode projections carry the RoPE/KV and SwiGLU epilogues
   uint32_t* d_tokens = nullptr;
   uint32_t* d_gen = nullptr;  // [max_seq + 1] tokens produced by greedy argmax
   int* d_pos = nullptr;
@@ -457,13 +503,30 @@ BlobLayout blob_layout(const mri_llama* m) {
   return b;
 }
 
+// Launch with programmatic stream serialization (see the glue-kernel note).
+template <typename... KArgs, typename... Args>
+cudaError_t pdl_launch(void (*k)(KArgs...), dim3 grid, dim3 block, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k, static_cast<KArgs>(args)...);
+}
+
 // One INT8 projection with per-tensor quantization of x [rows, k], with the
 // producer op fused in front (RMSNorm weight `norm`, or SwiGLU over [gate|up]
 // rows) and the residual add fused behind (out = residual + product).
 int proj(mri_llama* m, const float* x, size_t rows, const mri_qmatrix& w, float* out,
-         const float* norm = nullptr, int swiglu = 0, const float* residual = nullptr) {
+         const float* norm = nullptr, int swiglu = 0, const float* residual = nullptr,
+         const mri::EpiArgs* epi = nullptr) {
   LL_RC(mri::matmul_int8_fused(m->ctx, x, rows, w.k_in, norm, m->cfg.rms_eps, swiglu, &w, residual,
-                               out));
+                               out, epi));
   return MRI_OK;
 }
 
@@ -473,22 +536,40 @@ int proj(mri_llama* m, const float* x, size_t rows, const mri_qmatrix& w, float*
 //   rope + cache write; attention
 //   x   = x + proj(attn, wo)                 (:374-393)
 //   x   = x + proj(swiglu(proj(rmsnorm(x, ffn_norm), wgu)), wdown)  (:395-402)
+// The gate/up rows of wgu are interleaved.  In the fused decode step the RoPE
+// rotation, the cache write and the SwiGLU run in the projections' epilogues.
 int run_blocks(mri_llama* m, size_t rows, int pos0, bool decode_dev) {
   const auto& c = m->cfg;
   cudaStream_t st = m->ctx->stream;
   const float scale = 1.0f / std::sqrt(static_cast<float>(m->hd));
   const size_t layer_kv = static_cast<size_t>(c.max_seq) * m->kvd;
+  const bool fused = decode_dev && m->fused_decode;
   for (uint32_t l = 0; l < c.n_layers; ++l) {
     float* kc = m->kc + l * layer_kv;
     float* vc = m->vc + l * layer_kv;
-    if (int rc = proj(m, m->x, rows, m->wqkv[l], m->qkv, m->attn_norm + l * c.dim)) return rc;
-    rope_kv_kernel<<<dim3(static_cast<unsigned>(rows), c.n_heads + c.n_kv_heads), 64, 0, st>>>(
-        m->qkv, m->qkv_w, c.n_heads, c.n_kv_heads, m->hd, m->rope_cos, m->rope_sin, pos0,
-        decode_dev ? m->d_pos : nullptr, kc, vc);
+    if (fused) {
+      mri::EpiArgs e;
+      e.mode = mri::EPI_ROPE_KV;
+      e.pos_dev = m->d_pos;
+      e.cos_t = m->rope_cos;
+      e.sin_t = m->rope_sin;
+      e.hd = m->hd;
+      e.qd = m->qd;
+      e.kvd = m->kvd;
+      e.kc = kc;
+      e.vc = vc;
+      if (int rc = proj(m, m->x, rows, m->wqkv[l], m->qkv, m->attn_norm + l * c.dim, 0, nullptr, &e))
+        return rc;
+    } else {
+      if (int rc = proj(m, m->x, rows, m->wqkv[l], m->qkv, m->attn_norm + l * c.dim)) return rc;
+      LL_TRY(pdl_launch(rope_kv_kernel, dim3(static_cast<unsigned>(rows), c.n_heads + c.n_kv_heads),
+                        dim3(64), st, m->qkv, m->qkv_w, c.n_heads, c.n_kv_heads, m->hd, m->rope_cos,
+                        m->rope_sin, pos0, decode_dev ? m->d_pos : nullptr, kc, vc));
+    }
     if (decode_dev) {
-      attn_decode_partial<<<dim3(c.n_heads, m->max_splits), 128, 0, st>>>(
-          m->qkv, c.n_heads, c.n_kv_heads, m->hd, kc, vc, m->d_pos, scale, m->part, m->max_splits);
-      attn_decode_combine<<<c.n_heads, 128, 0, st>>>(m->part, m->hd, m->max_splits, m->attn);
+      LL_TRY(pdl_launch(attn_decode_kernel, dim3(c.n_heads, m->max_splits), dim3(128), st, m->qkv,
+                        c.n_heads, c.n_kv_heads, m->hd, kc, vc, m->d_pos, scale, m->part,
+                        m->max_splits, m->tickets, m->attn));
     } else {
       const size_t smem = (kPrefillKT * (kMaxHeadDim + 1) + kPrefillKT * kMaxHeadDim +
                            kPrefillQ * kMaxHeadDim) * sizeof(float);
@@ -505,8 +586,15 @@ int run_blocks(mri_llama* m, size_t rows, int pos0, bool decode_dev) {
                                              m->qd);
     }
     if (int rc = proj(m, m->attn, rows, m->wo[l], m->x, nullptr, 0, m->x)) return rc;
-    if (int rc = proj(m, m->x, rows, m->wgu[l], m->gu, m->ffn_norm + l * c.dim)) return rc;
-    if (int rc = proj(m, m->gu, rows, m->wdown[l], m->x, nullptr, 1, m->x)) return rc;
+    if (fused) {
+      mri::EpiArgs e;
+      e.mode = mri::EPI_SWIGLU;
+      if (int rc = proj(m, m->x, rows, m->wgu[l], m->gu, m->ffn_norm + l * c.dim, 0, nullptr, &e)) return rc;
+      if (int rc = proj(m, m->gu, rows, m->wdown[l], m->x, nullptr, 0, m->x)) return rc;
+    } else {
+      if (int rc = proj(m, m->x, rows, m->wgu[l], m->gu, m->ffn_norm + l * c.dim)) return rc;
+      if (int rc = proj(m, m->gu, rows, m->wdown[l], m->x, nullptr, 1, m->x)) return rc;
+    }
   }
   LL_TRY(cudaGetLastError());
   return MRI_OK;
@@ -536,16 +624,21 @@ int prefill(mri_llama* m, const uint32_t* tokens, size_t n) {
   return run_blocks(m, n, 0, false);
 }
 
+int launch_argmax(mri_llama* m) {
+  LL_TRY(pdl_launch(argmax_kernel, dim3(kArgmaxBlocks), dim3(256), m->ctx->stream, m->logits,
+                    static_cast<int>(m->cfg.vocab), m->amax_v, m->amax_i, m->tickets + m->cfg.n_heads,
+                    m->d_tokens, m->d_pos, m->d_gen));
+  return MRI_OK;
+}
+
 // One decode step entirely on the device: token from d_tokens[0], position
 // from *d_pos; ends with argmax -> d_tokens[0] and *d_pos += 1.
 int decode_step(mri_llama* m) {
   cudaStream_t st = m->ctx->stream;
-  embed_kernel<<<1, 256, 0, st>>>(m->d_tokens, m->embd, m->cfg.dim, m->x);
+  LL_TRY(pdl_launch(embed_kernel, dim3(1), dim3(256), st, m->d_tokens, m->embd, m->cfg.dim, m->x));
   if (int rc = run_blocks(m, 1, 0, true)) return rc;
   if (int rc = lm_head(m, 0, 1)) return rc;
-  argmax_kernel<<<1, 1024, 0, st>>>(m->logits, m->cfg.vocab, m->d_tokens, m->d_pos, m->d_gen);
-  LL_TRY(cudaGetLastError());
-  return MRI_OK;
+  return launch_argmax(m);
 }
 
 int ensure_decode_graph(mri_llama* m) {
@@ -592,8 +685,8 @@ int mri_llama_create(mri_ctx* ctx, const mri_llama_config* cfg, mri_llama** out)
   if (c.dim % c.n_heads || c.n_heads % n_kv)
     return fail(MRI_ERR_INVALID_SHAPE, "dim %% n_heads and n_heads %% n_kv_heads must be 0");
   const int hd = static_cast<int>(c.dim / c.n_heads);
-  if (hd % 2 || hd > kMaxHeadDim)
-    return fail(MRI_ERR_INVALID_SHAPE, "head_dim=%d must be even and <= %d", hd, kMaxHeadDim);
+  if (hd % 8 || hd > kMaxHeadDim)
+    return fail(MRI_ERR_INVALID_SHAPE, "head_dim=%d must be a multiple of 8 and <= %d", hd, kMaxHeadDim);
   cudaSetDevice(ctx->device);
   mri_llama* m = new mri_llama();
   // A private context on the caller's stream: its scratch is the model's own,
@@ -633,6 +726,9 @@ int mri_llama_create(mri_ctx* ctx, const mri_llama_config* cfg, mri_llama** out)
   rc = rc ? rc : dalloc(m, &m->d_tokens, T);
   rc = rc ? rc : dalloc(m, &m->d_gen, T + 1);
   rc = rc ? rc : dalloc(m, &m->d_pos, 1);
+  rc = rc ? rc : dalloc(m, &m->tickets, c.n_heads + 1);
+  rc = rc ? rc : dalloc(m, &m->amax_v, kArgmaxBlocks);
+  rc = rc ? rc : dalloc(m, &m->amax_i, kArgmaxBlocks);
   if (rc != MRI_OK) {
     mri_llama_free(m);
     return rc;
@@ -644,6 +740,7 @@ int mri_llama_create(mri_ctx* ctx, const mri_llama_config* cfg, mri_llama** out)
     mri_llama_free(m);
     return fail(r, "scratch reservation: %s", mri_last_error());
   }
+  cudaMemset(m->tickets, 0, (c.n_heads + 1) * sizeof(int));
   cudaMemset(m->kc, 0, static_cast<size_t>(c.n_layers) * c.max_seq * m->kvd * sizeof(float));
   cudaMemset(m->vc, 0, static_cast<size_t>(c.n_layers) * c.max_seq * m->kvd * sizeof(float));
   // Carve the blobs into QuantizedMatrix views, each starting 256-byte
@@ -662,6 +759,9 @@ int mri_llama_create(mri_ctx* ctx, const mri_llama_config* cfg, mri_llama** out)
     m->wdown.push_back(view(c.dim, c.ffn_dim));
   }
   m->wout = view(c.vocab, c.dim);
+  m->fused_decode = mri::matmul_int8_epilogue_supported(m->ctx, 1, &m->wqkv[0]) &&
+                    mri::matmul_int8_epilogue_supported(m->ctx, 1, &m->wgu[0]) &&
+                    mri::matmul_int8_epilogue_supported(m->ctx, 1, &m->wdown[0]);
   *out = m;
   return MRI_OK;
 }
@@ -719,8 +819,19 @@ int mri_llama_set_layer(mri_llama* m, uint32_t layer, const int8_t* wq, const fl
   if (int rc = put_rows(m->wqkv[layer], m->qd, wk, sk, m->kvd)) return rc;
   if (int rc = put_rows(m->wqkv[layer], m->qd + m->kvd, wv, sv, m->kvd)) return rc;
   if (int rc = put_rows(m->wo[layer], 0, wo, so, c.dim)) return rc;
-  if (int rc = put_rows(m->wgu[layer], 0, wgate, sgate, c.ffn_dim)) return rc;
-  if (int rc = put_rows(m->wgu[layer], c.ffn_dim, wup, sup, c.ffn_dim)) return rc;
+  {
+    // gate and up rows interleaved: row 2i = gate i, row 2i+1 = up i.
+    const size_t F = c.ffn_dim, D = c.dim;
+    std::vector<int8_t> w(2 * F * D);
+    std::vector<float> sc(2 * F);
+    for (size_t i = 0; i < F; ++i) {
+      std::memcpy(w.data() + (2 * i) * D, wgate + i * D, D);
+      std::memcpy(w.data() + (2 * i + 1) * D, wup + i * D, D);
+      sc[2 * i] = sgate[i];
+      sc[2 * i + 1] = sup[i];
+    }
+    if (int rc = put_rows(m->wgu[layer], 0, w.data(), sc.data(), 2 * F)) return rc;
+  }
   if (int rc = put_rows(m->wdown[layer], 0, wdown, sdown, c.dim)) return rc;
   return MRI_OK;
 }
@@ -808,7 +919,7 @@ int mri_llama_generate_greedy(mri_llama* m, const uint32_t* prompt, size_t n_pro
   if (rc == MRI_OK) {
     const int p = static_cast<int>(n_prompt) - 1;  // argmax advances it to n_prompt
     cudaMemcpyAsync(m->d_pos, &p, sizeof(int), cudaMemcpyHostToDevice, st);
-    argmax_kernel<<<1, 1024, 0, st>>>(m->logits, m->cfg.vocab, m->d_tokens, m->d_pos, m->d_gen);
+    rc = launch_argmax(m);
     cudaEventRecord(e1, st);
     for (size_t i = 0; i < n_decode && rc == MRI_OK; ++i)
       if (cudaGraphLaunch(m->decode_exec, st) != cudaSuccess) rc = fail(MRI_ERR_CUDA, "graph launch");

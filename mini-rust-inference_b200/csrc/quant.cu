@@ -123,8 +123,8 @@ __global__ void __launch_bounds__(kQThreads) quant_apply_kernel(const float* __r
 __device__ __forceinline__ float xform(const float* __restrict__ x, size_t k, size_t K, int r,
                                        const float* __restrict__ norm_w, float inv_r, int swiglu) {
   if (swiglu) {
-    const float g = __ldg(x + static_cast<size_t>(r) * 2 * K + k);
-    const float u = __ldg(x + static_cast<size_t>(r) * 2 * K + K + k);
+    const float g = __ldg(x + static_cast<size_t>(r) * 2 * K + 2 * k);
+    const float u = __ldg(x + static_cast<size_t>(r) * 2 * K + 2 * k + 1);
     return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
   }
   const float v = __ldg(x + static_cast<size_t>(r) * K + k);

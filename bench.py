@@ -313,6 +313,101 @@ def model_measurement(mri, device, peak_hbm):
         return {"error": str(e)[:300]}
 
 
+def sharded_measurement(torch, mri, device, world, dist, peak_hbm, peak_tc):
+    """Llama-70B FFN projections, W int8 gate/up [28672, 8192]
+    and down [8192, 28672] with per-channel scales, N-sharded over the ranks
+    (rank r holds rows [r*N/P, (r+1)*N/P)); each call returns the full [M, N]
+    f32 product on every rank through mri_sharded_matmul_int8_from_f32
+    (per-shard kernels + NCCL all-gather).  M=1 calls are replayed from a CUDA
+    graph over rotating weight copies (> 300 MB per rank, so shards stream
+    from HBM); M=2048 calls are timed eagerly.  Times are max over ranks."""
+    s = torch.cuda.Stream(device)
+    ctx = mri.Context(device, stream=s)
+    comm = mri.Communicator.from_process_group(ctx=ctx) if world > 1 else \
+        mri.Communicator(mri.Communicator.unique_id(), 1, 0, ctx=ctx)
+    lib = ctx._lib
+    res = {"P": world, "collective": "NCCL all-gather of f32 [M, N/P] slices",
+           "data": "synthetic int8 weights, x ~ N(0,1)"}
+    rng = np.random.default_rng(comm.rank)
+
+    def max_ms(ms):
+        if dist is None:
+            return ms
+        t = torch.tensor([ms], device=f"cuda:{device}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for name, (N, K) in {"gate_up": (28672, 8192), "down": (8192, 28672)}.items():
+        ns = N // world
+        shard_bytes = ns * K
+        wq = rng.integers(-127, 128, size=shard_bytes, dtype=np.int8)
+        ws = rng.uniform(0.001, 0.02, size=ns).astype(np.float32)
+        copies = max(2, int(np.ceil(300e6 / shard_bytes)))
+        mats = [mri.QuantizedMatrix(wq, ws, ns, K, ctx=ctx, keep_host=False) for _ in range(copies)]
+        del wq
+        # M = 1 (decode)
+        calls = 2 * copies
+        x = torch.randn(calls, K, device=f"cuda:{device}")
+        out = torch.empty(calls, N, device=f"cuda:{device}")
+
+        def body():
+            for i in range(calls):
+                rc = lib.mri_sharded_matmul_int8_from_f32(comm.handle, ctypes.c_void_p(x[i].data_ptr()), 1, K,
+                                                          mats[i % copies].handle, N,
+                                                          ctypes.c_void_p(out[i].data_ptr()))
+                if rc != 0:
+                    raise RuntimeError(mri._lib.last_error())
+        body()
+        comm.wait()
+        if dist is not None:
+            dist.barrier()
+        g = graph_of(torch, s, body)
+        reps = 10
+        ms = max_ms(time_graph(torch, s, g, reps, 3))
+        del g
+        t = ms / 1e3 / (reps * calls)
+        res[f"{name}_m1"] = {"us_per_call": round(t * 1e6, 3),
+                             "weight_gbs_aggregate": round(N * K / t / 1e9, 1),
+                             "weight_gbs_per_gpu": round(shard_bytes / t / 1e9, 1),
+                             "frac_hbm_per_gpu": round(shard_bytes / t / 1e9 / peak_hbm, 4),
+                             "gather_bytes_per_rank": 4 * N}
+        del x, out
+        # M = 2048 (prefill)
+        M = 2048
+        x = torch.randn(M, K, device=f"cuda:{device}")
+        out = torch.empty(M, N, device=f"cuda:{device}")
+
+        def call(i):
+            rc = lib.mri_sharded_matmul_int8_from_f32(comm.handle, ctypes.c_void_p(x.data_ptr()), M, K,
+                                                      mats[i % copies].handle, N, ctypes.c_void_p(out.data_ptr()))
+            if rc != 0:
+                raise RuntimeError(mri._lib.last_error())
+        call(0)
+        comm.wait()
+        if dist is not None:
+            dist.barrier()
+        reps = 6
+        with torch.cuda.stream(s):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(s)
+            for i in range(reps):
+                call(i)
+            e1.record(s)
+        comm.wait()
+        ms = max_ms(e0.elapsed_time(e1))
+        t = ms / 1e3 / reps
+        ops = 2.0 * M * N * K
+        res[f"{name}_m2048"] = {"ms_per_call": round(t * 1e3, 4),
+                                "tops_aggregate": round(ops / t / 1e12, 2),
+                                "tops_per_gpu": round(ops / world / t / 1e12, 2),
+                                "frac_int8_per_gpu": round(ops / world / t / 1e12 / (2 * peak_tc), 4),
+                                "gather_bytes_per_rank": 4 * M * N}
+        del x, out, mats
+        torch.cuda.empty_cache()
+    comm.close()
+    return res
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     mri = importlib.import_module("mini-rust-inference_b200")
@@ -417,6 +512,12 @@ def run_ours(args, rank, world, local_rank):
     secondary = None
     if world == 1 and not args.no_secondary:
         secondary = secondary_measurements(torch, mri, lib, device, peak_hbm, peak_tc)
+    sharded = None
+    if not args.no_secondary:
+        try:
+            sharded = sharded_measurement(torch, mri, device, world, dist, peak_hbm, peak_tc)
+        except Exception as e:  # noqa: BLE001 - side measurement only
+            sharded = {"error": str(e)[:300]}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -453,6 +554,8 @@ def run_ours(args, rank, world, local_rank):
         }
         if secondary is not None:
             line["secondary"] = secondary
+        if sharded is not None:
+            line["sharded_70b_ffn"] = sharded
         print(json.dumps(line), flush=True)
     if dist:
         dist.barrier()

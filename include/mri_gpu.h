@@ -224,10 +224,51 @@ MRI_API int mri_matmul_int8_from_f32_noalloc(const float* x_dev, size_t m, size_
                                              size_t n, float* out_dev, void* cuda_stream);
 MRI_API const char* mri_noalloc_last_error(void);
 
+/* ── N-sharded products over NCCL ───────────────────────────────────────────── */
+/* No counterpart in the reference (it runs on one host).  For weight matrices
+ * split across the GPUs of one node, one process (or thread) per GPU: rank r
+ * of P holds rows [r*N/P, (r+1)*N/P) of W (mri_shard_rows, then
+ * mri_qmatrix_upload_rows), and mri_sharded_matmul_int8_from_f32 returns the
+ * full [m, N] product on every rank, bit-identical to the unsharded
+ * mri_matmul_int8_from_f32 (same kernels per element, per-tensor activation
+ * scale over the whole input on every rank, NCCL all-gather of f32 slices).
+ *   - NCCL is loaded at run time (libnccl.so.2); mri_comm_available() says
+ *     whether it could be.  Rank 0 calls mri_comm_unique_id and the host
+ *     application sends the MRI_COMM_ID_BYTES bytes to the other ranks.
+ *   - mri_comm_create binds the communicator to the context's device and
+ *     stream.  Host-side waits (creation, enqueue, mri_comm_wait) give up
+ *     after timeout_ms (<= 0: 60 s), abort the communicator and return
+ *     MRI_ERR_TIMEOUT; an aborted communicator refuses further calls.
+ *   - mri_sharded_matmul_int8_from_f32 is asynchronous on the context's
+ *     stream; x_dev [m,k] f32, out_dev [m,n_total] f32.  For m > 1 the rows
+ *     are processed in chunks whose all-gathers overlap the next chunk's
+ *     product; the staging buffer grows on demand (a growth synchronizes).
+ *     N % P != 0 -> MRI_ERR_INVALID_SHAPE, wrong shard height or k ->
+ *     MRI_ERR_SHAPE_MISMATCH, NCCL failures -> MRI_ERR_COMM.
+ *   - mri_comm_wait synchronizes the context's stream and the communicator's
+ *     side stream, watching NCCL's asynchronous error state. */
+typedef struct mri_comm mri_comm;
+#define MRI_COMM_ID_BYTES 128
+MRI_API int mri_comm_available(void);
+MRI_API int mri_comm_unique_id(uint8_t* id /* [MRI_COMM_ID_BYTES] */);
+MRI_API int mri_comm_create(mri_ctx* ctx, const uint8_t* id, int nranks, int rank, int timeout_ms,
+                            mri_comm** out);
+MRI_API int mri_comm_destroy(mri_comm* comm);
+MRI_API int mri_comm_rank(const mri_comm* comm, int* rank, int* nranks);
+MRI_API int mri_comm_wait(mri_comm* comm);
+MRI_API int mri_shard_rows(size_t n, int nranks, int rank, size_t* row_begin, size_t* row_end);
+MRI_API int mri_sharded_matmul_int8_from_f32(mri_comm* comm, const float* x_dev, size_t m, size_t k,
+                                             const mri_qmatrix* w_shard, size_t n_total,
+                                             float* out_dev);
+
 /* ── diagnostics ──────────────────────────────────────────────────────────── */
 /* Kernel path chosen for an INT8 product of this shape:
  * 0 = streaming GEMV (TMA bulk), 1 = generic GEMV, 2 = tensor-core GEMM. */
 MRI_API int mri_int8_path(mri_ctx* ctx, size_t m, size_t n, size_t k);
+/* Launch shape of the streaming INT8 GEMV for (m <= 8, n, k): plan[0..5] =
+ * grid, CTAs per SM used, CTAs per SM that fit (registers and shared
+ * memory), pipeline stages, K-chunks per row group, dynamic shared bytes. */
+MRI_API int mri_int8_gemv_plan(mri_ctx* ctx, size_t m, size_t n, size_t k, int* plan /* [6] */);
 
 #ifdef __cplusplus
 }

@@ -36,6 +36,8 @@ __all__ = [
     "matmul_int8", "matmul_int8_avx2", "matmul_int8_neon", "matmul_int8_parallel",
     "matmul_int8_from_f32", "matmul_q8_0_direct", "matmul_q4_0_dequant", "formats",
     "LlamaConfig", "LlamaModelInt8",
+    "comm_available", "shard_rows", "Communicator", "shard_quantized_matrix",
+    "matmul_int8_from_f32_sharded",
 ]
 
 
@@ -134,6 +136,13 @@ class Context:
 
     def int8_path(self, m, n, k):
         return int(self._lib.mri_int8_path(self.handle, m, n, k))
+
+    def int8_gemv_plan(self, m, n, k):
+        """Launch shape of the streaming INT8 GEMV (diagnostics)."""
+        p = (ctypes.c_int * 6)()
+        _check(self._lib.mri_int8_gemv_plan(self.handle, m, n, k, p))
+        keys = ("grid", "ctas_per_sm", "resident_ctas", "stages", "k_chunks", "smem_bytes")
+        return dict(zip(keys, list(p)))
 
 
 _tls = threading.local()
@@ -397,6 +406,99 @@ def matmul_q4_0_dequant(input, weight_q4, n_out, k, ctx=None):  # noqa: A002
 
 def library_path():
     return _lib.library_path()
+
+
+# ── N-sharded products (no reference counterpart) ─────────────────────────────
+
+def comm_available():
+    """True when libnccl.so.2 could be loaded by the library."""
+    return bool(_lib.load().mri_comm_available())
+
+
+def shard_rows(n, nranks, rank):
+    """Rows [begin, end) of an [n, k] weight that rank `rank` of `nranks` holds
+    (equal shards; InvalidShape when n % nranks != 0)."""
+    lib = _lib.load()
+    b, e = ctypes.c_size_t(), ctypes.c_size_t()
+    _check(lib.mri_shard_rows(int(n), int(nranks), int(rank), ctypes.byref(b), ctypes.byref(e)))
+    return b.value, e.value
+
+
+class Communicator:
+    """NCCL communicator bound to one context (mri_comm).  One per rank; rank
+    0's `unique_id()` bytes must reach every rank before construction."""
+
+    ID_BYTES = 128
+
+    @staticmethod
+    def unique_id():
+        buf = (ctypes.c_uint8 * Communicator.ID_BYTES)()
+        _check(_lib.load().mri_comm_unique_id(buf))
+        return bytes(buf)
+
+    def __init__(self, unique_id, nranks, rank, ctx=None, timeout_ms=60000):
+        self.ctx = ctx or default_context()
+        if len(unique_id) != self.ID_BYTES:
+            raise ValueError(f"unique id must be {self.ID_BYTES} bytes")
+        buf = (ctypes.c_uint8 * self.ID_BYTES).from_buffer_copy(unique_id)
+        h = ctypes.c_void_p()
+        _check(self.ctx._lib.mri_comm_create(self.ctx.handle, buf, int(nranks), int(rank), int(timeout_ms),
+                                             ctypes.byref(h)))
+        self.handle = h
+        self.rank, self.size = int(rank), int(nranks)
+
+    @classmethod
+    def from_process_group(cls, ctx=None, group=None, timeout_ms=60000):
+        """Rendezvous over an initialised torch.distributed group (rank 0's id
+        broadcast with broadcast_object_list)."""
+        import torch.distributed as dist
+        obj = [cls.unique_id() if dist.get_rank(group) == 0 else None]
+        dist.broadcast_object_list(obj, src=0, group=group)
+        return cls(obj[0], dist.get_world_size(group), dist.get_rank(group), ctx=ctx, timeout_ms=timeout_ms)
+
+    def wait(self):
+        _check(self.ctx._lib.mri_comm_wait(self.handle))
+
+    def close(self):
+        if self.handle:
+            self.ctx._lib.mri_comm_destroy(self.handle)
+            self.handle = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001 - interpreter shutdown
+            pass
+
+
+def shard_quantized_matrix(data, scales, n_out, k_in, comm, keep_host=False):
+    """Upload this rank's N-shard (shard_rows) of a QuantizedMatrix."""
+    return QuantizedMatrix(data, scales, n_out, k_in, ctx=comm.ctx,
+                           rows=shard_rows(n_out, comm.size, comm.rank), keep_host=keep_host)
+
+
+def matmul_int8_from_f32_sharded(input, w_shard, n_total, comm):  # noqa: A002
+    """matmul_int8_from_f32 (ops/matmul/int8.rs:113-143) of the full weight
+    whose rows are split across the communicator's ranks: every rank gets the
+    full [m, n_total] product.  Device tensors in -> device tensor out
+    (asynchronous); host arrays -> host array (synchronous)."""
+    x = _as_2d(input, "matmul_int8_from_f32_sharded")
+    m, k = x.shape
+    lib = comm.ctx._lib
+    if _is_cuda_tensor(x):
+        out = _new_out(x, m, n_total)
+        _check(lib.mri_sharded_matmul_int8_from_f32(comm.handle, _vp(x), m, k, w_shard.handle, n_total,
+                                                    _vp(out)))
+        return out
+    import torch
+    dev = f"cuda:{comm.ctx.device}"
+    dx = torch.from_numpy(np.ascontiguousarray(x)).to(dev)
+    dout = torch.empty((m, n_total), dtype=torch.float32, device=dev)
+    torch.cuda.synchronize(comm.ctx.device)
+    _check(lib.mri_sharded_matmul_int8_from_f32(comm.handle, _vp(dx), m, k, w_shard.handle, n_total,
+                                                _vp(dout)))
+    comm.wait()
+    return dout.cpu().numpy()
 
 
 # ── LlamaModelInt8 (model/llama/forward_int8.rs:416-547) ─────────────────────

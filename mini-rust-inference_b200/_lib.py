@@ -58,6 +58,15 @@ SIGNATURES = {
     "mri_host_matmul_q8_0_direct": (_I, [_P, _P, _SZ, _SZ, _P, _P]),
     "mri_host_matmul_q4_0_dequant": (_I, [_P, _P, _SZ, _SZ, _P, _P]),
     "mri_int8_path": (_I, [_P, _SZ, _SZ, _SZ]),
+    "mri_int8_gemv_plan": (_I, [_P, _SZ, _SZ, _SZ, _P]),
+    "mri_comm_available": (_I, []),
+    "mri_comm_unique_id": (_I, [_P]),
+    "mri_comm_create": (_I, [_P, _P, _I, _I, _I, _PP]),
+    "mri_comm_destroy": (_I, [_P]),
+    "mri_comm_rank": (_I, [_P, ctypes.POINTER(_I), ctypes.POINTER(_I)]),
+    "mri_comm_wait": (_I, [_P]),
+    "mri_shard_rows": (_I, [_SZ, _I, _I, ctypes.POINTER(_SZ), ctypes.POINTER(_SZ)]),
+    "mri_sharded_matmul_int8_from_f32": (_I, [_P, _P, _SZ, _SZ, _P, _SZ, _P]),
     "mri_llama_create": (_I, [_P, _P, _PP]),
     "mri_llama_free": (_I, [_P]),
     "mri_llama_last_error": (ctypes.c_char_p, []),

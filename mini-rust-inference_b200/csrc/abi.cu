@@ -180,6 +180,35 @@ int run_int8(mri_ctx* ctx, ActArgs act, const mri_qmatrix* w, size_t m, float* o
 
 }  // namespace
 
+int mri::set_error(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int mri::quantize_to_scratch(::mri_ctx* ctx, const float* x, size_t m, size_t k, int8_t** q,
+                             float** scale_dev) {
+  if (int rc = enter(ctx)) return rc;
+  const size_t need = amax_bytes(m) + al(sizeof(float)) + al(m * k);
+  if (int rc = ensure_scratch(ctx, need)) return rc;
+  float* amax = reinterpret_cast<float*>(ctx->scratch);
+  *scale_dev = reinterpret_cast<float*>(ctx->scratch + amax_bytes(m));
+  *q = reinterpret_cast<int8_t*>(ctx->scratch + amax_bytes(m) + al(sizeof(float)));
+  MRI_CUDA_TRY(mri::launch_quantize(ctx->dev, ctx->stream, x, m, k, 0, *q, *scale_dev, amax, &ctx->ls));
+  return MRI_OK;
+}
+
+int mri::matmul_int8_act(::mri_ctx* ctx, const ActArgs& act, const ::mri_qmatrix* w, size_t m,
+                         float* out) {
+  if (int rc = enter(ctx)) return rc;
+  if (!w) return fail(MRI_ERR_INVALID_ARGUMENT, "null weight handle");
+  return run_int8(ctx, act, w, m, out, nullptr);
+}
+
 bool mri::matmul_int8_epilogue_supported(const ::mri_ctx* ctx, size_t m, const ::mri_qmatrix* w) {
   return ctx && w && w->n_out % 2 == 0 && stream_gemv_applies(ctx, m, w);
 }
@@ -670,6 +699,22 @@ int mri_int8_path(mri_ctx* ctx, size_t m, size_t n, size_t k) {
   if (m <= 8 && m > 0 && mri::gemv_i8_tma_supported(ctx->dev, static_cast<int>(m), k)) return 0;
   if (mri::gemm_i8_tc_supported(ctx->dev, m, n, k)) return 2;  // (16-byte aligned activations)
   return 1;
+}
+
+int mri_int8_gemv_plan(mri_ctx* ctx, size_t m, size_t n, size_t k, int* plan) {
+  if (int rc = enter(ctx)) return rc;
+  if (!plan) return fail(MRI_ERR_INVALID_ARGUMENT, "null plan");
+  if (m < 1 || m > 8 || !mri::gemv_i8_tma_supported(ctx->dev, static_cast<int>(m), k))
+    return fail(MRI_ERR_INVALID_SHAPE, "no streaming GEMV for m=%zu, k=%zu", m, k);
+  mri::GemvPlan p;
+  MRI_CUDA_TRY(mri::gemv_i8_tma_plan(ctx->dev, static_cast<int>(m), n, k, &p));
+  plan[0] = p.grid;
+  plan[1] = p.ctas_per_sm;
+  plan[2] = p.resident;
+  plan[3] = p.stages;
+  plan[4] = p.k_chunks;
+  plan[5] = static_cast<int>(p.smem);
+  return MRI_OK;
 }
 
 }  // extern "C"

@@ -1003,14 +1003,19 @@ cudaError_t launch_stream_kernel(void (*k)(KArgs...), int grid, size_t smem, cud
 
 // K-chunk count for the INT8 stream: the smallest nk whose 8 x kc stage
 // leaves room for three stages next to the activations.
+// Fewest K-chunks that give at least three stages, preferring (up to four
+// chunks) a configuration with two CTAs per SM: their prologues and tails
+// overlap each other's streaming.
 int i8_chunks(int M, size_t K, StreamConfig* cfg_out) {
-  for (int nk = 1; nk <= 64; ++nk) {
-    const size_t kc = nk == 1 ? K : align_up((K + nk - 1) / nk, 16);
-    if (nk > 1 && kc * (nk - 1) >= K) break;  // chunks would be empty
-    const StreamConfig c = pick_config(fixed_bytes_of(M * K, 0), kRowsPerStage * kc);
-    if (c.stages >= 3) {
-      if (cfg_out) *cfg_out = c;
-      return nk;
+  for (int pass = 0; pass < 2; ++pass) {
+    for (int nk = 1; nk <= (pass == 0 ? 4 : 64); ++nk) {
+      const size_t kc = nk == 1 ? K : align_up((K + nk - 1) / nk, 16);
+      if (nk > 1 && kc * (nk - 1) >= K) break;  // chunks would be empty
+      const StreamConfig c = pick_config(fixed_bytes_of(M * K, 0), kRowsPerStage * kc);
+      if (c.stages >= 3 && (pass == 1 || c.ctas_per_sm >= 2)) {
+        if (cfg_out) *cfg_out = c;
+        return nk;
+      }
     }
   }
   return 0;
@@ -1021,28 +1026,41 @@ bool gemv_i8_tma_supported(const DeviceInfo&, int M, size_t K) {
   return i8_chunks(M, K, nullptr) > 0;
 }
 
+cudaError_t gemv_i8_tma_plan(const DeviceInfo& dev, int M, size_t N, size_t K, GemvPlan* plan) {
+  StreamConfig cfg;
+  const int nk = i8_chunks(M, K, &cfg);
+  if (nk == 0 || M < 1 || M > 8) return cudaErrorInvalidValue;
+  const size_t kc = nk == 1 ? K : align_up((K + nk - 1) / nk, 16);
+  GemvPlan p;
+  p.stages = cfg.stages;
+  p.k_chunks = nk;
+  p.smem = make_layout(M * K, 0, kRowsPerStage * kc, p.stages).total;
+  MRI_DISPATCH_M(M, {
+    cudaError_t e = set_smem(gemv_i8_tma_kernel<kM>, p.smem, dev.device);
+    if (e != cudaSuccess) return e;
+    p.resident = resident_ctas(gemv_i8_tma_kernel<kM>, p.smem, dev.device);
+  });
+  p.ctas_per_sm = std::min(cfg.ctas_per_sm, p.resident);
+  p.grid = stream_grid(dev, N, p.ctas_per_sm);
+  *plan = p;
+  return cudaSuccess;
+}
+
 cudaError_t launch_gemv_i8_tma(const DeviceInfo& dev, cudaStream_t st, int M, const int8_t* W,
                                const float* w_scales, size_t N, size_t K, const ActArgs& act,
                                float* out, int32_t* acc_out, int* status, LaunchStats* ls,
                                const float* residual, const EpiArgs* epi) {
-  StreamConfig cfg;
-  const int nk = i8_chunks(M, K, &cfg);
   EpiArgs e_args;
   if (epi) {
     if (N % 2 || residual || acc_out) return cudaErrorInvalidValue;
     e_args = *epi;
   }
-  if (nk == 0) return cudaErrorInvalidValue;
-  const size_t kc = nk == 1 ? K : align_up((K + nk - 1) / nk, 16);
-  const int stages = cfg.stages;
-  const size_t smem = make_layout(M * K, 0, kRowsPerStage * kc, stages).total;
+  GemvPlan p;
+  if (cudaError_t e = gemv_i8_tma_plan(dev, M, N, K, &p)) return e;
   MRI_DISPATCH_M(M, {
-    cudaError_t e = set_smem(gemv_i8_tma_kernel<kM>, smem, dev.device);
-    if (e != cudaSuccess) return e;
-    const int grid = stream_grid(
-        dev, N, std::min(cfg.ctas_per_sm, resident_ctas(gemv_i8_tma_kernel<kM>, smem, dev.device)));
-    e = launch_stream_kernel(gemv_i8_tma_kernel<kM>, grid, smem, st, W, w_scales, N, K, act, out,
-                             acc_out, stages, nk, status, residual, e_args);
+    cudaError_t e = launch_stream_kernel(gemv_i8_tma_kernel<kM>, p.grid, p.smem, st, W, w_scales, N, K,
+                                         act, out, acc_out, p.stages, p.k_chunks, status, residual,
+                                         e_args);
     if (e != cudaSuccess) return e;
   });
   if (ls) ls->launches++;

@@ -94,6 +94,12 @@ cudaError_t launch_add_residual(const DeviceInfo& dev, cudaStream_t st, float* o
 // INT8 per-channel.  Requires K % 16 == 0 and 16-byte aligned W.
 bool gemv_i8_tma_supported(const DeviceInfo& dev, int M, size_t K);
 // residual (nullable): out = residual + product, element-wise (may alias out).
+// Launch shape the INT8 streaming GEMV uses for (M, N, K).
+struct GemvPlan {
+  int grid = 0, ctas_per_sm = 0, resident = 0, stages = 0, k_chunks = 0;
+  size_t smem = 0;
+};
+cudaError_t gemv_i8_tma_plan(const DeviceInfo& dev, int M, size_t N, size_t K, GemvPlan* plan);
 // epi (nullable): a pair epilogue (EpiArgs); not combined with residual or acc_out.
 cudaError_t launch_gemv_i8_tma(const DeviceInfo& dev, cudaStream_t st, int M, const int8_t* W,
                                const float* w_scales, size_t N, size_t K, const ActArgs& act,
@@ -132,6 +138,16 @@ int matmul_int8_fused(struct ::mri_ctx* ctx, const float* x, size_t m, size_t k,
                       const float* norm_w, float eps, int swiglu,
                       const struct ::mri_qmatrix* w, const float* residual, float* out,
                       const EpiArgs* epi = nullptr);
+// Records the calling thread's last error (mri_last_error) and returns code.
+int set_error(int code, const char* fmt, ...);
+// Per-tensor quantization of x [m, k] into the context scratch (quantized
+// values and one device scale), for callers that run several products on
+// slices of the same quantized input.
+int quantize_to_scratch(struct ::mri_ctx* ctx, const float* x, size_t m, size_t k, int8_t** q,
+                        float** scale_dev);
+// The INT8 dispatch (streaming GEMV / tensor-core GEMM) for any ActArgs mode.
+int matmul_int8_act(struct ::mri_ctx* ctx, const ActArgs& act, const struct ::mri_qmatrix* w,
+                    size_t m, float* out);
 bool matmul_int8_epilogue_supported(const struct ::mri_ctx* ctx, size_t m,
                                     const struct ::mri_qmatrix* w);
 

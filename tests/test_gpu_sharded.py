@@ -1,0 +1,101 @@
+"""N-sharded INT8 product on the GPU (mri_sharded_matmul_int8_from_f32).
+
+Bar: bit-exact against the unsharded product.  Each output element comes
+from the same kernels on the same weight row and the same per-tensor
+activation scale; the NCCL all-gather moves f32 values unchanged.
+"""
+import multiprocessing as mp
+import time
+
+import numpy as np
+import pytest
+import torch
+
+import shard_workers
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def comm1(mri, gpu_ctx):
+    if not mri.comm_available():
+        pytest.fail("libnccl.so.2 not loadable on the GPU box")
+    c = mri.Communicator(mri.Communicator.unique_id(), 1, 0, ctx=gpu_ctx, timeout_ms=30000)
+    yield c
+    c.close()
+
+
+@pytest.mark.parametrize("m", [1, 3, 8, 300, 1100])
+def test_single_rank_matches_unsharded(mri, gpu_ctx, comm1, m):
+    n, k = 1024, 512
+    x, wq, ws = shard_workers.problem(m, n, k, 11 + m)
+    full = mri.QuantizedMatrix(wq.reshape(-1), ws, n, k, ctx=gpu_ctx)
+    shard = mri.shard_quantized_matrix(wq.reshape(-1), ws, n, k, comm1)
+    xd = torch.from_numpy(x).cuda()
+    want = mri.matmul_int8_from_f32(xd, full)
+    got = mri.matmul_int8_from_f32_sharded(xd, shard, n, comm1)
+    comm1.wait()
+    gpu_ctx.synchronize()
+    np.testing.assert_array_equal(got.cpu().numpy(), want.cpu().numpy())
+
+
+@pytest.mark.parametrize("p", [2, 4, 8])
+@pytest.mark.parametrize("m", [1, 6, 600])
+def test_emulated_shards_concatenate_to_unsharded(mri, gpu_ctx, oracle, p, m):
+    """P shards computed one after another on one GPU and concatenated along
+    N equal the unsharded product (the per-rank math of the sharded call)."""
+    n, k = 2048, 1024
+    x, wq, ws = shard_workers.problem(m, n, k, 5 * p + m)
+    xd = torch.from_numpy(x).cuda()
+    parts = []
+    for r in range(p):
+        b, e = mri.shard_rows(n, p, r)
+        w = mri.QuantizedMatrix(wq.reshape(-1), ws, n, k, ctx=gpu_ctx, rows=(b, e))
+        parts.append(mri.matmul_int8_from_f32(xd, w).cpu().numpy())
+    got = np.concatenate(parts, axis=1)
+    if m <= 8:
+        want = oracle.matmul_int8_from_f32(x, m, k, wq.reshape(-1), ws, n, k)
+    else:
+        want = mri.matmul_int8_from_f32(xd, mri.QuantizedMatrix(wq.reshape(-1), ws, n, k, ctx=gpu_ctx)).cpu().numpy()
+    np.testing.assert_array_equal(got, want)
+
+
+def test_sharded_argument_errors(mri, gpu_ctx, comm1):
+    n, k = 64, 32
+    x, wq, ws = shard_workers.problem(2, n, k, 1)
+    w = mri.shard_quantized_matrix(wq.reshape(-1), ws, n, k, comm1)
+    xd = torch.from_numpy(x).cuda()
+    with pytest.raises(mri.ShapeMismatch):
+        mri.matmul_int8_from_f32_sharded(xd[:, :16].contiguous(), w, n, comm1)
+    with pytest.raises(mri.ShapeMismatch):
+        mri.matmul_int8_from_f32_sharded(xd, w, 2 * n, comm1)
+
+
+def test_comm_init_times_out_when_peer_never_joins(mri, gpu_ctx):
+    """Rank 1 of 2 never joins: creation gives up after the deadline with
+    DeviceTimeout and aborts the communicator (host-side wait; no kernel)."""
+    t0 = time.time()
+    with pytest.raises(mri.DeviceTimeout):
+        mri.Communicator(mri.Communicator.unique_id(), 2, 0, ctx=gpu_ctx, timeout_ms=1500)
+    assert time.time() - t0 < 30
+
+
+def test_two_ranks_match_unsharded(mri, gpu_ctx, oracle):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    m, n, k, seed = 4, 4096, 2048, 3
+    uid = mri.Communicator.unique_id()
+    ctx = mp.get_context("spawn")
+    results = ctx.Queue()
+    procs = [ctx.Process(target=shard_workers.nccl_shard_worker, args=(r, 2, uid, m, n, k, seed, results))
+             for r in range(2)]
+    for p in procs:
+        p.start()
+    got = dict(results.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=120)
+    x, wq, ws = shard_workers.problem(m, n, k, seed)
+    want = oracle.matmul_int8_from_f32(x, m, k, wq.reshape(-1), ws, n, k)
+    for r in range(2):
+        assert not isinstance(got[r], str), got[r]
+        np.testing.assert_array_equal(got[r], want)

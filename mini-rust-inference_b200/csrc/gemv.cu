@@ -67,7 +67,7 @@ __host__ __device__ inline StreamLayout make_layout(size_t act_bytes, size_t ext
   StreamLayout L{};
   L.stages = stages;
   L.bars = 0;
-  L.scales = align_up(2 * stages * sizeof(uint64_t), 16);
+  L.scales = align_up((2 * stages + 2) * sizeof(uint64_t), 16);  // + act-issued barrier
   L.act = align_up(L.scales + 16 * sizeof(float), 128);
   L.extra = align_up(L.act + act_bytes, 128);
   L.stage = align_up(L.extra + extra_bytes, 128);
@@ -113,12 +113,14 @@ __device__ void stream_producer(const uint8_t* W, size_t row_bytes, size_t begin
     mbar_wait(&full[it % n_stages], (it / n_stages) & 1, status);
 }
 
-__device__ __forceinline__ void init_barriers(uint64_t* full, uint64_t* empty, int n_stages) {
+__device__ __forceinline__ void init_barriers(uint64_t* full, uint64_t* empty, int n_stages,
+                                              uint64_t* act_issued = nullptr) {
   if (threadIdx.x == 0) {
     for (int s = 0; s < n_stages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kConsumerWarps);
     }
+    if (act_issued) mbar_init(act_issued, kConsumerWarps);
     fence_barrier_init();
   }
   __syncthreads();
@@ -201,63 +203,74 @@ __device__ __forceinline__ char4 quant4(float4 v, float inv) {
 
 // Quantize (or copy) the M activation rows into shared memory as int8 [M][K]
 // row-major and fill s_scale[0..M).  Optional fused producer ops (RMSNorm,
-// SwiGLU) are applied to the f32 values first.
-template <int M>
+// SwiGLU) are applied to the f32 values first.  VEC > 0 selects the decode
+// path: per-tensor f32 input of at most VEC float4 per consumer thread, read
+// once into registers (the host checks the preconditions).  Each consumer
+// warp arrives on `act_issued` (nullable) once its activation loads are in
+// flight: the producer holds back later weight stages until then, so those
+// loads do not queue behind them.
+template <int M, int VEC>
 __device__ void load_act_i8_rowmajor(const ActArgs& act, size_t K, int8_t* s_act, float* s_scale,
-                                     float* red) {
+                                     float* red, uint64_t* act_issued) {
   const int ct = threadIdx.x - 32;
   const size_t total = static_cast<size_t>(M) * K;
   __shared__ float s_inv[8];
+  if constexpr (VEC > 0) {
+    ActView v{act.x, act.norm_w, s_inv, K, K, 0};
+    float4 x4[VEC];
+    const int n4 = static_cast<int>(total / 4), K32 = static_cast<int>(K);
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) {
+      const int i = ct + j * kConsumerThreads;
+      x4[j] = i < n4 ? __ldg(reinterpret_cast<const float4*>(act.x) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    if (act_issued) {
+      __syncwarp();
+      if ((threadIdx.x & 31) == 0) mbar_arrive(act_issued);
+    }
+    if (act.norm_w) {
+      for (int r = 0; r < M; ++r) {
+        float ss = 0.0f;
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) {
+          const int i = ct + j * kConsumerThreads;
+          if (i < n4 && (M == 1 || (i * 4) / K32 == r)) {
+            ss = __fmaf_rn(x4[j].x, x4[j].x, ss);
+            ss = __fmaf_rn(x4[j].y, x4[j].y, ss);
+            ss = __fmaf_rn(x4[j].z, x4[j].z, ss);
+            ss = __fmaf_rn(x4[j].w, x4[j].w, ss);
+          }
+        }
+        ss = consumer_sum(ss, red);
+        if (ct == 0) s_inv[r] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(K)), act.eps)));
+      }
+      named_bar_sync(1, kConsumerThreads);
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) {
+        const int i = ct + j * kConsumerThreads;
+        if (i < n4) x4[j] = v.norm(x4[j], M == 1 ? 0 : (i * 4) / K32, M == 1 ? i * 4 : (i * 4) % K32);
+      }
+    }
+    float m = 0.0f;
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) m = absmax4(m, x4[j]);
+    const float scale = sym_scale(consumer_max(m, red));
+    const float inv = __fdiv_rn(1.0f, scale);
+    if (ct < M) s_scale[ct] = scale;
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) {
+      const int i = ct + j * kConsumerThreads;
+      if (i < n4) reinterpret_cast<char4*>(s_act)[i] = quant4(x4[j], inv);
+    }
+    named_bar_sync(1, kConsumerThreads);
+    return;
+  }
+  if (act_issued && (threadIdx.x & 31) == 0) mbar_arrive(act_issued);
   if (act.mode == ACT_F32_PER_TENSOR || act.mode == ACT_F32_PER_ROW) {
     ActView v{act.x, act.norm_w, s_inv, K, act.swiglu ? 2 * K : K, act.swiglu};
-    constexpr int kRegVec = 12;  // float4 per consumer thread held in registers (K <= 12288 at M=1)
     const bool vec = (reinterpret_cast<uintptr_t>(act.x) & 15) == 0 && K % 4 == 0 &&
                      (!act.norm_w || (reinterpret_cast<uintptr_t>(act.norm_w) & 15) == 0);
-    if (vec && act.mode == ACT_F32_PER_TENSOR && !act.swiglu &&
-        total <= static_cast<size_t>(kRegVec) * 4 * kConsumerThreads) {
-      // Decode-size input: one global read, values kept in registers through
-      // the RMSNorm statistics, the absmax and the quantization.
-      float4 x4[kRegVec];
-      const int n4 = static_cast<int>(total / 4), K32 = static_cast<int>(K);
-#pragma unroll
-      for (int j = 0; j < kRegVec; ++j) {
-        const int i = ct + j * kConsumerThreads;
-        x4[j] = i < n4 ? __ldg(reinterpret_cast<const float4*>(act.x) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-      if (act.norm_w) {
-        for (int r = 0; r < M; ++r) {
-          float ss = 0.0f;
-#pragma unroll
-          for (int j = 0; j < kRegVec; ++j) {
-            const int i = ct + j * kConsumerThreads;
-            if (i < n4 && (M == 1 || (i * 4) / K32 == r)) {
-              ss = __fmaf_rn(x4[j].x, x4[j].x, ss);
-              ss = __fmaf_rn(x4[j].y, x4[j].y, ss);
-              ss = __fmaf_rn(x4[j].z, x4[j].z, ss);
-              ss = __fmaf_rn(x4[j].w, x4[j].w, ss);
-            }
-          }
-          ss = consumer_sum(ss, red);
-          if (ct == 0) s_inv[r] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(K)), act.eps)));
-        }
-        named_bar_sync(1, kConsumerThreads);
-#pragma unroll
-        for (int j = 0; j < kRegVec; ++j) {
-          const int i = ct + j * kConsumerThreads;
-          if (i < n4) x4[j] = v.norm(x4[j], M == 1 ? 0 : (i * 4) / K32, M == 1 ? i * 4 : (i * 4) % K32);
-        }
-      }
-      float m = 0.0f;
-#pragma unroll
-      for (int j = 0; j < kRegVec; ++j) m = absmax4(m, x4[j]);
-      const float scale = sym_scale(consumer_max(m, red));
-      const float inv = __fdiv_rn(1.0f, scale);
-      if (ct < M) s_scale[ct] = scale;
-#pragma unroll
-      for (int j = 0; j < kRegVec; ++j) {
-        const int i = ct + j * kConsumerThreads;
-        if (i < n4) reinterpret_cast<char4*>(s_act)[i] = quant4(x4[j], inv);
-      }
+    if (false) {
     } else if (vec) {
       if (act.norm_w) {
         for (int r = 0; r < M; ++r) {
@@ -335,13 +348,16 @@ __device__ void load_act_i8_rowmajor(const ActArgs& act, size_t K, int8_t* s_act
 
 __device__ void stream_producer_i8(const int8_t* W, size_t K, size_t kc, int nk, size_t begin,
                                    size_t end, uint64_t* full, uint64_t* empty, uint8_t* stages_base,
-                                   size_t stage_stride, int n_stages, int* status) {
+                                   size_t stage_stride, int n_stages, int* status,
+                                   uint64_t* act_issued, int pre) {
   const uint64_t policy = l2_policy_evict_first();
   const int groups = static_cast<int>((end - begin + kRowsPerStage - 1) / kRowsPerStage);
   const int iters = groups * nk;
   int issued = 0;
   for (int it = 0; it < iters; ++it) {
     const int s = it % n_stages;
+    // Stages after the first `pre` wait until the activation loads are issued.
+    if (it == pre && !mbar_wait(act_issued, 0, status)) break;
     if (it >= n_stages) {
       if (!mbar_wait(&empty[s], ((it / n_stages) - 1) & 1, status)) break;
     }
@@ -399,11 +415,12 @@ __device__ __forceinline__ void pair_epilogue(const EpiArgs& epi, int M, size_t 
   else if (r >= qk) epi.vc[static_cast<size_t>(pos) * epi.kvd + (r - qk)] = y;
 }
 
-template <int M>
+template <int M, int VEC>
 __global__ void __launch_bounds__(kThreads, M <= 2 ? 2 : 1)
     gemv_i8_tma_kernel(const int8_t* __restrict__ W, const float* __restrict__ w_scales, size_t N,
                        size_t K, ActArgs act, float* out, int32_t* __restrict__ acc_out,
-                       int n_stages, int nk, int* status, const float* residual, EpiArgs epi) {
+                       int n_stages, int nk, int pre, int* status, const float* residual,
+                       EpiArgs epi) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ float s_pair[2][kConsumerWarps][8];
   const size_t kc = nk == 1 ? K : align_up((K + nk - 1) / nk, 16);
@@ -418,18 +435,19 @@ __global__ void __launch_bounds__(kThreads, M <= 2 ? 2 : 1)
   size_t begin, end;
   // Pair epilogues need both rows of a pair in the same CTA and stage.
   cta_rows(N, epi.mode != EPI_NONE ? 2 : 1, begin, end);
-  init_barriers(full, empty, n_stages);
+  uint64_t* act_issued = empty + n_stages;
+  init_barriers(full, empty, n_stages, act_issued);
   if (begin >= end) return;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (warp == 0) {
     if (lane == 0)
       stream_producer_i8(W, K, kc, nk, begin, end, full, empty, stage0, L.stage_bytes, n_stages,
-                         status);
+                         status, act_issued, pre);
     return;
   }
   pdl_wait();
-  load_act_i8_rowmajor<M>(act, K, s_act, s_scale, red);
+  load_act_i8_rowmajor<M, VEC>(act, K, s_act, s_scale, red, act_issued);
   float s_a[M];
 #pragma unroll
   for (int m = 0; m < M; ++m) s_a[m] = s_scale[m];
@@ -599,7 +617,7 @@ __global__ void __launch_bounds__(kThreads, M <= 2 ? 2 : 1)
   ActArgs act;
   act.x = x;
   act.mode = ACT_F32_PER_ROW;
-  load_act_i8_rowmajor<M>(act, K, s_act, s_scale, red);
+  load_act_i8_rowmajor<M, 0>(act, K, s_act, s_scale, red, nullptr);
   float s_a[M];
 #pragma unroll
   for (int m = 0; m < M; ++m) s_a[m] = s_scale[m];
@@ -1026,7 +1044,39 @@ bool gemv_i8_tma_supported(const DeviceInfo&, int M, size_t K) {
   return i8_chunks(M, K, nullptr) > 0;
 }
 
-cudaError_t gemv_i8_tma_plan(const DeviceInfo& dev, int M, size_t N, size_t K, GemvPlan* plan) {
+// Register-path width for the activation prologue: float4 per consumer
+// thread when the input is a per-tensor f32 buffer without SwiGLU and fits
+// (4 or 12), else 0 (streamed through the general path).
+int reg_vec(int M, size_t K, const ActArgs* act) {
+  if (act) {
+    if (act->mode != ACT_F32_PER_TENSOR || act->swiglu || K % 4) return 0;
+    if ((reinterpret_cast<uintptr_t>(act->x) & 15) ||
+        (act->norm_w && (reinterpret_cast<uintptr_t>(act->norm_w) & 15)))
+      return 0;
+  }
+  const size_t per = (static_cast<size_t>(M) * K / 4 + kConsumerThreads - 1) / kConsumerThreads;
+  return per <= 4 ? 4 : (per <= 12 ? 12 : 0);
+}
+
+#define MRI_DISPATCH_VEC(V, ...)                              \
+  switch (V) {                                                \
+    case 4: { constexpr int kV = 4; __VA_ARGS__; } break;     \
+    case 12: { constexpr int kV = 12; __VA_ARGS__; } break;   \
+    default: { constexpr int kV = 0; __VA_ARGS__; } break;    \
+  }
+
+// Weight stages a producer issues before the activation loads are in flight
+// (MRI_GEMV_PRE_STAGES; default all).
+int pre_stages(int stages) {
+  static const int v = [] {
+    const char* e = std::getenv("MRI_GEMV_PRE_STAGES");
+    return e ? std::max(0, std::atoi(e)) : 1 << 20;
+  }();
+  return std::min(v, stages);
+}
+
+cudaError_t gemv_i8_tma_plan(const DeviceInfo& dev, int M, size_t N, size_t K, GemvPlan* plan,
+                             int vec) {
   StreamConfig cfg;
   const int nk = i8_chunks(M, K, &cfg);
   if (nk == 0 || M < 1 || M > 8) return cudaErrorInvalidValue;
@@ -1034,11 +1084,14 @@ cudaError_t gemv_i8_tma_plan(const DeviceInfo& dev, int M, size_t N, size_t K, G
   GemvPlan p;
   p.stages = cfg.stages;
   p.k_chunks = nk;
+  p.vec = vec < 0 ? reg_vec(M, K, nullptr) : vec;
   p.smem = make_layout(M * K, 0, kRowsPerStage * kc, p.stages).total;
   MRI_DISPATCH_M(M, {
-    cudaError_t e = set_smem(gemv_i8_tma_kernel<kM>, p.smem, dev.device);
-    if (e != cudaSuccess) return e;
-    p.resident = resident_ctas(gemv_i8_tma_kernel<kM>, p.smem, dev.device);
+    MRI_DISPATCH_VEC(p.vec, {
+      cudaError_t e = set_smem(gemv_i8_tma_kernel<kM, kV>, p.smem, dev.device);
+      if (e != cudaSuccess) return e;
+      p.resident = resident_ctas(gemv_i8_tma_kernel<kM, kV>, p.smem, dev.device);
+    });
   });
   p.ctas_per_sm = std::min(cfg.ctas_per_sm, p.resident);
   p.grid = stream_grid(dev, N, p.ctas_per_sm);
@@ -1056,12 +1109,15 @@ cudaError_t launch_gemv_i8_tma(const DeviceInfo& dev, cudaStream_t st, int M, co
     e_args = *epi;
   }
   GemvPlan p;
-  if (cudaError_t e = gemv_i8_tma_plan(dev, M, N, K, &p)) return e;
+  if (cudaError_t e = gemv_i8_tma_plan(dev, M, N, K, &p, reg_vec(M, K, &act))) return e;
+  const int pre = pre_stages(p.stages);
   MRI_DISPATCH_M(M, {
-    cudaError_t e = launch_stream_kernel(gemv_i8_tma_kernel<kM>, p.grid, p.smem, st, W, w_scales, N, K,
-                                         act, out, acc_out, p.stages, p.k_chunks, status, residual,
-                                         e_args);
-    if (e != cudaSuccess) return e;
+    MRI_DISPATCH_VEC(p.vec, {
+      cudaError_t e = launch_stream_kernel(gemv_i8_tma_kernel<kM, kV>, p.grid, p.smem, st, W, w_scales,
+                                           N, K, act, out, acc_out, p.stages, p.k_chunks, pre, status,
+                                           residual, e_args);
+      if (e != cudaSuccess) return e;
+    });
   });
   if (ls) ls->launches++;
   return cudaGetLastError();

@@ -96,10 +96,12 @@ bool gemv_i8_tma_supported(const DeviceInfo& dev, int M, size_t K);
 // residual (nullable): out = residual + product, element-wise (may alias out).
 // Launch shape the INT8 streaming GEMV uses for (M, N, K).
 struct GemvPlan {
-  int grid = 0, ctas_per_sm = 0, resident = 0, stages = 0, k_chunks = 0;
+  int grid = 0, ctas_per_sm = 0, resident = 0, stages = 0, k_chunks = 0, vec = 0;
   size_t smem = 0;
 };
-cudaError_t gemv_i8_tma_plan(const DeviceInfo& dev, int M, size_t N, size_t K, GemvPlan* plan);
+// vec < 0: the register-path width of a plain per-tensor f32 input.
+cudaError_t gemv_i8_tma_plan(const DeviceInfo& dev, int M, size_t N, size_t K, GemvPlan* plan,
+                             int vec = -1);
 // epi (nullable): a pair epilogue (EpiArgs); not combined with residual or acc_out.
 cudaError_t launch_gemv_i8_tma(const DeviceInfo& dev, cudaStream_t st, int M, const int8_t* W,
                                const float* w_scales, size_t N, size_t K, const ActArgs& act,

@@ -7,8 +7,8 @@ INT8 quantization -> W int8 [N=11008, K=4096] per-channel GEMV -> f32
 [1,11008].  metric = weight GB/s (45,088,768 int8 weight bytes per call).
 
   step     = 256 independent decode-projection calls (256 distinct activation
-             vectors), replayed from one CUDA graph; weights rotate over 6
-             device copies (270 MB > 2x the 126 MB L2) so every call streams
+             vectors), replayed from one CUDA graph; weights rotate over 16
+             device copies (721 MB, 5.7x the 126 MB L2) so every call streams
              its weights from HBM.
   value    = weight bytes of all calls on all ranks / max-over-ranks time.
   e2e      = the same calls through the host-buffer C-ABI drop-in
@@ -44,7 +44,7 @@ K_DIM, N_DIM = 4096, 11008
 WEIGHT_BYTES = N_DIM * K_DIM                          # int8 weights per call
 ALG_BYTES = WEIGHT_BYTES + 4 * N_DIM + K_DIM * 4 + 4 * N_DIM  # + scales + x f32 + out f32
 CALLS_PER_STEP = 256
-WEIGHT_COPIES = 6
+WEIGHT_COPIES = 16
 REF_CALLS_PER_STEP = 4
 
 THROTTLE_BITS = {0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",

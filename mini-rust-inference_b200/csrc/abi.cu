@@ -210,7 +210,7 @@ int mri::matmul_int8_act(::mri_ctx* ctx, const ActArgs& act, const ::mri_qmatrix
 }
 
 bool mri::matmul_int8_epilogue_supported(const ::mri_ctx* ctx, size_t m, const ::mri_qmatrix* w) {
-  return ctx && w && w->n_out % 2 == 0 && stream_gemv_applies(ctx, m, w);
+  return ctx && w && m == 1 && w->n_out % 2 == 0 && stream_gemv_applies(ctx, m, w);
 }
 
 int mri::matmul_int8_fused(::mri_ctx* ctx, const float* x, size_t m, size_t k, const float* norm_w,
@@ -225,7 +225,8 @@ int mri::matmul_int8_fused(::mri_ctx* ctx, const float* x, size_t m, size_t k, c
   a.norm_w = norm_w;
   a.eps = eps;
   a.swiglu = swiglu;
-  if (epi && (residual || w->n_out % 2)) return fail(MRI_ERR_INVALID_ARGUMENT, "pair epilogue needs even N and no residual");
+  if (epi && (residual || w->n_out % 2 || m != 1))
+    return fail(MRI_ERR_INVALID_ARGUMENT, "pair epilogue needs one row, even N and no residual");
   return run_int8(ctx, a, w, m, out, nullptr, residual, epi);
 }
 

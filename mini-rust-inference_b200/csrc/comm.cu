@@ -25,6 +25,7 @@
 #include <string>
 #include <thread>
 
+#include "common.cuh"
 #include "internal.h"
 #include "mri_gpu.h"
 
@@ -137,7 +138,7 @@ __global__ void unshard_kernel(const float* __restrict__ g, int P, size_t rows, 
     const size_t ns4 = ns / 4, w4 = width / 4;
     for (size_t t = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; t < total / 4; t += stride) {
       const size_t i = t / w4, c = t - i * w4, p = c / ns4, j = c - p * ns4;
-      const float4 v = __ldg(reinterpret_cast<const float4*>(g + (p * rows + i) * ns) + j);
+      const float4 v = mri::ld_act(reinterpret_cast<const float4*>(g + (p * rows + i) * ns) + j);
       reinterpret_cast<float4*>(out + i * ld)[c] = v;
     }
   } else {

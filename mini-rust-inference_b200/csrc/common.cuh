@@ -93,6 +93,15 @@ __device__ __forceinline__ uint64_t l2_policy_evict_first() {
   return p;
 }
 
+// Loads of data that an earlier kernel in the stream wrote (activations, the
+// KV cache, gathered slices).  Kernels here start early under programmatic
+// dependent launch, so the SM's L1 can hold lines of these buffers from
+// before the producer kernel rewrote them; the non-coherent read-only path
+// (ld.global.nc) could return such stale lines.  These loads are cached in
+// L2 only.
+template <typename T>
+__device__ __forceinline__ T ld_act(const T* p) { return __ldcg(p); }
+
 // Named barrier among `threads` threads (ids 1..15; 0 is __syncthreads).
 __device__ __forceinline__ void named_bar_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");

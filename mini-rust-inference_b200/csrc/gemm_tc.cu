@@ -249,7 +249,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       tc_fence_after();
       const int m_blk = tile % m_tiles, n_blk = tile / m_tiles;
       const int row = m_blk * BM + q * 32 + lane;
-      const float s_a = scale_per_row ? (row < M ? act_scale[row] : 0.0f) : act_scale[0];
+      const float s_a = scale_per_row ? (row < M ? ld_act(act_scale + row) : 0.0f) : ld_act(act_scale);
       float* orow = out + static_cast<size_t>(row) * N;
       // forward_int8.rs:100-121: x + projected; residual may alias out.
       const float* rrow = residual ? residual + static_cast<size_t>(row) * N : nullptr;
@@ -274,7 +274,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
               o.z = rescale(static_cast<int>(v[j + 2]), s_a, sw.z);
               o.w = rescale(static_cast<int>(v[j + 3]), s_a, sw.w);
               if (rrow) {
-                const float4 r = *reinterpret_cast<const float4*>(rrow + col0 + j);
+                const float4 r = ld_act(reinterpret_cast<const float4*>(rrow + col0 + j));
                 o.x = __fadd_rn(r.x, o.x);
                 o.y = __fadd_rn(r.y, o.y);
                 o.z = __fadd_rn(r.z, o.z);
@@ -292,7 +292,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
               const int col = col0 + j;
               if (col < N) {
                 const float val = rescale(static_cast<int>(v[j]), s_a, __ldg(w_scales + col));
-                orow[col] = rrow ? __fadd_rn(rrow[col], val) : val;
+                orow[col] = rrow ? __fadd_rn(ld_act(rrow + col), val) : val;
                 if (arow) arow[col] = static_cast<int>(v[j]);
               }
             }

@@ -172,11 +172,11 @@ struct ActView {
   __device__ __forceinline__ float4 get(int r, size_t k) const {
     const float* row = x + r * ld;
     if (swiglu) {
-      const float4 a = __ldg(reinterpret_cast<const float4*>(row + 2 * k));
-      const float4 b = __ldg(reinterpret_cast<const float4*>(row + 2 * k + 4));
+      const float4 a = ld_act(reinterpret_cast<const float4*>(row + 2 * k));
+      const float4 b = ld_act(reinterpret_cast<const float4*>(row + 2 * k + 4));
       return make_float4(swiglu1(a.x, a.y), swiglu1(a.z, a.w), swiglu1(b.x, b.y), swiglu1(b.z, b.w));
     }
-    float4 v = __ldg(reinterpret_cast<const float4*>(row + k));
+    float4 v = ld_act(reinterpret_cast<const float4*>(row + k));
     if (w) v = norm(v, r, k);
     return v;
   }
@@ -222,7 +222,7 @@ __device__ void load_act_i8_rowmajor(const ActArgs& act, size_t K, int8_t* s_act
 #pragma unroll
     for (int j = 0; j < VEC; ++j) {
       const int i = ct + j * kConsumerThreads;
-      x4[j] = i < n4 ? __ldg(reinterpret_cast<const float4*>(act.x) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      x4[j] = i < n4 ? ld_act(reinterpret_cast<const float4*>(act.x) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     if (act_issued) {
       __syncwarp();
@@ -277,7 +277,7 @@ __device__ void load_act_i8_rowmajor(const ActArgs& act, size_t K, int8_t* s_act
           const float* row = act.x + r * K;
           float ss = 0.0f;
           for (size_t i = ct; i < K / 4; i += kConsumerThreads) {
-            const float4 t = __ldg(reinterpret_cast<const float4*>(row) + i);
+            const float4 t = ld_act(reinterpret_cast<const float4*>(row) + i);
             ss = __fmaf_rn(t.x, t.x, ss);
             ss = __fmaf_rn(t.y, t.y, ss);
             ss = __fmaf_rn(t.z, t.z, ss);
@@ -311,7 +311,7 @@ __device__ void load_act_i8_rowmajor(const ActArgs& act, size_t K, int8_t* s_act
         const size_t lo = act.mode == ACT_F32_PER_ROW ? r * K : 0;
         const size_t hi = act.mode == ACT_F32_PER_ROW ? lo + K : total;
         float m = 0.0f;
-        for (size_t i = lo + ct; i < hi; i += kConsumerThreads) m = absmax_acc(m, __ldg(x + i));
+        for (size_t i = lo + ct; i < hi; i += kConsumerThreads) m = absmax_acc(m, ld_act(x + i));
         const float scale = sym_scale(consumer_max(m, red));
         const float inv = __fdiv_rn(1.0f, scale);
         if (act.mode == ACT_F32_PER_ROW) {
@@ -319,21 +319,21 @@ __device__ void load_act_i8_rowmajor(const ActArgs& act, size_t K, int8_t* s_act
         } else if (ct < M) {
           s_scale[ct] = scale;
         }
-        for (size_t i = lo + ct; i < hi; i += kConsumerThreads) s_act[i] = sym_quant(__ldg(x + i), inv);
+        for (size_t i = lo + ct; i < hi; i += kConsumerThreads) s_act[i] = sym_quant(ld_act(x + i), inv);
       }
     }
   } else {
     const int8_t* xq = act.xq;
     if ((reinterpret_cast<uintptr_t>(xq) & 15) == 0 && (total % 16) == 0) {
       for (size_t i = ct; i < total / 16; i += kConsumerThreads)
-        reinterpret_cast<uint4*>(s_act)[i] = __ldg(reinterpret_cast<const uint4*>(xq) + i);
+        reinterpret_cast<uint4*>(s_act)[i] = ld_act(reinterpret_cast<const uint4*>(xq) + i);
     } else {
       for (size_t i = ct; i < total; i += kConsumerThreads) s_act[i] = xq[i];
     }
     if (ct < M) {
       if (act.mode == ACT_I8_HOST_SCALE) s_scale[ct] = act.scale_host;
-      else if (act.mode == ACT_I8_DEV_SCALE) s_scale[ct] = act.scale_dev[0];
-      else s_scale[ct] = act.scale_dev[ct];
+      else if (act.mode == ACT_I8_DEV_SCALE) s_scale[ct] = ld_act(act.scale_dev);
+      else s_scale[ct] = ld_act(act.scale_dev + ct);
     }
   }
   named_bar_sync(1, kConsumerThreads);
@@ -346,6 +346,7 @@ __device__ void load_act_i8_rowmajor(const ActArgs& act, size_t K, int8_t* s_act
 // copied row by row, and a warp keeps its row's INT32 partial sums in
 // registers across the chunks (integer sums: the split is exact).
 
+template <bool CHUNK>
 __device__ void stream_producer_i8(const int8_t* W, size_t K, size_t kc, int nk, size_t begin,
                                    size_t end, uint64_t* full, uint64_t* empty, uint8_t* stages_base,
                                    size_t stage_stride, int n_stages, int* status,
@@ -365,7 +366,7 @@ __device__ void stream_producer_i8(const int8_t* W, size_t K, size_t kc, int nk,
     const size_t r0 = begin + static_cast<size_t>(g) * kRowsPerStage;
     const size_t nrows = std::min<size_t>(kRowsPerStage, end - r0);
     uint8_t* dst = stages_base + s * stage_stride;
-    if (nk == 1) {
+    if constexpr (!CHUNK) {
       const uint32_t bytes = static_cast<uint32_t>(nrows * K);
       mbar_arrive_expect_tx(&full[s], bytes);
       bulk_copy_g2s_stream(dst, W + r0 * K, bytes, &full[s], policy);
@@ -399,7 +400,7 @@ __device__ __forceinline__ void pair_epilogue(const EpiArgs& epi, int M, size_t 
     return;
   }
   const int r = static_cast<int>(row);
-  const int pos = (epi.pos_dev ? *epi.pos_dev : epi.pos0) + m;
+  const int pos = (epi.pos_dev ? ld_act(epi.pos_dev) : epi.pos0) + m;
   const int qk = epi.qd + epi.kvd;
   float y = val;
   if (r < qk) {
@@ -415,7 +416,9 @@ __device__ __forceinline__ void pair_epilogue(const EpiArgs& epi, int M, size_t 
   else if (r >= qk) epi.vc[static_cast<size_t>(pos) * epi.kvd + (r - qk)] = y;
 }
 
-template <int M, int VEC>
+// CHUNK: rows may be split into nk K-chunks; EPI: pair epilogue (epi.mode).
+// Both are compile-time so the plain decode kernel carries neither.
+template <int M, int VEC, bool CHUNK, bool EPI>
 __global__ void __launch_bounds__(kThreads, M <= 2 ? 2 : 1)
     gemv_i8_tma_kernel(const int8_t* __restrict__ W, const float* __restrict__ w_scales, size_t N,
                        size_t K, ActArgs act, float* out, int32_t* __restrict__ acc_out,
@@ -423,7 +426,8 @@ __global__ void __launch_bounds__(kThreads, M <= 2 ? 2 : 1)
                        EpiArgs epi) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ float s_pair[2][kConsumerWarps][8];
-  const size_t kc = nk == 1 ? K : align_up((K + nk - 1) / nk, 16);
+  if constexpr (!CHUNK) nk = 1;
+  const size_t kc = CHUNK ? align_up((K + nk - 1) / nk, 16) : K;
   const StreamLayout L = make_layout(M * K, 0, kRowsPerStage * kc, n_stages);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
   uint64_t* empty = full + n_stages;
@@ -434,7 +438,7 @@ __global__ void __launch_bounds__(kThreads, M <= 2 ? 2 : 1)
 
   size_t begin, end;
   // Pair epilogues need both rows of a pair in the same CTA and stage.
-  cta_rows(N, epi.mode != EPI_NONE ? 2 : 1, begin, end);
+  cta_rows(N, EPI ? 2 : 1, begin, end);
   uint64_t* act_issued = empty + n_stages;
   init_barriers(full, empty, n_stages, act_issued);
   if (begin >= end) return;
@@ -442,7 +446,7 @@ __global__ void __launch_bounds__(kThreads, M <= 2 ? 2 : 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (warp == 0) {
     if (lane == 0)
-      stream_producer_i8(W, K, kc, nk, begin, end, full, empty, stage0, L.stage_bytes, n_stages,
+      stream_producer_i8<CHUNK>(W, K, kc, nk, begin, end, full, empty, stage0, L.stage_bytes, n_stages,
                          status, act_issued, pre);
     return;
   }
@@ -501,11 +505,11 @@ __global__ void __launch_bounds__(kThreads, M <= 2 ? 2 : 1)
       for (int m = 0; m < M; ++m)
         if (lane == m) val = rescale(acc[m], s_a[m], sw);
     }
-    if (epi.mode != EPI_NONE) {
+    if constexpr (EPI) {
       pair_epilogue(epi, M, N, row, valid, val, lane, cw, g, s_pair, out);
     } else if (valid && lane < M) {
       // forward_int8.rs:100-121: x + projected (residual may alias out).
-      out[lane * N + row] = residual ? __fadd_rn(residual[lane * N + row], val) : val;
+      out[lane * N + row] = residual ? __fadd_rn(ld_act(residual + lane * N + row), val) : val;
       if (acc_out) {
 #pragma unroll
         for (int m = 0; m < M; ++m)
@@ -529,8 +533,8 @@ __global__ void __launch_bounds__(256) gemv_i8_generic_kernel(const int8_t* __re
 #pragma unroll
   for (int m = 0; m < M; ++m)
     s_a[m] = act.mode == ACT_I8_HOST_SCALE ? act.scale_host
-             : act.mode == ACT_I8_DEV_SCALE ? act.scale_dev[0]
-                                            : act.scale_dev[m];
+             : act.mode == ACT_I8_DEV_SCALE ? ld_act(act.scale_dev)
+                                            : ld_act(act.scale_dev + m);
   for (size_t row = static_cast<size_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
        row < N; row += warps) {
     const int8_t* wr = W + row * K;
@@ -781,10 +785,10 @@ __global__ void __launch_bounds__(kThreads, M <= 2 ? 2 : 1)
   for (size_t i = ct; i < static_cast<size_t>(M) * K / 4; i += kConsumerThreads) {
     const size_t r = (i * 4) / K, k = (i * 4) % K;
     float4 v;
-    v.x = __ldg(x + r * K + k);
-    v.y = __ldg(x + r * K + k + 1);
-    v.z = __ldg(x + r * K + k + 2);
-    v.w = __ldg(x + r * K + k + 3);
+    v.x = ld_act(x + r * K + k);
+    v.y = ld_act(x + r * K + k + 1);
+    v.z = ld_act(x + r * K + k + 2);
+    v.w = ld_act(x + r * K + k + 3);
     s_x4[(r * 8 + (k % 32) / 4) * nb + k / 32] = v;
   }
   named_bar_sync(1, kConsumerThreads);
@@ -864,8 +868,8 @@ __global__ void __launch_bounds__(256) gemv_q4_0_generic_kernel(const uint8_t* _
         const float hi = __fmul_rn(d, static_cast<float>(static_cast<int>(byte >> 4) - 8));
 #pragma unroll
         for (int m = 0; m < M; ++m) {
-          acc[m] = __fmaf_rn(__ldg(x + m * K + b * 32 + 2 * j), lo, acc[m]);
-          acc[m] = __fmaf_rn(__ldg(x + m * K + b * 32 + 2 * j + 1), hi, acc[m]);
+          acc[m] = __fmaf_rn(ld_act(x + m * K + b * 32 + 2 * j), lo, acc[m]);
+          acc[m] = __fmaf_rn(ld_act(x + m * K + b * 32 + 2 * j + 1), hi, acc[m]);
         }
       }
     }
@@ -1065,18 +1069,37 @@ int reg_vec(int M, size_t K, const ActArgs* act) {
     default: { constexpr int kV = 0; __VA_ARGS__; } break;    \
   }
 
+// The INT8 stream kernel for (M, VEC, CHUNK, EPI) as `kKernel`.  The pair
+// epilogue exists for M = 1 only (the decode step).
+#define MRI_DISPATCH_I8_TMA(M, V, CH, EP, ...)                                              \
+  if (EP) {                                                                                 \
+    MRI_DISPATCH_VEC(V, {                                                                   \
+      if (CH) { auto kKernel = gemv_i8_tma_kernel<1, kV, true, true>; __VA_ARGS__; }         \
+      else { auto kKernel = gemv_i8_tma_kernel<1, kV, false, true>; __VA_ARGS__; }           \
+    });                                                                                     \
+  } else {                                                                                  \
+    MRI_DISPATCH_M(M, {                                                                     \
+      MRI_DISPATCH_VEC(V, {                                                                 \
+        if (CH) { auto kKernel = gemv_i8_tma_kernel<kM, kV, true, false>; __VA_ARGS__; }     \
+        else { auto kKernel = gemv_i8_tma_kernel<kM, kV, false, false>; __VA_ARGS__; }       \
+      });                                                                                   \
+    });                                                                                     \
+  }
+
 // Weight stages a producer issues before the activation loads are in flight
-// (MRI_GEMV_PRE_STAGES; default all).
+// (MRI_GEMV_PRE_STAGES; default 1: the activation loads of a decode step then
+// queue behind one stage per CTA instead of the whole ring).
 int pre_stages(int stages) {
   static const int v = [] {
     const char* e = std::getenv("MRI_GEMV_PRE_STAGES");
-    return e ? std::max(0, std::atoi(e)) : 1 << 20;
+    return e ? std::max(0, std::atoi(e)) : 1;
   }();
   return std::min(v, stages);
 }
 
 cudaError_t gemv_i8_tma_plan(const DeviceInfo& dev, int M, size_t N, size_t K, GemvPlan* plan,
-                             int vec) {
+                             int vec, bool epi) {
+  if (epi && M != 1) return cudaErrorInvalidValue;
   StreamConfig cfg;
   const int nk = i8_chunks(M, K, &cfg);
   if (nk == 0 || M < 1 || M > 8) return cudaErrorInvalidValue;
@@ -1086,12 +1109,11 @@ cudaError_t gemv_i8_tma_plan(const DeviceInfo& dev, int M, size_t N, size_t K, G
   p.k_chunks = nk;
   p.vec = vec < 0 ? reg_vec(M, K, nullptr) : vec;
   p.smem = make_layout(M * K, 0, kRowsPerStage * kc, p.stages).total;
-  MRI_DISPATCH_M(M, {
-    MRI_DISPATCH_VEC(p.vec, {
-      cudaError_t e = set_smem(gemv_i8_tma_kernel<kM, kV>, p.smem, dev.device);
-      if (e != cudaSuccess) return e;
-      p.resident = resident_ctas(gemv_i8_tma_kernel<kM, kV>, p.smem, dev.device);
-    });
+  p.epi = epi;
+  MRI_DISPATCH_I8_TMA(M, p.vec, nk > 1, epi, {
+    cudaError_t e = set_smem(kKernel, p.smem, dev.device);
+    if (e != cudaSuccess) return e;
+    p.resident = resident_ctas(kKernel, p.smem, dev.device);
   });
   p.ctas_per_sm = std::min(cfg.ctas_per_sm, p.resident);
   p.grid = stream_grid(dev, N, p.ctas_per_sm);
@@ -1109,15 +1131,12 @@ cudaError_t launch_gemv_i8_tma(const DeviceInfo& dev, cudaStream_t st, int M, co
     e_args = *epi;
   }
   GemvPlan p;
-  if (cudaError_t e = gemv_i8_tma_plan(dev, M, N, K, &p, reg_vec(M, K, &act))) return e;
+  if (cudaError_t e = gemv_i8_tma_plan(dev, M, N, K, &p, reg_vec(M, K, &act), epi != nullptr)) return e;
   const int pre = pre_stages(p.stages);
-  MRI_DISPATCH_M(M, {
-    MRI_DISPATCH_VEC(p.vec, {
-      cudaError_t e = launch_stream_kernel(gemv_i8_tma_kernel<kM, kV>, p.grid, p.smem, st, W, w_scales,
-                                           N, K, act, out, acc_out, p.stages, p.k_chunks, pre, status,
-                                           residual, e_args);
-      if (e != cudaSuccess) return e;
-    });
+  MRI_DISPATCH_I8_TMA(M, p.vec, p.k_chunks > 1, p.epi, {
+    cudaError_t e = launch_stream_kernel(kKernel, p.grid, p.smem, st, W, w_scales, N, K, act, out,
+                                         acc_out, p.stages, p.k_chunks, pre, status, residual, e_args);
+    if (e != cudaSuccess) return e;
   });
   if (ls) ls->launches++;
   return cudaGetLastError();

@@ -97,11 +97,12 @@ bool gemv_i8_tma_supported(const DeviceInfo& dev, int M, size_t K);
 // Launch shape the INT8 streaming GEMV uses for (M, N, K).
 struct GemvPlan {
   int grid = 0, ctas_per_sm = 0, resident = 0, stages = 0, k_chunks = 0, vec = 0;
+  bool epi = false;
   size_t smem = 0;
 };
 // vec < 0: the register-path width of a plain per-tensor f32 input.
 cudaError_t gemv_i8_tma_plan(const DeviceInfo& dev, int M, size_t N, size_t K, GemvPlan* plan,
-                             int vec = -1);
+                             int vec = -1, bool epi = false);
 // epi (nullable): a pair epilogue (EpiArgs); not combined with residual or acc_out.
 cudaError_t launch_gemv_i8_tma(const DeviceInfo& dev, cudaStream_t st, int M, const int8_t* W,
                                const float* w_scales, size_t N, size_t K, const ActArgs& act,
@@ -134,8 +135,9 @@ cudaError_t launch_gemv_q4_0_generic(const DeviceInfo& dev, cudaStream_t st, int
 // INT8 product of an f32 [m, k] input with per-tensor quantization and the
 // optional fused producer ops of ActArgs (RMSNorm or SwiGLU; for SwiGLU the
 // input rows are 2k wide) and residual epilogue.  `epi` (nullable) selects a
-// pair epilogue; it is only available on the streaming GEMV path
-// (matmul_int8_epilogue_supported).  Status code as the C ABI.
+// pair epilogue; it is only available for one activation row on the
+// streaming GEMV path (matmul_int8_epilogue_supported).  Status code as the
+// C ABI.
 int matmul_int8_fused(struct ::mri_ctx* ctx, const float* x, size_t m, size_t k,
                       const float* norm_w, float eps, int swiglu,
                       const struct ::mri_qmatrix* w, const float* residual, float* out,

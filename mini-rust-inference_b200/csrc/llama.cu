@@ -26,6 +26,7 @@
 #include <utility>
 #include <cstdio>
 #include <cstring>
+#include <cstdlib>
 #include <string>
 #include <vector>
 
@@ -55,7 +56,7 @@ __global__ void embed_kernel(const uint32_t* __restrict__ tokens, const float* _
                              int d, float* __restrict__ x) {
   pdl_trigger();
   pdl_wait();
-  const uint32_t tok = tokens[blockIdx.x];
+  const uint32_t tok = mri::ld_act(tokens + blockIdx.x);
   const float* src = embd + static_cast<size_t>(tok) * d;
   float* dst = x + static_cast<size_t>(blockIdx.x) * d;
   for (int i = threadIdx.x; i < d; i += blockDim.x) dst[i] = src[i];
@@ -73,14 +74,14 @@ __global__ void rope_kv_kernel(float* __restrict__ qkv, int ld, int n_heads, int
   pdl_trigger();
   pdl_wait();
   const int i = blockIdx.x, h = blockIdx.y;
-  const int pos = (pos_dev ? *pos_dev : pos0) + i;
+  const int pos = (pos_dev ? mri::ld_act(pos_dev) : pos0) + i;
   const int half = hd / 2;
   float* row = qkv + static_cast<size_t>(i) * ld;
   const int kvd = n_kv * hd, qd = n_heads * hd;
   float* base = h < n_heads ? row + h * hd : row + qd + (h - n_heads) * hd;
   for (int j = threadIdx.x; j < half; j += blockDim.x) {
     const float c = cos_t[pos * half + j], sn = sin_t[pos * half + j];
-    const float x0 = base[2 * j], x1 = base[2 * j + 1];
+    const float x0 = mri::ld_act(base + 2 * j), x1 = mri::ld_act(base + 2 * j + 1);
     const float y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
     const float y1 = __fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, sn));
     base[2 * j] = y0;
@@ -92,8 +93,8 @@ __global__ void rope_kv_kernel(float* __restrict__ qkv, int ld, int n_heads, int
       const float* vsrc = row + qd + kvd + kh * hd;
       krow[2 * j] = y0;
       krow[2 * j + 1] = y1;
-      vrow[2 * j] = vsrc[2 * j];
-      vrow[2 * j + 1] = vsrc[2 * j + 1];
+      vrow[2 * j] = mri::ld_act(vsrc + 2 * j);
+      vrow[2 * j + 1] = mri::ld_act(vsrc + 2 * j + 1);
     }
   }
 }
@@ -116,7 +117,7 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const float* __restric
   pdl_trigger();
   pdl_wait();
   const int h = blockIdx.x, s = blockIdx.y;
-  const int pos = *pos_dev;
+  const int pos = mri::ld_act(pos_dev);
   const int j0 = s * kAttnChunk;
   if (j0 > pos) return;
   const int active = pos / kAttnChunk + 1;
@@ -139,7 +140,7 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const float* __restric
   for (int i = 0; i < kV4; ++i) {
     const int idx = threadIdx.x + 128 * i;
     const int j = idx / hd4, d4 = idx - j * hd4;
-    v4[i] = j < nkeys ? __ldg(reinterpret_cast<const float4*>(vbase + static_cast<size_t>(j) * kvd) + d4)
+    v4[i] = j < nkeys ? mri::ld_act(reinterpret_cast<const float4*>(vbase + static_cast<size_t>(j) * kvd) + d4)
                       : make_float4(0.f, 0.f, 0.f, 0.f);
   }
   const int jk = threadIdx.x >> 1, half = threadIdx.x & 1;
@@ -148,9 +149,9 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const float* __restric
 #pragma unroll
   for (int i = 0; i < kMaxHeadDim / 8; ++i)
     k4[i] = (jk < nkeys && i < hh4)
-                ? __ldg(reinterpret_cast<const float4*>(kbase + static_cast<size_t>(jk) * kvd) + half * hh4 + i)
+                ? mri::ld_act(reinterpret_cast<const float4*>(kbase + static_cast<size_t>(jk) * kvd) + half * hh4 + i)
                 : make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int t = threadIdx.x; t < hd; t += blockDim.x) sq[t] = q[h * hd + t];
+  for (int t = threadIdx.x; t < hd; t += blockDim.x) sq[t] = mri::ld_act(q + h * hd + t);
   __syncthreads();
   float dot = 0.0f;
 #pragma unroll
@@ -358,7 +359,7 @@ __global__ void __launch_bounds__(256) argmax_kernel(const float* __restrict__ l
   const int lo = blockIdx.x * per, hi = min(V, lo + per);
   float best = -INFINITY;
   int idx = 0x7fffffff;
-  for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) better(best, idx, logits[i], i);
+  for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) better(best, idx, mri::ld_act(logits + i), i);
   block_argmax(best, idx, sb, si);
   if (threadIdx.x == 0) {
     part_v[blockIdx.x] = best;
@@ -377,9 +378,10 @@ __global__ void __launch_bounds__(256) argmax_kernel(const float* __restrict__ l
   block_argmax(best, idx, sb, si);
   if (threadIdx.x == 0) {
     const uint32_t t = static_cast<uint32_t>(idx == 0x7fffffff ? 0 : idx);
+    const int p = mri::ld_act(pos);
     *token = t;
-    gen[*pos + 1] = t;  // the token generated for position pos + 1
-    *pos += 1;
+    gen[p + 1] = t;  // the token generated for position pos + 1
+    *pos = p + 1;
     *ticket = 0;
   }
 }
@@ -515,7 +517,11 @@ cudaError_t pdl_launch(void (*k)(KArgs...), dim3 grid, dim3 block, cudaStream_t 
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  static const bool pdl_on = [] {
+    const char* e = std::getenv("MRI_PDL");
+    return !e || std::atoi(e) != 0;
+  }();
+  cfg.numAttrs = pdl_on ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, k, static_cast<KArgs>(args)...);
 }
 

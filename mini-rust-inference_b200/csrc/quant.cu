@@ -26,12 +26,12 @@ __global__ void __launch_bounds__(kQThreads) absmax_tensor_kernel(const float* _
     const size_t n4 = n / 4;
     const float4* x4 = reinterpret_cast<const float4*>(x);
     for (size_t j = i; j < n4; j += stride) {
-      const float4 v = __ldg(x4 + j);
+      const float4 v = ld_act(x4 + j);
       m = absmax_acc(absmax_acc(absmax_acc(absmax_acc(m, v.x), v.y), v.z), v.w);
     }
-    for (size_t j = n4 * 4 + i; j < n; j += stride) m = absmax_acc(m, __ldg(x + j));
+    for (size_t j = n4 * 4 + i; j < n; j += stride) m = absmax_acc(m, ld_act(x + j));
   } else {
-    for (size_t j = i; j < n; j += stride) m = absmax_acc(m, __ldg(x + j));
+    for (size_t j = i; j < n; j += stride) m = absmax_acc(m, ld_act(x + j));
   }
   m = warp_max(m);
   __shared__ float red[kQThreads / 32];
@@ -67,7 +67,7 @@ __global__ void __launch_bounds__(kQThreads) absmax_row_kernel(const float* __re
                                                                size_t k, float* amax) {
   const float* row = x + static_cast<size_t>(blockIdx.x) * k;
   float m = 0.0f;
-  for (size_t j = threadIdx.x; j < k; j += kQThreads) m = absmax_acc(m, __ldg(row + j));
+  for (size_t j = threadIdx.x; j < k; j += kQThreads) m = absmax_acc(m, ld_act(row + j));
   m = warp_max(m);
   __shared__ float red[kQThreads / 32];
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
@@ -95,7 +95,7 @@ __global__ void __launch_bounds__(kQThreads) quant_apply_kernel(const float* __r
     if ((reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(q) & 3) == 0) {
       const size_t n4 = n / 4;
       for (size_t j = tid; j < n4; j += stride) {
-        const float4 v = __ldg(reinterpret_cast<const float4*>(x) + j);
+        const float4 v = ld_act(reinterpret_cast<const float4*>(x) + j);
         char4 o;
         o.x = sym_quant(v.x, inv);
         o.y = sym_quant(v.y, inv);
@@ -103,16 +103,16 @@ __global__ void __launch_bounds__(kQThreads) quant_apply_kernel(const float* __r
         o.w = sym_quant(v.w, inv);
         reinterpret_cast<char4*>(q)[j] = o;
       }
-      for (size_t j = n4 * 4 + tid; j < n; j += stride) q[j] = sym_quant(__ldg(x + j), inv);
+      for (size_t j = n4 * 4 + tid; j < n; j += stride) q[j] = sym_quant(ld_act(x + j), inv);
     } else {
-      for (size_t j = tid; j < n; j += stride) q[j] = sym_quant(__ldg(x + j), inv);
+      for (size_t j = tid; j < n; j += stride) q[j] = sym_quant(ld_act(x + j), inv);
     }
   } else {
     for (size_t r = tid; r < m; r += stride) scale_out[r] = sym_scale(amax[r]);
     for (size_t j = tid; j < n; j += stride) {
       const size_t r = j / k;
       const float scale = sym_scale(amax[r]);
-      q[j] = sym_quant(__ldg(x + j), __fdiv_rn(1.0f, scale));
+      q[j] = sym_quant(ld_act(x + j), __fdiv_rn(1.0f, scale));
     }
   }
 }
@@ -123,11 +123,11 @@ __global__ void __launch_bounds__(kQThreads) quant_apply_kernel(const float* __r
 __device__ __forceinline__ float xform(const float* __restrict__ x, size_t k, size_t K, int r,
                                        const float* __restrict__ norm_w, float inv_r, int swiglu) {
   if (swiglu) {
-    const float g = __ldg(x + static_cast<size_t>(r) * 2 * K + 2 * k);
-    const float u = __ldg(x + static_cast<size_t>(r) * 2 * K + 2 * k + 1);
+    const float g = ld_act(x + static_cast<size_t>(r) * 2 * K + 2 * k);
+    const float u = ld_act(x + static_cast<size_t>(r) * 2 * K + 2 * k + 1);
     return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
   }
-  const float v = __ldg(x + static_cast<size_t>(r) * K + k);
+  const float v = ld_act(x + static_cast<size_t>(r) * K + k);
   return norm_w ? __fmul_rn(__ldg(norm_w + k), __fmul_rn(v, inv_r)) : v;
 }
 
@@ -143,7 +143,7 @@ __global__ void __launch_bounds__(kQThreads) row_stats_kernel(const float* __res
   if (norm_w) {
     float ss = 0.0f;
     for (size_t k = threadIdx.x; k < K; k += kQThreads) {
-      const float v = __ldg(x + static_cast<size_t>(r) * K + k);
+      const float v = ld_act(x + static_cast<size_t>(r) * K + k);
       ss = __fmaf_rn(v, v, ss);
     }
     ss = warp_sum_f(ss);

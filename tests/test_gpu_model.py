@@ -125,3 +125,20 @@ def test_larger_gqa_model_uses_gemm_and_matches(mri, oracle):
     for r in (0, 17, 39):
         assert rel_range_err(got[r], want[r]) < TOL, r
     assert rel_range_err(gpu.forward_decode(5, 40), ref.forward_decode(5, 40)) < TOL
+
+
+def test_decode_is_deterministic_at_scale(mri):
+    """Two greedy runs and two decodes of the same step agree bit for bit on a
+    model large enough that consecutive kernels overlap under programmatic
+    dependent launch (a kernel that read a buffer through a stale cache line
+    of its predecessor would make these differ)."""
+    cfg = mri.LlamaConfig(4, 2048, 16, 5632, 8000, 160)
+    m = mri.LlamaModelInt8.random(cfg, seed=3)
+    prompt = np.random.default_rng(1).integers(0, 8000, size=96).astype(np.uint32)
+    a, _, _ = m.generate_greedy(prompt, 24)
+    b, _, _ = m.generate_greedy(prompt, 24)
+    np.testing.assert_array_equal(a, b)
+    m.forward(prompt)
+    la = m.forward_decode(int(a[0]), 96)
+    lb = m.forward_decode(int(a[0]), 96)
+    np.testing.assert_array_equal(la, lb)

@@ -62,6 +62,8 @@ def parse_args():
                     help="skip the Q8_0 / Q4_0 / prefill side measurements")
     ap.add_argument("--no-cpu-baseline", action="store_true",
                     help="skip the timed CPU sample (profiling runs)")
+    ap.add_argument("--only", choices=["q8_0", "q4_0", "prefill", "model", "sharded"],
+                    help="run one side measurement alone and print it (profiling runs)")
     return ap.parse_args()
 
 
@@ -216,15 +218,18 @@ def time_graph(torch, stream, g, steps, warmup):
     return e0.elapsed_time(e1)
 
 
-def secondary_measurements(torch, mri, lib, device, peak_hbm, peak_tc):
-    """Q8_0 / Q4_0 decode (M=1, M=8) and the prefill GEMM, 1 GPU, each from a
-    CUDA graph over rotating weight copies."""
+SIDE_PARTS = ("q8_0", "q4_0", "prefill", "model")
+
+
+def secondary_measurements(torch, mri, lib, device, peak_hbm, peak_tc, parts=SIDE_PARTS):
+    """Q8_0 / Q4_0 decode (M=1, M=8), the prefill GEMM and the 7B model, 1 GPU;
+    the products from CUDA graphs over rotating weight copies."""
     res = {}
     rng = np.random.default_rng(0)
     wf = rng.normal(0, 0.02, size=(N_DIM, K_DIM)).astype(np.float32)
     s = torch.cuda.Stream(device)
     ctx = mri.Context(device, stream=s)
-    for fmt in ("q8_0", "q4_0"):
+    for fmt in [f for f in ("q8_0", "q4_0") if f in parts]:
         wb = mri.formats.quantize_q8_0(wf, N_DIM, K_DIM) if fmt == "q8_0" else \
             mri.formats.quantize_q4_0(wf, N_DIM, K_DIM)
         copies = max(3, int(np.ceil(300e6 / wb.size)))
@@ -254,6 +259,8 @@ def secondary_measurements(torch, mri, lib, device, peak_hbm, peak_tc):
         del ws
     # Prefill GEMM [512,4096] x [4096,11008]^T
     try:
+        if "prefill" not in parts:
+            raise LookupError
         M = 512
         wq = rng.integers(-127, 128, size=N_DIM * K_DIM, dtype=np.int8)
         wsc = rng.uniform(0.001, 0.02, size=N_DIM).astype(np.float32)
@@ -279,10 +286,13 @@ def secondary_measurements(torch, mri, lib, device, peak_hbm, peak_tc):
                                "roofline_frac_int8": round(tops / (2 * peak_tc), 4),
                                "int8_peak_note": "int8 dense peak taken as 2x measured bf16"}
         del g
+    except LookupError:
+        pass
     except Exception as e:  # noqa: BLE001 - side measurement only
         res["prefill_m512"] = {"error": str(e)[:200]}
     ctx.synchronize()
-    res["llama7b_int8"] = model_measurement(mri, device, peak_hbm)
+    if "model" in parts:
+        res["llama7b_int8"] = model_measurement(mri, device, peak_hbm)
     return res
 
 
@@ -420,6 +430,17 @@ def run_ours(args, rank, world, local_rank):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device(f"cuda:{device}"))
     peak_hbm, peak_tc, peak_kind = measured_peaks()
+    if args.only:
+        if args.only == "sharded":
+            out = sharded_measurement(torch, mri, device, world, dist, peak_hbm, peak_tc)
+        else:
+            out = secondary_measurements(torch, mri, lib, device, peak_hbm, peak_tc, parts=(args.only,))
+        if rank == 0:
+            print(json.dumps({"only": args.only, "n_gpus": world, "result": out}), flush=True)
+        if dist:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
 
     rng = np.random.default_rng(0)
     wq = rng.integers(-127, 128, size=N_DIM * K_DIM, dtype=np.int8)

@@ -42,6 +42,11 @@ constexpr int UMMA_K = 32;
 constexpr int kEpiWarps = 4;
 constexpr int kTcThreads = 32 * (2 + kEpiWarps);
 
+// TMEM columns between the two accumulator buffers: a power of two, so both
+// buffers start on an aligned column whatever the tile width.
+template <int BN>
+constexpr int acc_stride() { return BN <= 128 ? 128 : 256; }
+
 template <int BN, int kStages>
 struct TcLayout {
   static constexpr size_t a_bytes = BM * BK;
@@ -167,7 +172,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_addr(tmem_slot)),
-                 "r"(2 * BN)
+                 "r"(2 * acc_stride<BN>())
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -215,7 +220,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int b = t & 1;
         if (t >= 2 && !wait_or_abort(&tempty[b], ((t >> 1) - 1) & 1, status, abort_flag)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + b * BN;
+        const uint32_t d_tmem = tmem_base + b * acc_stride<BN>();
         for (int kb = 0; kb < kblocks; ++kb, ++it) {
           const int s = it % kStages;
           if (!wait_or_abort(&full[s], (it / kStages) & 1, status, abort_flag)) {
@@ -261,7 +266,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t v[32];
-        tmem_ld_32cols(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + b * BN + c * 32, v);
+        tmem_ld_32cols(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + b * acc_stride<BN>() + c * 32, v);
         const int col0 = n_blk * BN + c * 32;
         if (row < M) {
           if (vec && col0 + 32 <= N) {
@@ -309,7 +314,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
-                 "r"(2 * BN)
+                 "r"(2 * acc_stride<BN>())
                  : "memory");
   }
 }
@@ -365,17 +370,27 @@ bool pdl_enabled() {
 
 // Tile width: the one whose wave count times tile width is smallest (ties
 // go to the wider tile, which reads less shared memory per MAC).
+// Tile width: the BN (a multiple of 32 from 128 to 256; tcgen05 needs N % 16
+// == 0 at M = 128, the epilogue reads 32 TMEM columns at a time) that
+// minimises rounds-of-tiles x BN over the persistent grid, larger BN on ties
+// (fewer shared-memory bytes per MMA).  MRI_GEMM_BN overrides.
 int pick_bn(const DeviceInfo& dev, size_t M, size_t N) {
   if (const char* e = std::getenv("MRI_GEMM_BN")) {
     const int v = std::atoi(e);
-    if (v == 128 || v == 256) return v;
+    if (v >= 128 && v <= 256 && v % 32 == 0) return v;
   }
   const size_t mt = (M + BM - 1) / BM;
-  auto cost = [&](size_t bn) {
+  int best = 128;
+  size_t best_cost = ~size_t(0);
+  for (int bn = 256; bn >= 128; bn -= 32) {
     const size_t tiles = mt * ((N + bn - 1) / bn);
-    return ((tiles + dev.sm_count - 1) / dev.sm_count) * bn;
-  };
-  return cost(128) < cost(256) ? 128 : 256;
+    const size_t cost = ((tiles + dev.sm_count - 1) / dev.sm_count) * bn;
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = bn;
+    }
+  }
+  return best;
 }
 
 template <int BN, int kStages>
@@ -383,6 +398,7 @@ cudaError_t launch_bn(const DeviceInfo& dev, cudaStream_t st, const CUtensorMap&
                       const CUtensorMap& tb, const float* act_scale, int per_row,
                       const float* w_scales, size_t M, size_t N, size_t K, float* out,
                       int32_t* acc_out, int* status, const float* residual) {
+  static_assert(TcLayout<BN, kStages>::total <= 232448, "stage ring exceeds the per-CTA shared memory");
   const size_t smem = TcLayout<BN, kStages>::total;
   cudaError_t e = set_smem_tc(gemm_i8_tc_kernel<BN, kStages>, smem, dev.device);
   if (e != cudaSuccess) return e;
@@ -421,11 +437,23 @@ cudaError_t launch_gemm_i8_tc(const DeviceInfo& dev, cudaStream_t st, const int8
   const int bn = pick_bn(dev, M, N);
   CUtensorMap ta, tb;
   if (!make_map(&ta, xq, M, K, BM) || !make_map(&tb, W, N, K, bn)) return cudaErrorInvalidValue;
-  // Four 48 KB stages (BN=256) or six 32 KB stages (BN=128): 192 KB either way.
-  cudaError_t e = bn == 128 ? launch_bn<128, 6>(dev, st, ta, tb, act_scale_dev, scale_per_row,
-                                                w_scales, M, N, K, out, acc_out, status, residual)
-                            : launch_bn<256, 4>(dev, st, ta, tb, act_scale_dev, scale_per_row,
-                                                w_scales, M, N, K, out, acc_out, status, residual);
+  // Stage counts keep the ring within the 227 KB a CTA may use.
+  cudaError_t e;
+#define MRI_GEMM_BN_CASE(BNV, ST)                                                              \
+  case BNV:                                                                                    \
+    e = launch_bn<BNV, ST>(dev, st, ta, tb, act_scale_dev, scale_per_row, w_scales, M, N, K, out, \
+                           acc_out, status, residual);                                         \
+    break;
+  switch (bn) {
+    MRI_GEMM_BN_CASE(128, 6)
+    MRI_GEMM_BN_CASE(160, 6)
+    MRI_GEMM_BN_CASE(192, 5)
+    MRI_GEMM_BN_CASE(224, 5)
+    default:
+      e = launch_bn<256, 4>(dev, st, ta, tb, act_scale_dev, scale_per_row, w_scales, M, N, K, out,
+                            acc_out, status, residual);
+  }
+#undef MRI_GEMM_BN_CASE
   if (ls) ls->launches++;
   return e;
 }

@@ -281,6 +281,24 @@ def test_prefill_shape_sampled_rows_exact(mri, oracle, gpu_ctx):
     assert np.array_equal(bits(got[rows]), bits(want))
 
 
+@pytest.mark.parametrize("bn", [128, 160, 192, 224, 256])
+def test_gemm_tile_widths_exact(mri, oracle, gpu_ctx, monkeypatch, bn):
+    """Every tensor-core tile width (MRI_GEMM_BN) gives the oracle's INT32
+    sums and f32 outputs on ragged M and N, with a residual-free epilogue."""
+    monkeypatch.setenv("MRI_GEMM_BN", str(bn))
+    rng = np.random.default_rng(100 + bn)
+    m, n, k = 333, 1000, 4096 + 256
+    aq = rng.integers(-127, 128, size=m * k, dtype=np.int8)
+    wq = rng.integers(-127, 128, size=n * k, dtype=np.int8)
+    ws = rng.uniform(0.001, 0.02, size=n).astype(np.float32)
+    qm = mri.QuantizedMatrix(wq, ws, n, k)
+    acc = np.zeros((m, n), np.int32)
+    got = mri.matmul_int8(aq, np.float32(0.0123), qm, m, acc_out=acc)
+    want, want_acc = oracle.matmul_int8(aq, np.float32(0.0123), wq, ws, n, k, m)
+    assert np.array_equal(acc, want_acc)
+    assert np.array_equal(bits(got), bits(want))
+
+
 def test_device_status_clean(mri, gpu_ctx):
     """No bounded device-side wait gave up during the tests above."""
     gpu_ctx.check_device_status()

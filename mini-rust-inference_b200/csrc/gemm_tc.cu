@@ -16,9 +16,15 @@
 //                 one lane issues tcgen05.mma (M=128, N=BN, K=32 per
 //                 instruction) and tcgen05.commit's stage releases and
 //                 "accumulator ready" signals to mbarriers.
-//   warps 2..5  : epilogue.  tcgen05.ld of their 32-lane TMEM quarter,
-//                 rescale, vectorised f32 stores; the other accumulator
-//                 buffer is being filled meanwhile.
+//   warps 2..5  : epilogue.  While a tile's MMAs run they stage its weight
+//                 scales in shared memory; then tcgen05.ld of their 32-lane
+//                 TMEM quarter (a thread per row), rescale, vectorised f32
+//                 stores; the other accumulator buffer is being filled
+//                 meanwhile.  (Scales read from global memory inside the
+//                 chunk loop cost one L2 round trip per 4 columns there.)
+// The producer issues the weight tiles of its first stages before
+// griddepcontrol.wait (weights do not depend on the previous kernel) and the
+// activation tiles after it.
 // Every mbarrier wait is bounded; a timeout records MRI_ERR_TIMEOUT, raises
 // a CTA-wide abort flag, drains in-flight copies / MMAs, frees TMEM, returns.
 #include <cuda.h>
@@ -52,9 +58,12 @@ struct TcLayout {
   static constexpr size_t a_bytes = BM * BK;
   static constexpr size_t b_bytes = BN * BK;
   static constexpr size_t stage_bytes = a_bytes + b_bytes;
-  static constexpr size_t bars = kStages * stage_bytes;
-  // full[S], empty[S], tfull[2], tempty[2], mma_done, abort flag + tmem slot
-  static constexpr size_t bars_bytes = (2 * kStages + 5) * 8 + 16;
+  // Weight scales of the tile, one buffer per accumulator buffer.
+  static constexpr size_t epi = kStages * stage_bytes;
+  static constexpr size_t epi_bytes = 2 * 256 * 4;
+  static constexpr size_t bars = epi + epi_bytes;
+  // full[S], empty[S], tfull[2], tempty[2], sready[2], mma_done, abort flag + tmem slot
+  static constexpr size_t bars_bytes = (2 * kStages + 7) * 8 + 16;
   static constexpr size_t total = bars + bars_bytes + 1024;  // + alignment slack
 };
 
@@ -147,7 +156,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint64_t* empty = full + kStages;
   uint64_t* tfull = empty + kStages;
   uint64_t* tempty = tfull + 2;
-  uint64_t* mma_done = tempty + 2;
+  uint64_t* sready = tempty + 2;
+  uint64_t* mma_done = sready + 2;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(mma_done + 1);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1) + 1;
 
@@ -164,6 +174,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], kEpiWarps);
+      mbar_init(&sready[b], kEpiWarps);
     }
     mbar_init(mma_done, 1);
     *abort_flag = 0;
@@ -180,31 +191,42 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  // Programmatic dependent launch: let the next kernel start early, and read
-  // nothing a previous kernel may still be writing (activations, scales)
-  // before griddepcontrol.wait.  No-ops without the launch attribute.
+  // Programmatic dependent launch: let the next kernel start early.  Nothing
+  // a previous kernel may still be writing (activations, scales, residual) is
+  // read before griddepcontrol.wait: the producer waits after issuing the
+  // weight tiles of its first stages, the epilogue warps before their first
+  // global read.  The MMA warp reads only shared memory and TMEM.  No-ops
+  // without the launch attribute.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  asm volatile("griddepcontrol.wait;" ::: "memory");
 
   if (warp == 0) {
     if (lane == 0) {
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
-      int it = 0;
-      bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        const int m_blk = tile % m_tiles, n_blk = tile / m_tiles;
-        for (int kb = 0; kb < kblocks; ++kb, ++it) {
-          const int s = it % kStages;
-          if (it >= kStages && !wait_or_abort(&empty[s], ((it / kStages) - 1) & 1, status, abort_flag)) {
-            ok = false;
-            break;
-          }
-          uint8_t* sa = smem + s * L::stage_bytes;
-          mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(L::stage_bytes));
-          tma_load_2d(sa, &tmA, kb * BK, m_blk * BM, &full[s]);
-          tma_load_2d(sa + L::a_bytes, &tmB, kb * BK, n_blk * BN, &full[s]);
-        }
+      // Stage it holds k-block it % kblocks of this CTA's tile number it / kblocks.
+      const int my_tiles = blockIdx.x < num_tiles ? (num_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+      const int iters = my_tiles * kblocks;
+      const int pre = std::min(kStages, iters);
+      for (int it = 0; it < pre; ++it) {
+        const int tile = blockIdx.x + (it / kblocks) * gridDim.x, kb = it % kblocks;
+        uint8_t* sa = smem + it * L::stage_bytes;
+        mbar_arrive_expect_tx(&full[it], static_cast<uint32_t>(L::stage_bytes));
+        tma_load_2d(sa + L::a_bytes, &tmB, kb * BK, (tile / m_tiles) * BN, &full[it]);
+      }
+      asm volatile("griddepcontrol.wait;" ::: "memory");
+      for (int it = 0; it < pre; ++it) {
+        const int tile = blockIdx.x + (it / kblocks) * gridDim.x, kb = it % kblocks;
+        tma_load_2d(smem + it * L::stage_bytes, &tmA, kb * BK, (tile % m_tiles) * BM, &full[it]);
+      }
+      int it = pre;
+      for (; it < iters; ++it) {
+        const int s = it % kStages;
+        if (!wait_or_abort(&empty[s], ((it / kStages) - 1) & 1, status, abort_flag)) break;
+        const int tile = blockIdx.x + (it / kblocks) * gridDim.x, kb = it % kblocks;
+        uint8_t* sa = smem + s * L::stage_bytes;
+        mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(L::stage_bytes));
+        tma_load_2d(sa, &tmA, kb * BK, (tile % m_tiles) * BM, &full[s]);
+        tma_load_2d(sa + L::a_bytes, &tmB, kb * BK, (tile / m_tiles) * BN, &full[s]);
       }
       // Drain: every copy issued by this thread has landed before it exits.
       for (int j = std::max(0, it - kStages); j < it; ++j)
@@ -245,45 +267,63 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     __syncwarp();
   } else {
     const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int et = threadIdx.x - 64;  // 0..127 among the epilogue warps
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const float s_all = scale_per_row ? 0.0f : ld_act(act_scale);
+    const bool vec = (N % 4) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(acc_out) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(residual) & 15) == 0;
     int t = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++t) {
       const int b = t & 1;
-      // Warp-uniform outcome: tcgen05.ld below is a .sync.aligned warp op.
-      const bool ok = wait_or_abort(&tfull[b], (t >> 1) & 1, status, abort_flag);
-      if (!__all_sync(0xffffffffu, ok)) break;
-      tc_fence_after();
       const int m_blk = tile % m_tiles, n_blk = tile / m_tiles;
       const int row = m_blk * BM + q * 32 + lane;
-      const float s_a = scale_per_row ? (row < M ? ld_act(act_scale + row) : 0.0f) : ld_act(act_scale);
+      // Stage this tile's weight scales (the MMAs are still running).  Buffer
+      // b was last read for tile t-2, which every warp finished before it
+      // arrived on sready for tile t-1.
+      float* s_sw = reinterpret_cast<float*>(smem + L::epi) + b * 256;
+      for (int i = et; i < BN; i += 32 * kEpiWarps) {
+        const int col = n_blk * BN + i;
+        s_sw[i] = col < N ? __ldg(w_scales + col) : 0.0f;
+      }
+      const float s_a = scale_per_row ? (row < M ? ld_act(act_scale + row) : 0.0f) : s_all;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sready[b]);
+      bool ok = wait_or_abort(&sready[b], (t >> 1) & 1, status, abort_flag);
+      // Warp-uniform outcome: tcgen05.ld below is a .sync.aligned warp op.
+      ok = ok && wait_or_abort(&tfull[b], (t >> 1) & 1, status, abort_flag);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      tc_fence_after();
       float* orow = out + static_cast<size_t>(row) * N;
       // forward_int8.rs:100-121: x + projected; residual may alias out.
       const float* rrow = residual ? residual + static_cast<size_t>(row) * N : nullptr;
       int32_t* arow = acc_out ? acc_out + static_cast<size_t>(row) * N : nullptr;
-      const bool vec = (N % 4) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0 &&
-                       (reinterpret_cast<uintptr_t>(acc_out) & 15) == 0 &&
-                       (reinterpret_cast<uintptr_t>(w_scales) & 15) == 0 &&
-                       (reinterpret_cast<uintptr_t>(residual) & 15) == 0;
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t v[32];
         tmem_ld_32cols(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + b * acc_stride<BN>() + c * 32, v);
         const int col0 = n_blk * BN + c * 32;
+        const float* sw = s_sw + c * 32;
         if (row < M) {
           if (vec && col0 + 32 <= N) {
+            float4 r[8];
+            if (rrow) {  // all residual loads in flight before the first use
+#pragma unroll
+              for (int j = 0; j < 8; ++j) r[j] = ld_act(reinterpret_cast<const float4*>(rrow + col0) + j);
+            }
 #pragma unroll
             for (int j = 0; j < 32; j += 4) {
-              const float4 sw = __ldg(reinterpret_cast<const float4*>(w_scales + col0 + j));
+              const float4 w = *reinterpret_cast<const float4*>(sw + j);
               float4 o;
-              o.x = rescale(static_cast<int>(v[j]), s_a, sw.x);
-              o.y = rescale(static_cast<int>(v[j + 1]), s_a, sw.y);
-              o.z = rescale(static_cast<int>(v[j + 2]), s_a, sw.z);
-              o.w = rescale(static_cast<int>(v[j + 3]), s_a, sw.w);
+              o.x = rescale(static_cast<int>(v[j]), s_a, w.x);
+              o.y = rescale(static_cast<int>(v[j + 1]), s_a, w.y);
+              o.z = rescale(static_cast<int>(v[j + 2]), s_a, w.z);
+              o.w = rescale(static_cast<int>(v[j + 3]), s_a, w.w);
               if (rrow) {
-                const float4 r = ld_act(reinterpret_cast<const float4*>(rrow + col0 + j));
-                o.x = __fadd_rn(r.x, o.x);
-                o.y = __fadd_rn(r.y, o.y);
-                o.z = __fadd_rn(r.z, o.z);
-                o.w = __fadd_rn(r.w, o.w);
+                o.x = __fadd_rn(r[j / 4].x, o.x);
+                o.y = __fadd_rn(r[j / 4].y, o.y);
+                o.z = __fadd_rn(r[j / 4].z, o.z);
+                o.w = __fadd_rn(r[j / 4].w, o.w);
               }
               *reinterpret_cast<float4*>(orow + col0 + j) = o;
               if (arow)
@@ -296,7 +336,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             for (int j = 0; j < 32; ++j) {
               const int col = col0 + j;
               if (col < N) {
-                const float val = rescale(static_cast<int>(v[j]), s_a, __ldg(w_scales + col));
+                const float val = rescale(static_cast<int>(v[j]), s_a, sw[j]);
                 orow[col] = rrow ? __fadd_rn(ld_act(rrow + col), val) : val;
                 if (arow) arow[col] = static_cast<int>(v[j]);
               }

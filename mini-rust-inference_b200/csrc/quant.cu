@@ -6,6 +6,7 @@
 // element-wise quantization.  HBM-bound: 4 B read + 1 B written per element in
 // the second pass, 4 B read in the first.
 #include <algorithm>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "internal.h"
@@ -15,17 +16,58 @@ namespace {
 
 constexpr int kQThreads = 256;
 
+// Programmatic dependent launch: the successor (typically the GEMM, which
+// prefetches its weight tiles before waiting) may start now; this kernel reads
+// its input only after the predecessor has completed.
+__device__ __forceinline__ void pdl_enter() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+bool quant_pdl() {
+  static const bool v = [] {
+    const char* e = std::getenv("MRI_PDL");
+    return !e || std::atoi(e) != 0;
+  }();
+  return v;
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t qlaunch(void (*k)(KArgs...), unsigned grid, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kQThreads);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = quant_pdl() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, k, static_cast<KArgs>(args)...);
+}
+
 // Per-tensor, pass 1: every block folds its grid-stride share and writes its
 // partial maximum to partial[blockIdx.x] (no atomics, no clearing needed).
 __global__ void __launch_bounds__(kQThreads) absmax_tensor_kernel(const float* __restrict__ x,
                                                                   size_t n, float* partial) {
+  pdl_enter();
   float m = 0.0f;
   const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
   size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if ((reinterpret_cast<uintptr_t>(x) & 15) == 0) {
     const size_t n4 = n / 4;
     const float4* x4 = reinterpret_cast<const float4*>(x);
-    for (size_t j = i; j < n4; j += stride) {
+    constexpr int U = 4;  // independent loads in flight per thread
+    size_t j = i;
+    for (; j + (U - 1) * stride < n4; j += U * stride) {
+      float4 v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) v[u] = ld_act(x4 + j + u * stride);
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        m = absmax_acc(absmax_acc(absmax_acc(absmax_acc(m, v[u].x), v[u].y), v[u].z), v[u].w);
+    }
+    for (; j < n4; j += stride) {
       const float4 v = ld_act(x4 + j);
       m = absmax_acc(absmax_acc(absmax_acc(absmax_acc(m, v.x), v.y), v.z), v.w);
     }
@@ -49,7 +91,7 @@ __device__ float reduce_partials(const float* __restrict__ partial, int count) {
   __shared__ float red[kQThreads / 32];
   __shared__ float result;
   float m = 0.0f;
-  for (int i = threadIdx.x; i < count; i += kQThreads) m = fmaxf(m, partial[i]);
+  for (int i = threadIdx.x; i < count; i += kQThreads) m = fmaxf(m, ld_act(partial + i));
   m = warp_max(m);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
   __syncthreads();
@@ -65,6 +107,7 @@ __device__ float reduce_partials(const float* __restrict__ partial, int count) {
 // Per-row: one block per row.
 __global__ void __launch_bounds__(kQThreads) absmax_row_kernel(const float* __restrict__ x,
                                                                size_t k, float* amax) {
+  pdl_enter();
   const float* row = x + static_cast<size_t>(blockIdx.x) * k;
   float m = 0.0f;
   for (size_t j = threadIdx.x; j < k; j += kQThreads) m = absmax_acc(m, ld_act(row + j));
@@ -85,6 +128,7 @@ __global__ void __launch_bounds__(kQThreads) quant_apply_kernel(const float* __r
                                                                 int n_partials,
                                                                 int8_t* __restrict__ q,
                                                                 float* __restrict__ scale_out) {
+  pdl_enter();
   const size_t n = m * k;
   const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
   const size_t tid = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -108,10 +152,10 @@ __global__ void __launch_bounds__(kQThreads) quant_apply_kernel(const float* __r
       for (size_t j = tid; j < n; j += stride) q[j] = sym_quant(ld_act(x + j), inv);
     }
   } else {
-    for (size_t r = tid; r < m; r += stride) scale_out[r] = sym_scale(amax[r]);
+    for (size_t r = tid; r < m; r += stride) scale_out[r] = sym_scale(ld_act(amax + r));
     for (size_t j = tid; j < n; j += stride) {
       const size_t r = j / k;
-      const float scale = sym_scale(amax[r]);
+      const float scale = sym_scale(ld_act(amax + r));
       q[j] = sym_quant(ld_act(x + j), __fdiv_rn(1.0f, scale));
     }
   }
@@ -136,6 +180,7 @@ __global__ void __launch_bounds__(kQThreads) row_stats_kernel(const float* __res
                                                               float eps, int swiglu,
                                                               float* __restrict__ row_inv,
                                                               float* __restrict__ partial) {
+  pdl_enter();
   const int r = blockIdx.x;
   __shared__ float red[kQThreads / 32];
   __shared__ float inv_s;
@@ -177,6 +222,7 @@ __global__ void __launch_bounds__(kQThreads) quant_apply_xform_kernel(
     const float* __restrict__ x, size_t m, size_t K, int per_row, const float* __restrict__ partial,
     const float* __restrict__ norm_w, const float* __restrict__ row_inv, int swiglu,
     int8_t* __restrict__ q, float* __restrict__ scale_out) {
+  pdl_enter();
   const size_t n = m * K;
   const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
   const size_t tid = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -186,13 +232,52 @@ __global__ void __launch_bounds__(kQThreads) quant_apply_xform_kernel(
     inv_t = __fdiv_rn(1.0f, scale);
     if (tid == 0) scale_out[0] = scale;
   } else {
-    for (size_t r = tid; r < m; r += stride) scale_out[r] = sym_scale(partial[r]);
+    for (size_t r = tid; r < m; r += stride) scale_out[r] = sym_scale(ld_act(partial + r));
+  }
+  const bool vec = K % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+                   (!norm_w || (reinterpret_cast<uintptr_t>(norm_w) & 15) == 0) &&
+                   (reinterpret_cast<uintptr_t>(q) & 3) == 0;
+  if (vec) {
+    // Four elements of one row per step (K % 4 == 0).
+    const size_t K4 = K / 4;
+    for (size_t j = tid; j < n / 4; j += stride) {
+      const int r = static_cast<int>(j / K4);
+      const size_t k = (j - r * K4) * 4;
+      const float inv = per_row ? __fdiv_rn(1.0f, sym_scale(ld_act(partial + r))) : inv_t;
+      float4 v;
+      if (swiglu) {
+        const float* row = x + static_cast<size_t>(r) * 2 * K + 2 * k;
+        const float4 a = ld_act(reinterpret_cast<const float4*>(row));
+        const float4 b = ld_act(reinterpret_cast<const float4*>(row + 4));
+        v.x = __fmul_rn(__fdiv_rn(a.x, __fadd_rn(1.0f, expf(-a.x))), a.y);
+        v.y = __fmul_rn(__fdiv_rn(a.z, __fadd_rn(1.0f, expf(-a.z))), a.w);
+        v.z = __fmul_rn(__fdiv_rn(b.x, __fadd_rn(1.0f, expf(-b.x))), b.y);
+        v.w = __fmul_rn(__fdiv_rn(b.z, __fadd_rn(1.0f, expf(-b.z))), b.w);
+      } else {
+        v = ld_act(reinterpret_cast<const float4*>(x + static_cast<size_t>(r) * K + k));
+        if (norm_w) {
+          const float ir = ld_act(row_inv + r);
+          const float4 w = __ldg(reinterpret_cast<const float4*>(norm_w + k));
+          v.x = __fmul_rn(w.x, __fmul_rn(v.x, ir));
+          v.y = __fmul_rn(w.y, __fmul_rn(v.y, ir));
+          v.z = __fmul_rn(w.z, __fmul_rn(v.z, ir));
+          v.w = __fmul_rn(w.w, __fmul_rn(v.w, ir));
+        }
+      }
+      char4 o;
+      o.x = sym_quant(v.x, inv);
+      o.y = sym_quant(v.y, inv);
+      o.z = sym_quant(v.z, inv);
+      o.w = sym_quant(v.w, inv);
+      reinterpret_cast<char4*>(q)[j] = o;
+    }
+    return;
   }
   for (size_t j = tid; j < n; j += stride) {
     const int r = static_cast<int>(j / K);
     const size_t k = j % K;
-    const float inv = per_row ? __fdiv_rn(1.0f, sym_scale(partial[r])) : inv_t;
-    q[j] = sym_quant(xform(x, k, K, r, norm_w, norm_w ? row_inv[r] : 1.0f, swiglu), inv);
+    const float inv = per_row ? __fdiv_rn(1.0f, sym_scale(ld_act(partial + r))) : inv_t;
+    q[j] = sym_quant(xform(x, k, K, r, norm_w, norm_w ? ld_act(row_inv + r) : 1.0f, swiglu), inv);
   }
 }
 
@@ -220,14 +305,15 @@ cudaError_t launch_quantize(const DeviceInfo& dev, cudaStream_t st, const float*
     // amax_scratch holds 2 * max(m, kQuantPartials) floats: row maxima, then 1/rms.
     float* partial = amax_scratch;
     float* row_inv = amax_scratch + std::max(m, kQuantPartials);
-    row_stats_kernel<<<static_cast<unsigned>(m), kQThreads, 0, st>>>(x, k, norm_w, eps, swiglu, row_inv,
-                                                                    partial);
+    cudaError_t e = qlaunch(row_stats_kernel, static_cast<unsigned>(m), st, x, k, norm_w, eps, swiglu,
+                            row_inv, partial);
+    if (e != cudaSuccess) return e;
     const int apply_blocks = static_cast<int>(std::max<size_t>(
         1, std::min<size_t>(static_cast<size_t>(dev.sm_count) * 8, (n + kQThreads * 4 - 1) / (kQThreads * 4))));
-    quant_apply_xform_kernel<<<apply_blocks, kQThreads, 0, st>>>(x, m, k, per_row, partial, norm_w,
-                                                                 row_inv, swiglu, q, scale);
+    e = qlaunch(quant_apply_xform_kernel, static_cast<unsigned>(apply_blocks), st, x, m, k, per_row,
+                partial, norm_w, row_inv, swiglu, q, scale);
     if (ls) ls->launches += 2;
-    return cudaGetLastError();
+    return e;
   }
   if (n == 0) {
     // Empty input: the reference's fold yields 0 -> scale 1.0.
@@ -242,18 +328,17 @@ cudaError_t launch_quantize(const DeviceInfo& dev, cudaStream_t st, const float*
   const int blocks = static_cast<int>(std::max<size_t>(
       1, std::min<size_t>(std::min<size_t>(static_cast<size_t>(dev.sm_count) * 2, kQuantPartials),
                           (n + kQThreads * 16 - 1) / (kQThreads * 16))));
-  if (!per_row) {
-    absmax_tensor_kernel<<<blocks, kQThreads, 0, st>>>(x, n, amax_scratch);
-  } else {
-    absmax_row_kernel<<<static_cast<unsigned>(m), kQThreads, 0, st>>>(x, k, amax_scratch);
-  }
+  cudaError_t e = per_row
+                      ? qlaunch(absmax_row_kernel, static_cast<unsigned>(m), st, x, k, amax_scratch)
+                      : qlaunch(absmax_tensor_kernel, static_cast<unsigned>(blocks), st, x, n, amax_scratch);
+  if (e != cudaSuccess) return e;
   if (ls) ls->launches++;
   const int apply_blocks = static_cast<int>(std::max<size_t>(
       1, std::min<size_t>(static_cast<size_t>(dev.sm_count) * 8, (n + kQThreads * 4 - 1) / (kQThreads * 4))));
-  quant_apply_kernel<<<apply_blocks, kQThreads, 0, st>>>(x, m, k, per_row, amax_scratch, blocks, q,
-                                                         scale);
+  e = qlaunch(quant_apply_kernel, static_cast<unsigned>(apply_blocks), st, x, m, k, per_row,
+              amax_scratch, blocks, q, scale);
   if (ls) ls->launches++;
-  return cudaGetLastError();
+  return e;
 }
 
 }  // namespace mri

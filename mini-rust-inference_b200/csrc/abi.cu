@@ -209,6 +209,26 @@ int mri::matmul_int8_act(::mri_ctx* ctx, const ActArgs& act, const ::mri_qmatrix
   return run_int8(ctx, act, w, m, out, nullptr);
 }
 
+bool mri::stream_gemv_ok(const ::mri_ctx* ctx, size_t m, const ::mri_qmatrix* w) {
+  return ctx && w && stream_gemv_applies(ctx, m, w);
+}
+
+int mri::matmul_int8_gather(::mri_ctx* ctx, const float* x, size_t m, size_t k,
+                            const ::mri_qmatrix* w, const EpiArgs& e) {
+  if (int rc = enter(ctx)) return rc;
+  if (!w) return fail(MRI_ERR_INVALID_ARGUMENT, "null weight handle");
+  if (int rc = check_k("sharded matmul", m, k, w->k_in)) return rc;
+  if (!stream_gemv_applies(ctx, m, w))
+    return fail(MRI_ERR_INVALID_ARGUMENT, "peer gather needs the streaming GEMV (m <= 8, K %% 16 == 0)");
+  ActArgs a;
+  a.x = x;
+  a.mode = mri::ACT_F32_PER_TENSOR;
+  MRI_CUDA_TRY(mri::launch_gemv_i8_tma(ctx->dev, ctx->stream, static_cast<int>(m), w->data, w->scales,
+                                       w->n_out, w->k_in, a, e.g_out, nullptr, ctx->d_status, &ctx->ls,
+                                       nullptr, &e));
+  return MRI_OK;
+}
+
 bool mri::matmul_int8_epilogue_supported(const ::mri_ctx* ctx, size_t m, const ::mri_qmatrix* w) {
   return ctx && w && m == 1 && w->n_out % 2 == 0 && stream_gemv_applies(ctx, m, w);
 }

@@ -8,6 +8,14 @@
 // and f32 epilogue) as the unsharded product, and an NCCL all-gather over
 // NVLink assembles the full [M, N] output on every rank.
 //
+// For m <= 8 (decode) the gather runs inside the GEMV instead: every rank
+// maps every other rank's staging buffer and arrival counter (CUDA IPC over
+// NVLink), the GEMV epilogue stores each output value to all ranks, and each
+// CTA waits (bounded) until all ranks' CTAs have arrived before copying the
+// assembled result out.  One kernel per call, no collective launch.  The
+// ranks agree collectively whether the mappings work; if any rank cannot map
+// them, all use the NCCL path.
+//
 // NCCL is resolved at run time (dlopen of libnccl.so.2): a process that
 // already loaded NCCL (torch.distributed) shares that library, and the
 // shared object stays loadable on machines without NCCL.  Communicators are
@@ -24,6 +32,7 @@
 #include <mutex>
 #include <string>
 #include <thread>
+#include <vector>
 
 #include "common.cuh"
 #include "internal.h"
@@ -86,6 +95,15 @@ struct mri_comm {
   cudaEvent_t side_done = nullptr;
   float* gather = nullptr;  // rank-major staging [chunk][P][rows][N/P]
   size_t gather_bytes = 0;
+  // Peer-memory gather (m <= 8).
+  bool peer_tried = false, peer_ok = false;
+  float* stage = nullptr;                 // local staging [2][stage_half]
+  size_t stage_half = 0;
+  unsigned long long* ctrs = nullptr;     // [0] arrival counter, [8] calls done, [9] CTA ticket
+  float* peer_stage[mri::EpiArgs::kMaxRanks] = {};
+  unsigned long long* peer_ctr[mri::EpiArgs::kMaxRanks] = {};
+  std::vector<void*> retired;             // earlier staging buffers (peers may still map them)
+  std::vector<void*> opened;              // peer mappings to close
 };
 
 namespace {
@@ -190,6 +208,144 @@ int check_comm(mri_comm* c) {
   return MRI_OK;
 }
 
+bool peer_gather_enabled() {
+  static const bool v = [] {
+    const char* e = std::getenv("MRI_SHARD_PEER");
+    return !e || std::atoi(e) != 0;
+  }();
+  return v;
+}
+
+// All-gathers `bytes` bytes of host data from every rank (through a device
+// buffer and NCCL on the context stream); synchronizes the stream.
+int exchange(mri_comm* c, const void* mine, size_t bytes, std::vector<uint8_t>* all) {
+  void* d = nullptr;
+  COMM_CUDA_TRY(cudaMalloc(&d, bytes * c->size));
+  int rc = MRI_OK;
+  cudaError_t e = cudaMemcpyAsync(static_cast<uint8_t*>(d) + bytes * c->rank, mine, bytes,
+                                  cudaMemcpyHostToDevice, c->ctx->stream);
+  if (e != cudaSuccess) rc = cuda_err(e, "exchange upload");
+  if (!rc)
+    rc = settle(c, nccl().all_gather(static_cast<uint8_t*>(d) + bytes * c->rank, d, bytes, ncclUint8,
+                                     c->comm, c->ctx->stream),
+                "ncclAllGather (peer setup)");
+  if (!rc) rc = mri_comm_wait(c);
+  all->resize(bytes * c->size);
+  if (!rc) {
+    e = cudaMemcpy(all->data(), d, bytes * c->size, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) rc = cuda_err(e, "exchange download");
+  }
+  cudaFree(d);
+  return rc;
+}
+
+// Collective: makes sure every rank's staging holds `half` floats per half and
+// every rank maps every other rank's staging and counters.  Sets peer_ok to
+// the ranks' joint verdict.  Called with the same `half` on every rank (the
+// ranks issue the same sequence of sharded calls).
+int ensure_peer(mri_comm* c, size_t half) {
+  if (c->peer_tried && (!c->peer_ok || half <= c->stage_half)) return MRI_OK;
+  c->peer_tried = true;
+  const bool first = c->ctrs == nullptr;
+  half = std::max(half, c->stage_half * 2);
+  struct Msg {
+    int ok;
+    int pad;
+    cudaIpcMemHandle_t stage, ctrs;
+  } mine{};
+  float* stage = nullptr;
+  mine.ok = 1;
+  if (cudaMalloc(&stage, 2 * half * sizeof(float)) != cudaSuccess) {
+    cudaGetLastError();
+    stage = nullptr;
+    mine.ok = 0;
+  }
+  if (mine.ok && first) {
+    void* ctrs = nullptr;
+    if (cudaMalloc(&ctrs, 256) != cudaSuccess || cudaMemset(ctrs, 0, 256) != cudaSuccess) {
+      cudaGetLastError();
+      mine.ok = 0;
+    } else {
+      c->ctrs = static_cast<unsigned long long*>(ctrs);
+    }
+  }
+  if (mine.ok && c->size > 1) {
+    if (cudaIpcGetMemHandle(&mine.stage, stage) != cudaSuccess ||
+        cudaIpcGetMemHandle(&mine.ctrs, c->ctrs) != cudaSuccess) {
+      cudaGetLastError();
+      mine.ok = 0;
+    }
+  }
+  std::vector<uint8_t> all;
+  if (int rc = c->size > 1 ? exchange(c, &mine, sizeof(Msg), &all) : MRI_OK) {
+    if (stage) cudaFree(stage);
+    c->peer_ok = false;
+    return rc;
+  }
+  bool every = mine.ok != 0;
+  for (int p = 0; p < c->size && c->size > 1; ++p)
+    every = every && reinterpret_cast<const Msg*>(all.data())[p].ok;
+  // Map the other ranks' buffers, then agree again on whether that worked.
+  int mapped = every ? 1 : 0;
+  float* new_stage[mri::EpiArgs::kMaxRanks] = {};
+  unsigned long long* new_ctr[mri::EpiArgs::kMaxRanks] = {};
+  std::vector<void*> opened_now;
+  if (every) {
+    for (int p = 0; p < c->size; ++p) {
+      if (p == c->rank) {
+        new_stage[p] = stage;
+        new_ctr[p] = c->ctrs;
+        continue;
+      }
+      const Msg& m = reinterpret_cast<const Msg*>(all.data())[p];
+      void* ps = nullptr;
+      void* pc = c->peer_ctr[p];
+      if (cudaIpcOpenMemHandle(&ps, m.stage, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+        cudaGetLastError();
+        mapped = 0;
+        break;
+      }
+      opened_now.push_back(ps);
+      if (!pc) {
+        if (cudaIpcOpenMemHandle(&pc, m.ctrs, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+          cudaGetLastError();
+          mapped = 0;
+          break;
+        }
+        opened_now.push_back(pc);
+      }
+      new_stage[p] = static_cast<float*>(ps);
+      new_ctr[p] = static_cast<unsigned long long*>(pc);
+    }
+  }
+  if (c->size > 1) {
+    std::vector<uint8_t> verdicts;
+    if (int rc = exchange(c, &mapped, sizeof(int), &verdicts)) {
+      for (void* v : opened_now) cudaIpcCloseMemHandle(v);
+      if (stage) cudaFree(stage);
+      c->peer_ok = false;
+      return rc;
+    }
+    for (int p = 0; p < c->size; ++p) mapped = mapped && reinterpret_cast<const int*>(verdicts.data())[p];
+  }
+  if (!mapped) {
+    for (void* v : opened_now) cudaIpcCloseMemHandle(v);
+    if (stage) cudaFree(stage);
+    c->peer_ok = false;
+    return MRI_OK;
+  }
+  if (c->stage) c->retired.push_back(c->stage);
+  c->stage = stage;
+  c->stage_half = half;
+  for (int p = 0; p < c->size; ++p) {
+    c->peer_stage[p] = new_stage[p];
+    c->peer_ctr[p] = new_ctr[p];
+  }
+  c->opened.insert(c->opened.end(), opened_now.begin(), opened_now.end());
+  c->peer_ok = true;
+  return MRI_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -261,6 +417,10 @@ int mri_comm_destroy(mri_comm* c) {
     if (mri_comm_wait(c) == MRI_OK && c->comm) nccl().destroy(c->comm);
   }
   if (c->gather) cudaFree(c->gather);
+  for (void* v : c->opened) cudaIpcCloseMemHandle(v);
+  for (void* v : c->retired) cudaFree(v);
+  if (c->stage) cudaFree(c->stage);
+  if (c->ctrs) cudaFree(c->ctrs);
   for (auto& ev : c->chunk_ready)
     if (ev) cudaEventDestroy(ev);
   if (c->side_done) cudaEventDestroy(c->side_done);
@@ -299,6 +459,14 @@ int mri_comm_wait(mri_comm* c) {
       std::this_thread::sleep_for(std::chrono::microseconds(20));
     }
   }
+  // A peer-gather kernel that gave up waiting for the other ranks leaves the
+  // arrival counts inconsistent: the communicator cannot be used again.
+  if (int rc = mri_ctx_check_device_status(c->ctx)) {
+    if (c->comm) nccl().abort(c->comm);
+    c->comm = nullptr;
+    c->aborted = true;
+    return rc;
+  }
   return MRI_OK;
 }
 
@@ -322,6 +490,25 @@ int mri_sharded_matmul_int8_from_f32(mri_comm* c, const float* x_dev, size_t m, 
   COMM_CUDA_TRY(cudaSetDevice(ctx->device));
   cudaStream_t st = ctx->stream;
   const NcclApi& api = nccl();
+
+  if (m <= 8 && peer_gather_enabled() && mri::stream_gemv_ok(ctx, m, w_shard)) {
+    if (int rc = ensure_peer(c, m * n_total)) return rc;
+    if (c->peer_ok) {
+      mri::EpiArgs e;
+      e.mode = mri::EPI_GATHER;
+      for (int p = 0; p < P; ++p) {
+        e.g_stage[p] = c->peer_stage[p];
+        e.g_ctr[p] = c->peer_ctr[p];
+      }
+      e.g_seq = c->ctrs + 8;
+      e.g_half = c->stage_half;
+      e.g_ntotal = n_total;
+      e.g_ranks = P;
+      e.g_rank = r;
+      e.g_out = out_dev;
+      return mri::matmul_int8_gather(ctx, x_dev, m, k, w_shard, e);
+    }
+  }
 
   if (m == 1) {
     // One row: the rank-major gather layout is the output layout.

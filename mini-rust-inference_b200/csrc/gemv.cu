@@ -416,9 +416,58 @@ __device__ __forceinline__ void pair_epilogue(const EpiArgs& epi, int M, size_t 
   else if (r >= qk) epi.vc[static_cast<size_t>(pos) * epi.kvd + (r - qk)] = y;
 }
 
-// CHUNK: rows may be split into nk K-chunks; EPI: pair epilogue (epi.mode).
-// Both are compile-time so the plain decode kernel carries neither.
-template <int M, int VEC, bool CHUNK, bool EPI>
+__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// EPI_GATHER tail, consumer threads: count this CTA in on every rank, wait
+// until every CTA of every rank has arrived here, copy this CTA's share of the
+// staged result out, and (last CTA) advance the call sequence.
+template <int M>
+__device__ void gather_finish(const EpiArgs& epi, unsigned long long seq, int* status, int* s_flag) {
+  __threadfence_system();  // this thread's stores to all ranks' staging
+  named_bar_sync(1, kConsumerThreads);
+  if (threadIdx.x == 32) {
+    for (int p = 0; p < epi.g_ranks; ++p) atomicAdd_system(epi.g_ctr[p], 1ull);
+    const unsigned long long target =
+        (seq + 1) * static_cast<unsigned long long>(epi.g_ranks) * gridDim.x;
+    int ok = 1;
+    const long long t0 = clock64();
+    while (ld_acquire_sys_u64(epi.g_ctr[epi.g_rank]) < target) {
+      if (clock64() - t0 > kWaitBudgetClocks) {
+        *reinterpret_cast<volatile int*>(status) = MRI_ERR_TIMEOUT;
+        ok = 0;
+        break;
+      }
+      __nanosleep(64);
+    }
+    *s_flag = ok;
+  }
+  named_bar_sync(1, kConsumerThreads);
+  if (*s_flag) {
+    const size_t total = static_cast<size_t>(M) * epi.g_ntotal;
+    const size_t per = (total + gridDim.x - 1) / gridDim.x;
+    const size_t lo = std::min(total, per * blockIdx.x), hi = std::min(total, lo + per);
+    const float* src = epi.g_stage[epi.g_rank] + (seq & 1) * epi.g_half;
+    for (size_t i = lo + (threadIdx.x - 32); i < hi; i += kConsumerThreads) epi.g_out[i] = ld_act(src + i);
+  }
+  named_bar_sync(1, kConsumerThreads);
+  if (threadIdx.x == 32) {
+    __threadfence();
+    if (atomicAdd(epi.g_seq + 1, 1ull) == gridDim.x - 1) {
+      epi.g_seq[1] = 0;
+      epi.g_seq[0] = seq + 1;
+      __threadfence();
+    }
+  }
+}
+
+// CHUNK: rows may be split into nk K-chunks; EPI: 0 none, 1 pair epilogue
+// (epi.mode), 2 peer gather.  All compile-time so the plain decode kernel
+// carries none of them.
+template <int M, int VEC, bool CHUNK, int EPI>
 __global__ void __launch_bounds__(kThreads, M <= 2 ? 2 : 1)
     gemv_i8_tma_kernel(const int8_t* __restrict__ W, const float* __restrict__ w_scales, size_t N,
                        size_t K, ActArgs act, float* out, int32_t* __restrict__ acc_out,
@@ -438,10 +487,11 @@ __global__ void __launch_bounds__(kThreads, M <= 2 ? 2 : 1)
 
   size_t begin, end;
   // Pair epilogues need both rows of a pair in the same CTA and stage.
-  cta_rows(N, EPI ? 2 : 1, begin, end);
+  cta_rows(N, EPI == 1 ? 2 : 1, begin, end);
   uint64_t* act_issued = empty + n_stages;
   init_barriers(full, empty, n_stages, act_issued);
-  if (begin >= end) return;
+  // A gather CTA without rows still takes part in the arrival count.
+  if (begin >= end && EPI != 2) return;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (warp == 0) {
@@ -452,6 +502,9 @@ __global__ void __launch_bounds__(kThreads, M <= 2 ? 2 : 1)
   }
   pdl_wait();
   load_act_i8_rowmajor<M, VEC>(act, K, s_act, s_scale, red, act_issued);
+  __shared__ int s_flag;
+  unsigned long long seq = 0;
+  if constexpr (EPI == 2) seq = ld_act(epi.g_seq);
   float s_a[M];
 #pragma unroll
   for (int m = 0; m < M; ++m) s_a[m] = s_scale[m];
@@ -505,8 +558,13 @@ __global__ void __launch_bounds__(kThreads, M <= 2 ? 2 : 1)
       for (int m = 0; m < M; ++m)
         if (lane == m) val = rescale(acc[m], s_a[m], sw);
     }
-    if constexpr (EPI) {
+    if constexpr (EPI == 1) {
       pair_epilogue(epi, M, N, row, valid, val, lane, cw, g, s_pair, out);
+    } else if constexpr (EPI == 2) {
+      if (valid && lane < M) {
+        const size_t off = (seq & 1) * epi.g_half + lane * epi.g_ntotal + epi.g_rank * N + row;
+        for (int p = 0; p < epi.g_ranks; ++p) epi.g_stage[p][off] = val;
+      }
     } else if (valid && lane < M) {
       // forward_int8.rs:100-121: x + projected (residual may alias out).
       out[lane * N + row] = residual ? __fadd_rn(ld_act(residual + lane * N + row), val) : val;
@@ -517,6 +575,7 @@ __global__ void __launch_bounds__(kThreads, M <= 2 ? 2 : 1)
       }
     }
   }
+  if constexpr (EPI == 2) gather_finish<M>(epi, seq, status, &s_flag);
 }
 
 // ── generic INT8 GEMV: any K / alignment, pre-quantized activations ─────────
@@ -992,20 +1051,36 @@ int resident_ctas(KernelT k, size_t smem, int device) {
 }
 
 // Launch with the programmatic-stream-serialization attribute when enabled.
+// `cooperative`: the CTAs wait on one another, so all must be resident.
 template <typename... KArgs, typename... Args>
-cudaError_t launch_stream_kernel(void (*k)(KArgs...), int grid, size_t smem, cudaStream_t st,
-                                 Args&&... args) {
+cudaError_t launch_stream_kernel_ex(bool cooperative, void (*k)(KArgs...), int grid, size_t smem,
+                                    cudaStream_t st, Args&&... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (tuning().pdl) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (cooperative) {
+    attr[n].id = cudaLaunchAttributeCooperative;
+    attr[n].val.cooperative = 1;
+    ++n;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = tuning().pdl ? 1 : 0;
+  cfg.numAttrs = n;
   return cudaLaunchKernelEx(&cfg, k, std::forward<Args>(args)...);
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_stream_kernel(void (*k)(KArgs...), int grid, size_t smem, cudaStream_t st,
+                                 Args&&... args) {
+  return launch_stream_kernel_ex(false, k, grid, smem, st, std::forward<Args>(args)...);
 }
 
 #define MRI_DISPATCH_M(M, ...)                           \
@@ -1072,16 +1147,23 @@ int reg_vec(int M, size_t K, const ActArgs* act) {
 // The INT8 stream kernel for (M, VEC, CHUNK, EPI) as `kKernel`.  The pair
 // epilogue exists for M = 1 only (the decode step).
 #define MRI_DISPATCH_I8_TMA(M, V, CH, EP, ...)                                              \
-  if (EP) {                                                                                 \
+  if ((EP) == 1) {                                                                          \
     MRI_DISPATCH_VEC(V, {                                                                   \
-      if (CH) { auto kKernel = gemv_i8_tma_kernel<1, kV, true, true>; __VA_ARGS__; }         \
-      else { auto kKernel = gemv_i8_tma_kernel<1, kV, false, true>; __VA_ARGS__; }           \
+      if (CH) { auto kKernel = gemv_i8_tma_kernel<1, kV, true, 1>; __VA_ARGS__; }            \
+      else { auto kKernel = gemv_i8_tma_kernel<1, kV, false, 1>; __VA_ARGS__; }              \
+    });                                                                                     \
+  } else if ((EP) == 2) {                                                                   \
+    MRI_DISPATCH_M(M, {                                                                     \
+      MRI_DISPATCH_VEC(V, {                                                                 \
+        if (CH) { auto kKernel = gemv_i8_tma_kernel<kM, kV, true, 2>; __VA_ARGS__; }         \
+        else { auto kKernel = gemv_i8_tma_kernel<kM, kV, false, 2>; __VA_ARGS__; }           \
+      });                                                                                   \
     });                                                                                     \
   } else {                                                                                  \
     MRI_DISPATCH_M(M, {                                                                     \
       MRI_DISPATCH_VEC(V, {                                                                 \
-        if (CH) { auto kKernel = gemv_i8_tma_kernel<kM, kV, true, false>; __VA_ARGS__; }     \
-        else { auto kKernel = gemv_i8_tma_kernel<kM, kV, false, false>; __VA_ARGS__; }       \
+        if (CH) { auto kKernel = gemv_i8_tma_kernel<kM, kV, true, 0>; __VA_ARGS__; }         \
+        else { auto kKernel = gemv_i8_tma_kernel<kM, kV, false, 0>; __VA_ARGS__; }           \
       });                                                                                   \
     });                                                                                     \
   }
@@ -1098,8 +1180,8 @@ int pre_stages(int stages) {
 }
 
 cudaError_t gemv_i8_tma_plan(const DeviceInfo& dev, int M, size_t N, size_t K, GemvPlan* plan,
-                             int vec, bool epi) {
-  if (epi && M != 1) return cudaErrorInvalidValue;
+                             int vec, int epi) {
+  if (epi == 1 && M != 1) return cudaErrorInvalidValue;
   StreamConfig cfg;
   const int nk = i8_chunks(M, K, &cfg);
   if (nk == 0 || M < 1 || M > 8) return cudaErrorInvalidValue;
@@ -1126,16 +1208,20 @@ cudaError_t launch_gemv_i8_tma(const DeviceInfo& dev, cudaStream_t st, int M, co
                                float* out, int32_t* acc_out, int* status, LaunchStats* ls,
                                const float* residual, const EpiArgs* epi) {
   EpiArgs e_args;
+  int kind = 0;
   if (epi) {
-    if (N % 2 || residual || acc_out) return cudaErrorInvalidValue;
+    kind = epi->mode == EPI_GATHER ? 2 : 1;
+    if ((kind == 1 && N % 2) || residual || acc_out) return cudaErrorInvalidValue;
+    if (kind == 2 && (epi->g_ranks < 1 || epi->g_ranks > EpiArgs::kMaxRanks)) return cudaErrorInvalidValue;
     e_args = *epi;
   }
   GemvPlan p;
-  if (cudaError_t e = gemv_i8_tma_plan(dev, M, N, K, &p, reg_vec(M, K, &act), epi != nullptr)) return e;
+  if (cudaError_t e = gemv_i8_tma_plan(dev, M, N, K, &p, reg_vec(M, K, &act), kind)) return e;
   const int pre = pre_stages(p.stages);
   MRI_DISPATCH_I8_TMA(M, p.vec, p.k_chunks > 1, p.epi, {
-    cudaError_t e = launch_stream_kernel(kKernel, p.grid, p.smem, st, W, w_scales, N, K, act, out,
-                                         acc_out, p.stages, p.k_chunks, pre, status, residual, e_args);
+    cudaError_t e = launch_stream_kernel_ex(kind == 2, kKernel, p.grid, p.smem, st, W, w_scales, N, K,
+                                            act, out, acc_out, p.stages, p.k_chunks, pre, status,
+                                            residual, e_args);
     if (e != cudaSuccess) return e;
   });
   if (ls) ls->launches++;

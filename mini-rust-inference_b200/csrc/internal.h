@@ -49,6 +49,14 @@ enum EpiMode : int {
   // else pos0), written to out; rotated k and plain v also written to the
   // cache rows kc/vc [pos + m] (attention/cached.rs:90-93).
   EPI_ROPE_KV = 2,
+  // N-sharded product gathered over peer memory (no NCCL): every output value
+  // is also stored into the staging buffer of every rank ([2][M][n_total],
+  // half `seq & 1`, columns of rank r at [r*N, (r+1)*N)); each CTA then counts
+  // itself in on every rank's arrival counter, waits (bounded) until all
+  // ranks' CTAs have arrived on its own, and copies its share of the staged
+  // [M][n_total] result to `g_out`.  The last CTA advances the local call
+  // sequence.
+  EPI_GATHER = 3,
 };
 
 struct EpiArgs {
@@ -60,6 +68,15 @@ struct EpiArgs {
   int hd = 0, qd = 0, kvd = 0;
   float* kc = nullptr;  // [max_seq, kvd]
   float* vc = nullptr;
+  // EPI_GATHER
+  static constexpr int kMaxRanks = 8;
+  float* g_stage[kMaxRanks] = {};              // per rank (peer pointers)
+  unsigned long long* g_ctr[kMaxRanks] = {};   // per rank arrival counters
+  unsigned long long* g_seq = nullptr;         // local: [0] calls done, [1] CTA ticket
+  size_t g_half = 0;                           // floats per staging half
+  size_t g_ntotal = 0;
+  int g_ranks = 1, g_rank = 0;
+  float* g_out = nullptr;
 };
 
 // Kernel counts for launch accounting.
@@ -97,12 +114,13 @@ bool gemv_i8_tma_supported(const DeviceInfo& dev, int M, size_t K);
 // Launch shape the INT8 streaming GEMV uses for (M, N, K).
 struct GemvPlan {
   int grid = 0, ctas_per_sm = 0, resident = 0, stages = 0, k_chunks = 0, vec = 0;
-  bool epi = false;
+  int epi = 0;
   size_t smem = 0;
 };
 // vec < 0: the register-path width of a plain per-tensor f32 input.
+// epi_kind: 0 none, 1 pair epilogue (M = 1), 2 peer gather.
 cudaError_t gemv_i8_tma_plan(const DeviceInfo& dev, int M, size_t N, size_t K, GemvPlan* plan,
-                             int vec = -1, bool epi = false);
+                             int vec = -1, int epi_kind = 0);
 // epi (nullable): a pair epilogue (EpiArgs); not combined with residual or acc_out.
 cudaError_t launch_gemv_i8_tma(const DeviceInfo& dev, cudaStream_t st, int M, const int8_t* W,
                                const float* w_scales, size_t N, size_t K, const ActArgs& act,
@@ -152,6 +170,12 @@ int quantize_to_scratch(struct ::mri_ctx* ctx, const float* x, size_t m, size_t 
 // The INT8 dispatch (streaming GEMV / tensor-core GEMM) for any ActArgs mode.
 int matmul_int8_act(struct ::mri_ctx* ctx, const ActArgs& act, const struct ::mri_qmatrix* w,
                     size_t m, float* out);
+// The streaming GEMV serves an INT8 product of m activation rows with w.
+bool stream_gemv_ok(const struct ::mri_ctx* ctx, size_t m, const struct ::mri_qmatrix* w);
+// N-sharded product of x [m <= 8, k] with this rank's shard, gathered over
+// peer memory (EPI_GATHER); e carries the gather fields.  Status as the C ABI.
+int matmul_int8_gather(struct ::mri_ctx* ctx, const float* x, size_t m, size_t k,
+                       const struct ::mri_qmatrix* w, const EpiArgs& e);
 bool matmul_int8_epilogue_supported(const struct ::mri_ctx* ctx, size_t m,
                                     const struct ::mri_qmatrix* w);
 

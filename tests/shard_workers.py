@@ -52,7 +52,11 @@ def gloo_shard_worker(rank, world, port, m, n, k, seed, results):
         dist.destroy_process_group()
 
 
-def nccl_shard_worker(rank, world, uid, m, n, k, seed, results):
+def nccl_shard_worker(rank, world, results, uid, ms, n, k, seed, env=None):
+    """Runs the sharded product for every m in `ms` (same sequence on every
+    rank) and reports {m: output}.  `env` is applied before the library loads
+    (MRI_SHARD_PEER=0 selects the NCCL path for small m)."""
+    os.environ.update(env or {})
     import torch
 
     from conftest import load_mri
@@ -62,11 +66,49 @@ def nccl_shard_worker(rank, world, uid, m, n, k, seed, results):
         torch.cuda.set_device(rank)
         ctx = mri.Context(rank)
         comm = mri.Communicator(uid, world, rank, ctx=ctx, timeout_ms=60000)
-        x, wq, ws = problem(m, n, k, seed)
-        w = mri.shard_quantized_matrix(wq.reshape(-1), ws, n, k, comm)
-        out = mri.matmul_int8_from_f32_sharded(torch.from_numpy(x).cuda(rank), w, n, comm)
-        comm.wait()
-        results.put((rank, out.cpu().numpy()))
+        outs = {}
+        for m in ms:
+            x, wq, ws = problem(m, n, k, seed + m)
+            w = mri.shard_quantized_matrix(wq.reshape(-1), ws, n, k, comm)
+            out = mri.matmul_int8_from_f32_sharded(torch.from_numpy(x).cuda(rank), w, n, comm)
+            comm.wait()
+            outs[m] = out.cpu().numpy()
+        results.put((rank, outs))
         comm.close()
     except Exception as e:  # noqa: BLE001 - reported to the parent
         results.put((rank, repr(e)))
+
+
+def peer_timeout_worker(rank, world, results, uid, n, k, done):
+    """Both ranks run one gathered product; then rank 0 runs a second one that
+    rank 1 skips.  Rank 0's kernel must give up waiting for rank 1's arrivals
+    (bounded wait) and report a timeout.  Rank 1 stays alive, with its buffers
+    mapped and no work in flight, until rank 0 is done."""
+    import torch
+
+    from conftest import load_mri
+
+    try:
+        mri = load_mri()
+        torch.cuda.set_device(rank)
+        ctx = mri.Context(rank)
+        comm = mri.Communicator(uid, world, rank, ctx=ctx, timeout_ms=60000)
+        x, wq, ws = problem(1, n, k, 5)
+        w = mri.shard_quantized_matrix(wq.reshape(-1), ws, n, k, comm)
+        xd = torch.from_numpy(x).cuda(rank)
+        mri.matmul_int8_from_f32_sharded(xd, w, n, comm)
+        comm.wait()
+        if rank == 0:
+            mri.matmul_int8_from_f32_sharded(xd, w, n, comm)
+            try:
+                comm.wait()
+                results.put((rank, "no timeout"))
+            except mri.DeviceTimeout:
+                results.put((rank, "timeout"))
+            done.set()
+        else:
+            done.wait(120)
+            results.put((rank, "idle"))
+    except Exception as e:  # noqa: BLE001 - reported to the parent
+        results.put((rank, repr(e)))
+        done.set()

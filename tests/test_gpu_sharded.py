@@ -80,22 +80,48 @@ def test_comm_init_times_out_when_peer_never_joins(mri, gpu_ctx):
     assert time.time() - t0 < 30
 
 
-def test_two_ranks_match_unsharded(mri, gpu_ctx, oracle):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
-    m, n, k, seed = 4, 4096, 2048, 3
-    uid = mri.Communicator.unique_id()
+def _run_two(target, args):
+    """Spawns ranks 0 and 1 as target(rank, 2, results, *args[, event])."""
     ctx = mp.get_context("spawn")
     results = ctx.Queue()
-    procs = [ctx.Process(target=shard_workers.nccl_shard_worker, args=(r, 2, uid, m, n, k, seed, results))
-             for r in range(2)]
+    extra = (ctx.Event(),) if target is shard_workers.peer_timeout_worker else ()
+    procs = [ctx.Process(target=target, args=(r, 2, results) + args + extra) for r in range(2)]
     for p in procs:
         p.start()
-    got = dict(results.get(timeout=300) for _ in procs)
+    got = dict(results.get(timeout=180) for _ in procs)
     for p in procs:
         p.join(timeout=120)
-    x, wq, ws = shard_workers.problem(m, n, k, seed)
-    want = oracle.matmul_int8_from_f32(x, m, k, wq.reshape(-1), ws, n, k)
+    return got
+
+
+@pytest.mark.parametrize("path", ["peer", "nccl"])
+def test_two_ranks_match_unsharded(mri, gpu_ctx, oracle, path):
+    """Two GPUs: m = 1 and 4 through the peer-memory gather (or NCCL when
+    MRI_SHARD_PEER=0), m = 300 through the chunked NCCL all-gather; every
+    rank's result equals the unsharded product bit for bit."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    n, k, seed, ms = 4096, 2048, 3, (1, 4, 300, 1)
+    env = {"MRI_SHARD_PEER": "0"} if path == "nccl" else {}
+    got = _run_two(shard_workers.nccl_shard_worker, (mri.Communicator.unique_id(), ms, n, k, seed, env))
     for r in range(2):
         assert not isinstance(got[r], str), got[r]
-        np.testing.assert_array_equal(got[r], want)
+        for m in ms:
+            x, wq, ws = shard_workers.problem(m, n, k, seed + m)
+            if m <= 8:
+                want = oracle.matmul_int8_from_f32(x, m, k, wq.reshape(-1), ws, n, k)
+            else:
+                xd = torch.from_numpy(x).cuda()
+                want = mri.matmul_int8_from_f32(xd, mri.QuantizedMatrix(wq.reshape(-1), ws, n, k,
+                                                                       ctx=gpu_ctx)).cpu().numpy()
+            np.testing.assert_array_equal(got[r][m], want)
+
+
+def test_peer_gather_wait_is_bounded(mri):
+    """A rank that skips a call: the other rank's gather kernel stops waiting
+    after its budget and the host sees DeviceTimeout (no GPU fault, no hang)."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    got = _run_two(shard_workers.peer_timeout_worker, (mri.Communicator.unique_id(), 2048, 1024))
+    assert got[0] == "timeout", got
+    assert got[1] == "idle", got

@@ -226,6 +226,8 @@ int mri::matmul_int8_gather(::mri_ctx* ctx, const float* x, size_t m, size_t k,
   MRI_CUDA_TRY(mri::launch_gemv_i8_tma(ctx->dev, ctx->stream, static_cast<int>(m), w->data, w->scales,
                                        w->n_out, w->k_in, a, e.g_out, nullptr, ctx->d_status, &ctx->ls,
                                        nullptr, &e));
+  MRI_CUDA_TRY(mri::launch_gather_collect(ctx->dev, ctx->stream, e, static_cast<int>(m), ctx->d_status,
+                                          &ctx->ls));
   return MRI_OK;
 }
 

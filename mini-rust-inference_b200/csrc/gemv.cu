@@ -272,16 +272,26 @@ __device__ void load_act_i8_rowmajor(const ActArgs& act, size_t K, int8_t* s_act
                      (!act.norm_w || (reinterpret_cast<uintptr_t>(act.norm_w) & 15) == 0);
     if (false) {
     } else if (vec) {
+      // Rows of K/4 float4, four independent loads in flight per thread.
+      constexpr int U = 4;
+      constexpr int T = kConsumerThreads;
+      const int K4 = static_cast<int>(K / 4);
       if (act.norm_w) {
         for (int r = 0; r < M; ++r) {
-          const float* row = act.x + r * K;
+          const float4* row = reinterpret_cast<const float4*>(act.x + r * K);
           float ss = 0.0f;
-          for (size_t i = ct; i < K / 4; i += kConsumerThreads) {
-            const float4 t = ld_act(reinterpret_cast<const float4*>(row) + i);
-            ss = __fmaf_rn(t.x, t.x, ss);
-            ss = __fmaf_rn(t.y, t.y, ss);
-            ss = __fmaf_rn(t.z, t.z, ss);
-            ss = __fmaf_rn(t.w, t.w, ss);
+          for (int i0 = ct; i0 < K4; i0 += U * T) {
+            float4 t[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+              t[u] = i0 + u * T < K4 ? ld_act(row + i0 + u * T) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+              ss = __fmaf_rn(t[u].x, t[u].x, ss);
+              ss = __fmaf_rn(t[u].y, t[u].y, ss);
+              ss = __fmaf_rn(t[u].z, t[u].z, ss);
+              ss = __fmaf_rn(t[u].w, t[u].w, ss);
+            }
           }
           ss = consumer_sum(ss, red);
           if (ct == 0) s_inv[r] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(K)), act.eps)));
@@ -289,20 +299,37 @@ __device__ void load_act_i8_rowmajor(const ActArgs& act, size_t K, int8_t* s_act
         named_bar_sync(1, kConsumerThreads);
       }
       const bool per_row = act.mode == ACT_F32_PER_ROW;
-      for (int r = 0; r < (per_row ? M : 1); ++r) {
-        const size_t lo = per_row ? r * K / 4 : 0, hi = per_row ? (r + 1) * K / 4 : total / 4;
+      // Per tensor: one scale over all M rows; per row: one scale per row.
+      for (int r0 = 0; r0 < (per_row ? M : 1); ++r0) {
+        const int r_lo = per_row ? r0 : 0, r_hi = per_row ? r0 + 1 : M;
         float m = 0.0f;
-        for (size_t i = lo + ct; i < hi; i += kConsumerThreads)
-          m = absmax4(m, v.get(static_cast<int>((i * 4) / K), (i * 4) % K));
+        for (int r = r_lo; r < r_hi; ++r)
+          for (int i0 = ct; i0 < K4; i0 += U * T) {
+            float4 t[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+              if (i0 + u * T < K4) t[u] = v.get(r, static_cast<size_t>(i0 + u * T) * 4);
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+              if (i0 + u * T < K4) m = absmax4(m, t[u]);
+          }
         const float scale = sym_scale(consumer_max(m, red));
         const float inv = __fdiv_rn(1.0f, scale);
         if (per_row) {
-          if (ct == 0) s_scale[r] = scale;
+          if (ct == 0) s_scale[r0] = scale;
         } else if (ct < M) {
           s_scale[ct] = scale;
         }
-        for (size_t i = lo + ct; i < hi; i += kConsumerThreads)
-          reinterpret_cast<char4*>(s_act)[i] = quant4(v.get(static_cast<int>((i * 4) / K), (i * 4) % K), inv);
+        for (int r = r_lo; r < r_hi; ++r)
+          for (int i0 = ct; i0 < K4; i0 += U * T) {
+            float4 t[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+              if (i0 + u * T < K4) t[u] = v.get(r, static_cast<size_t>(i0 + u * T) * 4);
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+              if (i0 + u * T < K4) reinterpret_cast<char4*>(s_act)[r * K4 + i0 + u * T] = quant4(t[u], inv);
+          }
       }
     } else {
       // Scalar path (unaligned input; no fused producer ops reach here).
@@ -422,43 +449,36 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned 
   return v;
 }
 
-// EPI_GATHER tail, consumer threads: count this CTA in on every rank, wait
-// until every CTA of every rank has arrived here, copy this CTA's share of the
-// staged result out, and (last CTA) advance the call sequence.
+// EPI_GATHER tail, consumer threads.  The CTA's output rows were collected in
+// shared memory (s_out [M][cap]); they are written to every rank's staging
+// with coalesced stores (one remote transfer per 128 bytes instead of one per
+// value), fenced, and the CTA counts itself in on every rank's arrival
+// counter.  The kernel does not wait: gather_collect_kernel, launched after
+// it, waits for the other ranks and copies the result out, so this grid's
+// CTAs retire as soon as their rows are done.
+// Call state (g_seq, local): [0] arrivals expected after the last call,
+// [1] CTA ticket, [2] calls issued (parity = staging half).
 template <int M>
-__device__ void gather_finish(const EpiArgs& epi, unsigned long long seq, int* status, int* s_flag) {
-  __threadfence_system();  // this thread's stores to all ranks' staging
+__device__ void gather_signal(const EpiArgs& epi, unsigned long long seq, size_t N, size_t begin,
+                              size_t end, const float* s_out, int cap) {
+  named_bar_sync(1, kConsumerThreads);
+  const int ct = threadIdx.x - 32;
+  const int rows = static_cast<int>(end - begin);
+  const size_t half = (seq & 1) * epi.g_half;
+  for (int p = 0; p < epi.g_ranks; ++p)
+    for (int m = 0; m < M; ++m) {
+      float* dst = epi.g_stage[p] + half + m * epi.g_ntotal + epi.g_rank * N + begin;
+      for (int i = ct; i < rows; i += kConsumerThreads) dst[i] = s_out[m * cap + i];
+    }
+  __threadfence_system();
   named_bar_sync(1, kConsumerThreads);
   if (threadIdx.x == 32) {
     for (int p = 0; p < epi.g_ranks; ++p) atomicAdd_system(epi.g_ctr[p], 1ull);
-    const unsigned long long target =
-        (seq + 1) * static_cast<unsigned long long>(epi.g_ranks) * gridDim.x;
-    int ok = 1;
-    const long long t0 = clock64();
-    while (ld_acquire_sys_u64(epi.g_ctr[epi.g_rank]) < target) {
-      if (clock64() - t0 > kWaitBudgetClocks) {
-        *reinterpret_cast<volatile int*>(status) = MRI_ERR_TIMEOUT;
-        ok = 0;
-        break;
-      }
-      __nanosleep(64);
-    }
-    *s_flag = ok;
-  }
-  named_bar_sync(1, kConsumerThreads);
-  if (*s_flag) {
-    const size_t total = static_cast<size_t>(M) * epi.g_ntotal;
-    const size_t per = (total + gridDim.x - 1) / gridDim.x;
-    const size_t lo = std::min(total, per * blockIdx.x), hi = std::min(total, lo + per);
-    const float* src = epi.g_stage[epi.g_rank] + (seq & 1) * epi.g_half;
-    for (size_t i = lo + (threadIdx.x - 32); i < hi; i += kConsumerThreads) epi.g_out[i] = ld_act(src + i);
-  }
-  named_bar_sync(1, kConsumerThreads);
-  if (threadIdx.x == 32) {
     __threadfence();
     if (atomicAdd(epi.g_seq + 1, 1ull) == gridDim.x - 1) {
       epi.g_seq[1] = 0;
-      epi.g_seq[0] = seq + 1;
+      epi.g_seq[0] += static_cast<unsigned long long>(epi.g_ranks) * gridDim.x;
+      epi.g_seq[2] = seq + 1;
       __threadfence();
     }
   }
@@ -502,9 +522,11 @@ __global__ void __launch_bounds__(kThreads, M <= 2 ? 2 : 1)
   }
   pdl_wait();
   load_act_i8_rowmajor<M, VEC>(act, K, s_act, s_scale, red, act_issued);
-  __shared__ int s_flag;
+  // EPI_GATHER: this CTA's outputs [M][cap], written to all ranks at the end.
+  constexpr int kGatherCap = EPI == 2 ? 1024 / M : 1;
+  __shared__ float s_gout[EPI == 2 ? 1024 : 1];
   unsigned long long seq = 0;
-  if constexpr (EPI == 2) seq = ld_act(epi.g_seq);
+  if constexpr (EPI == 2) seq = ld_act(epi.g_seq + 2);
   float s_a[M];
 #pragma unroll
   for (int m = 0; m < M; ++m) s_a[m] = s_scale[m];
@@ -561,10 +583,7 @@ __global__ void __launch_bounds__(kThreads, M <= 2 ? 2 : 1)
     if constexpr (EPI == 1) {
       pair_epilogue(epi, M, N, row, valid, val, lane, cw, g, s_pair, out);
     } else if constexpr (EPI == 2) {
-      if (valid && lane < M) {
-        const size_t off = (seq & 1) * epi.g_half + lane * epi.g_ntotal + epi.g_rank * N + row;
-        for (int p = 0; p < epi.g_ranks; ++p) epi.g_stage[p][off] = val;
-      }
+      if (valid && lane < M) s_gout[lane * kGatherCap + (row - begin)] = val;
     } else if (valid && lane < M) {
       // forward_int8.rs:100-121: x + projected (residual may alias out).
       out[lane * N + row] = residual ? __fadd_rn(ld_act(residual + lane * N + row), val) : val;
@@ -575,7 +594,7 @@ __global__ void __launch_bounds__(kThreads, M <= 2 ? 2 : 1)
       }
     }
   }
-  if constexpr (EPI == 2) gather_finish<M>(epi, seq, status, &s_flag);
+  if constexpr (EPI == 2) gather_signal<M>(epi, seq, N, begin, end, s_gout, kGatherCap);
 }
 
 // ── generic INT8 GEMV: any K / alignment, pre-quantized activations ─────────
@@ -1051,36 +1070,35 @@ int resident_ctas(KernelT k, size_t smem, int device) {
 }
 
 // Launch with the programmatic-stream-serialization attribute when enabled.
-// `cooperative`: the CTAs wait on one another, so all must be resident.
 template <typename... KArgs, typename... Args>
-cudaError_t launch_stream_kernel_ex(bool cooperative, void (*k)(KArgs...), int grid, size_t smem,
-                                    cudaStream_t st, Args&&... args) {
+cudaError_t launch_stream_kernel(void (*k)(KArgs...), int grid, size_t smem, cudaStream_t st,
+                                 Args&&... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[2];
-  int n = 0;
-  if (tuning().pdl) {
-    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[n].val.programmaticStreamSerializationAllowed = 1;
-    ++n;
-  }
-  if (cooperative) {
-    attr[n].id = cudaLaunchAttributeCooperative;
-    attr[n].val.cooperative = 1;
-    ++n;
-  }
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = n;
+  cfg.numAttrs = tuning().pdl ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, k, std::forward<Args>(args)...);
 }
 
 template <typename... KArgs, typename... Args>
-cudaError_t launch_stream_kernel(void (*k)(KArgs...), int grid, size_t smem, cudaStream_t st,
-                                 Args&&... args) {
-  return launch_stream_kernel_ex(false, k, grid, smem, st, std::forward<Args>(args)...);
+cudaError_t launch_stream_kernel_threads(void (*k)(KArgs...), int grid, int threads, cudaStream_t st,
+                                         Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(threads);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = tuning().pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, k, static_cast<KArgs>(args)...);
 }
 
 #define MRI_DISPATCH_M(M, ...)                           \
@@ -1217,15 +1235,67 @@ cudaError_t launch_gemv_i8_tma(const DeviceInfo& dev, cudaStream_t st, int M, co
   }
   GemvPlan p;
   if (cudaError_t e = gemv_i8_tma_plan(dev, M, N, K, &p, reg_vec(M, K, &act), kind)) return e;
+  // A gather CTA keeps its output rows in a 1024-float shared buffer.
+  if (kind == 2 && ((N + p.grid - 1) / p.grid) * M > 1024) return cudaErrorInvalidValue;
   const int pre = pre_stages(p.stages);
   MRI_DISPATCH_I8_TMA(M, p.vec, p.k_chunks > 1, p.epi, {
-    cudaError_t e = launch_stream_kernel_ex(kind == 2, kKernel, p.grid, p.smem, st, W, w_scales, N, K,
-                                            act, out, acc_out, p.stages, p.k_chunks, pre, status,
-                                            residual, e_args);
+    // The gather CTAs wait for one another, so all must be resident at once:
+    // the grid never exceeds the CTAs that fit (resident_ctas), and a
+    // dependent launch can only start once every CTA of this grid has
+    // started.  A cooperative launch would also serialise it against the
+    // previous kernel, which costs more than the wait saves.
+    cudaError_t e = launch_stream_kernel(kKernel, p.grid, p.smem, st, W, w_scales, N, K, act, out,
+                                         acc_out, p.stages, p.k_chunks, pre, status, residual, e_args);
     if (e != cudaSuccess) return e;
   });
   if (ls) ls->launches++;
   return cudaGetLastError();
+}
+
+// Second half of the peer gather: wait (bounded) until every rank's CTAs of the
+// preceding gather GEMV have arrived on the local counter, then copy the
+// assembled [M][n_total] result from the staging half of that call to out.
+__global__ void __launch_bounds__(256) gather_collect_kernel(const unsigned long long* ctr,
+                                                             const unsigned long long* call,
+                                                             const float* stage, size_t half,
+                                                             size_t total, float* out, int* status) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  __shared__ int s_ok;
+  const unsigned long long target = ld_act(call);
+  const unsigned long long issued = ld_act(call + 2);
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    const long long t0 = clock64();
+    while (ld_acquire_sys_u64(ctr) < target) {
+      if (clock64() - t0 > kWaitBudgetClocks) {
+        *reinterpret_cast<volatile int*>(status) = MRI_ERR_TIMEOUT;
+        ok = 0;
+        break;
+      }
+      __nanosleep(64);
+    }
+    s_ok = ok;
+  }
+  __syncthreads();
+  if (!s_ok) return;
+  const float* src = stage + ((issued - 1) & 1) * half;
+  const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total; i += stride)
+    out[i] = ld_act(src + i);
+}
+
+cudaError_t launch_gather_collect(const DeviceInfo& dev, cudaStream_t st, const EpiArgs& e, int M,
+                                  int* status, LaunchStats* ls) {
+  const size_t total = static_cast<size_t>(M) * e.g_ntotal;
+  const int grid = static_cast<int>(std::max<size_t>(1, std::min<size_t>(dev.sm_count, (total + 1023) / 1024)));
+  cudaError_t err = launch_stream_kernel_threads(gather_collect_kernel, grid, 256, st,
+                                                 static_cast<const unsigned long long*>(e.g_ctr[e.g_rank]),
+                                                 static_cast<const unsigned long long*>(e.g_seq),
+                                                 static_cast<const float*>(e.g_stage[e.g_rank]), e.g_half, total,
+                                                 e.g_out, status);
+  if (ls) ls->launches++;
+  return err;
 }
 
 cudaError_t launch_gemv_i8_generic(const DeviceInfo& dev, cudaStream_t st, int M, const int8_t* W,

@@ -49,13 +49,11 @@ enum EpiMode : int {
   // else pos0), written to out; rotated k and plain v also written to the
   // cache rows kc/vc [pos + m] (attention/cached.rs:90-93).
   EPI_ROPE_KV = 2,
-  // N-sharded product gathered over peer memory (no NCCL): every output value
-  // is also stored into the staging buffer of every rank ([2][M][n_total],
-  // half `seq & 1`, columns of rank r at [r*N, (r+1)*N)); each CTA then counts
-  // itself in on every rank's arrival counter, waits (bounded) until all
-  // ranks' CTAs have arrived on its own, and copies its share of the staged
-  // [M][n_total] result to `g_out`.  The last CTA advances the local call
-  // sequence.
+  // N-sharded product gathered over peer memory (no NCCL): each CTA writes its
+  // output rows into the staging buffer of every rank ([2][M][n_total], half =
+  // parity of the call count, columns of rank r at [r*N, (r+1)*N)) and counts
+  // itself in on every rank's arrival counter; launch_gather_collect then
+  // waits for all ranks and copies the staged result to `g_out`.
   EPI_GATHER = 3,
 };
 
@@ -72,7 +70,7 @@ struct EpiArgs {
   static constexpr int kMaxRanks = 8;
   float* g_stage[kMaxRanks] = {};              // per rank (peer pointers)
   unsigned long long* g_ctr[kMaxRanks] = {};   // per rank arrival counters
-  unsigned long long* g_seq = nullptr;         // local: [0] calls done, [1] CTA ticket
+  unsigned long long* g_seq = nullptr;         // local call state, 4 words (gemv.cu)
   size_t g_half = 0;                           // floats per staging half
   size_t g_ntotal = 0;
   int g_ranks = 1, g_rank = 0;
@@ -126,6 +124,10 @@ cudaError_t launch_gemv_i8_tma(const DeviceInfo& dev, cudaStream_t st, int M, co
                                const float* w_scales, size_t N, size_t K, const ActArgs& act,
                                float* out, int32_t* acc_out, int* status, LaunchStats* ls,
                                const float* residual = nullptr, const EpiArgs* epi = nullptr);
+// Second kernel of an EPI_GATHER product: waits (bounded) for every rank's
+// arrivals of the preceding gather GEMV and copies [M][n_total] to e.g_out.
+cudaError_t launch_gather_collect(const DeviceInfo& dev, cudaStream_t st, const EpiArgs& e, int M,
+                                  int* status, LaunchStats* ls);
 // Any K, any alignment; activations must be pre-quantized (modes 2-4).
 cudaError_t launch_gemv_i8_generic(const DeviceInfo& dev, cudaStream_t st, int M, const int8_t* W,
                                    const float* w_scales, size_t N, size_t K, const ActArgs& act,

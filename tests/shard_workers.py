@@ -84,6 +84,7 @@ def peer_timeout_worker(rank, world, results, uid, n, k, done):
     rank 1 skips.  Rank 0's kernel must give up waiting for rank 1's arrivals
     (bounded wait) and report a timeout.  Rank 1 stays alive, with its buffers
     mapped and no work in flight, until rank 0 is done."""
+    os.environ["MRI_SHARD_PEER"] = "1"
     import torch
 
     from conftest import load_mri

@@ -96,13 +96,13 @@ def _run_two(target, args):
 
 @pytest.mark.parametrize("path", ["peer", "nccl"])
 def test_two_ranks_match_unsharded(mri, gpu_ctx, oracle, path):
-    """Two GPUs: m = 1 and 4 through the peer-memory gather (or NCCL when
-    MRI_SHARD_PEER=0), m = 300 through the chunked NCCL all-gather; every
-    rank's result equals the unsharded product bit for bit."""
+    """Two GPUs: m = 1 and 4 through the peer-memory gather
+    (MRI_SHARD_PEER=1) or NCCL, m = 300 through the chunked NCCL all-gather;
+    every rank's result equals the unsharded product bit for bit."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     n, k, seed, ms = 4096, 2048, 3, (1, 4, 300, 1)
-    env = {"MRI_SHARD_PEER": "0"} if path == "nccl" else {}
+    env = {"MRI_SHARD_PEER": "0" if path == "nccl" else "1"}
     got = _run_two(shard_workers.nccl_shard_worker, (mri.Communicator.unique_id(), ms, n, k, seed, env))
     for r in range(2):
         assert not isinstance(got[r], str), got[r]

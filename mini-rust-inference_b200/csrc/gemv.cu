@@ -91,12 +91,15 @@ __device__ __forceinline__ void cta_rows(size_t N, size_t gran, size_t& begin, s
 // [begin + 8*it, ...) whose bytes start at W + row*row_bytes.
 __device__ void stream_producer(const uint8_t* W, size_t row_bytes, size_t begin, size_t end,
                                 uint64_t* full, uint64_t* empty, uint8_t* stages_base,
-                                size_t stage_stride, int n_stages, int* status) {
+                                size_t stage_stride, int n_stages, int* status,
+                                uint64_t* act_issued = nullptr, int pre = 1 << 30) {
   const uint64_t policy = l2_policy_evict_first();
   const int iters = static_cast<int>((end - begin + kRowsPerStage - 1) / kRowsPerStage);
   int issued = 0;
   for (int it = 0; it < iters; ++it) {
     const int s = it % n_stages;
+    // Stages after the first `pre` wait until the activation loads are issued.
+    if (act_issued && it == pre && !mbar_wait(act_issued, 0, status)) break;
     if (it >= n_stages) {
       if (!mbar_wait(&empty[s], ((it / n_stages) - 1) & 1, status)) break;
     }
@@ -661,11 +664,11 @@ __device__ __forceinline__ void load_q8_block(const uint8_t* blk, uint32_t& dbit
 
 __host__ __device__ constexpr size_t q8_term_stride(size_t nb) { return align_up(nb, 4) + 4; }
 
-template <int M>
+template <int M, int VEC>
 __global__ void __launch_bounds__(kThreads, M <= 2 ? 2 : 1)
     gemv_q8_0_tma_kernel(const uint8_t* __restrict__ W, size_t N, size_t K,
                          const float* __restrict__ x, float* __restrict__ out, int n_stages,
-                         int* status) {
+                         int pre, int* status) {
   extern __shared__ __align__(128) uint8_t smem[];
   const size_t nb = K / 32;
   const size_t row_bytes = nb * 34;
@@ -684,22 +687,23 @@ __global__ void __launch_bounds__(kThreads, M <= 2 ? 2 : 1)
   const size_t g = 8 / (nb % 8 == 0 ? 8 : (nb % 4 == 0 ? 4 : (nb % 2 == 0 ? 2 : 1)));
   size_t begin, end;
   cta_rows(N, g, begin, end);
-  init_barriers(full, empty, n_stages);
+  uint64_t* act_issued = empty + n_stages;
+  init_barriers(full, empty, n_stages, act_issued);
   if (begin >= end) return;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (warp == 0) {
     if (lane == 0)
       stream_producer(W, row_bytes, begin, end, full, empty, stage0, L.stage_bytes, n_stages,
-                      status);
+                      status, act_issued, pre);
     return;
   }
   pdl_wait();
-  // Prologue: per-row quantization (q8_direct.rs:264).
+  // Prologue: per-row quantization (q8_direct.rs:264); one row is one tensor.
   ActArgs act;
   act.x = x;
-  act.mode = ACT_F32_PER_ROW;
-  load_act_i8_rowmajor<M, 0>(act, K, s_act, s_scale, red, nullptr);
+  act.mode = M == 1 ? ACT_F32_PER_TENSOR : ACT_F32_PER_ROW;
+  load_act_i8_rowmajor<M, VEC>(act, K, s_act, s_scale, red, act_issued);
   float s_a[M];
 #pragma unroll
   for (int m = 0; m < M; ++m) s_a[m] = s_scale[m];
@@ -833,7 +837,7 @@ template <int M>
 __global__ void __launch_bounds__(kThreads, M <= 2 ? 2 : 1)
     gemv_q4_0_tma_kernel(const uint8_t* __restrict__ W, size_t N, size_t K,
                          const float* __restrict__ x, float* __restrict__ out, int n_stages,
-                         int* status) {
+                         int pre, int* status) {
   extern __shared__ __align__(128) uint8_t smem[];
   const size_t nb = K / 32;
   const size_t row_bytes = nb * 18;
@@ -846,28 +850,55 @@ __global__ void __launch_bounds__(kThreads, M <= 2 ? 2 : 1)
   const size_t g = 8 / (nb % 8 == 0 ? 8 : (nb % 4 == 0 ? 4 : (nb % 2 == 0 ? 2 : 1)));
   size_t begin, end;
   cta_rows(N, g, begin, end);
-  init_barriers(full, empty, n_stages);
+  uint64_t* act_issued = empty + n_stages;
+  init_barriers(full, empty, n_stages, act_issued);
   if (begin >= end) return;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (warp == 0) {
     if (lane == 0)
       stream_producer(W, row_bytes, begin, end, full, empty, stage0, L.stage_bytes, n_stages,
-                      status);
+                      status, act_issued, pre);
     return;
   }
   pdl_wait();
   // Activations as float4 chunks transposed to [m][chunk 0..7][block], so
-  // lane b reads chunk c of block b conflict-free.
+  // lane b reads chunk c of block b conflict-free.  Four independent loads in
+  // flight per thread; each consumer warp arrives on act_issued once its
+  // first loads are issued (the producer holds back later weight stages).
   const int ct = threadIdx.x - 32;
-  for (size_t i = ct; i < static_cast<size_t>(M) * K / 4; i += kConsumerThreads) {
-    const size_t r = (i * 4) / K, k = (i * 4) % K;
-    float4 v;
-    v.x = ld_act(x + r * K + k);
-    v.y = ld_act(x + r * K + k + 1);
-    v.z = ld_act(x + r * K + k + 2);
-    v.w = ld_act(x + r * K + k + 3);
-    s_x4[(r * 8 + (k % 32) / 4) * nb + k / 32] = v;
+  const int K4 = static_cast<int>(K / 4), n4 = M * K4;
+  const bool xvec = (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+  constexpr int U = 4;
+  const int rounds = (n4 + U * kConsumerThreads - 1) / (U * kConsumerThreads);
+  for (int rd = 0; rd < std::max(rounds, 1); ++rd) {
+    float4 v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int idx = rd * U * kConsumerThreads + u * kConsumerThreads + ct;
+      if (idx < n4) {
+        if (xvec) {
+          v[u] = ld_act(reinterpret_cast<const float4*>(x) + idx);
+        } else {
+          v[u].x = ld_act(x + 4 * static_cast<size_t>(idx));
+          v[u].y = ld_act(x + 4 * static_cast<size_t>(idx) + 1);
+          v[u].z = ld_act(x + 4 * static_cast<size_t>(idx) + 2);
+          v[u].w = ld_act(x + 4 * static_cast<size_t>(idx) + 3);
+        }
+      }
+    }
+    if (rd == 0) {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(act_issued);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int idx = rd * U * kConsumerThreads + u * kConsumerThreads + ct;
+      if (idx < n4) {
+        const int r = idx / K4, k = (idx - r * K4) * 4;
+        s_x4[(r * 8 + (k % 32) / 4) * nb + k / 32] = v[u];
+      }
+    }
   }
   named_bar_sync(1, kConsumerThreads);
 
@@ -1325,14 +1356,21 @@ cudaError_t launch_gemv_q8_0_tma(const DeviceInfo& dev, cudaStream_t st, int M, 
   const int stages = cfg.stages;
   if (stages < 2) return cudaErrorInvalidValue;
   const size_t smem = make_layout(M * K, extra, kRowsPerStage * nb * 34, stages).total;
+  // M = 1: per-row is per-tensor, so the register prologue applies.
+  ActArgs probe;
+  probe.x = x;
+  const int vec = M == 1 ? reg_vec(1, K, &probe) : 0;
+  const int pre = pre_stages(stages);
   MRI_DISPATCH_M(M, {
-    cudaError_t e = set_smem(gemv_q8_0_tma_kernel<kM>, smem, dev.device);
-    if (e != cudaSuccess) return e;
-    const int grid = stream_grid(
-        dev, N, std::min(cfg.ctas_per_sm, resident_ctas(gemv_q8_0_tma_kernel<kM>, smem, dev.device)));
-    e = launch_stream_kernel(gemv_q8_0_tma_kernel<kM>, grid, smem, st, W, N, K, x, out, stages,
-                             status);
-    if (e != cudaSuccess) return e;
+    MRI_DISPATCH_VEC(M == 1 ? vec : 0, {
+      auto kern = gemv_q8_0_tma_kernel<kM, (kM == 1 ? kV : 0)>;
+      cudaError_t e = set_smem(kern, smem, dev.device);
+      if (e != cudaSuccess) return e;
+      const int grid =
+          stream_grid(dev, N, std::min(cfg.ctas_per_sm, resident_ctas(kern, smem, dev.device)));
+      e = launch_stream_kernel(kern, grid, smem, st, W, N, K, x, out, stages, pre, status);
+      if (e != cudaSuccess) return e;
+    });
   });
   if (ls) ls->launches++;
   return cudaGetLastError();
@@ -1368,7 +1406,7 @@ cudaError_t launch_gemv_q4_0_tma(const DeviceInfo& dev, cudaStream_t st, int M, 
     const int grid = stream_grid(
         dev, N, std::min(cfg.ctas_per_sm, resident_ctas(gemv_q4_0_tma_kernel<kM>, smem, dev.device)));
     e = launch_stream_kernel(gemv_q4_0_tma_kernel<kM>, grid, smem, st, W, N, K, x, out, stages,
-                             status);
+                             pre_stages(stages), status);
     if (e != cudaSuccess) return e;
   });
   if (ls) ls->launches++;

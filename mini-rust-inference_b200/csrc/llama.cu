@@ -101,11 +101,13 @@ __global__ void rope_kv_kernel(float* __restrict__ qkv, int ld, int n_heads, int
 
 // Decode attention, split over keys (attention/cached.rs:141-190 with
 // gqa.rs:217-237): block (h, s) handles keys [s*64, min(s*64+64, pos+1)).
-// Every thread issues its V-tile loads and its K loads (two threads per key,
-// half a row each) before using any of them, so the block waits for memory
-// about once.  Each block writes its max, exp-sum and weighted V sum; the
-// last block of a head to finish (ticket counter) merges the head's splits
-// and resets the counter for the next launch.  hd % 8 == 0, hd <= 128.
+// Warp w takes 16 of them in two rounds of 8; a lane owns 4 head dimensions
+// (hd % 4 == 0, hd <= 128), loads the 8 keys' and values' float4 before using
+// any, reduces each score over the warp with shuffles and keeps an online
+// softmax (running max, exp-sum, weighted V sum) — no block-wide barrier until
+// the 4 warps' partials are combined.  Each block writes its partial; the last
+// block of a head to finish (ticket counter) merges the head's splits and
+// resets the counter for the next launch.
 __global__ void __launch_bounds__(128) attn_decode_kernel(const float* __restrict__ q, int n_heads,
                                                           int n_kv, int hd,
                                                           const float* __restrict__ kc,
@@ -125,83 +127,68 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const float* __restric
   const int kv_h = h / (n_heads / n_kv);
   const int kvd = n_kv * hd;
   constexpr int kStride = kMaxHeadDim + 2;
-  __shared__ __align__(16) float sq[kMaxHeadDim];
-  __shared__ __align__(16) float sv[kAttnChunk * kMaxHeadDim];
-  __shared__ float sp[kAttnChunk];
-  __shared__ float red[4];
+  constexpr int kRound = 8;  // keys in flight per warp
+  __shared__ float wm[4], wl[4];
+  __shared__ __align__(16) float wo[4][kMaxHeadDim];
   __shared__ int last;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int hd4 = hd / 4;
-  const float* kbase = kc + static_cast<size_t>(j0) * kvd + kv_h * hd;
-  const float* vbase = vc + static_cast<size_t>(j0) * kvd + kv_h * hd;
-  constexpr int kV4 = kAttnChunk * kMaxHeadDim / 4 / 128;  // float4 of the V tile per thread
-  float4 v4[kV4];
+  const bool dim_ok = lane * 4 < hd;
+  const size_t base = static_cast<size_t>(kv_h) * hd + lane * 4;
+  const float4 qv = dim_ok ? mri::ld_act(reinterpret_cast<const float4*>(q + h * hd + lane * 4))
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+  float m = -INFINITY, l = 0.0f;
+  float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int r = 0; r < 2; ++r) {
+    const int k0 = warp * 2 * kRound + r * kRound;  // first key of this round, within the chunk
+    float4 kk[kRound], vv[kRound];
 #pragma unroll
-  for (int i = 0; i < kV4; ++i) {
-    const int idx = threadIdx.x + 128 * i;
-    const int j = idx / hd4, d4 = idx - j * hd4;
-    v4[i] = j < nkeys ? mri::ld_act(reinterpret_cast<const float4*>(vbase + static_cast<size_t>(j) * kvd) + d4)
-                      : make_float4(0.f, 0.f, 0.f, 0.f);
-  }
-  const int jk = threadIdx.x >> 1, half = threadIdx.x & 1;
-  const int hh4 = hd4 / 2;
-  float4 k4[kMaxHeadDim / 8];
+    for (int i = 0; i < kRound; ++i) {
+      const bool ok = dim_ok && k0 + i < nkeys;
+      const size_t row = static_cast<size_t>(j0 + k0 + i) * kvd + base;
+      kk[i] = ok ? mri::ld_act(reinterpret_cast<const float4*>(kc + row)) : make_float4(0.f, 0.f, 0.f, 0.f);
+      vv[i] = ok ? mri::ld_act(reinterpret_cast<const float4*>(vc + row)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
 #pragma unroll
-  for (int i = 0; i < kMaxHeadDim / 8; ++i)
-    k4[i] = (jk < nkeys && i < hh4)
-                ? mri::ld_act(reinterpret_cast<const float4*>(kbase + static_cast<size_t>(jk) * kvd) + half * hh4 + i)
-                : make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int t = threadIdx.x; t < hd; t += blockDim.x) sq[t] = mri::ld_act(q + h * hd + t);
-  __syncthreads();
-  float dot = 0.0f;
-#pragma unroll
-  for (int i = 0; i < kMaxHeadDim / 8; ++i) {
-    if (i < hh4) {
-      const float4 qq = reinterpret_cast<const float4*>(sq)[half * hh4 + i];
-      dot = __fmaf_rn(qq.x, k4[i].x, dot);
-      dot = __fmaf_rn(qq.y, k4[i].y, dot);
-      dot = __fmaf_rn(qq.z, k4[i].z, dot);
-      dot = __fmaf_rn(qq.w, k4[i].w, dot);
+    for (int i = 0; i < kRound; ++i) {
+      if (k0 + i >= nkeys) break;  // warp-uniform
+      float d = __fmaf_rn(qv.x, kk[i].x, 0.0f);
+      d = __fmaf_rn(qv.y, kk[i].y, d);
+      d = __fmaf_rn(qv.z, kk[i].z, d);
+      d = __fmaf_rn(qv.w, kk[i].w, d);
+      d = mri::warp_sum_f(d);
+      const float sc = __fmul_rn(d, scale);
+      const float mn = fmaxf(m, sc);
+      const float corr = expf(m - mn), p = expf(sc - mn);
+      l = __fadd_rn(__fmul_rn(l, corr), p);
+      o.x = __fmaf_rn(p, vv[i].x, __fmul_rn(o.x, corr));
+      o.y = __fmaf_rn(p, vv[i].y, __fmul_rn(o.y, corr));
+      o.z = __fmaf_rn(p, vv[i].z, __fmul_rn(o.z, corr));
+      o.w = __fmaf_rn(p, vv[i].w, __fmul_rn(o.w, corr));
+      m = mn;
     }
   }
-  dot += __shfl_xor_sync(0xffffffffu, dot, 1);
-  if (half == 0 && jk < nkeys) sp[jk] = __fmul_rn(dot, scale);
-#pragma unroll
-  for (int i = 0; i < kV4; ++i) reinterpret_cast<float4*>(sv)[threadIdx.x + 128 * i] = v4[i];
-  __syncthreads();
-  float mx = -INFINITY;
-  for (int t = threadIdx.x; t < nkeys; t += blockDim.x) mx = fmaxf(mx, sp[t]);
-  mx = mri::warp_max(mx);
-  if (lane == 0) red[warp] = mx;
-  __syncthreads();
-  mx = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
-  __syncthreads();
-  float l = 0.0f;
-  for (int t = threadIdx.x; t < nkeys; t += blockDim.x) {
-    const float p = expf(sp[t] - mx);
-    sp[t] = p;
-    l += p;
+  // Combine the 4 warps (a warp without keys has m = -inf, l = 0).
+  if (lane == 0) {
+    wm[warp] = m;
+    wl[warp] = l;
   }
-  l = mri::warp_sum_f(l);
-  if (lane == 0) red[warp] = l;
+  if (dim_ok) reinterpret_cast<float4*>(wo[warp])[lane] = o;
   __syncthreads();
-  l = red[0] + red[1] + red[2] + red[3];
+  const float bm = fmaxf(fmaxf(wm[0], wm[1]), fmaxf(wm[2], wm[3]));
   float* pout = part + (static_cast<size_t>(h) * max_splits + s) * kStride;
   for (int t = threadIdx.x; t < hd; t += blockDim.x) {
-    float o0 = 0.0f, o1 = 0.0f, o2 = 0.0f, o3 = 0.0f;
-    int j = 0;
-    for (; j + 4 <= nkeys; j += 4) {
-      o0 = __fmaf_rn(sp[j], sv[j * hd + t], o0);
-      o1 = __fmaf_rn(sp[j + 1], sv[(j + 1) * hd + t], o1);
-      o2 = __fmaf_rn(sp[j + 2], sv[(j + 2) * hd + t], o2);
-      o3 = __fmaf_rn(sp[j + 3], sv[(j + 3) * hd + t], o3);
-    }
-    for (; j < nkeys; ++j) o0 = __fmaf_rn(sp[j], sv[j * hd + t], o0);
-    pout[2 + t] = (o0 + o1) + (o2 + o3);
+    float acc = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w)
+      if (wm[w] != -INFINITY) acc = __fmaf_rn(wo[w][t], expf(wm[w] - bm), acc);
+    pout[2 + t] = acc;
   }
   if (threadIdx.x == 0) {
-    pout[0] = mx;
-    pout[1] = l;
+    float bl = 0.0f;
+    for (int w = 0; w < 4; ++w)
+      if (wm[w] != -INFINITY) bl = __fmaf_rn(wl[w], expf(wm[w] - bm), bl);
+    pout[0] = bm;
+    pout[1] = bl;
   }
   // Publish this split, then take a ticket; the last split of the head merges.
   __threadfence();
@@ -217,10 +204,10 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const float* __restric
   for (int t = 0; t < active; ++t) gl += __ldcg(ph + t * kStride + 1) * expf(__ldcg(ph + t * kStride) - gm);
   const float inv = __fdiv_rn(1.0f, gl);
   for (int d = threadIdx.x; d < hd; d += blockDim.x) {
-    float o = 0.0f;
+    float acc = 0.0f;
     for (int t = 0; t < active; ++t)
-      o += __ldcg(ph + t * kStride + 2 + d) * expf(__ldcg(ph + t * kStride) - gm);
-    out[h * hd + d] = o * inv;
+      acc += __ldcg(ph + t * kStride + 2 + d) * expf(__ldcg(ph + t * kStride) - gm);
+    out[h * hd + d] = acc * inv;
   }
   if (threadIdx.x == 0) tickets[h] = 0;
 }

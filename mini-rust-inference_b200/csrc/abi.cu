@@ -350,123 +350,6 @@ int host_stage(mri_ctx* ctx, size_t in_bytes, size_t out_bytes, size_t acc_bytes
 
 }  // namespace
 
-namespace {
-
-// ── replayable host-buffer calls ─────────────────────────────────────────────
-// A decode-size host call (x H2D, fused GEMV, out D2H, sync) costs several
-// separate submissions.  From the second call with the same weights and shape
-// on, the three operations are replayed from one CUDA graph whose copy nodes
-// are pointed at the caller's (pinned) buffers each time.  The graph keeps the
-// scratch addresses it was captured with, so it is rebuilt when the scratch
-// moves.  Pageable buffers take the stream path.
-struct HostGraph {
-  const int8_t* data = nullptr;
-  const float* scales = nullptr;
-  size_t m = 0, k = 0, n = 0;
-  const uint8_t* scratch = nullptr;
-  int seen = 0;
-  cudaGraphExec_t exec = nullptr;
-  cudaGraphNode_t h2d = nullptr, d2h = nullptr;
-};
-
-struct HostGraphs {
-  std::vector<HostGraph> entries;
-};
-
-bool pinned(const void* p) {
-  cudaPointerAttributes a;
-  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
-    cudaGetLastError();
-    return false;
-  }
-  return a.type == cudaMemoryTypeHost;
-}
-
-void free_host_graphs(mri_ctx* ctx) {
-  auto* hg = static_cast<HostGraphs*>(ctx->host_graphs);
-  if (!hg) return;
-  for (auto& e : hg->entries)
-    if (e.exec) cudaGraphExecDestroy(e.exec);
-  delete hg;
-  ctx->host_graphs = nullptr;
-}
-
-// Returns false to let the caller take the stream path (first call of a
-// shape, or the graph could not be built); *rc is the call's status otherwise.
-bool host_graph_call(mri_ctx* ctx, const float* x, size_t m, size_t k, const mri_qmatrix* w,
-                     float* out, const HostStage& hs, int* rc) {
-  if (!ctx->host_graphs) ctx->host_graphs = new HostGraphs();
-  auto& entries = static_cast<HostGraphs*>(ctx->host_graphs)->entries;
-  HostGraph* e = nullptr;
-  for (auto& c : entries)
-    if (c.data == w->data && c.scales == w->scales && c.m == m && c.k == k && c.n == w->n_out) e = &c;
-  if (!e) {
-    if (entries.size() >= 16) {
-      if (entries.front().exec) cudaGraphExecDestroy(entries.front().exec);
-      entries.erase(entries.begin());
-    }
-    entries.push_back(HostGraph{w->data, w->scales, m, k, w->n_out});
-    e = &entries.back();
-  }
-  if (e->exec && e->scratch != ctx->scratch) {
-    cudaGraphExecDestroy(e->exec);
-    e->exec = nullptr;
-  }
-  if (!e->exec) {
-    if (e->seen++ == 0) return false;  // the first call runs eagerly and warms the launch caches
-    cudaStream_t st = ctx->stream;
-    cudaGraph_t g = nullptr;
-    if (cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
-      cudaGetLastError();
-      return false;
-    }
-    ActArgs a;
-    a.x = reinterpret_cast<float*>(hs.in);
-    a.mode = mri::ACT_F32_PER_TENSOR;
-    bool ok = cudaMemcpyAsync(hs.in, x, m * k * 4, cudaMemcpyHostToDevice, st) == cudaSuccess;
-    ok = ok && run_int8(ctx, a, w, m, hs.out, nullptr) == MRI_OK;
-    ok = ok && cudaMemcpyAsync(out, hs.out, m * w->n_out * 4, cudaMemcpyDeviceToHost, st) == cudaSuccess;
-    const bool ended = cudaStreamEndCapture(st, &g) == cudaSuccess;
-    if (!ok || !ended || !g) {
-      if (g) cudaGraphDestroy(g);
-      cudaGetLastError();
-      g_last_error.clear();
-      return false;
-    }
-    size_t n = 0;
-    cudaGraphGetNodes(g, nullptr, &n);
-    std::vector<cudaGraphNode_t> nodes(n);
-    cudaGraphGetNodes(g, nodes.data(), &n);
-    for (auto nd : nodes) {
-      cudaGraphNodeType t;
-      if (cudaGraphNodeGetType(nd, &t) != cudaSuccess || t != cudaGraphNodeTypeMemcpy) continue;
-      cudaMemcpy3DParms p{};
-      cudaGraphMemcpyNodeGetParams(nd, &p);
-      (p.kind == cudaMemcpyHostToDevice ? e->h2d : e->d2h) = nd;
-    }
-    const bool inst = e->h2d && e->d2h && cudaGraphInstantiate(&e->exec, g, 0) == cudaSuccess;
-    cudaGraphDestroy(g);
-    if (!inst) {
-      cudaGetLastError();
-      e->exec = nullptr;
-      return false;
-    }
-    e->scratch = ctx->scratch;
-  }
-  cudaStream_t st = ctx->stream;
-  cudaError_t err = cudaGraphExecMemcpyNodeSetParams1D(e->exec, e->h2d, hs.in, x, m * k * 4,
-                                                       cudaMemcpyHostToDevice);
-  if (err == cudaSuccess)
-    err = cudaGraphExecMemcpyNodeSetParams1D(e->exec, e->d2h, out, hs.out, m * w->n_out * 4,
-                                             cudaMemcpyDeviceToHost);
-  if (err == cudaSuccess) err = cudaGraphLaunch(e->exec, st);
-  if (err == cudaSuccess) err = cudaStreamSynchronize(st);
-  *rc = err != cudaSuccess ? cuda_fail(err, "host graph call") : read_status(ctx);
-  return true;
-}
-
-}  // namespace
-
 extern "C" {
 
 int mri_abi_version(void) { return MRI_ABI_VERSION; }
@@ -533,7 +416,6 @@ int mri_ctx_destroy(mri_ctx* ctx) {
   if (!ctx) return MRI_OK;
   use_device(ctx->device);
   cudaStreamSynchronize(ctx->stream);
-  free_host_graphs(ctx);
   if (ctx->scratch) cudaFree(ctx->scratch);
   if (ctx->h_status) cudaFreeHost(ctx->h_status);
   if (ctx->own_stream) cudaStreamDestroy(ctx->stream);
@@ -796,10 +678,7 @@ int mri_host_matmul_int8_from_f32(mri_ctx* ctx, const float* x, size_t m, size_t
   const size_t N = w->n_out;
   HostStage hs;
   if (int rc = host_stage(ctx, m * k * 4, m * N * 4, 0, m, k, &hs)) return rc;
-  if (m * k && m * N && pinned(x) && pinned(out) && stream_gemv_applies(ctx, m, w)) {
-    int rc = MRI_OK;
-    if (host_graph_call(ctx, x, m, k, w, out, hs, &rc)) return rc;
-  }
+
   if (m * k) MRI_CUDA_TRY(cudaMemcpyAsync(hs.in, x, m * k * 4, cudaMemcpyHostToDevice, ctx->stream));
   ActArgs a;
   a.x = reinterpret_cast<float*>(hs.in);

@@ -211,7 +211,6 @@ struct mri_ctx {
   uint8_t* scratch = nullptr;
   size_t scratch_bytes = 0;
   mri::LaunchStats ls;
-  void* host_graphs = nullptr;  // replayable host-buffer calls (abi.cu)
 };
 
 struct mri_qmatrix {

@@ -299,30 +299,6 @@ def test_gemm_tile_widths_exact(mri, oracle, gpu_ctx, monkeypatch, bn):
     assert np.array_equal(bits(got), bits(want))
 
 
-@pytest.mark.parametrize("m", [1, 3])
-def test_host_call_replay_exact(mri, oracle, gpu_ctx, m):
-    """Pinned host buffers through mri_host_matmul_int8_from_f32: the first
-    call runs on the stream, later calls replay a captured graph with the
-    copies pointed at the caller's buffers; every call is bit-exact."""
-    import ctypes
-    import torch
-    rng = np.random.default_rng(40 + m)
-    n, k = 3000, 1024
-    wq = rng.integers(-127, 128, size=n * k, dtype=np.int8)
-    ws = rng.uniform(0.001, 0.02, size=n).astype(np.float32)
-    qm = mri.QuantizedMatrix(wq, ws, n, k, ctx=gpu_ctx)
-    xh = torch.empty(m * k).pin_memory()
-    oh = torch.empty(m * n).pin_memory()
-    for i in range(4):
-        x = rng.normal(0, 1 + i, size=m * k).astype(np.float32)
-        xh.copy_(torch.from_numpy(x))
-        rc = gpu_ctx._lib.mri_host_matmul_int8_from_f32(gpu_ctx.handle, ctypes.c_void_p(xh.data_ptr()), m, k,
-                                                       qm.handle, ctypes.c_void_p(oh.data_ptr()))
-        assert rc == 0, mri._lib.last_error()
-        want = oracle.matmul_int8_from_f32(x, m, k, wq, ws, n, k)
-        assert np.array_equal(bits(oh.numpy().reshape(m, n)), bits(want)), i
-
-
 def test_device_status_clean(mri, gpu_ctx):
     """No bounded device-side wait gave up during the tests above."""
     gpu_ctx.check_device_status()

@@ -125,6 +125,26 @@ int run_int8(mri_ctx* ctx, ActArgs act, const mri_qmatrix* w, size_t m, float* o
 
   const bool w_aligned = (reinterpret_cast<uintptr_t>(w->data) & 15) == 0;
   if (stream_gemv_applies(ctx, m, w)) {
+    // An f32 input too long for the register prologue (M*K > 12288) would be
+    // read twice from L2 by every CTA; quantize it once instead (two small
+    // kernels the GEMV's weight prefetch overlaps) and stream int8 rows.
+    if (f32_in && !epi && mri::reg_vec(static_cast<int>(m), K, &act) == 0) {
+      const size_t need = amax_bytes(m) + al(m * sizeof(float)) + al(m * K);
+      if (int rc = ensure_scratch(ctx, need)) return rc;
+      float* amax = reinterpret_cast<float*>(ctx->scratch);
+      float* scales = reinterpret_cast<float*>(ctx->scratch + amax_bytes(m));
+      int8_t* q = reinterpret_cast<int8_t*>(ctx->scratch + amax_bytes(m) + al(m * sizeof(float)));
+      const int per_row = act.mode == mri::ACT_F32_PER_ROW;
+      MRI_CUDA_TRY(mri::launch_quantize(ctx->dev, st, act.x, m, K, per_row, q, scales, amax, &ctx->ls,
+                                        act.norm_w, act.eps, act.swiglu));
+      ActArgs a;
+      a.xq = q;
+      a.mode = per_row ? mri::ACT_I8_DEV_ROW_SCALE : mri::ACT_I8_DEV_SCALE;
+      a.scale_dev = scales;
+      MRI_CUDA_TRY(mri::launch_gemv_i8_tma(ctx->dev, st, static_cast<int>(m), w->data, w->scales, N,
+                                           K, a, out, acc, ctx->d_status, &ctx->ls, residual));
+      return MRI_OK;
+    }
     MRI_CUDA_TRY(mri::launch_gemv_i8_tma(ctx->dev, st, static_cast<int>(m), w->data, w->scales, N,
                                          K, act, out, acc, ctx->d_status, &ctx->ls, residual, epi));
     return MRI_OK;

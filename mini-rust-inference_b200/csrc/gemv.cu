@@ -1149,12 +1149,12 @@ cudaError_t launch_stream_kernel_threads(void (*k)(KArgs...), int grid, int thre
 
 // K-chunk count for the INT8 stream: the smallest nk whose 8 x kc stage
 // leaves room for three stages next to the activations.
-// Fewest K-chunks that give at least three stages, preferring (up to four
+// Fewest K-chunks that give at least three stages, preferring (up to 16
 // chunks) a configuration with two CTAs per SM: their prologues and tails
 // overlap each other's streaming.
 int i8_chunks(int M, size_t K, StreamConfig* cfg_out) {
   for (int pass = 0; pass < 2; ++pass) {
-    for (int nk = 1; nk <= (pass == 0 ? 4 : 64); ++nk) {
+    for (int nk = 1; nk <= (pass == 0 ? 16 : 64); ++nk) {
       const size_t kc = nk == 1 ? K : align_up((K + nk - 1) / nk, 16);
       if (nk > 1 && kc * (nk - 1) >= K) break;  // chunks would be empty
       const StreamConfig c = pick_config(fixed_bytes_of(M * K, 0), kRowsPerStage * kc);

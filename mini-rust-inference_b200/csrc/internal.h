@@ -109,6 +109,9 @@ cudaError_t launch_add_residual(const DeviceInfo& dev, cudaStream_t st, float* o
 // INT8 per-channel.  Requires K % 16 == 0 and 16-byte aligned W.
 bool gemv_i8_tma_supported(const DeviceInfo& dev, int M, size_t K);
 // residual (nullable): out = residual + product, element-wise (may alias out).
+// Register-prologue width (float4 per consumer thread: 4 or 12) the INT8
+// streaming GEMV uses for this input, 0 when the input takes the general path.
+int reg_vec(int M, size_t K, const ActArgs* act);
 // Launch shape the INT8 streaming GEMV uses for (M, N, K).
 struct GemvPlan {
   int grid = 0, ctas_per_sm = 0, resident = 0, stages = 0, k_chunks = 0, vec = 0;

@@ -275,28 +275,39 @@ int mri::matmul_int8_fused(::mri_ctx* ctx, const float* x, size_t m, size_t k, c
 
 namespace {
 
+// Chunks of at most 8 activation rows.  A chunk of 2..8 rows whose shape the
+// MMA kernel covers, and every chunk without a streaming kernel,
+// read activations quantized per row once for the whole call (q8_direct.rs:264);
+// the streaming kernel for the rest quantizes in its prologue.
 int run_q8_0(mri_ctx* ctx, const float* x, size_t m, const mri_q8_0_matrix* w, float* out) {
   const size_t N = w->n_out, K = w->k_in;
   if (m == 0 || N == 0) return MRI_OK;
   cudaStream_t st = ctx->stream;
-  if (K > 0 && mri::gemv_q8_0_tma_supported(ctx->dev, static_cast<int>(std::min<size_t>(m, 8)), K)) {
-    for (size_t m0 = 0; m0 < m; m0 += 8) {
-      const int mc = static_cast<int>(std::min<size_t>(8, m - m0));
-      MRI_CUDA_TRY(mri::launch_gemv_q8_0_tma(ctx->dev, st, mc, w->data, N, K, x + m0 * K,
-                                             out + m0 * N, ctx->d_status, &ctx->ls));
-    }
-    return MRI_OK;
-  }
-  const size_t need = amax_bytes(m) + al(m * sizeof(float)) + al(m * K);
-  if (int rc = ensure_scratch(ctx, need)) return rc;
-  float* amax = reinterpret_cast<float*>(ctx->scratch);
-  float* scales = reinterpret_cast<float*>(ctx->scratch + amax_bytes(m));
-  int8_t* q = reinterpret_cast<int8_t*>(ctx->scratch + amax_bytes(m) + al(m * sizeof(float)));
-  MRI_CUDA_TRY(mri::launch_quantize(ctx->dev, st, x, m, K, 1, q, scales, amax, &ctx->ls));
+  int8_t* q = nullptr;
+  float* scales = nullptr;
   for (size_t m0 = 0; m0 < m; m0 += 8) {
     const int mc = static_cast<int>(std::min<size_t>(8, m - m0));
-    MRI_CUDA_TRY(mri::launch_gemv_q8_0_generic(ctx->dev, st, mc, w->data, N, K, q + m0 * K,
-                                               scales + m0, out + m0 * N, &ctx->ls));
+    const bool pin = mri::q8_0_mma_supported(mc, K);
+    if (!pin && K > 0 && mri::gemv_q8_0_tma_supported(ctx->dev, mc, K)) {
+      MRI_CUDA_TRY(mri::launch_gemv_q8_0_tma(ctx->dev, st, mc, w->data, N, K, x + m0 * K,
+                                             out + m0 * N, ctx->d_status, &ctx->ls));
+      continue;
+    }
+    if (q == nullptr) {
+      const size_t need = amax_bytes(m) + al(m * sizeof(float)) + al(m * K);
+      if (int rc = ensure_scratch(ctx, need)) return rc;
+      float* amax = reinterpret_cast<float*>(ctx->scratch);
+      scales = reinterpret_cast<float*>(ctx->scratch + amax_bytes(m));
+      q = reinterpret_cast<int8_t*>(ctx->scratch + amax_bytes(m) + al(m * sizeof(float)));
+      MRI_CUDA_TRY(mri::launch_quantize(ctx->dev, st, x, m, K, 1, q, scales, amax, &ctx->ls));
+    }
+    if (pin) {
+      MRI_CUDA_TRY(mri::launch_gemv_q8_0_mma(ctx->dev, st, mc, w->data, N, K, q + m0 * K,
+                                             scales + m0, out + m0 * N, ctx->d_status, &ctx->ls));
+    } else {
+      MRI_CUDA_TRY(mri::launch_gemv_q8_0_generic(ctx->dev, st, mc, w->data, N, K, q + m0 * K,
+                                                 scales + m0, out + m0 * N, &ctx->ls));
+    }
   }
   return MRI_OK;
 }

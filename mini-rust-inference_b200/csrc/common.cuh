@@ -131,6 +131,15 @@ __device__ __forceinline__ float rescale(int acc, float s_a, float s_w) {
   return __fmul_rn(__fmul_rn(__int2float_rn(acc), s_a), s_w);
 }
 
+// (f32)v for |v| < 2^22 without the conversion unit: v added to the bit
+// pattern of 1.5 * 2^23 lands in the mantissa of a float in [2^23, 2^24),
+// whose value is exactly 1.5 * 2^23 + v; subtracting 1.5 * 2^23 is exact too.
+// Equal to __int2float_rn(v) in that range (a Q8_0 block dot is at most
+// 32 * 127 * 127 in magnitude).
+__device__ __forceinline__ float small_int_to_float(int v) {
+  return __fsub_rn(__int_as_float(v + 0x4B400000), 12582912.0f);
+}
+
 // f16_to_f32 (gguf/quantization.rs:416-461) is the exact IEEE conversion.
 __device__ __forceinline__ float f16_bits_to_f32(uint32_t bits16) {
   return __half2float(__ushort_as_half(static_cast<unsigned short>(bits16 & 0xFFFFu)));

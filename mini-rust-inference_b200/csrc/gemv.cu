@@ -643,10 +643,13 @@ __global__ void __launch_bounds__(256) gemv_i8_generic_kernel(const int8_t* __re
 // ── Q8_0 helpers ─────────────────────────────────────────────────────────────
 
 // Loads block `blk` (34 bytes at an even address) from any address space:
-// d (f16 bits) and the 32 quants as 8 little-endian words.
+// d (f16 bits) and the 32 quants as 8 little-endian words.  The aligned-down
+// word pointer is formed by pointer arithmetic on `blk` (no integer round
+// trip), so the compiler still sees a shared-memory pointer and issues
+// shared loads rather than generic ones.
 __device__ __forceinline__ void load_q8_block(const uint8_t* blk, uint32_t& dbits, uint32_t q[8]) {
-  const uintptr_t a = reinterpret_cast<uintptr_t>(blk);
-  const uint32_t* w = reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3));
+  const uint32_t a = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(blk)) & 3u;
+  const uint32_t* w = reinterpret_cast<const uint32_t*>(blk - a);
   const bool odd = (a & 2) != 0;  // block starts 2 bytes into a word
   uint32_t r[9];  // 36 bytes from the aligned-down start cover the block
 #pragma unroll
@@ -735,7 +738,7 @@ __global__ void __launch_bounds__(kThreads, M <= 2 ? 2 : 1)
           dot = dp4a(q[5], a1.y, dot);
           dot = dp4a(q[6], a1.z, dot);
           dot = dp4a(q[7], a1.w, dot);
-          T[m * ts32 + b] = __fmul_rn(__fmul_rn(__int2float_rn(dot), s_a[m]), d);
+          T[m * ts32 + b] = __fmul_rn(__fmul_rn(small_int_to_float(dot), s_a[m]), d);
         }
       }
       __syncwarp();
@@ -759,6 +762,228 @@ __global__ void __launch_bounds__(kThreads, M <= 2 ? 2 : 1)
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
+  }
+}
+
+// ── K4, M = 2..8: Q8_0 block dots on the warp-level integer MMA ─────────────
+// At M > 1 the block dot products outgrow the CUDA cores: 8 dp4a per
+// (weight row, block, activation row).  One mma.sync m16n8k32 (s8 x s8 ->
+// s32) computes a block's dots for 8 weight rows (rows 8..15 of the A tile are
+// zero) and 8 activation rows at once: A = the 32 quants of row g of the stage
+// (groupID g = lane / 4), B = the quantized activation block of row m = g,
+// which a dot warp keeps in registers for its whole range of blocks.  Thread
+// (g, t = lane % 4) receives the dots of (row g, m = 2t, 2t+1) and writes the
+// block terms (f32)dot * s_a * d into a double-buffered term buffer
+// [row][block][m]; two sum warps add every (row, m)'s terms in block order
+// from 0.0 (q8_direct.rs:266-285), one chain per thread, while the dot warps
+// work on the next stage.  The integer dots are exact, so the result is the
+// reference's bit for bit.  Activations arrive quantized per row (the
+// quantizer kernel runs first; its launch overlaps this kernel's weight
+// stream).  Rows are copied into stage slots padded by 16 bytes so the 8 rows
+// a warp reads fall in different banks.  Preconditions (launcher): nb % 8 == 0,
+// nb <= 256, 16-byte aligned xq.
+constexpr int kQ8MmaDotWarps = kConsumerWarps;
+constexpr int kQ8MmaSumWarps = 2;
+constexpr int kQ8MmaThreads = 32 * (1 + kQ8MmaDotWarps + kQ8MmaSumWarps);
+constexpr int kQ8MmaMaxBpw = 32;  // blocks per dot warp (B fragments in registers)
+constexpr int kQ8MmaBatch = 8;    // blocks whose shared loads are issued together
+
+__host__ __device__ constexpr size_t q8_mma_row_stride(size_t nb) { return nb * 34 + 16; }
+// Floats per stage row in the term buffer: [block][8 m] plus 8 floats of pad.
+__host__ __device__ constexpr size_t q8_mma_term_row(size_t nb) { return nb * 8 + 8; }
+__host__ __device__ constexpr size_t q8_mma_term_bytes(size_t nb) {
+  return 2 * kRowsPerStage * q8_mma_term_row(nb) * sizeof(float);
+}
+
+__device__ __forceinline__ void mma_s8_m16n8k32(int d[4], uint32_t a0, uint32_t a2, uint32_t b0,
+                                                uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+      "{%8, %9}, {%10, %11, %12, %13};"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+
+template <int M>
+__global__ void __launch_bounds__(kQ8MmaThreads, 1)
+    gemv_q8_0_mma_kernel(const uint8_t* __restrict__ W, size_t N, size_t K,
+                         const int8_t* __restrict__ xq, const float* __restrict__ x_scales,
+                         float* __restrict__ out, int n_stages, int* status) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const size_t nb = K / 32;
+  const size_t row_bytes = nb * 34;
+  const size_t rstride = q8_mma_row_stride(nb);
+  const size_t trow = q8_mma_term_row(nb);
+  const StreamLayout L = make_layout(q8_mma_term_bytes(nb), 64, kRowsPerStage * rstride, n_stages);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
+  uint64_t* empty = full + n_stages;
+  uint64_t* tfull = reinterpret_cast<uint64_t*>(smem + L.extra);  // [2], dot warps arrive
+  uint64_t* tempty = tfull + 2;                                    // [2], sum warps arrive
+  uint64_t* xfull = tempty + 2;                                    // quantized activations landed
+  float* T = reinterpret_cast<float*>(smem + L.act);               // [2][8 rows][trow]
+  uint8_t* stage0 = smem + L.stage;
+  const size_t plane = kRowsPerStage * trow;  // floats per term buffer
+  // Until the first stage's terms are written the second term buffer holds
+  // the quantized activation rows, K + 16 bytes apart (the pad spreads the
+  // rows over the banks).
+  int8_t* s_x = reinterpret_cast<int8_t*>(T + plane);
+  const size_t xstride = K + 16;
+
+  size_t begin, end;
+  cta_rows(N, 1, begin, end);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < n_stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kQ8MmaDotWarps);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], kQ8MmaDotWarps);
+      mbar_init(&tempty[b], kQ8MmaSumWarps);
+    }
+    mbar_init(xfull, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  pdl_launch_dependents();
+  if (begin >= end) return;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int iters = static_cast<int>((end - begin + kRowsPerStage - 1) / kRowsPerStage);
+  if (warp == 0) {
+    // Producer: the whole ring first (weights do not depend on the previous
+    // kernel), then the activation rows once the quantizer has finished, then
+    // the rest of the weights.  Each stage row is its own bulk copy into a
+    // padded slot.
+    if (lane == 0) {
+      const uint64_t policy = l2_policy_evict_first();
+      int issued = 0;
+      bool ok = true;
+      for (int it = 0; it < iters && ok; ++it) {
+        const int s = it % n_stages;
+        if (it >= n_stages && !mbar_wait(&empty[s], ((it / n_stages) - 1) & 1, status)) {
+          ok = false;
+          break;
+        }
+        const size_t r0 = begin + static_cast<size_t>(it) * kRowsPerStage;
+        const size_t nrows = std::min<size_t>(kRowsPerStage, end - r0);
+        uint8_t* dst = stage0 + s * L.stage_bytes;
+        mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(nrows * row_bytes));
+        for (size_t r = 0; r < nrows; ++r)
+          bulk_copy_g2s_stream(dst + r * rstride, W + (r0 + r) * row_bytes,
+                               static_cast<uint32_t>(row_bytes), &full[s], policy);
+        issued = it + 1;
+        if (issued == std::min(iters, n_stages)) {
+          pdl_wait();
+          mbar_arrive_expect_tx(xfull, static_cast<uint32_t>(M * K));
+          for (int m = 0; m < M; ++m)
+            bulk_copy_g2s(s_x + m * xstride, xq + static_cast<size_t>(m) * K,
+                          static_cast<uint32_t>(K), xfull);
+        }
+      }
+      for (int it = std::max(0, issued - n_stages); it < issued; ++it)
+        mbar_wait(&full[it % n_stages], (it / n_stages) & 1, status);
+      if (issued >= std::min(iters, n_stages)) mbar_wait(xfull, 0, status);
+    }
+    return;
+  }
+  pdl_wait();
+  if (warp > kQ8MmaDotWarps) {
+    // Sum warps: chain c = (stage row r, activation row m).
+    const int c = (warp - 1 - kQ8MmaDotWarps) * 32 + lane;
+    const int r = c / M, m = c % M;
+    for (int it = 0; it < iters; ++it) {
+      const int tb = it & 1;
+      if (!mbar_wait(&tfull[tb], (it >> 1) & 1, status)) return;
+      const size_t row = begin + static_cast<size_t>(it) * kRowsPerStage + r;
+      if (c < kRowsPerStage * M && row < end) {
+        const float* t = T + tb * plane + r * trow + m;
+        float acc = 0.0f;
+#pragma unroll 16
+        for (size_t j = 0; j < nb; ++j) acc = __fadd_rn(acc, t[j * 8]);
+        out[static_cast<size_t>(m) * N + row] = acc;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[tb]);
+    }
+    return;
+  }
+
+  // Dot warps: warp w owns blocks [w*bpw, (w+1)*bpw); B fragments of its
+  // blocks (activation row g, bytes 4t..4t+3 and 16+4t..16+4t+3) stay in
+  // registers.
+  const int dw = warp - 1;
+  const int g = lane >> 2, t = lane & 3;
+  const int bpw = static_cast<int>(nb / kQ8MmaDotWarps);
+  const int kb0 = dw * bpw;
+  // On a timeout every dot warp still reaches the named barrier below (with
+  // zero fragments) and returns after it.
+  const bool xok = mbar_wait(xfull, 0, status);
+  uint32_t bf[kQ8MmaMaxBpw][2];
+#pragma unroll
+  for (int i = 0; i < kQ8MmaMaxBpw; ++i) {
+    const bool ok = xok && i < bpw && g < M;
+    const uint32_t* p = reinterpret_cast<const uint32_t*>(
+        s_x + (ok ? g : 0) * xstride + static_cast<size_t>(kb0 + (ok ? i : 0)) * 32) + t;
+    bf[i][0] = ok ? p[0] : 0u;
+    bf[i][1] = ok ? p[4] : 0u;
+  }
+  const float sa0 = 2 * t < M ? ld_act(x_scales + 2 * t) : 0.0f;
+  const float sa1 = 2 * t + 1 < M ? ld_act(x_scales + 2 * t + 1) : 0.0f;
+  // The second term buffer is written from stage 1 on: every dot warp has
+  // its fragments first.
+  named_bar_sync(1, kQ8MmaDotWarps * 32);
+  if (!xok) return;
+
+  for (int it = 0; it < iters; ++it) {
+    const int s = it % n_stages, tb = it & 1;
+    if (!mbar_wait(&full[s], (it / n_stages) & 1, status)) return;
+    if (it >= 2 && !mbar_wait(&tempty[tb], ((it >> 1) - 1) & 1, status)) return;
+    // Row g of the stage (rows past the valid ones hold stale bytes: their
+    // terms are written but never summed).
+    const uint8_t* rowp = stage0 + s * L.stage_bytes + g * rstride;
+    float* Tr = T + tb * plane + g * trow + 2 * t;
+    // Batches of kQ8MmaBatch blocks: every shared load of a batch is issued
+    // before its term stores (which the compiler cannot move loads across).
+#pragma unroll
+    for (int i0 = 0; i0 < kQ8MmaMaxBpw; i0 += kQ8MmaBatch) {
+      if (i0 >= bpw) break;
+      uint32_t a0[kQ8MmaBatch], a2[kQ8MmaBatch], dbits[kQ8MmaBatch];
+#pragma unroll
+      for (int u = 0; u < kQ8MmaBatch; ++u) {
+        // Past the warp's range (bpw not a multiple of the batch) the loads
+        // repeat block kb0 and the stores are skipped.
+        const int kb = i0 + u < bpw ? kb0 + i0 + u : kb0;
+        // Block kb starts at 34*kb, its quants at +2: 2 mod 4 for even kb,
+        // word aligned for odd kb (warp-uniform).  Row slots are 4 banks
+        // apart, so the 8 rows x 4 threads of a load hit 32 banks.
+        const uint8_t* blk = rowp + kb * 34;
+        if ((kb & 1) == 0) {
+          const uint32_t* w = reinterpret_cast<const uint32_t*>(blk) + t;
+          a0[u] = __funnelshift_r(w[0], w[1], 16);
+          a2[u] = __funnelshift_r(w[4], w[5], 16);
+        } else {
+          const uint32_t* w = reinterpret_cast<const uint32_t*>(blk + 2) + t;
+          a0[u] = w[0];
+          a2[u] = w[4];
+        }
+        dbits[u] = *reinterpret_cast<const uint16_t*>(blk);
+      }
+#pragma unroll
+      for (int u = 0; u < kQ8MmaBatch; ++u) {
+        int dd[4];
+        mma_s8_m16n8k32(dd, a0[u], a2[u], bf[i0 + u][0], bf[i0 + u][1]);
+        const float d = f16_bits_to_f32(dbits[u]);
+        float2 tv;
+        tv.x = __fmul_rn(__fmul_rn(small_int_to_float(dd[0]), sa0), d);
+        tv.y = __fmul_rn(__fmul_rn(small_int_to_float(dd[1]), sa1), d);
+        if (i0 + u < bpw) *reinterpret_cast<float2*>(Tr + (kb0 + i0 + u) * 8) = tv;
+      }
+    }
+    __syncwarp();
+    if (lane == 0) {
+      mbar_arrive(&empty[s]);
+      mbar_arrive(&tfull[tb]);
+    }
   }
 }
 
@@ -814,9 +1039,10 @@ __global__ void __launch_bounds__(256) gemv_q8_0_generic_kernel(const uint8_t* _
 // ── K5: Q4_0 streaming GEMV (f32 activations) ───────────────────────────────
 // Activations are stored transposed to [m][element 0..31][block] floats.
 
+// Same for an 18-byte Q4_0 block (even address; shared loads, see above).
 __device__ __forceinline__ void load_q4_block(const uint8_t* blk, uint32_t& dbits, uint32_t q[4]) {
-  const uintptr_t a = reinterpret_cast<uintptr_t>(blk);
-  const uint32_t* w = reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3));
+  const uint32_t a = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(blk)) & 3u;
+  const uint32_t* w = reinterpret_cast<const uint32_t*>(blk - a);
   const bool odd = (a & 2) != 0;
   uint32_t r[5];
 #pragma unroll
@@ -1083,7 +1309,7 @@ int stream_grid(const DeviceInfo& dev, size_t units, int ctas_per_sm) {
 // shared memory), cached per (kernel, device, smem).  The persistent grid is
 // never sized above it: a second wave would double the kernel's time.
 template <typename KernelT>
-int resident_ctas(KernelT k, size_t smem, int device) {
+int resident_ctas(KernelT k, size_t smem, int device, int threads = kThreads) {
   static std::mutex mu;
   static std::map<std::tuple<const void*, int, size_t>, int> done;
   std::lock_guard<std::mutex> lock(mu);
@@ -1091,7 +1317,7 @@ int resident_ctas(KernelT k, size_t smem, int device) {
   auto it = done.find(key);
   if (it != done.end()) return it->second;
   int n = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, kThreads, smem) != cudaSuccess) {
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, threads, smem) != cudaSuccess) {
     cudaGetLastError();
     n = 1;
   }
@@ -1101,12 +1327,12 @@ int resident_ctas(KernelT k, size_t smem, int device) {
 }
 
 // Launch with the programmatic-stream-serialization attribute when enabled.
-template <typename... KArgs, typename... Args>
+template <int Threads = kThreads, typename... KArgs, typename... Args>
 cudaError_t launch_stream_kernel(void (*k)(KArgs...), int grid, size_t smem, cudaStream_t st,
                                  Args&&... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(Threads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -1345,6 +1571,53 @@ bool gemv_q8_0_tma_supported(const DeviceInfo&, int M, size_t K) {
   const size_t nb = K / 32;
   return pick_stages(fixed_bytes_of(M * K, kConsumerWarps * M * q8_term_stride(nb) * 4),
                      kRowsPerStage * nb * 34) >= 3;
+}
+
+// The MMA Q8_0 kernel covers M = 2..8 when nb % 8 == 0 (16-byte aligned
+// rows, an equal block range per dot warp), nb <= 8 * kQ8MmaMaxBpw and three
+// stages fit.
+bool q8_0_mma_supported(int M, size_t K) {
+  static const bool off = [] {
+    const char* e = std::getenv("MRI_Q8_MMA");
+    return e != nullptr && std::atoi(e) == 0;
+  }();
+  if (off || M < 2 || M > 8 || K == 0 || K % 32 != 0) return false;
+  const size_t nb = K / 32;
+  if (nb % kQ8MmaDotWarps != 0 || nb > static_cast<size_t>(kQ8MmaDotWarps * kQ8MmaMaxBpw)) return false;
+  return stages_within(fixed_bytes_of(q8_mma_term_bytes(nb), 64), kRowsPerStage * q8_mma_row_stride(nb),
+                       kSmemBudget) >= 3;
+}
+
+cudaError_t launch_gemv_q8_0_mma(const DeviceInfo& dev, cudaStream_t st, int M, const uint8_t* W,
+                                 size_t N, size_t K, const int8_t* xq, const float* x_scales,
+                                 float* out, int* status, LaunchStats* ls) {
+  if (!q8_0_mma_supported(M, K) || (reinterpret_cast<uintptr_t>(xq) & 15) != 0 ||
+      (reinterpret_cast<uintptr_t>(W) & 15) != 0)
+    return cudaErrorInvalidValue;
+  const size_t nb = K / 32;
+  const size_t stage_bytes = kRowsPerStage * q8_mma_row_stride(nb);
+  const int stages = std::min(kMaxStages, stages_within(fixed_bytes_of(q8_mma_term_bytes(nb), 64),
+                                                         stage_bytes, kSmemBudget));
+  const size_t smem = make_layout(q8_mma_term_bytes(nb), 64, stage_bytes, stages).total;
+  void (*kern)(const uint8_t*, size_t, size_t, const int8_t*, const float*, float*, int, int*) =
+      nullptr;
+  switch (M) {
+    case 2: kern = gemv_q8_0_mma_kernel<2>; break;
+    case 3: kern = gemv_q8_0_mma_kernel<3>; break;
+    case 4: kern = gemv_q8_0_mma_kernel<4>; break;
+    case 5: kern = gemv_q8_0_mma_kernel<5>; break;
+    case 6: kern = gemv_q8_0_mma_kernel<6>; break;
+    case 7: kern = gemv_q8_0_mma_kernel<7>; break;
+    case 8: kern = gemv_q8_0_mma_kernel<8>; break;
+    default: return cudaErrorInvalidValue;
+  }
+  cudaError_t e = set_smem(kern, smem, dev.device);
+  if (e != cudaSuccess) return e;
+  e = launch_stream_kernel<kQ8MmaThreads>(kern, stream_grid(dev, N, 1), smem, st, W, N, K, xq, x_scales,
+                                          out, stages, status);
+  if (e != cudaSuccess) return e;
+  if (ls) ls->launches++;
+  return cudaGetLastError();
 }
 
 cudaError_t launch_gemv_q8_0_tma(const DeviceInfo& dev, cudaStream_t st, int M, const uint8_t* W,

@@ -161,6 +161,53 @@ __global__ void __launch_bounds__(kQThreads) quant_apply_kernel(const float* __r
   }
 }
 
+// Per row in one pass, for rows of at most kRowVec float4 per thread: block r
+// reads row r once into registers, reduces its absmax and writes the
+// quantized row and its scale (symmetric.rs:41-56 per row).  x and q 16- and
+// 4-byte aligned, k % 4 == 0 (the launcher checks).
+constexpr int kRowVec = 8;
+
+__global__ void __launch_bounds__(kQThreads) quant_rows_kernel(const float* __restrict__ x, size_t k,
+                                                               int8_t* __restrict__ q,
+                                                               float* __restrict__ scale_out) {
+  pdl_enter();
+  const size_t k4 = k / 4;
+  const float4* row = reinterpret_cast<const float4*>(x + static_cast<size_t>(blockIdx.x) * k);
+  float4 v[kRowVec];
+  float m = 0.0f;
+#pragma unroll
+  for (int j = 0; j < kRowVec; ++j) {
+    const size_t i = threadIdx.x + static_cast<size_t>(j) * kQThreads;
+    v[j] = i < k4 ? ld_act(row + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+#pragma unroll
+  for (int j = 0; j < kRowVec; ++j)
+    m = absmax_acc(absmax_acc(absmax_acc(absmax_acc(m, v[j].x), v[j].y), v[j].z), v[j].w);
+  m = warp_max(m);
+  __shared__ float red[kQThreads / 32];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  float t = 0.0f;
+#pragma unroll
+  for (int i = 0; i < kQThreads / 32; ++i) t = fmaxf(t, red[i]);
+  const float scale = sym_scale(t);
+  const float inv = __fdiv_rn(1.0f, scale);
+  if (threadIdx.x == 0) scale_out[blockIdx.x] = scale;
+  char4* qr = reinterpret_cast<char4*>(q + static_cast<size_t>(blockIdx.x) * k);
+#pragma unroll
+  for (int j = 0; j < kRowVec; ++j) {
+    const size_t i = threadIdx.x + static_cast<size_t>(j) * kQThreads;
+    if (i < k4) {
+      char4 o;
+      o.x = sym_quant(v[j].x, inv);
+      o.y = sym_quant(v[j].y, inv);
+      o.z = sym_quant(v[j].z, inv);
+      o.w = sym_quant(v[j].w, inv);
+      qr[i] = o;
+    }
+  }
+}
+
 // Fused producer ops (RMSNorm or SwiGLU) in front of the quantizer.  Pass 1,
 // one block per row: 1/rms of the row (RMSNorm) into row_inv[r] and the
 // absmax of the row's transformed values into partial[r].
@@ -322,6 +369,12 @@ cudaError_t launch_quantize(const DeviceInfo& dev, cudaStream_t st, const float*
       return cudaMemcpyAsync(scale, &one, sizeof(float), cudaMemcpyHostToDevice, st);
     }
     if (m == 0) return cudaSuccess;
+  }
+  if (per_row && k % 4 == 0 && k <= static_cast<size_t>(kRowVec) * kQThreads * 4 &&
+      (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(q) & 3) == 0) {
+    cudaError_t e = qlaunch(quant_rows_kernel, static_cast<unsigned>(m), st, x, k, q, scale);
+    if (ls) ls->launches++;
+    return e;
   }
   // Pass 1 writes one partial maximum per block into amax_scratch, which must
   // hold kQuantPartials floats (per tensor) or m floats (per row).

@@ -229,6 +229,27 @@ def test_q8_0_bit_exact(m, n, k, mri, oracle, gpu_ctx):
     assert np.array_equal(bits(got), bits(want))
 
 
+# M = 2..8 with K % 256 == 0 take the MMA Q8_0 kernel (activations quantized
+# per row first) while three stages fit (K <= 5120); (2, 1000, 8192),
+# (4, 300, 6144), (5, 71, 96) and (8, 40, 4128) exercise the fallbacks.
+Q8_PIN_SHAPES = [(2, 1000, 8192), (4, 300, 6144), (3, 517, 2048), (7, 2049, 3072), (3, 333, 5120),
+                 (6, 333, 5120), (8, 3, 1024), (2, 148 * 8 + 1, 4096), (5, 71, 96), (8, 40, 4096 + 32)]
+
+
+@pytest.mark.parametrize("m,n,k", Q8_PIN_SHAPES)
+def test_q8_0_multirow_bit_exact(m, n, k, mri, oracle, gpu_ctx):
+    rng = np.random.default_rng(3500 + m + n + k)
+    w = rng.normal(0, 0.02, size=(n, k)).astype(np.float32)
+    x = rng.normal(0, 1, size=(m, k)).astype(np.float32)
+    x[0, :] = 0.0            # zero row: scale 1.0
+    x[m - 1, 5] = 1.0e4      # one large element dominates its row's scale
+    wb = oracle.quantize_q8_0_matrix(w, n, k)
+    W = mri.Q8_0WeightMatrix.from_raw_bytes(wb, n, k)
+    got = mri.matmul_q8_0_direct(x, W)
+    want = oracle.matmul_q8_0_direct(x, m, k, wb, n, k)
+    assert np.array_equal(bits(got), bits(want))
+
+
 def q4_close(got, want, x, wdeq):
     floor = Q4_FLOOR * (np.abs(x) @ np.abs(wdeq).T)
     err = np.abs(got - want)

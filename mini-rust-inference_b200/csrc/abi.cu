@@ -317,9 +317,21 @@ int run_q4_0(mri_ctx* ctx, const float* x, size_t m, const mri_q4_0_matrix* w, f
   if (m == 0 || N == 0) return MRI_OK;
   cudaStream_t st = ctx->stream;
   const bool tma = K > 0 && mri::gemv_q4_0_tma_supported(ctx->dev, static_cast<int>(std::min<size_t>(m, 8)), K);
+  const bool x_vec = (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+  uint32_t* xs = nullptr;  // split activations of all m rows, made on first use
   for (size_t m0 = 0; m0 < m; m0 += 8) {
     const int mc = static_cast<int>(std::min<size_t>(8, m - m0));
-    if (tma) {
+    if (x_vec && mri::q4_0_mma_supported(mc, K)) {
+      if (xs == nullptr) {
+        if (int rc = ensure_scratch(ctx, al(mri::q4_0_split_bytes(m, K)))) return rc;
+        xs = reinterpret_cast<uint32_t*>(ctx->scratch);
+        MRI_CUDA_TRY(mri::launch_q4_0_split(ctx->dev, st, x, m, K, xs, &ctx->ls));
+      }
+      MRI_CUDA_TRY(mri::launch_gemv_q4_0_mma(
+          ctx->dev, st, mc, w->data, N, K,
+          reinterpret_cast<const uint32_t*>(reinterpret_cast<const uint8_t*>(xs) + mri::q4_0_split_bytes(m0, K)),
+          out + m0 * N, ctx->d_status, &ctx->ls));
+    } else if (tma) {
       MRI_CUDA_TRY(mri::launch_gemv_q4_0_tma(ctx->dev, st, mc, w->data, N, K, x + m0 * K,
                                              out + m0 * N, ctx->d_status, &ctx->ls));
     } else {
@@ -742,7 +754,9 @@ int mri_host_matmul_q4_0_dequant(mri_ctx* ctx, const float* x, size_t m, size_t 
   if (int rc = check_k("matmul_q4_0_dequant", m, k, w->k)) return rc;
   const size_t N = w->n_out;
   HostStage hs;
-  if (int rc = host_stage(ctx, m * k * 4, m * N * 4, 0, 0, 0, &hs)) return rc;
+  // The reserved front of scratch holds run_q4_0's split activations (m rows
+  // of 4k + 64 bytes).
+  if (int rc = host_stage(ctx, m * k * 4, m * N * 4, 0, m, 4 * k + 64, &hs)) return rc;
   if (m * k) MRI_CUDA_TRY(cudaMemcpyAsync(hs.in, x, m * k * 4, cudaMemcpyHostToDevice, ctx->stream));
   if (int rc = run_q4_0(ctx, reinterpret_cast<float*>(hs.in), m, w, hs.out)) return rc;
   if (m * N) MRI_CUDA_TRY(cudaMemcpyAsync(out, hs.out, m * N * 4, cudaMemcpyDeviceToHost, ctx->stream));

@@ -25,6 +25,8 @@
 #include <tuple>
 #include <utility>
 
+#include <cuda_bf16.h>
+
 #include "common.cuh"
 #include "internal.h"
 
@@ -1180,6 +1182,252 @@ __global__ void __launch_bounds__(kThreads, M <= 2 ? 2 : 1)
   }
 }
 
+// ── K5, M = 2..8: Q4_0 on the bf16 warp MMA ─────────────────────────────────
+// The f32 products of the CUDA-core kernel above are bound by the shared-
+// memory reads of the activations (128 bytes per block, weight row and
+// activation row).  Here each block's dots for 8 weight rows x 8 activation
+// rows are one pair of mma.sync m16n8k16 (bf16 x bf16 -> f32): the weights
+// (q - 8, exact in bf16) are the B operand (n = weight row g of the stage, a
+// thread's 4 elements of a 16-element k step), and the activations are the A
+// operand with rows 0..7 = bf16(x) and rows 8..15 = bf16(x - bf16(x)) of the 8
+// activation rows, so one MMA returns both halves of the split and the block
+// dot is D[m] + D[m + 8] (16 significant bits of each activation).  A thread's
+// k positions are the same in A and B (a0 <-> b0, a2 <-> b1), so any
+// assignment of the block's 32 elements to them gives the same dot.  The
+// block dot times the block scale d is added to f32 partial sums per (row,
+// m); the dot warps' partials are added in warp order by one sum warp.  The
+// sum is reassociated (q4_0.rs:94-181 adds element by element): within the
+// Q4_0 tolerance.  A pre-kernel writes the split activations in fragment
+// order, [m][block][k step j][thread t][a0 a1 a2 a3] holding elements
+// 8t + 4j .. 8t + 4j + 3 of the block, rows K*4 + 64 bytes apart
+// (the pad puts consecutive rows in opposite bank halves); the producer
+// copies them into shared memory once.  Preconditions (launcher): nb % 8 == 0,
+// M rows of split activations plus three stages fit.
+constexpr int kQ4MmaDotWarps = kConsumerWarps;
+constexpr int kQ4MmaThreads = 32 * (1 + kQ4MmaDotWarps + 1);
+constexpr int kQ4MmaBatch = 8;
+
+__host__ __device__ constexpr size_t q4_split_row_bytes(size_t K) { return K * 4 + 64; }
+__host__ __device__ constexpr size_t q4_mma_row_stride(size_t nb) { return nb * 18 + 16; }
+__host__ __device__ constexpr size_t q4_mma_fixed_bytes(int M, size_t K) {
+  return static_cast<size_t>(M) * q4_split_row_bytes(K) + 2 * kQ4MmaDotWarps * 64 * sizeof(float);
+}
+
+__device__ __forceinline__ uint32_t bf16x2_bits(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+// x f32 [M, K] -> split bf16 pairs in fragment order (see above); one thread
+// per 4 consecutive elements.
+__global__ void __launch_bounds__(256) q4_split_act_kernel(const float* __restrict__ x, size_t M,
+                                                           size_t K, uint32_t* __restrict__ xs) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const size_t k4 = K / 4;
+  if (i >= M * k4) return;
+  const size_t m = i / k4, e = (i - m * k4) * 4;
+  const float4 v = ld_act(reinterpret_cast<const float4*>(x + m * K + e));
+  const float h0 = __bfloat162float(__float2bfloat16_rn(v.x));
+  const float h1 = __bfloat162float(__float2bfloat16_rn(v.y));
+  const float h2 = __bfloat162float(__float2bfloat16_rn(v.z));
+  const float h3 = __bfloat162float(__float2bfloat16_rn(v.w));
+  uint4 o;
+  o.x = bf16x2_bits(h0, h1);
+  o.y = bf16x2_bits(__fsub_rn(v.x, h0), __fsub_rn(v.y, h1));
+  o.z = bf16x2_bits(h2, h3);
+  o.w = bf16x2_bits(__fsub_rn(v.z, h2), __fsub_rn(v.w, h3));
+  // Elements 32*kb + 8*t + 4*j + {0..3} form record (kb, j, t) of row m.
+  const size_t kb = e / 32, i4 = (e % 32) / 4, t = i4 >> 1, j = i4 & 1;
+  uint8_t* row = reinterpret_cast<uint8_t*>(xs) + m * q4_split_row_bytes(K);
+  reinterpret_cast<uint4*>(row)[kb * 8 + j * 4 + t] = o;
+}
+
+__device__ __forceinline__ void mma_bf16_m16n8k16(float d[4], const uint4& a, uint32_t b0,
+                                                  uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+      "{%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b0), "r"(b1));
+}
+
+// Four nibble codes (bytes of v, each < 16) as two bf16 pairs q - 8: the code
+// goes into the mantissa of bf16(128), then 136 is subtracted (exact).
+__device__ __forceinline__ void nib_bf16x2(uint32_t v, uint32_t& p01, uint32_t& p23) {
+  const __nv_bfloat162 off = __floats2bfloat162_rn(136.0f, 136.0f);
+  uint32_t a = __byte_perm(v, 0x43u, 0x4140), b = __byte_perm(v, 0x43u, 0x4342);
+  const __nv_bfloat162 ra = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&a), off);
+  const __nv_bfloat162 rb = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&b), off);
+  p01 = *reinterpret_cast<const uint32_t*>(&ra);
+  p23 = *reinterpret_cast<const uint32_t*>(&rb);
+}
+
+template <int M>
+__global__ void __launch_bounds__(kQ4MmaThreads, 1)
+    gemv_q4_0_mma_kernel(const uint8_t* __restrict__ W, size_t N, size_t K,
+                         const uint32_t* __restrict__ xs, float* __restrict__ out, int n_stages,
+                         int* status) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const size_t nb = K / 32;
+  const size_t row_bytes = nb * 18;
+  const size_t rstride = q4_mma_row_stride(nb);
+  const size_t xrow = q4_split_row_bytes(K);
+  const StreamLayout L = make_layout(q4_mma_fixed_bytes(M, K), 5 * 8, kRowsPerStage * rstride, n_stages);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
+  uint64_t* empty = full + n_stages;
+  uint64_t* xfull = reinterpret_cast<uint64_t*>(smem + L.extra);
+  uint64_t* pfull = xfull + 1;   // [2], dot warps arrive
+  uint64_t* pempty = pfull + 2;  // [2], the sum warp arrives
+  uint8_t* s_x = smem + L.act;   // [M][xrow]
+  float* P = reinterpret_cast<float*>(smem + L.act + static_cast<size_t>(M) * xrow);  // [2][8][64]
+  uint8_t* stage0 = smem + L.stage;
+
+  size_t begin, end;
+  cta_rows(N, 1, begin, end);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < n_stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kQ4MmaDotWarps);
+    }
+    mbar_init(xfull, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&pfull[b], kQ4MmaDotWarps);
+      mbar_init(&pempty[b], 1);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+  pdl_launch_dependents();
+  if (begin >= end) return;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int iters = static_cast<int>((end - begin + kRowsPerStage - 1) / kRowsPerStage);
+  if (warp == 0) {
+    // Producer: the whole ring first, then the split activations once the
+    // pre-kernel has finished, then the rest of the weights.  Each stage row
+    // is its own bulk copy into a padded slot.
+    if (lane == 0) {
+      const uint64_t policy = l2_policy_evict_first();
+      const int first = std::min(iters, n_stages);
+      int issued = 0;
+      for (int it = 0; it < iters; ++it) {
+        const int s = it % n_stages;
+        if (it >= n_stages && !mbar_wait(&empty[s], ((it / n_stages) - 1) & 1, status)) break;
+        const size_t r0 = begin + static_cast<size_t>(it) * kRowsPerStage;
+        const size_t nrows = std::min<size_t>(kRowsPerStage, end - r0);
+        uint8_t* dst = stage0 + s * L.stage_bytes;
+        mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(nrows * row_bytes));
+        for (size_t r = 0; r < nrows; ++r)
+          bulk_copy_g2s_stream(dst + r * rstride, W + (r0 + r) * row_bytes,
+                               static_cast<uint32_t>(row_bytes), &full[s], policy);
+        issued = it + 1;
+        if (issued == first) {
+          pdl_wait();
+          const uint32_t xbytes = static_cast<uint32_t>(M * xrow);
+          mbar_arrive_expect_tx(xfull, xbytes);
+          bulk_copy_g2s(s_x, xs, xbytes, xfull);
+        }
+      }
+      for (int it = std::max(0, issued - n_stages); it < issued; ++it)
+        mbar_wait(&full[it % n_stages], (it / n_stages) & 1, status);
+      if (issued >= first) mbar_wait(xfull, 0, status);
+    }
+    return;
+  }
+  pdl_wait();
+  if (warp > kQ4MmaDotWarps) {
+    // Sum warp: output o = m * 8 + n (activation row m, stage row n), the
+    // dot warps' partials added in warp order.
+    for (int it = 0; it < iters; ++it) {
+      const int b = it & 1;
+      if (!mbar_wait(&pfull[b], (it >> 1) & 1, status)) return;
+      const float* pb = P + b * kQ4MmaDotWarps * 64;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int o = lane + 32 * h, m = o >> 3, n = o & 7;
+        float v = pb[o];
+#pragma unroll
+        for (int w = 1; w < kQ4MmaDotWarps; ++w) v = __fadd_rn(v, pb[w * 64 + o]);
+        const size_t row = begin + static_cast<size_t>(it) * kRowsPerStage + n;
+        if (m < M && row < end) out[static_cast<size_t>(m) * N + row] = v;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&pempty[b]);
+    }
+    return;
+  }
+
+  // Dot warp w owns blocks [w*bpw, (w+1)*bpw).  Thread (g, t): A rows m = g
+  // (hi) and g + 8 (lo); B column n = g (weight row g of the stage); D gives
+  // (m = g, n = 2t, 2t + 1).
+  const int dw = warp - 1;
+  const int g = lane >> 2, t = lane & 3;
+  const int bpw = static_cast<int>(nb / kQ4MmaDotWarps);
+  const int kb0 = dw * bpw;
+  if (!mbar_wait(xfull, 0, status)) return;
+  const uint8_t* xa = s_x + static_cast<size_t>(g < M ? g : 0) * xrow;
+  const bool arow = g < M;
+  for (int it = 0; it < iters; ++it) {
+    const int s = it % n_stages, pb = it & 1;
+    if (!mbar_wait(&full[s], (it / n_stages) & 1, status)) return;
+    const uint8_t* st = stage0 + s * L.stage_bytes;
+    const uint8_t* rowg = st + g * rstride;     // B: weight row g
+    const uint8_t* row0 = st + 2 * t * rstride;  // block scales of rows 2t, 2t + 1
+    float acc0 = 0.0f, acc1 = 0.0f;
+    for (int i0 = 0; i0 < bpw; i0 += kQ4MmaBatch) {
+      uint32_t wq[kQ4MmaBatch], db[kQ4MmaBatch];
+      uint4 a0[kQ4MmaBatch], a1[kQ4MmaBatch];
+#pragma unroll
+      for (int u = 0; u < kQ4MmaBatch; ++u) {
+        // Past the warp's range the loads repeat block kb0; those dots are
+        // not added.
+        const int kb = i0 + u < bpw ? kb0 + i0 + u : kb0;
+        // Block kb starts at 18*kb, its quants at +2: 2 mod 4 for even kb,
+        // word aligned for odd kb (warp-uniform).
+        const uint8_t* blk = rowg + kb * 18;
+        if ((kb & 1) == 0) {
+          const uint32_t* w = reinterpret_cast<const uint32_t*>(blk) + t;
+          wq[u] = __funnelshift_r(w[0], w[1], 16);
+        } else {
+          wq[u] = reinterpret_cast<const uint32_t*>(blk + 2)[t];
+        }
+        const uint8_t* d0 = row0 + kb * 18;
+        db[u] = static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(d0)) |
+                (static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(d0 + rstride)) << 16);
+        const uint4* ar = reinterpret_cast<const uint4*>(xa + static_cast<size_t>(kb) * 128) + t;
+        a0[u] = arow ? ar[0] : make_uint4(0u, 0u, 0u, 0u);
+        a1[u] = arow ? ar[4] : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int u = 0; u < kQ4MmaBatch; ++u) {
+        // Byte i of a Q4_0 block holds elements 2i (low nibble) and 2i + 1
+        // (high nibble) (q4_0.rs:59-68): thread t's word holds elements
+        // 8t..8t+7, the first four for k step 0 and the rest for k step 1.
+        const uint32_t lo = wq[u] & 0x0F0F0F0Fu, hi = (wq[u] >> 4) & 0x0F0F0F0Fu;
+        uint32_t b00, b01, b10, b11;
+        nib_bf16x2(__byte_perm(lo, hi, 0x5140), b00, b01);  // elements 8t..8t+3
+        nib_bf16x2(__byte_perm(lo, hi, 0x7362), b10, b11);  // elements 8t+4..8t+7
+        float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        mma_bf16_m16n8k16(d, a0[u], b00, b01);
+        mma_bf16_m16n8k16(d, a1[u], b10, b11);
+        if (i0 + u < bpw) {
+          acc0 = __fmaf_rn(f16_bits_to_f32(db[u] & 0xFFFFu), __fadd_rn(d[0], d[2]), acc0);
+          acc1 = __fmaf_rn(f16_bits_to_f32(db[u] >> 16), __fadd_rn(d[1], d[3]), acc1);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+    if (it >= 2 && !mbar_wait(&pempty[pb], ((it >> 1) - 1) & 1, status)) return;
+    *reinterpret_cast<float2*>(P + (pb * kQ4MmaDotWarps + dw) * 64 + g * 8 + 2 * t) =
+        make_float2(acc0, acc1);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&pfull[pb]);
+  }
+}
+
 template <int M>
 __global__ void __launch_bounds__(256) gemv_q4_0_generic_kernel(const uint8_t* __restrict__ W,
                                                                 size_t N, size_t K,
@@ -1682,6 +1930,70 @@ cudaError_t launch_gemv_q4_0_tma(const DeviceInfo& dev, cudaStream_t st, int M, 
                              pre_stages(stages), status);
     if (e != cudaSuccess) return e;
   });
+  if (ls) ls->launches++;
+  return cudaGetLastError();
+}
+
+// The bf16-MMA Q4_0 kernel covers M = 2..8 when nb % 8 == 0 (16-byte aligned
+// rows, an equal block range per dot warp) and the split activations plus
+// three stages fit.
+int q4_0_mma_stages(int M, size_t K) {
+  const size_t nb = K / 32;
+  return std::min(kMaxStages, stages_within(fixed_bytes_of(q4_mma_fixed_bytes(M, K), 5 * 8),
+                                            kRowsPerStage * q4_mma_row_stride(nb), kSmemBudget));
+}
+
+bool q4_0_mma_supported(int M, size_t K) {
+  static const bool off = [] {
+    const char* e = std::getenv("MRI_Q4_MMA");
+    return e != nullptr && std::atoi(e) == 0;
+  }();
+  if (off || M < 2 || M > 8 || K == 0 || K % 32 != 0) return false;
+  if ((K / 32) % kQ4MmaDotWarps != 0) return false;
+  return q4_0_mma_stages(M, K) >= 3;
+}
+
+size_t q4_0_split_bytes(size_t m, size_t K) { return m * q4_split_row_bytes(K); }
+
+cudaError_t launch_q4_0_split(const DeviceInfo&, cudaStream_t st, const float* x, size_t m, size_t K,
+                              uint32_t* xs, LaunchStats* ls) {
+  if ((reinterpret_cast<uintptr_t>(x) & 15) != 0 || (reinterpret_cast<uintptr_t>(xs) & 15) != 0 ||
+      K % 4 != 0)
+    return cudaErrorInvalidValue;
+  const size_t n4 = m * (K / 4);
+  if (n4 == 0) return cudaSuccess;
+  const int grid = static_cast<int>((n4 + 255) / 256);
+  cudaError_t e = launch_stream_kernel_threads(q4_split_act_kernel, grid, 256, st, x, m, K, xs);
+  if (ls) ls->launches++;
+  return e;
+}
+
+cudaError_t launch_gemv_q4_0_mma(const DeviceInfo& dev, cudaStream_t st, int M, const uint8_t* W,
+                                 size_t N, size_t K, const uint32_t* xs, float* out, int* status,
+                                 LaunchStats* ls) {
+  if (!q4_0_mma_supported(M, K) || (reinterpret_cast<uintptr_t>(xs) & 15) != 0 ||
+      (reinterpret_cast<uintptr_t>(W) & 15) != 0)
+    return cudaErrorInvalidValue;
+  const size_t nb = K / 32;
+  const int stages = q4_0_mma_stages(M, K);
+  const size_t smem =
+      make_layout(q4_mma_fixed_bytes(M, K), 5 * 8, kRowsPerStage * q4_mma_row_stride(nb), stages).total;
+  void (*kern)(const uint8_t*, size_t, size_t, const uint32_t*, float*, int, int*) = nullptr;
+  switch (M) {
+    case 2: kern = gemv_q4_0_mma_kernel<2>; break;
+    case 3: kern = gemv_q4_0_mma_kernel<3>; break;
+    case 4: kern = gemv_q4_0_mma_kernel<4>; break;
+    case 5: kern = gemv_q4_0_mma_kernel<5>; break;
+    case 6: kern = gemv_q4_0_mma_kernel<6>; break;
+    case 7: kern = gemv_q4_0_mma_kernel<7>; break;
+    case 8: kern = gemv_q4_0_mma_kernel<8>; break;
+    default: return cudaErrorInvalidValue;
+  }
+  cudaError_t e = set_smem(kern, smem, dev.device);
+  if (e != cudaSuccess) return e;
+  e = launch_stream_kernel<kQ4MmaThreads>(kern, stream_grid(dev, N, 1), smem, st, W, N, K, xs, out,
+                                          stages, status);
+  if (e != cudaSuccess) return e;
   if (ls) ls->launches++;
   return cudaGetLastError();
 }

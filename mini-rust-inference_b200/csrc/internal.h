@@ -154,6 +154,17 @@ cudaError_t launch_gemv_q8_0_generic(const DeviceInfo& dev, cudaStream_t st, int
                                      const float* scales, float* out, LaunchStats* ls);
 
 // Q4_0 (18-byte blocks), f32 activations.
+// M = 2..8 on the bf16 warp MMA: launch_q4_0_split writes x [m, K] (16-byte
+// aligned) as split bf16 pairs in fragment order (q4_0_split_bytes(m, K)
+// bytes, 16-byte aligned; a chunk of rows starts at row * q4_0_split_bytes(1,
+// K)), which launch_gemv_q4_0_mma then reads.
+bool q4_0_mma_supported(int M, size_t K);
+size_t q4_0_split_bytes(size_t m, size_t K);
+cudaError_t launch_q4_0_split(const DeviceInfo& dev, cudaStream_t st, const float* x, size_t m,
+                              size_t K, uint32_t* xs, LaunchStats* ls);
+cudaError_t launch_gemv_q4_0_mma(const DeviceInfo& dev, cudaStream_t st, int M, const uint8_t* W,
+                                 size_t N, size_t K, const uint32_t* xs, float* out, int* status,
+                                 LaunchStats* ls);
 bool gemv_q4_0_tma_supported(const DeviceInfo& dev, int M, size_t K);
 cudaError_t launch_gemv_q4_0_tma(const DeviceInfo& dev, cudaStream_t st, int M, const uint8_t* W,
                                  size_t N, size_t K, const float* x, float* out, int* status,

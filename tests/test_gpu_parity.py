@@ -268,6 +268,26 @@ def test_q4_0_within_tolerance(m, n, k, mri, oracle, gpu_ctx):
     assert ok, worst
 
 
+# M = 2..8 with K % 256 == 0 take the bf16-MMA Q4_0 kernel while the split
+# activations and three stages fit; (4, 20, 40960) and (3, 50, 96) fall back.
+Q4_MMA_SHAPES = [(3, 517, 2048), (7, 2049, 3072), (2, 148 * 8 + 1, 4096), (6, 333, 5120),
+                 (8, 40, 256), (8, 11008, 4096), (4, 20, 40960), (3, 50, 96)]
+
+
+@pytest.mark.parametrize("m,n,k", Q4_MMA_SHAPES)
+def test_q4_0_multirow_within_tolerance(m, n, k, mri, oracle, gpu_ctx):
+    rng = np.random.default_rng(4500 + m + n + k)
+    w = rng.normal(0, 0.02, size=(n, k)).astype(np.float32)
+    x = rng.normal(0, 1, size=(m, k)).astype(np.float32)
+    x[0, :] = 0.0            # a zero row
+    x[m - 1, 7] = 3.0e4      # one large element
+    wb = oracle.quantize_q4_0_matrix(w, n, k)
+    got = mri.matmul_q4_0_dequant(x, wb, n, k)
+    want = oracle.matmul_q4_0_dequant(x, m, k, wb, n, k)
+    ok, worst = q4_close(got, want, x, oracle.dequantize_q4_0(wb).reshape(n, k))
+    assert ok, worst
+
+
 def test_sharded_equals_unsharded(mri, oracle, gpu_ctx):
     """An N-column shard computes bit-identical columns (the per-(m, n)
     arithmetic does not depend on the other rows of W)."""

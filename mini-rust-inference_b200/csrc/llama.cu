@@ -37,6 +37,7 @@
 namespace {
 
 constexpr int kAttnChunk = 64;   // keys per split in decode attention
+constexpr int kMergeChunk = 256;  // splits whose merge weights sit in shared memory at once
 constexpr int kPrefillQ = 16;    // queries per block in prefill attention
 constexpr int kPrefillKT = 64;   // keys per shared-memory tile in prefill attention
 constexpr int kMaxHeadDim = 128;
@@ -101,9 +102,9 @@ __global__ void rope_kv_kernel(float* __restrict__ qkv, int ld, int n_heads, int
 
 // Decode attention, split over keys (attention/cached.rs:141-190 with
 // gqa.rs:217-237): block (h, s) handles keys [s*64, min(s*64+64, pos+1)).
-// Warp w takes 16 of them in two rounds of 8; a lane owns 4 head dimensions
-// (hd % 4 == 0, hd <= 128), loads the 8 keys' and values' float4 before using
-// any, reduces each score over the warp with shuffles and keeps an online
+// Warp w takes 16 of them; a lane owns 4 head dimensions (hd % 4 == 0,
+// hd <= 128), loads the 16 keys' and values' float4 before using any,
+// reduces each score over the warp with shuffles and keeps an online
 // softmax (running max, exp-sum, weighted V sum) — no block-wide barrier until
 // the 4 warps' partials are combined.  Each block writes its partial; the last
 // block of a head to finish (ticket counter) merges the head's splits and
@@ -138,32 +139,37 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const float* __restric
                            : make_float4(0.f, 0.f, 0.f, 0.f);
   float m = -INFINITY, l = 0.0f;
   float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+  // All of the warp's keys and values are loaded before any is used (one
+  // memory latency per split), then scored in key order.
+  float4 kk[2 * kRound], vv[2 * kRound];
+#pragma unroll
+  for (int i = 0; i < 2 * kRound; ++i) {
+    const int key = warp * 2 * kRound + i;
+    const bool ok = dim_ok && key < nkeys;
+    const size_t row = static_cast<size_t>(j0 + key) * kvd + base;
+    kk[i] = ok ? mri::ld_act(reinterpret_cast<const float4*>(kc + row)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    vv[i] = ok ? mri::ld_act(reinterpret_cast<const float4*>(vc + row)) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+#pragma unroll
   for (int r = 0; r < 2; ++r) {
     const int k0 = warp * 2 * kRound + r * kRound;  // first key of this round, within the chunk
-    float4 kk[kRound], vv[kRound];
-#pragma unroll
-    for (int i = 0; i < kRound; ++i) {
-      const bool ok = dim_ok && k0 + i < nkeys;
-      const size_t row = static_cast<size_t>(j0 + k0 + i) * kvd + base;
-      kk[i] = ok ? mri::ld_act(reinterpret_cast<const float4*>(kc + row)) : make_float4(0.f, 0.f, 0.f, 0.f);
-      vv[i] = ok ? mri::ld_act(reinterpret_cast<const float4*>(vc + row)) : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
 #pragma unroll
     for (int i = 0; i < kRound; ++i) {
       if (k0 + i >= nkeys) break;  // warp-uniform
-      float d = __fmaf_rn(qv.x, kk[i].x, 0.0f);
-      d = __fmaf_rn(qv.y, kk[i].y, d);
-      d = __fmaf_rn(qv.z, kk[i].z, d);
-      d = __fmaf_rn(qv.w, kk[i].w, d);
+      const float4 kv = kk[r * kRound + i], vw = vv[r * kRound + i];
+      float d = __fmaf_rn(qv.x, kv.x, 0.0f);
+      d = __fmaf_rn(qv.y, kv.y, d);
+      d = __fmaf_rn(qv.z, kv.z, d);
+      d = __fmaf_rn(qv.w, kv.w, d);
       d = mri::warp_sum_f(d);
       const float sc = __fmul_rn(d, scale);
       const float mn = fmaxf(m, sc);
       const float corr = expf(m - mn), p = expf(sc - mn);
       l = __fadd_rn(__fmul_rn(l, corr), p);
-      o.x = __fmaf_rn(p, vv[i].x, __fmul_rn(o.x, corr));
-      o.y = __fmaf_rn(p, vv[i].y, __fmul_rn(o.y, corr));
-      o.z = __fmaf_rn(p, vv[i].z, __fmul_rn(o.z, corr));
-      o.w = __fmaf_rn(p, vv[i].w, __fmul_rn(o.w, corr));
+      o.x = __fmaf_rn(p, vw.x, __fmul_rn(o.x, corr));
+      o.y = __fmaf_rn(p, vw.y, __fmul_rn(o.y, corr));
+      o.z = __fmaf_rn(p, vw.z, __fmul_rn(o.z, corr));
+      o.w = __fmaf_rn(p, vw.w, __fmul_rn(o.w, corr));
       m = mn;
     }
   }
@@ -197,17 +203,49 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const float* __restric
   __syncthreads();
   if (!last) return;
   __threadfence();
+  // Merge.  The splits' maxima are read in parallel and each split's weight
+  // exp(m_t - gm) is computed once into shared memory; the sums then run over
+  // t in increasing order as before (loads independent, so they overlap).
   const float* ph = part + static_cast<size_t>(h) * max_splits * kStride;
-  float gm = -INFINITY;
-  for (int t = 0; t < active; ++t) gm = fmaxf(gm, __ldcg(ph + t * kStride));
+  __shared__ float s_w[kMergeChunk];
+  __shared__ float s_red[4];
+  float lm = -INFINITY;
+  for (int t = threadIdx.x; t < active; t += blockDim.x) lm = fmaxf(lm, __ldcg(ph + t * kStride));
+  lm = mri::warp_max(lm);
+  if (lane == 0) s_red[warp] = lm;
+  __syncthreads();
+  const float gm = fmaxf(fmaxf(s_red[0], s_red[1]), fmaxf(s_red[2], s_red[3]));
   float gl = 0.0f;
-  for (int t = 0; t < active; ++t) gl += __ldcg(ph + t * kStride + 1) * expf(__ldcg(ph + t * kStride) - gm);
-  const float inv = __fdiv_rn(1.0f, gl);
-  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
-    float acc = 0.0f;
-    for (int t = 0; t < active; ++t)
-      acc += __ldcg(ph + t * kStride + 2 + d) * expf(__ldcg(ph + t * kStride) - gm);
-    out[h * hd + d] = acc * inv;
+  float acc[(kMaxHeadDim + 127) / 128];
+#pragma unroll
+  for (int i = 0; i < (kMaxHeadDim + 127) / 128; ++i) acc[i] = 0.0f;
+  for (int t0 = 0; t0 < active; t0 += kMergeChunk) {
+    const int tn = min(kMergeChunk, active - t0);
+    const float* pc = ph + static_cast<size_t>(t0) * kStride;
+    for (int t = threadIdx.x; t < tn; t += blockDim.x) s_w[t] = expf(__ldcg(pc + t * kStride) - gm);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+#pragma unroll 8
+      for (int t = 0; t < tn; ++t) gl += __ldcg(pc + t * kStride + 1) * s_w[t];
+    }
+#pragma unroll
+    for (int i = 0; i < (kMaxHeadDim + 127) / 128; ++i) {
+      const int d = threadIdx.x + i * 128;
+      if (d < hd) {
+#pragma unroll 8
+        for (int t = 0; t < tn; ++t) acc[i] += __ldcg(pc + t * kStride + 2 + d) * s_w[t];
+      }
+    }
+    __syncthreads();
+  }
+  __shared__ float s_gl;
+  if (threadIdx.x == 0) s_gl = gl;
+  __syncthreads();
+  const float inv = __fdiv_rn(1.0f, s_gl);
+#pragma unroll
+  for (int i = 0; i < (kMaxHeadDim + 127) / 128; ++i) {
+    const int d = threadIdx.x + i * 128;
+    if (d < hd) out[h * hd + d] = acc[i] * inv;
   }
   if (threadIdx.x == 0) tickets[h] = 0;
 }

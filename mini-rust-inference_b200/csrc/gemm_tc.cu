@@ -141,8 +141,11 @@ __device__ __forceinline__ void tmem_ld_32cols(uint32_t taddr, uint32_t (&v)[32]
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-template <int BN, int kStages>
-__global__ void __launch_bounds__(kTcThreads, 1)
+// kBufs TMEM accumulator buffers: 2 for the persistent grid (tile t + 1's MMAs
+// run while tile t is drained), 1 when every CTA takes exactly one tile and two
+// CTAs share an SM (each holds half of the SM's 512 TMEM columns).
+template <int BN, int kStages, int kBufs>
+__global__ void __launch_bounds__(kTcThreads, kBufs == 1 ? 2 : 1)
     gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const float* __restrict__ act_scale, int scale_per_row,
                       const float* __restrict__ w_scales, float* out,
@@ -183,7 +186,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_addr(tmem_slot)),
-                 "r"(2 * acc_stride<BN>())
+                 "r"(kBufs * acc_stride<BN>())
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -354,7 +357,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
-                 "r"(2 * acc_stride<BN>())
+                 "r"(kBufs * acc_stride<BN>())
                  : "memory");
   }
 }
@@ -433,18 +436,25 @@ int pick_bn(const DeviceInfo& dev, size_t M, size_t N) {
   return best;
 }
 
-template <int BN, int kStages>
+template <int BN, int kStages, int kBufs = 2>
 cudaError_t launch_bn(const DeviceInfo& dev, cudaStream_t st, const CUtensorMap& ta,
                       const CUtensorMap& tb, const float* act_scale, int per_row,
                       const float* w_scales, size_t M, size_t N, size_t K, float* out,
                       int32_t* acc_out, int* status, const float* residual) {
   static_assert(TcLayout<BN, kStages>::total <= 232448, "stage ring exceeds the per-CTA shared memory");
+  // Two CTAs per SM: both rings plus the 1 KB the runtime reserves per CTA
+  // within the SM's 228 KB.
+  static_assert(kBufs == 2 || 2 * (TcLayout<BN, kStages>::total + 1024) <= 233472,
+                "two CTAs per SM do not fit");
   const size_t smem = TcLayout<BN, kStages>::total;
-  cudaError_t e = set_smem_tc(gemm_i8_tc_kernel<BN, kStages>, smem, dev.device);
+  cudaError_t e = set_smem_tc(gemm_i8_tc_kernel<BN, kStages, kBufs>, smem, dev.device);
   if (e != cudaSuccess) return e;
   const size_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  // One tile per CTA when kBufs == 1 (the launcher only picks it for
+  // tiles <= 2 * sm_count).
+  if (kBufs == 1 && tiles > 2 * static_cast<size_t>(dev.sm_count)) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(std::min<size_t>(tiles, dev.sm_count)));
+  cfg.gridDim = dim3(static_cast<unsigned>(kBufs == 1 ? tiles : std::min<size_t>(tiles, dev.sm_count)));
   cfg.blockDim = dim3(kTcThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
@@ -453,7 +463,7 @@ cudaError_t launch_bn(const DeviceInfo& dev, cudaStream_t st, const CUtensorMap&
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, gemm_i8_tc_kernel<BN, kStages>, ta, tb, act_scale, per_row, w_scales,
+  return cudaLaunchKernelEx(&cfg, gemm_i8_tc_kernel<BN, kStages, kBufs>, ta, tb, act_scale, per_row, w_scales,
                             out, acc_out, static_cast<int>(M), static_cast<int>(N),
                             static_cast<int>(K), status, residual);
 }
@@ -484,6 +494,24 @@ cudaError_t launch_gemm_i8_tc(const DeviceInfo& dev, cudaStream_t st, const int8
     e = launch_bn<BNV, ST>(dev, st, ta, tb, act_scale_dev, scale_per_row, w_scales, M, N, K, out, \
                            acc_out, status, residual);                                         \
     break;
+  // Between one and two rounds of tiles, one tile per CTA with two CTAs per
+  // SM (3-stage rings, one accumulator buffer each): the second CTA's loads
+  // and MMAs fill the first one's gaps, and each CTA's epilogue overlaps the
+  // other's main loop.  MRI_GEMM_2CTA=0 keeps the persistent grid.
+  static const bool two_cta = [] {
+    const char* v = std::getenv("MRI_GEMM_2CTA");
+    return v == nullptr || std::atoi(v) != 0;
+  }();
+  const size_t tiles = ((M + BM - 1) / BM) * ((N + bn - 1) / bn);
+  if (two_cta && (bn == 128 || bn == 160) && tiles > static_cast<size_t>(dev.sm_count) &&
+      tiles <= 2 * static_cast<size_t>(dev.sm_count)) {
+    e = bn == 128 ? launch_bn<128, 3, 1>(dev, st, ta, tb, act_scale_dev, scale_per_row, w_scales, M, N, K,
+                                         out, acc_out, status, residual)
+                  : launch_bn<160, 3, 1>(dev, st, ta, tb, act_scale_dev, scale_per_row, w_scales, M, N, K,
+                                         out, acc_out, status, residual);
+    if (ls) ls->launches++;
+    return e;
+  }
   switch (bn) {
     MRI_GEMM_BN_CASE(128, 6)
     MRI_GEMM_BN_CASE(160, 6)

@@ -340,6 +340,25 @@ def test_gemm_tile_widths_exact(mri, oracle, gpu_ctx, monkeypatch, bn):
     assert np.array_equal(bits(got), bits(want))
 
 
+@pytest.mark.parametrize("bn", [128, 160])
+def test_gemm_two_ctas_per_sm_exact(mri, oracle, gpu_ctx, monkeypatch, bn):
+    """Between one and two rounds of tiles (here 196 or 244 tiles on 148 SMs)
+    the GEMM runs one tile per CTA, two CTAs per SM: same INT32 sums and f32
+    outputs as the oracle on ragged M and N."""
+    monkeypatch.setenv("MRI_GEMM_BN", str(bn))
+    rng = np.random.default_rng(200 + bn)
+    m, n, k = 500, 7717, 1024 + 256
+    aq = rng.integers(-127, 128, size=m * k, dtype=np.int8)
+    wq = rng.integers(-127, 128, size=n * k, dtype=np.int8)
+    ws = rng.uniform(0.001, 0.02, size=n).astype(np.float32)
+    qm = mri.QuantizedMatrix(wq, ws, n, k)
+    acc = np.zeros((m, n), np.int32)
+    got = mri.matmul_int8(aq, np.float32(0.0123), qm, m, acc_out=acc)
+    want, want_acc = oracle.matmul_int8(aq, np.float32(0.0123), wq, ws, n, k, m)
+    assert np.array_equal(acc, want_acc)
+    assert np.array_equal(bits(got), bits(want))
+
+
 def test_device_status_clean(mri, gpu_ctx):
     """No bounded device-side wait gave up during the tests above."""
     gpu_ctx.check_device_status()

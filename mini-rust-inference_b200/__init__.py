@@ -22,6 +22,7 @@ Import with importlib (the directory name is not an identifier):
     mri = importlib.import_module("mini-rust-inference_b200")
 """
 import ctypes
+import sys
 import threading
 
 import numpy as np
@@ -115,6 +116,11 @@ class Context:
             self.handle = ctypes.c_void_p()
 
     def __del__(self):
+        # At interpreter exit objects are finalized in no fixed order (a
+        # context's stream may already be gone when a model or matrix that used
+        # it is collected), and the process releases device memory anyway.
+        if sys.is_finalizing():
+            return
         try:
             self.close()
         except Exception:  # noqa: BLE001 - interpreter shutdown
@@ -192,6 +198,11 @@ class QuantizedMatrix:
             self.scales = scales[begin:end]
 
     def __del__(self):
+        # At interpreter exit objects are finalized in no fixed order (a
+        # context's stream may already be gone when a model or matrix that used
+        # it is collected), and the process releases device memory anyway.
+        if sys.is_finalizing():
+            return
         try:
             if self.handle:
                 self.ctx._lib.mri_qmatrix_free(self.handle)
@@ -245,6 +256,11 @@ class Q8_0WeightMatrix:
         return formats.dequantize_q8_0(self.data)
 
     def __del__(self):
+        # At interpreter exit objects are finalized in no fixed order (a
+        # context's stream may already be gone when a model or matrix that used
+        # it is collected), and the process releases device memory anyway.
+        if sys.is_finalizing():
+            return
         try:
             if self.handle:
                 self.ctx._lib.mri_q8_0_free(self.handle)
@@ -264,6 +280,11 @@ class Q4_0Matrix:
         self.handle, self.data, self.n_out, self.k = h, d, n_out, k
 
     def __del__(self):
+        # At interpreter exit objects are finalized in no fixed order (a
+        # context's stream may already be gone when a model or matrix that used
+        # it is collected), and the process releases device memory anyway.
+        if sys.is_finalizing():
+            return
         try:
             if self.handle:
                 self.ctx._lib.mri_q4_0_free(self.handle)
@@ -465,6 +486,11 @@ class Communicator:
             self.handle = ctypes.c_void_p()
 
     def __del__(self):
+        # At interpreter exit objects are finalized in no fixed order (a
+        # context's stream may already be gone when a model or matrix that used
+        # it is collected), and the process releases device memory anyway.
+        if sys.is_finalizing():
+            return
         try:
             self.close()
         except Exception:  # noqa: BLE001 - interpreter shutdown
@@ -542,6 +568,11 @@ class LlamaModelInt8:
         self.handle = h
 
     def __del__(self):
+        # At interpreter exit objects are finalized in no fixed order (a
+        # context's stream may already be gone when a model or matrix that used
+        # it is collected), and the process releases device memory anyway.
+        if sys.is_finalizing():
+            return
         try:
             if self.handle:
                 self._lib.mri_llama_free(self.handle)

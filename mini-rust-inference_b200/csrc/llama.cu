@@ -341,6 +341,231 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(const float* __restri
   }
 }
 
+// Prefill attention on the tensor cores (flash-attention style): block (h, qb)
+// handles queries [qb*64, qb*64+64) of head h, a warp 16 of them.  Per tile of
+// 64 cached keys, S = Q K^T and O += P V run on mma.sync m16n8k16 with f16
+// operands and f32 accumulators: Q is held as A fragments, K and V^T are
+// converted into shared memory (rows padded so a fragment load hits 32
+// banks), P comes straight from S's accumulator layout.  Every operand is
+// split into f16 hi + lo parts and each product is hi.hi + hi.lo + lo.hi
+// (about 22 significant bits, close to the f32 kernel): the attention output
+// is quantized to int8 by the next projection, and an error of ~1e-3 (single
+// f16 operands) flips enough of those roundings to move the logits by a few
+// percent of their range.  The causal mask (key <= start + query), the scale
+// and the online softmax (running max, sum) are f32, per row over the 4
+// threads that hold it.  q, k and v must lie within the f16 range.  HD = head
+// dim (64 or 128).
+constexpr int kFaQ = 64;   // queries per block
+constexpr int kFaKT = 64;  // keys per tile
+
+__device__ __forceinline__ uint32_t half2_bits(float lo, float hi) {
+  const __half2 v = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+// Two floats as f16 pairs hi = f16(x), lo = f16(x - hi).
+__device__ __forceinline__ void split_half2(float2 v, uint32_t& hi, uint32_t& lo) {
+  const __half2 h = __floats2half2_rn(v.x, v.y);
+  const float2 hf = __half22float2(h);
+  hi = *reinterpret_cast<const uint32_t*>(&h);
+  lo = half2_bits(__fsub_rn(v.x, hf.x), __fsub_rn(v.y, hf.y));
+}
+
+__device__ __forceinline__ void mma_f16_m16n8k16(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+      "{%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+template <int HD>
+__global__ void __launch_bounds__(128) attn_prefill_tc_kernel(const float* __restrict__ qkv, int ld,
+                                                              int n_heads, int n_kv, int M, int start,
+                                                              const float* __restrict__ kc,
+                                                              const float* __restrict__ vc, float scale,
+                                                              float* __restrict__ out, int out_ld) {
+  constexpr int KS = HD / 16;     // k steps of S = Q K^T
+  constexpr int NT = HD / 8;      // n tiles of O
+  constexpr int SK = HD + 8;      // halves per K row in shared memory
+  constexpr int SV = kFaKT + 8;   // halves per V^T row (one head dim) in shared memory
+  extern __shared__ __align__(16) __half fa_smem[];
+  __half* sK = fa_smem;                 // [64 keys][SK] hi parts
+  __half* sKl = sK + kFaKT * SK;        // [64 keys][SK] lo parts
+  __half* sVt = sKl + kFaKT * SK;       // [HD][SV] hi parts
+  __half* sVtl = sVt + HD * SV;         // [HD][SV] lo parts
+  const int h = blockIdx.x, q0 = blockIdx.y * kFaQ;
+  const int kv_h = h / (n_heads / n_kv);
+  const int kvd = n_kv * HD;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int ra = q0 + warp * 16 + g, rb = ra + 8;  // this thread's two query rows
+  // Q fragments (rows ra, rb; dims 16k + 2t, +1 and 16k + 8 + 2t, +1), hi and lo.
+  uint32_t qa[KS][4], ql[KS][4];
+#pragma unroll
+  for (int k = 0; k < KS; ++k) {
+    const int d0 = 16 * k + 2 * t;
+    float2 a = make_float2(0.f, 0.f), b = a, c = a, e = a;
+    if (ra < M) {
+      const float* q = qkv + static_cast<size_t>(ra) * ld + h * HD;
+      a = *reinterpret_cast<const float2*>(q + d0);
+      c = *reinterpret_cast<const float2*>(q + d0 + 8);
+    }
+    if (rb < M) {
+      const float* q = qkv + static_cast<size_t>(rb) * ld + h * HD;
+      b = *reinterpret_cast<const float2*>(q + d0);
+      e = *reinterpret_cast<const float2*>(q + d0 + 8);
+    }
+    split_half2(a, qa[k][0], ql[k][0]);
+    split_half2(b, qa[k][1], ql[k][1]);
+    split_half2(c, qa[k][2], ql[k][2]);
+    split_half2(e, qa[k][3], ql[k][3]);
+  }
+  float o[NT][4];
+#pragma unroll
+  for (int n = 0; n < NT; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
+  float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.0f, l_b = 0.0f;
+  const int last_key = start + min(q0 + kFaQ, M) - 1;
+  for (int kt = 0; kt <= last_key; kt += kFaKT) {
+    const int nk = min(kFaKT, last_key + 1 - kt);
+    __syncthreads();
+    // K tile -> sK[key][dim], V tile -> sVt[dim][key] (f16); keys past nk are 0.
+    for (int i = threadIdx.x; i < kFaKT * (HD / 4); i += blockDim.x) {
+      const int j = i / (HD / 4), d = (i % (HD / 4)) * 4;
+      float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+      if (j < nk) {
+        const size_t off = static_cast<size_t>(kt + j) * kvd + kv_h * HD + d;
+        kv = *reinterpret_cast<const float4*>(kc + off);
+        vv = *reinterpret_cast<const float4*>(vc + off);
+      }
+      uint32_t h0, l0, h1, l1;
+      split_half2(make_float2(kv.x, kv.y), h0, l0);
+      split_half2(make_float2(kv.z, kv.w), h1, l1);
+      *reinterpret_cast<uint2*>(sK + j * SK + d) = make_uint2(h0, h1);
+      *reinterpret_cast<uint2*>(sKl + j * SK + d) = make_uint2(l0, l1);
+      const float vf[4] = {vv.x, vv.y, vv.z, vv.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const __half hv = __float2half_rn(vf[i]);
+        sVt[(d + i) * SV + j] = hv;
+        sVtl[(d + i) * SV + j] = __float2half_rn(__fsub_rn(vf[i], __half2float(hv)));
+      }
+    }
+    __syncthreads();
+    // S = Q K^T for this warp's 16 queries x 64 keys (8 n tiles of 8 keys).
+    float sc[kFaKT / 8][4];
+#pragma unroll
+    for (int n = 0; n < kFaKT / 8; ++n) {
+      sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.0f;
+      const __half* kr = sK + (n * 8 + g) * SK + 2 * t;
+      const __half* klr = sKl + (n * 8 + g) * SK + 2 * t;
+#pragma unroll
+      for (int k = 0; k < KS; ++k) {
+        const uint32_t kh0 = *reinterpret_cast<const uint32_t*>(kr + 16 * k);
+        const uint32_t kh1 = *reinterpret_cast<const uint32_t*>(kr + 16 * k + 8);
+        mma_f16_m16n8k16(sc[n], qa[k], kh0, kh1);
+        mma_f16_m16n8k16(sc[n], ql[k], kh0, kh1);
+        mma_f16_m16n8k16(sc[n], qa[k], *reinterpret_cast<const uint32_t*>(klr + 16 * k),
+                         *reinterpret_cast<const uint32_t*>(klr + 16 * k + 8));
+      }
+    }
+    // Scale and causal mask; row maxima over the 4 threads of a row.
+    float mx_a = -INFINITY, mx_b = -INFINITY;
+#pragma unroll
+    for (int n = 0; n < kFaKT / 8; ++n) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int key = kt + n * 8 + 2 * t + (c & 1);
+        const int row = c < 2 ? ra : rb;
+        const bool ok = key - kt < nk && row < M && key <= start + row;
+        sc[n][c] = ok ? __fmul_rn(sc[n][c], scale) : -INFINITY;
+      }
+      mx_a = fmaxf(mx_a, fmaxf(sc[n][0], sc[n][1]));
+      mx_b = fmaxf(mx_b, fmaxf(sc[n][2], sc[n][3]));
+    }
+    mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 1));
+    mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 2));
+    mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 1));
+    mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 2));
+    const float mn_a = fmaxf(m_a, mx_a), mn_b = fmaxf(m_b, mx_b);
+    // A row with nothing visible yet keeps m = -inf, l = 0, o = 0.
+    const float corr_a = mn_a == -INFINITY ? 1.0f : expf(m_a - mn_a);
+    const float corr_b = mn_b == -INFINITY ? 1.0f : expf(m_b - mn_b);
+    float ps_a = 0.0f, ps_b = 0.0f;
+#pragma unroll
+    for (int n = 0; n < kFaKT / 8; ++n) {
+      sc[n][0] = sc[n][0] == -INFINITY ? 0.0f : expf(sc[n][0] - mn_a);
+      sc[n][1] = sc[n][1] == -INFINITY ? 0.0f : expf(sc[n][1] - mn_a);
+      sc[n][2] = sc[n][2] == -INFINITY ? 0.0f : expf(sc[n][2] - mn_b);
+      sc[n][3] = sc[n][3] == -INFINITY ? 0.0f : expf(sc[n][3] - mn_b);
+      ps_a += sc[n][0] + sc[n][1];
+      ps_b += sc[n][2] + sc[n][3];
+    }
+    l_a = l_a * corr_a + ps_a;
+    l_b = l_b * corr_b + ps_b;
+    m_a = mn_a;
+    m_b = mn_b;
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+      o[n][0] *= corr_a;
+      o[n][1] *= corr_a;
+      o[n][2] *= corr_b;
+      o[n][3] *= corr_b;
+    }
+    // O += P V: P's k step j (keys 16j..16j+15) is S's n tiles 2j and 2j+1.
+#pragma unroll
+    for (int j = 0; j < kFaKT / 16; ++j) {
+      uint32_t pa[4], pl[4];
+      split_half2(make_float2(sc[2 * j][0], sc[2 * j][1]), pa[0], pl[0]);
+      split_half2(make_float2(sc[2 * j][2], sc[2 * j][3]), pa[1], pl[1]);
+      split_half2(make_float2(sc[2 * j + 1][0], sc[2 * j + 1][1]), pa[2], pl[2]);
+      split_half2(make_float2(sc[2 * j + 1][2], sc[2 * j + 1][3]), pa[3], pl[3]);
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+        const __half* vr = sVt + (n * 8 + g) * SV + 16 * j + 2 * t;
+        const __half* vlr = sVtl + (n * 8 + g) * SV + 16 * j + 2 * t;
+        const uint32_t vh0 = *reinterpret_cast<const uint32_t*>(vr);
+        const uint32_t vh1 = *reinterpret_cast<const uint32_t*>(vr + 8);
+        mma_f16_m16n8k16(o[n], pa, vh0, vh1);
+        mma_f16_m16n8k16(o[n], pl, vh0, vh1);
+        mma_f16_m16n8k16(o[n], pa, *reinterpret_cast<const uint32_t*>(vlr),
+                         *reinterpret_cast<const uint32_t*>(vlr + 8));
+      }
+    }
+  }
+  // Row sums over the 4 threads of a row, then O / l.
+  l_a += __shfl_xor_sync(0xffffffffu, l_a, 1);
+  l_a += __shfl_xor_sync(0xffffffffu, l_a, 2);
+  l_b += __shfl_xor_sync(0xffffffffu, l_b, 1);
+  l_b += __shfl_xor_sync(0xffffffffu, l_b, 2);
+  const float ia = __fdiv_rn(1.0f, l_a), ib = __fdiv_rn(1.0f, l_b);
+#pragma unroll
+  for (int n = 0; n < NT; ++n) {
+    const int d = n * 8 + 2 * t;
+    if (ra < M)
+      *reinterpret_cast<float2*>(out + static_cast<size_t>(ra) * out_ld + h * HD + d) =
+          make_float2(o[n][0] * ia, o[n][1] * ia);
+    if (rb < M)
+      *reinterpret_cast<float2*>(out + static_cast<size_t>(rb) * out_ld + h * HD + d) =
+          make_float2(o[n][2] * ib, o[n][3] * ib);
+  }
+}
+
+// Dynamic shared memory of attn_prefill_tc_kernel<hd>: K and V^T tiles, hi and lo.
+size_t fa_smem_bytes(int hd) {
+  return (2 * static_cast<size_t>(kFaKT) * (hd + 8) + 2 * static_cast<size_t>(hd) * (kFaKT + 8)) *
+         sizeof(__half);
+}
+
+// MRI_TC_ATTN=0 keeps the CUDA-core prefill attention.
+bool tc_attn() {
+  static const bool on = [] {
+    const char* e = std::getenv("MRI_TC_ATTN");
+    return e == nullptr || std::atoi(e) != 0;
+  }();
+  return on;
+}
+
 // Greedy sampling: argmax (first index on ties; NaN never wins) -> next
 // token; position += 1.  Block b reduces a slice of the logits into
 // part[b]; the last block to finish (ticket) reduces the partials, writes the
@@ -601,6 +826,26 @@ int run_blocks(mri_llama* m, size_t rows, int pos0, bool decode_dev) {
       LL_TRY(pdl_launch(attn_decode_kernel, dim3(c.n_heads, m->max_splits), dim3(128), st, m->qkv,
                         c.n_heads, c.n_kv_heads, m->hd, kc, vc, m->d_pos, scale, m->part,
                         m->max_splits, m->tickets, m->attn));
+    } else if ((m->hd == 64 || m->hd == 128) && (m->qkv_w % 2) == 0 && (m->qd % 2) == 0 && tc_attn()) {
+      const dim3 grid(c.n_heads, static_cast<unsigned>((rows + kFaQ - 1) / kFaQ));
+      const size_t smem = fa_smem_bytes(m->hd);
+      static bool fa_attr_set[64] = {false};
+      const int dv = m->ctx->device;
+      if (dv >= 0 && dv < 64 && !fa_attr_set[dv]) {
+        LL_TRY(cudaFuncSetAttribute(attn_prefill_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(fa_smem_bytes(64))));
+        LL_TRY(cudaFuncSetAttribute(attn_prefill_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(fa_smem_bytes(128))));
+        fa_attr_set[dv] = true;
+      }
+      if (m->hd == 64)
+        attn_prefill_tc_kernel<64><<<grid, 128, smem, st>>>(m->qkv, m->qkv_w, c.n_heads, c.n_kv_heads,
+                                                            static_cast<int>(rows), pos0, kc, vc, scale,
+                                                            m->attn, m->qd);
+      else
+        attn_prefill_tc_kernel<128><<<grid, 128, smem, st>>>(m->qkv, m->qkv_w, c.n_heads, c.n_kv_heads,
+                                                             static_cast<int>(rows), pos0, kc, vc, scale,
+                                                             m->attn, m->qd);
     } else {
       const size_t smem = (kPrefillKT * (kMaxHeadDim + 1) + kPrefillKT * kMaxHeadDim +
                            kPrefillQ * kMaxHeadDim) * sizeof(float);

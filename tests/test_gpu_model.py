@@ -127,6 +127,20 @@ def test_larger_gqa_model_uses_gemm_and_matches(mri, oracle):
     assert rel_range_err(gpu.forward_decode(5, 40), ref.forward_decode(5, 40)) < TOL
 
 
+def test_head_dim_128_prefill_spans_tiles(mri, oracle):
+    """Head dim 128 (the Llama-7B head), 4 query / 2 KV heads, a 150-token
+    prefill: three 64-query blocks and three 64-key tiles of the tensor-core
+    prefill attention, then a cached decode step."""
+    cfg = dict(n_layers=2, dim=512, n_heads=4, n_kv_heads=2, ffn_dim=768, vocab=500, max_seq=192,
+               rope_base=10000.0, rms_eps=1e-5)
+    gpu, ref = build_pair(mri, oracle, cfg, random_weights(cfg, 5))
+    toks = list(np.random.default_rng(6).integers(0, 500, size=150))
+    got, want = gpu.forward(toks), ref.prefill_cached(toks)
+    for r in (0, 63, 64, 127, 128, 149):
+        assert rel_range_err(got[r], want[r]) < TOL, r
+    assert rel_range_err(gpu.forward_decode(7, 150), ref.forward_decode(7, 150)) < TOL
+
+
 def test_decode_is_deterministic_at_scale(mri):
     """Two greedy runs and two decodes of the same step agree bit for bit on a
     model large enough that consecutive kernels overlap under programmatic

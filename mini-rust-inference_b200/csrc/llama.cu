@@ -68,6 +68,44 @@ __global__ void embed_kernel(const uint32_t* __restrict__ tokens, const float* _
 // (i, h): head h of token row i at absolute position base + i, where base is
 // *pos_dev if given, else pos0; heads [0, H) are queries, [H, H+Hkv) keys
 // (whose blocks also copy the matching value head into the cache).
+// Prefill form: block i takes token row i whole (all query and key heads and
+// the value copy), four elements (two rotation pairs) per thread step, the
+// same arithmetic per element.  hd % 4 == 0, ld % 4 == 0, 16-byte aligned
+// rows and caches.
+__global__ void __launch_bounds__(256) rope_kv_rows_kernel(float* __restrict__ qkv, int ld, int n_heads,
+                                                           int n_kv, int hd,
+                                                           const float* __restrict__ cos_t,
+                                                           const float* __restrict__ sin_t, int pos0,
+                                                           float* __restrict__ kc, float* __restrict__ vc) {
+  pdl_trigger();
+  pdl_wait();
+  const int i = blockIdx.x;
+  const int pos = pos0 + i;
+  const int half = hd / 2;
+  float* row = qkv + static_cast<size_t>(i) * ld;
+  const int kvd = n_kv * hd, qd = n_heads * hd;
+  const float* cr = cos_t + static_cast<size_t>(pos) * half;
+  const float* sr = sin_t + static_cast<size_t>(pos) * half;
+  float* krow = kc + static_cast<size_t>(pos) * kvd;
+  float* vrow = vc + static_cast<size_t>(pos) * kvd;
+  // q and k: elements e..e+3 of the (qd + kvd)-wide rotated part.
+  for (int e = threadIdx.x * 4; e < qd + kvd; e += blockDim.x * 4) {
+    const int j = (e % hd) / 2;  // first of the two pairs
+    float4 v = mri::ld_act(reinterpret_cast<const float4*>(row + e));
+    const float2 c = *reinterpret_cast<const float2*>(cr + j);
+    const float2 sn = *reinterpret_cast<const float2*>(sr + j);
+    float4 y;
+    y.x = __fsub_rn(__fmul_rn(v.x, c.x), __fmul_rn(v.y, sn.x));
+    y.y = __fadd_rn(__fmul_rn(v.y, c.x), __fmul_rn(v.x, sn.x));
+    y.z = __fsub_rn(__fmul_rn(v.z, c.y), __fmul_rn(v.w, sn.y));
+    y.w = __fadd_rn(__fmul_rn(v.w, c.y), __fmul_rn(v.z, sn.y));
+    *reinterpret_cast<float4*>(row + e) = y;
+    if (e >= qd) *reinterpret_cast<float4*>(krow + (e - qd)) = y;
+  }
+  for (int e = threadIdx.x * 4; e < kvd; e += blockDim.x * 4)
+    *reinterpret_cast<float4*>(vrow + e) = mri::ld_act(reinterpret_cast<const float4*>(row + qd + kvd + e));
+}
+
 __global__ void rope_kv_kernel(float* __restrict__ qkv, int ld, int n_heads, int n_kv, int hd,
                                const float* __restrict__ cos_t, const float* __restrict__ sin_t,
                                int pos0, const int* __restrict__ pos_dev, float* __restrict__ kc,
@@ -818,9 +856,14 @@ int run_blocks(mri_llama* m, size_t rows, int pos0, bool decode_dev) {
         return rc;
     } else {
       if (int rc = proj(m, m->x, rows, m->wqkv[l], m->qkv, m->attn_norm + l * c.dim)) return rc;
-      LL_TRY(pdl_launch(rope_kv_kernel, dim3(static_cast<unsigned>(rows), c.n_heads + c.n_kv_heads),
-                        dim3(64), st, m->qkv, m->qkv_w, c.n_heads, c.n_kv_heads, m->hd, m->rope_cos,
-                        m->rope_sin, pos0, decode_dev ? m->d_pos : nullptr, kc, vc));
+      if (!decode_dev && m->hd % 4 == 0 && m->qkv_w % 4 == 0) {
+        LL_TRY(pdl_launch(rope_kv_rows_kernel, dim3(static_cast<unsigned>(rows)), dim3(256), st, m->qkv,
+                          m->qkv_w, c.n_heads, c.n_kv_heads, m->hd, m->rope_cos, m->rope_sin, pos0, kc, vc));
+      } else {
+        LL_TRY(pdl_launch(rope_kv_kernel, dim3(static_cast<unsigned>(rows), c.n_heads + c.n_kv_heads),
+                          dim3(64), st, m->qkv, m->qkv_w, c.n_heads, c.n_kv_heads, m->hd, m->rope_cos,
+                          m->rope_sin, pos0, decode_dev ? m->d_pos : nullptr, kc, vc));
+      }
     }
     if (decode_dev) {
       LL_TRY(pdl_launch(attn_decode_kernel, dim3(c.n_heads, m->max_splits), dim3(128), st, m->qkv,

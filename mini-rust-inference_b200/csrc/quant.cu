@@ -222,6 +222,28 @@ __device__ __forceinline__ float xform(const float* __restrict__ x, size_t k, si
   return norm_w ? __fmul_rn(__ldg(norm_w + k), __fmul_rn(v, inv_r)) : v;
 }
 
+// Four transformed elements k..k+3 of row r (K % 4 == 0, 16-byte aligned x
+// and norm_w): the same arithmetic as xform, element by element.
+__device__ __forceinline__ float4 xform4(const float* __restrict__ x, size_t k, size_t K, int r,
+                                         const float* __restrict__ norm_w, float inv_r, int swiglu) {
+  if (swiglu) {
+    const float* row = x + static_cast<size_t>(r) * 2 * K + 2 * k;
+    const float4 a = ld_act(reinterpret_cast<const float4*>(row));
+    const float4 b = ld_act(reinterpret_cast<const float4*>(row + 4));
+    return make_float4(__fmul_rn(__fdiv_rn(a.x, __fadd_rn(1.0f, expf(-a.x))), a.y),
+                       __fmul_rn(__fdiv_rn(a.z, __fadd_rn(1.0f, expf(-a.z))), a.w),
+                       __fmul_rn(__fdiv_rn(b.x, __fadd_rn(1.0f, expf(-b.x))), b.y),
+                       __fmul_rn(__fdiv_rn(b.z, __fadd_rn(1.0f, expf(-b.z))), b.w));
+  }
+  float4 v = ld_act(reinterpret_cast<const float4*>(x + static_cast<size_t>(r) * K + k));
+  if (norm_w) {
+    const float4 w = __ldg(reinterpret_cast<const float4*>(norm_w + k));
+    v = make_float4(__fmul_rn(w.x, __fmul_rn(v.x, inv_r)), __fmul_rn(w.y, __fmul_rn(v.y, inv_r)),
+                    __fmul_rn(w.z, __fmul_rn(v.z, inv_r)), __fmul_rn(w.w, __fmul_rn(v.w, inv_r)));
+  }
+  return v;
+}
+
 __global__ void __launch_bounds__(kQThreads) row_stats_kernel(const float* __restrict__ x, size_t K,
                                                               const float* __restrict__ norm_w,
                                                               float eps, int swiglu,
@@ -232,8 +254,28 @@ __global__ void __launch_bounds__(kQThreads) row_stats_kernel(const float* __res
   __shared__ float red[kQThreads / 32];
   __shared__ float inv_s;
   float inv_r = 1.0f;
+  // float4 loads, four in flight per thread, when rows allow it.
+  const bool vec = K % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+                   (!norm_w || (reinterpret_cast<uintptr_t>(norm_w) & 15) == 0);
   if (norm_w) {
     float ss = 0.0f;
+    if (vec) {
+      const float4* row = reinterpret_cast<const float4*>(x + static_cast<size_t>(r) * K);
+      const size_t k4 = K / 4;
+      for (size_t i0 = threadIdx.x; i0 < k4; i0 += 4 * kQThreads) {
+        float4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          v[u] = i0 + u * kQThreads < k4 ? ld_act(row + i0 + u * kQThreads) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          ss = __fmaf_rn(v[u].x, v[u].x, ss);
+          ss = __fmaf_rn(v[u].y, v[u].y, ss);
+          ss = __fmaf_rn(v[u].z, v[u].z, ss);
+          ss = __fmaf_rn(v[u].w, v[u].w, ss);
+        }
+      }
+    } else
     for (size_t k = threadIdx.x; k < K; k += kQThreads) {
       const float v = ld_act(x + static_cast<size_t>(r) * K + k);
       ss = __fmaf_rn(v, v, ss);
@@ -251,7 +293,21 @@ __global__ void __launch_bounds__(kQThreads) row_stats_kernel(const float* __res
     inv_r = inv_s;
   }
   float m = 0.0f;
-  for (size_t k = threadIdx.x; k < K; k += kQThreads) m = absmax_acc(m, xform(x, k, K, r, norm_w, inv_r, swiglu));
+  if (vec) {
+    const size_t k4 = K / 4;
+    for (size_t i0 = threadIdx.x; i0 < k4; i0 += 4 * kQThreads) {
+      float4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        v[u] = i0 + u * kQThreads < k4 ? xform4(x, (i0 + u * kQThreads) * 4, K, r, norm_w, inv_r, swiglu)
+                                       : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        m = absmax_acc(absmax_acc(absmax_acc(absmax_acc(m, v[u].x), v[u].y), v[u].z), v[u].w);
+    }
+  } else {
+    for (size_t k = threadIdx.x; k < K; k += kQThreads) m = absmax_acc(m, xform(x, k, K, r, norm_w, inv_r, swiglu));
+  }
   m = warp_max(m);
   __syncthreads();
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;

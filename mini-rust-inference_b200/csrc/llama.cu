@@ -380,7 +380,7 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(const float* __restri
 }
 
 // Prefill attention on the tensor cores (flash-attention style): block (h, qb)
-// handles queries [qb*64, qb*64+64) of head h, a warp 16 of them.  Per tile of
+// handles queries [qb*128, qb*128+128) of head h, a warp 16 of them.  Per tile of
 // 64 cached keys, S = Q K^T and O += P V run on mma.sync m16n8k16 with f16
 // operands and f32 accumulators: Q is held as A fragments, K and V^T are
 // converted into shared memory (rows padded so a fragment load hits 32
@@ -393,7 +393,8 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(const float* __restri
 // and the online softmax (running max, sum) are f32, per row over the 4
 // threads that hold it.  q, k and v must lie within the f16 range.  HD = head
 // dim (64 or 128).
-constexpr int kFaQ = 64;   // queries per block
+constexpr int kFaQ = 128;  // queries per block (a warp per 16): each K/V tile is converted once per 128 queries
+constexpr int kFaThreads = 2 * kFaQ;
 constexpr int kFaKT = 64;  // keys per tile
 
 __device__ __forceinline__ uint32_t half2_bits(float lo, float hi) {
@@ -418,7 +419,7 @@ __device__ __forceinline__ void mma_f16_m16n8k16(float d[4], const uint32_t a[4]
 }
 
 template <int HD>
-__global__ void __launch_bounds__(128) attn_prefill_tc_kernel(const float* __restrict__ qkv, int ld,
+__global__ void __launch_bounds__(kFaThreads) attn_prefill_tc_kernel(const float* __restrict__ qkv, int ld,
                                                               int n_heads, int n_kv, int M, int start,
                                                               const float* __restrict__ kc,
                                                               const float* __restrict__ vc, float scale,
@@ -882,11 +883,11 @@ int run_blocks(mri_llama* m, size_t rows, int pos0, bool decode_dev) {
         fa_attr_set[dv] = true;
       }
       if (m->hd == 64)
-        attn_prefill_tc_kernel<64><<<grid, 128, smem, st>>>(m->qkv, m->qkv_w, c.n_heads, c.n_kv_heads,
+        attn_prefill_tc_kernel<64><<<grid, kFaThreads, smem, st>>>(m->qkv, m->qkv_w, c.n_heads, c.n_kv_heads,
                                                             static_cast<int>(rows), pos0, kc, vc, scale,
                                                             m->attn, m->qd);
       else
-        attn_prefill_tc_kernel<128><<<grid, 128, smem, st>>>(m->qkv, m->qkv_w, c.n_heads, c.n_kv_heads,
+        attn_prefill_tc_kernel<128><<<grid, kFaThreads, smem, st>>>(m->qkv, m->qkv_w, c.n_heads, c.n_kv_heads,
                                                              static_cast<int>(rows), pos0, kc, vc, scale,
                                                              m->attn, m->qd);
     } else {

@@ -491,6 +491,10 @@ __global__ void __launch_bounds__(kFaThreads) attn_prefill_tc_kernel(const float
       }
     }
     __syncthreads();
+    // A tile every key of which lies past this warp's last query is masked
+    // for all of its rows: skip its MMAs (warp-uniform; the loads above are
+    // shared by the block and stay).
+    if (kt > start + q0 + warp * 16 + 15) continue;
     // S = Q K^T for this warp's 16 queries x 64 keys (8 n tiles of 8 keys).
     float sc[kFaKT / 8][4];
 #pragma unroll

@@ -36,7 +36,8 @@
 
 namespace {
 
-constexpr int kAttnChunk = 64;   // keys per split in decode attention
+constexpr int kAttnRounds = 1;   // rounds of 8 keys per warp in decode attention
+constexpr int kAttnChunk = 4 * 8 * kAttnRounds;  // keys per split (4 warps)
 constexpr int kMergeChunk = 256;  // splits whose merge weights sit in shared memory at once
 constexpr int kPrefillQ = 16;    // queries per block in prefill attention
 constexpr int kPrefillKT = 64;   // keys per shared-memory tile in prefill attention
@@ -139,9 +140,9 @@ __global__ void rope_kv_kernel(float* __restrict__ qkv, int ld, int n_heads, int
 }
 
 // Decode attention, split over keys (attention/cached.rs:141-190 with
-// gqa.rs:217-237): block (h, s) handles keys [s*64, min(s*64+64, pos+1)).
-// Warp w takes 16 of them; a lane owns 4 head dimensions (hd % 4 == 0,
-// hd <= 128), loads the 16 keys' and values' float4 before using any,
+// gqa.rs:217-237): block (h, s) handles keys [s*C, min(s*C+C, pos+1)) for
+// C = kAttnChunk (32).  Warp w takes 8 of them; a lane owns 4 head dimensions
+// (hd % 4 == 0, hd <= 128), loads its keys' and values' float4 before using any,
 // reduces each score over the warp with shuffles and keeps an online
 // softmax (running max, exp-sum, weighted V sum) — no block-wide barrier until
 // the 4 warps' partials are combined.  Each block writes its partial; the last
@@ -179,18 +180,18 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const float* __restric
   float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
   // All of the warp's keys and values are loaded before any is used (one
   // memory latency per split), then scored in key order.
-  float4 kk[2 * kRound], vv[2 * kRound];
+  float4 kk[kAttnRounds * kRound], vv[kAttnRounds * kRound];
 #pragma unroll
-  for (int i = 0; i < 2 * kRound; ++i) {
-    const int key = warp * 2 * kRound + i;
+  for (int i = 0; i < kAttnRounds * kRound; ++i) {
+    const int key = warp * kAttnRounds * kRound + i;
     const bool ok = dim_ok && key < nkeys;
     const size_t row = static_cast<size_t>(j0 + key) * kvd + base;
     kk[i] = ok ? mri::ld_act(reinterpret_cast<const float4*>(kc + row)) : make_float4(0.f, 0.f, 0.f, 0.f);
     vv[i] = ok ? mri::ld_act(reinterpret_cast<const float4*>(vc + row)) : make_float4(0.f, 0.f, 0.f, 0.f);
   }
 #pragma unroll
-  for (int r = 0; r < 2; ++r) {
-    const int k0 = warp * 2 * kRound + r * kRound;  // first key of this round, within the chunk
+  for (int r = 0; r < kAttnRounds; ++r) {
+    const int k0 = warp * kAttnRounds * kRound + r * kRound;  // first key of this round, within the chunk
 #pragma unroll
     for (int i = 0; i < kRound; ++i) {
       if (k0 + i >= nkeys) break;  // warp-uniform

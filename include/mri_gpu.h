@@ -107,6 +107,32 @@ MRI_API int mri_q4_0_upload(mri_ctx* ctx, const uint8_t* bytes, size_t len, size
                     size_t k, mri_q4_0_matrix** out);
 MRI_API int mri_q4_0_free(mri_q4_0_matrix* w);
 
+/* ── GGUF tensor data to device weights ───────────────────────────────────── */
+/* ggml storage types TensorExtractor::extract accepts (gguf/dtype.rs:30-43,
+ * extract.rs:728-732). */
+#define MRI_GGML_F32 0
+#define MRI_GGML_F16 1
+#define MRI_GGML_Q4_0 2
+#define MRI_GGML_Q8_0 8
+/* quantize_tensor(&extractor.extract(name)) (forward_int8.rs:52-62 with
+ * extract.rs:719-737): `bytes` is the tensor's raw GGUF data in host memory
+ * (e.g. a slice of the mapped file), [n_out, k_in] its row-major shape (GGUF
+ * dims reversed, tensor_info.rs:145-147).  The bytes are copied to the device
+ * and dequantized and requantized per output row there; the result is
+ * bit-identical to dequantize-then-quantize_per_channel on the host.
+ * Unsupported type -> MRI_ERR_INVALID_ARGUMENT (GgufError::TypeMismatch);
+ * n_out*k_in not a multiple of 32 for Q8_0/Q4_0, or len not the type's byte
+ * count -> MRI_ERR_SHAPE_MISMATCH (GgufError::ShapeMismatch).  Synchronous. */
+MRI_API int mri_qmatrix_from_gguf(mri_ctx* ctx, int ggml_type, const uint8_t* bytes, size_t len,
+                                  size_t n_out, size_t k_in, mri_qmatrix** out);
+/* Copies a matrix's rows and scales back to host memory (the data / scales
+ * fields of QuantizedMatrix, per_channel.rs:29-40).  Synchronous. */
+MRI_API int mri_qmatrix_download(const mri_qmatrix* w, int8_t* data, float* scales);
+/* TensorExtractor::extract (extract.rs:719-737) into device memory: numel f32
+ * values at out_dev.  Same checks as mri_qmatrix_from_gguf.  Synchronous. */
+MRI_API int mri_gguf_dequant(mri_ctx* ctx, int ggml_type, const uint8_t* bytes, size_t len,
+                             size_t numel, float* out_dev);
+
 /* ── activation quantizer (quantize_symmetric, symmetric.rs:42-57) ────────── */
 /* x_dev [m,k] f32 -> q_dev [m,k] i8 and scale_dev (1 value for PER_TENSOR,
  * m values for PER_ROW). */
@@ -182,6 +208,32 @@ MRI_API int mri_llama_set_layer(mri_llama* m, uint32_t layer, const int8_t* wq, 
                                 const float* sgate, const int8_t* wup, const float* sup,
                                 const int8_t* wdown, const float* sdown);
 MRI_API int mri_llama_set_output(mri_llama* m, const int8_t* w, const float* s); /* [vocab, dim] */
+/* Weights from a GGUF file (LlamaModelInt8::from_loader, forward_int8.rs:461-507):
+ * one tensor's raw GGUF data in host memory, stored as MRI_GGML_F32 / F16 /
+ * Q8_0 / Q4_0, row-major shape [rows, cols] (a 1-D tensor of d values is
+ * [1, d]).  Projections and the output matrix are dequantized and requantized
+ * per output row on the device (quantize_tensor of extract, bit-identical to
+ * the host path); the embedding and the norm vectors are dequantized to f32
+ * on the device.  Roles follow weight_name / global_weight_name
+ * (model/llama/weights.rs:62-104); `layer` is ignored for the three global
+ * tensors.  A shape other than the configuration's -> MRI_ERR_SHAPE_MISMATCH;
+ * type and byte-length errors as mri_qmatrix_from_gguf.  Synchronous. */
+enum {
+  MRI_TENSOR_TOKEN_EMBD = 0, /* token_embd.weight  [vocab, dim] */
+  MRI_TENSOR_OUTPUT_NORM = 1, /* output_norm.weight [dim] */
+  MRI_TENSOR_OUTPUT = 2,     /* output.weight      [vocab, dim] */
+  MRI_TENSOR_ATTN_Q = 3,     /* blk.L.attn_q.weight      [n_heads*hd, dim] */
+  MRI_TENSOR_ATTN_K = 4,     /* blk.L.attn_k.weight      [n_kv*hd, dim] */
+  MRI_TENSOR_ATTN_V = 5,     /* blk.L.attn_v.weight      [n_kv*hd, dim] */
+  MRI_TENSOR_ATTN_OUTPUT = 6, /* blk.L.attn_output.weight [dim, n_heads*hd] */
+  MRI_TENSOR_ATTN_NORM = 7,  /* blk.L.attn_norm.weight   [dim] */
+  MRI_TENSOR_FFN_GATE = 8,   /* blk.L.ffn_gate.weight    [ffn, dim] */
+  MRI_TENSOR_FFN_UP = 9,     /* blk.L.ffn_up.weight      [ffn, dim] */
+  MRI_TENSOR_FFN_DOWN = 10,  /* blk.L.ffn_down.weight    [dim, ffn] */
+  MRI_TENSOR_FFN_NORM = 11   /* blk.L.ffn_norm.weight    [dim] */
+};
+MRI_API int mri_llama_load_tensor(mri_llama* m, int role, uint32_t layer, int ggml_type,
+                                  const uint8_t* bytes, size_t len, size_t rows, size_t cols);
 /* Synthetic weights generated on the device (benchmarking only). */
 MRI_API int mri_llama_init_random(mri_llama* m, uint64_t seed);
 /* LlamaModelInt8::forward (forward_int8.rs:516-529): logits [n, vocab]; also

@@ -38,7 +38,7 @@ __all__ = [
     "matmul_int8_from_f32", "matmul_q8_0_direct", "matmul_q4_0_dequant", "formats",
     "LlamaConfig", "LlamaModelInt8",
     "comm_available", "shard_rows", "Communicator", "shard_quantized_matrix",
-    "matmul_int8_from_f32_sharded",
+    "matmul_int8_from_f32_sharded", "gguf_dequant",
 ]
 
 
@@ -209,6 +209,27 @@ class QuantizedMatrix:
         except Exception:  # noqa: BLE001
             pass
 
+    @classmethod
+    def from_gguf(cls, ggml_type, raw, n_out, k_in, ctx=None, keep_host=True):
+        """quantize_tensor(&extractor.extract(name)) (forward_int8.rs:52-62,
+        gguf/extract.rs:719-737) from a tensor's raw GGUF bytes: dequantized and
+        requantized per row on the device, bit-identical to the host path."""
+        self = cls.__new__(cls)
+        self.ctx = ctx or default_context()
+        raw = np.frombuffer(raw, dtype=np.uint8) if not isinstance(raw, np.ndarray) else raw
+        raw = np.ascontiguousarray(raw, dtype=np.uint8).reshape(-1)
+        h = ctypes.c_void_p()
+        self.handle = None
+        _check(self.ctx._lib.mri_qmatrix_from_gguf(self.ctx.handle, int(ggml_type), _vp(raw), raw.size,
+                                                   n_out, k_in, ctypes.byref(h)))
+        self.handle = h
+        self.n_out, self.k_in, self.row_range = n_out, k_in, (0, n_out)
+        if keep_host:
+            self.data = np.empty(n_out * k_in, np.int8)
+            self.scales = np.empty(n_out, np.float32)
+            _check(self.ctx._lib.mri_qmatrix_download(h, _vp(self.data), _vp(self.scales)))
+        return self
+
     def row(self, n):
         """per_channel.rs:45-48"""
         return self.data[n * self.k_in:(n + 1) * self.k_in]
@@ -293,6 +314,24 @@ class Q4_0Matrix:
 
 
 # ── quantizers ────────────────────────────────────────────────────────────────
+
+def gguf_dequant(ggml_type, raw, numel, out=None, ctx=None):
+    """TensorExtractor::extract (gguf/extract.rs:719-737) of a tensor's raw GGUF
+    bytes, dequantized on the device: `out` (a CUDA float32 tensor of numel
+    values) is filled, or a host float32 array is returned."""
+    ctx = ctx or default_context()
+    raw = np.ascontiguousarray(np.frombuffer(raw, dtype=np.uint8) if not isinstance(raw, np.ndarray)
+                               else raw, dtype=np.uint8).reshape(-1)
+    if out is not None:
+        _check(ctx._lib.mri_gguf_dequant(ctx.handle, int(ggml_type), _vp(raw), raw.size, numel, _vp(out)))
+        ctx.synchronize()
+        return out
+    import torch
+    dev = torch.empty(max(numel, 1), dtype=torch.float32, device=f"cuda:{ctx.device}")
+    _check(ctx._lib.mri_gguf_dequant(ctx.handle, int(ggml_type), _vp(raw), raw.size, numel, _vp(dev)))
+    ctx.synchronize()
+    return dev[:numel].cpu().numpy()
+
 
 def _host_quantize(values, m, k, granularity, ctx):
     ctx = ctx or default_context()
@@ -608,6 +647,42 @@ class LlamaModelInt8:
         od, os_ = i8(w["output"][0]), f32(w["output"][1])
         _check_model(lib.mri_llama_set_output(m.handle, _vp(od), _vp(os_)), lib)
         m.set_rope(*(rope or (None, None)))
+        return m
+
+    @classmethod
+    def from_gguf(cls, path, ctx=None, max_seq=None):
+        """LlamaModelInt8::from_loader (forward_int8.rs:461-507): configuration
+        from the file's metadata (LlamaConfig::from_metadata), every tensor's
+        raw bytes from the mapped file to the device, projections requantized
+        per channel there, embedding and norms dequantized to f32 there.
+        `max_seq` (default: llama.context_length) sizes the KV cache and the
+        RoPE table.  Raises gguf.MissingMetadataKey / InvalidConfig /
+        KeyNotFound / TensorDataUnavailable, or the ABI's errors."""
+        from . import gguf
+        g = path if isinstance(path, gguf.GgufFile) else gguf.GgufFile(path)
+        c = gguf.llama_config(g.metadata)
+        cfg = LlamaConfig(c["block_count"], c["embedding_length"], c["n_heads"], c["feed_forward_length"],
+                          c["vocab_size"], int(max_seq or c["context_length"]), n_kv_heads=c["n_kv_heads"],
+                          rope_base=c["rope_freq_base"], rms_eps=c["rms_norm_eps"])
+        m = cls(cfg, ctx)
+        lib = m._lib
+
+        def load(name, role, layer):
+            info = g.tensor(name)
+            raw = g.tensor_data(name)
+            if raw is None:
+                raise gguf.TensorDataUnavailable(name)
+            shape = info.shape_row_major()
+            rows, cols = (1, shape[0]) if len(shape) == 1 else (int(np.prod(shape[:-1])), shape[-1])
+            _check_model(lib.mri_llama_load_tensor(m.handle, role, layer, info.dtype, _vp(raw), raw.size,
+                                                   rows, cols), lib)
+
+        for name, role in gguf.GLOBAL_TENSORS:
+            load(name, role, 0)
+        for layer in range(cfg.n_layers):
+            for suffix, role in gguf.LAYER_TENSORS:
+                load(gguf.weight_name(layer, suffix), role, layer)
+        m.set_rope()
         return m
 
     @classmethod

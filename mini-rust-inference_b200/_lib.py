@@ -67,6 +67,9 @@ SIGNATURES = {
     "mri_comm_wait": (_I, [_P]),
     "mri_shard_rows": (_I, [_SZ, _I, _I, ctypes.POINTER(_SZ), ctypes.POINTER(_SZ)]),
     "mri_sharded_matmul_int8_from_f32": (_I, [_P, _P, _SZ, _SZ, _P, _SZ, _P]),
+    "mri_qmatrix_from_gguf": (_I, [_P, _I, _P, _SZ, _SZ, _SZ, _PP]),
+    "mri_qmatrix_download": (_I, [_P, _P, _P]),
+    "mri_gguf_dequant": (_I, [_P, _I, _P, _SZ, _SZ, _P]),
     "mri_llama_create": (_I, [_P, _P, _PP]),
     "mri_llama_free": (_I, [_P]),
     "mri_llama_last_error": (ctypes.c_char_p, []),
@@ -75,6 +78,7 @@ SIGNATURES = {
     "mri_llama_set_norms": (_I, [_P, _P, _P, _P]),
     "mri_llama_set_layer": (_I, [_P, ctypes.c_uint32] + [_P] * 14),
     "mri_llama_set_output": (_I, [_P, _P, _P]),
+    "mri_llama_load_tensor": (_I, [_P, _I, ctypes.c_uint32, _I, _P, _SZ, _SZ, _SZ]),
     "mri_llama_init_random": (_I, [_P, ctypes.c_uint64]),
     "mri_llama_forward": (_I, [_P, _P, _SZ, _P]),
     "mri_llama_forward_decode": (_I, [_P, ctypes.c_uint32, _SZ, _P]),

@@ -529,6 +529,69 @@ int mri_qmatrix_dims(const mri_qmatrix* w, size_t* n_out, size_t* k_in) {
   return MRI_OK;
 }
 
+int mri_qmatrix_from_gguf(mri_ctx* ctx, int ggml_type, const uint8_t* bytes, size_t len,
+                          size_t n_out, size_t k_in, mri_qmatrix** out) {
+  if (int rc = enter(ctx)) return rc;
+  if (!out) return fail(MRI_ERR_INVALID_ARGUMENT, "null output pointer");
+  std::string err;
+  if (int rc = mri::gguf_check(ggml_type, len, n_out * k_in, &err)) return fail(rc, "%s", err.c_str());
+  mri_qmatrix* w = new mri_qmatrix{ctx->device, nullptr, nullptr, n_out, k_in, true};
+  // Same zeroed slack after the rows as upload_bytes leaves.
+  int rc = MRI_OK;
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, n_out * k_in + kWeightPad);
+  if (e == cudaSuccess) {
+    w->data = static_cast<int8_t*>(p);
+    e = cudaMemsetAsync(p, 0, n_out * k_in + kWeightPad, ctx->stream);
+  }
+  if (e == cudaSuccess) e = cudaMalloc(&p, n_out * sizeof(float) + kWeightPad);
+  if (e == cudaSuccess) w->scales = static_cast<float*>(p);
+  if (e != cudaSuccess) rc = cuda_fail(e, "weight allocation");
+  if (rc == MRI_OK) {
+    mri::GgufDst d;
+    d.q = w->data;
+    d.q_stride = k_in;
+    d.scales = w->scales;
+    rc = mri::gguf_to_device(ctx->stream, ggml_type, bytes, len, n_out, k_in, d, &err);
+    if (rc != MRI_OK) fail(rc, "%s", err.c_str());
+  }
+  if (rc != MRI_OK) {
+    if (w->data) cudaFree(w->data);
+    if (w->scales) cudaFree(w->scales);
+    delete w;
+    return rc;
+  }
+  *out = w;
+  return MRI_OK;
+}
+
+int mri_qmatrix_download(const mri_qmatrix* w, int8_t* data, float* scales) {
+  if (!w) return fail(MRI_ERR_INVALID_ARGUMENT, "null matrix");
+  if ((!data && w->n_out * w->k_in) || (!scales && w->n_out))
+    return fail(MRI_ERR_INVALID_ARGUMENT, "null output pointer");
+  if (int rc = use_device(w->device)) return rc;
+  if (w->n_out * w->k_in)
+    MRI_CUDA_TRY(cudaMemcpy(data, w->data, w->n_out * w->k_in, cudaMemcpyDeviceToHost));
+  if (w->n_out) MRI_CUDA_TRY(cudaMemcpy(scales, w->scales, w->n_out * 4, cudaMemcpyDeviceToHost));
+  return MRI_OK;
+}
+
+int mri_gguf_dequant(mri_ctx* ctx, int ggml_type, const uint8_t* bytes, size_t len, size_t numel,
+                     float* out_dev) {
+  if (int rc = enter(ctx)) return rc;
+  if (!out_dev && numel) return fail(MRI_ERR_INVALID_ARGUMENT, "null output pointer");
+  mri::GgufDst d;
+  d.f32 = out_dev;
+  std::string err;
+  // Viewed as rows of one block (32 values) so that the copy goes in steps.
+  const size_t cols = numel % 32 == 0 && numel ? 32 : numel;
+  const size_t rows = cols ? numel / cols : 0;
+  if (int rc = mri::gguf_check(ggml_type, len, numel, &err)) return fail(rc, "%s", err.c_str());
+  if (int rc = mri::gguf_to_device(ctx->stream, ggml_type, bytes, len, rows, cols, d, &err))
+    return fail(rc, "%s", err.c_str());
+  return MRI_OK;
+}
+
 int mri_q8_0_upload(mri_ctx* ctx, const uint8_t* bytes, size_t len, size_t n_out, size_t k_in,
                     mri_q8_0_matrix** out) {
   if (int rc = enter(ctx)) return rc;

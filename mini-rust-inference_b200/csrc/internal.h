@@ -6,6 +6,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <string>
+
 struct mri_ctx;
 struct mri_qmatrix;
 
@@ -218,6 +220,28 @@ cudaError_t launch_gemm_i8_tc(const DeviceInfo& dev, cudaStream_t st, const int8
                               const float* w_scales, size_t M, size_t N, size_t K, float* out,
                               int32_t* acc_out, int* status, LaunchStats* ls,
                               const float* residual = nullptr);
+
+// ── GGUF tensor data to device weights (load.cu) ────────────────────────────
+// Destination of one converted tensor: either per-channel INT8 rows (row r ->
+// q + r * q_stride, its scale -> scales[r * s_stride]) or, when f32 is set,
+// the dequantized values (element i -> f32[i]).
+struct GgufDst {
+  int8_t* q = nullptr;
+  size_t q_stride = 0;
+  float* scales = nullptr;
+  size_t s_stride = 1;
+  float* f32 = nullptr;
+};
+// Bytes of `numel` elements stored as ggml type `type` (0 for other types).
+size_t gguf_type_bytes(int type, size_t numel);
+// TensorExtractor's type and length checks; status code as the C ABI and the
+// reason in *err.
+int gguf_check(int type, size_t len, size_t numel, std::string* err);
+// Copies the host bytes of a [rows, cols] GGUF tensor to the device in steps
+// of whole rows and converts them into `d` on stream `st`; returns after the
+// last step has completed.
+int gguf_to_device(cudaStream_t st, int type, const uint8_t* bytes, size_t len, size_t rows,
+                   size_t cols, const GgufDst& d, std::string* err);
 
 }  // namespace mri
 

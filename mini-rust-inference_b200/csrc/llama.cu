@@ -1166,6 +1166,73 @@ int mri_llama_set_output(mri_llama* m, const int8_t* w, const float* s) {
   return put_rows(m->wout, 0, w, s, m->cfg.vocab);
 }
 
+int mri_llama_load_tensor(mri_llama* m, int role, uint32_t layer, int ggml_type,
+                          const uint8_t* bytes, size_t len, size_t rows, size_t cols) {
+  if (!m) return fail(MRI_ERR_INVALID_ARGUMENT, "null model");
+  const auto& c = m->cfg;
+  const bool global = role == MRI_TENSOR_TOKEN_EMBD || role == MRI_TENSOR_OUTPUT_NORM ||
+                      role == MRI_TENSOR_OUTPUT;
+  if (!global && layer >= c.n_layers) return fail(MRI_ERR_INVALID_SHAPE, "layer %u out of range", layer);
+  const size_t D = c.dim, F = c.ffn_dim, V = c.vocab, QD = m->qd, KVD = m->kvd;
+  // Expected [rows, cols] and destination of each role (the fused Q/K/V and
+  // gate/up layouts of mri_llama_set_layer).
+  size_t er = 0, ec = D;
+  mri::GgufDst d;
+  switch (role) {
+    case MRI_TENSOR_TOKEN_EMBD: er = V; d.f32 = m->embd; break;
+    case MRI_TENSOR_OUTPUT_NORM: er = 1; d.f32 = m->out_norm; break;
+    case MRI_TENSOR_ATTN_NORM: er = 1; d.f32 = m->attn_norm + layer * D; break;
+    case MRI_TENSOR_FFN_NORM: er = 1; d.f32 = m->ffn_norm + layer * D; break;
+    case MRI_TENSOR_OUTPUT:
+      er = V;
+      d.q = m->wout.data;
+      d.scales = m->wout.scales;
+      break;
+    case MRI_TENSOR_ATTN_Q:
+    case MRI_TENSOR_ATTN_K:
+    case MRI_TENSOR_ATTN_V: {
+      const size_t row0 = role == MRI_TENSOR_ATTN_Q ? 0 : role == MRI_TENSOR_ATTN_K ? QD : QD + KVD;
+      er = role == MRI_TENSOR_ATTN_Q ? QD : KVD;
+      d.q = m->wqkv[layer].data + row0 * D;
+      d.scales = m->wqkv[layer].scales + row0;
+      break;
+    }
+    case MRI_TENSOR_ATTN_OUTPUT:
+      er = D;
+      ec = QD;
+      d.q = m->wo[layer].data;
+      d.scales = m->wo[layer].scales;
+      break;
+    case MRI_TENSOR_FFN_GATE:
+    case MRI_TENSOR_FFN_UP: {
+      // Row 2i = gate i, row 2i+1 = up i.
+      const size_t odd = role == MRI_TENSOR_FFN_UP ? 1 : 0;
+      er = F;
+      d.q = m->wgu[layer].data + odd * D;
+      d.q_stride = 2 * D;
+      d.scales = m->wgu[layer].scales + odd;
+      d.s_stride = 2;
+      break;
+    }
+    case MRI_TENSOR_FFN_DOWN:
+      er = D;
+      ec = F;
+      d.q = m->wdown[layer].data;
+      d.scales = m->wdown[layer].scales;
+      break;
+    default: return fail(MRI_ERR_INVALID_ARGUMENT, "unknown tensor role %d", role);
+  }
+  if (rows != er || cols != ec)
+    return fail(MRI_ERR_SHAPE_MISMATCH, "tensor role %d: expected [%zu, %zu], got [%zu, %zu]", role,
+                er, ec, rows, cols);
+  if (d.q && !d.q_stride) d.q_stride = ec;
+  LL_TRY(cudaSetDevice(m->ctx->device));
+  std::string err;
+  if (int rc = mri::gguf_to_device(m->ctx->stream, ggml_type, bytes, len, rows, cols, d, &err))
+    return fail(rc, "%s", err.c_str());
+  return MRI_OK;
+}
+
 int mri_llama_init_random(mri_llama* m, uint64_t seed) {
   if (!m) return fail(MRI_ERR_INVALID_ARGUMENT, "null model");
   const auto& c = m->cfg;

@@ -237,6 +237,39 @@ def dequantize_q4_0(data):
     return out
 
 
+_F16 = None
+
+
+def _f16_table():
+    """f16_to_f32 (quantization.rs:416-461) of all 65536 bit patterns."""
+    global _F16
+    if _F16 is None:
+        _F16 = np.array([f16_to_f32(h) for h in range(65536)], dtype=np.float32)
+    return _F16
+
+
+# gguf/extract.rs:719-737: F32 / F16 / Q8_0 / Q4_0 tensor bytes -> f32 values
+# (extract_f32_from_bytes :772-815, f16_to_f32 per element, dequantize_q8_0 /
+# dequantize_q4_0, dequant.rs:103-133 / 471-506).
+def extract(ggml_type, raw):
+    d = _u8(raw)
+    if ggml_type == 0:
+        return d.view(np.float32).copy()
+    if ggml_type == 1:
+        return _f16_table()[d.view(np.uint16)]
+    if ggml_type == 8:
+        return dequantize_q8_0(d)
+    if ggml_type == 2:
+        return dequantize_q4_0(d)
+    raise OracleError("TypeMismatch")
+
+
+# forward_int8.rs:52-62 (quantize_tensor) over extract(): what from_loader
+# keeps of each projection.
+def quantize_tensor(ggml_type, raw, n_out, k_in):
+    return quantize_per_channel(extract(ggml_type, raw), n_out, k_in)
+
+
 def q8_0_check_raw(data_len, n_out, k_in):
     return lib().oref_q8_0_check_raw(data_len, n_out, k_in)
 

@@ -53,7 +53,10 @@ constexpr int kTcThreads = 32 * (2 + kEpiWarps);
 template <int BN>
 constexpr int acc_stride() { return BN <= 128 ? 128 : 256; }
 
-template <int BN, int kStages>
+// Output staging of the store epilogue: a 32 x 32 f32 block per epilogue warp.
+constexpr size_t kStgBytes = kEpiWarps * 32 * 32 * 4;
+
+template <int BN, int kStages, int kBufs = 2>
 struct TcLayout {
   static constexpr size_t a_bytes = BM * BK;
   static constexpr size_t b_bytes = BN * BK;
@@ -61,7 +64,10 @@ struct TcLayout {
   // Weight scales of the tile, one buffer per accumulator buffer.
   static constexpr size_t epi = kStages * stage_bytes;
   static constexpr size_t epi_bytes = 2 * 256 * 4;
-  static constexpr size_t bars = epi + epi_bytes;
+  // With one tile per CTA the stage ring is idle once the tile's MMAs are
+  // done, and the epilogue stages its output there; otherwise it has its own.
+  static constexpr size_t stg = kBufs == 1 ? 0 : epi + epi_bytes;
+  static constexpr size_t bars = epi + epi_bytes + (kBufs == 1 ? 0 : kStgBytes);
   // full[S], empty[S], tfull[2], tempty[2], sready[2], mma_done, abort flag + tmem slot
   static constexpr size_t bars_bytes = (2 * kStages + 7) * 8 + 16;
   static constexpr size_t total = bars + bars_bytes + 1024;  // + alignment slack
@@ -151,7 +157,7 @@ __global__ void __launch_bounds__(kTcThreads, kBufs == 1 ? 2 : 1)
                       const float* __restrict__ w_scales, float* out,
                       int32_t* __restrict__ acc_out, int M, int N, int K, int* status,
                       const float* residual) {
-  using L = TcLayout<BN, kStages>;
+  using L = TcLayout<BN, kStages, kBufs>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_addr(smem_raw);
   uint8_t* smem = smem_raw + ((1024 - (raw & 1023)) & 1023);
@@ -301,12 +307,59 @@ __global__ void __launch_bounds__(kTcThreads, kBufs == 1 ? 2 : 1)
       // forward_int8.rs:100-121: x + projected; residual may alias out.
       const float* rrow = residual ? residual + static_cast<size_t>(row) * N : nullptr;
       int32_t* arow = acc_out ? acc_out + static_cast<size_t>(row) * N : nullptr;
+      // This warp's 32 x 32 staging block (16-byte chunks XOR-swizzled by row).
+      float* stg = reinterpret_cast<float*>(smem + L::stg) + q * 32 * 32;
+      const int row0 = m_blk * BM + q * 32;
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t v[32];
         tmem_ld_32cols(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + b * acc_stride<BN>() + c * 32, v);
         const int col0 = n_blk * BN + c * 32;
         const float* sw = s_sw + c * 32;
+        if (vec && !arow && col0 + 32 <= N && row0 + 32 <= M) {
+          // Whole 32 x 32 block in range (warp-uniform): lane = row holds a
+          // row's 32 columns; they go through shared memory so that each
+          // store instruction writes four full 128-byte row segments instead
+          // of 32 rows' 16 bytes.
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float4 w = *reinterpret_cast<const float4*>(sw + 4 * j);
+            float4 o;
+            o.x = rescale(static_cast<int>(v[4 * j]), s_a, w.x);
+            o.y = rescale(static_cast<int>(v[4 * j + 1]), s_a, w.y);
+            o.z = rescale(static_cast<int>(v[4 * j + 2]), s_a, w.z);
+            o.w = rescale(static_cast<int>(v[4 * j + 3]), s_a, w.w);
+            *reinterpret_cast<float4*>(stg + lane * 32 + 4 * (j ^ (lane & 7))) = o;
+          }
+          __syncwarp();
+          const int rs = lane >> 3, jc = lane & 7;
+          float4 o[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int r = 4 * i + rs;
+            o[i] = *reinterpret_cast<const float4*>(stg + r * 32 + 4 * (jc ^ (r & 7)));
+          }
+          __syncwarp();
+          if (residual) {
+            float4 rr[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              rr[i] = ld_act(reinterpret_cast<const float4*>(
+                  residual + static_cast<size_t>(row0 + 4 * i + rs) * N + col0 + 4 * jc));
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              o[i].x = __fadd_rn(rr[i].x, o[i].x);
+              o[i].y = __fadd_rn(rr[i].y, o[i].y);
+              o[i].z = __fadd_rn(rr[i].z, o[i].z);
+              o[i].w = __fadd_rn(rr[i].w, o[i].w);
+            }
+          }
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            *reinterpret_cast<float4*>(out + static_cast<size_t>(row0 + 4 * i + rs) * N + col0 + 4 * jc) =
+                o[i];
+          continue;
+        }
         if (row < M) {
           if (vec && col0 + 32 <= N) {
             float4 r[8];
@@ -441,12 +494,13 @@ cudaError_t launch_bn(const DeviceInfo& dev, cudaStream_t st, const CUtensorMap&
                       const CUtensorMap& tb, const float* act_scale, int per_row,
                       const float* w_scales, size_t M, size_t N, size_t K, float* out,
                       int32_t* acc_out, int* status, const float* residual) {
-  static_assert(TcLayout<BN, kStages>::total <= 232448, "stage ring exceeds the per-CTA shared memory");
+  static_assert(TcLayout<BN, kStages, kBufs>::total <= 232448,
+                "stage ring exceeds the per-CTA shared memory");
   // Two CTAs per SM: both rings plus the 1 KB the runtime reserves per CTA
   // within the SM's 228 KB.
-  static_assert(kBufs == 2 || 2 * (TcLayout<BN, kStages>::total + 1024) <= 233472,
+  static_assert(kBufs == 2 || 2 * (TcLayout<BN, kStages, kBufs>::total + 1024) <= 233472,
                 "two CTAs per SM do not fit");
-  const size_t smem = TcLayout<BN, kStages>::total;
+  const size_t smem = TcLayout<BN, kStages, kBufs>::total;
   cudaError_t e = set_smem_tc(gemm_i8_tc_kernel<BN, kStages, kBufs>, smem, dev.device);
   if (e != cudaSuccess) return e;
   const size_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
@@ -514,9 +568,9 @@ cudaError_t launch_gemm_i8_tc(const DeviceInfo& dev, cudaStream_t st, const int8
   }
   switch (bn) {
     MRI_GEMM_BN_CASE(128, 6)
-    MRI_GEMM_BN_CASE(160, 6)
+    MRI_GEMM_BN_CASE(160, 5)
     MRI_GEMM_BN_CASE(192, 5)
-    MRI_GEMM_BN_CASE(224, 5)
+    MRI_GEMM_BN_CASE(224, 4)
     default:
       e = launch_bn<256, 4>(dev, st, ta, tb, act_scale_dev, scale_per_row, w_scales, M, N, K, out,
                             acc_out, status, residual);

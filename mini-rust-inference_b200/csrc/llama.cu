@@ -424,7 +424,9 @@ __global__ void __launch_bounds__(kFaThreads) attn_prefill_tc_kernel(const float
                                                               int n_heads, int n_kv, int M, int start,
                                                               const float* __restrict__ kc,
                                                               const float* __restrict__ vc, float scale,
-                                                              float* __restrict__ out, int out_ld) {
+                                                              float* __restrict__ out, int out_ld,
+                                                              float* __restrict__ part,
+                                                              int* __restrict__ tickets, int split_min) {
   constexpr int KS = HD / 16;     // k steps of S = Q K^T
   constexpr int NT = HD / 8;      // n tiles of O
   constexpr int SK = HD + 8;      // halves per K row in shared memory
@@ -434,7 +436,13 @@ __global__ void __launch_bounds__(kFaThreads) attn_prefill_tc_kernel(const float
   __half* sKl = sK + kFaKT * SK;        // [64 keys][SK] lo parts
   __half* sVt = sKl + kFaKT * SK;       // [HD][SV] hi parts
   __half* sVtl = sVt + HD * SV;         // [HD][SV] lo parts
-  const int h = blockIdx.x, q0 = blockIdx.y * kFaQ;
+  // blockIdx.y = (query block, split), the longest walks (last query
+  // blocks) first so that the short ones fill in behind them.
+  const int splits_grid = split_min > 0 ? 2 : 1;
+  const int n_qb = static_cast<int>(gridDim.y) / splits_grid;
+  const int qb = n_qb - 1 - static_cast<int>(blockIdx.y) / splits_grid;
+  const int split = static_cast<int>(blockIdx.y) % splits_grid;
+  const int h = blockIdx.x, q0 = qb * kFaQ;
   const int kv_h = h / (n_heads / n_kv);
   const int kvd = n_kv * HD;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -466,7 +474,14 @@ __global__ void __launch_bounds__(kFaThreads) attn_prefill_tc_kernel(const float
   for (int n = 0; n < NT; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
   float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.0f, l_b = 0.0f;
   const int last_key = start + min(q0 + kFaQ, M) - 1;
-  for (int kt = 0; kt <= last_key; kt += kFaKT) {
+  // Key tiles [t0, t1) of this block.  The causal prefix of the last query
+  // blocks is the longest walk; from split_min tiles on it goes to two
+  // blocks (split 0 and 1) whose partial results the later one merges.
+  const int n_tiles = last_key / kFaKT + 1;
+  const int n_splits = split_min > 0 && n_tiles >= split_min ? 2 : 1;
+  if (split >= n_splits) return;
+  const int t0 = split * n_tiles / n_splits, t1 = (split + 1) * n_tiles / n_splits;
+  for (int kt = t0 * kFaKT; kt < t1 * kFaKT; kt += kFaKT) {
     const int nk = min(kFaKT, last_key + 1 - kt);
     __syncthreads();
     // K tile -> sK[key][dim], V tile -> sVt[dim][key] (f16); keys past nk are 0.
@@ -582,6 +597,61 @@ __global__ void __launch_bounds__(kFaThreads) attn_prefill_tc_kernel(const float
   l_a += __shfl_xor_sync(0xffffffffu, l_a, 2);
   l_b += __shfl_xor_sync(0xffffffffu, l_b, 1);
   l_b += __shfl_xor_sync(0xffffffffu, l_b, 2);
+  if (n_splits > 1) {
+    // Both splits store (o, m, l) of their 128 rows; the block that arrives
+    // second merges the two records in split order (the same sums whichever
+    // finishes first) and resets the ticket for the next launch.
+    constexpr int kRec = kFaQ * (HD + 2);
+    const int pair = qb * gridDim.x + h;
+    float* rec = part + (static_cast<size_t>(pair) * 2 + split) * kRec;
+    const int la = warp * 16 + g, lb = la + 8;  // local rows
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+      const int d = n * 8 + 2 * t;
+      *reinterpret_cast<float2*>(rec + la * HD + d) = make_float2(o[n][0], o[n][1]);
+      *reinterpret_cast<float2*>(rec + lb * HD + d) = make_float2(o[n][2], o[n][3]);
+    }
+    if (t == 0) {
+      rec[kFaQ * HD + la] = m_a;
+      rec[kFaQ * HD + lb] = m_b;
+      rec[kFaQ * HD + kFaQ + la] = l_a;
+      rec[kFaQ * HD + kFaQ + lb] = l_b;
+    }
+    __threadfence();
+    __syncthreads();
+    __shared__ int fa_last;
+    if (threadIdx.x == 0) fa_last = atomicAdd(tickets + pair, 1) == 1;
+    __syncthreads();
+    if (!fa_last) return;
+    __threadfence();
+    if (threadIdx.x == 0) tickets[pair] = 0;
+    const float* r0 = part + static_cast<size_t>(pair) * 2 * kRec;
+    const float* r1 = r0 + kRec;
+    const float m0a = __ldcg(r0 + kFaQ * HD + la), m1a = __ldcg(r1 + kFaQ * HD + la);
+    const float m0b = __ldcg(r0 + kFaQ * HD + lb), m1b = __ldcg(r1 + kFaQ * HD + lb);
+    const float mxa = fmaxf(m0a, m1a), mxb = fmaxf(m0b, m1b);
+    // A split that saw no key of a row (m = -inf) contributes nothing.
+    const float c0a = m0a == -INFINITY ? 0.0f : expf(m0a - mxa);
+    const float c1a = m1a == -INFINITY ? 0.0f : expf(m1a - mxa);
+    const float c0b = m0b == -INFINITY ? 0.0f : expf(m0b - mxb);
+    const float c1b = m1b == -INFINITY ? 0.0f : expf(m1b - mxb);
+    l_a = __fadd_rn(__fmul_rn(__ldcg(r0 + kFaQ * HD + kFaQ + la), c0a),
+                    __fmul_rn(__ldcg(r1 + kFaQ * HD + kFaQ + la), c1a));
+    l_b = __fadd_rn(__fmul_rn(__ldcg(r0 + kFaQ * HD + kFaQ + lb), c0b),
+                    __fmul_rn(__ldcg(r1 + kFaQ * HD + kFaQ + lb), c1b));
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+      const int d = n * 8 + 2 * t;
+      const float2 p0a = __ldcg(reinterpret_cast<const float2*>(r0 + la * HD + d));
+      const float2 p1a = __ldcg(reinterpret_cast<const float2*>(r1 + la * HD + d));
+      const float2 p0b = __ldcg(reinterpret_cast<const float2*>(r0 + lb * HD + d));
+      const float2 p1b = __ldcg(reinterpret_cast<const float2*>(r1 + lb * HD + d));
+      o[n][0] = __fadd_rn(__fmul_rn(p0a.x, c0a), __fmul_rn(p1a.x, c1a));
+      o[n][1] = __fadd_rn(__fmul_rn(p0a.y, c0a), __fmul_rn(p1a.y, c1a));
+      o[n][2] = __fadd_rn(__fmul_rn(p0b.x, c0b), __fmul_rn(p1b.x, c1b));
+      o[n][3] = __fadd_rn(__fmul_rn(p0b.y, c0b), __fmul_rn(p1b.y, c1b));
+    }
+  }
   const float ia = __fdiv_rn(1.0f, l_a), ib = __fdiv_rn(1.0f, l_b);
 #pragma unroll
   for (int n = 0; n < NT; ++n) {
@@ -593,6 +663,16 @@ __global__ void __launch_bounds__(kFaThreads) attn_prefill_tc_kernel(const float
       *reinterpret_cast<float2*>(out + static_cast<size_t>(rb) * out_ld + h * HD + d) =
           make_float2(o[n][2] * ib, o[n][3] * ib);
   }
+}
+
+// Key tiles from which a query block's walk is split over two blocks
+// (MRI_FA_SPLIT; 0 = never).
+int fa_split_min() {
+  static const int v = [] {
+    const char* e = std::getenv("MRI_FA_SPLIT");
+    return e ? std::max(0, std::atoi(e)) : 3;
+  }();
+  return v;
 }
 
 // Dynamic shared memory of attn_prefill_tc_kernel<hd>: K and V^T tiles, hi and lo.
@@ -750,6 +830,8 @@ struct mri_llama {
   float *x = nullptr, *qkv = nullptr, *attn = nullptr, *gu = nullptr;
   float *logits = nullptr, *part = nullptr;
   int* tickets = nullptr;      // [n_heads] decode-attention split counters, then 1 argmax counter
+  float* fa_part = nullptr;    // prefill attention: two split records per (query block, head)
+  int* fa_tickets = nullptr;   // prefill attention: split counters per (query block, head)
   float* amax_v = nullptr;     // argmax partials
   int* amax_i = nullptr;
   bool fused_decode = false;   // decode projections carry the RoPE/KV and SwiGLU epilogues
@@ -876,7 +958,8 @@ int run_blocks(mri_llama* m, size_t rows, int pos0, bool decode_dev) {
                         c.n_heads, c.n_kv_heads, m->hd, kc, vc, m->d_pos, scale, m->part,
                         m->max_splits, m->tickets, m->attn));
     } else if ((m->hd == 64 || m->hd == 128) && (m->qkv_w % 2) == 0 && (m->qd % 2) == 0 && tc_attn()) {
-      const dim3 grid(c.n_heads, static_cast<unsigned>((rows + kFaQ - 1) / kFaQ));
+      const int split_min = fa_split_min();
+      const dim3 grid(c.n_heads, static_cast<unsigned>((rows + kFaQ - 1) / kFaQ) * (split_min > 0 ? 2 : 1));
       const size_t smem = fa_smem_bytes(m->hd);
       static bool fa_attr_set[64] = {false};
       const int dv = m->ctx->device;
@@ -890,11 +973,13 @@ int run_blocks(mri_llama* m, size_t rows, int pos0, bool decode_dev) {
       if (m->hd == 64)
         attn_prefill_tc_kernel<64><<<grid, kFaThreads, smem, st>>>(m->qkv, m->qkv_w, c.n_heads, c.n_kv_heads,
                                                             static_cast<int>(rows), pos0, kc, vc, scale,
-                                                            m->attn, m->qd);
+                                                            m->attn, m->qd, m->fa_part, m->fa_tickets,
+                                                            split_min);
       else
         attn_prefill_tc_kernel<128><<<grid, kFaThreads, smem, st>>>(m->qkv, m->qkv_w, c.n_heads, c.n_kv_heads,
                                                              static_cast<int>(rows), pos0, kc, vc, scale,
-                                                             m->attn, m->qd);
+                                                             m->attn, m->qd, m->fa_part, m->fa_tickets,
+                                                             split_min);
     } else {
       const size_t smem = (kPrefillKT * (kMaxHeadDim + 1) + kPrefillKT * kMaxHeadDim +
                            kPrefillQ * kMaxHeadDim) * sizeof(float);
@@ -1052,6 +1137,11 @@ int mri_llama_create(mri_ctx* ctx, const mri_llama_config* cfg, mri_llama** out)
   rc = rc ? rc : dalloc(m, &m->d_gen, T + 1);
   rc = rc ? rc : dalloc(m, &m->d_pos, 1);
   rc = rc ? rc : dalloc(m, &m->tickets, c.n_heads + 1);
+  const size_t fa_pairs = static_cast<size_t>(c.n_heads) * ((m->max_tokens + kFaQ - 1) / kFaQ);
+  if (m->hd == 64 || m->hd == 128) {
+    rc = rc ? rc : dalloc(m, &m->fa_part, fa_pairs * 2 * kFaQ * (m->hd + 2));
+    rc = rc ? rc : dalloc(m, &m->fa_tickets, fa_pairs);
+  }
   rc = rc ? rc : dalloc(m, &m->amax_v, kArgmaxBlocks);
   rc = rc ? rc : dalloc(m, &m->amax_i, kArgmaxBlocks);
   if (rc != MRI_OK) {
@@ -1066,6 +1156,7 @@ int mri_llama_create(mri_ctx* ctx, const mri_llama_config* cfg, mri_llama** out)
     return fail(r, "scratch reservation: %s", mri_last_error());
   }
   cudaMemset(m->tickets, 0, (c.n_heads + 1) * sizeof(int));
+  if (m->fa_tickets) cudaMemset(m->fa_tickets, 0, fa_pairs * sizeof(int));
   cudaMemset(m->kc, 0, static_cast<size_t>(c.n_layers) * c.max_seq * m->kvd * sizeof(float));
   cudaMemset(m->vc, 0, static_cast<size_t>(c.n_layers) * c.max_seq * m->kvd * sizeof(float));
   // Carve the blobs into QuantizedMatrix views, each starting 256-byte

@@ -141,6 +141,23 @@ def test_head_dim_128_prefill_spans_tiles(mri, oracle):
     assert rel_range_err(gpu.forward_decode(7, 150), ref.forward_decode(7, 150)) < TOL
 
 
+def test_prefill_split_key_walks(mri, oracle):
+    """Head dim 64, a 330-token prefill: query blocks 1 and 2 walk 4 and 6
+    key tiles, which two blocks split and the later one merges.  Rows on both
+    sides of each split point against the oracle, and a second prefill gives
+    the same logits bit for bit (the merge does not depend on which split
+    finishes first)."""
+    cfg = dict(n_layers=2, dim=256, n_heads=4, n_kv_heads=2, ffn_dim=512, vocab=300, max_seq=352,
+               rope_base=10000.0, rms_eps=1e-5)
+    gpu, ref = build_pair(mri, oracle, cfg, random_weights(cfg, 8))
+    toks = list(np.random.default_rng(9).integers(0, 300, size=330))
+    got, want = gpu.forward(toks), ref.prefill_cached(toks)
+    for r in (0, 127, 128, 191, 192, 255, 256, 300, 329):
+        assert rel_range_err(got[r], want[r]) < TOL, r
+    np.testing.assert_array_equal(gpu.forward(toks), got)
+    assert rel_range_err(gpu.forward_decode(11, 330), ref.forward_decode(11, 330)) < TOL
+
+
 def test_decode_is_deterministic_at_scale(mri):
     """Two greedy runs and two decodes of the same step agree bit for bit on a
     model large enough that consecutive kernels overlap under programmatic

@@ -35,7 +35,9 @@ GGML_TYPES = {
     6: ("Q5_0", 32, 22), 7: ("Q5_1", 32, 24), 8: ("Q8_0", 32, 34), 9: ("Q8_1", 32, 40),
     10: ("Q2_K", 256, 84), 11: ("Q3_K", 256, 110), 12: ("Q4_K", 256, 144),
     13: ("Q5_K", 256, 176), 14: ("Q6_K", 256, 210), 15: ("Q8_K", 256, 292),
-    24: ("I8", 1, 1), 25: ("I16", 1, 2), 26: ("I32", 1, 4), 27: ("I64", 1, 8),
+    16: ("IQ2_XXS", 256, 66), 17: ("IQ2_XS", 256, 74), 18: ("IQ3_XXS", 256, 98),
+    19: ("IQ1_S", 256, 50), 20: ("IQ4_NL", 256, 136), 21: ("IQ3_S", 256, 110),
+    22: ("IQ2_S", 256, 82), 23: ("IQ4_XS", 256, 136), 24: ("I8", 1, 1), 25: ("I16", 1, 2), 26: ("I32", 1, 4), 27: ("I64", 1, 8),
     28: ("F64", 1, 8), 29: ("BF16", 1, 2),
 }
 F32, F16, Q4_0, Q8_0 = 0, 1, 2, 8
@@ -296,7 +298,7 @@ class GgufFile:
             dims = [cur.scalar("<Q", "tensor dimension") for _ in range(n_dims)]
             dtype = cur.scalar("<I", "tensor type")
             if dtype not in GGML_TYPES:
-                raise ValueOutOfRange(f"ggml type {dtype}")
+                raise UnknownValueType(dtype)  # GgmlType::from_u32 (dtype.rs:94-125)
             offset = cur.scalar("<Q", "tensor offset")
             if name in self.tensors:
                 raise KeyNotFound(f"duplicate tensor name: {name}")

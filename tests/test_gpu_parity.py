@@ -359,6 +359,57 @@ def test_gemm_two_ctas_per_sm_exact(mri, oracle, gpu_ctx, monkeypatch, bn):
     assert np.array_equal(bits(got), bits(want))
 
 
+# The epilogue stages each warp's 32 x 32 output block in shared memory when the
+# block lies inside M and N and no INT32 copy is requested (acc_out selects the
+# direct per-row stores); the cases below leave acc_out out so that the staged
+# stores are the ones checked, on full and ragged blocks.
+@pytest.mark.parametrize("bn", [128, 160, 192, 224, 256])
+def test_gemm_staged_epilogue_exact(mri, oracle, gpu_ctx, monkeypatch, bn):
+    monkeypatch.setenv("MRI_GEMM_BN", str(bn))
+    rng = np.random.default_rng(300 + bn)
+    m, n, k = 333, 1000, 4096 + 256
+    aq = rng.integers(-127, 128, size=m * k, dtype=np.int8)
+    wq = rng.integers(-127, 128, size=n * k, dtype=np.int8)
+    ws = rng.uniform(0.001, 0.02, size=n).astype(np.float32)
+    qm = mri.QuantizedMatrix(wq, ws, n, k)
+    got = mri.matmul_int8(aq, np.float32(0.0123), qm, m)
+    want, _ = oracle.matmul_int8(aq, np.float32(0.0123), wq, ws, n, k, m)
+    assert np.array_equal(bits(got), bits(want))
+
+
+@pytest.mark.parametrize("bn", [128, 160])
+def test_gemm_two_ctas_per_sm_staged_exact(mri, oracle, gpu_ctx, monkeypatch, bn):
+    """One tile per CTA, two CTAs per SM: the output block is staged in the
+    (then idle) stage ring."""
+    monkeypatch.setenv("MRI_GEMM_BN", str(bn))
+    rng = np.random.default_rng(400 + bn)
+    m, n, k = 500, 7717, 1024 + 256
+    aq = rng.integers(-127, 128, size=m * k, dtype=np.int8)
+    wq = rng.integers(-127, 128, size=n * k, dtype=np.int8)
+    ws = rng.uniform(0.001, 0.02, size=n).astype(np.float32)
+    qm = mri.QuantizedMatrix(wq, ws, n, k)
+    got = mri.matmul_int8(aq, np.float32(0.0123), qm, m)
+    want, _ = oracle.matmul_int8(aq, np.float32(0.0123), wq, ws, n, k, m)
+    assert np.array_equal(bits(got), bits(want))
+
+
+def test_prefill_shape_f32_exact(mri, oracle, gpu_ctx):
+    """BASELINE prefill config through matmul_int8_from_f32 (per-tensor
+    quantizer + tensor-core GEMM with the staged epilogue): 16 sampled rows
+    bit-equal to the oracle's."""
+    rng = np.random.default_rng(11)
+    m, n, k = 512, 11008, 4096
+    x = rng.normal(0, 1, size=(m, k)).astype(np.float32)
+    wq = rng.integers(-127, 128, size=n * k, dtype=np.int8)
+    ws = rng.uniform(0.001, 0.02, size=n).astype(np.float32)
+    qm = mri.QuantizedMatrix(wq, ws, n, k)
+    got = mri.matmul_int8_from_f32(x, qm)
+    aq, s = oracle.quantize_symmetric(x)
+    rows = np.sort(np.concatenate([[0, 31, 32, 127, 128, 511], rng.choice(m, size=10, replace=False)]))
+    want, _ = oracle.matmul_int8(aq.reshape(m, k)[rows].reshape(-1), s, wq, ws, n, k, len(rows))
+    assert np.array_equal(bits(got[rows]), bits(want))
+
+
 def test_device_status_clean(mri, gpu_ctx):
     """No bounded device-side wait gave up during the tests above."""
     gpu_ctx.check_device_status()

@@ -138,14 +138,23 @@ __global__ void __launch_bounds__(kQThreads) quant_apply_kernel(const float* __r
     if (tid == 0) scale_out[0] = scale;
     if ((reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(q) & 3) == 0) {
       const size_t n4 = n / 4;
-      for (size_t j = tid; j < n4; j += stride) {
-        const float4 v = ld_act(reinterpret_cast<const float4*>(x) + j);
-        char4 o;
-        o.x = sym_quant(v.x, inv);
-        o.y = sym_quant(v.y, inv);
-        o.z = sym_quant(v.z, inv);
-        o.w = sym_quant(v.w, inv);
-        reinterpret_cast<char4*>(q)[j] = o;
+      const float4* x4 = reinterpret_cast<const float4*>(x);
+      char4* q4 = reinterpret_cast<char4*>(q);
+      constexpr int U = 4;  // independent loads in flight per thread
+      size_t j = tid;
+      for (; j + (U - 1) * stride < n4; j += U * stride) {
+        float4 v[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) v[u] = ld_act(x4 + j + u * stride);
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+          q4[j + u * stride] = make_char4(sym_quant(v[u].x, inv), sym_quant(v[u].y, inv),
+                                          sym_quant(v[u].z, inv), sym_quant(v[u].w, inv));
+      }
+      for (; j < n4; j += stride) {
+        const float4 v = ld_act(x4 + j);
+        q4[j] = make_char4(sym_quant(v.x, inv), sym_quant(v.y, inv), sym_quant(v.z, inv),
+                           sym_quant(v.w, inv));
       }
       for (size_t j = n4 * 4 + tid; j < n; j += stride) q[j] = sym_quant(ld_act(x + j), inv);
     } else {

@@ -181,7 +181,10 @@ def test_int8_per_row_granularity(m, k, mri, oracle, gpu_ctx):
         assert np.array_equal(bits(got[r:r + 1]), bits(want)), r
 
 
-@pytest.mark.parametrize("m,k", [(1, 4096), (8, 4096), (512, 4096), (3, 7), (1, 1), (64, 8192)])
+# (1001, 4099): more than four grid strides of float4s in the per-tensor pass
+# (its unrolled loop, the remainder loop and a 3-element scalar tail).
+@pytest.mark.parametrize("m,k", [(1, 4096), (8, 4096), (512, 4096), (3, 7), (1, 1), (64, 8192),
+                                 (1001, 4099)])
 def test_quantizer_bit_exact(m, k, mri, oracle, gpu_ctx):
     rng = np.random.default_rng(m * 31 + k)
     x = rng.normal(0, 1, size=(m, k)).astype(np.float32)

@@ -140,6 +140,27 @@ class Context:
     def stream_handle(self):
         return int(self._lib.mri_ctx_stream(self.handle) or 0)
 
+    def ordered_with_torch(self, device, launch):
+        """Run `launch()`, which enqueues work on this context's stream, in
+        order with torch's current stream on `device`: the context's stream
+        first waits for what torch has queued (e.g. the copy that made an input
+        contiguous), and torch's current stream then waits for the launched
+        work, so torch consumers and torch's caching allocator see the outputs
+        only once they are written.  The context's own stream is created
+        non-blocking, so without these waits the two streams run unordered."""
+        import torch
+        cur = torch.cuda.current_stream(device)
+        if cur.cuda_stream == self.stream_handle:
+            return launch()
+        ts = getattr(self, "_torch_stream", None)
+        if ts is None:
+            ts = self._torch_stream = torch.cuda.ExternalStream(self.stream_handle, device=device)
+        ts.wait_stream(cur)
+        try:
+            return launch()
+        finally:
+            cur.wait_stream(ts)
+
     def int8_path(self, m, n, k):
         return int(self._lib.mri_int8_path(self.handle, m, n, k))
 
@@ -390,9 +411,11 @@ def matmul_int8(act_q, act_scale, weights, m, acc_out=None):
     ctx = weights.ctx
     n = weights.n_out
     if _is_cuda_tensor(act_q):
+        act_q = act_q.contiguous()
         out = _new_out(act_q, m, n)
-        _check(ctx._lib.mri_matmul_int8(ctx.handle, _vp(act_q), act_q.numel(), float(act_scale),
-                                        weights.handle, m, _vp(out), _vp(acc_out)))
+        ctx.ordered_with_torch(act_q.device, lambda: _check(ctx._lib.mri_matmul_int8(
+            ctx.handle, _vp(act_q), act_q.numel(), float(act_scale), weights.handle, m, _vp(out),
+            _vp(acc_out))))
         return out
     a = np.ascontiguousarray(act_q, dtype=np.int8).reshape(-1)
     out = np.empty((m, n), dtype=np.float32)
@@ -416,8 +439,8 @@ def matmul_int8_from_f32(input, weights, granularity=_lib.PER_TENSOR):  # noqa: 
     ctx = weights.ctx
     out = _new_out(x, m, weights.n_out)
     if _is_cuda_tensor(x):
-        _check(ctx._lib.mri_matmul_int8_from_f32_g(ctx.handle, _vp(x), m, k, granularity,
-                                                   weights.handle, _vp(out)))
+        ctx.ordered_with_torch(x.device, lambda: _check(ctx._lib.mri_matmul_int8_from_f32_g(
+            ctx.handle, _vp(x), m, k, granularity, weights.handle, _vp(out))))
     elif granularity == _lib.PER_TENSOR:
         _check(ctx._lib.mri_host_matmul_int8_from_f32(ctx.handle, _vp(x), m, k, weights.handle, _vp(out)))
     else:
@@ -441,8 +464,11 @@ def matmul_q8_0_direct(input, weights):  # noqa: A002
         raise ShapeMismatch(f"expected [{m}, {weights.k_in}], got [{m}, {k}]")
     ctx = weights.ctx
     out = _new_out(x, m, weights.n_out)
-    fn = ctx._lib.mri_matmul_q8_0_direct if _is_cuda_tensor(x) else ctx._lib.mri_host_matmul_q8_0_direct
-    _check(fn(ctx.handle, _vp(x), m, k, weights.handle, _vp(out)))
+    if _is_cuda_tensor(x):
+        ctx.ordered_with_torch(x.device, lambda: _check(ctx._lib.mri_matmul_q8_0_direct(
+            ctx.handle, _vp(x), m, k, weights.handle, _vp(out))))
+    else:
+        _check(ctx._lib.mri_host_matmul_q8_0_direct(ctx.handle, _vp(x), m, k, weights.handle, _vp(out)))
     return out
 
 
@@ -459,8 +485,11 @@ def matmul_q4_0_dequant(input, weight_q4, n_out, k, ctx=None):  # noqa: A002
         raise InvalidShape(f"Q4_0Matrix is [{w.n_out}, {w.k}], call says [{n_out}, {k}]")
     c = w.ctx
     out = _new_out(x, m, n_out)
-    fn = c._lib.mri_matmul_q4_0_dequant if _is_cuda_tensor(x) else c._lib.mri_host_matmul_q4_0_dequant
-    _check(fn(c.handle, _vp(x), m, k, w.handle, _vp(out)))
+    if _is_cuda_tensor(x):
+        c.ordered_with_torch(x.device, lambda: _check(c._lib.mri_matmul_q4_0_dequant(
+            c.handle, _vp(x), m, k, w.handle, _vp(out))))
+    else:
+        _check(c._lib.mri_host_matmul_q4_0_dequant(c.handle, _vp(x), m, k, w.handle, _vp(out)))
     return out
 
 
@@ -552,8 +581,8 @@ def matmul_int8_from_f32_sharded(input, w_shard, n_total, comm):  # noqa: A002
     lib = comm.ctx._lib
     if _is_cuda_tensor(x):
         out = _new_out(x, m, n_total)
-        _check(lib.mri_sharded_matmul_int8_from_f32(comm.handle, _vp(x), m, k, w_shard.handle, n_total,
-                                                    _vp(out)))
+        comm.ctx.ordered_with_torch(x.device, lambda: _check(lib.mri_sharded_matmul_int8_from_f32(
+            comm.handle, _vp(x), m, k, w_shard.handle, n_total, _vp(out))))
         return out
     import torch
     dev = f"cuda:{comm.ctx.device}"

@@ -413,6 +413,81 @@ def test_prefill_shape_f32_exact(mri, oracle, gpu_ctx):
     assert np.array_equal(bits(got[rows]), bits(want))
 
 
+def _transposed_input(scale, offset, on_device):
+    """The reference's non-contiguous input: the [2, 64] transpose of a
+    row-major [64, 2] tensor holding i * scale + offset.  Returns the view, its
+    contiguous copy (same residency) and the contiguous host values."""
+    t = (np.arange(128, dtype=np.float32) * np.float32(scale) + np.float32(offset)).reshape(64, 2)
+    host = np.ascontiguousarray(t.T)
+    if on_device:
+        import torch
+        nc = torch.from_numpy(t).cuda().t()
+        assert not nc.is_contiguous()
+        return nc, nc.contiguous(), host
+    nc = t.T
+    assert not nc.flags["C_CONTIGUOUS"]
+    return nc, np.ascontiguousarray(nc), host
+
+
+def _to_host(a):
+    return a.cpu().numpy() if hasattr(a, "cpu") else np.asarray(a)
+
+
+@pytest.mark.parametrize("on_device", [False, True], ids=["host", "device"])
+def test_non_contiguous_inputs_match_contiguous(mri, oracle, gpu_ctx, on_device):
+    """int8.rs:274-288, q8_direct.rs:449-464, q4_0.rs:283-303: a transposed
+    [2, 64] input gives bit for bit the outputs of its contiguous copy, and the
+    oracle's (Q4_0 within the Q4_0 bar), for host arrays and CUDA tensors."""
+    # INT8 (int8.rs:276-286)
+    nc, c, xh = _transposed_input(0.05, -3.0, on_device)
+    w = np.arange(192, dtype=np.float32) * np.float32(0.02) - np.float32(2.0)
+    qw = mri.quantize_per_channel(w, 3, 64)
+    got_nc = _to_host(mri.matmul_int8_from_f32(nc, qw))
+    got_c = _to_host(mri.matmul_int8_from_f32(c, qw))
+    assert np.array_equal(bits(got_nc), bits(got_c))
+    want = oracle.matmul_int8_from_f32(xh, 2, 64, qw.data, qw.scales, 3, 64)
+    assert np.array_equal(bits(got_nc), bits(want))
+    # Q8_0 (q8_direct.rs:451-463)
+    qw8 = mri.Q8_0WeightMatrix.from_f32_tensor(w.reshape(3, 64))
+    got_nc = _to_host(mri.matmul_q8_0_direct(nc, qw8))
+    got_c = _to_host(mri.matmul_q8_0_direct(c, qw8))
+    assert np.array_equal(bits(got_nc), bits(got_c))
+    want = oracle.matmul_q8_0_direct(xh, 2, 64, qw8.data, 3, 64)
+    assert np.array_equal(bits(got_nc), bits(want))
+    # Q4_0 (q4_0.rs:285-302)
+    nc, c, xh = _transposed_input(0.01, 0.0, on_device)
+    w4 = ((np.arange(3)[:, None] + np.arange(64)[None, :]).astype(np.float32) * np.float32(0.03)
+          - np.float32(0.5))
+    wb = oracle.quantize_q4_0_matrix(w4, 3, 64)
+    got_nc = _to_host(mri.matmul_q4_0_dequant(nc, wb, 3, 64))
+    got_c = _to_host(mri.matmul_q4_0_dequant(c, wb, 3, 64))
+    assert got_nc.shape == (2, 3)
+    assert np.array_equal(bits(got_nc), bits(got_c))
+    want = oracle.matmul_q4_0_dequant(xh, 2, 64, wb, 3, 64)
+    ok, worst = q4_close(got_nc, want, xh, oracle.dequantize_q4_0(wb).reshape(3, 64))
+    assert ok, worst
+
+
+def test_device_inputs_ordered_with_torch_stream(mri, oracle, gpu_ctx):
+    """A context's stream is non-blocking.  An input that torch is still
+    writing on its current stream when the call is made must be complete
+    before the kernels read it, and torch must see the finished output, with
+    no explicit synchronization in between."""
+    import torch
+    rng = np.random.default_rng(21)
+    m, n, k = 4, 1024, 4096
+    x, wq, ws = rand_case(rng, m, n, k)
+    qm = mri.QuantizedMatrix(wq, ws, n, k)
+    src = torch.from_numpy(x).cuda()
+    xd = torch.zeros(m, k, device="cuda")
+    torch.cuda.synchronize()
+    torch.cuda._sleep(2_000_000)  # keep torch's stream busy (about a millisecond) ...
+    xd.copy_(src)                 # ... so that the input is written late
+    got = (mri.matmul_int8_from_f32(xd, qm) * 1.0).cpu().numpy()
+    want = oracle.matmul_int8_from_f32(x, m, k, wq, ws, n, k)
+    assert np.array_equal(bits(got), bits(want))
+
+
 def test_device_status_clean(mri, gpu_ctx):
     """No bounded device-side wait gave up during the tests above."""
     gpu_ctx.check_device_status()

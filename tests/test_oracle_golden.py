@@ -83,6 +83,21 @@ def test_parallel_bit_identical_to_scalar(oracle):
     assert np.array_equal(ref.view(np.uint32), par.view(np.uint32))
 
 
+def test_neon_and_avx2_agree(oracle):
+    """int8_neon.rs:318-332 on the reference's inputs.  Off aarch64 the NEON
+    kernel's dot is the scalar one (int8_neon.rs:126-131); every dot is an
+    exact INT32 sum, so the AVX2 outputs equal the scalar outputs bit for bit
+    (the reference asks for a relative error below 1e-6)."""
+    k, n, m = 128, 6, 4
+    w = np.arange(n * k, dtype=np.float32) * np.float32(0.01) - np.float32(5.0)
+    inp = np.arange(m * k, dtype=np.float32) * np.float32(0.02) - np.float32(5.0)
+    wq, ws = oracle.quantize_per_channel(w, n, k)
+    aq, s = oracle.quantize_symmetric(inp)
+    scalar, _ = oracle.matmul_int8(aq, s, wq, ws, n, k, m)
+    avx2 = oracle.matmul_int8_avx2(aq, s, wq, ws, n, k, m)
+    assert np.array_equal(scalar.view(np.uint32), avx2.view(np.uint32))
+
+
 def test_f16_exhaustive_against_numpy(oracle):
     """f16_to_f32 (quantization.rs:416-461) is exact for every non-NaN code."""
     for h in range(0, 1 << 16, 7):

@@ -344,7 +344,8 @@ def gguf_dequant(ggml_type, raw, numel, out=None, ctx=None):
     raw = np.ascontiguousarray(np.frombuffer(raw, dtype=np.uint8) if not isinstance(raw, np.ndarray)
                                else raw, dtype=np.uint8).reshape(-1)
     if out is not None:
-        _check(ctx._lib.mri_gguf_dequant(ctx.handle, int(ggml_type), _vp(raw), raw.size, numel, _vp(out)))
+        ctx.ordered_with_torch(out.device, lambda: _check(ctx._lib.mri_gguf_dequant(
+            ctx.handle, int(ggml_type), _vp(raw), raw.size, numel, _vp(out))))
         ctx.synchronize()
         return out
     import torch

@@ -255,6 +255,20 @@ def test_gguf_dequant_bit_exact(mri, gpu_ctx, oracle, ggml_type):
 
 
 @pytest.mark.gpu
+def test_gguf_dequant_into_device_tensor(mri, gpu_ctx, oracle):
+    """The `out=` form fills a caller's CUDA tensor, after the fill that
+    torch queued on it."""
+    import torch
+    rng = np.random.default_rng(12)
+    w = rng.normal(0, 1.0, size=(3, 160)).astype(np.float32)
+    raw = np.frombuffer(encode(oracle, w, 3, 160, gguf.Q8_0), np.uint8)
+    out = torch.full((w.size,), float("nan"), device="cuda")
+    got = mri.gguf_dequant(gguf.Q8_0, raw, w.size, out=out, ctx=gpu_ctx)
+    assert got is out
+    np.testing.assert_array_equal(out.cpu().numpy(), oracle.extract(gguf.Q8_0, raw))
+
+
+@pytest.mark.gpu
 def test_block_rows_not_on_block_boundary(mri, gpu_ctx, oracle):
     """[2, 48] Q8_0: 96 values = 3 blocks, the middle one straddles the rows
     (extract dequantizes the flat block stream)."""

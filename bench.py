@@ -46,6 +46,8 @@ ALG_BYTES = WEIGHT_BYTES + 4 * N_DIM + K_DIM * 4 + 4 * N_DIM  # + scales + x f32
 CALLS_PER_STEP = 256
 WEIGHT_COPIES = 16
 REF_CALLS_PER_STEP = 4
+WORKLOAD = ("decode projection [1,4096]x[4096,11008] int8 per-channel, "
+            "per-tensor act quant (BASELINE config 0)")
 
 THROTTLE_BITS = {0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
                  0x80: "hw_power_brake_slowdown", 0x4: "sw_power_cap", 0x2: "applications_clocks",
@@ -186,7 +188,7 @@ def run_reference(args, rank):
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(el / args.steps * 1e3, 4), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "int8->int32->f32", "data": "synthetic (seed 0)",
-        "config": {"workload": "decode projection [1,4096]x[4096,11008] int8 per-channel, per-tensor act quant",
+        "config": {"workload": WORKLOAD,
                    "calls_per_step": REF_CALLS_PER_STEP},
         "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": 1, "kind": "port",
                          "sample": sample},
@@ -577,8 +579,7 @@ def run_ours(args, rank, world, local_rank):
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8->int32->f32", "data": "synthetic (seed 0)",
-            "config": {"workload": "decode projection [1,4096]x[4096,11008] int8 per-channel, "
-                                   "per-tensor act quant fused (BASELINE config 0)",
+            "config": {"workload": WORKLOAD,
                        "calls_per_step": CALLS_PER_STEP, "parallelism": f"replicas x{world}",
                        "l2": f"weights rotate over {WEIGHT_COPIES} copies "
                              f"({WEIGHT_COPIES * WEIGHT_BYTES / 1e6:.0f} MB > 2x L2)",

@@ -1,6 +1,7 @@
 """CPU-only checks of the boundary: the C-ABI library loads, exports every
-symbol include/*.h declares, fails loudly without a GPU, and the host-side
-weight codecs match the oracle bit for bit."""
+symbol include/*.h declares, fails loudly without a GPU, raises the reference's
+shape errors before any device work, and the host-side weight codecs match the
+oracle bit for bit."""
 import glob
 import os
 import re
@@ -50,6 +51,32 @@ def test_no_gpu_fails_loudly(mri):
         pytest.skip("a GPU is present")
     with pytest.raises(mri.CudaError):
         mri.Context(0)
+
+
+class _WeightStub:
+    """Only the attributes the products' shape checks read.  It has no handle
+    and no context, so any device work would fail on it."""
+    n_out, k_in = 3, 64
+
+
+def test_shape_checks_run_before_device_work(mri):
+    """The reference's error order (int8.rs:114-132, q8_direct.rs:230-246,
+    q4_0.rs:101-119): a non-2-D input is InvalidShape and a K that differs
+    from the weight's is ShapeMismatch, raised before anything touches the
+    device (so here, without a GPU, no CudaError)."""
+    w = _WeightStub()
+    x3 = np.zeros((2, 3, 64), np.float32)
+    x_bad_k = np.zeros((2, 32), np.float32)
+    for fn in (mri.matmul_int8_from_f32, mri.matmul_q8_0_direct):
+        with pytest.raises(mri.InvalidShape):
+            fn(x3, w)
+        with pytest.raises(mri.ShapeMismatch):
+            fn(x_bad_k, w)
+    with pytest.raises(mri.InvalidShape):
+        mri.matmul_q4_0_dequant(x3, b"", 3, 64)
+    with pytest.raises(mri.ShapeMismatch):
+        mri.matmul_q4_0_dequant(x_bad_k, b"", 3, 64)
+    assert issubclass(mri.InvalidShape, mri.TensorError) and issubclass(mri.ShapeMismatch, mri.TensorError)
 
 
 @pytest.mark.parametrize("seed", [0, 1, 2])

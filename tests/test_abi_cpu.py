@@ -99,6 +99,19 @@ def test_q4_0_codec_matches_oracle(mri, oracle, seed):
     assert np.array_equal(mri.formats.quantize_q4_0(w, n, k), oracle.quantize_q4_0_matrix(w, n, k))
 
 
+def test_codecs_match_oracle_on_non_finite_values(mri, oracle):
+    """create_q8_0_block / create_q4_0_block (dequant.rs:389-424, 706-749) on
+    blocks holding inf, -inf, NaN, values past the f16 range and 1e30: the
+    host codecs produce the oracle's bytes."""
+    rng = np.random.default_rng(0)
+    w = rng.normal(0, 1, size=(4, 64)).astype(np.float32)
+    w[0, 3], w[1, 40], w[2, 7] = np.inf, -np.inf, np.nan
+    w[3, :32], w[3, 33] = 1e30, 7e4
+    with np.errstate(all="ignore"):
+        assert np.array_equal(mri.formats.quantize_q8_0(w, 4, 64), oracle.quantize_q8_0_matrix(w, 4, 64))
+        assert np.array_equal(mri.formats.quantize_q4_0(w, 4, 64), oracle.quantize_q4_0_matrix(w, 4, 64))
+
+
 def test_f16_truncation_matches_oracle(mri, oracle):
     rng = np.random.default_rng(3)
     vals = np.concatenate([rng.normal(0, 1e-4, 2000), rng.normal(0, 100, 2000),

@@ -314,7 +314,9 @@ MRI_API int mri_sharded_matmul_int8_from_f32(mri_comm* comm, const float* x_dev,
                                              float* out_dev);
 
 /* ── diagnostics ──────────────────────────────────────────────────────────── */
-/* Kernel path chosen for an INT8 product of this shape:
+/* No counterpart in the reference (its dot kernel is routed by target
+ * architecture at build time, src/ops/matmul/parallel.rs:258-275).
+ * Kernel path chosen for an INT8 product of this shape:
  * 0 = streaming GEMV (TMA bulk), 1 = generic GEMV, 2 = tensor-core GEMM. */
 MRI_API int mri_int8_path(mri_ctx* ctx, size_t m, size_t n, size_t k);
 /* Launch shape of the streaming INT8 GEMV for (m <= 8, n, k): plan[0..5] =

@@ -83,6 +83,30 @@ MRI_API int mri_ctx_check_device_status(mri_ctx* ctx);
 /* Number of kernels this context has launched (for launch accounting). */
 MRI_API uint64_t mri_ctx_launch_count(const mri_ctx* ctx);
 
+/* Kernel-variant options of a context.  No counterpart in the reference (its
+ * kernel choice is fixed at build time, src/ops/matmul/parallel.rs:258-275).
+ * The defaults are the measured best choices; every other value selects a
+ * variant that computes the same result (bit for bit where the product is
+ * bit-exact) and exists for tests and measurements.  Options apply to
+ * launches made after the call; a model's decode graph keeps the variant it
+ * was captured with.  In a sharded job every rank sets the same values.
+ * Unknown option or value out of range -> MRI_ERR_INVALID_ARGUMENT. */
+enum mri_option {
+  MRI_OPT_PDL = 0,        /* 1 (default): programmatic dependent launch between kernels; 0: off */
+  MRI_OPT_GEMM_BN = 1,    /* 0 (default): GEMM tile width per shape; 128..256 (step 32): forced */
+  MRI_OPT_GEMM_2CTA = 2,  /* 1 (default): between one and two rounds of GEMM tiles, one tile per CTA
+                             and two CTAs per SM; 0: the persistent grid */
+  MRI_OPT_Q8_MMA = 3,     /* 1 (default): Q8_0 at m = 2..8 on the integer warp MMA; 0: streaming kernel */
+  MRI_OPT_Q4_MMA = 4,     /* 1 (default): Q4_0 at m = 2..8 on the bf16 warp MMA; 0: streaming kernel */
+  MRI_OPT_TC_ATTN = 5,    /* 1 (default): tensor-core prefill attention for head dim 64 / 128;
+                             0: the CUDA-core kernel */
+  MRI_OPT_FA_SPLIT = 6,   /* 3 (default): prefill key walks of at least this many 64-key tiles are
+                             split over two blocks; 0: never */
+  MRI_OPT_SHARD_PEER = 7  /* 0 (default): sharded m <= 8 gathered by NCCL; 1: over peer memory */
+};
+MRI_API int mri_ctx_set_option(mri_ctx* ctx, int option, int value);
+MRI_API int mri_ctx_get_option(mri_ctx* ctx, int option, int* value);
+
 /* ── device-resident weights ──────────────────────────────────────────────── */
 /* QuantizedMatrix { data: [n_out,k_in] i8 row-major, scales: [n_out] f32 }
  * (per_channel.rs:29-40).  Host pointers; synchronous upload. */
@@ -255,25 +279,35 @@ MRI_API int mri_llama_launches_per_decode_step(const mri_llama* m, size_t* count
  * memory at call time (a host runtime that owns the device memory pool and
  * forbids cudaMalloc/cudaFree, or code that must not touch an allocator while
  * a framework manages the stream): matmul_int8_from_f32 with per-tensor
- * quantization, whose scratch (quantized activations, absmax, scale) lives in
- * a fixed file-scope device array instead of a context buffer.
+ * quantization, whose scratch (quantized activations, absmax, scale, status
+ * word) lives in a fixed file-scope device array instead of a context buffer.
+ * 1..8 rows run on the streaming GEMV, more on the tensor-core GEMM; the
+ * result equals mri_matmul_int8_from_f32 bit for bit.
  *   - Takes raw device pointers and a cudaStream_t (NULL = legacy stream);
  *     needs no context.  w_dev: [n,k] int8 row-major (16-byte aligned),
  *     w_scales_dev: [n] f32, x_dev: [m,k] f32, out_dev: [m,n] f32.
  *   - m*k must not exceed MRI_NOALLOC_MAX_ACT_BYTES, else
- *     MRI_ERR_INVALID_ARGUMENT; k must be a positive multiple of 16.
+ *     MRI_ERR_INVALID_ARGUMENT before any work; k must be a positive multiple
+ *     of 16.
  *   - The first call on a device resolves the array's device address
- *     (cudaGetSymbolAddress) and device properties; make that first call
- *     before any stream capture.
+ *     (cudaGetSymbolAddress) and device properties and clears the status
+ *     word; make that first call before any stream capture.
  *   - All calls share the one array: calls that overlap on the GPU (other
  *     streams, other threads) race.  Serialize them on one stream.
  *   - Every GPU that loads this library keeps the array allocated until the
  *     process exits.
+ *   - The call is asynchronous, and a bounded device-side wait that gives up
+ *     cannot change its return value: it records MRI_ERR_TIMEOUT in the
+ *     array's status word (the output is then incomplete).  The word stays
+ *     set until mri_noalloc_check_status(stream) synchronizes `stream`, reads
+ *     it into host memory, clears it and returns it (MRI_OK or
+ *     MRI_ERR_TIMEOUT); call it before using outputs that must be complete.
  *   - Errors: mri_noalloc_last_error(). */
 #define MRI_NOALLOC_MAX_ACT_BYTES (4u << 20)
 MRI_API int mri_matmul_int8_from_f32_noalloc(const float* x_dev, size_t m, size_t k,
                                              const int8_t* w_dev, const float* w_scales_dev,
                                              size_t n, float* out_dev, void* cuda_stream);
+MRI_API int mri_noalloc_check_status(void* cuda_stream);
 MRI_API const char* mri_noalloc_last_error(void);
 
 /* ── N-sharded products over NCCL ───────────────────────────────────────────── */
@@ -319,10 +353,19 @@ MRI_API int mri_sharded_matmul_int8_from_f32(mri_comm* comm, const float* x_dev,
  * Kernel path chosen for an INT8 product of this shape:
  * 0 = streaming GEMV (TMA bulk), 1 = generic GEMV, 2 = tensor-core GEMM. */
 MRI_API int mri_int8_path(mri_ctx* ctx, size_t m, size_t n, size_t k);
-/* Launch shape of the streaming INT8 GEMV for (m <= 8, n, k): plan[0..5] =
+/* Launch shape of the streaming INT8 GEMV for (m <= 8, n, k): plan[0..7] =
  * grid, CTAs per SM used, CTAs per SM that fit (registers and shared
- * memory), pipeline stages, K-chunks per row group, dynamic shared bytes. */
-MRI_API int mri_int8_gemv_plan(mri_ctx* ctx, size_t m, size_t n, size_t k, int* plan /* [6] */);
+ * memory), pipeline stages, K-chunks per row group, dynamic shared bytes,
+ * register-prologue width of a per-tensor f32 input (4 or 12 float4 per
+ * consumer thread, 0 = none), and 1 when such an input is quantized by the
+ * quantizer kernels first (then the GEMV streams int8 activations). */
+MRI_API int mri_int8_gemv_plan(mri_ctx* ctx, size_t m, size_t n, size_t k, int* plan /* [8] */);
+/* Launch shape of the tensor-core INT8 GEMM for (m, n, k): plan[0..5] = tile
+ * width BN, ring stages, TMEM accumulator buffers per CTA (2: persistent
+ * grid, each CTA walks tiles t, t + grid, ...; 1: one tile per CTA, two CTAs
+ * per SM), grid, tiles, and the most tiles one CTA takes.  Follows the
+ * context's options.  No tensor-core GEMM for the shape -> MRI_ERR_INVALID_SHAPE. */
+MRI_API int mri_int8_gemm_plan(mri_ctx* ctx, size_t m, size_t n, size_t k, int* plan /* [6] */);
 
 #ifdef __cplusplus
 }

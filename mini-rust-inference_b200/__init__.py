@@ -21,6 +21,7 @@ context's stream).  There is no CPU compute path.
 Import with importlib (the directory name is not an identifier):
     mri = importlib.import_module("mini-rust-inference_b200")
 """
+import contextlib
 import ctypes
 import sys
 import threading
@@ -40,6 +41,13 @@ __all__ = [
     "comm_available", "shard_rows", "Communicator", "shard_quantized_matrix",
     "matmul_int8_from_f32_sharded", "gguf_dequant",
 ]
+
+
+# Activation-quantization granularity (mri_granularity).
+PER_TENSOR, PER_ROW = _lib.PER_TENSOR, _lib.PER_ROW
+
+# Kernel-variant options of a Context (mri_option in include/mri_gpu.h).
+OPT_PDL, OPT_GEMM_BN, OPT_GEMM_2CTA, OPT_Q8_MMA, OPT_Q4_MMA, OPT_TC_ATTN, OPT_FA_SPLIT, OPT_SHARD_PEER = range(8)
 
 
 class TensorError(Exception):
@@ -166,10 +174,37 @@ class Context:
 
     def int8_gemv_plan(self, m, n, k):
         """Launch shape of the streaming INT8 GEMV (diagnostics)."""
-        p = (ctypes.c_int * 6)()
+        p = (ctypes.c_int * 8)()
         _check(self._lib.mri_int8_gemv_plan(self.handle, m, n, k, p))
-        keys = ("grid", "ctas_per_sm", "resident_ctas", "stages", "k_chunks", "smem_bytes")
+        keys = ("grid", "ctas_per_sm", "resident_ctas", "stages", "k_chunks", "smem_bytes", "reg_vec",
+                "quantize_first")
         return dict(zip(keys, list(p)))
+
+    def int8_gemm_plan(self, m, n, k):
+        """Launch shape of the tensor-core INT8 GEMM (diagnostics)."""
+        p = (ctypes.c_int * 6)()
+        _check(self._lib.mri_int8_gemm_plan(self.handle, m, n, k, p))
+        keys = ("bn", "stages", "acc_buffers", "grid", "tiles", "tiles_per_cta")
+        return dict(zip(keys, list(p)))
+
+    def set_option(self, option, value):
+        """Kernel-variant option (OPT_* below; mri_ctx_set_option)."""
+        _check(self._lib.mri_ctx_set_option(self.handle, int(option), int(value)))
+
+    def get_option(self, option):
+        v = ctypes.c_int()
+        _check(self._lib.mri_ctx_get_option(self.handle, int(option), ctypes.byref(v)))
+        return v.value
+
+    @contextlib.contextmanager
+    def option(self, option, value):
+        """Sets an option for the body of a with-statement, then restores it."""
+        old = self.get_option(option)
+        self.set_option(option, value)
+        try:
+            yield self
+        finally:
+            self.set_option(option, old)
 
 
 _tls = threading.local()

@@ -37,6 +37,8 @@ SIGNATURES = {
     "mri_ctx_stream": (_P, [_P]),
     "mri_ctx_check_device_status": (_I, [_P]),
     "mri_ctx_launch_count": (ctypes.c_uint64, [_P]),
+    "mri_ctx_set_option": (_I, [_P, _I, _I]),
+    "mri_ctx_get_option": (_I, [_P, _I, ctypes.POINTER(_I)]),
     "mri_qmatrix_upload": (_I, [_P, _P, _P, _SZ, _SZ, _PP]),
     "mri_qmatrix_upload_rows": (_I, [_P, _P, _P, _SZ, _SZ, _SZ, _SZ, _PP]),
     "mri_qmatrix_free": (_I, [_P]),
@@ -59,6 +61,7 @@ SIGNATURES = {
     "mri_host_matmul_q4_0_dequant": (_I, [_P, _P, _SZ, _SZ, _P, _P]),
     "mri_int8_path": (_I, [_P, _SZ, _SZ, _SZ]),
     "mri_int8_gemv_plan": (_I, [_P, _SZ, _SZ, _SZ, _P]),
+    "mri_int8_gemm_plan": (_I, [_P, _SZ, _SZ, _SZ, _P]),
     "mri_comm_available": (_I, []),
     "mri_comm_unique_id": (_I, [_P]),
     "mri_comm_create": (_I, [_P, _P, _I, _I, _I, _PP]),
@@ -86,6 +89,7 @@ SIGNATURES = {
     "mri_llama_launches_per_decode_step": (_I, [_P, ctypes.POINTER(_SZ)]),
     "mri_matmul_int8_from_f32_noalloc": (_I, [_P, _SZ, _SZ, _P, _P, _SZ, _P, _P]),
     "mri_noalloc_last_error": (ctypes.c_char_p, []),
+    "mri_noalloc_check_status": (_I, [_P]),
 }
 
 _lock = threading.Lock()

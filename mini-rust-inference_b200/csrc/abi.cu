@@ -287,7 +287,7 @@ int run_q8_0(mri_ctx* ctx, const float* x, size_t m, const mri_q8_0_matrix* w, f
   float* scales = nullptr;
   for (size_t m0 = 0; m0 < m; m0 += 8) {
     const int mc = static_cast<int>(std::min<size_t>(8, m - m0));
-    const bool pin = mri::q8_0_mma_supported(mc, K);
+    const bool pin = mri::q8_0_mma_supported(ctx->dev, mc, K);
     if (!pin && K > 0 && mri::gemv_q8_0_tma_supported(ctx->dev, mc, K)) {
       MRI_CUDA_TRY(mri::launch_gemv_q8_0_tma(ctx->dev, st, mc, w->data, N, K, x + m0 * K,
                                              out + m0 * N, ctx->d_status, &ctx->ls));
@@ -321,7 +321,7 @@ int run_q4_0(mri_ctx* ctx, const float* x, size_t m, const mri_q4_0_matrix* w, f
   uint32_t* xs = nullptr;  // split activations of all m rows, made on first use
   for (size_t m0 = 0; m0 < m; m0 += 8) {
     const int mc = static_cast<int>(std::min<size_t>(8, m - m0));
-    if (x_vec && mri::q4_0_mma_supported(mc, K)) {
+    if (x_vec && mri::q4_0_mma_supported(ctx->dev, mc, K)) {
       if (xs == nullptr) {
         if (int rc = ensure_scratch(ctx, al(mri::q4_0_split_bytes(m, K)))) return rc;
         xs = reinterpret_cast<uint32_t*>(ctx->scratch);
@@ -481,6 +481,46 @@ int mri_ctx_check_device_status(mri_ctx* ctx) {
 }
 
 uint64_t mri_ctx_launch_count(const mri_ctx* ctx) { return ctx ? ctx->ls.launches : 0; }
+
+namespace {
+int* option_slot(mri_ctx* ctx, int option) {
+  mri::Options& o = ctx->dev.opt;
+  switch (option) {
+    case MRI_OPT_PDL: return &o.pdl;
+    case MRI_OPT_GEMM_BN: return &o.gemm_bn;
+    case MRI_OPT_GEMM_2CTA: return &o.gemm_2cta;
+    case MRI_OPT_Q8_MMA: return &o.q8_mma;
+    case MRI_OPT_Q4_MMA: return &o.q4_mma;
+    case MRI_OPT_TC_ATTN: return &o.tc_attn;
+    case MRI_OPT_FA_SPLIT: return &o.fa_split;
+    case MRI_OPT_SHARD_PEER: return &o.shard_peer;
+    default: return nullptr;
+  }
+}
+}  // namespace
+
+int mri_ctx_set_option(mri_ctx* ctx, int option, int value) {
+  if (!ctx) return fail(MRI_ERR_INVALID_ARGUMENT, "null context");
+  int* slot = option_slot(ctx, option);
+  if (!slot) return fail(MRI_ERR_INVALID_ARGUMENT, "unknown option %d", option);
+  bool ok = true;
+  switch (option) {
+    case MRI_OPT_GEMM_BN: ok = value == 0 || (value >= 128 && value <= 256 && value % 32 == 0); break;
+    case MRI_OPT_FA_SPLIT: ok = value >= 0; break;
+    default: ok = value == 0 || value == 1;
+  }
+  if (!ok) return fail(MRI_ERR_INVALID_ARGUMENT, "value %d out of range for option %d", value, option);
+  *slot = value;
+  return MRI_OK;
+}
+
+int mri_ctx_get_option(mri_ctx* ctx, int option, int* value) {
+  if (!ctx || !value) return fail(MRI_ERR_INVALID_ARGUMENT, "null context or output");
+  const int* slot = option_slot(ctx, option);
+  if (!slot) return fail(MRI_ERR_INVALID_ARGUMENT, "unknown option %d", option);
+  *value = *slot;
+  return MRI_OK;
+}
 
 // ── weights ──────────────────────────────────────────────────────────────────
 
@@ -847,6 +887,26 @@ int mri_int8_gemv_plan(mri_ctx* ctx, size_t m, size_t n, size_t k, int* plan) {
   plan[3] = p.stages;
   plan[4] = p.k_chunks;
   plan[5] = static_cast<int>(p.smem);
+  // The register-prologue width of a per-tensor f32 input of this shape
+  // (4 or 12 float4 per consumer thread; 0 = the input is quantized by the
+  // quantizer kernels first and the GEMV streams int8 activations).
+  plan[6] = p.vec;
+  plan[7] = p.vec == 0 ? 1 : 0;
+  return MRI_OK;
+}
+
+int mri_int8_gemm_plan(mri_ctx* ctx, size_t m, size_t n, size_t k, int* plan) {
+  if (int rc = enter(ctx)) return rc;
+  if (!plan) return fail(MRI_ERR_INVALID_ARGUMENT, "null plan");
+  mri::GemmPlan p;
+  if (mri::gemm_i8_tc_plan(ctx->dev, m, n, k, &p) != cudaSuccess)
+    return fail(MRI_ERR_INVALID_SHAPE, "no tensor-core GEMM for m=%zu, n=%zu, k=%zu", m, n, k);
+  plan[0] = p.bn;
+  plan[1] = p.stages;
+  plan[2] = p.bufs;
+  plan[3] = p.grid;
+  plan[4] = p.tiles;
+  plan[5] = p.tiles_per_cta;
   return MRI_OK;
 }
 

@@ -194,10 +194,9 @@ int ensure_gather(mri_comm* c, size_t bytes) {
 }
 
 // Row chunks of an M-row sharded product: each chunk's all-gather overlaps the
-// next chunk's GEMM.  MRI_SHARD_CHUNKS overrides the count.
+// next chunk's GEMM.
 int chunk_count(size_t m) {
   int n = m >= 1024 ? 4 : (m >= 256 ? 2 : 1);
-  if (const char* e = std::getenv("MRI_SHARD_CHUNKS")) n = std::atoi(e);
   n = std::max(1, std::min(n, kMaxChunks));
   return static_cast<int>(std::min<size_t>(n, std::max<size_t>(1, m)));
 }
@@ -206,17 +205,6 @@ int check_comm(mri_comm* c) {
   if (!c) return mri::set_error(MRI_ERR_INVALID_ARGUMENT, "null communicator");
   if (c->aborted) return mri::set_error(MRI_ERR_COMM, "communicator was aborted after a timeout");
   return MRI_OK;
-}
-
-// MRI_SHARD_PEER=1 selects the peer-memory gather for m <= 8.  Off by
-// default: on 2 B200s it measured 34.1 us per 70B gate/up shard call against
-// 32.2 us for GEMV + NCCL all-gather (the shard GEMV alone: 19.8 us).
-bool peer_gather_enabled() {
-  static const bool v = [] {
-    const char* e = std::getenv("MRI_SHARD_PEER");
-    return e && std::atoi(e) != 0;
-  }();
-  return v;
 }
 
 // All-gathers `bytes` bytes of host data from every rank (through a device
@@ -506,7 +494,11 @@ int mri_sharded_matmul_int8_from_f32(mri_comm* c, const float* x_dev, size_t m, 
       m <= 8 && mri::stream_gemv_ok(ctx, m, w_shard) &&
       mri::gemv_i8_tma_plan(ctx->dev, static_cast<int>(m), ns, k, &plan, -1, 2) == cudaSuccess &&
       ((ns + plan.grid - 1) / plan.grid) * m <= 1024;
-  if (gather_fits && peer_gather_enabled()) {
+  // The context's MRI_OPT_SHARD_PEER selects the peer-memory gather for
+  // m <= 8.  Off by default: on 2 B200s it measured 34.1 us per 70B gate/up
+  // shard call against 32.2 us for GEMV + NCCL all-gather (the shard GEMV
+  // alone: 19.8 us).
+  if (gather_fits && c->ctx->dev.opt.shard_peer) {
     if (int rc = ensure_peer(c, m * n_total)) return rc;
     if (c->peer_ok) {
       mri::EpiArgs e;

@@ -456,25 +456,13 @@ cudaError_t set_smem_tc(KernelT k, size_t bytes, int device) {
   return e;
 }
 
-bool pdl_enabled() {
-  static const bool on = [] {
-    const char* e = std::getenv("MRI_PDL");
-    return e == nullptr || std::atoi(e) != 0;
-  }();
-  return on;
-}
-
-// Tile width: the one whose wave count times tile width is smallest (ties
-// go to the wider tile, which reads less shared memory per MAC).
 // Tile width: the BN (a multiple of 32 from 128 to 256; tcgen05 needs N % 16
 // == 0 at M = 128, the epilogue reads 32 TMEM columns at a time) that
 // minimises rounds-of-tiles x BN over the persistent grid, larger BN on ties
-// (fewer shared-memory bytes per MMA).  MRI_GEMM_BN overrides.
+// (fewer shared-memory bytes per MMA).  The context's MRI_OPT_GEMM_BN forces one.
 int pick_bn(const DeviceInfo& dev, size_t M, size_t N) {
-  if (const char* e = std::getenv("MRI_GEMM_BN")) {
-    const int v = std::atoi(e);
-    if (v >= 128 && v <= 256 && v % 32 == 0) return v;
-  }
+  const int v = dev.opt.gemm_bn;
+  if (v >= 128 && v <= 256 && v % 32 == 0) return v;
   const size_t mt = (M + BM - 1) / BM;
   int best = 128;
   size_t best_cost = ~size_t(0);
@@ -516,7 +504,7 @@ cudaError_t launch_bn(const DeviceInfo& dev, cudaStream_t st, const CUtensorMap&
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  cfg.numAttrs = dev.opt.pdl ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, gemm_i8_tc_kernel<BN, kStages, kBufs>, ta, tb, act_scale, per_row, w_scales,
                             out, acc_out, static_cast<int>(M), static_cast<int>(N),
                             static_cast<int>(K), status, residual);
@@ -531,6 +519,42 @@ bool gemm_i8_tc_supported(const DeviceInfo& dev, size_t M, size_t N, size_t K) {
   return encode_fn() != nullptr;
 }
 
+// Stage counts keep the ring within the 227 KB a CTA may use.
+static int persistent_stages(int bn) {
+  switch (bn) {
+    case 128: return 6;
+    case 160: return 5;
+    case 192: return 5;
+    case 224: return 4;
+    default: return 4;
+  }
+}
+
+cudaError_t gemm_i8_tc_plan(const DeviceInfo& dev, size_t M, size_t N, size_t K, GemmPlan* plan) {
+  if (!gemm_i8_tc_supported(dev, M, N, K)) return cudaErrorInvalidValue;
+  GemmPlan p;
+  p.bn = pick_bn(dev, M, N);
+  p.tiles = static_cast<int>(((M + BM - 1) / BM) * ((N + p.bn - 1) / p.bn));
+  // Between one and two rounds of tiles, one tile per CTA with two CTAs per
+  // SM (3-stage rings, one accumulator buffer each): the second CTA's loads
+  // and MMAs fill the first one's gaps, and each CTA's epilogue overlaps the
+  // other's main loop.  The context's MRI_OPT_GEMM_2CTA = 0 keeps the
+  // persistent grid.
+  if (dev.opt.gemm_2cta && (p.bn == 128 || p.bn == 160) && p.tiles > dev.sm_count &&
+      p.tiles <= 2 * dev.sm_count) {
+    p.bufs = 1;
+    p.stages = 3;
+    p.grid = p.tiles;
+  } else {
+    p.bufs = 2;
+    p.stages = persistent_stages(p.bn);
+    p.grid = std::min(p.tiles, dev.sm_count);
+  }
+  p.tiles_per_cta = (p.tiles + p.grid - 1) / p.grid;
+  *plan = p;
+  return cudaSuccess;
+}
+
 cudaError_t launch_gemm_i8_tc(const DeviceInfo& dev, cudaStream_t st, const int8_t* xq,
                               const float* act_scale_dev, int scale_per_row, const int8_t* W,
                               const float* w_scales, size_t M, size_t N, size_t K, float* out,
@@ -538,44 +562,24 @@ cudaError_t launch_gemm_i8_tc(const DeviceInfo& dev, cudaStream_t st, const int8
                               const float* residual) {
   if ((reinterpret_cast<uintptr_t>(xq) & 15) || (reinterpret_cast<uintptr_t>(W) & 15))
     return cudaErrorMisalignedAddress;
-  const int bn = pick_bn(dev, M, N);
+  GemmPlan p;
+  if (cudaError_t e = gemm_i8_tc_plan(dev, M, N, K, &p)) return e;
   CUtensorMap ta, tb;
-  if (!make_map(&ta, xq, M, K, BM) || !make_map(&tb, W, N, K, bn)) return cudaErrorInvalidValue;
-  // Stage counts keep the ring within the 227 KB a CTA may use.
+  if (!make_map(&ta, xq, M, K, BM) || !make_map(&tb, W, N, K, p.bn)) return cudaErrorInvalidValue;
   cudaError_t e;
-#define MRI_GEMM_BN_CASE(BNV, ST)                                                              \
-  case BNV:                                                                                    \
-    e = launch_bn<BNV, ST>(dev, st, ta, tb, act_scale_dev, scale_per_row, w_scales, M, N, K, out, \
-                           acc_out, status, residual);                                         \
-    break;
-  // Between one and two rounds of tiles, one tile per CTA with two CTAs per
-  // SM (3-stage rings, one accumulator buffer each): the second CTA's loads
-  // and MMAs fill the first one's gaps, and each CTA's epilogue overlaps the
-  // other's main loop.  MRI_GEMM_2CTA=0 keeps the persistent grid.
-  static const bool two_cta = [] {
-    const char* v = std::getenv("MRI_GEMM_2CTA");
-    return v == nullptr || std::atoi(v) != 0;
-  }();
-  const size_t tiles = ((M + BM - 1) / BM) * ((N + bn - 1) / bn);
-  if (two_cta && (bn == 128 || bn == 160) && tiles > static_cast<size_t>(dev.sm_count) &&
-      tiles <= 2 * static_cast<size_t>(dev.sm_count)) {
-    e = bn == 128 ? launch_bn<128, 3, 1>(dev, st, ta, tb, act_scale_dev, scale_per_row, w_scales, M, N, K,
-                                         out, acc_out, status, residual)
-                  : launch_bn<160, 3, 1>(dev, st, ta, tb, act_scale_dev, scale_per_row, w_scales, M, N, K,
-                                         out, acc_out, status, residual);
-    if (ls) ls->launches++;
-    return e;
+#define MRI_GEMM_ARGS dev, st, ta, tb, act_scale_dev, scale_per_row, w_scales, M, N, K, out, acc_out, status, residual
+  if (p.bufs == 1) {
+    e = p.bn == 128 ? launch_bn<128, 3, 1>(MRI_GEMM_ARGS) : launch_bn<160, 3, 1>(MRI_GEMM_ARGS);
+  } else {
+    switch (p.bn) {
+      case 128: e = launch_bn<128, 6>(MRI_GEMM_ARGS); break;
+      case 160: e = launch_bn<160, 5>(MRI_GEMM_ARGS); break;
+      case 192: e = launch_bn<192, 5>(MRI_GEMM_ARGS); break;
+      case 224: e = launch_bn<224, 4>(MRI_GEMM_ARGS); break;
+      default: e = launch_bn<256, 4>(MRI_GEMM_ARGS);
+    }
   }
-  switch (bn) {
-    MRI_GEMM_BN_CASE(128, 6)
-    MRI_GEMM_BN_CASE(160, 5)
-    MRI_GEMM_BN_CASE(192, 5)
-    MRI_GEMM_BN_CASE(224, 4)
-    default:
-      e = launch_bn<256, 4>(dev, st, ta, tb, act_scale_dev, scale_per_row, w_scales, M, N, K, out,
-                            acc_out, status, residual);
-  }
-#undef MRI_GEMM_BN_CASE
+#undef MRI_GEMM_ARGS
   if (ls) ls->launches++;
   return e;
 }

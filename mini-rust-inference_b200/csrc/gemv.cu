@@ -1466,29 +1466,6 @@ __global__ void __launch_bounds__(256) gemv_q4_0_generic_kernel(const uint8_t* _
 
 // ── host side: layouts, attributes, dispatch on M ────────────────────────────
 
-// Launch tuning, read once from the environment (defaults are the measured
-// best on B200; the variables exist for sweeps):
-//   MRI_GEMV_SMEM_KB   shared-memory budget per CTA for the stage ring
-//   MRI_GEMV_CTAS_PER_SM  persistent CTAs per SM
-//   MRI_PDL            1 = programmatic dependent launch between kernels
-struct GemvTuning {
-  size_t smem_budget = 0;  // 0 = automatic (see pick_config)
-  int ctas_per_sm = 0;     // 0 = automatic
-  bool pdl = true;
-};
-
-const GemvTuning& tuning() {
-  static GemvTuning t = [] {
-    GemvTuning v;
-    if (const char* e = std::getenv("MRI_GEMV_SMEM_KB")) v.smem_budget = std::strtoul(e, nullptr, 10) * 1024;
-    if (const char* e = std::getenv("MRI_GEMV_CTAS_PER_SM")) v.ctas_per_sm = std::max(1, std::atoi(e));
-    if (const char* e = std::getenv("MRI_PDL")) v.pdl = std::atoi(e) != 0;
-    v.smem_budget = std::min<size_t>(v.smem_budget, kSmemBudget);
-    return v;
-  }();
-  return t;
-}
-
 int stages_within(size_t fixed_bytes, size_t stage_bytes, size_t budget) {
   for (int s = kMaxStages; s >= 2; --s) {
     const StreamLayout L = make_layout(0, 0, stage_bytes, s);
@@ -1506,20 +1483,14 @@ struct StreamConfig {
 };
 
 StreamConfig pick_config(size_t fixed_bytes, size_t stage_bytes) {
-  const GemvTuning& t = tuning();
   StreamConfig c;
-  if (t.smem_budget) {
-    c.stages = stages_within(fixed_bytes, stage_bytes, t.smem_budget);
-    c.ctas_per_sm = t.ctas_per_sm ? t.ctas_per_sm : 1;
-    return c;
-  }
   c.stages = std::min(4, stages_within(fixed_bytes, stage_bytes, 112 * 1024));
   if (c.stages >= 3) {
-    c.ctas_per_sm = t.ctas_per_sm ? t.ctas_per_sm : 2;
+    c.ctas_per_sm = 2;
     return c;
   }
   c.stages = stages_within(fixed_bytes, stage_bytes, kSmemBudget);
-  c.ctas_per_sm = t.ctas_per_sm ? t.ctas_per_sm : 1;
+  c.ctas_per_sm = 1;
   return c;
 }
 
@@ -1574,10 +1545,11 @@ int resident_ctas(KernelT k, size_t smem, int device, int threads = kThreads) {
   return n;
 }
 
-// Launch with the programmatic-stream-serialization attribute when enabled.
+// Launch with the programmatic-stream-serialization attribute when the
+// context's MRI_OPT_PDL is on.
 template <int Threads = kThreads, typename... KArgs, typename... Args>
-cudaError_t launch_stream_kernel(void (*k)(KArgs...), int grid, size_t smem, cudaStream_t st,
-                                 Args&&... args) {
+cudaError_t launch_stream_kernel(const DeviceInfo& dev, void (*k)(KArgs...), int grid, size_t smem,
+                                 cudaStream_t st, Args&&... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(Threads);
@@ -1587,13 +1559,13 @@ cudaError_t launch_stream_kernel(void (*k)(KArgs...), int grid, size_t smem, cud
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = tuning().pdl ? 1 : 0;
+  cfg.numAttrs = dev.opt.pdl ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, k, std::forward<Args>(args)...);
 }
 
 template <typename... KArgs, typename... Args>
-cudaError_t launch_stream_kernel_threads(void (*k)(KArgs...), int grid, int threads, cudaStream_t st,
-                                         Args... args) {
+cudaError_t launch_stream_kernel_threads(const DeviceInfo& dev, void (*k)(KArgs...), int grid, int threads,
+                                         cudaStream_t st, Args... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(threads);
@@ -1602,7 +1574,7 @@ cudaError_t launch_stream_kernel_threads(void (*k)(KArgs...), int grid, int thre
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = tuning().pdl ? 1 : 0;
+  cfg.numAttrs = dev.opt.pdl ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, k, static_cast<KArgs>(args)...);
 }
 
@@ -1691,16 +1663,11 @@ int reg_vec(int M, size_t K, const ActArgs* act) {
     });                                                                                     \
   }
 
-// Weight stages a producer issues before the activation loads are in flight
-// (MRI_GEMV_PRE_STAGES; default 1: the activation loads of a decode step then
-// queue behind one stage per CTA instead of the whole ring).
-int pre_stages(int stages) {
-  static const int v = [] {
-    const char* e = std::getenv("MRI_GEMV_PRE_STAGES");
-    return e ? std::max(0, std::atoi(e)) : 1;
-  }();
-  return std::min(v, stages);
-}
+// Weight stages a producer issues before the activation loads are in flight:
+// one, so that the activation loads of a decode step queue behind one stage
+// per CTA instead of the whole ring (swept 0..3 on the 7B decode chain: 488,
+// 505, 500, 484 tok/s).
+int pre_stages(int stages) { return std::min(1, stages); }
 
 cudaError_t gemv_i8_tma_plan(const DeviceInfo& dev, int M, size_t N, size_t K, GemvPlan* plan,
                              int vec, int epi) {
@@ -1749,7 +1716,7 @@ cudaError_t launch_gemv_i8_tma(const DeviceInfo& dev, cudaStream_t st, int M, co
     // dependent launch can only start once every CTA of this grid has
     // started.  A cooperative launch would also serialise it against the
     // previous kernel, which costs more than the wait saves.
-    cudaError_t e = launch_stream_kernel(kKernel, p.grid, p.smem, st, W, w_scales, N, K, act, out,
+    cudaError_t e = launch_stream_kernel(dev, kKernel, p.grid, p.smem, st, W, w_scales, N, K, act, out,
                                          acc_out, p.stages, p.k_chunks, pre, status, residual, e_args);
     if (e != cudaSuccess) return e;
   });
@@ -1794,7 +1761,7 @@ cudaError_t launch_gather_collect(const DeviceInfo& dev, cudaStream_t st, const 
                                   int* status, LaunchStats* ls) {
   const size_t total = static_cast<size_t>(M) * e.g_ntotal;
   const int grid = static_cast<int>(std::max<size_t>(1, std::min<size_t>(dev.sm_count, (total + 1023) / 1024)));
-  cudaError_t err = launch_stream_kernel_threads(gather_collect_kernel, grid, 256, st,
+  cudaError_t err = launch_stream_kernel_threads(dev, gather_collect_kernel, grid, 256, st,
                                                  static_cast<const unsigned long long*>(e.g_ctr[e.g_rank]),
                                                  static_cast<const unsigned long long*>(e.g_seq),
                                                  static_cast<const float*>(e.g_stage[e.g_rank]), e.g_half, total,
@@ -1824,12 +1791,8 @@ bool gemv_q8_0_tma_supported(const DeviceInfo&, int M, size_t K) {
 // The MMA Q8_0 kernel covers M = 2..8 when nb % 8 == 0 (16-byte aligned
 // rows, an equal block range per dot warp), nb <= 8 * kQ8MmaMaxBpw and three
 // stages fit.
-bool q8_0_mma_supported(int M, size_t K) {
-  static const bool off = [] {
-    const char* e = std::getenv("MRI_Q8_MMA");
-    return e != nullptr && std::atoi(e) == 0;
-  }();
-  if (off || M < 2 || M > 8 || K == 0 || K % 32 != 0) return false;
+bool q8_0_mma_supported(const DeviceInfo& dev, int M, size_t K) {
+  if (!dev.opt.q8_mma || M < 2 || M > 8 || K == 0 || K % 32 != 0) return false;
   const size_t nb = K / 32;
   if (nb % kQ8MmaDotWarps != 0 || nb > static_cast<size_t>(kQ8MmaDotWarps * kQ8MmaMaxBpw)) return false;
   return stages_within(fixed_bytes_of(q8_mma_term_bytes(nb), 64), kRowsPerStage * q8_mma_row_stride(nb),
@@ -1839,7 +1802,7 @@ bool q8_0_mma_supported(int M, size_t K) {
 cudaError_t launch_gemv_q8_0_mma(const DeviceInfo& dev, cudaStream_t st, int M, const uint8_t* W,
                                  size_t N, size_t K, const int8_t* xq, const float* x_scales,
                                  float* out, int* status, LaunchStats* ls) {
-  if (!q8_0_mma_supported(M, K) || (reinterpret_cast<uintptr_t>(xq) & 15) != 0 ||
+  if (!q8_0_mma_supported(dev, M, K) || (reinterpret_cast<uintptr_t>(xq) & 15) != 0 ||
       (reinterpret_cast<uintptr_t>(W) & 15) != 0)
     return cudaErrorInvalidValue;
   const size_t nb = K / 32;
@@ -1861,7 +1824,7 @@ cudaError_t launch_gemv_q8_0_mma(const DeviceInfo& dev, cudaStream_t st, int M, 
   }
   cudaError_t e = set_smem(kern, smem, dev.device);
   if (e != cudaSuccess) return e;
-  e = launch_stream_kernel<kQ8MmaThreads>(kern, stream_grid(dev, N, 1), smem, st, W, N, K, xq, x_scales,
+  e = launch_stream_kernel<kQ8MmaThreads>(dev, kern, stream_grid(dev, N, 1), smem, st, W, N, K, xq, x_scales,
                                           out, stages, status);
   if (e != cudaSuccess) return e;
   if (ls) ls->launches++;
@@ -1889,7 +1852,7 @@ cudaError_t launch_gemv_q8_0_tma(const DeviceInfo& dev, cudaStream_t st, int M, 
       if (e != cudaSuccess) return e;
       const int grid =
           stream_grid(dev, N, std::min(cfg.ctas_per_sm, resident_ctas(kern, smem, dev.device)));
-      e = launch_stream_kernel(kern, grid, smem, st, W, N, K, x, out, stages, pre, status);
+      e = launch_stream_kernel(dev, kern, grid, smem, st, W, N, K, x, out, stages, pre, status);
       if (e != cudaSuccess) return e;
     });
   });
@@ -1926,7 +1889,7 @@ cudaError_t launch_gemv_q4_0_tma(const DeviceInfo& dev, cudaStream_t st, int M, 
     if (e != cudaSuccess) return e;
     const int grid = stream_grid(
         dev, N, std::min(cfg.ctas_per_sm, resident_ctas(gemv_q4_0_tma_kernel<kM>, smem, dev.device)));
-    e = launch_stream_kernel(gemv_q4_0_tma_kernel<kM>, grid, smem, st, W, N, K, x, out, stages,
+    e = launch_stream_kernel(dev, gemv_q4_0_tma_kernel<kM>, grid, smem, st, W, N, K, x, out, stages,
                              pre_stages(stages), status);
     if (e != cudaSuccess) return e;
   });
@@ -1943,19 +1906,15 @@ int q4_0_mma_stages(int M, size_t K) {
                                             kRowsPerStage * q4_mma_row_stride(nb), kSmemBudget));
 }
 
-bool q4_0_mma_supported(int M, size_t K) {
-  static const bool off = [] {
-    const char* e = std::getenv("MRI_Q4_MMA");
-    return e != nullptr && std::atoi(e) == 0;
-  }();
-  if (off || M < 2 || M > 8 || K == 0 || K % 32 != 0) return false;
+bool q4_0_mma_supported(const DeviceInfo& dev, int M, size_t K) {
+  if (!dev.opt.q4_mma || M < 2 || M > 8 || K == 0 || K % 32 != 0) return false;
   if ((K / 32) % kQ4MmaDotWarps != 0) return false;
   return q4_0_mma_stages(M, K) >= 3;
 }
 
 size_t q4_0_split_bytes(size_t m, size_t K) { return m * q4_split_row_bytes(K); }
 
-cudaError_t launch_q4_0_split(const DeviceInfo&, cudaStream_t st, const float* x, size_t m, size_t K,
+cudaError_t launch_q4_0_split(const DeviceInfo& dev, cudaStream_t st, const float* x, size_t m, size_t K,
                               uint32_t* xs, LaunchStats* ls) {
   if ((reinterpret_cast<uintptr_t>(x) & 15) != 0 || (reinterpret_cast<uintptr_t>(xs) & 15) != 0 ||
       K % 4 != 0)
@@ -1963,7 +1922,7 @@ cudaError_t launch_q4_0_split(const DeviceInfo&, cudaStream_t st, const float* x
   const size_t n4 = m * (K / 4);
   if (n4 == 0) return cudaSuccess;
   const int grid = static_cast<int>((n4 + 255) / 256);
-  cudaError_t e = launch_stream_kernel_threads(q4_split_act_kernel, grid, 256, st, x, m, K, xs);
+  cudaError_t e = launch_stream_kernel_threads(dev, q4_split_act_kernel, grid, 256, st, x, m, K, xs);
   if (ls) ls->launches++;
   return e;
 }
@@ -1971,7 +1930,7 @@ cudaError_t launch_q4_0_split(const DeviceInfo&, cudaStream_t st, const float* x
 cudaError_t launch_gemv_q4_0_mma(const DeviceInfo& dev, cudaStream_t st, int M, const uint8_t* W,
                                  size_t N, size_t K, const uint32_t* xs, float* out, int* status,
                                  LaunchStats* ls) {
-  if (!q4_0_mma_supported(M, K) || (reinterpret_cast<uintptr_t>(xs) & 15) != 0 ||
+  if (!q4_0_mma_supported(dev, M, K) || (reinterpret_cast<uintptr_t>(xs) & 15) != 0 ||
       (reinterpret_cast<uintptr_t>(W) & 15) != 0)
     return cudaErrorInvalidValue;
   const size_t nb = K / 32;
@@ -1991,7 +1950,7 @@ cudaError_t launch_gemv_q4_0_mma(const DeviceInfo& dev, cudaStream_t st, int M, 
   }
   cudaError_t e = set_smem(kern, smem, dev.device);
   if (e != cudaSuccess) return e;
-  e = launch_stream_kernel<kQ4MmaThreads>(kern, stream_grid(dev, N, 1), smem, st, W, N, K, xs, out,
+  e = launch_stream_kernel<kQ4MmaThreads>(dev, kern, stream_grid(dev, N, 1), smem, st, W, N, K, xs, out,
                                           stages, status);
   if (e != cudaSuccess) return e;
   if (ls) ls->launches++;

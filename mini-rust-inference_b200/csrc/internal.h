@@ -84,13 +84,29 @@ struct LaunchStats {
   unsigned long long launches = 0;
 };
 
-// Per-device properties the launchers need.
+// Kernel-variant options of a context (mri_ctx_set_option).  The defaults are
+// the measured best choices; the others exist so that every variant the
+// launchers can take is reachable, and tested, without a rebuild.  They are
+// set explicitly through the C ABI, never read from the environment.
+struct Options {
+  int pdl = 1;         // MRI_OPT_PDL: programmatic dependent launch between kernels
+  int gemm_bn = 0;     // MRI_OPT_GEMM_BN: 0 = tile width per shape, else 128..256 step 32
+  int gemm_2cta = 1;   // MRI_OPT_GEMM_2CTA: one tile per CTA, two CTAs per SM, between one and two rounds of tiles
+  int q8_mma = 1;      // MRI_OPT_Q8_MMA: Q8_0 at m = 2..8 on the integer warp MMA
+  int q4_mma = 1;      // MRI_OPT_Q4_MMA: Q4_0 at m = 2..8 on the bf16 warp MMA
+  int tc_attn = 1;     // MRI_OPT_TC_ATTN: tensor-core prefill attention (head dim 64 / 128)
+  int fa_split = 3;    // MRI_OPT_FA_SPLIT: key tiles from which a prefill key walk is split (0 = never)
+  int shard_peer = 0;  // MRI_OPT_SHARD_PEER: sharded m <= 8 gathered over peer memory instead of NCCL
+};
+
+// Per-device properties the launchers need, and the context's options.
 struct DeviceInfo {
   int device = 0;
   int sm_count = 0;
   int max_smem_optin = 0;
   int cc_major = 0, cc_minor = 0;
   size_t l2_bytes = 0;
+  Options opt;
 };
 
 // ── quantizer (quant.cu) ─────────────────────────────────────────────────────
@@ -146,7 +162,7 @@ cudaError_t launch_gemv_q8_0_tma(const DeviceInfo& dev, cudaStream_t st, int M, 
 // M = 2..8 with the activations quantized per row beforehand (xq [M, K],
 // 16-byte aligned, and x_scales [M] on the device): block dots on the warp
 // MMA.  q8_0_mma_supported tells where the kernel applies.
-bool q8_0_mma_supported(int M, size_t K);
+bool q8_0_mma_supported(const DeviceInfo& dev, int M, size_t K);
 cudaError_t launch_gemv_q8_0_mma(const DeviceInfo& dev, cudaStream_t st, int M, const uint8_t* W,
                                  size_t N, size_t K, const int8_t* xq, const float* x_scales,
                                  float* out, int* status, LaunchStats* ls);
@@ -160,7 +176,7 @@ cudaError_t launch_gemv_q8_0_generic(const DeviceInfo& dev, cudaStream_t st, int
 // aligned) as split bf16 pairs in fragment order (q4_0_split_bytes(m, K)
 // bytes, 16-byte aligned; a chunk of rows starts at row * q4_0_split_bytes(1,
 // K)), which launch_gemv_q4_0_mma then reads.
-bool q4_0_mma_supported(int M, size_t K);
+bool q4_0_mma_supported(const DeviceInfo& dev, int M, size_t K);
 size_t q4_0_split_bytes(size_t m, size_t K);
 cudaError_t launch_q4_0_split(const DeviceInfo& dev, cudaStream_t st, const float* x, size_t m,
                               size_t K, uint32_t* xs, LaunchStats* ls);
@@ -214,6 +230,14 @@ size_t int8_scratch_bytes(size_t m, size_t k);
 
 // ── tensor-core INT8 GEMM (gemm_tc.cu) ──────────────────────────────────────
 bool gemm_i8_tc_supported(const DeviceInfo& dev, size_t M, size_t N, size_t K);
+// Launch shape of the tensor-core GEMM for (M, N, K): tile width, ring
+// stages, TMEM accumulator buffers per CTA (2: persistent grid, a CTA walks
+// tiles t, t + grid, ...; 1: one tile per CTA, two CTAs per SM), grid,
+// tiles, and the most tiles one CTA takes.
+struct GemmPlan {
+  int bn = 0, stages = 0, bufs = 0, grid = 0, tiles = 0, tiles_per_cta = 0;
+};
+cudaError_t gemm_i8_tc_plan(const DeviceInfo& dev, size_t M, size_t N, size_t K, GemmPlan* plan);
 // xq [M,K] i8, W [N,K] i8 (both K-major), scale(s) in device memory.
 cudaError_t launch_gemm_i8_tc(const DeviceInfo& dev, cudaStream_t st, const int8_t* xq,
                               const float* act_scale_dev, int scale_per_row, const int8_t* W,

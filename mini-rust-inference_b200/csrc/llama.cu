@@ -665,29 +665,10 @@ __global__ void __launch_bounds__(kFaThreads) attn_prefill_tc_kernel(const float
   }
 }
 
-// Key tiles from which a query block's walk is split over two blocks
-// (MRI_FA_SPLIT; 0 = never).
-int fa_split_min() {
-  static const int v = [] {
-    const char* e = std::getenv("MRI_FA_SPLIT");
-    return e ? std::max(0, std::atoi(e)) : 3;
-  }();
-  return v;
-}
-
 // Dynamic shared memory of attn_prefill_tc_kernel<hd>: K and V^T tiles, hi and lo.
 size_t fa_smem_bytes(int hd) {
   return (2 * static_cast<size_t>(kFaKT) * (hd + 8) + 2 * static_cast<size_t>(hd) * (kFaKT + 8)) *
          sizeof(__half);
-}
-
-// MRI_TC_ATTN=0 keeps the CUDA-core prefill attention.
-bool tc_attn() {
-  static const bool on = [] {
-    const char* e = std::getenv("MRI_TC_ATTN");
-    return e == nullptr || std::atoi(e) != 0;
-  }();
-  return on;
 }
 
 // Greedy sampling: argmax (first index on ties; NaN never wins) -> next
@@ -883,7 +864,8 @@ BlobLayout blob_layout(const mri_llama* m) {
 
 // Launch with programmatic stream serialization (see the glue-kernel note).
 template <typename... KArgs, typename... Args>
-cudaError_t pdl_launch(void (*k)(KArgs...), dim3 grid, dim3 block, cudaStream_t st, Args... args) {
+cudaError_t pdl_launch(const mri_llama* m, void (*k)(KArgs...), dim3 grid, dim3 block, cudaStream_t st,
+                       Args... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
@@ -893,11 +875,7 @@ cudaError_t pdl_launch(void (*k)(KArgs...), dim3 grid, dim3 block, cudaStream_t 
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  static const bool pdl_on = [] {
-    const char* e = std::getenv("MRI_PDL");
-    return !e || std::atoi(e) != 0;
-  }();
-  cfg.numAttrs = pdl_on ? 1 : 0;
+  cfg.numAttrs = m->ctx->dev.opt.pdl ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, k, static_cast<KArgs>(args)...);
 }
 
@@ -945,20 +923,22 @@ int run_blocks(mri_llama* m, size_t rows, int pos0, bool decode_dev) {
     } else {
       if (int rc = proj(m, m->x, rows, m->wqkv[l], m->qkv, m->attn_norm + l * c.dim)) return rc;
       if (!decode_dev && m->hd % 4 == 0 && m->qkv_w % 4 == 0) {
-        LL_TRY(pdl_launch(rope_kv_rows_kernel, dim3(static_cast<unsigned>(rows)), dim3(256), st, m->qkv,
+        LL_TRY(pdl_launch(m, rope_kv_rows_kernel, dim3(static_cast<unsigned>(rows)), dim3(256), st, m->qkv,
                           m->qkv_w, c.n_heads, c.n_kv_heads, m->hd, m->rope_cos, m->rope_sin, pos0, kc, vc));
       } else {
-        LL_TRY(pdl_launch(rope_kv_kernel, dim3(static_cast<unsigned>(rows), c.n_heads + c.n_kv_heads),
+        LL_TRY(pdl_launch(m, rope_kv_kernel, dim3(static_cast<unsigned>(rows), c.n_heads + c.n_kv_heads),
                           dim3(64), st, m->qkv, m->qkv_w, c.n_heads, c.n_kv_heads, m->hd, m->rope_cos,
                           m->rope_sin, pos0, decode_dev ? m->d_pos : nullptr, kc, vc));
       }
     }
     if (decode_dev) {
-      LL_TRY(pdl_launch(attn_decode_kernel, dim3(c.n_heads, m->max_splits), dim3(128), st, m->qkv,
+      LL_TRY(pdl_launch(m, attn_decode_kernel, dim3(c.n_heads, m->max_splits), dim3(128), st, m->qkv,
                         c.n_heads, c.n_kv_heads, m->hd, kc, vc, m->d_pos, scale, m->part,
                         m->max_splits, m->tickets, m->attn));
-    } else if ((m->hd == 64 || m->hd == 128) && (m->qkv_w % 2) == 0 && (m->qd % 2) == 0 && tc_attn()) {
-      const int split_min = fa_split_min();
+    } else if ((m->hd == 64 || m->hd == 128) && (m->qkv_w % 2) == 0 && (m->qd % 2) == 0 &&
+               m->ctx->dev.opt.tc_attn) {
+      // Key tiles from which a query block's walk is split over two blocks (0 = never).
+      const int split_min = std::max(0, m->ctx->dev.opt.fa_split);
       const dim3 grid(c.n_heads, static_cast<unsigned>((rows + kFaQ - 1) / kFaQ) * (split_min > 0 ? 2 : 1));
       const size_t smem = fa_smem_bytes(m->hd);
       static bool fa_attr_set[64] = {false};
@@ -1035,7 +1015,7 @@ int prefill(mri_llama* m, const uint32_t* tokens, size_t n) {
 }
 
 int launch_argmax(mri_llama* m) {
-  LL_TRY(pdl_launch(argmax_kernel, dim3(kArgmaxBlocks), dim3(256), m->ctx->stream, m->logits,
+  LL_TRY(pdl_launch(m, argmax_kernel, dim3(kArgmaxBlocks), dim3(256), m->ctx->stream, m->logits,
                     static_cast<int>(m->cfg.vocab), m->amax_v, m->amax_i, m->tickets + m->cfg.n_heads,
                     m->d_tokens, m->d_pos, m->d_gen));
   return MRI_OK;
@@ -1045,7 +1025,7 @@ int launch_argmax(mri_llama* m) {
 // from *d_pos; ends with argmax -> d_tokens[0] and *d_pos += 1.
 int decode_step(mri_llama* m) {
   cudaStream_t st = m->ctx->stream;
-  LL_TRY(pdl_launch(embed_kernel, dim3(1), dim3(256), st, m->d_tokens, m->embd, m->cfg.dim, m->x));
+  LL_TRY(pdl_launch(m, embed_kernel, dim3(1), dim3(256), st, m->d_tokens, m->embd, m->cfg.dim, m->x));
   if (int rc = run_blocks(m, 1, 0, true)) return rc;
   if (int rc = lm_head(m, 0, 1)) return rc;
   return launch_argmax(m);

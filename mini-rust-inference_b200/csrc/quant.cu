@@ -24,16 +24,9 @@ __device__ __forceinline__ void pdl_enter() {
   asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
-bool quant_pdl() {
-  static const bool v = [] {
-    const char* e = std::getenv("MRI_PDL");
-    return !e || std::atoi(e) != 0;
-  }();
-  return v;
-}
-
 template <typename... KArgs, typename... Args>
-cudaError_t qlaunch(void (*k)(KArgs...), unsigned grid, cudaStream_t st, Args... args) {
+cudaError_t qlaunch(const DeviceInfo& dev, void (*k)(KArgs...), unsigned grid, cudaStream_t st,
+                    Args... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kQThreads);
@@ -42,7 +35,7 @@ cudaError_t qlaunch(void (*k)(KArgs...), unsigned grid, cudaStream_t st, Args...
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = quant_pdl() ? 1 : 0;
+  cfg.numAttrs = dev.opt.pdl ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, k, static_cast<KArgs>(args)...);
 }
 
@@ -417,12 +410,12 @@ cudaError_t launch_quantize(const DeviceInfo& dev, cudaStream_t st, const float*
     // amax_scratch holds 2 * max(m, kQuantPartials) floats: row maxima, then 1/rms.
     float* partial = amax_scratch;
     float* row_inv = amax_scratch + std::max(m, kQuantPartials);
-    cudaError_t e = qlaunch(row_stats_kernel, static_cast<unsigned>(m), st, x, k, norm_w, eps, swiglu,
+    cudaError_t e = qlaunch(dev, row_stats_kernel, static_cast<unsigned>(m), st, x, k, norm_w, eps, swiglu,
                             row_inv, partial);
     if (e != cudaSuccess) return e;
     const int apply_blocks = static_cast<int>(std::max<size_t>(
         1, std::min<size_t>(static_cast<size_t>(dev.sm_count) * 8, (n + kQThreads * 4 - 1) / (kQThreads * 4))));
-    e = qlaunch(quant_apply_xform_kernel, static_cast<unsigned>(apply_blocks), st, x, m, k, per_row,
+    e = qlaunch(dev, quant_apply_xform_kernel, static_cast<unsigned>(apply_blocks), st, x, m, k, per_row,
                 partial, norm_w, row_inv, swiglu, q, scale);
     if (ls) ls->launches += 2;
     return e;
@@ -437,7 +430,7 @@ cudaError_t launch_quantize(const DeviceInfo& dev, cudaStream_t st, const float*
   }
   if (per_row && k % 4 == 0 && k <= static_cast<size_t>(kRowVec) * kQThreads * 4 &&
       (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(q) & 3) == 0) {
-    cudaError_t e = qlaunch(quant_rows_kernel, static_cast<unsigned>(m), st, x, k, q, scale);
+    cudaError_t e = qlaunch(dev, quant_rows_kernel, static_cast<unsigned>(m), st, x, k, q, scale);
     if (ls) ls->launches++;
     return e;
   }
@@ -447,13 +440,13 @@ cudaError_t launch_quantize(const DeviceInfo& dev, cudaStream_t st, const float*
       1, std::min<size_t>(std::min<size_t>(static_cast<size_t>(dev.sm_count) * 2, kQuantPartials),
                           (n + kQThreads * 16 - 1) / (kQThreads * 16))));
   cudaError_t e = per_row
-                      ? qlaunch(absmax_row_kernel, static_cast<unsigned>(m), st, x, k, amax_scratch)
-                      : qlaunch(absmax_tensor_kernel, static_cast<unsigned>(blocks), st, x, n, amax_scratch);
+                      ? qlaunch(dev, absmax_row_kernel, static_cast<unsigned>(m), st, x, k, amax_scratch)
+                      : qlaunch(dev, absmax_tensor_kernel, static_cast<unsigned>(blocks), st, x, n, amax_scratch);
   if (e != cudaSuccess) return e;
   if (ls) ls->launches++;
   const int apply_blocks = static_cast<int>(std::max<size_t>(
       1, std::min<size_t>(static_cast<size_t>(dev.sm_count) * 8, (n + kQThreads * 4 - 1) / (kQThreads * 4))));
-  e = qlaunch(quant_apply_kernel, static_cast<unsigned>(apply_blocks), st, x, m, k, per_row,
+  e = qlaunch(dev, quant_apply_kernel, static_cast<unsigned>(apply_blocks), st, x, m, k, per_row,
               amax_scratch, blocks, q, scale);
   if (ls) ls->launches++;
   return e;

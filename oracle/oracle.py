@@ -46,7 +46,7 @@ def lib():
             "oref_dot_i8_scalar": (ctypes.c_int32, [_P, _P, _SZ]),
             "oref_matmul_int8_avx2": (ctypes.c_int, [_P, _SZ, ctypes.c_float, _P, _P, _SZ, _SZ, _SZ, _P]),
             "oref_matmul_int8_parallel": (ctypes.c_int, [_P, _SZ, ctypes.c_float, _P, _P, _SZ, _SZ, _SZ, _P,
-                                                         ctypes.c_int]),
+                                                         ctypes.c_int, _P]),
             "oref_f16_to_f32": (ctypes.c_float, [ctypes.c_uint16]),
             "oref_f32_to_f16": (ctypes.c_uint16, [ctypes.c_float]),
             "oref_create_q8_0_block": (None, [_P, _P]),
@@ -174,14 +174,19 @@ def matmul_int8_avx2(act_q, act_scale, w_data, w_scales, n_out, k_in, m):
     return out
 
 
-# parallel.rs:308-346
-def matmul_int8_parallel(act_q, act_scale, w_data, w_scales, n_out, k_in, m, n_threads=0, out=None):
+# parallel.rs:308-346.  acc_out (optional int32 [m, n_out]) receives the dots
+# before the epilogue (a checker's addition, for INT32 comparisons at sizes
+# the scalar matmul_int8 is too slow for).
+def matmul_int8_parallel(act_q, act_scale, w_data, w_scales, n_out, k_in, m, n_threads=0, out=None,
+                         acc_out=None):
     act_q = _i8(act_q).ravel()
     if out is None:
         out = np.empty((m, n_out), dtype=np.float32)
+    if acc_out is not None:
+        assert acc_out.dtype == np.int32 and acc_out.size == m * n_out and acc_out.flags["C_CONTIGUOUS"]
     _check(lib().oref_matmul_int8_parallel(_ptr(act_q), act_q.size, ctypes.c_float(act_scale),
                                            _ptr(_i8(w_data)), _ptr(_f32(w_scales)), n_out, k_in, m,
-                                           _ptr(out), int(n_threads)))
+                                           _ptr(out), int(n_threads), _ptr(acc_out)))
     return out
 
 

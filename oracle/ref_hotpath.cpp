@@ -195,9 +195,12 @@ int oref_hardware_threads(void) {
 // ops/matmul/parallel.rs:308-346.  rayon's par_chunks_mut(n) hands out one
 // output row per task; here a fixed pool pulls row indices from an atomic
 // counter.  At m == 1 exactly one thread works, as in the reference.
+// acc_out (nullable, not in the reference's signature) receives the i32 dot
+// of every (row, column) before the epilogue, for checks of INT32 sums.
 int oref_matmul_int8_parallel(const int8_t* act_q, size_t act_len, float act_scale,
                               const int8_t* w, const float* scales, size_t n_out,
-                              size_t k_in, size_t m, float* out, int n_threads) {
+                              size_t k_in, size_t m, float* out, int n_threads,
+                              int32_t* acc_out) {
   if (act_len != m * k_in) return OREF_INVALID_SHAPE;
   size_t threads = n_threads > 0 ? static_cast<size_t>(n_threads)
                                  : static_cast<size_t>(oref_hardware_threads());
@@ -212,6 +215,7 @@ int oref_matmul_int8_parallel(const int8_t* act_q, size_t act_len, float act_sca
       float* out_row = out + mi * n_out;
       for (size_t ni = 0; ni < n_out; ++ni) {
         const int32_t acc = oref_dot_i8_avx2(a_row, w + ni * k_in, k_in);
+        if (acc_out) acc_out[mi * n_out + ni] = acc;
         out_row[ni] = (static_cast<float>(acc) * act_scale) * scales[ni];
       }
     }

@@ -64,10 +64,12 @@ int oref_matmul_int8_avx2(const int8_t* act_q, size_t act_len, float act_scale,
                           size_t k_in, size_t m, float* out);
 
 /* ops/matmul/parallel.rs:308-346: one task per output row m (rayon
- * par_chunks_mut(n)); n_threads <= 0 means all hardware threads. */
+ * par_chunks_mut(n)); n_threads <= 0 means all hardware threads.  acc_out
+ * (nullable; a checker's addition) receives the i32 sums [m, n_out]. */
 int oref_matmul_int8_parallel(const int8_t* act_q, size_t act_len, float act_scale,
                               const int8_t* w, const float* scales, size_t n_out,
-                              size_t k_in, size_t m, float* out, int n_threads);
+                              size_t k_in, size_t m, float* out, int n_threads,
+                              int32_t* acc_out);
 
 /* gguf/quantization.rs:416-461 and :464-498 */
 float oref_f16_to_f32(uint16_t h);

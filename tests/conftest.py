@@ -37,3 +37,18 @@ def gpu_ctx(mri):
     if not torch.cuda.is_available():
         pytest.fail("GPU test collected on a machine without CUDA")
     return mri.default_context(0)
+
+
+@pytest.fixture
+def ctx_option(gpu_ctx):
+    """set(option, value): a kernel-variant option of the default context for
+    the duration of one test (restored afterwards)."""
+    saved = []
+
+    def set_(option, value):
+        saved.append((option, gpu_ctx.get_option(option)))
+        gpu_ctx.set_option(option, value)
+
+    yield set_
+    for option, value in reversed(saved):
+        gpu_ctx.set_option(option, value)

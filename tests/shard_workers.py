@@ -52,11 +52,10 @@ def gloo_shard_worker(rank, world, port, m, n, k, seed, results):
         dist.destroy_process_group()
 
 
-def nccl_shard_worker(rank, world, results, uid, ms, n, k, seed, env=None):
+def nccl_shard_worker(rank, world, results, uid, ms, n, k, seed, peer=0):
     """Runs the sharded product for every m in `ms` (same sequence on every
-    rank) and reports {m: output}.  `env` is applied before the library loads
-    (MRI_SHARD_PEER=0 selects the NCCL path for small m)."""
-    os.environ.update(env or {})
+    rank) and reports {m: output}.  `peer` is the context's OPT_SHARD_PEER
+    (0: small m gathered by NCCL, 1: over peer memory)."""
     import torch
 
     from conftest import load_mri
@@ -65,6 +64,7 @@ def nccl_shard_worker(rank, world, results, uid, ms, n, k, seed, env=None):
         mri = load_mri()
         torch.cuda.set_device(rank)
         ctx = mri.Context(rank)
+        ctx.set_option(mri.OPT_SHARD_PEER, peer)
         comm = mri.Communicator(uid, world, rank, ctx=ctx, timeout_ms=60000)
         outs = {}
         for m in ms:
@@ -84,7 +84,6 @@ def peer_timeout_worker(rank, world, results, uid, n, k, done):
     rank 1 skips.  Rank 0's kernel must give up waiting for rank 1's arrivals
     (bounded wait) and report a timeout.  Rank 1 stays alive, with its buffers
     mapped and no work in flight, until rank 0 is done."""
-    os.environ["MRI_SHARD_PEER"] = "1"
     import torch
 
     from conftest import load_mri
@@ -93,6 +92,7 @@ def peer_timeout_worker(rank, world, results, uid, n, k, done):
         mri = load_mri()
         torch.cuda.set_device(rank)
         ctx = mri.Context(rank)
+        ctx.set_option(mri.OPT_SHARD_PEER, 1)
         comm = mri.Communicator(uid, world, rank, ctx=ctx, timeout_ms=60000)
         x, wq, ws = problem(1, n, k, 5)
         w = mri.shard_quantized_matrix(wq.reshape(-1), ws, n, k, comm)

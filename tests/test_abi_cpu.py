@@ -129,3 +129,14 @@ def test_dequantize_codecs_match_oracle(mri, oracle):
     b4 = oracle.quantize_q4_0_matrix(w, 3, 64)
     assert np.array_equal(mri.formats.dequantize_q8_0(b8), oracle.dequantize_q8_0(b8))
     assert np.array_equal(mri.formats.dequantize_q4_0(b4), oracle.dequantize_q4_0(b4))
+
+
+@pytest.mark.parametrize("m,k", [((4 << 20) // 1024 + 1, 1024), ((1 << 60) + 1, 16), (1, (4 << 20) + 16)])
+def test_noalloc_size_check_precedes_device_work(mri, m, k):
+    """The allocation-free entry point rejects an input larger than its fixed
+    array before it touches the device (null pointers, no GPU here), also
+    when m * k would wrap around in 64 bits."""
+    lib = mri._lib.load()
+    rc = lib.mri_matmul_int8_from_f32_noalloc(None, m, k, None, None, 8, None, None)
+    assert rc == 6  # MRI_ERR_INVALID_ARGUMENT
+    assert b"exceed the fixed scratch" in lib.mri_noalloc_last_error()

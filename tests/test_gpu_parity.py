@@ -326,10 +326,10 @@ def test_prefill_shape_sampled_rows_exact(mri, oracle, gpu_ctx):
 
 
 @pytest.mark.parametrize("bn", [128, 160, 192, 224, 256])
-def test_gemm_tile_widths_exact(mri, oracle, gpu_ctx, monkeypatch, bn):
-    """Every tensor-core tile width (MRI_GEMM_BN) gives the oracle's INT32
+def test_gemm_tile_widths_exact(mri, oracle, ctx_option, bn):
+    """Every tensor-core tile width (OPT_GEMM_BN) gives the oracle's INT32
     sums and f32 outputs on ragged M and N, with a residual-free epilogue."""
-    monkeypatch.setenv("MRI_GEMM_BN", str(bn))
+    ctx_option(mri.OPT_GEMM_BN, bn)
     rng = np.random.default_rng(100 + bn)
     m, n, k = 333, 1000, 4096 + 256
     aq = rng.integers(-127, 128, size=m * k, dtype=np.int8)
@@ -344,11 +344,11 @@ def test_gemm_tile_widths_exact(mri, oracle, gpu_ctx, monkeypatch, bn):
 
 
 @pytest.mark.parametrize("bn", [128, 160])
-def test_gemm_two_ctas_per_sm_exact(mri, oracle, gpu_ctx, monkeypatch, bn):
+def test_gemm_two_ctas_per_sm_exact(mri, oracle, ctx_option, bn):
     """Between one and two rounds of tiles (here 196 or 244 tiles on 148 SMs)
     the GEMM runs one tile per CTA, two CTAs per SM: same INT32 sums and f32
     outputs as the oracle on ragged M and N."""
-    monkeypatch.setenv("MRI_GEMM_BN", str(bn))
+    ctx_option(mri.OPT_GEMM_BN, bn)
     rng = np.random.default_rng(200 + bn)
     m, n, k = 500, 7717, 1024 + 256
     aq = rng.integers(-127, 128, size=m * k, dtype=np.int8)
@@ -367,8 +367,8 @@ def test_gemm_two_ctas_per_sm_exact(mri, oracle, gpu_ctx, monkeypatch, bn):
 # direct per-row stores); the cases below leave acc_out out so that the staged
 # stores are the ones checked, on full and ragged blocks.
 @pytest.mark.parametrize("bn", [128, 160, 192, 224, 256])
-def test_gemm_staged_epilogue_exact(mri, oracle, gpu_ctx, monkeypatch, bn):
-    monkeypatch.setenv("MRI_GEMM_BN", str(bn))
+def test_gemm_staged_epilogue_exact(mri, oracle, ctx_option, bn):
+    ctx_option(mri.OPT_GEMM_BN, bn)
     rng = np.random.default_rng(300 + bn)
     m, n, k = 333, 1000, 4096 + 256
     aq = rng.integers(-127, 128, size=m * k, dtype=np.int8)
@@ -381,10 +381,10 @@ def test_gemm_staged_epilogue_exact(mri, oracle, gpu_ctx, monkeypatch, bn):
 
 
 @pytest.mark.parametrize("bn", [128, 160])
-def test_gemm_two_ctas_per_sm_staged_exact(mri, oracle, gpu_ctx, monkeypatch, bn):
+def test_gemm_two_ctas_per_sm_staged_exact(mri, oracle, ctx_option, bn):
     """One tile per CTA, two CTAs per SM: the output block is staged in the
     (then idle) stage ring."""
-    monkeypatch.setenv("MRI_GEMM_BN", str(bn))
+    ctx_option(mri.OPT_GEMM_BN, bn)
     rng = np.random.default_rng(400 + bn)
     m, n, k = 500, 7717, 1024 + 256
     aq = rng.integers(-127, 128, size=m * k, dtype=np.int8)

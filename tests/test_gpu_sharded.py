@@ -1,8 +1,9 @@
 """N-sharded INT8 product on the GPU (mri_sharded_matmul_int8_from_f32).
 
-Bar: bit-exact against the unsharded product.  Each output element comes
-from the same kernels on the same weight row and the same per-tensor
-activation scale; the NCCL all-gather moves f32 values unchanged.
+Bar: bit-exact against the oracle's unsharded product (proj_int8_par,
+forward_int8.rs:87-96).  Each output element comes from the same kernels on
+the same weight row and the same per-tensor activation scale; the NCCL
+all-gather moves f32 values unchanged.
 """
 import multiprocessing as mp
 import time
@@ -16,6 +17,14 @@ import shard_workers
 pytestmark = pytest.mark.gpu
 
 
+def oracle_product(oracle, x, wq, ws, n, k):
+    """proj_int8_par (forward_int8.rs:87-96): quantize_symmetric over the
+    whole input, then matmul_int8_parallel (parallel.rs:308-346)."""
+    m = x.shape[0]
+    aq, s = oracle.quantize_symmetric(x)
+    return oracle.matmul_int8_parallel(aq, s, wq.reshape(-1), ws, n, k, m)
+
+
 @pytest.fixture(scope="module")
 def comm1(mri, gpu_ctx):
     if not mri.comm_available():
@@ -26,17 +35,16 @@ def comm1(mri, gpu_ctx):
 
 
 @pytest.mark.parametrize("m", [1, 3, 8, 300, 1100])
-def test_single_rank_matches_unsharded(mri, gpu_ctx, comm1, m):
+def test_single_rank_matches_unsharded(mri, gpu_ctx, comm1, oracle, m):
     n, k = 1024, 512
     x, wq, ws = shard_workers.problem(m, n, k, 11 + m)
-    full = mri.QuantizedMatrix(wq.reshape(-1), ws, n, k, ctx=gpu_ctx)
     shard = mri.shard_quantized_matrix(wq.reshape(-1), ws, n, k, comm1)
     xd = torch.from_numpy(x).cuda()
-    want = mri.matmul_int8_from_f32(xd, full)
+    want = oracle_product(oracle, x, wq, ws, n, k)
     got = mri.matmul_int8_from_f32_sharded(xd, shard, n, comm1)
     comm1.wait()
     gpu_ctx.synchronize()
-    np.testing.assert_array_equal(got.cpu().numpy(), want.cpu().numpy())
+    np.testing.assert_array_equal(got.cpu().numpy().view(np.uint32), want.view(np.uint32))
 
 
 @pytest.mark.parametrize("p", [2, 4, 8])
@@ -53,11 +61,33 @@ def test_emulated_shards_concatenate_to_unsharded(mri, gpu_ctx, oracle, p, m):
         w = mri.QuantizedMatrix(wq.reshape(-1), ws, n, k, ctx=gpu_ctx, rows=(b, e))
         parts.append(mri.matmul_int8_from_f32(xd, w).cpu().numpy())
     got = np.concatenate(parts, axis=1)
-    if m <= 8:
-        want = oracle.matmul_int8_from_f32(x, m, k, wq.reshape(-1), ws, n, k)
-    else:
-        want = mri.matmul_int8_from_f32(xd, mri.QuantizedMatrix(wq.reshape(-1), ws, n, k, ctx=gpu_ctx)).cpu().numpy()
-    np.testing.assert_array_equal(got, want)
+    want = oracle_product(oracle, x, wq, ws, n, k)
+    np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+@pytest.mark.parametrize("m", [1, 300])
+@pytest.mark.parametrize("which", ["gate_up", "down"])
+def test_emulated_70b_shards_match_oracle(mri, gpu_ctx, oracle, which, m):
+    """The Llama-70B FFN projections (gate/up W [28672, 8192], down W [8192,
+    28672]) cut into the 8 shards of an 8-GPU node, each shard's product
+    computed on this GPU, concatenated along N: the oracle's unsharded
+    product bit for bit."""
+    n, k = (28672, 8192) if which == "gate_up" else (8192, 28672)
+    p = 8
+    rng = np.random.default_rng(70 + m)
+    x = rng.normal(0, 1, size=(m, k)).astype(np.float32)
+    wq = rng.integers(-127, 128, size=n * k, dtype=np.int8)
+    ws = rng.uniform(0.001, 0.02, size=n).astype(np.float32)
+    xd = torch.from_numpy(x).cuda()
+    parts = []
+    for r in range(p):
+        b, e = mri.shard_rows(n, p, r)
+        w = mri.QuantizedMatrix(wq, ws, n, k, ctx=gpu_ctx, rows=(b, e))
+        parts.append(mri.matmul_int8_from_f32(xd, w).cpu().numpy())
+        del w
+    got = np.concatenate(parts, axis=1)
+    want = oracle_product(oracle, x, wq, ws, n, k)
+    np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
 
 
 def test_sharded_argument_errors(mri, gpu_ctx, comm1):
@@ -97,24 +127,22 @@ def _run_two(target, args):
 @pytest.mark.parametrize("path", ["peer", "nccl"])
 def test_two_ranks_match_unsharded(mri, gpu_ctx, oracle, path):
     """Two GPUs: m = 1 and 4 through the peer-memory gather
-    (MRI_SHARD_PEER=1) or NCCL, m = 300 through the chunked NCCL all-gather;
-    every rank's result equals the unsharded product bit for bit."""
+    (OPT_SHARD_PEER = 1) or NCCL, m = 300 through the chunked NCCL all-gather;
+    every rank's result equals the oracle's unsharded product bit for bit."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     n, k, seed, ms = 4096, 2048, 3, (1, 4, 300, 1)
-    env = {"MRI_SHARD_PEER": "0" if path == "nccl" else "1"}
-    got = _run_two(shard_workers.nccl_shard_worker, (mri.Communicator.unique_id(), ms, n, k, seed, env))
+    peer = 0 if path == "nccl" else 1
+    got = _run_two(shard_workers.nccl_shard_worker, (mri.Communicator.unique_id(), ms, n, k, seed, peer))
     for r in range(2):
         assert not isinstance(got[r], str), got[r]
         for m in ms:
             x, wq, ws = shard_workers.problem(m, n, k, seed + m)
-            if m <= 8:
-                want = oracle.matmul_int8_from_f32(x, m, k, wq.reshape(-1), ws, n, k)
-            else:
-                xd = torch.from_numpy(x).cuda()
-                want = mri.matmul_int8_from_f32(xd, mri.QuantizedMatrix(wq.reshape(-1), ws, n, k,
-                                                                       ctx=gpu_ctx)).cpu().numpy()
-            np.testing.assert_array_equal(got[r][m], want)
+            # proj_int8_par (forward_int8.rs:87-96): quantize_symmetric over
+            # the whole input, then matmul_int8_parallel.
+            aq, s = oracle.quantize_symmetric(x)
+            want = oracle.matmul_int8_parallel(aq, s, wq.reshape(-1), ws, n, k, m)
+            np.testing.assert_array_equal(got[r][m].view(np.uint32), want.view(np.uint32))
 
 
 def test_peer_gather_wait_is_bounded(mri):

@@ -1,0 +1,223 @@
+"""Every kernel variant the benchmarks run, pinned to the oracle at the
+benchmarked shapes (INT8 bars: INT32 sums and f32 outputs bit-exact).
+
+Each test first asks the library which launch shape it will use for the shape
+(mri_int8_gemm_plan / mri_int8_gemv_plan) and asserts that it is the variant
+the test is meant to cover, so a change of dispatch cannot silently move a
+benchmarked path out from under its test.  The oracle here is
+matmul_int8_parallel (parallel.rs:308-346) with its INT32 sums, which equals
+the scalar matmul_int8 (int8.rs:61-98) element for element and finishes
+these sizes in seconds on the host's cores.
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def bits(a):
+    return np.ascontiguousarray(a, dtype=np.float32).view(np.uint32)
+
+
+def weights(rng, n, k):
+    wq = rng.integers(-127, 128, size=n * k, dtype=np.int8)
+    ws = rng.uniform(0.001, 0.02, size=n).astype(np.float32)
+    return wq, ws
+
+
+def oracle_from_f32(oracle, x, wq, ws, n, k):
+    """matmul_int8_from_f32 (int8.rs:113-143) as proj_int8_par runs it
+    (forward_int8.rs:87-96): per-tensor quantize_symmetric, then the
+    row-parallel product; returns (out, acc)."""
+    m = x.shape[0]
+    aq, s = oracle.quantize_symmetric(x)
+    acc = np.empty((m, n), np.int32)
+    out = oracle.matmul_int8_parallel(aq, s, wq, ws, n, k, m, acc_out=acc)
+    return out, acc, aq, s
+
+
+def check_prequantized(mri, oracle, aq, s, wq, ws, qm, m, n, k):
+    """matmul_int8 with the INT32 sums requested (direct-store epilogue)."""
+    acc = np.zeros((m, n), np.int32)
+    got = mri.matmul_int8(aq, s, qm, m, acc_out=acc)
+    want_acc = np.empty((m, n), np.int32)
+    want = oracle.matmul_int8_parallel(aq, s, wq, ws, n, k, m, acc_out=want_acc)
+    assert np.array_equal(acc, want_acc), f"{np.count_nonzero(acc != want_acc)} INT32 sums differ"
+    assert np.array_equal(bits(got), bits(want))
+
+
+# ── tensor-core GEMM ─────────────────────────────────────────────────────────
+
+# (m, n, k): the 7B prefill gate/up GEMM at 1024 rows, and a Llama-70B gate/up
+# shard of an 8-GPU node at 2048 rows (N = 28672 / 8).
+PERSISTENT_SHAPES = [(1024, 11008, 4096), (2048, 3584, 8192)]
+
+
+@pytest.mark.parametrize("m,n,k", PERSISTENT_SHAPES)
+def test_gemm_persistent_multi_tile_exact(mri, oracle, gpu_ctx, m, n, k):
+    """The persistent grid with two TMEM accumulator buffers and three or
+    more tiles per CTA (tile t + 1's MMAs run while tile t drains; the
+    buffers alternate and wait on the epilogue's release).  Every row, both
+    epilogues: the staged f32 stores (no INT32 copy) through
+    matmul_int8_from_f32, and the direct stores with INT32 sums."""
+    plan = gpu_ctx.int8_gemm_plan(m, n, k)
+    assert plan["acc_buffers"] == 2 and plan["tiles_per_cta"] >= 3, plan
+    assert plan["grid"] <= 148, plan
+    rng = np.random.default_rng(m + n)
+    x = rng.normal(0, 1, size=(m, k)).astype(np.float32)
+    wq, ws = weights(rng, n, k)
+    qm = mri.QuantizedMatrix(wq, ws, n, k)
+    want, want_acc, aq, s = oracle_from_f32(oracle, x, wq, ws, n, k)
+    got = mri.matmul_int8_from_f32(x, qm)
+    assert np.array_equal(bits(got), bits(want)), f"{np.count_nonzero(bits(got) != bits(want))} outputs differ"
+    acc = np.zeros((m, n), np.int32)
+    got = mri.matmul_int8(aq, s, qm, m, acc_out=acc)
+    assert np.array_equal(acc, want_acc)
+    assert np.array_equal(bits(got), bits(want))
+
+
+def test_gemm_persistent_grid_when_two_cta_off(mri, oracle, gpu_ctx, ctx_option):
+    """OPT_GEMM_2CTA = 0 between one and two rounds of tiles (the prefill
+    shape, 276 tiles): the persistent grid, two tiles on most CTAs, every
+    row against the oracle."""
+    m, n, k = 512, 11008, 4096
+    assert gpu_ctx.int8_gemm_plan(m, n, k)["acc_buffers"] == 1
+    ctx_option(mri.OPT_GEMM_2CTA, 0)
+    plan = gpu_ctx.int8_gemm_plan(m, n, k)
+    assert plan["acc_buffers"] == 2 and plan["tiles_per_cta"] == 2 and plan["grid"] == 148, plan
+    rng = np.random.default_rng(5)
+    x = rng.normal(0, 1, size=(m, k)).astype(np.float32)
+    wq, ws = weights(rng, n, k)
+    qm = mri.QuantizedMatrix(wq, ws, n, k)
+    want, want_acc, aq, s = oracle_from_f32(oracle, x, wq, ws, n, k)
+    assert np.array_equal(bits(mri.matmul_int8_from_f32(x, qm)), bits(want))
+    acc = np.zeros((m, n), np.int32)
+    got = mri.matmul_int8(aq, s, qm, m, acc_out=acc)
+    assert np.array_equal(acc, want_acc)
+    assert np.array_equal(bits(got), bits(want))
+
+
+@pytest.fixture(scope="module")
+def prefill_case(mri, oracle):
+    """BASELINE prefill config: A from N(0,1) activations [512, 4096], B the
+    per-channel quantization of N(0, 0.02) weights [11008, 4096]; seed 1."""
+    rng = np.random.default_rng(1)
+    m, n, k = 512, 11008, 4096
+    x = rng.normal(0, 1, size=(m, k)).astype(np.float32)
+    wf = rng.normal(0, 0.02, size=(n, k)).astype(np.float32)
+    wq, ws = oracle.quantize_per_channel(wf, n, k)
+    return x, wq, ws, m, n, k
+
+
+def test_prefill_all_rows_per_tensor(mri, oracle, gpu_ctx, prefill_case):
+    """matmul_int8_from_f32 at the prefill config (two CTAs per SM, one tile
+    each, staged epilogue): all 512 x 11008 outputs bit-equal to the oracle,
+    and all INT32 sums through matmul_int8."""
+    x, wq, ws, m, n, k = prefill_case
+    plan = gpu_ctx.int8_gemm_plan(m, n, k)
+    assert plan["acc_buffers"] == 1 and plan["grid"] == plan["tiles"], plan
+    qm = mri.QuantizedMatrix(wq, ws, n, k)
+    want, want_acc, aq, s = oracle_from_f32(oracle, x, wq, ws, n, k)
+    assert np.array_equal(bits(mri.matmul_int8_from_f32(x, qm)), bits(want))
+    check_prequantized(mri, oracle, aq, s, wq, ws, qm, m, n, k)
+
+
+def test_prefill_all_rows_per_row(mri, oracle, gpu_ctx, prefill_case):
+    """The per-row granularity BASELINE's prefill config names (each
+    activation row quantized with its own scale, q8_direct.rs:260-264), all
+    rows: out[m, n] = ((f32)acc * s_a[m]) * s_w[n] with the oracle's sums
+    and per-row scales."""
+    x, wq, ws, m, n, k = prefill_case
+    qm = mri.QuantizedMatrix(wq, ws, n, k)
+    got = mri.matmul_int8_from_f32(x, qm, granularity=mri.PER_ROW)
+    aq, sr = oracle.quantize_symmetric_rows(x, m, k)
+    acc = np.empty((m, n), np.int32)
+    oracle.matmul_int8_parallel(aq, np.float32(1.0), wq, ws, n, k, m, acc_out=acc)
+    want = (acc.astype(np.float32) * sr[:, None]).astype(np.float32) * ws[None, :]
+    assert np.array_equal(bits(got), bits(want))
+
+
+# ── streaming GEMV at the benchmarked long-K shapes ──────────────────────────
+
+# (m, n, k): the 7B down projection (K = 11008) at 1 and 8 rows, the 70B down
+# projection (K = 28672) at 1 and 8 rows, and the 70B gate/up (K = 8192).
+GEMV_SHAPES = [(1, 4096, 11008), (8, 4096, 11008), (1, 8192, 28672), (8, 8192, 28672), (1, 28672, 8192)]
+
+
+@pytest.mark.parametrize("m,n,k", GEMV_SHAPES)
+def test_gemv_long_k_exact(mri, oracle, gpu_ctx, m, n, k):
+    """The streaming INT8 GEMV with K-chunked stages: the register prologue
+    (width 12) where the input fits it, else the quantize-first path (the
+    quantizer kernels, then int8 activations streamed with the device scale).
+    f32 input through matmul_int8_from_f32, and pre-quantized input with the
+    INT32 sums, against the oracle."""
+    assert gpu_ctx.int8_path(m, n, k) == 0
+    plan = gpu_ctx.int8_gemv_plan(m, n, k)
+    assert plan["grid"] <= plan["ctas_per_sm"] * 148, plan
+    assert plan["ctas_per_sm"] <= plan["resident_ctas"], plan
+    if k >= 11008:
+        assert plan["k_chunks"] > 1, plan
+    if (m, k) == (1, 11008):
+        assert plan["reg_vec"] == 12 and plan["quantize_first"] == 0, plan
+    if k == 28672 or m == 8:
+        assert plan["reg_vec"] == 0 and plan["quantize_first"] == 1, plan
+    rng = np.random.default_rng(m * 7 + k)
+    x = rng.normal(0, 1, size=(m, k)).astype(np.float32)
+    wq, ws = weights(rng, n, k)
+    qm = mri.QuantizedMatrix(wq, ws, n, k)
+    want, _, aq, s = oracle_from_f32(oracle, x, wq, ws, n, k)
+    assert np.array_equal(bits(mri.matmul_int8_from_f32(x, qm)), bits(want))
+    check_prequantized(mri, oracle, aq, s, wq, ws, qm, m, n, k)
+
+
+def test_pdl_off_same_results(mri, oracle, ctx_option):
+    """OPT_PDL = 0 (every kernel launched without programmatic dependent
+    launch): the decode GEMV and the prefill GEMM give the oracle's outputs."""
+    ctx_option(mri.OPT_PDL, 0)
+    rng = np.random.default_rng(77)
+    for m, n, k in ((1, 11008, 4096), (300, 2000, 4096)):
+        x = rng.normal(0, 1, size=(m, k)).astype(np.float32)
+        wq, ws = weights(rng, n, k)
+        want, _, _, _ = oracle_from_f32(oracle, x, wq, ws, n, k)
+        got = mri.matmul_int8_from_f32(x, mri.QuantizedMatrix(wq, ws, n, k))
+        assert np.array_equal(bits(got), bits(want))
+
+
+# ── Q8_0 / Q4_0 at 2..8 rows without the warp-MMA kernels ────────────────────
+
+@pytest.mark.parametrize("m", [2, 8])
+def test_q8_0_streaming_kernel_when_mma_off(mri, oracle, ctx_option, m):
+    """OPT_Q8_MMA = 0: Q8_0 at m = 2..8 on the streaming kernel (per-row
+    quantization in its prologue, dp4a block dots), bit-exact."""
+    ctx_option(mri.OPT_Q8_MMA, 0)
+    rng = np.random.default_rng(30 + m)
+    n, k = 2048, 4096
+    wb = oracle.quantize_q8_0_matrix(rng.normal(0, 0.02, size=(n, k)).astype(np.float32), n, k)
+    x = rng.normal(0, 1, size=(m, k)).astype(np.float32)
+    got = mri.matmul_q8_0_direct(x, mri.Q8_0WeightMatrix.from_raw_bytes(wb, n, k))
+    want = oracle.matmul_q8_0_direct(x, m, k, wb, n, k)
+    assert np.array_equal(bits(got), bits(want))
+
+
+@pytest.mark.parametrize("m", [2, 8])
+def test_q4_0_streaming_kernel_when_mma_off(mri, oracle, ctx_option, m):
+    """OPT_Q4_MMA = 0: Q4_0 at m = 2..8 on the CUDA-core streaming kernel,
+    within 1e-3 relative (absolute floor 1e-5 * sum |x * w|)."""
+    from test_gpu_parity import q4_close
+    ctx_option(mri.OPT_Q4_MMA, 0)
+    rng = np.random.default_rng(40 + m)
+    n, k = 2048, 4096
+    wb = oracle.quantize_q4_0_matrix(rng.normal(0, 0.02, size=(n, k)).astype(np.float32), n, k)
+    x = rng.normal(0, 1, size=(m, k)).astype(np.float32)
+    got = mri.matmul_q4_0_dequant(x, wb, n, k)
+    want = oracle.matmul_q4_0_dequant(x, m, k, wb, n, k)
+    ok, worst = q4_close(got, want, x, oracle.dequantize_q4_0(wb).reshape(n, k))
+    assert ok, worst
+
+
+def test_options_reject_bad_values(mri, gpu_ctx):
+    with pytest.raises(ValueError):
+        gpu_ctx.set_option(mri.OPT_GEMM_BN, 100)
+    with pytest.raises(ValueError):
+        gpu_ctx.set_option(99, 1)
+    assert gpu_ctx.get_option(mri.OPT_PDL) == 1

@@ -4,7 +4,10 @@ It exists for callers that cannot allocate device memory at call time: its
 scratch is a fixed device array inside the library instead of a context's
 growing buffer.  Through the C ABI it must agree with the regular entry point
 (mri_matmul_int8_from_f32) bit for bit, on consecutive calls that reuse the
-same scratch, and reject inputs larger than the array.
+same scratch, on each of its paths (the streaming GEMV with the input
+quantized in its prologue, the GEMV after quantizing a long input into the
+array, the tensor-core GEMM), leave its sticky status word clear, and reject
+inputs larger than the array.
 
 This file is named so that pytest collects it last.
 """
@@ -38,7 +41,9 @@ def _run_pair(mri, lib, ctx, m, n, k, x_scale, seed):
                                               n, ctypes.c_void_p(out_na.data_ptr()),
                                               ctypes.c_void_p(stream.cuda_stream))
     assert rc == 0, lib.mri_noalloc_last_error().decode()
-    torch.cuda.synchronize()
+    # No bounded wait gave up (this also synchronizes the stream).
+    rc = lib.mri_noalloc_check_status(ctypes.c_void_p(stream.cuda_stream))
+    assert rc == 0, lib.mri_noalloc_last_error().decode()
     a = out_ref.cpu().numpy().view(np.uint32)
     b = out_na.cpu().numpy().view(np.uint32)
     assert np.array_equal(a, b), f"m={m}: {np.count_nonzero(a != b)} of {a.size} outputs differ"
@@ -54,14 +59,28 @@ def test_noalloc_matches_regular_entry_on_consecutive_calls(mri):
     _run_pair(mri, lib, ctx, 37, 520, 2048, 0.25, seed=2)
 
 
+def test_noalloc_decode_rows_match_regular_entry(mri):
+    """1 and 8 rows (streaming GEMV, input quantized in its prologue), then a
+    long input (K = 28672, quantized into the array first), then one row
+    again: each against the regular entry point."""
+    lib = mri._lib.load()
+    ctx = mri.Context(0)
+    _run_pair(mri, lib, ctx, 1, 11008, 4096, 1.0, seed=3)
+    _run_pair(mri, lib, ctx, 8, 1000, 4096, 3.0, seed=4)
+    _run_pair(mri, lib, ctx, 1, 2048, 28672, 0.5, seed=5)
+    _run_pair(mri, lib, ctx, 1, 300, 1024, 2.0, seed=6)
+
+
 def test_noalloc_rejects_oversized_input(mri):
     import torch
     lib = mri._lib.load()
     cap = 4 << 20
-    m, k = cap // 1024 + 1, 1024
     x = torch.zeros(1, device="cuda")
-    rc = lib.mri_matmul_int8_from_f32_noalloc(ctypes.c_void_p(x.data_ptr()), m, k,
-                                              ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(x.data_ptr()),
-                                              8, ctypes.c_void_p(x.data_ptr()), None)
-    assert rc == 6  # MRI_ERR_INVALID_ARGUMENT, before any launch
-    assert b"exceeds the fixed scratch" in lib.mri_noalloc_last_error()
+    # One row too many, and a size whose product m * k wraps around to a
+    # small number in 64 bits (2^60 + 1 rows of 16).
+    for m, k in ((cap // 1024 + 1, 1024), ((1 << 60) + 1, 16)):
+        rc = lib.mri_matmul_int8_from_f32_noalloc(ctypes.c_void_p(x.data_ptr()), m, k,
+                                                  ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(x.data_ptr()),
+                                                  8, ctypes.c_void_p(x.data_ptr()), None)
+        assert rc == 6  # MRI_ERR_INVALID_ARGUMENT, before any launch
+        assert b"exceed the fixed scratch" in lib.mri_noalloc_last_error()

@@ -261,8 +261,33 @@ MRI_API int mri_llama_load_tensor(mri_llama* m, int role, uint32_t layer, int gg
 /* Synthetic weights generated on the device (benchmarking only). */
 MRI_API int mri_llama_init_random(mri_llama* m, uint64_t seed);
 /* LlamaModelInt8::forward (forward_int8.rs:516-529): logits [n, vocab]; also
- * fills the KV cache for positions [0, n). */
+ * fills the KV cache for positions [0, n).
+ * Prefill attention runs on the tensor cores with q, k and v split into f16
+ * high and low parts.  A call that meets a q, k or v value beyond the f16
+ * range (|v| > 65504) or a NaN is run again with the f32 CUDA-core attention
+ * (mri_llama_attention_fallbacks counts such calls); this holds for
+ * mri_llama_forward_at and mri_llama_generate_greedy too. */
 MRI_API int mri_llama_forward(mri_llama* m, const uint32_t* tokens, size_t n, float* logits);
+/* The block loop of TransformerBlockInt8::forward_cached_parallel
+ * (forward_int8.rs:232-249, with forward_cached :206-215) at start_pos for
+ * every layer, then the output norm and head: the n tokens take positions
+ * [start_pos, start_pos + n), their K/V rows are written to the cache there,
+ * and each attends to cache rows [0, its position] — rows [0, start_pos)
+ * must hold an earlier prefill or decode of the same sequence.  Logits
+ * [n, vocab].  start_pos + n > max_seq -> MRI_ERR_INVALID_SHAPE.  (The
+ * reference's MIN_PARALLEL_SEQ switch, :243-246, only chooses its thread
+ * schedule; both of its paths give the same numbers, as does this one.) */
+MRI_API int mri_llama_forward_at(mri_llama* m, const uint32_t* tokens, size_t n, size_t start_pos,
+                                 float* logits);
+/* TransformerBlockInt8::forward_cached_parallel(x, start_pos, cache, layer)
+ * (forward_int8.rs:232-249; equal to forward_cached :206-215): one block of
+ * layer `layer` on the host input x [n, dim] at positions [start_pos,
+ * start_pos + n), with the model's KV cache standing for `cache[layer]`
+ * (rows written there, rows [0, start_pos) read).  out [n, dim] (may alias
+ * x).  Synchronous.  layer >= n_layers, n == 0 or start_pos + n > max_seq ->
+ * MRI_ERR_INVALID_SHAPE. */
+MRI_API int mri_llama_block_forward(mri_llama* m, uint32_t layer, const float* x, size_t n,
+                                    size_t start_pos, float* out);
 /* LlamaModelInt8::forward_decode (forward_int8.rs:538-546): logits [vocab]. */
 MRI_API int mri_llama_forward_decode(mri_llama* m, uint32_t token, size_t pos, float* logits);
 /* Prefill the prompt into the cache (an addition: the reference has no
@@ -273,6 +298,14 @@ MRI_API int mri_llama_generate_greedy(mri_llama* m, const uint32_t* prompt, size
                                       size_t n_decode, uint32_t* out_tokens, float* prefill_ms,
                                       float* decode_ms);
 MRI_API int mri_llama_launches_per_decode_step(const mri_llama* m, size_t* count);
+/* No counterpart in the reference.  A model starts with the kernel-variant
+ * options of the context it was created on; this sets one for the model
+ * alone (mri_ctx_set_option semantics; a captured decode graph keeps the
+ * variant it was captured with). */
+MRI_API int mri_llama_set_option(mri_llama* m, int option, int value);
+/* No counterpart in the reference.  Calls run again with the f32 prefill
+ * attention because a q, k or v value left the f16 range. */
+MRI_API int mri_llama_attention_fallbacks(const mri_llama* m, size_t* count);
 
 /* ── allocation-free entry point ───────────────────────────────────────────── */
 /* No counterpart in the reference.  For callers that cannot allocate device

@@ -764,6 +764,38 @@ class LlamaModelInt8:
         _check_model(self._lib.mri_llama_forward(self.handle, _vp(t), t.size, _vp(out)), self._lib)
         return out
 
+    def forward_at(self, tokens, start_pos):
+        """The block loop of TransformerBlockInt8::forward_cached_parallel
+        (forward_int8.rs:232-249) at `start_pos`: the tokens take positions
+        [start_pos, start_pos + len), write their K/V cache rows there and
+        attend to the cache from row 0.  Logits [len(tokens), vocab]."""
+        t = np.ascontiguousarray(tokens, np.uint32)
+        out = np.empty((t.size, self.cfg.vocab), np.float32)
+        _check_model(self._lib.mri_llama_forward_at(self.handle, _vp(t), t.size, int(start_pos), _vp(out)),
+                     self._lib)
+        return out
+
+    def block_forward(self, layer, x, start_pos):
+        """TransformerBlockInt8::forward_cached_parallel(x, start_pos, cache,
+        layer) (forward_int8.rs:232-249) with the model's KV cache: x f32
+        [n, dim] -> [n, dim]."""
+        xa = np.ascontiguousarray(x, np.float32).reshape(-1, self.cfg.dim)
+        out = np.empty_like(xa)
+        _check_model(self._lib.mri_llama_block_forward(self.handle, int(layer), _vp(xa), xa.shape[0],
+                                                       int(start_pos), _vp(out)), self._lib)
+        return out
+
+    def set_option(self, option, value):
+        """A kernel-variant option (OPT_*) for this model alone."""
+        _check_model(self._lib.mri_llama_set_option(self.handle, int(option), int(value)), self._lib)
+
+    def attention_fallbacks(self):
+        """Calls run again with the f32 prefill attention (q, k or v beyond
+        the f16 range)."""
+        n = ctypes.c_size_t()
+        _check_model(self._lib.mri_llama_attention_fallbacks(self.handle, ctypes.byref(n)), self._lib)
+        return n.value
+
     def forward_decode(self, token, pos):
         """forward_int8.rs:538-546: logits [vocab] for `token` at `pos` (the
         cache must hold positions [0, pos))."""

@@ -84,6 +84,10 @@ SIGNATURES = {
     "mri_llama_load_tensor": (_I, [_P, _I, ctypes.c_uint32, _I, _P, _SZ, _SZ, _SZ]),
     "mri_llama_init_random": (_I, [_P, ctypes.c_uint64]),
     "mri_llama_forward": (_I, [_P, _P, _SZ, _P]),
+    "mri_llama_forward_at": (_I, [_P, _P, _SZ, _SZ, _P]),
+    "mri_llama_block_forward": (_I, [_P, ctypes.c_uint32, _P, _SZ, _SZ, _P]),
+    "mri_llama_set_option": (_I, [_P, _I, _I]),
+    "mri_llama_attention_fallbacks": (_I, [_P, ctypes.POINTER(_SZ)]),
     "mri_llama_forward_decode": (_I, [_P, ctypes.c_uint32, _SZ, _P]),
     "mri_llama_generate_greedy": (_I, [_P, _P, _SZ, _SZ, _P, _P, _P]),
     "mri_llama_launches_per_decode_step": (_I, [_P, ctypes.POINTER(_SZ)]),

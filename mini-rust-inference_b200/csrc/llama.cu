@@ -392,8 +392,9 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(const float* __restri
 // f16 operands) flips enough of those roundings to move the logits by a few
 // percent of their range.  The causal mask (key <= start + query), the scale
 // and the online softmax (running max, sum) are f32, per row over the 4
-// threads that hold it.  q, k and v must lie within the f16 range.  HD = head
-// dim (64 or 128).
+// threads that hold it.  HD = head dim (64 or 128).  q, k and v must lie
+// within the f16 range: a block that loads a value beyond it (or a NaN) sets
+// *range_flag, and the host runs the call again on the f32 CUDA-core kernel.
 constexpr int kFaQ = 128;  // queries per block (a warp per 16): each K/V tile is converted once per 128 queries
 constexpr int kFaThreads = 2 * kFaQ;
 constexpr int kFaKT = 64;  // keys per tile
@@ -401,6 +402,12 @@ constexpr int kFaKT = 64;  // keys per tile
 __device__ __forceinline__ uint32_t half2_bits(float lo, float hi) {
   const __half2 v = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+// True when either value is NaN or beyond the largest finite f16 (65504):
+// its f16 hi part would be infinite.
+__device__ __forceinline__ bool beyond_f16(float2 v) {
+  return !(fabsf(v.x) <= 65504.0f) | !(fabsf(v.y) <= 65504.0f);
 }
 
 // Two floats as f16 pairs hi = f16(x), lo = f16(x - hi).
@@ -426,7 +433,8 @@ __global__ void __launch_bounds__(kFaThreads) attn_prefill_tc_kernel(const float
                                                               const float* __restrict__ vc, float scale,
                                                               float* __restrict__ out, int out_ld,
                                                               float* __restrict__ part,
-                                                              int* __restrict__ tickets, int split_min) {
+                                                              int* __restrict__ tickets, int split_min,
+                                                              int* __restrict__ range_flag) {
   constexpr int KS = HD / 16;     // k steps of S = Q K^T
   constexpr int NT = HD / 8;      // n tiles of O
   constexpr int SK = HD + 8;      // halves per K row in shared memory
@@ -450,6 +458,7 @@ __global__ void __launch_bounds__(kFaThreads) attn_prefill_tc_kernel(const float
   const int ra = q0 + warp * 16 + g, rb = ra + 8;  // this thread's two query rows
   // Q fragments (rows ra, rb; dims 16k + 2t, +1 and 16k + 8 + 2t, +1), hi and lo.
   uint32_t qa[KS][4], ql[KS][4];
+  bool bad = false;  // a q, k or v value this thread converted lies beyond the f16 range
 #pragma unroll
   for (int k = 0; k < KS; ++k) {
     const int d0 = 16 * k + 2 * t;
@@ -464,11 +473,13 @@ __global__ void __launch_bounds__(kFaThreads) attn_prefill_tc_kernel(const float
       b = *reinterpret_cast<const float2*>(q + d0);
       e = *reinterpret_cast<const float2*>(q + d0 + 8);
     }
+    bad |= beyond_f16(a) | beyond_f16(b) | beyond_f16(c) | beyond_f16(e);
     split_half2(a, qa[k][0], ql[k][0]);
     split_half2(b, qa[k][1], ql[k][1]);
     split_half2(c, qa[k][2], ql[k][2]);
     split_half2(e, qa[k][3], ql[k][3]);
   }
+  if (bad) *reinterpret_cast<volatile int*>(range_flag) = 1;
   float o[NT][4];
 #pragma unroll
   for (int n = 0; n < NT; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
@@ -492,6 +503,8 @@ __global__ void __launch_bounds__(kFaThreads) attn_prefill_tc_kernel(const float
         const size_t off = static_cast<size_t>(kt + j) * kvd + kv_h * HD + d;
         kv = *reinterpret_cast<const float4*>(kc + off);
         vv = *reinterpret_cast<const float4*>(vc + off);
+        bad |= beyond_f16(make_float2(kv.x, kv.y)) | beyond_f16(make_float2(kv.z, kv.w)) |
+               beyond_f16(make_float2(vv.x, vv.y)) | beyond_f16(make_float2(vv.z, vv.w));
       }
       uint32_t h0, l0, h1, l1;
       split_half2(make_float2(kv.x, kv.y), h0, l0);
@@ -592,6 +605,7 @@ __global__ void __launch_bounds__(kFaThreads) attn_prefill_tc_kernel(const float
       }
     }
   }
+  if (bad) *reinterpret_cast<volatile int*>(range_flag) = 1;
   // Row sums over the 4 threads of a row, then O / l.
   l_a += __shfl_xor_sync(0xffffffffu, l_a, 1);
   l_a += __shfl_xor_sync(0xffffffffu, l_a, 2);
@@ -813,6 +827,9 @@ struct mri_llama {
   int* tickets = nullptr;      // [n_heads] decode-attention split counters, then 1 argmax counter
   float* fa_part = nullptr;    // prefill attention: two split records per (query block, head)
   int* fa_tickets = nullptr;   // prefill attention: split counters per (query block, head)
+  int* fa_range = nullptr;     // prefill attention: set when q, k or v lay beyond the f16 range
+  bool cuda_core_attn = false; // rerun after such a call: prefill attention on the f32 CUDA-core kernel
+  size_t attn_fallbacks = 0;   // calls rerun that way
   float* amax_v = nullptr;     // argmax partials
   int* amax_i = nullptr;
   bool fused_decode = false;   // decode projections carry the RoPE/KV and SwiGLU epilogues
@@ -898,13 +915,15 @@ int proj(mri_llama* m, const float* x, size_t rows, const mri_qmatrix& w, float*
 //   x   = x + proj(swiglu(proj(rmsnorm(x, ffn_norm), wgu)), wdown)  (:395-402)
 // The gate/up rows of wgu are interleaved.  In the fused decode step the RoPE
 // rotation, the cache write and the SwiGLU run in the projections' epilogues.
-int run_blocks(mri_llama* m, size_t rows, int pos0, bool decode_dev) {
+// Layers [l_begin, l_end) (all by default) on the residual stream m->x.
+int run_blocks(mri_llama* m, size_t rows, int pos0, bool decode_dev, uint32_t l_begin = 0,
+               uint32_t l_end = ~0u) {
   const auto& c = m->cfg;
   cudaStream_t st = m->ctx->stream;
   const float scale = 1.0f / std::sqrt(static_cast<float>(m->hd));
   const size_t layer_kv = static_cast<size_t>(c.max_seq) * m->kvd;
   const bool fused = decode_dev && m->fused_decode;
-  for (uint32_t l = 0; l < c.n_layers; ++l) {
+  for (uint32_t l = l_begin; l < std::min(l_end, c.n_layers); ++l) {
     float* kc = m->kc + l * layer_kv;
     float* vc = m->vc + l * layer_kv;
     if (fused) {
@@ -936,7 +955,7 @@ int run_blocks(mri_llama* m, size_t rows, int pos0, bool decode_dev) {
                         c.n_heads, c.n_kv_heads, m->hd, kc, vc, m->d_pos, scale, m->part,
                         m->max_splits, m->tickets, m->attn));
     } else if ((m->hd == 64 || m->hd == 128) && (m->qkv_w % 2) == 0 && (m->qd % 2) == 0 &&
-               m->ctx->dev.opt.tc_attn) {
+               m->ctx->dev.opt.tc_attn && !m->cuda_core_attn) {
       // Key tiles from which a query block's walk is split over two blocks (0 = never).
       const int split_min = std::max(0, m->ctx->dev.opt.fa_split);
       const dim3 grid(c.n_heads, static_cast<unsigned>((rows + kFaQ - 1) / kFaQ) * (split_min > 0 ? 2 : 1));
@@ -954,12 +973,12 @@ int run_blocks(mri_llama* m, size_t rows, int pos0, bool decode_dev) {
         attn_prefill_tc_kernel<64><<<grid, kFaThreads, smem, st>>>(m->qkv, m->qkv_w, c.n_heads, c.n_kv_heads,
                                                             static_cast<int>(rows), pos0, kc, vc, scale,
                                                             m->attn, m->qd, m->fa_part, m->fa_tickets,
-                                                            split_min);
+                                                            split_min, m->fa_range);
       else
         attn_prefill_tc_kernel<128><<<grid, kFaThreads, smem, st>>>(m->qkv, m->qkv_w, c.n_heads, c.n_kv_heads,
                                                              static_cast<int>(rows), pos0, kc, vc, scale,
                                                              m->attn, m->qd, m->fa_part, m->fa_tickets,
-                                                             split_min);
+                                                             split_min, m->fa_range);
     } else {
       const size_t smem = (kPrefillKT * (kMaxHeadDim + 1) + kPrefillKT * kMaxHeadDim +
                            kPrefillQ * kMaxHeadDim) * sizeof(float);
@@ -1006,12 +1025,44 @@ int check_tokens(const mri_llama* m, const uint32_t* tokens, size_t n) {
   return MRI_OK;
 }
 
-// Prefill `n` host tokens at positions [0, n) (writes the cache).
-int prefill(mri_llama* m, const uint32_t* tokens, size_t n) {
+// Prefill `n` host tokens at positions [pos0, pos0 + n): writes those cache
+// rows and attends to cache rows [0, pos0 + n).
+int prefill(mri_llama* m, const uint32_t* tokens, size_t n, size_t pos0 = 0) {
   cudaStream_t st = m->ctx->stream;
   LL_TRY(cudaMemcpyAsync(m->d_tokens, tokens, n * sizeof(uint32_t), cudaMemcpyHostToDevice, st));
   embed_kernel<<<static_cast<unsigned>(n), 256, 0, st>>>(m->d_tokens, m->embd, m->cfg.dim, m->x);
-  return run_blocks(m, n, 0, false);
+  return run_blocks(m, n, static_cast<int>(pos0), false);
+}
+
+// After the stream has drained: true (and the flag cleared) when a prefill
+// attention launch since the last check met a q, k or v value beyond the
+// f16 range.  The call that made it is then run again with the prefill
+// attention on the f32 CUDA-core kernel (m->cuda_core_attn), which rewrites
+// every buffer and cache row the first run wrote.
+bool take_range_flag(mri_llama* m) {
+  int v = 0;
+  if (cudaMemcpy(&v, m->fa_range, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess || v == 0) return false;
+  cudaMemset(m->fa_range, 0, sizeof(int));
+  return true;
+}
+
+// Prefill of `n` tokens at pos0 with logits of every row copied to the host
+// (LlamaModelInt8::forward at pos0 = 0; the block loop of
+// forward_cached_parallel at pos0 > 0).
+int forward_rows(mri_llama* m, const uint32_t* tokens, size_t n, size_t pos0, float* logits) {
+  for (int attempt = 0;; ++attempt) {
+    if (int rc = prefill(m, tokens, n, pos0)) return rc;
+    if (int rc = lm_head(m, 0, n)) return rc;
+    if (logits)
+      LL_TRY(cudaMemcpyAsync(logits, m->logits, n * m->cfg.vocab * 4, cudaMemcpyDeviceToHost,
+                             m->ctx->stream));
+    LL_TRY(cudaStreamSynchronize(m->ctx->stream));
+    const bool redo = attempt == 0 && take_range_flag(m);
+    m->cuda_core_attn = redo;
+    if (!redo) break;
+    m->attn_fallbacks++;
+  }
+  return mri_ctx_check_device_status(m->ctx) ? fail(MRI_ERR_TIMEOUT, "%s", mri_last_error()) : MRI_OK;
 }
 
 int launch_argmax(mri_llama* m) {
@@ -1086,6 +1137,7 @@ int mri_llama_create(mri_ctx* ctx, const mri_llama_config* cfg, mri_llama** out)
     delete m;
     return fail(MRI_ERR_CUDA, "model context: %s", mri_last_error());
   }
+  m->ctx->dev.opt = ctx->dev.opt;  // the creating context's kernel-variant options
   m->cfg = c;
   m->cfg.n_kv_heads = n_kv;
   m->hd = hd;
@@ -1122,6 +1174,7 @@ int mri_llama_create(mri_ctx* ctx, const mri_llama_config* cfg, mri_llama** out)
     rc = rc ? rc : dalloc(m, &m->fa_part, fa_pairs * 2 * kFaQ * (m->hd + 2));
     rc = rc ? rc : dalloc(m, &m->fa_tickets, fa_pairs);
   }
+  rc = rc ? rc : dalloc(m, &m->fa_range, 1);
   rc = rc ? rc : dalloc(m, &m->amax_v, kArgmaxBlocks);
   rc = rc ? rc : dalloc(m, &m->amax_i, kArgmaxBlocks);
   if (rc != MRI_OK) {
@@ -1137,6 +1190,7 @@ int mri_llama_create(mri_ctx* ctx, const mri_llama_config* cfg, mri_llama** out)
   }
   cudaMemset(m->tickets, 0, (c.n_heads + 1) * sizeof(int));
   if (m->fa_tickets) cudaMemset(m->fa_tickets, 0, fa_pairs * sizeof(int));
+  cudaMemset(m->fa_range, 0, sizeof(int));
   cudaMemset(m->kc, 0, static_cast<size_t>(c.n_layers) * c.max_seq * m->kvd * sizeof(float));
   cudaMemset(m->vc, 0, static_cast<size_t>(c.n_layers) * c.max_seq * m->kvd * sizeof(float));
   // Carve the blobs into QuantizedMatrix views, each starting 256-byte
@@ -1330,13 +1384,57 @@ int mri_llama_forward(mri_llama* m, const uint32_t* tokens, size_t n, float* log
   g_model_error.clear();
   if (int rc = check_tokens(m, tokens, n)) return rc;
   cudaSetDevice(m->ctx->device);
-  if (int rc = prefill(m, tokens, n)) return rc;
-  if (int rc = lm_head(m, 0, n)) return rc;
-  if (logits)
-    LL_TRY(cudaMemcpyAsync(logits, m->logits, n * m->cfg.vocab * 4, cudaMemcpyDeviceToHost,
-                           m->ctx->stream));
-  LL_TRY(cudaStreamSynchronize(m->ctx->stream));
+  return forward_rows(m, tokens, n, 0, logits);
+}
+
+int mri_llama_forward_at(mri_llama* m, const uint32_t* tokens, size_t n, size_t start_pos,
+                         float* logits) {
+  if (!m || !tokens) return fail(MRI_ERR_INVALID_ARGUMENT, "null argument");
+  g_model_error.clear();
+  if (int rc = check_tokens(m, tokens, n)) return rc;
+  if (start_pos > m->cfg.max_seq || n > m->cfg.max_seq - start_pos)
+    return fail(MRI_ERR_INVALID_SHAPE, "forward_at: positions [%zu, %zu) exceed max_seq %u", start_pos,
+                start_pos + n, m->cfg.max_seq);
+  cudaSetDevice(m->ctx->device);
+  return forward_rows(m, tokens, n, start_pos, logits);
+}
+
+int mri_llama_block_forward(mri_llama* m, uint32_t layer, const float* x, size_t n, size_t start_pos,
+                            float* out) {
+  if (!m || !x || !out) return fail(MRI_ERR_INVALID_ARGUMENT, "null argument");
+  g_model_error.clear();
+  if (layer >= m->cfg.n_layers)
+    return fail(MRI_ERR_INVALID_SHAPE, "layer %u >= n_layers %u", layer, m->cfg.n_layers);
+  if (n == 0) return fail(MRI_ERR_INVALID_SHAPE, "block forward: input must have at least one row");
+  if (start_pos > m->cfg.max_seq || n > m->cfg.max_seq - start_pos)
+    return fail(MRI_ERR_INVALID_SHAPE, "block forward: positions [%zu, %zu) exceed max_seq %u", start_pos,
+                start_pos + n, m->cfg.max_seq);
+  cudaSetDevice(m->ctx->device);
+  cudaStream_t st = m->ctx->stream;
+  const size_t bytes = n * m->cfg.dim * sizeof(float);
+  for (int attempt = 0;; ++attempt) {
+    LL_TRY(cudaMemcpyAsync(m->x, x, bytes, cudaMemcpyHostToDevice, st));
+    if (int rc = run_blocks(m, n, static_cast<int>(start_pos), false, layer, layer + 1)) return rc;
+    LL_TRY(cudaMemcpyAsync(out, m->x, bytes, cudaMemcpyDeviceToHost, st));
+    LL_TRY(cudaStreamSynchronize(st));
+    const bool redo = attempt == 0 && take_range_flag(m);
+    m->cuda_core_attn = redo;
+    if (!redo) break;
+    m->attn_fallbacks++;
+  }
   return mri_ctx_check_device_status(m->ctx) ? fail(MRI_ERR_TIMEOUT, "%s", mri_last_error()) : MRI_OK;
+}
+
+int mri_llama_set_option(mri_llama* m, int option, int value) {
+  if (!m) return fail(MRI_ERR_INVALID_ARGUMENT, "null model");
+  if (int rc = mri_ctx_set_option(m->ctx, option, value)) return fail(rc, "%s", mri_last_error());
+  return MRI_OK;
+}
+
+int mri_llama_attention_fallbacks(const mri_llama* m, size_t* count) {
+  if (!m || !count) return fail(MRI_ERR_INVALID_ARGUMENT, "null argument");
+  *count = m->attn_fallbacks;
+  return MRI_OK;
 }
 
 int mri_llama_forward_decode(mri_llama* m, uint32_t token, size_t pos, float* logits) {
@@ -1376,23 +1474,31 @@ int mri_llama_generate_greedy(mri_llama* m, const uint32_t* prompt, size_t n_pro
   cudaEventCreate(&e1);
   cudaEventCreate(&e2);
   int rc = MRI_OK;
-  cudaEventRecord(e0, st);
-  rc = prefill(m, prompt, n_prompt);
-  if (rc == MRI_OK) rc = lm_head(m, n_prompt - 1, 1);
-  if (rc == MRI_OK) {
-    const int p = static_cast<int>(n_prompt) - 1;  // argmax advances it to n_prompt
-    cudaMemcpyAsync(m->d_pos, &p, sizeof(int), cudaMemcpyHostToDevice, st);
-    rc = launch_argmax(m);
-    cudaEventRecord(e1, st);
-    for (size_t i = 0; i < n_decode && rc == MRI_OK; ++i)
-      if (cudaGraphLaunch(m->decode_exec, st) != cudaSuccess) rc = fail(MRI_ERR_CUDA, "graph launch");
-    cudaEventRecord(e2, st);
-    if (out_tokens)
-      cudaMemcpyAsync(out_tokens, m->d_gen + n_prompt, (n_decode + 1) * sizeof(uint32_t),
-                      cudaMemcpyDeviceToHost, st);
+  for (int attempt = 0;; ++attempt) {
+    cudaEventRecord(e0, st);
+    rc = prefill(m, prompt, n_prompt);
+    if (rc == MRI_OK) rc = lm_head(m, n_prompt - 1, 1);
+    if (rc == MRI_OK) {
+      const int p = static_cast<int>(n_prompt) - 1;  // argmax advances it to n_prompt
+      cudaMemcpyAsync(m->d_pos, &p, sizeof(int), cudaMemcpyHostToDevice, st);
+      rc = launch_argmax(m);
+      cudaEventRecord(e1, st);
+      for (size_t i = 0; i < n_decode && rc == MRI_OK; ++i)
+        if (cudaGraphLaunch(m->decode_exec, st) != cudaSuccess) rc = fail(MRI_ERR_CUDA, "graph launch");
+      cudaEventRecord(e2, st);
+      if (out_tokens)
+        cudaMemcpyAsync(out_tokens, m->d_gen + n_prompt, (n_decode + 1) * sizeof(uint32_t),
+                        cudaMemcpyDeviceToHost, st);
+    }
+    cudaError_t e = cudaStreamSynchronize(st);
+    if (rc == MRI_OK && e != cudaSuccess) rc = fail(MRI_ERR_CUDA, "%s", cudaGetErrorString(e));
+    // A prompt whose q, k or v left the f16 range: the whole call again, the
+    // prefill attention on the f32 kernel.
+    const bool redo = rc == MRI_OK && attempt == 0 && take_range_flag(m);
+    m->cuda_core_attn = redo;
+    if (!redo) break;
+    m->attn_fallbacks++;
   }
-  cudaError_t e = cudaStreamSynchronize(st);
-  if (rc == MRI_OK && e != cudaSuccess) rc = fail(MRI_ERR_CUDA, "%s", cudaGetErrorString(e));
   if (rc == MRI_OK) {
     float a = 0, b = 0;
     cudaEventElapsedTime(&a, e0, e1);

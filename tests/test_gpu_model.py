@@ -173,3 +173,208 @@ def test_decode_is_deterministic_at_scale(mri):
     la = m.forward_decode(int(a[0]), 96)
     lb = m.forward_decode(int(a[0]), 96)
     np.testing.assert_array_equal(la, lb)
+
+
+# ── model-level bars calibrated on a second correct restatement ─────────────
+#
+# The model quantizes every projection input per tensor to INT8, so its output
+# is a discontinuous function of the f32 glue: a 1-ulp difference in an RMSNorm
+# sum or an attention weight moves some INT8 codes by one step.  Two correct f32
+# implementations that differ only in rounding order therefore drift apart by
+# an amount set by the model's size, not by any error: the oracle with its glue
+# accumulated in float64 (llama_oracle glue="f64") differs from the oracle
+# itself by a median of ~1.9% of the block output's range per row at the 7B
+# dimensions (one block) and ~4.5% of the logit range (two blocks and the head),
+# more than the 2% bar used on the small configurations above.  The tests below
+# therefore hold the GPU's per-row errors against that drift, measured in the
+# test on the same inputs: its median, 90th percentile and maximum may exceed
+# the f64 restatement's by a small factor.  A semantic error (a wrong position,
+# cache row or mask, or the per-chunk activation scale of a chunked prefill
+# compared with one prefill) lands far outside: each test also checks that the
+# bar would reject such a difference.
+
+def row_errors(got, want, base=None):
+    """Per row: max |got - want| / range of want (of want - base with `base`,
+    i.e. of a block's own contribution to its residual input)."""
+    got, want = np.asarray(got, np.float32), np.asarray(want, np.float32)
+    out = []
+    for r in range(want.shape[0]):
+        ref = want[r] if base is None else want[r] - np.asarray(base[r], np.float32)
+        rng = float(ref.max() - ref.min())
+        out.append(float(np.max(np.abs(got[r] - want[r]))) / max(rng, 1e-30))
+    return np.array(out)
+
+
+def noise_bar(e_alt, slack=0.003):
+    """Bounds on (median, p90, max) of a row-error distribution: those of the
+    f64 restatement's errors, 1.25x (1.5x for the max) plus `slack`."""
+    return (1.25 * np.median(e_alt) + slack, 1.25 * np.quantile(e_alt, 0.9) + slack,
+            1.5 * e_alt.max() + 2 * slack)
+
+
+def within(e, bar):
+    return np.median(e) <= bar[0] and np.quantile(e, 0.9) <= bar[1] and e.max() <= bar[2]
+
+
+def describe(e, bar):
+    return (f"median {np.median(e):.4f} (bar {bar[0]:.4f}), p90 {np.quantile(e, 0.9):.4f} (bar {bar[1]:.4f}), "
+            f"max {e.max():.4f} (bar {bar[2]:.4f})")
+
+
+SEVEN_B = dict(n_layers=2, dim=4096, n_heads=32, n_kv_heads=32, ffn_dim=11008, vocab=32000, max_seq=520,
+               rope_base=10000.0, rms_eps=1e-5)
+
+
+@pytest.fixture(scope="module")
+def seven_b(mri, oracle):
+    """Two layers of the benchmarked Llama-7B shape (d 4096, 32 heads of 128,
+    FFN 11008, vocab 32000) with the oracle and the f64-glue restatement."""
+    w = random_weights(SEVEN_B, 12)
+    gpu, ref = build_pair(mri, oracle, SEVEN_B, w)
+    return gpu, ref, w
+
+
+def test_7b_dims_blocks_match_oracle(mri, oracle, seven_b):
+    """TransformerBlockInt8::forward_cached_parallel at the 7B dimensions
+    through the block entry point: both layers on the same 512-row input (the
+    benchmarked prefill: tensor-core GEMMs, tensor-core attention with split
+    key walks), the same rows in two chunks at an offset that cuts a query
+    block, and one row at position 512 (streaming GEMVs, the prefill attention
+    over the whole cache).  Every row against the oracle, within the f64
+    restatement's drift; the bar rejects the chunked-versus-whole difference
+    of the reference's own per-chunk quantization."""
+    gpu, _, w = seven_b
+    n, cut = 512, 259
+    x = np.random.default_rng(5).uniform(-1, 1, size=(n, SEVEN_B["dim"])).astype(np.float32)
+    for layer in (0, 1):
+        ref, alt = lo.LlamaInt8Oracle(SEVEN_B, w), lo.LlamaInt8Oracle(SEVEN_B, w, glue="f64")
+        a, b, g = ref.block_forward(layer, x, 0), alt.block_forward(layer, x, 0), gpu.block_forward(layer, x, 0)
+        bar = noise_bar(row_errors(b, a, x))
+        e = row_errors(g, a, x)
+        assert within(e, bar), (layer, "whole", describe(e, bar))
+        a2 = np.concatenate([ref.block_forward(layer, x[:cut], 0), ref.block_forward(layer, x[cut:], cut)])
+        b2 = np.concatenate([alt.block_forward(layer, x[:cut], 0), alt.block_forward(layer, x[cut:], cut)])
+        g2 = np.concatenate([gpu.block_forward(layer, x[:cut], 0), gpu.block_forward(layer, x[cut:], cut)])
+        bar2 = noise_bar(row_errors(b2, a2, x))
+        e2 = row_errors(g2, a2, x)
+        assert within(e2, bar2), (layer, "chunks", describe(e2, bar2))
+        assert not within(row_errors(a2, a, x), bar), "the bar must separate chunked from whole prefill"
+        a3, b3, g3 = (ref.block_forward(layer, x[:1], n), alt.block_forward(layer, x[:1], n),
+                      gpu.block_forward(layer, x[:1], n))
+        e3, f3 = row_errors(g3, a3, x[:1]), row_errors(b3, a3, x[:1])
+        assert e3[0] <= 1.5 * f3[0] + 0.006, (layer, "one row", e3[0], f3[0])
+    assert gpu.attention_fallbacks() == 0
+
+
+def test_7b_dims_model_matches_oracle(mri, oracle, seven_b):
+    """The whole two-layer 7B-shaped model: the 512-token prefill of
+    BASELINE's model config and 8 greedy decode steps through the captured
+    decode graph (streaming GEMVs with the RoPE/KV-cache and SwiGLU
+    epilogues, split decode attention), logits against the oracle within the
+    f64 restatement's drift."""
+    gpu, _, w = seven_b
+    toks = list(np.random.default_rng(13).integers(0, 32000, size=512))
+    ref, alt = lo.LlamaInt8Oracle(SEVEN_B, w), lo.LlamaInt8Oracle(SEVEN_B, w, glue="f64")
+    a, b, g = ref.prefill_cached(toks), alt.prefill_cached(toks), gpu.forward(toks)
+    bar = noise_bar(row_errors(b, a), slack=0.005)
+    e = row_errors(g, a)
+    assert within(e, bar), describe(e, bar)
+    tok = int(np.argmax(a[-1]))
+    da, db, dg = [], [], []
+    for step in range(8):
+        pos = 512 + step
+        da.append(ref.forward_decode(tok, pos))
+        db.append(alt.forward_decode(tok, pos))
+        dg.append(gpu.forward_decode(tok, pos))
+        tok = int(np.argmax(da[-1]))
+    bar = noise_bar(row_errors(db, da), slack=0.005)
+    e = row_errors(dg, da)
+    assert within(e, bar), describe(e, bar)
+    assert gpu.attention_fallbacks() == 0
+
+
+def _offset_cfg():
+    return dict(n_layers=2, dim=256, n_heads=4, n_kv_heads=2, ffn_dim=512, vocab=300, max_seq=400,
+                rope_base=10000.0, rms_eps=1e-5)
+
+
+def test_forward_at_chunks_match_oracle_chunks(mri, oracle):
+    """forward_cached_parallel's block loop at start_pos > 0 through the whole
+    model (forward_int8.rs:232-249): a 350-token prompt prefilled in chunks of
+    170 (GEMM), 5 (streaming GEMV) and 175 tokens (GEMM; key walks split over
+    two blocks), at offsets that cut through query blocks and key tiles,
+    against the oracle prefilling the same chunks (each chunk's activations
+    are quantized with their own per-tensor scale, as in the reference, so a
+    chunked prefill is not one prefill).  Then a decode step continues from
+    the chunked cache, and a chunk repeated on the same cache is
+    bit-identical."""
+    cfg = _offset_cfg()
+    w = random_weights(cfg, 31)
+    gpu, ref = build_pair(mri, oracle, cfg, w)
+    alt = lo.LlamaInt8Oracle(cfg, w, glue="f64")
+    toks = list(np.random.default_rng(32).integers(0, 300, size=350))
+    cuts = [(0, 170), (170, 175), (175, 350)]
+    g = np.concatenate([gpu.forward_at(toks[s:e], s) for s, e in cuts])
+    a = np.concatenate([ref.forward_cached(toks[s:e], s) for s, e in cuts])
+    b = np.concatenate([alt.forward_cached(toks[s:e], s) for s, e in cuts])
+    bar = noise_bar(row_errors(b, a), slack=0.005)
+    e = row_errors(g, a)
+    assert within(e, bar), describe(e, bar)
+    whole = lo.LlamaInt8Oracle(cfg, w).prefill_cached(toks)
+    assert not within(row_errors(a, whole), bar), "the bar must separate chunked from whole prefill"
+    d_g, d_a, d_b = gpu.forward_decode(7, 350), ref.forward_decode(7, 350), alt.forward_decode(7, 350)
+    assert row_errors([d_g], [d_a])[0] <= 1.5 * row_errors([d_b], [d_a])[0] + 0.01
+    np.testing.assert_array_equal(gpu.forward_at(toks[175:], 175), g[175:])
+
+
+def test_forward_at_rejects_positions_past_max_seq(mri, oracle):
+    cfg = _offset_cfg()
+    gpu, _ = build_pair(mri, oracle, cfg, random_weights(cfg, 33))
+    with pytest.raises(mri.InvalidShape):
+        gpu.forward_at([1, 2, 3], 398)
+    with pytest.raises(mri.InvalidShape):
+        gpu.forward_at([], 0)
+    with pytest.raises(mri.InvalidShape):
+        gpu.block_forward(2, np.zeros((1, 256), np.float32), 0)
+
+
+@pytest.mark.parametrize("option,value", [("OPT_TC_ATTN", 0), ("OPT_FA_SPLIT", 0)])
+def test_prefill_attention_variants_match_oracle(mri, oracle, option, value):
+    """The CUDA-core prefill attention (OPT_TC_ATTN = 0) and the tensor-core
+    kernel without split key walks (OPT_FA_SPLIT = 0) on the 330-token
+    head-dim-64 case: every row against the oracle within the f64
+    restatement's drift."""
+    cfg = dict(n_layers=2, dim=256, n_heads=4, n_kv_heads=2, ffn_dim=512, vocab=300, max_seq=352,
+               rope_base=10000.0, rms_eps=1e-5)
+    w = random_weights(cfg, 8)
+    gpu, ref = build_pair(mri, oracle, cfg, w)
+    gpu.set_option(getattr(mri, option), value)
+    toks = list(np.random.default_rng(9).integers(0, 300, size=330))
+    a, b, g = ref.prefill_cached(toks), lo.LlamaInt8Oracle(cfg, w, glue="f64").prefill_cached(toks), gpu.forward(toks)
+    bar = noise_bar(row_errors(b, a), slack=0.005)
+    e = row_errors(g, a)
+    assert within(e, bar), describe(e, bar)
+
+
+def test_prefill_attention_beyond_f16_range_falls_back(mri, oracle):
+    """Layer 0's q rows scaled so that q lies far beyond the f16 range
+    (|q| > 65504), which the tensor-core prefill attention cannot represent:
+    the call is run again on the f32 CUDA-core attention, its logits are
+    bit-identical to a forward with that kernel selected outright, and they
+    match the oracle within the f64 restatement's drift."""
+    cfg = dict(n_layers=2, dim=512, n_heads=4, n_kv_heads=2, ffn_dim=768, vocab=500, max_seq=192,
+               rope_base=10000.0, rms_eps=1e-5)
+    w = random_weights(cfg, 41)
+    wq, sq = w["layers"][0]["wq"]
+    w["layers"][0]["wq"] = (wq, (sq * np.float32(1e5)).astype(np.float32))
+    gpu, ref = build_pair(mri, oracle, cfg, w)
+    toks = list(np.random.default_rng(42).integers(0, 500, size=150))
+    got = gpu.forward(toks)
+    assert gpu.attention_fallbacks() == 1
+    a, b = ref.prefill_cached(toks), lo.LlamaInt8Oracle(cfg, w, glue="f64").prefill_cached(toks)
+    bar = noise_bar(row_errors(b, a), slack=0.005)
+    e = row_errors(got, a)
+    assert within(e, bar), describe(e, bar)
+    gpu.set_option(mri.OPT_TC_ATTN, 0)
+    np.testing.assert_array_equal(gpu.forward(toks), got)
+    assert gpu.attention_fallbacks() == 1

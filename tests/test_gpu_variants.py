@@ -48,20 +48,22 @@ def check_prequantized(mri, oracle, aq, s, wq, ws, qm, m, n, k):
 
 # ── tensor-core GEMM ─────────────────────────────────────────────────────────
 
-# (m, n, k): the 7B prefill gate/up GEMM at 1024 rows, and a Llama-70B gate/up
-# shard of an 8-GPU node at 2048 rows (N = 28672 / 8).
-PERSISTENT_SHAPES = [(1024, 11008, 4096), (2048, 3584, 8192)]
+# (m, n, k, fewest tiles per CTA): the 7B prefill gate/up GEMM at 1024 rows
+# (4 tiles per CTA: each TMEM buffer is reused, so its waits on the
+# epilogue's release run), and a Llama-70B gate/up shard of an 8-GPU node at
+# 2048 rows (N = 28672 / 8).
+PERSISTENT_SHAPES = [(1024, 11008, 4096, 3), (2048, 3584, 8192, 2)]
 
 
-@pytest.mark.parametrize("m,n,k", PERSISTENT_SHAPES)
-def test_gemm_persistent_multi_tile_exact(mri, oracle, gpu_ctx, m, n, k):
-    """The persistent grid with two TMEM accumulator buffers and three or
-    more tiles per CTA (tile t + 1's MMAs run while tile t drains; the
-    buffers alternate and wait on the epilogue's release).  Every row, both
+@pytest.mark.parametrize("m,n,k,min_tiles", PERSISTENT_SHAPES)
+def test_gemm_persistent_multi_tile_exact(mri, oracle, gpu_ctx, m, n, k, min_tiles):
+    """The persistent grid with two TMEM accumulator buffers and several
+    tiles per CTA (tile t + 1's MMAs run while tile t drains; from the third
+    tile on a buffer waits for the epilogue's release).  Every row, both
     epilogues: the staged f32 stores (no INT32 copy) through
     matmul_int8_from_f32, and the direct stores with INT32 sums."""
     plan = gpu_ctx.int8_gemm_plan(m, n, k)
-    assert plan["acc_buffers"] == 2 and plan["tiles_per_cta"] >= 3, plan
+    assert plan["acc_buffers"] == 2 and plan["tiles_per_cta"] >= min_tiles, plan
     assert plan["grid"] <= 148, plan
     rng = np.random.default_rng(m + n)
     x = rng.normal(0, 1, size=(m, k)).astype(np.float32)
@@ -140,8 +142,23 @@ def test_prefill_all_rows_per_row(mri, oracle, gpu_ctx, prefill_case):
 # ── streaming GEMV at the benchmarked long-K shapes ──────────────────────────
 
 # (m, n, k): the 7B down projection (K = 11008) at 1 and 8 rows, the 70B down
-# projection (K = 28672) at 1 and 8 rows, and the 70B gate/up (K = 8192).
-GEMV_SHAPES = [(1, 4096, 11008), (8, 4096, 11008), (1, 8192, 28672), (8, 8192, 28672), (1, 28672, 8192)]
+# projection (K = 28672) at 1 row, and the 70B gate/up (K = 8192).
+GEMV_SHAPES = [(1, 4096, 11008), (8, 4096, 11008), (1, 8192, 28672), (1, 28672, 8192)]
+
+
+def test_70b_down_projection_at_8_rows_takes_the_gemm(mri, oracle, gpu_ctx):
+    """8 rows of K = 28672 do not fit the streaming GEMV's shared-memory
+    activations; the product runs on the tensor-core GEMM (one 128-row tile
+    row, rows 8..127 zero-filled by TMA) and matches the oracle."""
+    m, n, k = 8, 8192, 28672
+    assert gpu_ctx.int8_path(m, n, k) == 2
+    rng = np.random.default_rng(828)
+    x = rng.normal(0, 1, size=(m, k)).astype(np.float32)
+    wq, ws = weights(rng, n, k)
+    qm = mri.QuantizedMatrix(wq, ws, n, k)
+    want, _, aq, s = oracle_from_f32(oracle, x, wq, ws, n, k)
+    assert np.array_equal(bits(mri.matmul_int8_from_f32(x, qm)), bits(want))
+    check_prequantized(mri, oracle, aq, s, wq, ws, qm, m, n, k)
 
 
 @pytest.mark.parametrize("m,n,k", GEMV_SHAPES)
@@ -161,6 +178,8 @@ def test_gemv_long_k_exact(mri, oracle, gpu_ctx, m, n, k):
         assert plan["reg_vec"] == 12 and plan["quantize_first"] == 0, plan
     if k == 28672 or m == 8:
         assert plan["reg_vec"] == 0 and plan["quantize_first"] == 1, plan
+    if (m, k) == (1, 8192):
+        assert plan["reg_vec"] == 12, plan
     rng = np.random.default_rng(m * 7 + k)
     x = rng.normal(0, 1, size=(m, k)).astype(np.float32)
     wq, ws = weights(rng, n, k)

@@ -64,7 +64,7 @@ def parse_args():
                     help="skip the Q8_0 / Q4_0 / prefill side measurements")
     ap.add_argument("--no-cpu-baseline", action="store_true",
                     help="skip the timed CPU sample (profiling runs)")
-    ap.add_argument("--only", choices=["q8_0", "q4_0", "prefill", "model", "sharded"],
+    ap.add_argument("--only", choices=["q8_0", "q4_0", "prefill", "model", "chain", "cpu", "sharded"],
                     help="run one side measurement alone and print it (profiling runs)")
     return ap.parse_args()
 
@@ -220,7 +220,129 @@ def time_graph(torch, stream, g, steps, warmup):
     return e0.elapsed_time(e1)
 
 
-SIDE_PARTS = ("q8_0", "q4_0", "prefill", "model")
+SIDE_PARTS = ("q8_0", "q4_0", "prefill", "model", "chain", "cpu")
+
+
+def decode_chain_measurement(torch, mri, lib, device, peak_hbm):
+    """The headline decode projection [1,4096]x[4096,11008] in two more forms:
+    independent calls with programmatic dependent launch off (each call's
+    weight stream starts only after the previous call has finished), and a
+    dependent chain, each call's input being the first 4096 outputs of the
+    previous call (as consecutive projections of a decode step are), with PDL
+    on and off.  Weights rotate over 16 copies as in the headline."""
+    s = torch.cuda.Stream(device)
+    ctx = mri.Context(device, stream=s)
+    rng = np.random.default_rng(0)
+    wq = rng.integers(-127, 128, size=N_DIM * K_DIM, dtype=np.int8)
+    ws = rng.uniform(0.001, 0.02, size=N_DIM).astype(np.float32)
+    weights = [mri.QuantizedMatrix(wq, ws, N_DIM, K_DIM, ctx=ctx, keep_host=False) for _ in range(WEIGHT_COPIES)]
+    calls = CALLS_PER_STEP
+    x = torch.randn(calls, K_DIM, device=f"cuda:{device}")
+    out = torch.empty(calls, N_DIM, device=f"cuda:{device}")
+    res = {}
+    for name, chained, pdl in (("independent_pdl_off", False, 0), ("chain_pdl_on", True, 1),
+                               ("chain_pdl_off", True, 0)):
+        ctx.set_option(mri.OPT_PDL, pdl)
+
+        def body():
+            for i in range(calls):
+                src = out[i - 1].data_ptr() if chained and i > 0 else x[i].data_ptr()
+                rc = lib.mri_matmul_int8_from_f32(ctx.handle, ctypes.c_void_p(src), 1, K_DIM,
+                                                  weights[i % WEIGHT_COPIES].handle,
+                                                  ctypes.c_void_p(out[i].data_ptr()))
+                if rc != 0:
+                    raise RuntimeError(mri._lib.last_error())
+        body()
+        ctx.synchronize()
+        g = graph_of(torch, s, body)
+        reps = 10
+        ms = time_graph(torch, s, g, reps, 3)
+        del g
+        t = ms / 1e3 / (reps * calls)
+        res[name] = {"us_per_call": round(t * 1e6, 3), "weight_gbs": round(WEIGHT_BYTES / t / 1e9, 1),
+                     "roofline_frac_hbm": round(ALG_BYTES / t / 1e9 / peak_hbm, 4)}
+    ctx.set_option(mri.OPT_PDL, 1)
+    res["note"] = ("value/roofline of the headline: independent calls with PDL on (a call's weight "
+                   "prefetch overlaps the previous call's tail)")
+    return res
+
+
+def cpu_side_baselines():
+    """The reference's CPU implementations of the secondary configs, timed on
+    this host through the C++ restatement (oracle), each a bounded sample:
+    matmul_int8_parallel at the prefill shape on all host threads (one row
+    task per thread, parallel.rs:308-346), the scalar matmul_q8_0_direct
+    (q8_direct.rs:229-289) and matmul_q4_0_dequant (q4_0.rs:94-181) at M = 1
+    and 8, and LlamaModelInt8::forward_decode (forward_int8.rs:538-546) at
+    the 7B shape with proj_int8_par projections (the 32 layers share one set
+    of weight arrays, which still stream from DRAM: 202 MB a layer)."""
+    import oracle
+    import llama_oracle
+    threads = oracle.hardware_threads()
+    res = {"cores_available": threads, "kind": "port"}
+    rng = np.random.default_rng(1)
+    # C3 prefill
+    M = 512
+    x = rng.normal(0, 1, size=(M, K_DIM)).astype(np.float32)
+    wq = rng.integers(-127, 128, size=N_DIM * K_DIM, dtype=np.int8)
+    ws = rng.uniform(0.001, 0.02, size=N_DIM).astype(np.float32)
+    out = np.empty((M, N_DIM), np.float32)
+    t0 = time.perf_counter()
+    aq, s = oracle.quantize_symmetric(x)
+    oracle.matmul_int8_parallel(aq, s, wq, ws, N_DIM, K_DIM, M, n_threads=threads, out=out)
+    el = time.perf_counter() - t0
+    res["prefill_m512"] = {"tops": round(2.0 * M * K_DIM * N_DIM / el / 1e12, 4), "s_per_call": round(el, 3),
+                           "cores": threads, "sample": "1 call of quantize_symmetric + matmul_int8_parallel"}
+    # C2 Q8_0 / Q4_0 (scalar, one thread)
+    wf = rng.normal(0, 0.02, size=(N_DIM, K_DIM)).astype(np.float32)
+    for fmt in ("q8_0", "q4_0"):
+        wb = oracle.quantize_q8_0_matrix(wf, N_DIM, K_DIM) if fmt == "q8_0" else \
+            oracle.quantize_q4_0_matrix(wf, N_DIM, K_DIM)
+        for m in (1, 8):
+            xm = rng.normal(0, 1, size=(m, K_DIM)).astype(np.float32)
+            calls, t0 = 0, time.perf_counter()
+            while True:
+                if fmt == "q8_0":
+                    oracle.matmul_q8_0_direct(xm, m, K_DIM, wb, N_DIM, K_DIM)
+                else:
+                    oracle.matmul_q4_0_dequant(xm, m, K_DIM, wb, N_DIM, K_DIM)
+                calls += 1
+                el = time.perf_counter() - t0
+                if el >= 1.5:
+                    break
+            t = el / calls
+            res[f"{fmt}_m{m}"] = {"weight_gbs": round(wb.size / t / 1e9, 3), "us_per_call": round(t * 1e6, 1),
+                                  "cores": 1, "sample": f"{calls} calls (scalar, as the reference)"}
+    del wf
+    # C4 decode (7B shape)
+    L, d, ffn, V, pos = 32, 4096, 11008, 32000, 576
+    cfg = dict(n_layers=L, dim=d, n_heads=32, n_kv_heads=32, ffn_dim=ffn, vocab=V, max_seq=pos + 4,
+               rope_base=10000.0, rms_eps=1e-5)
+
+    def q(rows, cols):
+        return (rng.integers(-127, 128, size=rows * cols, dtype=np.int8),
+                rng.uniform(4e-4, 8e-4, size=rows).astype(np.float32))
+    layer = dict(wq=q(d, d), wk=q(d, d), wv=q(d, d), wo=q(d, d), wgate=q(ffn, d), wup=q(ffn, d), wdown=q(d, ffn))
+    w = dict(token_embd=rng.uniform(-1, 1, size=V * d).astype(np.float32), layers=[layer] * L,
+             attn_norm=np.ones(L * d, np.float32), ffn_norm=np.ones(L * d, np.float32),
+             output_norm=np.ones(d, np.float32), output=q(V, d))
+    # The reference's decode step projects with the scalar proj_int8
+    # (forward_int8.rs:333-346, :72-74).
+    ref = llama_oracle.LlamaInt8Oracle(cfg, w, proj="scalar")
+    ref.kc[:, :pos] = rng.normal(0, 1, size=(pos, d)).astype(np.float32)[None]
+    ref.vc[:, :pos] = ref.kc[:, :pos]
+    tokens, t0 = 0, time.perf_counter()
+    while True:
+        ref.forward_decode(7 + tokens, pos + tokens)
+        tokens += 1
+        el = time.perf_counter() - t0
+        if el >= 2.0 or tokens == 3:
+            break
+    res["llama7b_int8_decode"] = {"tok_s": round(tokens / el, 3), "s_per_token": round(el / tokens, 3),
+                                  "cores": 1,
+                                  "sample": f"{tokens} decode tokens at position {pos}, scalar proj_int8 "
+                                            "projections as the reference's forward_decode; one thread"}
+    return res
 
 
 def secondary_measurements(torch, mri, lib, device, peak_hbm, peak_tc, parts=SIDE_PARTS):
@@ -301,12 +423,28 @@ def secondary_measurements(torch, mri, lib, device, peak_hbm, peak_tc, parts=SID
         del g
         kern_s = ms_k / 1e3 / (10 * copies)
         kern_tops = 2.0 * M * K_DIM * N_DIM / kern_s / 1e12
+
+        # Per-row activation quantization (BASELINE config 2 names it).
+        def body_r():
+            for i in range(copies):
+                rc = lib.mri_matmul_int8_from_f32_g(ctx.handle, ctypes.c_void_p(x.data_ptr()), M, K_DIM,
+                                                    mri.PER_ROW, qms[i].handle, ctypes.c_void_p(out.data_ptr()))
+                assert rc == 0, mri._lib.last_error()
+        body_r()
+        ctx.synchronize()
+        g = graph_of(torch, s, body_r)
+        ms_r = time_graph(torch, s, g, 10, 2)
+        del g
+        row_s = ms_r / 1e3 / (10 * copies)
+        row_tops = 2.0 * M * K_DIM * N_DIM / row_s / 1e12
         res["prefill_m512"] = {"tops": round(tops, 2), "us_per_call": round(per_call_s * 1e6, 2),
                                "path": {0: "stream-gemv", 1: "generic-gemv", 2: "tcgen05-gemm"}[path],
                                "roofline_frac_int8": round(tops / (2 * peak_tc), 4),
                                "gemm_kernel_tops": round(kern_tops, 2),
                                "gemm_kernel_us": round(kern_s * 1e6, 2),
                                "gemm_kernel_frac_int8": round(kern_tops / (2 * peak_tc), 4),
+                               "per_row_tops": round(row_tops, 2), "per_row_us_per_call": round(row_s * 1e6, 2),
+                               "per_row_frac_int8": round(row_tops / (2 * peak_tc), 4),
                                "int8_peak_note": "int8 dense peak taken as 2x measured bf16; "
                                                  "tops includes the activation quantizer"}
     except LookupError:
@@ -316,6 +454,16 @@ def secondary_measurements(torch, mri, lib, device, peak_hbm, peak_tc, parts=SID
     ctx.synchronize()
     if "model" in parts:
         res["llama7b_int8"] = model_measurement(mri, device, peak_hbm)
+    if "chain" in parts:
+        try:
+            res["decode_gemv_forms"] = decode_chain_measurement(torch, mri, lib, device, peak_hbm)
+        except Exception as e:  # noqa: BLE001 - side measurement only
+            res["decode_gemv_forms"] = {"error": str(e)[:200]}
+    if "cpu" in parts:
+        try:
+            res["cpu_baselines"] = cpu_side_baselines()
+        except Exception as e:  # noqa: BLE001 - side measurement only
+            res["cpu_baselines"] = {"error": str(e)[:200]}
     return res
 
 
@@ -555,7 +703,8 @@ def run_ours(args, rank, world, local_rank):
 
     secondary = None
     if world == 1 and not args.no_secondary:
-        secondary = secondary_measurements(torch, mri, lib, device, peak_hbm, peak_tc)
+        parts = tuple(p for p in SIDE_PARTS if p != "cpu" or not args.no_cpu_baseline)
+        secondary = secondary_measurements(torch, mri, lib, device, peak_hbm, peak_tc, parts=parts)
     sharded = None
     if not args.no_secondary:
         try:

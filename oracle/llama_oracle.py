@@ -81,7 +81,12 @@ def _swiglu64(gate, up):
 
 
 class LlamaInt8Oracle:
-    """glue="reference" (default): the reference's f32 glue, restated op by
+    """proj="par" (default): projections as proj_int8_par (the AVX2 row-parallel
+    product); proj="scalar": as proj_int8, the scalar matmul_int8_from_f32
+    that the reference's decode step calls (forward_int8.rs:333-346).  Both
+    give the same numbers.
+
+    glue="reference" (default): the reference's f32 glue, restated op by
     op.  glue="f64": the same model with RMSNorm, attention and SwiGLU
     accumulated in float64 and rounded to f32 — the same mathematics in
     another rounding order.  The projections (the INT8 products) are the
@@ -90,9 +95,9 @@ class LlamaInt8Oracle:
     activation quantization (a 1-ulp change of an activation can move its
     INT8 code), which sets the model-level tolerance."""
 
-    def __init__(self, cfg, w, glue="reference"):
-        assert glue in ("reference", "f64")
-        self.glue = glue
+    def __init__(self, cfg, w, glue="reference", proj="par"):
+        assert glue in ("reference", "f64") and proj in ("par", "scalar")
+        self.glue, self.proj = glue, proj
         self.cfg, self.w = cfg, w
         self.hd = cfg["dim"] // cfg["n_heads"]
         self.cos, self.sin = oracle.rope_table(cfg["max_seq"], self.hd, cfg["rope_base"])
@@ -106,6 +111,8 @@ class LlamaInt8Oracle:
         proj_int8 (:72-84), in the time the model-sized checks need."""
         data, scales = wpair
         k = x.size // rows
+        if self.proj == "scalar":  # proj_int8 (:72-74): matmul_int8_from_f32, scalar loop
+            return oracle.matmul_int8_from_f32(x, rows, k, data, scales, n_out, k).reshape(-1)
         aq, s = oracle.quantize_symmetric(x)
         return oracle.matmul_int8_parallel(aq, s, data, scales, n_out, k, rows).reshape(-1)
 

@@ -136,7 +136,7 @@ int run_int8(mri_ctx* ctx, ActArgs act, const mri_qmatrix* w, size_t m, float* o
       int8_t* q = reinterpret_cast<int8_t*>(ctx->scratch + amax_bytes(m) + al(m * sizeof(float)));
       const int per_row = act.mode == mri::ACT_F32_PER_ROW;
       MRI_CUDA_TRY(mri::launch_quantize(ctx->dev, st, act.x, m, K, per_row, q, scales, amax, &ctx->ls,
-                                        act.norm_w, act.eps, act.swiglu));
+                                        act.norm_w, act.eps, act.swiglu, ctx->d_sync, ctx->d_status));
       ActArgs a;
       a.xq = q;
       a.mode = per_row ? mri::ACT_I8_DEV_ROW_SCALE : mri::ACT_I8_DEV_SCALE;
@@ -163,7 +163,8 @@ int run_int8(mri_ctx* ctx, ActArgs act, const mri_qmatrix* w, size_t m, float* o
     int8_t* q = reinterpret_cast<int8_t*>(ctx->scratch + amax_bytes(m) + al(m * sizeof(float)));
     if (f32_in) {
       MRI_CUDA_TRY(mri::launch_quantize(ctx->dev, st, act.x, m, K, per_row, q, scales, amax,
-                                        &ctx->ls, act.norm_w, act.eps, act.swiglu));
+                                        &ctx->ls, act.norm_w, act.eps, act.swiglu, ctx->d_sync,
+                                        ctx->d_status));
       xq = q;
     } else {
       MRI_CUDA_TRY(cudaMemcpyAsync(scales, &act.scale_host, sizeof(float),
@@ -219,7 +220,8 @@ int mri::quantize_to_scratch(::mri_ctx* ctx, const float* x, size_t m, size_t k,
   float* amax = reinterpret_cast<float*>(ctx->scratch);
   *scale_dev = reinterpret_cast<float*>(ctx->scratch + amax_bytes(m));
   *q = reinterpret_cast<int8_t*>(ctx->scratch + amax_bytes(m) + al(sizeof(float)));
-  MRI_CUDA_TRY(mri::launch_quantize(ctx->dev, ctx->stream, x, m, k, 0, *q, *scale_dev, amax, &ctx->ls));
+  MRI_CUDA_TRY(mri::launch_quantize(ctx->dev, ctx->stream, x, m, k, 0, *q, *scale_dev, amax, &ctx->ls,
+                                    nullptr, 0.0f, 0, ctx->d_sync, ctx->d_status));
   return MRI_OK;
 }
 
@@ -358,12 +360,15 @@ int check_k(const char* fn, size_t m, size_t k, size_t k_w) {
   return MRI_OK;
 }
 
-// Reads and clears the mapped status word (the stream must be idle).
+// Reads and clears the mapped status word (the stream must be idle).  After a
+// timeout the quantizer's grid-barrier words may hold a partial count; they
+// are cleared too.
 int read_status(mri_ctx* ctx) {
   volatile int* hs = ctx->h_status;
   const int st = *hs;
   if (st != MRI_OK) {
     *hs = MRI_OK;
+    if (ctx->d_sync) cudaMemset(ctx->d_sync, 0, 2 * sizeof(unsigned));
     return fail(st, "a device-side bounded wait timed out");
   }
   return MRI_OK;
@@ -440,7 +445,11 @@ static int ctx_create(int device, void* stream, bool own, mri_ctx** out) {
     *c->h_status = 0;
     e = cudaHostGetDevicePointer(&c->d_status, c->h_status, 0);
   }
+  if (e == cudaSuccess) e = cudaMalloc(&c->d_sync, 256);
+  if (e == cudaSuccess) e = cudaMemset(c->d_sync, 0, 256);
   if (e != cudaSuccess) {
+    if (c->d_sync) cudaFree(c->d_sync);
+    if (c->h_status) cudaFreeHost(c->h_status);
     if (own) cudaStreamDestroy(c->stream);
     delete c;
     return cuda_fail(e, "status word");
@@ -461,6 +470,7 @@ int mri_ctx_destroy(mri_ctx* ctx) {
   cudaStreamSynchronize(ctx->stream);
   if (ctx->scratch) cudaFree(ctx->scratch);
   if (ctx->h_status) cudaFreeHost(ctx->h_status);
+  if (ctx->d_sync) cudaFree(ctx->d_sync);
   if (ctx->own_stream) cudaStreamDestroy(ctx->stream);
   delete ctx;
   return MRI_OK;
@@ -705,7 +715,8 @@ int mri_quantize_symmetric(mri_ctx* ctx, const float* x_dev, size_t m, size_t k,
     return fail(MRI_ERR_INVALID_ARGUMENT, "null device pointer");
   if (int rc = ensure_scratch(ctx, amax_bytes(m))) return rc;
   MRI_CUDA_TRY(mri::launch_quantize(ctx->dev, ctx->stream, x_dev, m, k, granularity, q_dev,
-                                    scale_dev, reinterpret_cast<float*>(ctx->scratch), &ctx->ls));
+                                    scale_dev, reinterpret_cast<float*>(ctx->scratch), &ctx->ls, nullptr,
+                                    0.0f, 0, ctx->d_sync, ctx->d_status));
   return MRI_OK;
 }
 
@@ -786,7 +797,8 @@ int mri_host_quantize_symmetric(mri_ctx* ctx, const float* x, size_t m, size_t k
   int8_t* qd = reinterpret_cast<int8_t*>(hs.in + al(m * k * 4));
   if (m * k) MRI_CUDA_TRY(cudaMemcpyAsync(xd, x, m * k * 4, cudaMemcpyHostToDevice, ctx->stream));
   MRI_CUDA_TRY(mri::launch_quantize(ctx->dev, ctx->stream, xd, m, k, granularity, qd, hs.out,
-                                    reinterpret_cast<float*>(ctx->scratch), &ctx->ls));
+                                    reinterpret_cast<float*>(ctx->scratch), &ctx->ls, nullptr, 0.0f, 0,
+                                    ctx->d_sync, ctx->d_status));
   if (m * k) MRI_CUDA_TRY(cudaMemcpyAsync(q, qd, m * k, cudaMemcpyDeviceToHost, ctx->stream));
   if (ns) MRI_CUDA_TRY(cudaMemcpyAsync(scale, hs.out, ns * 4, cudaMemcpyDeviceToHost, ctx->stream));
   MRI_CUDA_TRY(cudaStreamSynchronize(ctx->stream));

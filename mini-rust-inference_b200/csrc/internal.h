@@ -112,12 +112,15 @@ struct DeviceInfo {
 // ── quantizer (quant.cu) ─────────────────────────────────────────────────────
 // amax_scratch: 2 * max(M, kQuantPartials) floats of device scratch (per-block
 // partial maxima for PER_TENSOR, per-row maxima for PER_ROW, per-row 1/rms
-// when norm_w is given).
+// when norm_w is given).  sync (nullable): two zero-initialised words of
+// device memory owned by the caller's stream, the grid barrier of the
+// one-launch per-tensor quantizer; without them the two-kernel path runs.
+// status: where a barrier wait that gives up records MRI_ERR_TIMEOUT.
 constexpr size_t kQuantPartials = 1024;
 cudaError_t launch_quantize(const DeviceInfo& dev, cudaStream_t st, const float* x, size_t m,
                             size_t k, int per_row, int8_t* q, float* scale, float* amax_scratch,
                             LaunchStats* ls, const float* norm_w = nullptr, float eps = 0.0f,
-                            int swiglu = 0);
+                            int swiglu = 0, unsigned* sync = nullptr, int* status = nullptr);
 
 // out[i] = residual[i] + out[i] (the reference's x + projected).
 cudaError_t launch_add_residual(const DeviceInfo& dev, cudaStream_t st, float* out,
@@ -277,6 +280,7 @@ struct mri_ctx {
   mri::DeviceInfo dev;
   int* d_status = nullptr;   // device view of the status word
   int* h_status = nullptr;   // host view (mapped pinned memory)
+  unsigned* d_sync = nullptr;  // grid-barrier words of the one-launch quantizer (device memory)
   uint8_t* scratch = nullptr;
   size_t scratch_bytes = 0;
   mri::LaunchStats ls;

@@ -35,6 +35,7 @@ constexpr size_t kNoAllocMaxActBytes = MRI_NOALLOC_MAX_ACT_BYTES;
 // kHeaderBytes.
 constexpr size_t kScaleOffset = mri::kQuantPartials * sizeof(float);
 constexpr size_t kStatusOffset = kScaleOffset + 8;
+constexpr size_t kSyncOffset = kScaleOffset + 16;  // two words: the quantizer's grid barrier
 __device__ __align__(256) uint8_t g_noalloc_scratch[kHeaderBytes + kNoAllocMaxActBytes];
 
 constexpr int kMaxDevices = 64;
@@ -72,7 +73,8 @@ int setup_device(int device, cudaStream_t st, DeviceSetup** out) {
         (e = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device)) != cudaSuccess)
       return fail(MRI_ERR_CUDA, cudaGetErrorString(e));
     if (major != 10) return fail(MRI_ERR_CUDA, "device is not sm_100 (this library is built for sm_100a)");
-    if ((e = cudaMemsetAsync(static_cast<uint8_t*>(ptr) + kStatusOffset, 0, sizeof(int), st)) != cudaSuccess)
+    if ((e = cudaMemsetAsync(static_cast<uint8_t*>(ptr) + kStatusOffset, 0, kSyncOffset + 8 - kStatusOffset,
+                             st)) != cudaSuccess)
       return fail(MRI_ERR_CUDA, cudaGetErrorString(e));
     s.scratch = static_cast<uint8_t*>(ptr);
     s.dev.device = device;
@@ -136,8 +138,9 @@ int mri_matmul_int8_from_f32_noalloc(const float* x_dev, size_t m, size_t k, con
                                 nullptr, status, nullptr);
     return e == cudaSuccess ? MRI_OK : fail(MRI_ERR_CUDA, cudaGetErrorString(e));
   }
-  if ((e = mri::launch_quantize(s->dev, st, x_dev, m, k, /*per_row=*/0, xq, scale, amax, nullptr)) !=
-      cudaSuccess)
+  unsigned* sync = reinterpret_cast<unsigned*>(s->scratch + kSyncOffset);
+  if ((e = mri::launch_quantize(s->dev, st, x_dev, m, k, /*per_row=*/0, xq, scale, amax, nullptr, nullptr,
+                                0.0f, 0, sync, status)) != cudaSuccess)
     return fail(MRI_ERR_CUDA, cudaGetErrorString(e));
   if (gemv) {
     mri::ActArgs a;
@@ -168,6 +171,8 @@ int mri_noalloc_check_status(void* cuda_stream) {
   if ((e = cudaStreamSynchronize(st)) != cudaSuccess ||
       (e = cudaMemcpyAsync(&word, status, sizeof(int), cudaMemcpyDeviceToHost, st)) != cudaSuccess ||
       (e = cudaMemsetAsync(status, 0, sizeof(int), st)) != cudaSuccess ||
+      (word != MRI_OK &&
+       (e = cudaMemsetAsync(s->scratch + kSyncOffset, 0, 8, st)) != cudaSuccess) ||
       (e = cudaStreamSynchronize(st)) != cudaSuccess)
     return fail(MRI_ERR_CUDA, cudaGetErrorString(e));
   if (word != MRI_OK) {

@@ -1,12 +1,17 @@
 // quant.cu — K1: symmetric INT8 activation quantizer (quantize_symmetric,
 // src/quant/int8/symmetric.rs:42-57), per tensor or per row.
 //
-// Two passes over HBM/L2: an absmax reduction (order-independent, so the
-// scale is bit-identical to the reference's sequential fold) and the
-// element-wise quantization.  HBM-bound: 4 B read + 1 B written per element in
-// the second pass, 4 B read in the first.
+// Two passes: an absmax reduction (order-independent, so the scale is
+// bit-identical to the reference's sequential fold) and the element-wise
+// quantization.  Per tensor they run in one launch with a grid barrier
+// between them when the caller provides the barrier words (the values of the
+// first pass mostly stay in registers: 4 B read + 1 B written per element),
+// else as two kernels.  HBM-bound.
 #include <algorithm>
 #include <cstdlib>
+#include <map>
+#include <mutex>
+#include <utility>
 
 #include "common.cuh"
 #include "internal.h"
@@ -386,6 +391,285 @@ __global__ void __launch_bounds__(kQThreads) quant_apply_xform_kernel(
   }
 }
 
+// ── one-launch per-tensor quantizers ─────────────────────────────────────────
+// Both passes in one kernel: every block folds its share into a partial
+// maximum, the blocks meet at a grid barrier (sense reversal on sync[0] =
+// arrivals, sync[1] = generation; the last block to arrive reduces the
+// partials, publishes the scale, resets the count and advances the
+// generation), then each block quantizes its share, from registers where it
+// kept the values.  The result is bit-identical to the two-kernel path (the
+// same partial maxima, scale and element arithmetic).  The grid never exceeds
+// the blocks that fit on the device at once.  Every block releases the
+// successor kernel (griddepcontrol.launch_dependents) as it starts: the
+// successor can only launch once every block of this grid has done so, i.e.
+// once the whole grid is resident, so its CTAs cannot keep a block of this
+// grid from starting, and it prefetches its weights while this kernel runs.
+// The wait is bounded: on timeout the kernel records MRI_ERR_TIMEOUT and
+// returns without writing the output.
+constexpr int kOnceCache = 4;  // float4 per thread kept between the passes (flat kernel)
+
+__device__ __forceinline__ float absmax4(float m, float4 v) {
+  return absmax_acc(absmax_acc(absmax_acc(absmax_acc(m, v.x), v.y), v.z), v.w);
+}
+
+__device__ __forceinline__ char4 quant4(float4 v, float inv) {
+  return make_char4(sym_quant(v.x, inv), sym_quant(v.y, inv), sym_quant(v.z, inv), sym_quant(v.w, inv));
+}
+
+// Grid barrier of the one-launch quantizers.  With write_partial, the block's
+// maximum of the per-thread values `m` is first written to
+// partial[blockIdx.x]; the last block to arrive reduces partial[0,
+// n_partials).  Returns the tensor's scale in every thread, or -1 after a
+// timeout.
+__device__ float once_barrier_scale(float m, bool write_partial, float* __restrict__ partial, int n_partials,
+                                    unsigned* sync, float* __restrict__ scale_out, int* status) {
+  __shared__ float red[kQThreads / 32];
+  __shared__ float s_scale;
+  __shared__ int s_last;
+  m = warp_max(m);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  unsigned gen0 = 0;
+  if (threadIdx.x == 0) {
+    if (write_partial) {
+      float t = 0.0f;
+#pragma unroll
+      for (int i = 0; i < kQThreads / 32; ++i) t = fmaxf(t, red[i]);
+      partial[blockIdx.x] = t;
+    }
+    gen0 = *reinterpret_cast<volatile unsigned*>(sync + 1);
+    __threadfence();
+    s_last = atomicAdd(sync, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (s_last) {
+    __threadfence();
+    float t = 0.0f;
+    for (int i = threadIdx.x; i < n_partials; i += kQThreads) t = fmaxf(t, __ldcg(partial + i));
+    t = warp_max(t);
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = t;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float v = 0.0f;
+#pragma unroll
+      for (int i = 0; i < kQThreads / 32; ++i) v = fmaxf(v, red[i]);
+      const float scale = sym_scale(v);
+      scale_out[0] = scale;
+      s_scale = scale;
+      sync[0] = 0;
+      __threadfence();
+      atomicAdd(sync + 1, 1u);
+    }
+  } else if (threadIdx.x == 0) {
+    const long long t0 = clock64();
+    float scale = 0.0f;
+    for (;;) {
+      if (*reinterpret_cast<volatile unsigned*>(sync + 1) != gen0) {
+        __threadfence();
+        scale = __ldcg(scale_out);
+        break;
+      }
+      if (clock64() - t0 > kWaitBudgetClocks) {
+        if (status) *reinterpret_cast<volatile int*>(status) = MRI_ERR_TIMEOUT;
+        scale = -1.0f;
+        break;
+      }
+      __nanosleep(20);
+    }
+    s_scale = scale;
+  }
+  __syncthreads();
+  return s_scale;
+}
+
+// Flat: a grid-stride share of the n4 float4 of x (16-byte aligned, q 4-byte
+// aligned); the first kOnceCache of each thread stay in registers.
+__global__ void __launch_bounds__(kQThreads) quant_tensor_once_kernel(const float* __restrict__ x, size_t n4,
+                                                                      float* __restrict__ partial,
+                                                                      unsigned* sync,
+                                                                      int8_t* __restrict__ q,
+                                                                      float* __restrict__ scale_out,
+                                                                      int* status) {
+  pdl_enter();
+  const float4* x4 = reinterpret_cast<const float4*>(x);
+  const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+  const size_t tid = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  float4 v[kOnceCache];
+  float m = 0.0f;
+#pragma unroll
+  for (int u = 0; u < kOnceCache; ++u) {
+    const size_t j = tid + u * stride;
+    v[u] = j < n4 ? ld_act(x4 + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+#pragma unroll
+  for (int u = 0; u < kOnceCache; ++u) m = absmax4(m, v[u]);
+  size_t j = tid + kOnceCache * stride;
+  for (; j + 3 * stride < n4; j += 4 * stride) {
+    float4 w[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) w[u] = ld_act(x4 + j + u * stride);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) m = absmax4(m, w[u]);
+  }
+  for (; j < n4; j += stride) m = absmax4(m, ld_act(x4 + j));
+  const float scale = once_barrier_scale(m, true, partial, gridDim.x, sync, scale_out, status);
+  if (scale < 0.0f) return;
+  const float inv = __fdiv_rn(1.0f, scale);
+  char4* q4 = reinterpret_cast<char4*>(q);
+#pragma unroll
+  for (int u = 0; u < kOnceCache; ++u) {
+    const size_t i = tid + u * stride;
+    if (i < n4) q4[i] = quant4(v[u], inv);
+  }
+  for (j = tid + kOnceCache * stride; j < n4; j += stride) q4[j] = quant4(ld_act(x4 + j), inv);
+}
+
+// Row-wise, with the producer op fused in front (RMSNorm with weight norm_w,
+// or SwiGLU over interleaved gate/up rows of width 2K): block b takes rows b,
+// b + grid, ...; a row's transformed values are formed once per pass from its
+// K / 4 float4 (thread t: float4 t, t + 256, ..., at most kVec), its 1/rms
+// and maximum go to row_inv[r] and partial[r], and the block's first row
+// stays in registers.  The same arithmetic, in the same order, as
+// row_stats_kernel + quant_apply_xform_kernel.  per_row: each row's own scale
+// (no barrier).  K % 4 == 0, x / norm_w 16-byte aligned, q 4-byte aligned.
+template <int kVec>
+__device__ __forceinline__ void load_xform_row(const float* __restrict__ x, size_t K, int r,
+                                               const float* __restrict__ norm_w, float eps, int swiglu,
+                                               float4 (&v)[kVec], float* inv_out) {
+  const size_t k4 = K / 4;
+  __shared__ float red[kQThreads / 32];
+  __shared__ float inv_s;
+  if (swiglu) {
+    const float4* row = reinterpret_cast<const float4*>(x + static_cast<size_t>(r) * 2 * K);
+#pragma unroll
+    for (int j = 0; j < kVec; ++j) {
+      const size_t i = threadIdx.x + static_cast<size_t>(j) * kQThreads;
+      if (i < k4) {
+        const float4 a = ld_act(row + 2 * i), b = ld_act(row + 2 * i + 1);
+        v[j] = make_float4(__fmul_rn(__fdiv_rn(a.x, __fadd_rn(1.0f, expf(-a.x))), a.y),
+                           __fmul_rn(__fdiv_rn(a.z, __fadd_rn(1.0f, expf(-a.z))), a.w),
+                           __fmul_rn(__fdiv_rn(b.x, __fadd_rn(1.0f, expf(-b.x))), b.y),
+                           __fmul_rn(__fdiv_rn(b.z, __fadd_rn(1.0f, expf(-b.z))), b.w));
+      } else {
+        v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+    *inv_out = 1.0f;
+    return;
+  }
+  const float4* row = reinterpret_cast<const float4*>(x + static_cast<size_t>(r) * K);
+#pragma unroll
+  for (int j = 0; j < kVec; ++j) {
+    const size_t i = threadIdx.x + static_cast<size_t>(j) * kQThreads;
+    v[j] = i < k4 ? ld_act(row + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  if (!norm_w) {
+    *inv_out = 1.0f;
+    return;
+  }
+  float ss = 0.0f;
+#pragma unroll
+  for (int j = 0; j < kVec; ++j) {
+    ss = __fmaf_rn(v[j].x, v[j].x, ss);
+    ss = __fmaf_rn(v[j].y, v[j].y, ss);
+    ss = __fmaf_rn(v[j].z, v[j].z, ss);
+    ss = __fmaf_rn(v[j].w, v[j].w, ss);
+  }
+  ss = warp_sum_f(ss);
+  __syncthreads();  // red / inv_s of the previous row are no longer read
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.0f;
+    for (int i = 0; i < kQThreads / 32; ++i) t += red[i];
+    inv_s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, static_cast<float>(K)), eps)));
+  }
+  __syncthreads();
+  const float ir = inv_s;
+#pragma unroll
+  for (int j = 0; j < kVec; ++j) {
+    const size_t i = threadIdx.x + static_cast<size_t>(j) * kQThreads;
+    if (i < k4) {
+      const float4 w = __ldg(reinterpret_cast<const float4*>(norm_w) + i);
+      v[j] = make_float4(__fmul_rn(w.x, __fmul_rn(v[j].x, ir)), __fmul_rn(w.y, __fmul_rn(v[j].y, ir)),
+                         __fmul_rn(w.z, __fmul_rn(v[j].z, ir)), __fmul_rn(w.w, __fmul_rn(v[j].w, ir)));
+    }
+  }
+  *inv_out = ir;
+}
+
+template <int kVec>
+__device__ __forceinline__ float row_block_max(const float4 (&v)[kVec]) {
+  __shared__ float red[kQThreads / 32];
+  float m = 0.0f;
+#pragma unroll
+  for (int j = 0; j < kVec; ++j) m = absmax4(m, v[j]);
+  m = warp_max(m);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  float t = 0.0f;
+#pragma unroll
+  for (int i = 0; i < kQThreads / 32; ++i) t = fmaxf(t, red[i]);
+  return t;
+}
+
+template <int kVec>
+__device__ __forceinline__ void store_row_q(const float4 (&v)[kVec], size_t K, int r, float inv,
+                                            int8_t* __restrict__ q) {
+  const size_t k4 = K / 4;
+  char4* qr = reinterpret_cast<char4*>(q + static_cast<size_t>(r) * K);
+#pragma unroll
+  for (int j = 0; j < kVec; ++j) {
+    const size_t i = threadIdx.x + static_cast<size_t>(j) * kQThreads;
+    if (i < k4) qr[i] = quant4(v[j], inv);
+  }
+}
+
+template <int kVec>
+__global__ void __launch_bounds__(kQThreads) quant_rows_once_kernel(
+    const float* __restrict__ x, int m, size_t K, const float* __restrict__ norm_w, float eps, int swiglu,
+    int per_row, float* __restrict__ partial, unsigned* sync, int8_t* __restrict__ q,
+    float* __restrict__ scale_out, int* status) {
+  pdl_enter();
+  float4 v[kVec];
+  float ir0 = 1.0f;
+  const int r0 = blockIdx.x;
+  // Pass 1.  The block's first row stays in v.
+  load_xform_row<kVec>(x, K, r0, norm_w, eps, swiglu, v, &ir0);
+  float mx = row_block_max<kVec>(v);
+  if (threadIdx.x == 0) partial[r0] = mx;
+  if (per_row) {
+    if (threadIdx.x == 0) scale_out[r0] = sym_scale(mx);
+    store_row_q<kVec>(v, K, r0, __fdiv_rn(1.0f, sym_scale(mx)), q);
+    for (int r = r0 + gridDim.x; r < m; r += gridDim.x) {
+      float ir;
+      load_xform_row<kVec>(x, K, r, norm_w, eps, swiglu, v, &ir);
+      const float t = row_block_max<kVec>(v);
+      if (threadIdx.x == 0) scale_out[r] = sym_scale(t);
+      store_row_q<kVec>(v, K, r, __fdiv_rn(1.0f, sym_scale(t)), q);
+    }
+    return;
+  }
+  float4 w[kVec];
+  for (int r = r0 + gridDim.x; r < m; r += gridDim.x) {
+    float ir;
+    load_xform_row<kVec>(x, K, r, norm_w, eps, swiglu, w, &ir);
+    const float t = row_block_max<kVec>(w);
+    if (threadIdx.x == 0) partial[r] = t;
+  }
+  const float scale = once_barrier_scale(0.0f, false, partial, m, sync, scale_out, status);
+  if (scale < 0.0f) return;
+  const float inv = __fdiv_rn(1.0f, scale);
+  store_row_q<kVec>(v, K, r0, inv, q);
+  for (int r = r0 + gridDim.x; r < m; r += gridDim.x) {
+    float ir;
+    load_xform_row<kVec>(x, K, r, norm_w, eps, swiglu, w, &ir);
+    store_row_q<kVec>(w, K, r, inv, q);
+  }
+}
+
 __global__ void add_inplace_kernel(float* __restrict__ out, const float* __restrict__ res, size_t n) {
   for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<size_t>(gridDim.x) * blockDim.x)
@@ -402,14 +686,52 @@ cudaError_t launch_add_residual(const DeviceInfo& dev, cudaStream_t st, float* o
   return cudaGetLastError();
 }
 
+// Blocks of `k` that fit on one SM, cached per kernel and device.
+template <typename KernelT>
+int once_resident(KernelT k, int device) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, int> done;
+  std::lock_guard<std::mutex> lock(mu);
+  const auto key = std::make_pair(reinterpret_cast<const void*>(k), device);
+  auto it = done.find(key);
+  if (it != done.end()) return it->second;
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, kQThreads, 0) != cudaSuccess) {
+    cudaGetLastError();
+    n = 0;
+  }
+  done[key] = n;
+  return n;
+}
+
 cudaError_t launch_quantize(const DeviceInfo& dev, cudaStream_t st, const float* x, size_t m,
                             size_t k, int per_row, int8_t* q, float* scale, float* amax_scratch,
-                            LaunchStats* ls, const float* norm_w, float eps, int swiglu) {
+                            LaunchStats* ls, const float* norm_w, float eps, int swiglu,
+                            unsigned* sync, int* status) {
   const size_t n = m * k;
+  const bool x16 = (reinterpret_cast<uintptr_t>(x) & 15) == 0, q4 = (reinterpret_cast<uintptr_t>(q) & 3) == 0;
   if ((norm_w || swiglu) && n > 0) {
     // amax_scratch holds 2 * max(m, kQuantPartials) floats: row maxima, then 1/rms.
     float* partial = amax_scratch;
     float* row_inv = amax_scratch + std::max(m, kQuantPartials);
+    const size_t k4 = k / 4;
+    const bool once = (sync || per_row) && k % 4 == 0 && x16 && q4 &&
+                      (!norm_w || (reinterpret_cast<uintptr_t>(norm_w) & 15) == 0) &&
+                      k4 <= 12 * static_cast<size_t>(kQThreads) && m <= (1u << 30);
+    if (once) {
+      const bool small = k4 <= 4 * static_cast<size_t>(kQThreads);
+      auto kern = small ? quant_rows_once_kernel<4> : quant_rows_once_kernel<12>;
+      // Only when every row gets a block of its own (a block that took a
+      // second row would read and transform it twice).
+      const int fit = once_resident(kern, dev.device) * dev.sm_count;
+      if (fit > 0 && m <= static_cast<size_t>(fit)) {
+        const unsigned grid = static_cast<unsigned>(m);
+        cudaError_t e = qlaunch(dev, kern, grid, st, x, static_cast<int>(m), k, norm_w, eps, swiglu, per_row,
+                                partial, sync, q, scale, status);
+        if (ls) ls->launches++;
+        return e;
+      }
+    }
     cudaError_t e = qlaunch(dev, row_stats_kernel, static_cast<unsigned>(m), st, x, k, norm_w, eps, swiglu,
                             row_inv, partial);
     if (e != cudaSuccess) return e;
@@ -428,11 +750,23 @@ cudaError_t launch_quantize(const DeviceInfo& dev, cudaStream_t st, const float*
     }
     if (m == 0) return cudaSuccess;
   }
-  if (per_row && k % 4 == 0 && k <= static_cast<size_t>(kRowVec) * kQThreads * 4 &&
-      (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(q) & 3) == 0) {
+  if (per_row && k % 4 == 0 && k <= static_cast<size_t>(kRowVec) * kQThreads * 4 && x16 && q4) {
     cudaError_t e = qlaunch(dev, quant_rows_kernel, static_cast<unsigned>(m), st, x, k, q, scale);
     if (ls) ls->launches++;
     return e;
+  }
+  if (!per_row && sync && n % 4 == 0 && x16 && q4) {
+    const int fit = once_resident(quant_tensor_once_kernel, dev.device) * dev.sm_count;
+    if (fit > 0) {
+      const size_t n4 = n / 4;
+      const unsigned grid = static_cast<unsigned>(std::max<size_t>(
+          1, std::min<size_t>(std::min<size_t>(std::min<size_t>(static_cast<size_t>(fit), 4 * dev.sm_count),
+                                               kQuantPartials),
+                              (n4 + kQThreads - 1) / kQThreads)));
+      cudaError_t e = qlaunch(dev, quant_tensor_once_kernel, grid, st, x, n4, amax_scratch, sync, q, scale, status);
+      if (ls) ls->launches++;
+      return e;
+    }
   }
   // Pass 1 writes one partial maximum per block into amax_scratch, which must
   // hold kQuantPartials floats (per tensor) or m floats (per row).

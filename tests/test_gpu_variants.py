@@ -9,6 +9,8 @@ matmul_int8_parallel (parallel.rs:308-346) with its INT32 sums, which equals
 the scalar matmul_int8 (int8.rs:61-98) element for element and finishes
 these sizes in seconds on the host's cores.
 """
+import ctypes
+
 import numpy as np
 import pytest
 
@@ -240,3 +242,49 @@ def test_options_reject_bad_values(mri, gpu_ctx):
     with pytest.raises(ValueError):
         gpu_ctx.set_option(99, 1)
     assert gpu_ctx.get_option(mri.OPT_PDL) == 1
+
+
+# ── the one-launch per-tensor quantizer ──────────────────────────────────────
+
+@pytest.mark.parametrize("m,k", [(1, 16), (1, 28672), (512, 4096), (2048, 8192), (3, 4100), (7, 5)])
+def test_one_launch_quantizer_repeated_calls_exact(mri, oracle, gpu_ctx, m, k):
+    """quantize_symmetric per tensor (symmetric.rs:42-57) through the
+    one-launch kernel (grid barrier between the absmax and the quantization;
+    at 2048 x 8192 most values are re-read after the barrier, at 512 x 4096
+    all stay in registers) and, for sizes not a multiple of 4, the two-kernel
+    path: scale and codes bit-equal to the oracle on three calls in a row
+    with different inputs (the barrier words are reused)."""
+    import torch
+    rng = np.random.default_rng(m + k)
+    q = torch.empty(m, k, dtype=torch.int8, device="cuda")
+    s = torch.empty(1, device="cuda")
+    lib = mri._lib.load()
+    for rep in range(3):
+        x = (rng.normal(0, 1, size=(m, k)) * (1.0 + 3 * rep)).astype(np.float32)
+        x.reshape(-1)[rng.integers(0, m * k)] = 0.5 * np.abs(x).max()
+        xd = torch.from_numpy(x).cuda()
+        torch.cuda.synchronize()
+        rc = lib.mri_quantize_symmetric(gpu_ctx.handle, ctypes.c_void_p(xd.data_ptr()), m, k, mri.PER_TENSOR,
+                                        ctypes.c_void_p(q.data_ptr()), ctypes.c_void_p(s.data_ptr()))
+        assert rc == 0, mri._lib.last_error()
+        gpu_ctx.synchronize()
+        want_q, want_s = oracle.quantize_symmetric(x)
+        assert np.float32(s.item()) == want_s, rep
+        assert np.array_equal(q.cpu().numpy().reshape(-1), want_q), rep
+    gpu_ctx.check_device_status()
+
+
+def test_one_launch_quantizer_feeds_gemm_exact(mri, oracle, gpu_ctx):
+    """Consecutive prefill products on one stream (quantizer -> GEMM ->
+    quantizer -> GEMM under programmatic dependent launch): each output
+    bit-equal to the oracle."""
+    rng = np.random.default_rng(90)
+    m, n, k = 300, 1024, 4096
+    wq, ws = weights(rng, n, k)
+    qm = mri.QuantizedMatrix(wq, ws, n, k)
+    import torch
+    xs = [rng.normal(0, 1 + i, size=(m, k)).astype(np.float32) for i in range(3)]
+    outs = [mri.matmul_int8_from_f32(torch.from_numpy(x).cuda(), qm) for x in xs]
+    for x, o in zip(xs, outs):
+        want, _, _, _ = oracle_from_f32(oracle, x, wq, ws, n, k)
+        assert np.array_equal(bits(o.cpu().numpy()), bits(want))

@@ -288,3 +288,42 @@ def test_one_launch_quantizer_feeds_gemm_exact(mri, oracle, gpu_ctx):
     for x, o in zip(xs, outs):
         want, _, _, _ = oracle_from_f32(oracle, x, wq, ws, n, k)
         assert np.array_equal(bits(o.cpu().numpy()), bits(want))
+
+
+# ── Q4_0 at one row: int16 activations on dp2a, f32 for non-finite rows ─────
+
+@pytest.mark.parametrize("n,k", [(11008, 4096), (300, 1024), (7, 32), (2049, 8192)])
+def test_q4_0_one_row_int16_path(mri, oracle, n, k):
+    """matmul_q4_0_dequant (q4_0.rs:94-181) at M = 1: the activation row is
+    quantized to int16 and the block dots run on dp2a; within the Q4_0 bar of
+    the reference's f32 sum, including rows whose activations span a wide
+    range (a few large values, many tiny ones)."""
+    from test_gpu_parity import q4_close
+    rng = np.random.default_rng(n + k)
+    wf = rng.normal(0, 0.02, size=(n, k)).astype(np.float32)
+    wb = oracle.quantize_q4_0_matrix(wf, n, k)
+    wdeq = oracle.dequantize_q4_0(wb).reshape(n, k)
+    for x in (rng.normal(0, 1, size=(1, k)).astype(np.float32),
+              (rng.normal(0, 1e-3, size=(1, k)) * (rng.random((1, k)) < 0.99) +
+               rng.normal(0, 50, size=(1, k)) * (rng.random((1, k)) >= 0.99)).astype(np.float32),
+              np.zeros((1, k), np.float32)):
+        got = mri.matmul_q4_0_dequant(x, wb, n, k)
+        want = oracle.matmul_q4_0_dequant(x, 1, k, wb, n, k)
+        ok, worst = q4_close(got, want, x, wdeq)
+        assert ok, worst
+
+
+def test_q4_0_one_row_non_finite_takes_f32_path(mri, oracle):
+    """An inf or a NaN in the activation row: the f32 path, so the outputs
+    are non-finite exactly where the reference's are (q4_0.rs:94-181)."""
+    rng = np.random.default_rng(77)
+    n, k = 1000, 4096
+    wb = oracle.quantize_q4_0_matrix(rng.normal(0, 0.02, size=(n, k)).astype(np.float32), n, k)
+    for special in (np.inf, -np.inf, np.nan):
+        x = rng.normal(0, 1, size=(1, k)).astype(np.float32)
+        x[0, 123] = special
+        got = mri.matmul_q4_0_dequant(x, wb, n, k)
+        want = oracle.matmul_q4_0_dequant(x, 1, k, wb, n, k)
+        assert np.array_equal(np.isnan(got), np.isnan(want)), special
+        assert np.array_equal(np.isposinf(got), np.isposinf(want)), special
+        assert np.array_equal(np.isneginf(got), np.isneginf(want)), special

@@ -66,6 +66,9 @@ def parse_args():
                     help="skip the timed CPU sample (profiling runs)")
     ap.add_argument("--only", choices=["q8_0", "q4_0", "prefill", "model", "chain", "cpu", "sharded"],
                     help="run one side measurement alone and print it (profiling runs)")
+    ap.add_argument("--model-layers", type=int, default=32,
+                    help="layers of the Llama-7B-shaped model (profiling runs of its kernels on a "
+                         "smaller device footprint; the reported config uses 32)")
     return ap.parse_args()
 
 
@@ -345,7 +348,7 @@ def cpu_side_baselines():
     return res
 
 
-def secondary_measurements(torch, mri, lib, device, peak_hbm, peak_tc, parts=SIDE_PARTS):
+def secondary_measurements(torch, mri, lib, device, peak_hbm, peak_tc, parts=SIDE_PARTS, model_layers=32):
     """Q8_0 / Q4_0 decode (M=1, M=8), the prefill GEMM and the 7B model, 1 GPU;
     the products from CUDA graphs over rotating weight copies."""
     res = {}
@@ -453,7 +456,7 @@ def secondary_measurements(torch, mri, lib, device, peak_hbm, peak_tc, parts=SID
         res["prefill_m512"] = {"error": str(e)[:200]}
     ctx.synchronize()
     if "model" in parts:
-        res["llama7b_int8"] = model_measurement(mri, device, peak_hbm)
+        res["llama7b_int8"] = model_measurement(mri, device, peak_hbm, model_layers)
     if "chain" in parts:
         try:
             res["decode_gemv_forms"] = decode_chain_measurement(torch, mri, lib, device, peak_hbm)
@@ -467,13 +470,13 @@ def secondary_measurements(torch, mri, lib, device, peak_hbm, peak_tc, parts=SID
     return res
 
 
-def model_measurement(mri, device, peak_hbm):
+def model_measurement(mri, device, peak_hbm, layers=32):
     """Llama-7B-shaped LlamaModelInt8 (32 layers, d=4096,
     32 heads, FFN 11008, vocab 32000), synthetic weights generated on the
     device, 512-token prefill then 128 greedy decode steps (CUDA graph per
     step).  The second of two runs is reported."""
     try:
-        L, d, ffn, V = 32, 4096, 11008, 32000
+        L, d, ffn, V = layers, 4096, 11008, 32000
         cfg = mri.LlamaConfig(L, d, 32, ffn, V, 640)
         m = mri.LlamaModelInt8.random(cfg, seed=1, ctx=mri.Context(device))
         prompt = np.random.default_rng(0).integers(0, V, size=512).astype(np.uint32)
@@ -605,7 +608,8 @@ def run_ours(args, rank, world, local_rank):
         if args.only == "sharded":
             out = sharded_measurement(torch, mri, device, world, dist, peak_hbm, peak_tc)
         else:
-            out = secondary_measurements(torch, mri, lib, device, peak_hbm, peak_tc, parts=(args.only,))
+            out = secondary_measurements(torch, mri, lib, device, peak_hbm, peak_tc, parts=(args.only,),
+                                         model_layers=args.model_layers)
         if rank == 0:
             print(json.dumps({"only": args.only, "n_gpus": world, "result": out}), flush=True)
         if dist:

@@ -30,15 +30,16 @@
 #include <string>
 #include <vector>
 
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "internal.h"
 #include "mri_gpu.h"
 
+namespace cg = cooperative_groups;
+
 namespace {
 
-constexpr int kAttnRounds = 1;   // rounds of 8 keys per warp in decode attention
-constexpr int kAttnChunk = 4 * 8 * kAttnRounds;  // keys per split (4 warps)
-constexpr int kMergeChunk = 256;  // splits whose merge weights sit in shared memory at once
 constexpr int kPrefillQ = 16;    // queries per block in prefill attention
 constexpr int kPrefillKT = 64;   // keys per shared-memory tile in prefill attention
 constexpr int kMaxHeadDim = 128;
@@ -139,63 +140,59 @@ __global__ void rope_kv_kernel(float* __restrict__ qkv, int ld, int n_heads, int
   }
 }
 
-// Decode attention, split over keys (attention/cached.rs:141-190 with
-// gqa.rs:217-237): block (h, s) handles keys [s*C, min(s*C+C, pos+1)) for
-// C = kAttnChunk (32).  Warp w takes 8 of them; a lane owns 4 head dimensions
-// (hd % 4 == 0, hd <= 128), loads its keys' and values' float4 before using any,
-// reduces each score over the warp with shuffles and keeps an online
-// softmax (running max, exp-sum, weighted V sum) — no block-wide barrier until
-// the 4 warps' partials are combined.  Each block writes its partial; the last
-// block of a head to finish (ticket counter) merges the head's splits and
-// resets the counter for the next launch.
-__global__ void __launch_bounds__(128) attn_decode_kernel(const float* __restrict__ q, int n_heads,
-                                                          int n_kv, int hd,
-                                                          const float* __restrict__ kc,
-                                                          const float* __restrict__ vc,
-                                                          const int* __restrict__ pos_dev, float scale,
-                                                          float* __restrict__ part, int max_splits,
-                                                          int* __restrict__ tickets,
-                                                          float* __restrict__ out) {
+// Decode attention on thread-block clusters (attention/cached.rs:141-190
+// with gqa.rs:217-237): the kDecCluster CTAs of one cluster share head h, CTA
+// c taking the keys [c*chunk, (c+1)*chunk) of the pos + 1 cached ones.  Each
+// of its 8 warps scores rounds of 8 keys (warp w: keys base + 64 r + 8 w + i),
+// a lane owning 4 head dimensions, with all of a round's K and V float4 loaded
+// before any is used, and keeps an online softmax (running max, exp-sum,
+// weighted V sum).  The warps' partials are combined in warp order into the
+// CTA's partial in shared memory; after a cluster barrier CTA 0 reads the
+// other CTAs' partials through distributed shared memory and merges them in
+// rank order (no global scratch, fence or ticket), and a second cluster
+// barrier keeps every CTA's shared memory alive until that read is done.
+// Every CTA reaches both barriers (a CTA without keys contributes m = -inf).
+constexpr int kDecCluster = 8;
+constexpr int kDecWarps = 8;
+constexpr int kDecRound = 8;
+
+__global__ void __cluster_dims__(1, kDecCluster, 1) __launch_bounds__(kDecWarps * 32)
+    attn_decode_cluster_kernel(const float* __restrict__ q, int n_heads, int n_kv, int hd,
+                               const float* __restrict__ kc, const float* __restrict__ vc,
+                               const int* __restrict__ pos_dev, float scale, float* __restrict__ out) {
   pdl_trigger();
   pdl_wait();
-  const int h = blockIdx.x, s = blockIdx.y;
-  const int pos = mri::ld_act(pos_dev);
-  const int j0 = s * kAttnChunk;
-  if (j0 > pos) return;
-  const int active = pos / kAttnChunk + 1;
-  const int nkeys = min(kAttnChunk, pos + 1 - j0);
+  cg::cluster_group cluster = cg::this_cluster();
+  const int h = blockIdx.x;
+  const int c = static_cast<int>(cluster.block_rank());
+  const int total = mri::ld_act(pos_dev) + 1;
+  const int chunk = (total + kDecCluster - 1) / kDecCluster;
+  const int j0 = c * chunk, j1 = min(total, j0 + chunk);
   const int kv_h = h / (n_heads / n_kv);
   const int kvd = n_kv * hd;
-  constexpr int kStride = kMaxHeadDim + 2;
-  constexpr int kRound = 8;  // keys in flight per warp
-  __shared__ float wm[4], wl[4];
-  __shared__ __align__(16) float wo[4][kMaxHeadDim];
-  __shared__ int last;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool dim_ok = lane * 4 < hd;
   const size_t base = static_cast<size_t>(kv_h) * hd + lane * 4;
+  __shared__ float wm[kDecWarps], wl[kDecWarps];
+  __shared__ __align__(16) float wo[kDecWarps][kMaxHeadDim];
+  __shared__ __align__(16) float cpart[kMaxHeadDim + 4];  // o[hd], then m, l
   const float4 qv = dim_ok ? mri::ld_act(reinterpret_cast<const float4*>(q + h * hd + lane * 4))
                            : make_float4(0.f, 0.f, 0.f, 0.f);
   float m = -INFINITY, l = 0.0f;
   float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-  // All of the warp's keys and values are loaded before any is used (one
-  // memory latency per split), then scored in key order.
-  float4 kk[kAttnRounds * kRound], vv[kAttnRounds * kRound];
+  for (int k0 = j0 + warp * kDecRound; k0 < j1; k0 += kDecWarps * kDecRound) {
+    float4 kk[kDecRound], vv[kDecRound];
 #pragma unroll
-  for (int i = 0; i < kAttnRounds * kRound; ++i) {
-    const int key = warp * kAttnRounds * kRound + i;
-    const bool ok = dim_ok && key < nkeys;
-    const size_t row = static_cast<size_t>(j0 + key) * kvd + base;
-    kk[i] = ok ? mri::ld_act(reinterpret_cast<const float4*>(kc + row)) : make_float4(0.f, 0.f, 0.f, 0.f);
-    vv[i] = ok ? mri::ld_act(reinterpret_cast<const float4*>(vc + row)) : make_float4(0.f, 0.f, 0.f, 0.f);
-  }
+    for (int i = 0; i < kDecRound; ++i) {
+      const bool ok = dim_ok && k0 + i < j1;
+      const size_t row = static_cast<size_t>(k0 + i) * kvd + base;
+      kk[i] = ok ? mri::ld_act(reinterpret_cast<const float4*>(kc + row)) : make_float4(0.f, 0.f, 0.f, 0.f);
+      vv[i] = ok ? mri::ld_act(reinterpret_cast<const float4*>(vc + row)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
 #pragma unroll
-  for (int r = 0; r < kAttnRounds; ++r) {
-    const int k0 = warp * kAttnRounds * kRound + r * kRound;  // first key of this round, within the chunk
-#pragma unroll
-    for (int i = 0; i < kRound; ++i) {
-      if (k0 + i >= nkeys) break;  // warp-uniform
-      const float4 kv = kk[r * kRound + i], vw = vv[r * kRound + i];
+    for (int i = 0; i < kDecRound; ++i) {
+      if (k0 + i >= j1) break;  // warp-uniform
+      const float4 kv = kk[i], vw = vv[i];
       float d = __fmaf_rn(qv.x, kv.x, 0.0f);
       d = __fmaf_rn(qv.y, kv.y, d);
       d = __fmaf_rn(qv.z, kv.z, d);
@@ -212,81 +209,58 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const float* __restric
       m = mn;
     }
   }
-  // Combine the 4 warps (a warp without keys has m = -inf, l = 0).
+  // The CTA's partial: warps combined in warp order (a warp without keys has
+  // m = -inf, l = 0).
   if (lane == 0) {
     wm[warp] = m;
     wl[warp] = l;
   }
   if (dim_ok) reinterpret_cast<float4*>(wo[warp])[lane] = o;
   __syncthreads();
-  const float bm = fmaxf(fmaxf(wm[0], wm[1]), fmaxf(wm[2], wm[3]));
-  float* pout = part + (static_cast<size_t>(h) * max_splits + s) * kStride;
+  float bm = -INFINITY;
+#pragma unroll
+  for (int w = 0; w < kDecWarps; ++w) bm = fmaxf(bm, wm[w]);
   for (int t = threadIdx.x; t < hd; t += blockDim.x) {
     float acc = 0.0f;
 #pragma unroll
-    for (int w = 0; w < 4; ++w)
+    for (int w = 0; w < kDecWarps; ++w)
       if (wm[w] != -INFINITY) acc = __fmaf_rn(wo[w][t], expf(wm[w] - bm), acc);
-    pout[2 + t] = acc;
+    cpart[t] = acc;
   }
   if (threadIdx.x == 0) {
     float bl = 0.0f;
-    for (int w = 0; w < 4; ++w)
+#pragma unroll
+    for (int w = 0; w < kDecWarps; ++w)
       if (wm[w] != -INFINITY) bl = __fmaf_rn(wl[w], expf(wm[w] - bm), bl);
-    pout[0] = bm;
-    pout[1] = bl;
+    cpart[kMaxHeadDim] = bm;
+    cpart[kMaxHeadDim + 1] = bl;
   }
-  // Publish this split, then take a ticket; the last split of the head merges.
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) last = atomicAdd(&tickets[h], 1) == active - 1;
-  __syncthreads();
-  if (!last) return;
-  __threadfence();
-  // Merge.  The splits' maxima are read in parallel and each split's weight
-  // exp(m_t - gm) is computed once into shared memory; the sums then run over
-  // t in increasing order as before (loads independent, so they overlap).
-  const float* ph = part + static_cast<size_t>(h) * max_splits * kStride;
-  __shared__ float s_w[kMergeChunk];
-  __shared__ float s_red[4];
-  float lm = -INFINITY;
-  for (int t = threadIdx.x; t < active; t += blockDim.x) lm = fmaxf(lm, __ldcg(ph + t * kStride));
-  lm = mri::warp_max(lm);
-  if (lane == 0) s_red[warp] = lm;
-  __syncthreads();
-  const float gm = fmaxf(fmaxf(s_red[0], s_red[1]), fmaxf(s_red[2], s_red[3]));
-  float gl = 0.0f;
-  float acc[(kMaxHeadDim + 127) / 128];
+  cluster.sync();
+  if (c == 0) {
+    // Merge the cluster's partials in rank order.
+    float pm[kDecCluster], pw[kDecCluster];
+    float gm = -INFINITY;
 #pragma unroll
-  for (int i = 0; i < (kMaxHeadDim + 127) / 128; ++i) acc[i] = 0.0f;
-  for (int t0 = 0; t0 < active; t0 += kMergeChunk) {
-    const int tn = min(kMergeChunk, active - t0);
-    const float* pc = ph + static_cast<size_t>(t0) * kStride;
-    for (int t = threadIdx.x; t < tn; t += blockDim.x) s_w[t] = expf(__ldcg(pc + t * kStride) - gm);
-    __syncthreads();
-    if (threadIdx.x == 0) {
-#pragma unroll 8
-      for (int t = 0; t < tn; ++t) gl += __ldcg(pc + t * kStride + 1) * s_w[t];
+    for (int r = 0; r < kDecCluster; ++r) {
+      const float* pr = cluster.map_shared_rank(cpart, r);
+      pm[r] = pr[kMaxHeadDim];
+      gm = fmaxf(gm, pm[r]);
     }
+    float gl = 0.0f;
 #pragma unroll
-    for (int i = 0; i < (kMaxHeadDim + 127) / 128; ++i) {
-      const int d = threadIdx.x + i * 128;
-      if (d < hd) {
-#pragma unroll 8
-        for (int t = 0; t < tn; ++t) acc[i] += __ldcg(pc + t * kStride + 2 + d) * s_w[t];
-      }
+    for (int r = 0; r < kDecCluster; ++r) {
+      pw[r] = pm[r] == -INFINITY ? 0.0f : expf(pm[r] - gm);
+      gl = __fmaf_rn(cluster.map_shared_rank(cpart, r)[kMaxHeadDim + 1], pw[r], gl);
     }
-    __syncthreads();
-  }
-  __shared__ float s_gl;
-  if (threadIdx.x == 0) s_gl = gl;
-  __syncthreads();
-  const float inv = __fdiv_rn(1.0f, s_gl);
+    const float inv = __fdiv_rn(1.0f, gl);
+    for (int t = threadIdx.x; t < hd; t += blockDim.x) {
+      float acc = 0.0f;
 #pragma unroll
-  for (int i = 0; i < (kMaxHeadDim + 127) / 128; ++i) {
-    const int d = threadIdx.x + i * 128;
-    if (d < hd) out[h * hd + d] = acc[i] * inv;
+      for (int r = 0; r < kDecCluster; ++r) acc = __fmaf_rn(cluster.map_shared_rank(cpart, r)[t], pw[r], acc);
+      out[h * hd + t] = acc * inv;
+    }
   }
-  if (threadIdx.x == 0) tickets[h] = 0;
+  cluster.sync();
 }
 
 // Prefill attention (gqa.rs:217-237 with mask.rs:77-115): block (h, qb)
@@ -823,8 +797,8 @@ struct mri_llama {
   // cache and activations
   float *kc = nullptr, *vc = nullptr;
   float *x = nullptr, *qkv = nullptr, *attn = nullptr, *gu = nullptr;
-  float *logits = nullptr, *part = nullptr;
-  int* tickets = nullptr;      // [n_heads] decode-attention split counters, then 1 argmax counter
+  float* logits = nullptr;
+  int* tickets = nullptr;      // the greedy argmax's ticket counter
   float* fa_part = nullptr;    // prefill attention: two split records per (query block, head)
   int* fa_tickets = nullptr;   // prefill attention: split counters per (query block, head)
   int* fa_range = nullptr;     // prefill attention: set when q, k or v lay beyond the f16 range
@@ -836,7 +810,6 @@ struct mri_llama {
   uint32_t* d_tokens = nullptr;
   uint32_t* d_gen = nullptr;  // [max_seq + 1] tokens produced by greedy argmax
   int* d_pos = nullptr;
-  int max_splits = 0;
   cudaGraphExec_t decode_exec = nullptr;
   size_t graph_kernels = 0;
   std::vector<void*> allocs;
@@ -951,9 +924,8 @@ int run_blocks(mri_llama* m, size_t rows, int pos0, bool decode_dev, uint32_t l_
       }
     }
     if (decode_dev) {
-      LL_TRY(pdl_launch(m, attn_decode_kernel, dim3(c.n_heads, m->max_splits), dim3(128), st, m->qkv,
-                        c.n_heads, c.n_kv_heads, m->hd, kc, vc, m->d_pos, scale, m->part,
-                        m->max_splits, m->tickets, m->attn));
+      LL_TRY(pdl_launch(m, attn_decode_cluster_kernel, dim3(c.n_heads, kDecCluster), dim3(kDecWarps * 32), st,
+                        m->qkv, c.n_heads, c.n_kv_heads, m->hd, kc, vc, m->d_pos, scale, m->attn));
     } else if ((m->hd == 64 || m->hd == 128) && (m->qkv_w % 2) == 0 && (m->qd % 2) == 0 &&
                m->ctx->dev.opt.tc_attn && !m->cuda_core_attn) {
       // Key tiles from which a query block's walk is split over two blocks (0 = never).
@@ -1067,7 +1039,7 @@ int forward_rows(mri_llama* m, const uint32_t* tokens, size_t n, size_t pos0, fl
 
 int launch_argmax(mri_llama* m) {
   LL_TRY(pdl_launch(m, argmax_kernel, dim3(kArgmaxBlocks), dim3(256), m->ctx->stream, m->logits,
-                    static_cast<int>(m->cfg.vocab), m->amax_v, m->amax_i, m->tickets + m->cfg.n_heads,
+                    static_cast<int>(m->cfg.vocab), m->amax_v, m->amax_i, m->tickets,
                     m->d_tokens, m->d_pos, m->d_gen));
   return MRI_OK;
 }
@@ -1145,7 +1117,6 @@ int mri_llama_create(mri_ctx* ctx, const mri_llama_config* cfg, mri_llama** out)
   m->kvd = static_cast<int>(n_kv) * hd;
   m->qkv_w = m->qd + 2 * m->kvd;
   m->max_tokens = c.max_seq;
-  m->max_splits = static_cast<int>((c.max_seq + kAttnChunk - 1) / kAttnChunk);
   const size_t T = m->max_tokens;
   const BlobLayout b = blob_layout(m);
   int rc = MRI_OK;
@@ -1164,11 +1135,10 @@ int mri_llama_create(mri_ctx* ctx, const mri_llama_config* cfg, mri_llama** out)
   rc = rc ? rc : dalloc(m, &m->attn, T * m->qd);
   rc = rc ? rc : dalloc(m, &m->gu, T * 2 * c.ffn_dim);
   rc = rc ? rc : dalloc(m, &m->logits, T * c.vocab);
-  rc = rc ? rc : dalloc(m, &m->part, static_cast<size_t>(c.n_heads) * m->max_splits * (kMaxHeadDim + 2));
   rc = rc ? rc : dalloc(m, &m->d_tokens, T);
   rc = rc ? rc : dalloc(m, &m->d_gen, T + 1);
   rc = rc ? rc : dalloc(m, &m->d_pos, 1);
-  rc = rc ? rc : dalloc(m, &m->tickets, c.n_heads + 1);
+  rc = rc ? rc : dalloc(m, &m->tickets, 1);
   const size_t fa_pairs = static_cast<size_t>(c.n_heads) * ((m->max_tokens + kFaQ - 1) / kFaQ);
   if (m->hd == 64 || m->hd == 128) {
     rc = rc ? rc : dalloc(m, &m->fa_part, fa_pairs * 2 * kFaQ * (m->hd + 2));
@@ -1188,7 +1158,7 @@ int mri_llama_create(mri_ctx* ctx, const mri_llama_config* cfg, mri_llama** out)
     mri_llama_free(m);
     return fail(r, "scratch reservation: %s", mri_last_error());
   }
-  cudaMemset(m->tickets, 0, (c.n_heads + 1) * sizeof(int));
+  cudaMemset(m->tickets, 0, sizeof(int));
   if (m->fa_tickets) cudaMemset(m->fa_tickets, 0, fa_pairs * sizeof(int));
   cudaMemset(m->fa_range, 0, sizeof(int));
   cudaMemset(m->kc, 0, static_cast<size_t>(c.n_layers) * c.max_seq * m->kvd * sizeof(float));

@@ -586,6 +586,42 @@ def sharded_measurement(torch, mri, device, world, dist, peak_hbm, peak_tc):
                                 "tops_per_gpu": round(ops / world / t / 1e12, 2),
                                 "frac_int8_per_gpu": round(ops / world / t / 1e12 / (2 * peak_tc), 4),
                                 "gather_bytes_per_rank": 4 * M * N}
+        # Components of one call, each timed alone (max over ranks): the
+        # rank's shard product, and an NCCL all-gather of the same f32 bytes.
+        if world > 1:
+            out_s = torch.empty(M, ns, device=f"cuda:{device}")
+
+            def shard_call(i):
+                rc = lib.mri_matmul_int8_from_f32(ctx.handle, ctypes.c_void_p(x.data_ptr()), M, K,
+                                                  mats[i % copies].handle, ctypes.c_void_p(out_s.data_ptr()))
+                if rc != 0:
+                    raise RuntimeError(mri._lib.last_error())
+            shard_call(0)
+            ctx.synchronize()
+            dist.barrier()
+            with torch.cuda.stream(s):
+                e0.record(s)
+                for i in range(reps):
+                    shard_call(i)
+                e1.record(s)
+            ctx.synchronize()
+            gemm_ms = max_ms(e0.elapsed_time(e1)) / reps
+            flat = out_s.reshape(-1)
+            gathered = torch.empty(world * flat.numel(), device=f"cuda:{device}")
+            dist.all_gather_into_tensor(gathered, flat)
+            torch.cuda.synchronize()
+            dist.barrier()
+            g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            cur = torch.cuda.current_stream(device)
+            g0.record(cur)
+            for _ in range(reps):
+                dist.all_gather_into_tensor(gathered, flat)
+            g1.record(cur)
+            torch.cuda.synchronize()
+            ag_ms = max_ms(g0.elapsed_time(g1)) / reps
+            res[f"{name}_m2048"]["components_ms"] = {"shard_gemm": round(gemm_ms, 4),
+                                                     "allgather_alone": round(ag_ms, 4)}
+            del out_s, gathered
         del x, out, mats
         torch.cuda.empty_cache()
     comm.close()

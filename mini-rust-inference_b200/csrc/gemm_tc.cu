@@ -481,7 +481,7 @@ template <int BN, int kStages, int kBufs = 2>
 cudaError_t launch_bn(const DeviceInfo& dev, cudaStream_t st, const CUtensorMap& ta,
                       const CUtensorMap& tb, const float* act_scale, int per_row,
                       const float* w_scales, size_t M, size_t N, size_t K, float* out,
-                      int32_t* acc_out, int* status, const float* residual) {
+                      int32_t* acc_out, int* status, const float* residual, int grid) {
   static_assert(TcLayout<BN, kStages, kBufs>::total <= 232448,
                 "stage ring exceeds the per-CTA shared memory");
   // Two CTAs per SM: both rings plus the 1 KB the runtime reserves per CTA
@@ -492,11 +492,10 @@ cudaError_t launch_bn(const DeviceInfo& dev, cudaStream_t st, const CUtensorMap&
   cudaError_t e = set_smem_tc(gemm_i8_tc_kernel<BN, kStages, kBufs>, smem, dev.device);
   if (e != cudaSuccess) return e;
   const size_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
-  // One tile per CTA when kBufs == 1 (the launcher only picks it for
-  // tiles <= 2 * sm_count).
-  if (kBufs == 1 && tiles > 2 * static_cast<size_t>(dev.sm_count)) return cudaErrorInvalidValue;
+  // One tile per CTA when kBufs == 1; a persistent grid otherwise.
+  if (grid < 1 || (kBufs == 1 && static_cast<size_t>(grid) != tiles)) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(kBufs == 1 ? tiles : std::min<size_t>(tiles, dev.sm_count)));
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
   cfg.blockDim = dim3(kTcThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
@@ -533,22 +532,25 @@ static int persistent_stages(int bn) {
 cudaError_t gemm_i8_tc_plan(const DeviceInfo& dev, size_t M, size_t N, size_t K, GemmPlan* plan) {
   if (!gemm_i8_tc_supported(dev, M, N, K)) return cudaErrorInvalidValue;
   GemmPlan p;
-  p.bn = pick_bn(dev, M, N);
+  // SMs the grid may use (the sharded product keeps some free for NCCL).
+  const int sms = std::max(1, dev.sm_count - std::max(0, dev.opt.sm_reserve));
+  DeviceInfo d2 = dev;
+  d2.sm_count = sms;
+  p.bn = pick_bn(d2, M, N);
   p.tiles = static_cast<int>(((M + BM - 1) / BM) * ((N + p.bn - 1) / p.bn));
   // Between one and two rounds of tiles, one tile per CTA with two CTAs per
   // SM (3-stage rings, one accumulator buffer each): the second CTA's loads
   // and MMAs fill the first one's gaps, and each CTA's epilogue overlaps the
   // other's main loop.  The context's MRI_OPT_GEMM_2CTA = 0 keeps the
   // persistent grid.
-  if (dev.opt.gemm_2cta && (p.bn == 128 || p.bn == 160) && p.tiles > dev.sm_count &&
-      p.tiles <= 2 * dev.sm_count) {
+  if (dev.opt.gemm_2cta && (p.bn == 128 || p.bn == 160) && p.tiles > sms && p.tiles <= 2 * sms) {
     p.bufs = 1;
     p.stages = 3;
     p.grid = p.tiles;
   } else {
     p.bufs = 2;
     p.stages = persistent_stages(p.bn);
-    p.grid = std::min(p.tiles, dev.sm_count);
+    p.grid = std::min(p.tiles, sms);
   }
   p.tiles_per_cta = (p.tiles + p.grid - 1) / p.grid;
   *plan = p;
@@ -567,7 +569,7 @@ cudaError_t launch_gemm_i8_tc(const DeviceInfo& dev, cudaStream_t st, const int8
   CUtensorMap ta, tb;
   if (!make_map(&ta, xq, M, K, BM) || !make_map(&tb, W, N, K, p.bn)) return cudaErrorInvalidValue;
   cudaError_t e;
-#define MRI_GEMM_ARGS dev, st, ta, tb, act_scale_dev, scale_per_row, w_scales, M, N, K, out, acc_out, status, residual
+#define MRI_GEMM_ARGS dev, st, ta, tb, act_scale_dev, scale_per_row, w_scales, M, N, K, out, acc_out, status, residual, p.grid
   if (p.bufs == 1) {
     e = p.bn == 128 ? launch_bn<128, 3, 1>(MRI_GEMM_ARGS) : launch_bn<160, 3, 1>(MRI_GEMM_ARGS);
   } else {

@@ -97,6 +97,9 @@ struct Options {
   int tc_attn = 1;     // MRI_OPT_TC_ATTN: tensor-core prefill attention (head dim 64 / 128)
   int fa_split = 3;    // MRI_OPT_FA_SPLIT: key tiles from which a prefill key walk is split (0 = never)
   int shard_peer = 0;  // MRI_OPT_SHARD_PEER: sharded m <= 8 gathered over peer memory instead of NCCL
+  // Internal (not an ABI option): SMs the tensor-core GEMM leaves free for
+  // other work running beside it.
+  int sm_reserve = 0;
 };
 
 // Per-device properties the launchers need, and the context's options.

@@ -510,7 +510,8 @@ def sharded_measurement(torch, mri, device, world, dist, peak_hbm, peak_tc):
     comm = mri.Communicator.from_process_group(ctx=ctx) if world > 1 else \
         mri.Communicator(mri.Communicator.unique_id(), 1, 0, ctx=ctx)
     lib = ctx._lib
-    res = {"P": world, "collective": "NCCL all-gather of f32 [M, N/P] slices",
+    res = {"P": world, "collective": "M = 1: NCCL all-gather of f32 [M, N/P] slices; M = 2048: each "
+                                    "rank's GEMM epilogue writes its tiles to every rank over NVLink",
            "data": "synthetic int8 weights, x ~ N(0,1)"}
     rng = np.random.default_rng(comm.rank)
 
@@ -586,6 +587,23 @@ def sharded_measurement(torch, mri, device, world, dist, peak_hbm, peak_tc):
                                 "tops_per_gpu": round(ops / world / t / 1e12, 2),
                                 "frac_int8_per_gpu": round(ops / world / t / 1e12 / (2 * peak_tc), 4),
                                 "gather_bytes_per_rank": 4 * M * N}
+        if world > 1:
+            # The same call gathered by NCCL (OPT_SHARD_PEER = 0): the chunked
+            # all-gather of f32 slices and the unshard copy.
+            ctx.set_option(mri.OPT_SHARD_PEER, 0)
+            call(0)
+            comm.wait()
+            dist.barrier()
+            with torch.cuda.stream(s):
+                e0.record(s)
+                for i in range(reps):
+                    call(i)
+                e1.record(s)
+            comm.wait()
+            ctx.set_option(mri.OPT_SHARD_PEER, 2)
+            tp = max_ms(e0.elapsed_time(e1)) / 1e3 / reps
+            res[f"{name}_m2048"]["nccl_allgather"] = {"ms_per_call": round(tp * 1e3, 4),
+                                                      "tops_aggregate": round(ops / tp / 1e12, 2)}
         # Components of one call, each timed alone (max over ranks): the
         # rank's shard product, and an NCCL all-gather of the same f32 bytes.
         if world > 1:

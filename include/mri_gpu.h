@@ -102,7 +102,9 @@ enum mri_option {
                              0: the CUDA-core kernel */
   MRI_OPT_FA_SPLIT = 6,   /* 3 (default): prefill key walks of at least this many 64-key tiles are
                              split over two blocks; 0: never */
-  MRI_OPT_SHARD_PEER = 7  /* 0 (default): sharded m <= 8 gathered by NCCL; 1: over peer memory */
+  MRI_OPT_SHARD_PEER = 7  /* sharded products: 2 (default) gathered over peer memory for m > 8 (the
+                             GEMM epilogue writes each tile to every rank) and by NCCL for m <= 8;
+                             1: over peer memory for every m; 0: NCCL for every m */
 };
 MRI_API int mri_ctx_set_option(mri_ctx* ctx, int option, int value);
 MRI_API int mri_ctx_get_option(mri_ctx* ctx, int option, int* value);

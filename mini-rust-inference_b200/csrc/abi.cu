@@ -517,6 +517,7 @@ int mri_ctx_set_option(mri_ctx* ctx, int option, int value) {
   switch (option) {
     case MRI_OPT_GEMM_BN: ok = value == 0 || (value >= 128 && value <= 256 && value % 32 == 0); break;
     case MRI_OPT_FA_SPLIT: ok = value >= 0; break;
+    case MRI_OPT_SHARD_PEER: ok = value >= 0 && value <= 2; break;
     default: ok = value == 0 || value == 1;
   }
   if (!ok) return fail(MRI_ERR_INVALID_ARGUMENT, "value %d out of range for option %d", value, option);

@@ -154,10 +154,12 @@ template <int BN, int kStages, int kBufs>
 __global__ void __launch_bounds__(kTcThreads, kBufs == 1 ? 2 : 1)
     gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const float* __restrict__ act_scale, int scale_per_row,
-                      const float* __restrict__ w_scales, float* out,
+                      const float* __restrict__ w_scales, const __grid_constant__ GemmOut go,
                       int32_t* __restrict__ acc_out, int M, int N, int K, int* status,
                       const float* residual) {
   using L = TcLayout<BN, kStages, kBufs>;
+  float* const out = go.out;
+  const size_t ldo = go.ldo;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_addr(smem_raw);
   uint8_t* smem = smem_raw + ((1024 - (raw & 1023)) & 1023);
@@ -279,9 +281,13 @@ __global__ void __launch_bounds__(kTcThreads, kBufs == 1 ? 2 : 1)
     const int et = threadIdx.x - 64;  // 0..127 among the epilogue warps
     asm volatile("griddepcontrol.wait;" ::: "memory");
     const float s_all = scale_per_row ? 0.0f : ld_act(act_scale);
-    const bool vec = (N % 4) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0 &&
+    const bool vec = (N % 4) == 0 && (ldo % 4) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0 &&
                      (reinterpret_cast<uintptr_t>(acc_out) & 15) == 0 &&
-                     (reinterpret_cast<uintptr_t>(residual) & 15) == 0;
+                     (reinterpret_cast<uintptr_t>(residual) & 15) == 0 &&
+                     (go.ranks <= 1 || (go.col0 % 4) == 0);
+    // Gathered product: this call's staging half on the other ranks.
+    const unsigned long long gseq = go.ranks > 1 ? ld_act(go.seq + 2) : 0ull;
+    const size_t ghalf = (gseq & 1) * go.half;
     int t = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++t) {
       const int b = t & 1;
@@ -303,9 +309,9 @@ __global__ void __launch_bounds__(kTcThreads, kBufs == 1 ? 2 : 1)
       ok = ok && wait_or_abort(&tfull[b], (t >> 1) & 1, status, abort_flag);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
-      float* orow = out + static_cast<size_t>(row) * N;
+      float* orow = out + static_cast<size_t>(row) * ldo;
       // forward_int8.rs:100-121: x + projected; residual may alias out.
-      const float* rrow = residual ? residual + static_cast<size_t>(row) * N : nullptr;
+      const float* rrow = residual ? residual + static_cast<size_t>(row) * ldo : nullptr;
       int32_t* arow = acc_out ? acc_out + static_cast<size_t>(row) * N : nullptr;
       // This warp's 32 x 32 staging block (16-byte chunks XOR-swizzled by row).
       float* stg = reinterpret_cast<float*>(smem + L::stg) + q * 32 * 32;
@@ -345,7 +351,7 @@ __global__ void __launch_bounds__(kTcThreads, kBufs == 1 ? 2 : 1)
 #pragma unroll
             for (int i = 0; i < 8; ++i)
               rr[i] = ld_act(reinterpret_cast<const float4*>(
-                  residual + static_cast<size_t>(row0 + 4 * i + rs) * N + col0 + 4 * jc));
+                  residual + static_cast<size_t>(row0 + 4 * i + rs) * ldo + col0 + 4 * jc));
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
               o[i].x = __fadd_rn(rr[i].x, o[i].x);
@@ -356,8 +362,16 @@ __global__ void __launch_bounds__(kTcThreads, kBufs == 1 ? 2 : 1)
           }
 #pragma unroll
           for (int i = 0; i < 8; ++i)
-            *reinterpret_cast<float4*>(out + static_cast<size_t>(row0 + 4 * i + rs) * N + col0 + 4 * jc) =
+            *reinterpret_cast<float4*>(out + static_cast<size_t>(row0 + 4 * i + rs) * ldo + col0 + 4 * jc) =
                 o[i];
+          // The other ranks' copies: whole 128-byte row segments over NVLink.
+          for (int p = 0; p < go.ranks; ++p) {
+            if (p == go.rank) continue;
+            float* dst = go.stage[p] + ghalf + go.col0;
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              *reinterpret_cast<float4*>(dst + static_cast<size_t>(row0 + 4 * i + rs) * ldo + col0 + 4 * jc) = o[i];
+          }
           continue;
         }
         if (row < M) {
@@ -382,6 +396,10 @@ __global__ void __launch_bounds__(kTcThreads, kBufs == 1 ? 2 : 1)
                 o.w = __fadd_rn(r[j / 4].w, o.w);
               }
               *reinterpret_cast<float4*>(orow + col0 + j) = o;
+              for (int p = 0; p < go.ranks; ++p)
+                if (p != go.rank)
+                  *reinterpret_cast<float4*>(go.stage[p] + ghalf + go.col0 + static_cast<size_t>(row) * ldo +
+                                             col0 + j) = o;
               if (arow)
                 *reinterpret_cast<int4*>(arow + col0 + j) =
                     make_int4(static_cast<int>(v[j]), static_cast<int>(v[j + 1]),
@@ -394,6 +412,8 @@ __global__ void __launch_bounds__(kTcThreads, kBufs == 1 ? 2 : 1)
               if (col < N) {
                 const float val = rescale(static_cast<int>(v[j]), s_a, sw[j]);
                 orow[col] = rrow ? __fadd_rn(ld_act(rrow + col), val) : val;
+                for (int p = 0; p < go.ranks; ++p)
+                  if (p != go.rank) go.stage[p][ghalf + go.col0 + static_cast<size_t>(row) * ldo + col] = val;
                 if (arow) arow[col] = static_cast<int>(v[j]);
               }
             }
@@ -403,6 +423,24 @@ __global__ void __launch_bounds__(kTcThreads, kBufs == 1 ? 2 : 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[b]);
+    }
+    if (go.ranks > 1) {
+      // Gathered product: the CTA's tiles are on every rank; count the CTA in
+      // on every rank's arrival counter.  Call state (go.seq, local): [0]
+      // arrivals expected after the last call, [1] CTA ticket, [2] calls
+      // issued (its parity picks the staging half).
+      __threadfence_system();
+      named_bar_sync(1, 32 * kEpiWarps);
+      if (et == 0) {
+        for (int p = 0; p < go.ranks; ++p) atomicAdd_system(go.ctr[p], 1ull);
+        __threadfence();
+        if (atomicAdd(go.seq + 1, 1ull) == gridDim.x - 1) {
+          go.seq[1] = 0;
+          go.seq[0] += static_cast<unsigned long long>(go.ranks) * gridDim.x;
+          go.seq[2] = gseq + 1;
+          __threadfence();
+        }
+      }
     }
   }
   tc_fence_before();
@@ -480,7 +518,7 @@ int pick_bn(const DeviceInfo& dev, size_t M, size_t N) {
 template <int BN, int kStages, int kBufs = 2>
 cudaError_t launch_bn(const DeviceInfo& dev, cudaStream_t st, const CUtensorMap& ta,
                       const CUtensorMap& tb, const float* act_scale, int per_row,
-                      const float* w_scales, size_t M, size_t N, size_t K, float* out,
+                      const float* w_scales, size_t M, size_t N, size_t K, const GemmOut& out,
                       int32_t* acc_out, int* status, const float* residual, int grid) {
   static_assert(TcLayout<BN, kStages, kBufs>::total <= 232448,
                 "stage ring exceeds the per-CTA shared memory");
@@ -559,11 +597,20 @@ cudaError_t gemm_i8_tc_plan(const DeviceInfo& dev, size_t M, size_t N, size_t K,
 
 cudaError_t launch_gemm_i8_tc(const DeviceInfo& dev, cudaStream_t st, const int8_t* xq,
                               const float* act_scale_dev, int scale_per_row, const int8_t* W,
-                              const float* w_scales, size_t M, size_t N, size_t K, float* out,
+                              const float* w_scales, size_t M, size_t N, size_t K, float* out_ptr,
                               int32_t* acc_out, int* status, LaunchStats* ls,
-                              const float* residual) {
+                              const float* residual, const GemmOut* gather) {
   if ((reinterpret_cast<uintptr_t>(xq) & 15) || (reinterpret_cast<uintptr_t>(W) & 15))
     return cudaErrorMisalignedAddress;
+  GemmOut out;
+  if (gather) {
+    if (gather->ranks < 2 || gather->ranks > EpiArgs::kMaxRanks || residual || acc_out || !gather->seq)
+      return cudaErrorInvalidValue;
+    out = *gather;
+  } else {
+    out.out = out_ptr;
+    out.ldo = N;
+  }
   GemmPlan p;
   if (cudaError_t e = gemm_i8_tc_plan(dev, M, N, K, &p)) return e;
   CUtensorMap ta, tb;

@@ -96,7 +96,7 @@ struct Options {
   int q4_mma = 1;      // MRI_OPT_Q4_MMA: Q4_0 at m = 2..8 on the bf16 warp MMA
   int tc_attn = 1;     // MRI_OPT_TC_ATTN: tensor-core prefill attention (head dim 64 / 128)
   int fa_split = 3;    // MRI_OPT_FA_SPLIT: key tiles from which a prefill key walk is split (0 = never)
-  int shard_peer = 0;  // MRI_OPT_SHARD_PEER: sharded m <= 8 gathered over peer memory instead of NCCL
+  int shard_peer = 2;  // MRI_OPT_SHARD_PEER: 0 NCCL, 1 peer memory, 2 peer memory for m > 8 only
   // Internal (not an ABI option): SMs the tensor-core GEMM leaves free for
   // other work running beside it.
   int sm_reserve = 0;
@@ -235,6 +235,23 @@ int ctx_reserve_scratch(struct ::mri_ctx* ctx, size_t bytes);
 size_t int8_scratch_bytes(size_t m, size_t k);
 
 // ── tensor-core INT8 GEMM (gemm_tc.cu) ──────────────────────────────────────
+// Output of one GEMM call.  Plain: out [M][ldo] (ldo = N).  Gathered over
+// peer memory (ranks > 1, an N-sharded product): the tile is written to `out`
+// (this rank's columns of the full [M][n_total] output, i.e. out_full +
+// rank * N, row stride ldo = n_total) and to every other rank's staging half
+// (stage[p] + (seq & 1) * half + rank * N, same layout; seq = calls issued, in
+// *g_seq (EpiArgs convention)); each CTA then counts itself in on every
+// rank's arrival counter, and launch_gather_collect_cols copies the other
+// ranks' columns out of this rank's staging.
+struct GemmOut {
+  float* out = nullptr;
+  size_t ldo = 0;
+  int ranks = 0, rank = 0;
+  size_t half = 0, col0 = 0;
+  float* stage[EpiArgs::kMaxRanks] = {};
+  unsigned long long* ctr[EpiArgs::kMaxRanks] = {};
+  unsigned long long* seq = nullptr;
+};
 bool gemm_i8_tc_supported(const DeviceInfo& dev, size_t M, size_t N, size_t K);
 // Launch shape of the tensor-core GEMM for (M, N, K): tile width, ring
 // stages, TMEM accumulator buffers per CTA (2: persistent grid, a CTA walks
@@ -249,7 +266,13 @@ cudaError_t launch_gemm_i8_tc(const DeviceInfo& dev, cudaStream_t st, const int8
                               const float* act_scale_dev, int scale_per_row, const int8_t* W,
                               const float* w_scales, size_t M, size_t N, size_t K, float* out,
                               int32_t* acc_out, int* status, LaunchStats* ls,
-                              const float* residual = nullptr);
+                              const float* residual = nullptr, const GemmOut* gather = nullptr);
+// After a gathered GEMM: waits (bounded) for every rank's arrivals and copies
+// the columns of the other ranks from this rank's staging into out_full
+// [M][n_total] (this rank's own columns [rank * ns, (rank + 1) * ns) are
+// already there).
+cudaError_t launch_gather_collect_cols(const DeviceInfo& dev, cudaStream_t st, const GemmOut& g, size_t M,
+                                       size_t ns, float* out_full, int* status, LaunchStats* ls);
 
 // ── GGUF tensor data to device weights (load.cu) ────────────────────────────
 // Destination of one converted tensor: either per-channel INT8 rows (row r ->

@@ -124,15 +124,17 @@ def _run_two(target, args):
     return got
 
 
-@pytest.mark.parametrize("path", ["peer", "nccl"])
+@pytest.mark.parametrize("path", ["peer", "nccl", "default"])
 def test_two_ranks_match_unsharded(mri, gpu_ctx, oracle, path):
-    """Two GPUs: m = 1 and 4 through the peer-memory gather
-    (OPT_SHARD_PEER = 1) or NCCL, m = 300 through the chunked NCCL all-gather;
+    """Two GPUs, OPT_SHARD_PEER = 1 ("peer": m = 1 and 4 gathered by the
+    streaming GEMV's epilogue, m = 300 by the tensor-core GEMM's epilogue
+    over peer memory), 0 ("nccl": the NCCL all-gather, chunked for m = 300)
+    or 2 ("default": NCCL for m <= 8, the GEMM's peer gather for m = 300);
     every rank's result equals the oracle's unsharded product bit for bit."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
-    n, k, seed, ms = 4096, 2048, 3, (1, 4, 300, 1)
-    peer = 0 if path == "nccl" else 1
+    n, k, seed, ms = 4096, 2048, 3, (1, 4, 300, 1, 300)
+    peer = {"peer": 1, "nccl": 0, "default": 2}[path]
     got = _run_two(shard_workers.nccl_shard_worker, (mri.Communicator.unique_id(), ms, n, k, seed, peer))
     for r in range(2):
         assert not isinstance(got[r], str), got[r]

@@ -104,7 +104,11 @@ enum mri_option {
                              split over two blocks; 0: never */
   MRI_OPT_SHARD_PEER = 7  /* sharded products: 2 (default) gathered over peer memory for m > 8 (the
                              GEMM epilogue writes each tile to every rank) and by NCCL for m <= 8;
-                             1: over peer memory for every m; 0: NCCL for every m */
+                             1: over peer memory for every m; 0: NCCL for every m */,
+  MRI_OPT_GEMM_PAIR = 8   /* 1 (default): tensor-core GEMMs with a plain output (no residual, no
+                             INT32 copy) run on CTA pairs (tcgen05.mma.cta_group::2, 256-row tiles)
+                             from four rounds of pair tiles on; 2: pairs for any plain output of
+                             more than 128 rows; 0: one CTA per tile */
 };
 MRI_API int mri_ctx_set_option(mri_ctx* ctx, int option, int value);
 MRI_API int mri_ctx_get_option(mri_ctx* ctx, int option, int* value);
@@ -395,12 +399,14 @@ MRI_API int mri_int8_path(mri_ctx* ctx, size_t m, size_t n, size_t k);
  * consumer thread, 0 = none), and 1 when such an input is quantized by the
  * quantizer kernels first (then the GEMV streams int8 activations). */
 MRI_API int mri_int8_gemv_plan(mri_ctx* ctx, size_t m, size_t n, size_t k, int* plan /* [8] */);
-/* Launch shape of the tensor-core INT8 GEMM for (m, n, k): plan[0..5] = tile
- * width BN, ring stages, TMEM accumulator buffers per CTA (2: persistent
- * grid, each CTA walks tiles t, t + grid, ...; 1: one tile per CTA, two CTAs
- * per SM), grid, tiles, and the most tiles one CTA takes.  Follows the
- * context's options.  No tensor-core GEMM for the shape -> MRI_ERR_INVALID_SHAPE. */
-MRI_API int mri_int8_gemm_plan(mri_ctx* ctx, size_t m, size_t n, size_t k, int* plan /* [6] */);
+/* Launch shape of the tensor-core INT8 GEMM for (m, n, k) with a plain
+ * output (no residual, no INT32 copy): plan[0..6] = tile width BN, ring
+ * stages, TMEM accumulator buffers per CTA (2: persistent grid, each CTA (or
+ * CTA pair) walks tiles t, t + grid, ...; 1: one tile per CTA, two CTAs per
+ * SM), grid (CTAs), tiles, the most tiles one CTA (pair) takes, and 2 when
+ * CTA pairs run 256-row tiles on tcgen05.mma.cta_group::2 (else 1).  Follows
+ * the context's options.  No tensor-core GEMM -> MRI_ERR_INVALID_SHAPE. */
+MRI_API int mri_int8_gemm_plan(mri_ctx* ctx, size_t m, size_t n, size_t k, int* plan /* [7] */);
 
 #ifdef __cplusplus
 }

@@ -47,7 +47,8 @@ __all__ = [
 PER_TENSOR, PER_ROW = _lib.PER_TENSOR, _lib.PER_ROW
 
 # Kernel-variant options of a Context (mri_option in include/mri_gpu.h).
-OPT_PDL, OPT_GEMM_BN, OPT_GEMM_2CTA, OPT_Q8_MMA, OPT_Q4_MMA, OPT_TC_ATTN, OPT_FA_SPLIT, OPT_SHARD_PEER = range(8)
+(OPT_PDL, OPT_GEMM_BN, OPT_GEMM_2CTA, OPT_Q8_MMA, OPT_Q4_MMA, OPT_TC_ATTN, OPT_FA_SPLIT, OPT_SHARD_PEER,
+ OPT_GEMM_PAIR) = range(9)
 
 
 class TensorError(Exception):
@@ -182,9 +183,9 @@ class Context:
 
     def int8_gemm_plan(self, m, n, k):
         """Launch shape of the tensor-core INT8 GEMM (diagnostics)."""
-        p = (ctypes.c_int * 6)()
+        p = (ctypes.c_int * 7)()
         _check(self._lib.mri_int8_gemm_plan(self.handle, m, n, k, p))
-        keys = ("bn", "stages", "acc_buffers", "grid", "tiles", "tiles_per_cta")
+        keys = ("bn", "stages", "acc_buffers", "grid", "tiles", "tiles_per_cta", "cta_pair")
         return dict(zip(keys, list(p)))
 
     def set_option(self, option, value):

@@ -504,6 +504,7 @@ int* option_slot(mri_ctx* ctx, int option) {
     case MRI_OPT_TC_ATTN: return &o.tc_attn;
     case MRI_OPT_FA_SPLIT: return &o.fa_split;
     case MRI_OPT_SHARD_PEER: return &o.shard_peer;
+    case MRI_OPT_GEMM_PAIR: return &o.gemm_pair;
     default: return nullptr;
   }
 }
@@ -518,6 +519,7 @@ int mri_ctx_set_option(mri_ctx* ctx, int option, int value) {
     case MRI_OPT_GEMM_BN: ok = value == 0 || (value >= 128 && value <= 256 && value % 32 == 0); break;
     case MRI_OPT_FA_SPLIT: ok = value >= 0; break;
     case MRI_OPT_SHARD_PEER: ok = value >= 0 && value <= 2; break;
+    case MRI_OPT_GEMM_PAIR: ok = value >= 0 && value <= 2; break;
     default: ok = value == 0 || value == 1;
   }
   if (!ok) return fail(MRI_ERR_INVALID_ARGUMENT, "value %d out of range for option %d", value, option);
@@ -920,6 +922,7 @@ int mri_int8_gemm_plan(mri_ctx* ctx, size_t m, size_t n, size_t k, int* plan) {
   plan[3] = p.grid;
   plan[4] = p.tiles;
   plan[5] = p.tiles_per_cta;
+  plan[6] = p.pair;
   return MRI_OK;
 }
 

@@ -97,6 +97,7 @@ struct Options {
   int tc_attn = 1;     // MRI_OPT_TC_ATTN: tensor-core prefill attention (head dim 64 / 128)
   int fa_split = 3;    // MRI_OPT_FA_SPLIT: key tiles from which a prefill key walk is split (0 = never)
   int shard_peer = 2;  // MRI_OPT_SHARD_PEER: 0 NCCL, 1 peer memory, 2 peer memory for m > 8 only
+  int gemm_pair = 1;   // MRI_OPT_GEMM_PAIR: 1 CTA pairs from 4 rounds of pair tiles, 2 always, 0 never
   // Internal (not an ABI option): SMs the tensor-core GEMM leaves free for
   // other work running beside it.
   int sm_reserve = 0;
@@ -257,10 +258,13 @@ bool gemm_i8_tc_supported(const DeviceInfo& dev, size_t M, size_t N, size_t K);
 // stages, TMEM accumulator buffers per CTA (2: persistent grid, a CTA walks
 // tiles t, t + grid, ...; 1: one tile per CTA, two CTAs per SM), grid,
 // tiles, and the most tiles one CTA takes.
+// pair = 2: two-CTA clusters issuing M = 256 MMAs (cta_group::2), tiles of
+// 256 x bn (taken only for a plain output: no residual, no INT32 copy).
 struct GemmPlan {
-  int bn = 0, stages = 0, bufs = 0, grid = 0, tiles = 0, tiles_per_cta = 0;
+  int bn = 0, stages = 0, bufs = 0, grid = 0, tiles = 0, tiles_per_cta = 0, pair = 1;
 };
-cudaError_t gemm_i8_tc_plan(const DeviceInfo& dev, size_t M, size_t N, size_t K, GemmPlan* plan);
+cudaError_t gemm_i8_tc_plan(const DeviceInfo& dev, size_t M, size_t N, size_t K, GemmPlan* plan,
+                            bool plain = true);
 // xq [M,K] i8, W [N,K] i8 (both K-major), scale(s) in device memory.
 cudaError_t launch_gemm_i8_tc(const DeviceInfo& dev, cudaStream_t st, const int8_t* xq,
                               const float* act_scale_dev, int scale_per_row, const int8_t* W,

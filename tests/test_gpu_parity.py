@@ -366,9 +366,14 @@ def test_gemm_two_ctas_per_sm_exact(mri, oracle, ctx_option, bn):
 # block lies inside M and N and no INT32 copy is requested (acc_out selects the
 # direct per-row stores); the cases below leave acc_out out so that the staged
 # stores are the ones checked, on full and ragged blocks.
+@pytest.mark.parametrize("pair", [0, 2], ids=["one_cta", "cta_pair"])
 @pytest.mark.parametrize("bn", [128, 160, 192, 224, 256])
-def test_gemm_staged_epilogue_exact(mri, oracle, ctx_option, bn):
+def test_gemm_staged_epilogue_exact(mri, oracle, ctx_option, bn, pair):
+    """Plain outputs (no INT32 copy): the staged stores of the one-CTA kernel
+    (OPT_GEMM_PAIR = 0) and of the CTA-pair kernel (256-row tiles on
+    tcgen05.mma.cta_group::2), every tile width."""
     ctx_option(mri.OPT_GEMM_BN, bn)
+    ctx_option(mri.OPT_GEMM_PAIR, pair)
     rng = np.random.default_rng(300 + bn)
     m, n, k = 333, 1000, 4096 + 256
     aq = rng.integers(-127, 128, size=m * k, dtype=np.int8)
@@ -385,6 +390,7 @@ def test_gemm_two_ctas_per_sm_staged_exact(mri, oracle, ctx_option, bn):
     """One tile per CTA, two CTAs per SM: the output block is staged in the
     (then idle) stage ring."""
     ctx_option(mri.OPT_GEMM_BN, bn)
+    ctx_option(mri.OPT_GEMM_PAIR, 0)
     rng = np.random.default_rng(400 + bn)
     m, n, k = 500, 7717, 1024 + 256
     aq = rng.integers(-127, 128, size=m * k, dtype=np.int8)

@@ -58,14 +58,16 @@ PERSISTENT_SHAPES = [(1024, 11008, 4096, 3), (2048, 3584, 8192, 2)]
 
 
 @pytest.mark.parametrize("m,n,k,min_tiles", PERSISTENT_SHAPES)
-def test_gemm_persistent_multi_tile_exact(mri, oracle, gpu_ctx, m, n, k, min_tiles):
-    """The persistent grid with two TMEM accumulator buffers and several
-    tiles per CTA (tile t + 1's MMAs run while tile t drains; from the third
-    tile on a buffer waits for the epilogue's release).  Every row, both
-    epilogues: the staged f32 stores (no INT32 copy) through
-    matmul_int8_from_f32, and the direct stores with INT32 sums."""
+def test_gemm_persistent_multi_tile_exact(mri, oracle, gpu_ctx, ctx_option, m, n, k, min_tiles):
+    """The one-CTA persistent grid (OPT_GEMM_PAIR = 0) with two TMEM
+    accumulator buffers and several tiles per CTA (tile t + 1's MMAs run while
+    tile t drains; from the third tile on a buffer waits for the epilogue's
+    release).  Every row, both epilogues: the staged f32 stores (no INT32
+    copy) through matmul_int8_from_f32, and the direct stores with INT32
+    sums."""
+    ctx_option(mri.OPT_GEMM_PAIR, 0)
     plan = gpu_ctx.int8_gemm_plan(m, n, k)
-    assert plan["acc_buffers"] == 2 and plan["tiles_per_cta"] >= min_tiles, plan
+    assert plan["cta_pair"] == 1 and plan["acc_buffers"] == 2 and plan["tiles_per_cta"] >= min_tiles, plan
     assert plan["grid"] <= 148, plan
     rng = np.random.default_rng(m + n)
     x = rng.normal(0, 1, size=(m, k)).astype(np.float32)
@@ -85,6 +87,7 @@ def test_gemm_persistent_grid_when_two_cta_off(mri, oracle, gpu_ctx, ctx_option)
     shape, 276 tiles): the persistent grid, two tiles on most CTAs, every
     row against the oracle."""
     m, n, k = 512, 11008, 4096
+    ctx_option(mri.OPT_GEMM_PAIR, 0)
     assert gpu_ctx.int8_gemm_plan(m, n, k)["acc_buffers"] == 1
     ctx_option(mri.OPT_GEMM_2CTA, 0)
     plan = gpu_ctx.int8_gemm_plan(m, n, k)
@@ -101,6 +104,35 @@ def test_gemm_persistent_grid_when_two_cta_off(mri, oracle, gpu_ctx, ctx_option)
     assert np.array_equal(bits(got), bits(want))
 
 
+# (m, n, k): ragged rows and columns, one pair tile, several tiles per pair
+# (a 70B gate/up shard of an 8-GPU node at 2048 rows), the 7B gate/up at 1024
+# rows, and the full 70B gate/up at 2048 rows (19.5 rounds of pair tiles: the
+# default takes pairs there).
+PAIR_SHAPES = [(129, 1000, 256), (300, 520, 4352), (256, 160, 128), (2048, 3584, 8192), (1024, 11008, 4096),
+               (2048, 28672, 8192)]
+
+
+@pytest.mark.parametrize("m,n,k", PAIR_SHAPES)
+def test_gemm_cta_pair_exact(mri, oracle, gpu_ctx, ctx_option, m, n, k):
+    """The CTA-pair kernel: each CTA of a two-CTA cluster loads its 128 rows
+    of activations and half of the weight tile, the even CTA issues M = 256
+    MMAs over both, each CTA drains its TMEM rows.  Every output against the
+    oracle, on two calls in a row (barrier phases and TMEM buffers reused).
+    OPT_GEMM_PAIR = 2 takes pairs at every size (by default they run from
+    four rounds of pair tiles on)."""
+    ctx_option(mri.OPT_GEMM_PAIR, 2)
+    plan = gpu_ctx.int8_gemm_plan(m, n, k)
+    assert plan["cta_pair"] == 2, plan
+    rng = np.random.default_rng(m * 3 + n)
+    wq, ws = weights(rng, n, k)
+    qm = mri.QuantizedMatrix(wq, ws, n, k)
+    for rep in range(2):
+        x = rng.normal(0, 1 + rep, size=(m, k)).astype(np.float32)
+        want, _, _, _ = oracle_from_f32(oracle, x, wq, ws, n, k)
+        got = mri.matmul_int8_from_f32(x, qm)
+        assert np.array_equal(bits(got), bits(want)), (rep, int(np.count_nonzero(bits(got) != bits(want))))
+
+
 @pytest.fixture(scope="module")
 def prefill_case(mri, oracle):
     """BASELINE prefill config: A from N(0,1) activations [512, 4096], B the
@@ -113,13 +145,20 @@ def prefill_case(mri, oracle):
     return x, wq, ws, m, n, k
 
 
-def test_prefill_all_rows_per_tensor(mri, oracle, gpu_ctx, prefill_case):
-    """matmul_int8_from_f32 at the prefill config (two CTAs per SM, one tile
-    each, staged epilogue): all 512 x 11008 outputs bit-equal to the oracle,
-    and all INT32 sums through matmul_int8."""
+@pytest.mark.parametrize("pair", [2, 0], ids=["cta_pair", "one_cta"])
+def test_prefill_all_rows_per_tensor(mri, oracle, gpu_ctx, ctx_option, prefill_case, pair):
+    """matmul_int8_from_f32 at the prefill config, on the one-CTA kernel (the
+    default here: two CTAs per SM, one tile each) and on the CTA-pair kernel
+    (OPT_GEMM_PAIR = 2: 256-row tiles, tcgen05.mma.cta_group::2): all 512 x
+    11008 outputs bit-equal to the oracle, and all INT32 sums through
+    matmul_int8."""
     x, wq, ws, m, n, k = prefill_case
+    ctx_option(mri.OPT_GEMM_PAIR, pair)
     plan = gpu_ctx.int8_gemm_plan(m, n, k)
-    assert plan["acc_buffers"] == 1 and plan["grid"] == plan["tiles"], plan
+    if pair:
+        assert plan["cta_pair"] == 2 and plan["grid"] % 2 == 0, plan
+    else:
+        assert plan["cta_pair"] == 1 and plan["acc_buffers"] == 1 and plan["grid"] == plan["tiles"], plan
     qm = mri.QuantizedMatrix(wq, ws, n, k)
     want, want_acc, aq, s = oracle_from_f32(oracle, x, wq, ws, n, k)
     assert np.array_equal(bits(mri.matmul_int8_from_f32(x, qm)), bits(want))

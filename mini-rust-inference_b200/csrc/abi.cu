@@ -260,7 +260,7 @@ bool mri::matmul_int8_epilogue_supported(const ::mri_ctx* ctx, size_t m, const :
 
 int mri::matmul_int8_fused(::mri_ctx* ctx, const float* x, size_t m, size_t k, const float* norm_w,
                            float eps, int swiglu, const ::mri_qmatrix* w, const float* residual,
-                           float* out, const EpiArgs* epi) {
+                           float* out, const EpiArgs* epi, int pre_stages) {
   if (int rc = enter(ctx)) return rc;
   if (!w) return fail(MRI_ERR_INVALID_ARGUMENT, "null weight handle");
   if (int rc = check_k("matmul_int8_fused", m, k, w->k_in)) return rc;
@@ -270,6 +270,7 @@ int mri::matmul_int8_fused(::mri_ctx* ctx, const float* x, size_t m, size_t k, c
   a.norm_w = norm_w;
   a.eps = eps;
   a.swiglu = swiglu;
+  a.pre_stages = pre_stages;
   if (epi && (residual || w->n_out % 2 || m != 1))
     return fail(MRI_ERR_INVALID_ARGUMENT, "pair epilogue needs one row, even N and no residual");
   return run_int8(ctx, a, w, m, out, nullptr, residual, epi);

@@ -1709,7 +1709,7 @@ cudaError_t launch_gemv_i8_tma(const DeviceInfo& dev, cudaStream_t st, int M, co
   if (cudaError_t e = gemv_i8_tma_plan(dev, M, N, K, &p, reg_vec(M, K, &act), kind)) return e;
   // A gather CTA keeps its output rows in a 1024-float shared buffer.
   if (kind == 2 && ((N + p.grid - 1) / p.grid) * M > 1024) return cudaErrorInvalidValue;
-  const int pre = pre_stages(p.stages);
+  const int pre = act.pre_stages >= 0 ? std::min(act.pre_stages, p.stages) : pre_stages(p.stages);
   MRI_DISPATCH_I8_TMA(M, p.vec, p.k_chunks > 1, p.epi, {
     // The gather CTAs wait for one another, so all must be resident at once:
     // the grid never exceeds the CTAs that fit (resident_ctas), and a

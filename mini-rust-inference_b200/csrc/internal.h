@@ -37,6 +37,10 @@ struct ActArgs {
   const float* norm_w = nullptr;
   float eps = 0.0f;
   int swiglu = 0;
+  // Streaming GEMV: weight stages the producer issues before the activation
+  // loads are in flight (-1: one).  A projection that follows a kernel which
+  // leaves HBM mostly idle (decode attention) prefetches its whole ring.
+  int pre_stages = -1;
 };
 
 // Optional epilogues of the streaming INT8 GEMV that combine adjacent output
@@ -207,7 +211,7 @@ cudaError_t launch_gemv_q4_0_generic(const DeviceInfo& dev, cudaStream_t st, int
 int matmul_int8_fused(struct ::mri_ctx* ctx, const float* x, size_t m, size_t k,
                       const float* norm_w, float eps, int swiglu,
                       const struct ::mri_qmatrix* w, const float* residual, float* out,
-                      const EpiArgs* epi = nullptr);
+                      const EpiArgs* epi = nullptr, int pre_stages = -1);
 // Records the calling thread's last error (mri_last_error) and returns code.
 int set_error(int code, const char* fmt, ...);
 // Per-tensor quantization of x [m, k] into the context scratch (quantized

@@ -143,7 +143,7 @@ __global__ void rope_kv_kernel(float* __restrict__ qkv, int ld, int n_heads, int
 // Decode attention on thread-block clusters (attention/cached.rs:141-190
 // with gqa.rs:217-237): the kDecCluster CTAs of one cluster share head h, CTA
 // c taking the keys [c*chunk, (c+1)*chunk) of the pos + 1 cached ones.  Each
-// of its 8 warps scores rounds of 8 keys (warp w: keys base + 64 r + 8 w + i),
+// of its 8 warps scores rounds of 12 keys (warp w: keys base + 96 r + 12 w + i),
 // a lane owning 4 head dimensions, with all of a round's K and V float4 loaded
 // before any is used, and keeps an online softmax (running max, exp-sum,
 // weighted V sum).  The warps' partials are combined in warp order into the
@@ -874,9 +874,9 @@ cudaError_t pdl_launch(const mri_llama* m, void (*k)(KArgs...), dim3 grid, dim3 
 // rows) and the residual add fused behind (out = residual + product).
 int proj(mri_llama* m, const float* x, size_t rows, const mri_qmatrix& w, float* out,
          const float* norm = nullptr, int swiglu = 0, const float* residual = nullptr,
-         const mri::EpiArgs* epi = nullptr) {
+         const mri::EpiArgs* epi = nullptr, int pre_stages = -1) {
   LL_RC(mri::matmul_int8_fused(m->ctx, x, rows, w.k_in, norm, m->cfg.rms_eps, swiglu, &w, residual,
-                               out, epi));
+                               out, epi, pre_stages));
   return MRI_OK;
 }
 
@@ -966,7 +966,10 @@ int run_blocks(mri_llama* m, size_t rows, int pos0, bool decode_dev, uint32_t l_
                                              static_cast<int>(rows), pos0, kc, vc, scale, m->attn,
                                              m->qd);
     }
-    if (int rc = proj(m, m->attn, rows, m->wo[l], m->x, nullptr, 0, m->x)) return rc;
+    // The O projection follows attention, which leaves HBM mostly idle: in
+    // the decode step its producer fills the whole ring while attention runs.
+    if (int rc = proj(m, m->attn, rows, m->wo[l], m->x, nullptr, 0, m->x, nullptr, decode_dev ? 1 << 20 : -1))
+      return rc;
     if (fused) {
       mri::EpiArgs e;
       e.mode = mri::EPI_SWIGLU;

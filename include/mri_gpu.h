@@ -108,7 +108,9 @@ enum mri_option {
   MRI_OPT_GEMM_PAIR = 8   /* 1 (default): tensor-core GEMMs with a plain output (no residual, no
                              INT32 copy) run on CTA pairs (tcgen05.mma.cta_group::2, 256-row tiles)
                              from four rounds of pair tiles on; 2: pairs for any plain output of
-                             more than 128 rows; 0: one CTA per tile */
+                             more than 128 rows; 0: one CTA per tile */,
+  MRI_OPT_Q4_LIMB = 9     /* 1 (default): Q4_0 at m = 1 with K % 1024 == 0 on exact integer block
+                             dots (21-bit activation digits, dp4a); 0: the f32 streaming kernel */
 };
 MRI_API int mri_ctx_set_option(mri_ctx* ctx, int option, int value);
 MRI_API int mri_ctx_get_option(mri_ctx* ctx, int option, int* value);

@@ -48,7 +48,7 @@ PER_TENSOR, PER_ROW = _lib.PER_TENSOR, _lib.PER_ROW
 
 # Kernel-variant options of a Context (mri_option in include/mri_gpu.h).
 (OPT_PDL, OPT_GEMM_BN, OPT_GEMM_2CTA, OPT_Q8_MMA, OPT_Q4_MMA, OPT_TC_ATTN, OPT_FA_SPLIT, OPT_SHARD_PEER,
- OPT_GEMM_PAIR) = range(9)
+ OPT_GEMM_PAIR, OPT_Q4_LIMB) = range(10)
 
 
 class TensorError(Exception):
@@ -124,11 +124,12 @@ class Context:
             self._lib.mri_ctx_destroy(self.handle)
             self.handle = ctypes.c_void_p()
 
-    def __del__(self):
+    def __del__(self, _finalizing=sys.is_finalizing):
         # At interpreter exit objects are finalized in no fixed order (a
         # context's stream may already be gone when a model or matrix that used
         # it is collected), and the process releases device memory anyway.
-        if sys.is_finalizing():
+        # The check is bound at definition: module globals may be cleared by then.
+        if _finalizing():
             return
         try:
             self.close()
@@ -254,11 +255,12 @@ class QuantizedMatrix:
             self.data = data.reshape(n_out, k_in)[begin:end].reshape(-1)
             self.scales = scales[begin:end]
 
-    def __del__(self):
+    def __del__(self, _finalizing=sys.is_finalizing):
         # At interpreter exit objects are finalized in no fixed order (a
         # context's stream may already be gone when a model or matrix that used
         # it is collected), and the process releases device memory anyway.
-        if sys.is_finalizing():
+        # The check is bound at definition: module globals may be cleared by then.
+        if _finalizing():
             return
         try:
             if self.handle:
@@ -333,11 +335,12 @@ class Q8_0WeightMatrix:
     def dequantize_all(self):
         return formats.dequantize_q8_0(self.data)
 
-    def __del__(self):
+    def __del__(self, _finalizing=sys.is_finalizing):
         # At interpreter exit objects are finalized in no fixed order (a
         # context's stream may already be gone when a model or matrix that used
         # it is collected), and the process releases device memory anyway.
-        if sys.is_finalizing():
+        # The check is bound at definition: module globals may be cleared by then.
+        if _finalizing():
             return
         try:
             if self.handle:
@@ -357,11 +360,12 @@ class Q4_0Matrix:
         _check(self.ctx._lib.mri_q4_0_upload(self.ctx.handle, _vp(d), d.size, n_out, k, ctypes.byref(h)))
         self.handle, self.data, self.n_out, self.k = h, d, n_out, k
 
-    def __del__(self):
+    def __del__(self, _finalizing=sys.is_finalizing):
         # At interpreter exit objects are finalized in no fixed order (a
         # context's stream may already be gone when a model or matrix that used
         # it is collected), and the process releases device memory anyway.
-        if sys.is_finalizing():
+        # The check is bound at definition: module globals may be cleared by then.
+        if _finalizing():
             return
         try:
             if self.handle:
@@ -590,11 +594,12 @@ class Communicator:
             self.ctx._lib.mri_comm_destroy(self.handle)
             self.handle = ctypes.c_void_p()
 
-    def __del__(self):
+    def __del__(self, _finalizing=sys.is_finalizing):
         # At interpreter exit objects are finalized in no fixed order (a
         # context's stream may already be gone when a model or matrix that used
         # it is collected), and the process releases device memory anyway.
-        if sys.is_finalizing():
+        # The check is bound at definition: module globals may be cleared by then.
+        if _finalizing():
             return
         try:
             self.close()
@@ -672,11 +677,12 @@ class LlamaModelInt8:
         _check_model(self._lib.mri_llama_create(self.ctx.handle, ctypes.byref(cfg), ctypes.byref(h)), self._lib)
         self.handle = h
 
-    def __del__(self):
+    def __del__(self, _finalizing=sys.is_finalizing):
         # At interpreter exit objects are finalized in no fixed order (a
         # context's stream may already be gone when a model or matrix that used
         # it is collected), and the process releases device memory anyway.
-        if sys.is_finalizing():
+        # The check is bound at definition: module globals may be cleared by then.
+        if _finalizing():
             return
         try:
             if self.handle:

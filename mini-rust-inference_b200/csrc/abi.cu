@@ -324,7 +324,10 @@ int run_q4_0(mri_ctx* ctx, const float* x, size_t m, const mri_q4_0_matrix* w, f
   uint32_t* xs = nullptr;  // split activations of all m rows, made on first use
   for (size_t m0 = 0; m0 < m; m0 += 8) {
     const int mc = static_cast<int>(std::min<size_t>(8, m - m0));
-    if (x_vec && mri::q4_0_mma_supported(ctx->dev, mc, K)) {
+    if (mc == 1 && mri::gemv_q4_0_limb_supported(ctx->dev, K, x + m0 * K)) {
+      MRI_CUDA_TRY(mri::launch_gemv_q4_0_limb(ctx->dev, st, w->data, N, K, x + m0 * K, out + m0 * N,
+                                              ctx->d_status, &ctx->ls));
+    } else if (x_vec && mri::q4_0_mma_supported(ctx->dev, mc, K)) {
       if (xs == nullptr) {
         if (int rc = ensure_scratch(ctx, al(mri::q4_0_split_bytes(m, K)))) return rc;
         xs = reinterpret_cast<uint32_t*>(ctx->scratch);
@@ -506,6 +509,7 @@ int* option_slot(mri_ctx* ctx, int option) {
     case MRI_OPT_FA_SPLIT: return &o.fa_split;
     case MRI_OPT_SHARD_PEER: return &o.shard_peer;
     case MRI_OPT_GEMM_PAIR: return &o.gemm_pair;
+    case MRI_OPT_Q4_LIMB: return &o.q4_limb;
     default: return nullptr;
   }
 }

@@ -642,50 +642,69 @@ __global__ void __launch_bounds__(256) gemv_i8_generic_kernel(const int8_t* __re
   }
 }
 
-// ── Q8_0 helpers ─────────────────────────────────────────────────────────────
-
-// Loads block `blk` (34 bytes at an even address) from any address space:
-// d (f16 bits) and the 32 quants as 8 little-endian words.  The aligned-down
-// word pointer is formed by pointer arithmetic on `blk` (no integer round
-// trip), so the compiler still sees a shared-memory pointer and issues
-// shared loads rather than generic ones.
-__device__ __forceinline__ void load_q8_block(const uint8_t* blk, uint32_t& dbits, uint32_t q[8]) {
-  const uint32_t a = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(blk)) & 3u;
-  const uint32_t* w = reinterpret_cast<const uint32_t*>(blk - a);
-  const bool odd = (a & 2) != 0;  // block starts 2 bytes into a word
-  uint32_t r[9];  // 36 bytes from the aligned-down start cover the block
-#pragma unroll
-  for (int i = 0; i < 9; ++i) r[i] = w[i];
-  dbits = odd ? (r[0] >> 16) : (r[0] & 0xFFFFu);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) q[i] = odd ? r[i + 1] : __funnelshift_r(r[i], r[i + 1], 16);
-}
-
 // ── K4: Q8_0 streaming GEMV, bit-exact ───────────────────────────────────────
 // Activations are quantized per row into shared memory (row-major int8, so
-// block b of row m is the 32 bytes at m*K + 32*b).  Each consumer warp keeps
-// a term buffer T[m][ts]: lanes write the terms of their blocks, then lane m
-// adds row m's terms in block order (vectorised loads, a plain FADD chain).
+// block b of row m is the 32 bytes at m*K + 32*b).  The 256 consumer threads
+// split a stage's (row, block) pairs; a thread keeps the activation bytes of
+// its current block in registers (with K = 4096 it never changes block), so
+// shared-memory reads are the weight bytes alone.  The block terms
+// (f32)dot * s_a * d are computed into registers and the weight stage is
+// released at once; the terms then go to a term buffer T[row][m][block], and
+// a sum warp adds each (row, m) chain in block order from 0.0, one chain per
+// lane (q8_direct.rs:266-285), while the consumers move on to the next stage.
+// When a stage has more terms than the consumers' registers hold, they are
+// written straight into T after the sum warp has emptied it.
 
 __host__ __device__ constexpr size_t q8_term_stride(size_t nb) { return align_up(nb, 4) + 4; }
+constexpr int kQ8Threads = kThreads + 32;  // producer, 8 consumer warps, sum warp
+// Terms a consumer thread keeps in registers per activation row (the four of
+// K = 4096 at M = 1; a longer unrolled loop costs more than it saves).
+__host__ __device__ constexpr int q8_term_regs(int M) { return M >= 4 ? 1 : 4 / M; }
+// Shared bytes of the term buffer plus its two mbarriers.
+__host__ __device__ constexpr size_t q8_term_bytes(int M, size_t nb) {
+  return kConsumerWarps * static_cast<size_t>(M) * q8_term_stride(nb) * sizeof(float) + 16;
+}
+
+// Writes the terms tr[i] of units u0 + 256 i (u = row * nb + block) into the
+// term buffer T[row][m][block] (row stride M * ts floats).
+template <int M, int TR>
+__device__ __forceinline__ void q8_store_terms(float* T, uint32_t ts, uint32_t nb, uint32_t u0,
+                                               uint32_t rows_here, const float (&tr)[TR][M]) {
+  uint32_t r = u0 / nb, b = u0 - r * nb;
+  const uint32_t q_step = kConsumerThreads / nb, r_step = kConsumerThreads % nb;
+#pragma unroll
+  for (int i = 0; i < TR; ++i) {
+    if (r >= rows_here) break;  // r never decreases
+#pragma unroll
+    for (int m = 0; m < M; ++m) T[(r * M + m) * ts + b] = tr[i][m];
+    b += r_step;
+    r += q_step;
+    if (b >= nb) {
+      b -= nb;
+      ++r;
+    }
+  }
+}
 
 template <int M, int VEC>
-__global__ void __launch_bounds__(kThreads, M <= 2 ? 2 : 1)
+__global__ void __launch_bounds__(kQ8Threads, M <= 2 ? 2 : 1)
     gemv_q8_0_tma_kernel(const uint8_t* __restrict__ W, size_t N, size_t K,
                          const float* __restrict__ x, float* __restrict__ out, int n_stages,
                          int pre, int* status) {
   extern __shared__ __align__(128) uint8_t smem[];
+  constexpr int kTR = q8_term_regs(M);
   const size_t nb = K / 32;
   const size_t row_bytes = nb * 34;
   const size_t ts = q8_term_stride(nb);
-  const StreamLayout L = make_layout(M * K, kConsumerWarps * M * ts * sizeof(float),
-                                     kRowsPerStage * row_bytes, n_stages);
+  const StreamLayout L = make_layout(M * K, q8_term_bytes(M, nb), kRowsPerStage * row_bytes, n_stages);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
   uint64_t* empty = full + n_stages;
   float* s_scale = reinterpret_cast<float*>(smem + L.scales);
   float* red = s_scale + 8;
   int8_t* s_act = reinterpret_cast<int8_t*>(smem + L.act);
-  float* s_terms = reinterpret_cast<float*>(smem + L.extra);
+  float* T = reinterpret_cast<float*>(smem + L.extra);  // [8 rows][M][ts]
+  uint64_t* tfull = reinterpret_cast<uint64_t*>(smem + L.extra + q8_term_bytes(M, nb) - 16);
+  uint64_t* tempty = tfull + 1;
   uint8_t* stage0 = smem + L.stage;
 
   // Row ranges must start 16-byte aligned: begin * 34 * nb % 16 == 0.
@@ -693,10 +712,16 @@ __global__ void __launch_bounds__(kThreads, M <= 2 ? 2 : 1)
   size_t begin, end;
   cta_rows(N, g, begin, end);
   uint64_t* act_issued = empty + n_stages;
+  if (threadIdx.x == 0) {
+    mbar_init(tfull, kConsumerWarps);  // consumers wrote a stage's terms
+    mbar_init(tempty, 1);              // the sum warp has added them
+  }
   init_barriers(full, empty, n_stages, act_issued);
   if (begin >= end) return;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int iters = static_cast<int>((end - begin + kRowsPerStage - 1) / kRowsPerStage);
+  const uint32_t nb32 = static_cast<uint32_t>(nb), ts32 = static_cast<uint32_t>(ts);
   if (warp == 0) {
     if (lane == 0)
       stream_producer(W, row_bytes, begin, end, full, empty, stage0, L.stage_bytes, n_stages,
@@ -704,6 +729,34 @@ __global__ void __launch_bounds__(kThreads, M <= 2 ? 2 : 1)
     return;
   }
   pdl_wait();
+  if (warp == kConsumerWarps + 1) {
+    // Sum warp: chain c = (stage row c / M, activation row c % M).
+    for (int it = 0; it < iters; ++it) {
+      if (!mbar_wait(tfull, it & 1, status)) return;
+      for (int c = lane; c < kRowsPerStage * M; c += 32) {
+        const size_t row = begin + static_cast<size_t>(it) * kRowsPerStage + c / M;
+        if (row >= end) continue;
+        // acc += term in block order (q8_direct.rs:281), starting from 0.0.
+        const float* t = T + static_cast<size_t>(c) * ts;
+        const float4* t4 = reinterpret_cast<const float4*>(t);
+        float acc = 0.0f;
+        const uint32_t nb4 = nb32 / 4;
+#pragma unroll 8
+        for (uint32_t j = 0; j < nb4; ++j) {
+          const float4 v = t4[j];
+          acc = __fadd_rn(acc, v.x);
+          acc = __fadd_rn(acc, v.y);
+          acc = __fadd_rn(acc, v.z);
+          acc = __fadd_rn(acc, v.w);
+        }
+        for (uint32_t b = nb4 * 4; b < nb32; ++b) acc = __fadd_rn(acc, t[b]);
+        out[static_cast<size_t>(c % M) * N + row] = acc;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty);
+    }
+    return;
+  }
   // Prologue: per-row quantization (q8_direct.rs:264); one row is one tensor.
   ActArgs act;
   act.x = x;
@@ -713,57 +766,80 @@ __global__ void __launch_bounds__(kThreads, M <= 2 ? 2 : 1)
 #pragma unroll
   for (int m = 0; m < M; ++m) s_a[m] = s_scale[m];
 
-  const int cw = warp - 1;
-  float* T = s_terms + static_cast<size_t>(cw) * M * ts;
-  const int iters = static_cast<int>((end - begin + kRowsPerStage - 1) / kRowsPerStage);
+  // Consumer thread ct takes units u = ct, ct + 256, ... of the stage's
+  // (row, block) pairs, u = row * nb + block: for nb = 128 every thread
+  // keeps one block (its activation bytes stay in registers) and walks four
+  // of the eight rows.
+  const uint32_t ct = threadIdx.x - 32;
+  const uint32_t kCT = kConsumerThreads;
+  const bool buffered = kRowsPerStage * nb32 <= kCT * kTR;
+  const uint32_t q_step = kCT / nb32, r_step = kCT % nb32;
+  uint32_t xa[M][8];
+  uint32_t cur_b = 0xFFFFFFFFu;
+  float tr[kTR][M];
   for (int it = 0; it < iters; ++it) {
     const int s = it % n_stages;
     if (!mbar_wait(&full[s], (it / n_stages) & 1, status)) return;
-    const size_t row = begin + static_cast<size_t>(it) * kRowsPerStage + cw;
-    if (row < end) {
-      const uint8_t* rowp = stage0 + s * L.stage_bytes + cw * row_bytes;
-      const uint32_t nb32 = static_cast<uint32_t>(nb), K32 = static_cast<uint32_t>(K);
-      const uint32_t ts32 = static_cast<uint32_t>(ts);
-      for (uint32_t b = lane; b < nb32; b += 32) {
-        uint32_t dbits, q[8];
-        load_q8_block(rowp + b * 34u, dbits, q);
-        const float d = f16_bits_to_f32(dbits);
+    if (!buffered && it > 0 && !mbar_wait(tempty, (it - 1) & 1, status)) return;
+    const size_t r0 = begin + static_cast<size_t>(it) * kRowsPerStage;
+    const uint32_t rows_here = static_cast<uint32_t>(std::min<size_t>(kRowsPerStage, end - r0));
+    const uint8_t* st = stage0 + s * L.stage_bytes;
+    for (uint32_t p0 = 0; p0 < kRowsPerStage * nb32; p0 += kCT * kTR) {
+      uint32_t r = (p0 + ct) / nb32, b = (p0 + ct) - r * nb32;
 #pragma unroll
-        for (int m = 0; m < M; ++m) {
-          const uint4* a4 = reinterpret_cast<const uint4*>(s_act + m * K32 + b * 32u);
-          const uint4 a0 = a4[0], a1 = a4[1];
-          int dot = dp4a(q[0], a0.x, 0);
-          dot = dp4a(q[1], a0.y, dot);
-          dot = dp4a(q[2], a0.z, dot);
-          dot = dp4a(q[3], a0.w, dot);
-          dot = dp4a(q[4], a1.x, dot);
-          dot = dp4a(q[5], a1.y, dot);
-          dot = dp4a(q[6], a1.z, dot);
-          dot = dp4a(q[7], a1.w, dot);
-          T[m * ts32 + b] = __fmul_rn(__fmul_rn(small_int_to_float(dot), s_a[m]), d);
+      for (int i = 0; i < kTR; ++i) {
+        if (r >= rows_here) break;  // r never decreases
+        {
+          if (b != cur_b) {
+            cur_b = b;
+#pragma unroll
+            for (int m = 0; m < M; ++m) {
+              const uint4* a4 = reinterpret_cast<const uint4*>(s_act + m * K + b * 32u);
+              const uint4 a0 = a4[0], a1 = a4[1];
+              xa[m][0] = a0.x; xa[m][1] = a0.y; xa[m][2] = a0.z; xa[m][3] = a0.w;
+              xa[m][4] = a1.x; xa[m][5] = a1.y; xa[m][6] = a1.z; xa[m][7] = a1.w;
+            }
+          }
+          // Block b of row r: 34 bytes at an even address; the words covering
+          // it are realigned with one byte permute each.
+          const uint8_t* blk = st + r * row_bytes + b * 34u;
+          const uint32_t a = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(blk)) & 3u;
+          const uint32_t* w = reinterpret_cast<const uint32_t*>(blk - a);
+          const uint32_t sel = 0x5432u + (a >> 1) * 0x2222u;
+          uint32_t wr[9];
+#pragma unroll
+          for (int k = 0; k < 9; ++k) wr[k] = w[k];
+          const float d = f16_bits_to_f32(__byte_perm(wr[0], 0u, 0x4410u + (a >> 1) * 0x22u));
+          uint32_t q[8];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) q[k] = __byte_perm(wr[k], wr[k + 1], sel);
+#pragma unroll
+          for (int m = 0; m < M; ++m) {
+            int dot = 0;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) dot = dp4a(q[k], xa[m][k], dot);
+            tr[i][m] = __fmul_rn(__fmul_rn(small_int_to_float(dot), s_a[m]), d);
+          }
+        }
+        b += r_step;
+        r += q_step;
+        if (b >= nb32) {
+          b -= nb32;
+          ++r;
         }
       }
-      __syncwarp();
-      if (lane < M) {
-        // acc += term in block order (q8_direct.rs:281), starting from 0.0.
-        const float* t = T + lane * ts;
-        const float4* t4 = reinterpret_cast<const float4*>(t);
-        float acc = 0.0f;
-        const size_t nb4 = nb / 4;
-#pragma unroll 8
-        for (size_t j = 0; j < nb4; ++j) {
-          const float4 v = t4[j];
-          acc = __fadd_rn(acc, v.x);
-          acc = __fadd_rn(acc, v.y);
-          acc = __fadd_rn(acc, v.z);
-          acc = __fadd_rn(acc, v.w);
-        }
-        for (size_t b = nb4 * 4; b < nb; ++b) acc = __fadd_rn(acc, t[b]);
-        out[lane * N + row] = acc;
-      }
+      if (!buffered) q8_store_terms<M, kTR>(T, ts32, nb32, p0 + ct, rows_here, tr);
     }
+    // The weights are no longer needed: release the stage before waiting
+    // for the sum warp.
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
+    if (buffered) {
+      if (it > 0 && !mbar_wait(tempty, (it - 1) & 1, status)) return;
+      q8_store_terms<M, kTR>(T, ts32, nb32, ct, rows_here, tr);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(tfull);
   }
 }
 
@@ -1041,7 +1117,9 @@ __global__ void __launch_bounds__(256) gemv_q8_0_generic_kernel(const uint8_t* _
 // ── K5: Q4_0 streaming GEMV (f32 activations) ───────────────────────────────
 // Activations are stored transposed to [m][element 0..31][block] floats.
 
-// Same for an 18-byte Q4_0 block (even address; shared loads, see above).
+// Loads the 18-byte Q4_0 block `blk` (at an even address): d (f16 bits) and
+// the 16 quant bytes as 4 little-endian words.  The aligned-down word pointer
+// is formed by pointer arithmetic on `blk`, so shared loads stay shared.
 __device__ __forceinline__ void load_q4_block(const uint8_t* blk, uint32_t& dbits, uint32_t q[4]) {
   const uint32_t a = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(blk)) & 3u;
   const uint32_t* w = reinterpret_cast<const uint32_t*>(blk - a);
@@ -1061,39 +1139,17 @@ __device__ __forceinline__ float nib_minus8(uint32_t v, uint32_t byte_idx) {
          8388616.0f;
 }
 
+// Activations (M rows of K floats, consumer threads) into shared memory as
+// float4 chunks transposed to [m][chunk 0..7][block], so that lane b reads
+// chunk c of block b conflict-free.  Four independent loads in flight per
+// thread; each consumer warp arrives on act_issued (when given) once its
+// first loads are issued, and the producer holds back later weight stages
+// until then.  Ends with a consumer barrier.
 template <int M>
-__global__ void __launch_bounds__(kThreads, M <= 2 ? 2 : 1)
-    gemv_q4_0_tma_kernel(const uint8_t* __restrict__ W, size_t N, size_t K,
-                         const float* __restrict__ x, float* __restrict__ out, int n_stages,
-                         int pre, int* status) {
-  extern __shared__ __align__(128) uint8_t smem[];
+__device__ void q4_load_act_f32(const float* __restrict__ x, size_t K, float4* s_x4,
+                                uint64_t* act_issued) {
   const size_t nb = K / 32;
-  const size_t row_bytes = nb * 18;
-  const StreamLayout L = make_layout(M * K * sizeof(float), 0, kRowsPerStage * row_bytes, n_stages);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
-  uint64_t* empty = full + n_stages;
-  float4* s_x4 = reinterpret_cast<float4*>(smem + L.act);
-  uint8_t* stage0 = smem + L.stage;
-
-  const size_t g = 8 / (nb % 8 == 0 ? 8 : (nb % 4 == 0 ? 4 : (nb % 2 == 0 ? 2 : 1)));
-  size_t begin, end;
-  cta_rows(N, g, begin, end);
-  uint64_t* act_issued = empty + n_stages;
-  init_barriers(full, empty, n_stages, act_issued);
-  if (begin >= end) return;
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (warp == 0) {
-    if (lane == 0)
-      stream_producer(W, row_bytes, begin, end, full, empty, stage0, L.stage_bytes, n_stages,
-                      status, act_issued, pre);
-    return;
-  }
-  pdl_wait();
-  // Activations as float4 chunks transposed to [m][chunk 0..7][block], so
-  // lane b reads chunk c of block b conflict-free.  Four independent loads in
-  // flight per thread; each consumer warp arrives on act_issued once its
-  // first loads are issued (the producer holds back later weight stages).
+  const int lane = threadIdx.x & 31;
   const int ct = threadIdx.x - 32;
   const int K4 = static_cast<int>(K / 4), n4 = M * K4;
   const bool xvec = (reinterpret_cast<uintptr_t>(x) & 15) == 0;
@@ -1115,7 +1171,7 @@ __global__ void __launch_bounds__(kThreads, M <= 2 ? 2 : 1)
         }
       }
     }
-    if (rd == 0) {
+    if (rd == 0 && act_issued) {
       __syncwarp();
       if (lane == 0) mbar_arrive(act_issued);
     }
@@ -1129,7 +1185,17 @@ __global__ void __launch_bounds__(kThreads, M <= 2 ? 2 : 1)
     }
   }
   named_bar_sync(1, kConsumerThreads);
+}
 
+// The f32 Q4_0 product of rows [begin, end) streamed through the stage ring:
+// consumer warp w takes row w of each stage, its lanes blocks lane, lane + 32,
+// ... (activations from q4_load_act_f32's layout).
+template <int M>
+__device__ void q4_rows_f32(const float4* s_x4, const uint8_t* stage0, size_t stage_bytes,
+                            size_t row_bytes, size_t nb, size_t N, size_t begin, size_t end,
+                            uint64_t* full, uint64_t* empty, int n_stages,
+                            float* __restrict__ out, int* status) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int cw = warp - 1;
   const int iters = static_cast<int>((end - begin + kRowsPerStage - 1) / kRowsPerStage);
   for (int it = 0; it < iters; ++it) {
@@ -1137,7 +1203,7 @@ __global__ void __launch_bounds__(kThreads, M <= 2 ? 2 : 1)
     if (!mbar_wait(&full[s], (it / n_stages) & 1, status)) return;
     const size_t row = begin + static_cast<size_t>(it) * kRowsPerStage + cw;
     if (row < end) {
-      const uint8_t* rowp = stage0 + s * L.stage_bytes + cw * row_bytes;
+      const uint8_t* rowp = stage0 + s * stage_bytes + cw * row_bytes;
       float acc[M];
 #pragma unroll
       for (int m = 0; m < M; ++m) acc[m] = 0.0f;
@@ -1179,6 +1245,319 @@ __global__ void __launch_bounds__(kThreads, M <= 2 ? 2 : 1)
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
+  }
+}
+
+template <int M>
+__global__ void __launch_bounds__(kThreads, M <= 2 ? 2 : 1)
+    gemv_q4_0_tma_kernel(const uint8_t* __restrict__ W, size_t N, size_t K,
+                         const float* __restrict__ x, float* __restrict__ out, int n_stages,
+                         int pre, int* status) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const size_t nb = K / 32;
+  const size_t row_bytes = nb * 18;
+  const StreamLayout L = make_layout(M * K * sizeof(float), 0, kRowsPerStage * row_bytes, n_stages);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
+  uint64_t* empty = full + n_stages;
+  float4* s_x4 = reinterpret_cast<float4*>(smem + L.act);
+  uint8_t* stage0 = smem + L.stage;
+
+  const size_t g = 8 / (nb % 8 == 0 ? 8 : (nb % 4 == 0 ? 4 : (nb % 2 == 0 ? 2 : 1)));
+  size_t begin, end;
+  cta_rows(N, g, begin, end);
+  uint64_t* act_issued = empty + n_stages;
+  init_barriers(full, empty, n_stages, act_issued);
+  if (begin >= end) return;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp == 0) {
+    if (lane == 0)
+      stream_producer(W, row_bytes, begin, end, full, empty, stage0, L.stage_bytes, n_stages,
+                      status, act_issued, pre);
+    return;
+  }
+  pdl_wait();
+  q4_load_act_f32<M>(x, K, s_x4, act_issued);
+  q4_rows_f32<M>(s_x4, stage0, L.stage_bytes, row_bytes, nb, N, begin, end, full, empty, n_stages,
+                 out, status);
+}
+
+// ── K5, M = 1: Q4_0 on exact integer block dots ──────────────────────────────
+// The f32 kernel above spends ~4 instructions per weight (nibble -> float,
+// FMA, activation reads).  Here the activation row is turned, once per CTA,
+// into 21-bit integers per 32-element block: X = rint(x * 2^(19 - e)) with e
+// the exponent of the block's largest |x|, so |x - 2^(e-19) X| <= 2^-20 of the
+// block maximum, and X is split into three balanced base-128 digits (s8
+// planes h, m, l).  A block dot is then exact integer arithmetic: dp4a of the
+// unsigned nibbles q against each plane, combined as (h*128 + m)*128 + l,
+// minus 8 * sum X (the q - 8 of dequant_block_into, q4_0.rs:59-68).  It is
+// scaled by d * 2^(e-19) in f32, and a row's block values are added across
+// lanes and warps in a fixed order: the reference's element-by-element f32
+// sum (q4_0.rs:94-181) reassociated, within the Q4_0 tolerance.  A row with
+// an inf or a NaN takes the f32 kernel's loop instead, so its outputs are
+// non-finite where the reference's are.  Consumer thread ct takes units
+// u = ct, ct + 256, ... (u = row * nb + block); with nb % 32 == 0 the 32
+// lanes of a warp share a row in every unit.  For K = 4096 a thread keeps one
+// block, whose digit planes stay in registers.
+constexpr int kQ4LimbLoads = 4;   // float4 activation loads per thread in flight
+constexpr int kQ4LimbUnroll = 4;  // units per thread in flight (all four of K = 4096)
+
+__host__ __device__ constexpr size_t q4_limb_extra_bytes(size_t K) {
+  // digit planes, per-block scale (f32) and digit sum (s32), row partials [2][8][nb / 32]
+  return 3 * K + 8 * (K / 32) + 2 * kRowsPerStage * (K / 1024) * sizeof(float);
+}
+
+// d = c + sum of (unsigned byte of a) * (signed byte of b).
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+// X (|X| <= 2^20) as balanced base-128 digits, each in [-64, 64]:
+// X = h * 16384 + m * 128 + l.
+__device__ __forceinline__ void digits3(int X, int& h, int& m, int& l) {
+  l = ((X + 64) & 127) - 64;
+  const int x1 = (X - l) >> 7;  // exact: X - l is a multiple of 128
+  m = ((x1 + 64) & 127) - 64;
+  h = (x1 - m) >> 7;
+}
+
+// 2^k for -126 <= k <= 127.
+__device__ __forceinline__ float pow2f(int k) { return __int_as_float((k + 127) << 23); }
+
+// v * 2^k, exact while the products stay normal (|v * 2^k| <= 2^20 here).
+__device__ __forceinline__ float4 scale_pow2(float4 v, int k) {
+  if (k > 127) {
+    v = make_float4(v.x * 0x1p127f, v.y * 0x1p127f, v.z * 0x1p127f, v.w * 0x1p127f);
+    k -= 127;
+  }
+  if (k < -126) {
+    v = make_float4(v.x * 0x1p-126f, v.y * 0x1p-126f, v.z * 0x1p-126f, v.w * 0x1p-126f);
+    k += 126;
+  }
+  const float f = pow2f(k);
+  return make_float4(v.x * f, v.y * f, v.z * f, v.w * f);
+}
+
+__device__ __forceinline__ uint32_t pack_s8x4(int a, int b, int c, int d) {
+  return (static_cast<uint32_t>(a) & 0xFFu) | ((static_cast<uint32_t>(b) & 0xFFu) << 8) |
+         ((static_cast<uint32_t>(c) & 0xFFu) << 16) | (static_cast<uint32_t>(d) << 24);
+}
+
+// Consumer threads: the activation row x[0..K) (16-byte aligned) into the
+// digit planes s_l[3][K bytes], the block scales 2^(e-19) and the block digit
+// sums.  A plane holds each block's 32 digits in nibble order: the 16 even
+// elements, then the 16 odd ones (byte j of a Q4_0 block holds elements 2j
+// and 2j + 1), so nibble word k of a block pairs with plane words k and k + 4.  Float4 chunk i holds elements 4i..4i+3 of block i / 8, so the
+// 8 lanes of a block reduce with three shuffles.  Returns false (after a
+// consumer barrier) when the row holds an inf or a NaN.
+__device__ bool q4_limb_prologue(const float* __restrict__ x, size_t K, uint32_t* s_l, float* s_sb,
+                                 int* s_S, float* red, uint64_t* act_issued) {
+  const int ct = threadIdx.x - 32, lane = threadIdx.x & 31;
+  const int K4 = static_cast<int>(K / 4);
+  float bad = 0.0f;
+  for (int i0 = 0; i0 < K4; i0 += kQ4LimbLoads * kConsumerThreads) {
+    float4 v[kQ4LimbLoads];
+#pragma unroll
+    for (int u = 0; u < kQ4LimbLoads; ++u) {
+      const int i = i0 + u * kConsumerThreads + ct;
+      v[u] = i < K4 ? ld_act(reinterpret_cast<const float4*>(x) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    if (i0 == 0 && act_issued) {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(act_issued);
+    }
+#pragma unroll
+    for (int u = 0; u < kQ4LimbLoads; ++u) {
+      const int i = i0 + u * kConsumerThreads + ct;
+      const float4 t = v[u];
+      if (!(isfinite(t.x) && isfinite(t.y) && isfinite(t.z) && isfinite(t.w))) bad = 1.0f;
+      float a = fmaxf(fmaxf(fabsf(t.x), fabsf(t.y)), fmaxf(fabsf(t.z), fabsf(t.w)));
+      a = fmaxf(a, __shfl_xor_sync(0xFFFFFFFFu, a, 1));
+      a = fmaxf(a, __shfl_xor_sync(0xFFFFFFFFu, a, 2));
+      a = fmaxf(a, __shfl_xor_sync(0xFFFFFFFFu, a, 4));
+      const int field = static_cast<int>((__float_as_uint(a) >> 23) & 0xFFu);
+      const int e = (a > 0.0f && field != 0xFF) ? (field != 0 ? field - 127 : ilogbf(a)) : 0;
+      const float4 y = scale_pow2(t, 19 - e);
+      const int X0 = __float2int_rn(y.x), X1 = __float2int_rn(y.y);
+      const int X2 = __float2int_rn(y.z), X3 = __float2int_rn(y.w);
+      int h0, m0, l0, h1, m1, l1, h2, m2, l2, h3, m3, l3;
+      digits3(X0, h0, m0, l0);
+      digits3(X1, h1, m1, l1);
+      digits3(X2, h2, m2, l2);
+      digits3(X3, h3, m3, l3);
+      int S = X0 + X1 + X2 + X3;
+      S += __shfl_xor_sync(0xFFFFFFFFu, S, 1);
+      S += __shfl_xor_sync(0xFFFFFFFFu, S, 2);
+      S += __shfl_xor_sync(0xFFFFFFFFu, S, 4);
+      if (i < K4) {
+        // Elements 4c..4c+3 of the block (c = i % 8): the even ones go to
+        // bytes 2c, 2c+1 of the block's first 16 bytes, the odd ones to the
+        // same bytes of its second 16.
+        uint16_t* p = reinterpret_cast<uint16_t*>(s_l) + (i / 8) * 16 + (i % 8);
+        const size_t plane = K / 2;  // u16 per digit plane
+        p[0] = static_cast<uint16_t>(pack_s8x4(h0, h2, 0, 0));
+        p[8] = static_cast<uint16_t>(pack_s8x4(h1, h3, 0, 0));
+        p[plane] = static_cast<uint16_t>(pack_s8x4(m0, m2, 0, 0));
+        p[plane + 8] = static_cast<uint16_t>(pack_s8x4(m1, m3, 0, 0));
+        p[2 * plane] = static_cast<uint16_t>(pack_s8x4(l0, l2, 0, 0));
+        p[2 * plane + 8] = static_cast<uint16_t>(pack_s8x4(l1, l3, 0, 0));
+        if ((ct & 7) == 0) {
+          s_sb[i / 8] = e - 19 >= -126 ? pow2f(e - 19) : scalbnf(1.0f, e - 19);
+          s_S[i / 8] = S;
+        }
+      }
+    }
+  }
+  // The first of consumer_max's barriers also publishes the planes.
+  return consumer_max(bad, red) == 0.0f;
+}
+
+__global__ void __launch_bounds__(kThreads, 2)
+    gemv_q4_0_limb_kernel(const uint8_t* __restrict__ W, size_t N, size_t K,
+                          const float* __restrict__ x, float* __restrict__ out, int n_stages,
+                          int pre, int* status) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const size_t nb = K / 32;
+  const size_t row_bytes = nb * 18;  // a multiple of 16 (nb % 32 == 0)
+  const StreamLayout L =
+      make_layout(K * sizeof(float), q4_limb_extra_bytes(K), kRowsPerStage * row_bytes, n_stages);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
+  uint64_t* empty = full + n_stages;
+  float* red = reinterpret_cast<float*>(smem + L.scales) + 8;
+  float4* s_x4 = reinterpret_cast<float4*>(smem + L.act);  // f32 rows (non-finite rows only)
+  uint32_t* s_l = reinterpret_cast<uint32_t*>(smem + L.extra);
+  float* s_sb = reinterpret_cast<float*>(smem + L.extra + 3 * K);
+  int* s_S = reinterpret_cast<int*>(s_sb + nb);
+  float* part = reinterpret_cast<float*>(s_S + nb);  // [2][8 rows][nb / 32]
+  uint8_t* stage0 = smem + L.stage;
+
+  size_t begin, end;
+  cta_rows(N, 1, begin, end);
+  uint64_t* act_issued = empty + n_stages;
+  init_barriers(full, empty, n_stages, act_issued);
+  if (begin >= end) return;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp == 0) {
+    if (lane == 0)
+      stream_producer(W, row_bytes, begin, end, full, empty, stage0, L.stage_bytes, n_stages,
+                      status, act_issued, pre);
+    return;
+  }
+  pdl_wait();
+  if (!q4_limb_prologue(x, K, s_l, s_sb, s_S, red, act_issued)) {
+    q4_load_act_f32<1>(x, K, s_x4, nullptr);
+    q4_rows_f32<1>(s_x4, stage0, L.stage_bytes, row_bytes, nb, N, begin, end, full, empty,
+                   n_stages, out, status);
+    return;
+  }
+
+  const uint32_t ct = threadIdx.x - 32;
+  const uint32_t nb32 = static_cast<uint32_t>(nb), K4 = static_cast<uint32_t>(K / 4);
+  const uint32_t nbw = nb32 / 32;  // warp units per row
+  const uint32_t q_step = kConsumerThreads / nb32, r_step = kConsumerThreads % nb32;
+  uint32_t xh[8], xm[8], xl[8];
+  float sb = 0.0f;
+  int S8 = 0;
+  uint32_t cur_b = 0xFFFFFFFFu;
+  const int iters = static_cast<int>((end - begin + kRowsPerStage - 1) / kRowsPerStage);
+  for (int it = 0; it < iters; ++it) {
+    const int s = it % n_stages;
+    if (!mbar_wait(&full[s], (it / n_stages) & 1, status)) return;
+    const size_t r0 = begin + static_cast<size_t>(it) * kRowsPerStage;
+    const uint32_t rows_here = static_cast<uint32_t>(std::min<size_t>(kRowsPerStage, end - r0));
+    const uint8_t* st = stage0 + s * L.stage_bytes;
+    float* pb = part + (it & 1) * kRowsPerStage * nbw;
+    uint32_t r = ct / nb32, b = ct - r * nb32;
+    for (uint32_t i0 = 0; i0 < nbw; i0 += kQ4LimbUnroll) {
+      // Up to four units, their block values reduced across the warp together.
+      float v[kQ4LimbUnroll];
+      uint32_t ru[kQ4LimbUnroll], slot[kQ4LimbUnroll];
+#pragma unroll
+      for (int u = 0; u < kQ4LimbUnroll; ++u) {
+        ru[u] = r;
+        slot[u] = b / 32;
+        v[u] = 0.0f;
+        if (i0 + u < nbw && r < rows_here) {  // warp-uniform
+          if (b != cur_b) {
+            cur_b = b;
+            const uint4* ph = reinterpret_cast<const uint4*>(s_l + 8 * b);
+            const uint4* pm = reinterpret_cast<const uint4*>(s_l + K4 + 8 * b);
+            const uint4* pl = reinterpret_cast<const uint4*>(s_l + 2 * K4 + 8 * b);
+            const uint4 h0 = ph[0], h1 = ph[1], m0 = pm[0], m1 = pm[1], l0 = pl[0], l1 = pl[1];
+            xh[0] = h0.x; xh[1] = h0.y; xh[2] = h0.z; xh[3] = h0.w;
+            xh[4] = h1.x; xh[5] = h1.y; xh[6] = h1.z; xh[7] = h1.w;
+            xm[0] = m0.x; xm[1] = m0.y; xm[2] = m0.z; xm[3] = m0.w;
+            xm[4] = m1.x; xm[5] = m1.y; xm[6] = m1.z; xm[7] = m1.w;
+            xl[0] = l0.x; xl[1] = l0.y; xl[2] = l0.z; xl[3] = l0.w;
+            xl[4] = l1.x; xl[5] = l1.y; xl[6] = l1.z; xl[7] = l1.w;
+            sb = s_sb[b];
+            S8 = 8 * s_S[b];
+          }
+          // Block b of row r: 18 bytes at an even address (d, then 16 bytes of
+          // nibbles: byte j holds elements 2j (low) and 2j + 1 (high),
+          // gguf/dequant.rs:471-500).
+          const uint8_t* blk = st + r * row_bytes + b * 18u;
+          const uint32_t a = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(blk)) & 3u;
+          const uint32_t* w = reinterpret_cast<const uint32_t*>(blk - a);
+          const uint32_t sel = 0x5432u + (a >> 1) * 0x2222u;
+          uint32_t wr[5];
+#pragma unroll
+          for (int k = 0; k < 5; ++k) wr[k] = w[k];
+          const float d = f16_bits_to_f32(__byte_perm(wr[0], 0u, 0x4410u + (a >> 1) * 0x22u));
+          // Low nibbles as bytes q, high nibbles left in place as bytes 16 q
+          // (their sums are divided by 16 exactly afterwards).
+          int dh = 0, dm = 0, dl = 0, eh = 0, em = 0, el = 0;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint32_t q = __byte_perm(wr[k], wr[k + 1], sel);
+            const uint32_t lo = q & 0x0F0F0F0Fu, hi16 = q & 0xF0F0F0F0u;
+            dh = dp4a_us(lo, xh[k], dh);
+            dm = dp4a_us(lo, xm[k], dm);
+            dl = dp4a_us(lo, xl[k], dl);
+            eh = dp4a_us(hi16, xh[k + 4], eh);
+            em = dp4a_us(hi16, xm[k + 4], em);
+            el = dp4a_us(hi16, xl[k + 4], el);
+          }
+          dh += eh >> 4;
+          dm += em >> 4;
+          dl += el >> 4;
+          const int dot = (dh * 128 + dm) * 128 + dl - S8;  // sum (q - 8) X, exact (|dot| < 2^28)
+          v[u] = __fmul_rn(__int2float_rn(dot), __fmul_rn(d, sb));
+        }
+        b += r_step;
+        r += q_step;
+        if (b >= nb32) {
+          b -= nb32;
+          ++r;
+        }
+      }
+      // Sum each v[u] over the warp: two halving exchanges leave lane L with a
+      // partial of v[(L >> 3) & 3], three more add the lanes of that group.
+      const bool up16 = (lane & 16) != 0, up8 = (lane & 8) != 0;
+      const float a0 = (up16 ? v[2] : v[0]) + __shfl_xor_sync(0xFFFFFFFFu, up16 ? v[0] : v[2], 16);
+      const float a1 = (up16 ? v[3] : v[1]) + __shfl_xor_sync(0xFFFFFFFFu, up16 ? v[1] : v[3], 16);
+      float t = (up8 ? a1 : a0) + __shfl_xor_sync(0xFFFFFFFFu, up8 ? a0 : a1, 8);
+      t += __shfl_xor_sync(0xFFFFFFFFu, t, 4);
+      t += __shfl_xor_sync(0xFFFFFFFFu, t, 2);
+      t += __shfl_xor_sync(0xFFFFFFFFu, t, 1);
+      if ((lane & 7) == 0) {
+        const int u = lane >> 3;  // (up16, up8) -> unit 2 * up16 + up8
+        if (i0 + u < nbw && ru[u] < rows_here) pb[ru[u] * nbw + slot[u]] = t;
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+    // Row r's partials (one per 32 blocks) added in block order.
+    named_bar_sync(1, kConsumerThreads);
+    if (ct < rows_here) {
+      const float* pr = pb + ct * nbw;
+      float acc = 0.0f;
+      for (uint32_t j = 0; j < nbw; ++j) acc = __fadd_rn(acc, pr[j]);
+      out[r0 + ct] = acc;
+    }
   }
 }
 
@@ -1784,7 +2163,7 @@ cudaError_t launch_gemv_i8_generic(const DeviceInfo& dev, cudaStream_t st, int M
 bool gemv_q8_0_tma_supported(const DeviceInfo&, int M, size_t K) {
   if (M < 1 || M > 8 || K == 0 || K % 32 != 0) return false;
   const size_t nb = K / 32;
-  return pick_stages(fixed_bytes_of(M * K, kConsumerWarps * M * q8_term_stride(nb) * 4),
+  return pick_stages(fixed_bytes_of(M * K, q8_term_bytes(M, nb)),
                      kRowsPerStage * nb * 34) >= 3;
 }
 
@@ -1835,7 +2214,7 @@ cudaError_t launch_gemv_q8_0_tma(const DeviceInfo& dev, cudaStream_t st, int M, 
                                  size_t N, size_t K, const float* x, float* out, int* status,
                                  LaunchStats* ls) {
   const size_t nb = K / 32;
-  const size_t extra = kConsumerWarps * M * q8_term_stride(nb) * 4;
+  const size_t extra = q8_term_bytes(M, nb);
   const StreamConfig cfg = pick_config(fixed_bytes_of(M * K, extra), kRowsPerStage * nb * 34);
   const int stages = cfg.stages;
   if (stages < 2) return cudaErrorInvalidValue;
@@ -1850,9 +2229,10 @@ cudaError_t launch_gemv_q8_0_tma(const DeviceInfo& dev, cudaStream_t st, int M, 
       auto kern = gemv_q8_0_tma_kernel<kM, (kM == 1 ? kV : 0)>;
       cudaError_t e = set_smem(kern, smem, dev.device);
       if (e != cudaSuccess) return e;
-      const int grid =
-          stream_grid(dev, N, std::min(cfg.ctas_per_sm, resident_ctas(kern, smem, dev.device)));
-      e = launch_stream_kernel(dev, kern, grid, smem, st, W, N, K, x, out, stages, pre, status);
+      const int grid = stream_grid(
+          dev, N, std::min(cfg.ctas_per_sm, resident_ctas(kern, smem, dev.device, kQ8Threads)));
+      e = launch_stream_kernel<kQ8Threads>(dev, kern, grid, smem, st, W, N, K, x, out, stages, pre,
+                                           status);
       if (e != cudaSuccess) return e;
     });
   });
@@ -1893,6 +2273,35 @@ cudaError_t launch_gemv_q4_0_tma(const DeviceInfo& dev, cudaStream_t st, int M, 
                              pre_stages(stages), status);
     if (e != cudaSuccess) return e;
   });
+  if (ls) ls->launches++;
+  return cudaGetLastError();
+}
+
+static StreamConfig q4_0_limb_config(size_t K) {
+  return pick_config(fixed_bytes_of(K * sizeof(float), q4_limb_extra_bytes(K)),
+                     kRowsPerStage * (K / 32) * 18);
+}
+
+bool gemv_q4_0_limb_supported(const DeviceInfo& dev, size_t K, const float* x) {
+  if (!dev.opt.q4_limb || K == 0 || K % 1024 != 0 || (reinterpret_cast<uintptr_t>(x) & 15) != 0)
+    return false;
+  return q4_0_limb_config(K).stages >= 3;
+}
+
+cudaError_t launch_gemv_q4_0_limb(const DeviceInfo& dev, cudaStream_t st, const uint8_t* W, size_t N,
+                                  size_t K, const float* x, float* out, int* status, LaunchStats* ls) {
+  if (!gemv_q4_0_limb_supported(dev, K, x)) return cudaErrorInvalidValue;
+  const StreamConfig cfg = q4_0_limb_config(K);
+  const size_t stage_bytes = kRowsPerStage * (K / 32) * 18;
+  const size_t smem =
+      make_layout(K * sizeof(float), q4_limb_extra_bytes(K), stage_bytes, cfg.stages).total;
+  cudaError_t e = set_smem(gemv_q4_0_limb_kernel, smem, dev.device);
+  if (e != cudaSuccess) return e;
+  const int grid = stream_grid(
+      dev, N, std::min(cfg.ctas_per_sm, resident_ctas(gemv_q4_0_limb_kernel, smem, dev.device)));
+  e = launch_stream_kernel(dev, gemv_q4_0_limb_kernel, grid, smem, st, W, N, K, x, out, cfg.stages,
+                           pre_stages(cfg.stages), status);
+  if (e != cudaSuccess) return e;
   if (ls) ls->launches++;
   return cudaGetLastError();
 }

@@ -102,6 +102,7 @@ struct Options {
   int fa_split = 3;    // MRI_OPT_FA_SPLIT: key tiles from which a prefill key walk is split (0 = never)
   int shard_peer = 2;  // MRI_OPT_SHARD_PEER: 0 NCCL, 1 peer memory, 2 peer memory for m > 8 only
   int gemm_pair = 1;   // MRI_OPT_GEMM_PAIR: 1 CTA pairs from 4 rounds of pair tiles, 2 always, 0 never
+  int q4_limb = 1;     // MRI_OPT_Q4_LIMB: Q4_0 at m = 1 on integer block dots
   // Internal (not an ABI option): SMs the tensor-core GEMM leaves free for
   // other work running beside it.
   int sm_reserve = 0;
@@ -195,6 +196,11 @@ cudaError_t launch_gemv_q4_0_mma(const DeviceInfo& dev, cudaStream_t st, int M, 
                                  size_t N, size_t K, const uint32_t* xs, float* out, int* status,
                                  LaunchStats* ls);
 bool gemv_q4_0_tma_supported(const DeviceInfo& dev, int M, size_t K);
+// M = 1, K % 1024 == 0, x 16-byte aligned: integer block dots (f32 for a
+// row with an inf or a NaN).
+bool gemv_q4_0_limb_supported(const DeviceInfo& dev, size_t K, const float* x);
+cudaError_t launch_gemv_q4_0_limb(const DeviceInfo& dev, cudaStream_t st, const uint8_t* W, size_t N,
+                                  size_t K, const float* x, float* out, int* status, LaunchStats* ls);
 cudaError_t launch_gemv_q4_0_tma(const DeviceInfo& dev, cudaStream_t st, int M, const uint8_t* W,
                                  size_t N, size_t K, const float* x, float* out, int* status,
                                  LaunchStats* ls);

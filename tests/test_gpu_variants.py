@@ -329,15 +329,19 @@ def test_one_launch_quantizer_feeds_gemm_exact(mri, oracle, gpu_ctx):
         assert np.array_equal(bits(o.cpu().numpy()), bits(want))
 
 
-# ── Q4_0 at one row: int16 activations on dp2a, f32 for non-finite rows ─────
+# ── Q4_0 at one row: integer block dots, f32 for non-finite rows ─────────────
 
-@pytest.mark.parametrize("n,k", [(11008, 4096), (300, 1024), (7, 32), (2049, 8192)])
-def test_q4_0_one_row_int16_path(mri, oracle, n, k):
-    """matmul_q4_0_dequant (q4_0.rs:94-181) at M = 1: the activation row is
-    quantized to int16 and the block dots run on dp2a; within the Q4_0 bar of
-    the reference's f32 sum, including rows whose activations span a wide
-    range (a few large values, many tiny ones)."""
+@pytest.mark.parametrize("limb", [1, 0])
+@pytest.mark.parametrize("n,k", [(11008, 4096), (300, 1024), (7, 32), (2049, 8192), (64, 28672)])
+def test_q4_0_one_row(mri, oracle, ctx_option, n, k, limb):
+    """matmul_q4_0_dequant (q4_0.rs:94-181) at M = 1, on the integer kernel
+    (OPT_Q4_LIMB = 1, K % 1024 == 0: 21-bit activation digits per block, exact
+    dp4a block dots) and on the f32 streaming kernel (OPT_Q4_LIMB = 0, and
+    K = 32 either way); within the Q4_0 bar of the reference's f32 sum,
+    including rows whose activations span a wide range (a few large values,
+    many tiny ones)."""
     from test_gpu_parity import q4_close
+    ctx_option(mri.OPT_Q4_LIMB, limb)
     rng = np.random.default_rng(n + k)
     wf = rng.normal(0, 0.02, size=(n, k)).astype(np.float32)
     wb = oracle.quantize_q4_0_matrix(wf, n, k)
@@ -353,8 +357,9 @@ def test_q4_0_one_row_int16_path(mri, oracle, n, k):
 
 
 def test_q4_0_one_row_non_finite_takes_f32_path(mri, oracle):
-    """An inf or a NaN in the activation row: the f32 path, so the outputs
-    are non-finite exactly where the reference's are (q4_0.rs:94-181)."""
+    """An inf or a NaN in the activation row: the integer kernel switches to
+    the f32 loop, so the outputs are non-finite exactly where the
+    reference's are (q4_0.rs:94-181)."""
     rng = np.random.default_rng(77)
     n, k = 1000, 4096
     wb = oracle.quantize_q4_0_matrix(rng.normal(0, 0.02, size=(n, k)).astype(np.float32), n, k)

@@ -278,10 +278,11 @@ int mri::matmul_int8_fused(::mri_ctx* ctx, const float* x, size_t m, size_t k, c
 
 namespace {
 
-// Chunks of at most 8 activation rows.  A chunk of 2..8 rows whose shape the
-// MMA kernel covers, and every chunk without a streaming kernel,
-// read activations quantized per row once for the whole call (q8_direct.rs:264);
-// the streaming kernel for the rest quantizes in its prologue.
+// Chunks of at most 8 activation rows.  The streaming kernel quantizes its
+// rows per row in its prologue (q8_direct.rs:264); the MMA kernel (2..8 rows)
+// and the generic one read activations quantized per row once for the whole
+// call (measured: the quantizer kernel in front of the MMA kernel costs less
+// than the same reductions in its prologue).
 int run_q8_0(mri_ctx* ctx, const float* x, size_t m, const mri_q8_0_matrix* w, float* out) {
   const size_t N = w->n_out, K = w->k_in;
   if (m == 0 || N == 0) return MRI_OK;
@@ -305,8 +306,12 @@ int run_q8_0(mri_ctx* ctx, const float* x, size_t m, const mri_q8_0_matrix* w, f
       MRI_CUDA_TRY(mri::launch_quantize(ctx->dev, st, x, m, K, 1, q, scales, amax, &ctx->ls));
     }
     if (pin) {
-      MRI_CUDA_TRY(mri::launch_gemv_q8_0_mma(ctx->dev, st, mc, w->data, N, K, q + m0 * K,
-                                             scales + m0, out + m0 * N, ctx->d_status, &ctx->ls));
+      mri::ActArgs a;
+      a.xq = q + m0 * K;
+      a.scale_dev = scales + m0;
+      a.mode = mri::ACT_I8_DEV_ROW_SCALE;
+      MRI_CUDA_TRY(mri::launch_gemv_q8_0_mma(ctx->dev, st, mc, w->data, N, K, a, out + m0 * N,
+                                             ctx->d_status, &ctx->ls));
     } else {
       MRI_CUDA_TRY(mri::launch_gemv_q8_0_generic(ctx->dev, st, mc, w->data, N, K, q + m0 * K,
                                                  scales + m0, out + m0 * N, &ctx->ls));

@@ -855,11 +855,11 @@ __global__ void __launch_bounds__(kQ8Threads, M <= 2 ? 2 : 1)
 // [row][block][m]; two sum warps add every (row, m)'s terms in block order
 // from 0.0 (q8_direct.rs:266-285), one chain per thread, while the dot warps
 // work on the next stage.  The integer dots are exact, so the result is the
-// reference's bit for bit.  Activations arrive quantized per row (the
-// quantizer kernel runs first; its launch overlaps this kernel's weight
-// stream).  Rows are copied into stage slots padded by 16 bytes so the 8 rows
-// a warp reads fall in different banks.  Preconditions (launcher): nb % 8 == 0,
-// nb <= 256, 16-byte aligned xq.
+// reference's bit for bit.  The dot warps copy the activation rows, quantized
+// per row by the quantizer kernel (q8_direct.rs:264), into shared memory while
+// the producer streams the first stage.  Rows are copied into stage slots padded by 16 bytes so the 8 rows a
+// warp reads fall in different banks.  Preconditions (launcher): nb % 8 == 0,
+// nb <= 256.
 constexpr int kQ8MmaDotWarps = kConsumerWarps;
 constexpr int kQ8MmaSumWarps = 2;
 constexpr int kQ8MmaThreads = 32 * (1 + kQ8MmaDotWarps + kQ8MmaSumWarps);
@@ -885,8 +885,8 @@ __device__ __forceinline__ void mma_s8_m16n8k32(int d[4], uint32_t a0, uint32_t 
 template <int M>
 __global__ void __launch_bounds__(kQ8MmaThreads, 1)
     gemv_q8_0_mma_kernel(const uint8_t* __restrict__ W, size_t N, size_t K,
-                         const int8_t* __restrict__ xq, const float* __restrict__ x_scales,
-                         float* __restrict__ out, int n_stages, int* status) {
+                         ActArgs act, float* __restrict__ out, int n_stages, int pre,
+                         int* status) {
   extern __shared__ __align__(128) uint8_t smem[];
   const size_t nb = K / 32;
   const size_t row_bytes = nb * 34;
@@ -897,15 +897,15 @@ __global__ void __launch_bounds__(kQ8MmaThreads, 1)
   uint64_t* empty = full + n_stages;
   uint64_t* tfull = reinterpret_cast<uint64_t*>(smem + L.extra);  // [2], dot warps arrive
   uint64_t* tempty = tfull + 2;                                    // [2], sum warps arrive
-  uint64_t* xfull = tempty + 2;                                    // quantized activations landed
+  uint64_t* act_issued = tempty + 2;                               // dot warps' x loads issued
+  float* s_scale = reinterpret_cast<float*>(smem + L.scales);
+  float* red = s_scale + 8;
   float* T = reinterpret_cast<float*>(smem + L.act);               // [2][8 rows][trow]
   uint8_t* stage0 = smem + L.stage;
   const size_t plane = kRowsPerStage * trow;  // floats per term buffer
   // Until the first stage's terms are written the second term buffer holds
-  // the quantized activation rows, K + 16 bytes apart (the pad spreads the
-  // rows over the banks).
+  // the quantized activation rows [M][K].
   int8_t* s_x = reinterpret_cast<int8_t*>(T + plane);
-  const size_t xstride = K + 16;
 
   size_t begin, end;
   cta_rows(N, 1, begin, end);
@@ -918,7 +918,7 @@ __global__ void __launch_bounds__(kQ8MmaThreads, 1)
       mbar_init(&tfull[b], kQ8MmaDotWarps);
       mbar_init(&tempty[b], kQ8MmaSumWarps);
     }
-    mbar_init(xfull, 1);
+    mbar_init(act_issued, kQ8MmaDotWarps);
     fence_barrier_init();
   }
   __syncthreads();
@@ -928,16 +928,16 @@ __global__ void __launch_bounds__(kQ8MmaThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int iters = static_cast<int>((end - begin + kRowsPerStage - 1) / kRowsPerStage);
   if (warp == 0) {
-    // Producer: the whole ring first (weights do not depend on the previous
-    // kernel), then the activation rows once the quantizer has finished, then
-    // the rest of the weights.  Each stage row is its own bulk copy into a
-    // padded slot.
+    // Producer: `pre` stages, then the rest once the dot warps have issued
+    // their activation loads (so those loads do not queue behind the ring).
+    // Each stage row is its own bulk copy into a padded slot.
     if (lane == 0) {
       const uint64_t policy = l2_policy_evict_first();
       int issued = 0;
       bool ok = true;
       for (int it = 0; it < iters && ok; ++it) {
         const int s = it % n_stages;
+        if (it == pre && !mbar_wait(act_issued, 0, status)) break;
         if (it >= n_stages && !mbar_wait(&empty[s], ((it / n_stages) - 1) & 1, status)) {
           ok = false;
           break;
@@ -950,17 +950,9 @@ __global__ void __launch_bounds__(kQ8MmaThreads, 1)
           bulk_copy_g2s_stream(dst + r * rstride, W + (r0 + r) * row_bytes,
                                static_cast<uint32_t>(row_bytes), &full[s], policy);
         issued = it + 1;
-        if (issued == std::min(iters, n_stages)) {
-          pdl_wait();
-          mbar_arrive_expect_tx(xfull, static_cast<uint32_t>(M * K));
-          for (int m = 0; m < M; ++m)
-            bulk_copy_g2s(s_x + m * xstride, xq + static_cast<size_t>(m) * K,
-                          static_cast<uint32_t>(K), xfull);
-        }
       }
       for (int it = std::max(0, issued - n_stages); it < issued; ++it)
         mbar_wait(&full[it % n_stages], (it / n_stages) & 1, status);
-      if (issued >= std::min(iters, n_stages)) mbar_wait(xfull, 0, status);
     }
     return;
   }
@@ -993,24 +985,23 @@ __global__ void __launch_bounds__(kQ8MmaThreads, 1)
   const int g = lane >> 2, t = lane & 3;
   const int bpw = static_cast<int>(nb / kQ8MmaDotWarps);
   const int kb0 = dw * bpw;
-  // On a timeout every dot warp still reaches the named barrier below (with
-  // zero fragments) and returns after it.
-  const bool xok = mbar_wait(xfull, 0, status);
+  // The quantized activation rows into s_x; the prologue ends with a barrier
+  // of the dot warps.
+  load_act_i8_rowmajor<M, 0>(act, K, s_x, s_scale, red, act_issued);
   uint32_t bf[kQ8MmaMaxBpw][2];
 #pragma unroll
   for (int i = 0; i < kQ8MmaMaxBpw; ++i) {
-    const bool ok = xok && i < bpw && g < M;
+    const bool ok = i < bpw && g < M;
     const uint32_t* p = reinterpret_cast<const uint32_t*>(
-        s_x + (ok ? g : 0) * xstride + static_cast<size_t>(kb0 + (ok ? i : 0)) * 32) + t;
+        s_x + (ok ? g : 0) * K + static_cast<size_t>(kb0 + (ok ? i : 0)) * 32) + t;
     bf[i][0] = ok ? p[0] : 0u;
     bf[i][1] = ok ? p[4] : 0u;
   }
-  const float sa0 = 2 * t < M ? ld_act(x_scales + 2 * t) : 0.0f;
-  const float sa1 = 2 * t + 1 < M ? ld_act(x_scales + 2 * t + 1) : 0.0f;
+  const float sa0 = 2 * t < M ? s_scale[2 * t] : 0.0f;
+  const float sa1 = 2 * t + 1 < M ? s_scale[2 * t + 1] : 0.0f;
   // The second term buffer is written from stage 1 on: every dot warp has
   // its fragments first.
   named_bar_sync(1, kQ8MmaDotWarps * 32);
-  if (!xok) return;
 
   for (int it = 0; it < iters; ++it) {
     const int s = it % n_stages, tb = it & 1;
@@ -2179,18 +2170,17 @@ bool q8_0_mma_supported(const DeviceInfo& dev, int M, size_t K) {
 }
 
 cudaError_t launch_gemv_q8_0_mma(const DeviceInfo& dev, cudaStream_t st, int M, const uint8_t* W,
-                                 size_t N, size_t K, const int8_t* xq, const float* x_scales,
-                                 float* out, int* status, LaunchStats* ls) {
-  if (!q8_0_mma_supported(dev, M, K) || (reinterpret_cast<uintptr_t>(xq) & 15) != 0 ||
-      (reinterpret_cast<uintptr_t>(W) & 15) != 0)
+                                 size_t N, size_t K, const ActArgs& act, float* out, int* status,
+                                 LaunchStats* ls) {
+  if (!q8_0_mma_supported(dev, M, K) || (reinterpret_cast<uintptr_t>(W) & 15) != 0 ||
+      act.mode != ACT_I8_DEV_ROW_SCALE)
     return cudaErrorInvalidValue;
   const size_t nb = K / 32;
   const size_t stage_bytes = kRowsPerStage * q8_mma_row_stride(nb);
   const int stages = std::min(kMaxStages, stages_within(fixed_bytes_of(q8_mma_term_bytes(nb), 64),
                                                          stage_bytes, kSmemBudget));
   const size_t smem = make_layout(q8_mma_term_bytes(nb), 64, stage_bytes, stages).total;
-  void (*kern)(const uint8_t*, size_t, size_t, const int8_t*, const float*, float*, int, int*) =
-      nullptr;
+  void (*kern)(const uint8_t*, size_t, size_t, ActArgs, float*, int, int, int*) = nullptr;
   switch (M) {
     case 2: kern = gemv_q8_0_mma_kernel<2>; break;
     case 3: kern = gemv_q8_0_mma_kernel<3>; break;
@@ -2203,8 +2193,8 @@ cudaError_t launch_gemv_q8_0_mma(const DeviceInfo& dev, cudaStream_t st, int M, 
   }
   cudaError_t e = set_smem(kern, smem, dev.device);
   if (e != cudaSuccess) return e;
-  e = launch_stream_kernel<kQ8MmaThreads>(dev, kern, stream_grid(dev, N, 1), smem, st, W, N, K, xq, x_scales,
-                                          out, stages, status);
+  e = launch_stream_kernel<kQ8MmaThreads>(dev, kern, stream_grid(dev, N, 1), smem, st, W, N, K, act,
+                                          out, stages, pre_stages(stages), status);
   if (e != cudaSuccess) return e;
   if (ls) ls->launches++;
   return cudaGetLastError();

@@ -171,13 +171,13 @@ bool gemv_q8_0_tma_supported(const DeviceInfo& dev, int M, size_t K);
 cudaError_t launch_gemv_q8_0_tma(const DeviceInfo& dev, cudaStream_t st, int M, const uint8_t* W,
                                  size_t N, size_t K, const float* x, float* out, int* status,
                                  LaunchStats* ls);
-// M = 2..8 with the activations quantized per row beforehand (xq [M, K],
-// 16-byte aligned, and x_scales [M] on the device): block dots on the warp
-// MMA.  q8_0_mma_supported tells where the kernel applies.
+// M = 2..8: block dots on the warp MMA.  act is ACT_I8_DEV_ROW_SCALE: the
+// rows quantized per row beforehand (xq [M, K] and M scales on the device).
+// q8_0_mma_supported tells where the kernel applies.
 bool q8_0_mma_supported(const DeviceInfo& dev, int M, size_t K);
 cudaError_t launch_gemv_q8_0_mma(const DeviceInfo& dev, cudaStream_t st, int M, const uint8_t* W,
-                                 size_t N, size_t K, const int8_t* xq, const float* x_scales,
-                                 float* out, int* status, LaunchStats* ls);
+                                 size_t N, size_t K, const ActArgs& act, float* out, int* status,
+                                 LaunchStats* ls);
 // Generic: activations pre-quantized per row into xq/scales (device).
 cudaError_t launch_gemv_q8_0_generic(const DeviceInfo& dev, cudaStream_t st, int M,
                                      const uint8_t* W, size_t N, size_t K, const int8_t* xq,

@@ -66,6 +66,12 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
   }
 }
 
+// Bulk prefetch of [src, src + bytes) into L2 (src 16-byte aligned, bytes a
+// multiple of 16).  A hint: no completion, no effect on results.
+__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // 1-D bulk copy global -> shared, completing `bytes` of transaction count on
 // `bar`.  dst and src 16-byte aligned, bytes a multiple of 16.  No multicast.
 __device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes,

@@ -161,15 +161,29 @@ __global__ void __cluster_dims__(1, kDecCluster, 1) __launch_bounds__(kDecWarps 
                                const float* __restrict__ kc, const float* __restrict__ vc,
                                const int* __restrict__ pos_dev, float scale, float* __restrict__ out) {
   pdl_trigger();
-  pdl_wait();
   cg::cluster_group cluster = cg::this_cluster();
   const int h = blockIdx.x;
   const int c = static_cast<int>(cluster.block_rank());
+  const int kv_h = h / (n_heads / n_kv);
+  const int kvd = n_kv * hd;
+  {
+    // The cache rows before the current position were written by earlier
+    // steps: pull this CTA's share into L2 while the QKV projection in front
+    // (which writes the current row) finishes.  The position may still be
+    // the previous step's value here; a prefetch of the wrong rows only costs
+    // bandwidth, and every prefetched row lies inside the cache.
+    const int p = *reinterpret_cast<const volatile int*>(pos_dev);
+    const int chunk = (p + 1 + kDecCluster - 1) / kDecCluster;
+    const int a0 = c * chunk, a1 = min(p, a0 + chunk);
+    for (int i = a0 * 2 + static_cast<int>(threadIdx.x); i < a1 * 2; i += blockDim.x) {
+      const float* src = (i & 1 ? vc : kc) + static_cast<size_t>(i >> 1) * kvd + static_cast<size_t>(kv_h) * hd;
+      mri::prefetch_l2(src, static_cast<uint32_t>(hd * sizeof(float)));
+    }
+  }
+  pdl_wait();
   const int total = mri::ld_act(pos_dev) + 1;
   const int chunk = (total + kDecCluster - 1) / kDecCluster;
   const int j0 = c * chunk, j1 = min(total, j0 + chunk);
-  const int kv_h = h / (n_heads / n_kv);
-  const int kvd = n_kv * hd;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool dim_ok = lane * 4 < hd;
   const size_t base = static_cast<size_t>(kv_h) * hd + lane * 4;

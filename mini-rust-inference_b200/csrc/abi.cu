@@ -401,6 +401,32 @@ int host_stage(mri_ctx* ctx, size_t in_bytes, size_t out_bytes, size_t acc_bytes
   return MRI_OK;
 }
 
+// The device mapping of a caller's host buffer when it is page-locked and
+// mapped into the device's address space (e.g. from cudaHostAlloc), else null.
+float* mapped_host(void* p) {
+  cudaPointerAttributes a{};
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  if (a.type != cudaMemoryTypeHost || a.devicePointer == nullptr) return nullptr;
+  return static_cast<float*>(a.devicePointer);
+}
+
+// A host call's f32 result (n floats staged at `dev`) into the caller's
+// buffer: into a pinned buffer by a copy kernel writing its device mapping
+// (launched behind the product, no copy-engine round trip), else by a copy.
+int copy_result(mri_ctx* ctx, float* out, const float* dev, size_t n) {
+  if (n == 0) return MRI_OK;
+  float* mapped = n % 4 == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0 ? mapped_host(out) : nullptr;
+  if (mapped) {
+    const cudaError_t e = mri::launch_copy_out(ctx->dev, ctx->stream, dev, mapped, n, &ctx->ls);
+    return e == cudaSuccess ? MRI_OK : cuda_fail(e, "copy_out");
+  }
+  MRI_CUDA_TRY(cudaMemcpyAsync(out, dev, n * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  return MRI_OK;
+}
+
 // The quantizer area at the front of scratch must not overlap the host
 // staging area, so host calls reserve it explicitly (host_stage quant_*),
 // and run_int8/run_q8_0 carve from offset 0 within that reservation.
@@ -855,7 +881,7 @@ int mri_host_matmul_int8_from_f32(mri_ctx* ctx, const float* x, size_t m, size_t
   a.x = reinterpret_cast<float*>(hs.in);
   a.mode = mri::ACT_F32_PER_TENSOR;
   if (int rc = run_int8(ctx, a, w, m, hs.out, nullptr)) return rc;
-  if (m * N) MRI_CUDA_TRY(cudaMemcpyAsync(out, hs.out, m * N * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  if (int rc = copy_result(ctx, out, hs.out, m * N)) return rc;
   MRI_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
   return read_status(ctx);
 }
@@ -870,7 +896,7 @@ int mri_host_matmul_q8_0_direct(mri_ctx* ctx, const float* x, size_t m, size_t k
   if (int rc = host_stage(ctx, m * k * 4, m * N * 4, 0, m, k, &hs)) return rc;
   if (m * k) MRI_CUDA_TRY(cudaMemcpyAsync(hs.in, x, m * k * 4, cudaMemcpyHostToDevice, ctx->stream));
   if (int rc = run_q8_0(ctx, reinterpret_cast<float*>(hs.in), m, w, hs.out)) return rc;
-  if (m * N) MRI_CUDA_TRY(cudaMemcpyAsync(out, hs.out, m * N * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  if (int rc = copy_result(ctx, out, hs.out, m * N)) return rc;
   MRI_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
   return read_status(ctx);
 }
@@ -887,7 +913,7 @@ int mri_host_matmul_q4_0_dequant(mri_ctx* ctx, const float* x, size_t m, size_t 
   if (int rc = host_stage(ctx, m * k * 4, m * N * 4, 0, m, 4 * k + 64, &hs)) return rc;
   if (m * k) MRI_CUDA_TRY(cudaMemcpyAsync(hs.in, x, m * k * 4, cudaMemcpyHostToDevice, ctx->stream));
   if (int rc = run_q4_0(ctx, reinterpret_cast<float*>(hs.in), m, w, hs.out)) return rc;
-  if (m * N) MRI_CUDA_TRY(cudaMemcpyAsync(out, hs.out, m * N * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  if (int rc = copy_result(ctx, out, hs.out, m * N)) return rc;
   MRI_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
   return read_status(ctx);
 }

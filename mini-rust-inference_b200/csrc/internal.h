@@ -132,6 +132,10 @@ cudaError_t launch_quantize(const DeviceInfo& dev, cudaStream_t st, const float*
                             int swiglu = 0, unsigned* sync = nullptr, int* status = nullptr);
 
 // out[i] = residual[i] + out[i] (the reference's x + projected).
+// n floats (n % 4 == 0, both 16-byte aligned) from device memory into a
+// pinned host buffer's device mapping, after the previous kernel in the stream.
+cudaError_t launch_copy_out(const DeviceInfo& dev, cudaStream_t st, const float* src, float* dst,
+                            size_t n, LaunchStats* ls);
 cudaError_t launch_add_residual(const DeviceInfo& dev, cudaStream_t st, float* out,
                                 const float* residual, size_t n, LaunchStats* ls);
 

@@ -670,6 +670,17 @@ __global__ void __launch_bounds__(kQThreads) quant_rows_once_kernel(
   }
 }
 
+// Result rows from device memory into a caller's pinned host buffer (mapped
+// into the device's address space), 16 bytes per store, after the producing
+// kernel has finished.
+__global__ void __launch_bounds__(kQThreads) copy_out_kernel(const float4* __restrict__ src,
+                                                             float4* __restrict__ dst, size_t n4) {
+  pdl_enter();
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n4;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x)
+    dst[i] = ld_act(src + i);
+}
+
 __global__ void add_inplace_kernel(float* __restrict__ out, const float* __restrict__ res, size_t n) {
   for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<size_t>(gridDim.x) * blockDim.x)
@@ -677,6 +688,20 @@ __global__ void add_inplace_kernel(float* __restrict__ out, const float* __restr
 }
 
 }  // namespace
+
+cudaError_t launch_copy_out(const DeviceInfo& dev, cudaStream_t st, const float* src, float* dst,
+                            size_t n, LaunchStats* ls) {
+  if (n % 4 != 0 || (reinterpret_cast<uintptr_t>(src) & 15) != 0 ||
+      (reinterpret_cast<uintptr_t>(dst) & 15) != 0)
+    return cudaErrorInvalidValue;
+  if (n == 0) return cudaSuccess;
+  const size_t n4 = n / 4;
+  const unsigned grid = static_cast<unsigned>(std::min<size_t>(dev.sm_count, (n4 + kQThreads - 1) / kQThreads));
+  cudaError_t e = qlaunch(dev, copy_out_kernel, grid, st, reinterpret_cast<const float4*>(src),
+                          reinterpret_cast<float4*>(dst), n4);
+  if (ls) ls->launches++;
+  return e;
+}
 
 cudaError_t launch_add_residual(const DeviceInfo& dev, cudaStream_t st, float* out,
                                 const float* residual, size_t n, LaunchStats* ls) {

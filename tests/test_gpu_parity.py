@@ -497,3 +497,38 @@ def test_device_inputs_ordered_with_torch_stream(mri, oracle, gpu_ctx):
 def test_device_status_clean(mri, gpu_ctx):
     """No bounded device-side wait gave up during the tests above."""
     gpu_ctx.check_device_status()
+
+
+@pytest.mark.parametrize("m", [1, 3])
+def test_host_calls_with_pinned_buffers(mri, oracle, gpu_ctx, m):
+    """The host-buffer entry points write a pinned (page-locked, mapped)
+    output through a copy kernel on its device mapping instead of a
+    device-to-host copy: the results equal the reference's, and the same call
+    on pageable memory, bit for bit, also after the caller rewrites the
+    pinned input in place."""
+    import ctypes
+    import torch
+    lib = mri._lib.load()
+    rng = np.random.default_rng(77 + m)
+    n, k = 1000, 4096
+    x = rng.normal(0, 1, size=(m, k)).astype(np.float32)
+    wq, ws = rng.integers(-127, 128, size=n * k, dtype=np.int8), rng.uniform(0.001, 0.02, n).astype(np.float32)
+    wf = rng.normal(0, 0.02, size=(n, k)).astype(np.float32)
+    qm = mri.QuantizedMatrix(wq, ws, n, k)
+    q8 = mri.Q8_0WeightMatrix.from_raw_bytes(oracle.quantize_q8_0_matrix(wf, n, k), n, k)
+    q4b = oracle.quantize_q4_0_matrix(wf, n, k)
+    q4 = mri.Q4_0Matrix(q4b, n, k)
+    x_pin = torch.empty(m, k).pin_memory()
+    for x in (x, rng.normal(0, 3, size=(m, k)).astype(np.float32)):
+        x_pin.copy_(torch.from_numpy(x))  # rewritten in place for the second round
+        cases = [(lib.mri_host_matmul_int8_from_f32, qm, mri.matmul_int8_from_f32(x, qm)),
+                 (lib.mri_host_matmul_q8_0_direct, q8, mri.matmul_q8_0_direct(x, q8)),
+                 (lib.mri_host_matmul_q4_0_dequant, q4, mri.matmul_q4_0_dequant(x, q4b, n, k))]
+        for fn, w, pageable in cases:
+            out = torch.full((m, n), float("nan")).pin_memory()
+            rc = fn(gpu_ctx.handle, ctypes.c_void_p(x_pin.data_ptr()), m, k, w.handle,
+                    ctypes.c_void_p(out.data_ptr()))
+            assert rc == 0, mri._lib.last_error()
+            assert np.array_equal(bits(out.numpy()), bits(np.asarray(pageable, np.float32))), fn
+        want = oracle.matmul_int8_from_f32(x, m, k, wq, ws, n, k)
+        assert np.array_equal(bits(cases[0][2]), bits(want))

@@ -1466,6 +1466,61 @@ __global__ void __launch_bounds__(kThreads, 2)
       // Up to four units, their block values reduced across the warp together.
       float v[kQ4LimbUnroll];
       uint32_t ru[kQ4LimbUnroll], slot[kQ4LimbUnroll];
+      if (r_step == 0) {
+        // The thread's block never changes (nb divides 256): all the units'
+        // loads are issued before any of their arithmetic.
+        if (b != cur_b) {
+          cur_b = b;
+          const uint4* ph = reinterpret_cast<const uint4*>(s_l + 8 * b);
+          const uint4* pm = reinterpret_cast<const uint4*>(s_l + K4 + 8 * b);
+          const uint4* pl = reinterpret_cast<const uint4*>(s_l + 2 * K4 + 8 * b);
+          const uint4 h0 = ph[0], h1 = ph[1], m0 = pm[0], m1 = pm[1], l0 = pl[0], l1 = pl[1];
+          xh[0] = h0.x; xh[1] = h0.y; xh[2] = h0.z; xh[3] = h0.w;
+          xh[4] = h1.x; xh[5] = h1.y; xh[6] = h1.z; xh[7] = h1.w;
+          xm[0] = m0.x; xm[1] = m0.y; xm[2] = m0.z; xm[3] = m0.w;
+          xm[4] = m1.x; xm[5] = m1.y; xm[6] = m1.z; xm[7] = m1.w;
+          xl[0] = l0.x; xl[1] = l0.y; xl[2] = l0.z; xl[3] = l0.w;
+          xl[4] = l1.x; xl[5] = l1.y; xl[6] = l1.z; xl[7] = l1.w;
+          sb = s_sb[b];
+          S8 = 8 * s_S[b];
+        }
+        const uint32_t a = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(st + b * 18u)) & 3u;
+        const uint32_t sel = 0x5432u + (a >> 1) * 0x2222u;
+        uint32_t wr[kQ4LimbUnroll][5];
+        bool ok[kQ4LimbUnroll];
+#pragma unroll
+        for (int u = 0; u < kQ4LimbUnroll; ++u) {
+          ru[u] = r + q_step * u;
+          slot[u] = b / 32;
+          ok[u] = i0 + u < nbw && ru[u] < rows_here;
+          const uint32_t* w = reinterpret_cast<const uint32_t*>(
+              st + (ok[u] ? ru[u] * row_bytes : 0) + b * 18u - a);
+#pragma unroll
+          for (int k = 0; k < 5; ++k) wr[u][k] = w[k];
+        }
+#pragma unroll
+        for (int u = 0; u < kQ4LimbUnroll; ++u) {
+          const float d = f16_bits_to_f32(__byte_perm(wr[u][0], 0u, 0x4410u + (a >> 1) * 0x22u));
+          int dh = 0, dm = 0, dl = 0, eh = 0, em = 0, el = 0;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint32_t q = __byte_perm(wr[u][k], wr[u][k + 1], sel);
+            const uint32_t lo = q & 0x0F0F0F0Fu, hi16 = q & 0xF0F0F0F0u;
+            dh = dp4a_us(lo, xh[k], dh);
+            dm = dp4a_us(lo, xm[k], dm);
+            dl = dp4a_us(lo, xl[k], dl);
+            eh = dp4a_us(hi16, xh[k + 4], eh);
+            em = dp4a_us(hi16, xm[k + 4], em);
+            el = dp4a_us(hi16, xl[k + 4], el);
+          }
+          dh += eh >> 4;
+          dm += em >> 4;
+          dl += el >> 4;
+          const int dot = (dh * 128 + dm) * 128 + dl - S8;
+          v[u] = ok[u] ? __fmul_rn(__int2float_rn(dot), __fmul_rn(d, sb)) : 0.0f;
+        }
+        r += q_step * kQ4LimbUnroll;
+      } else {
 #pragma unroll
       for (int u = 0; u < kQ4LimbUnroll; ++u) {
         ru[u] = r;
@@ -1525,6 +1580,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           ++r;
         }
       }
+      }
       // Sum each v[u] over the warp: two halving exchanges leave lane L with a
       // partial of v[(L >> 3) & 3], three more add the lanes of that group.
       const bool up16 = (lane & 16) != 0, up8 = (lane & 8) != 0;
@@ -1536,7 +1592,10 @@ __global__ void __launch_bounds__(kThreads, 2)
       t += __shfl_xor_sync(0xFFFFFFFFu, t, 1);
       if ((lane & 7) == 0) {
         const int u = lane >> 3;  // (up16, up8) -> unit 2 * up16 + up8
-        if (i0 + u < nbw && ru[u] < rows_here) pb[ru[u] * nbw + slot[u]] = t;
+        // Register selects (no dynamic indexing into the unit arrays).
+        const uint32_t ur = u == 0 ? ru[0] : u == 1 ? ru[1] : u == 2 ? ru[2] : ru[3];
+        const uint32_t us = u == 0 ? slot[0] : u == 1 ? slot[1] : u == 2 ? slot[2] : slot[3];
+        if (i0 + u < nbw && ur < rows_here) pb[ur * nbw + us] = t;
       }
     }
     __syncwarp();

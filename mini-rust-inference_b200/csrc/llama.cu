@@ -62,6 +62,28 @@ __global__ void embed_kernel(const uint32_t* __restrict__ tokens, const float* _
   const uint32_t tok = mri::ld_act(tokens + blockIdx.x);
   const float* src = embd + static_cast<size_t>(tok) * d;
   float* dst = x + static_cast<size_t>(blockIdx.x) * d;
+  if ((d & 3) == 0 && ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0) {
+    // The row in 16-byte pieces, up to 8 loads in flight per thread before
+    // any store (one HBM round trip for a 4096-wide row).
+    constexpr int U = 8;
+    const int d4 = d / 4;
+    const float4* s4 = reinterpret_cast<const float4*>(src);
+    float4* o4 = reinterpret_cast<float4*>(dst);
+    for (int i0 = 0; i0 < d4; i0 += U * static_cast<int>(blockDim.x)) {
+      float4 v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int i = i0 + u * static_cast<int>(blockDim.x) + static_cast<int>(threadIdx.x);
+        if (i < d4) v[u] = s4[i];
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int i = i0 + u * static_cast<int>(blockDim.x) + static_cast<int>(threadIdx.x);
+        if (i < d4) o4[i] = v[u];
+      }
+    }
+    return;
+  }
   for (int i = threadIdx.x; i < d; i += blockDim.x) dst[i] = src[i];
 }
 
@@ -712,11 +734,22 @@ __global__ void __launch_bounds__(256) argmax_kernel(const float* __restrict__ l
   __shared__ float sb[8];
   __shared__ int si[8];
   __shared__ int last;
-  const int per = (V + gridDim.x - 1) / gridDim.x;
-  const int lo = blockIdx.x * per, hi = min(V, lo + per);
+  // Block ranges of a multiple of 4 logits, read in 16-byte pieces (the
+  // order of the comparisons does not matter: `better` is a total order on
+  // (value, -index) that never picks a NaN).
+  const int per = ((V + static_cast<int>(gridDim.x) - 1) / static_cast<int>(gridDim.x) + 3) & ~3;
+  const int lo = min(V, static_cast<int>(blockIdx.x) * per), hi = min(V, lo + per);
   float best = -INFINITY;
   int idx = 0x7fffffff;
-  for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) better(best, idx, mri::ld_act(logits + i), i);
+  const int hi4 = (reinterpret_cast<uintptr_t>(logits) & 15) == 0 ? lo + ((hi - lo) & ~3) : lo;
+  for (int i = lo + 4 * static_cast<int>(threadIdx.x); i < hi4; i += 4 * static_cast<int>(blockDim.x)) {
+    const float4 v = mri::ld_act(reinterpret_cast<const float4*>(logits + i));
+    better(best, idx, v.x, i);
+    better(best, idx, v.y, i + 1);
+    better(best, idx, v.z, i + 2);
+    better(best, idx, v.w, i + 3);
+  }
+  for (int i = hi4 + threadIdx.x; i < hi; i += blockDim.x) better(best, idx, mri::ld_act(logits + i), i);
   block_argmax(best, idx, sb, si);
   if (threadIdx.x == 0) {
     part_v[blockIdx.x] = best;

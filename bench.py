@@ -270,6 +270,71 @@ def decode_chain_measurement(torch, mri, lib, device, peak_hbm):
     return res
 
 
+def e2e_breakdown_measurement(torch, mri, lib, device):
+    """Where the time of one host-buffer call of the headline projection goes
+    (wall clock on the host, per call, weights rotating over 16 copies as in
+    the e2e figure): a bare stream synchronisation, the device-pointer call
+    plus synchronisation, the same after a pinned host-to-device copy of x,
+    and the host-buffer entry point with pageable and with pinned buffers
+    (the pinned output is written by a copy kernel instead of a copy)."""
+    # The context runs on a stream torch owns: torch's pinned-memory allocator
+    # records events on the streams its blocks were used on when they are
+    # freed, so that stream must outlive the tensors.
+    es = torch.cuda.Stream(device)
+    ctx = mri.Context(device, stream=es)
+    rng = np.random.default_rng(0)
+    wq = rng.integers(-127, 128, size=N_DIM * K_DIM, dtype=np.int8)
+    ws = rng.uniform(0.001, 0.02, size=N_DIM).astype(np.float32)
+    weights = [mri.QuantizedMatrix(wq, ws, N_DIM, K_DIM, ctx=ctx, keep_host=False) for _ in range(WEIGHT_COPIES)]
+    x_np = rng.normal(0, 1, size=(1, K_DIM)).astype(np.float32)
+    o_np = np.empty((1, N_DIM), np.float32)
+    x_pin = torch.from_numpy(x_np).pin_memory()
+    o_pin = torch.empty(1, N_DIM).pin_memory()
+    x_dev = torch.empty(1, K_DIM, device=f"cuda:{device}")
+    o_dev = torch.empty(1, N_DIM, device=f"cuda:{device}")
+    state = {"i": 0}
+
+    def w():
+        state["i"] += 1
+        return weights[state["i"] % WEIGHT_COPIES].handle
+
+    def check(rc):
+        if rc != 0:
+            raise RuntimeError(mri._lib.last_error())
+
+    def sync():
+        check(lib.mri_ctx_synchronize(ctx.handle))
+
+    def dev_call():
+        check(lib.mri_matmul_int8_from_f32(ctx.handle, ctypes.c_void_p(x_dev.data_ptr()), 1, K_DIM, w(),
+                                           ctypes.c_void_p(o_dev.data_ptr())))
+
+    def h2d_dev_call():
+        with torch.cuda.stream(es):
+            x_dev.copy_(x_pin, non_blocking=True)
+        dev_call()
+
+    def host(xp, op):
+        check(lib.mri_host_matmul_int8_from_f32(ctx.handle, ctypes.c_void_p(xp), 1, K_DIM, w(), ctypes.c_void_p(op)))
+
+    forms = (("sync_only", sync), ("device_call_sync", lambda: (dev_call(), sync())),
+             ("h2d_device_call_sync", lambda: (h2d_dev_call(), sync())),
+             ("host_call_pageable", lambda: host(x_np.ctypes.data, o_np.ctypes.data)),
+             ("host_call_pinned", lambda: host(x_pin.data_ptr(), o_pin.data_ptr())))
+    res = {}
+    for name, fn in forms:
+        for _ in range(50):
+            fn()
+        n = 500
+        t0 = time.perf_counter()
+        for _ in range(n):
+            fn()
+        res[name] = {"us_per_call": round((time.perf_counter() - t0) / n * 1e6, 2)}
+    res["note"] = "host wall clock per call; the e2e figure is host_call_pinned over 256 calls per step"
+    ctx.synchronize()
+    return res
+
+
 def cpu_side_baselines():
     """The reference's CPU implementations of the secondary configs, timed on
     this host through the C++ restatement (oracle), each a bounded sample:
@@ -462,6 +527,10 @@ def secondary_measurements(torch, mri, lib, device, peak_hbm, peak_tc, parts=SID
             res["decode_gemv_forms"] = decode_chain_measurement(torch, mri, lib, device, peak_hbm)
         except Exception as e:  # noqa: BLE001 - side measurement only
             res["decode_gemv_forms"] = {"error": str(e)[:200]}
+        try:
+            res["e2e_breakdown"] = e2e_breakdown_measurement(torch, mri, lib, device)
+        except Exception as e:  # noqa: BLE001 - side measurement only
+            res["e2e_breakdown"] = {"error": str(e)[:200]}
     if "cpu" in parts:
         try:
             res["cpu_baselines"] = cpu_side_baselines()

@@ -418,9 +418,13 @@ __device__ void stream_producer_i8(const int8_t* W, size_t K, size_t kc, int nk,
 // Pair epilogue (EpiArgs): the warps of rows 2i and 2i+1 swap their values
 // through shared memory (double-buffered by group parity, one 64-thread named
 // barrier per warp pair and group) and combine them.
+// pos0: the absolute position of activation row 0; rc, rs: the RoPE cosine
+// and sine of this row's pair at that position (rows below qd + kvd), loaded
+// by the caller ahead of time.
 __device__ __forceinline__ void pair_epilogue(const EpiArgs& epi, int M, size_t N, size_t row,
                                               bool valid, float val, int lane, int cw, int g,
-                                              float (*s_pair)[kConsumerWarps][8], float* out) {
+                                              float (*s_pair)[kConsumerWarps][8], float* out,
+                                              int pos0, float rc, float rs) {
   if (lane < M) s_pair[g & 1][cw][lane] = val;
   named_bar_sync(2 + (cw >> 1), 64);
   if (!valid || lane >= M) return;
@@ -432,16 +436,13 @@ __device__ __forceinline__ void pair_epilogue(const EpiArgs& epi, int M, size_t 
     return;
   }
   const int r = static_cast<int>(row);
-  const int pos = (epi.pos_dev ? ld_act(epi.pos_dev) : epi.pos0) + m;
+  const int pos = pos0 + m;
   const int qk = epi.qd + epi.kvd;
   float y = val;
   if (r < qk) {
     // ops/rope.rs:121-190: (x0, x1) -> (x0 c - x1 s, x1 c + x0 s), pair j of the head.
-    const int half = epi.hd / 2;
-    const int j = (r % epi.hd) >> 1;
-    const float c = __ldg(epi.cos_t + pos * half + j), sn = __ldg(epi.sin_t + pos * half + j);
-    y = (r & 1) == 0 ? __fsub_rn(__fmul_rn(val, c), __fmul_rn(other, sn))
-                     : __fadd_rn(__fmul_rn(val, c), __fmul_rn(other, sn));
+    y = (r & 1) == 0 ? __fsub_rn(__fmul_rn(val, rc), __fmul_rn(other, rs))
+                     : __fadd_rn(__fmul_rn(val, rc), __fmul_rn(other, rs));
   }
   out[m * N + row] = y;
   if (r >= epi.qd && r < qk) epi.kc[static_cast<size_t>(pos) * epi.kvd + (r - epi.qd)] = y;
@@ -538,9 +539,31 @@ __global__ void __launch_bounds__(kThreads, M <= 2 ? 2 : 1)
 
   const int cw = warp - 1;
   const int groups = static_cast<int>((end - begin + kRowsPerStage - 1) / kRowsPerStage);
-  // The per-row weight scale is loaded one group ahead so its global-load
-  // latency overlaps the stage waits and the dot products.
+  // The per-row weight scale, and the epilogue's other global reads (the
+  // residual; the RoPE cosine and sine), are loaded one group ahead so their
+  // latency overlaps the stage waits and the dot products instead of holding
+  // the warp after each group.  (A residual that aliases `out` is read for
+  // group g + 1 before group g + 1 writes it.)
   float sw_next = begin + cw < end ? __ldg(w_scales + begin + cw) : 0.0f;
+  int pos0 = 0;
+  if constexpr (EPI == 1) pos0 = epi.pos_dev ? ld_act(epi.pos_dev) : epi.pos0;
+  auto rope_cs = [&](size_t r, float& c, float& sn) {
+    c = 0.0f;
+    sn = 0.0f;
+    if constexpr (EPI == 1) {
+      if (epi.mode != EPI_SWIGLU && r < end && static_cast<int>(r) < epi.qd + epi.kvd) {
+        const int half = epi.hd / 2, j = (static_cast<int>(r) % epi.hd) >> 1;
+        c = __ldg(epi.cos_t + pos0 * half + j);
+        sn = __ldg(epi.sin_t + pos0 * half + j);
+      }
+    }
+  };
+  auto resid = [&](size_t r) {
+    return EPI == 0 && residual && r < end && lane < M ? ld_act(residual + lane * N + r) : 0.0f;
+  };
+  float rc_next, rs_next;
+  rope_cs(begin + cw, rc_next, rs_next);
+  float res_next = resid(begin + cw);
   // After a stage wait gives up (status set), the warp still walks the loop
   // without waiting or computing, so every warp reaches the same barriers.
   bool ok = true;
@@ -549,6 +572,9 @@ __global__ void __launch_bounds__(kThreads, M <= 2 ? 2 : 1)
     const size_t row = begin + static_cast<size_t>(g) * kRowsPerStage + cw;
     const float sw = sw_next;
     if (row + kRowsPerStage < end) sw_next = __ldg(w_scales + row + kRowsPerStage);
+    const float rc = rc_next, rs = rs_next, res = res_next;
+    rope_cs(row + kRowsPerStage, rc_next, rs_next);
+    res_next = resid(row + kRowsPerStage);
     int acc[M];
 #pragma unroll
     for (int m = 0; m < M; ++m) acc[m] = 0;
@@ -586,12 +612,12 @@ __global__ void __launch_bounds__(kThreads, M <= 2 ? 2 : 1)
         if (lane == m) val = rescale(acc[m], s_a[m], sw);
     }
     if constexpr (EPI == 1) {
-      pair_epilogue(epi, M, N, row, valid, val, lane, cw, g, s_pair, out);
+      pair_epilogue(epi, M, N, row, valid, val, lane, cw, g, s_pair, out, pos0, rc, rs);
     } else if constexpr (EPI == 2) {
       if (valid && lane < M) s_gout[lane * kGatherCap + (row - begin)] = val;
     } else if (valid && lane < M) {
       // forward_int8.rs:100-121: x + projected (residual may alias out).
-      out[lane * N + row] = residual ? __fadd_rn(ld_act(residual + lane * N + row), val) : val;
+      out[lane * N + row] = residual ? __fadd_rn(res, val) : val;
       if (acc_out) {
 #pragma unroll
         for (int m = 0; m < M; ++m)

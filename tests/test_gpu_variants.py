@@ -339,16 +339,22 @@ def test_q4_0_one_row(mri, oracle, ctx_option, n, k, limb):
     dp4a block dots) and on the f32 streaming kernel (OPT_Q4_LIMB = 0, and
     K = 32 either way); within the Q4_0 bar of the reference's f32 sum,
     including rows whose activations span a wide range (a few large values,
-    many tiny ones)."""
+    many tiny ones; blocks from 1e-30 to 1e30 and a block of subnormals)."""
     from test_gpu_parity import q4_close
     ctx_option(mri.OPT_Q4_LIMB, limb)
     rng = np.random.default_rng(n + k)
     wf = rng.normal(0, 0.02, size=(n, k)).astype(np.float32)
     wb = oracle.quantize_q4_0_matrix(wf, n, k)
     wdeq = oracle.dequantize_q4_0(wb).reshape(n, k)
+    # Blocks of 32 whose magnitudes run from 1e-30 to 1e30 (each block's own
+    # power-of-two scale), and one block of subnormals.
+    nb = k // 32
+    spread = (rng.normal(0, 1, size=(nb, 32)) * 10.0 ** np.linspace(-30, 30, nb)[:, None]).astype(np.float32)
+    spread[0] = rng.normal(0, 1e-39, size=32).astype(np.float32)
     for x in (rng.normal(0, 1, size=(1, k)).astype(np.float32),
               (rng.normal(0, 1e-3, size=(1, k)) * (rng.random((1, k)) < 0.99) +
                rng.normal(0, 50, size=(1, k)) * (rng.random((1, k)) >= 0.99)).astype(np.float32),
+              spread.reshape(1, k),
               np.zeros((1, k), np.float32)):
         got = mri.matmul_q4_0_dequant(x, wb, n, k)
         want = oracle.matmul_q4_0_dequant(x, 1, k, wb, n, k)

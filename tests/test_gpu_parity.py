@@ -216,8 +216,12 @@ def test_quantize_per_channel_matches_oracle(mri, oracle, gpu_ctx):
     assert np.array_equal(qm.data, d2) and np.array_equal(bits(qm.scales), bits(s2))
 
 
+# (1, 4096, 11008): nb = 344, a thread's units cross rows; (1, 300, 8192) and
+# (3, 200, 11008): more terms than the registers hold (written straight into
+# the term buffer), the latter on the streaming kernel at 3 rows (nb > 256).
 Q8_SHAPES = [(1, 11008, 4096), (8, 11008, 4096), (1, 1, 32), (2, 33, 64), (3, 100, 96), (5, 77, 1024),
-             (8, 9, 4096), (9, 50, 256), (1, 64, 28672), (4, 20, 40960), (16, 128, 512)]
+             (8, 9, 4096), (9, 50, 256), (1, 64, 28672), (4, 20, 40960), (16, 128, 512),
+             (1, 4096, 11008), (1, 300, 8192), (3, 200, 11008)]
 
 
 @pytest.mark.parametrize("m,n,k", Q8_SHAPES)

@@ -536,3 +536,9 @@ def test_host_calls_with_pinned_buffers(mri, oracle, gpu_ctx, m):
             assert np.array_equal(bits(out.numpy()), bits(np.asarray(pageable, np.float32))), fn
         want = oracle.matmul_int8_from_f32(x, m, k, wq, ws, n, k)
         assert np.array_equal(bits(cases[0][2]), bits(want))
+    # A pinned output that is not 16-byte aligned is copied instead.
+    buf = torch.full((m * n + 1,), float("nan")).pin_memory()
+    rc = lib.mri_host_matmul_int8_from_f32(gpu_ctx.handle, ctypes.c_void_p(x_pin.data_ptr()), m, k, qm.handle,
+                                           ctypes.c_void_p(buf.data_ptr() + 4))
+    assert rc == 0, mri._lib.last_error()
+    assert np.array_equal(bits(buf[1:].numpy().reshape(m, n)), bits(np.asarray(cases[0][2], np.float32)))

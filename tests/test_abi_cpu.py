@@ -140,3 +140,19 @@ def test_noalloc_size_check_precedes_device_work(mri, m, k):
     rc = lib.mri_matmul_int8_from_f32_noalloc(None, m, k, None, None, 8, None, None)
     assert rc == 6  # MRI_ERR_INVALID_ARGUMENT
     assert b"exceed the fixed scratch" in lib.mri_noalloc_last_error()
+
+
+def test_option_constants_match_header(mri):
+    """Every MRI_OPT_* value of include/mri_gpu.h has the same value as the
+    Python mirror's OPT_* constant, and the option calls reject a null
+    context without touching a device."""
+    import ctypes
+    header = open(os.path.join(REPO, "include", "mri_gpu.h")).read()
+    found = dict(re.findall(r"MRI_OPT_(\w+)\s*=\s*(\d+)", header))
+    assert len(found) >= 10
+    for name, value in found.items():
+        assert getattr(mri, "OPT_" + name) == int(value), name
+    lib = mri._lib.load()
+    assert lib.mri_ctx_set_option(None, 0, 1) == mri._lib.INVALID_ARGUMENT
+    v = ctypes.c_int(-1)
+    assert lib.mri_ctx_get_option(None, 0, ctypes.byref(v)) == mri._lib.INVALID_ARGUMENT
